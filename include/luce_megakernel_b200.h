@@ -1,0 +1,104 @@
+/*
+ * C ABI of libluce_megakernel_b200.so -- the sm_100a implementation of the Qwen3.5-0.8B
+ * hybrid decode / prefill hot path.  Plain pointers and sizes only; every pointer is a
+ * CUDA device pointer unless stated otherwise.
+ *
+ * The launch_* entry points keep the names and argument lists of the C entry points the
+ * reference's PyTorch extension binds (reference: megakernel/torch_bindings.cpp:56-71,
+ * 144-145, 354-368), so the reference's binding file links against this library unchanged.
+ * They return an int status (the reference returns void; a caller that ignores the value
+ * is unaffected): 0 = enqueued, otherwise one of the MK_ERR_* codes below.
+ *
+ * Threading: calls are asynchronous with respect to the host and are ordered on `stream`.
+ * The library keeps one small workspace per device (allocated on the first call on that
+ * device) and is not re-entrant for concurrent calls on the same device.
+ */
+#ifndef LUCE_MEGAKERNEL_B200_H
+#define LUCE_MEGAKERNEL_B200_H
+
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MK_OK 0
+#define MK_ERR_BAD_ARG 1        /* null pointer, misaligned pointer, size out of range */
+#define MK_ERR_CUDA 2           /* a CUDA runtime call failed; see mk_last_error_string() */
+#define MK_ERR_DEVICE_TIMEOUT 3 /* a previous launch gave up on a bounded device-side wait */
+
+/* Layer pointer table entry (reference: megakernel/torch_bindings.cpp:30-34,
+ * megakernel/kernel.cu:104-111).  24 entries; attention layers use 11 pointers, DeltaNet
+ * layers 14, in the order megakernel/model.py:95-133 packs them. */
+typedef struct {
+    int layer_type; /* 0 = Gated DeltaNet, 1 = full attention */
+    int _pad[3];
+    void *ptrs[14];
+} MkLayerWeights;
+
+/* One greedy decode step.  Replaces launch_decode (reference: megakernel/kernel.cu:952-1010,
+ * declared at megakernel/torch_bindings.cpp:56-71).  Scratch arguments the new kernel does not
+ * need (g_activations, g_residual, barrier_*, block_max_*, lm_sync_counter) are accepted and
+ * left untouched. */
+int launch_decode(
+    int input_token_id, int *output_token_id,
+    const void *embed_weight, const MkLayerWeights *layer_weights,
+    const void *final_norm_weight, const void *lm_head_weight,
+    void *fa_k_cache, void *fa_v_cache,
+    void *dn_states, void *conv_bufs,
+    void *hidden_buffer, void *g_activations, void *g_residual,
+    void *g_qkv_scratch, void *g_kv_scratch, void *g_attn_out,
+    void *g_mlp_inter, void *g_z_scratch, void *g_beta_scratch,
+    void *g_alpha_scratch, void *g_normalized,
+    unsigned int *barrier_counter, unsigned int *barrier_generation,
+    float *block_max_vals, int *block_max_idxs,
+    unsigned int *lm_sync_counter,
+    float *seen_token_mask,
+    float repetition_penalty,
+    int position, int max_seq_len, cudaStream_t stream);
+
+/* Resident-block ceiling and decode grid override
+ * (reference: megakernel/kernel.cu:1012-1020, megakernel/torch_bindings.cpp:144-145). */
+void set_decode_blocks_override(int blocks);
+int query_max_safe_decode_blocks(void);
+
+/* `steps` greedy decode steps with the token fed back on the device (no host sync between
+ * steps); output_tokens[i] receives step i's token, token_buffer[0] holds the running token
+ * and must contain the first input token on entry.  bf16 counterpart of
+ * launch_decode_many_nvfp4 (reference: megakernel/kernel_gb10_nvfp4.cu:2192-2257), same
+ * argument meaning as launch_decode otherwise. */
+int mk_decode_many_bf16(
+    int *token_buffer, int *output_tokens, int steps,
+    const void *embed_weight, const MkLayerWeights *layer_weights,
+    const void *final_norm_weight, const void *lm_head_weight,
+    void *fa_k_cache, void *fa_v_cache,
+    void *dn_states, void *conv_bufs,
+    void *hidden_buffer,
+    void *g_qkv_scratch, void *g_kv_scratch, void *g_attn_out,
+    void *g_mlp_inter, void *g_z_scratch, void *g_beta_scratch,
+    void *g_alpha_scratch, void *g_normalized,
+    float *seen_token_mask, float repetition_penalty,
+    int position, int max_seq_len, cudaStream_t stream);
+
+/* Model depth and vocabulary the entry points assume (defaults 24 and 248320, the
+ * compile-time constants of the reference: megakernel/kernel.cu:20,22).  Reduced values let
+ * the parity tests run the same kernels on a small model.  num_layers in [1,24]; the layer
+ * types are read from the pointer table. */
+int mk_set_model_dims(int num_layers, int vocab);
+
+/* Status of the last device-side failure on the current device (0 = none) and a text for the
+ * last error returned on this thread.  mk_clear_error() re-arms the library after a timeout. */
+int mk_device_status(void);
+const char *mk_last_error_string(void);
+void mk_clear_error(void);
+
+/* Optional per-phase timeline: `buf` is a device buffer of
+ * query_max_safe_decode_blocks() * slots_per_cta uint64; thread 0 of every CTA appends the global
+ * timer at four points of each phase (barrier entry, barrier exit, activations staged, rows done)
+ * and stops at slots_per_cta entries.  Pass NULL to switch it off. */
+void mk_set_trace_buffer(unsigned long long *buf, int slots_per_cta);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LUCE_MEGAKERNEL_B200_H */

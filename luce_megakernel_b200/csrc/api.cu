@@ -1,0 +1,228 @@
+// C ABI: argument validation, per-device workspace, launch bookkeeping.
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/luce_megakernel_b200.h"
+#include "mk_common.cuh"
+#include "mk_decode.h"
+
+namespace {
+
+constexpr int MAX_DEVICES = 64;
+
+struct DeviceState {
+    mk::DecodeWorkspace* ws = nullptr;
+    uint32_t* host_status = nullptr;      // mapped pinned word the kernels write on failure
+    uint32_t* host_status_dev = nullptr;  // its device alias
+    int max_grid = 0;
+};
+
+DeviceState g_dev[MAX_DEVICES];
+int g_blocks_override = 0;
+int g_num_layers = mk::MAX_LAYERS;
+int g_vocab = mk::DEFAULT_VOCAB;
+unsigned long long* g_trace = nullptr;
+int g_trace_slots = 0;
+thread_local char g_err[256] = "";
+
+int set_err(int code, const char* what, cudaError_t e = cudaSuccess) {
+    if (e != cudaSuccess) snprintf(g_err, sizeof(g_err), "%s: %s", what, cudaGetErrorString(e));
+    else snprintf(g_err, sizeof(g_err), "%s", what);
+    return code;
+}
+
+// Workspace of the current device; allocated and zeroed on first use (synchronous, once).
+int device_state(DeviceState** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaGetDevice", e);
+    if (dev < 0 || dev >= MAX_DEVICES) return set_err(MK_ERR_BAD_ARG, "device index out of range");
+    DeviceState& d = g_dev[dev];
+    if (!d.ws) {
+        e = cudaMalloc(&d.ws, sizeof(mk::DecodeWorkspace));
+        if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaMalloc(workspace)", e);
+        e = cudaMemset(d.ws, 0, sizeof(mk::DecodeWorkspace));
+        if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaMemset(workspace)", e);
+        e = cudaHostAlloc(&d.host_status, sizeof(uint32_t), cudaHostAllocMapped);
+        if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaHostAlloc(status)", e);
+        *d.host_status = 0;
+        e = cudaHostGetDevicePointer(&d.host_status_dev, d.host_status, 0);
+        if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaHostGetDevicePointer", e);
+        d.max_grid = mk::decode_max_grid();
+        if (d.max_grid <= 0) return set_err(MK_ERR_CUDA, "decode kernel does not fit on this device");
+    }
+    *out = &d;
+    return MK_OK;
+}
+
+bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
+
+int decode_grid(const DeviceState& d) {
+    int g = d.max_grid;
+    if (g_blocks_override > 0 && g_blocks_override < g) g = g_blocks_override;
+    return g;
+}
+
+int check_device_status(DeviceState& d, cudaStream_t stream) {
+    const uint32_t st = *reinterpret_cast<volatile uint32_t*>(d.host_status);
+    if (st == 0) return MK_OK;
+    snprintf(g_err, sizeof(g_err),
+             "a previous launch gave up on a bounded device-side wait (status %u); call mk_clear_error()", st);
+    (void)stream;
+    return MK_ERR_DEVICE_TIMEOUT;
+}
+
+struct DecodeCall {
+    const void *embed, *final_norm, *lm_head;
+    const MkLayerWeights* layers;
+    void *k_cache, *v_cache, *dn_states, *conv_bufs, *hidden;
+    void *qkv, *kv, *attn_out, *mlp_inter, *z, *beta, *alpha, *normalized;
+    float* seen;
+    float penalty;
+    int position, max_seq_len;
+};
+
+int validate(const DecodeCall& a) {
+    const void* req[] = {a.embed, a.final_norm, a.lm_head, a.layers, a.k_cache, a.v_cache, a.dn_states, a.conv_bufs,
+                         a.hidden, a.qkv, a.kv, a.attn_out, a.mlp_inter, a.z, a.beta, a.alpha, a.normalized};
+    for (const void* p : req)
+        if (!p) return set_err(MK_ERR_BAD_ARG, "null pointer argument");
+    const void* al[] = {a.embed, a.final_norm, a.lm_head, a.layers, a.k_cache, a.v_cache, a.dn_states, a.conv_bufs,
+                        a.hidden, a.qkv, a.kv, a.attn_out, a.mlp_inter, a.z, a.normalized};
+    for (const void* p : al)
+        if (misaligned16(p)) return set_err(MK_ERR_BAD_ARG, "pointer argument is not 16-byte aligned");
+    if (a.max_seq_len <= 0) return set_err(MK_ERR_BAD_ARG, "max_seq_len must be positive");
+    if (a.position < 0 || a.position >= a.max_seq_len) return set_err(MK_ERR_BAD_ARG, "position out of range");
+    if (!(a.penalty >= 1.0f) && a.penalty != 0.0f) return set_err(MK_ERR_BAD_ARG, "repetition_penalty must be >= 1");
+    return MK_OK;
+}
+
+mk::DecodeParams make_params(const DecodeCall& a, DeviceState& d) {
+    mk::DecodeParams p;
+    memset(&p, 0, sizeof(p));
+    p.embed = a.embed; p.layers = reinterpret_cast<const mk::LayerWeights*>(a.layers);
+    p.final_norm = a.final_norm; p.lm_head = a.lm_head;
+    p.k_cache = a.k_cache; p.v_cache = a.v_cache;
+    p.dn_states = (float*)a.dn_states; p.conv_bufs = (float*)a.conv_bufs;
+    p.hidden = a.hidden;
+    p.qkv = (float*)a.qkv; p.kv = (float*)a.kv; p.attn_out = (float*)a.attn_out; p.mlp_inter = (float*)a.mlp_inter;
+    p.z = (float*)a.z; p.beta = (float*)a.beta; p.alpha = (float*)a.alpha; p.normalized = (float*)a.normalized;
+    p.seen_mask = a.seen; p.rep_penalty = a.penalty;
+    p.position = a.position; p.max_seq_len = a.max_seq_len;
+    p.num_layers = g_num_layers; p.vocab = g_vocab;
+    p.ws = d.ws; p.host_status = d.host_status_dev; p.trace = g_trace; p.trace_slots = g_trace_slots;
+    return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int launch_decode(
+    int input_token_id, int* output_token_id,
+    const void* embed_weight, const MkLayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden_buffer, void* g_activations, void* g_residual,
+    void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch,
+    void* g_alpha_scratch, void* g_normalized,
+    unsigned int* barrier_counter, unsigned int* barrier_generation,
+    float* block_max_vals, int* block_max_idxs, unsigned int* lm_sync_counter,
+    float* seen_token_mask, float repetition_penalty,
+    int position, int max_seq_len, cudaStream_t stream) {
+    (void)g_activations; (void)g_residual; (void)barrier_counter; (void)barrier_generation;
+    (void)block_max_vals; (void)block_max_idxs; (void)lm_sync_counter;
+    DecodeCall a{embed_weight, final_norm_weight, lm_head_weight, layer_weights,
+                 fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden_buffer,
+                 g_qkv_scratch, g_kv_scratch, g_attn_out, g_mlp_inter, g_z_scratch, g_beta_scratch, g_alpha_scratch,
+                 g_normalized, seen_token_mask, repetition_penalty, position, max_seq_len};
+    if (!output_token_id) return set_err(MK_ERR_BAD_ARG, "null output_token_id");
+    if (input_token_id < 0 || input_token_id >= g_vocab) return set_err(MK_ERR_BAD_ARG, "input_token_id out of range");
+    int rc = validate(a);
+    if (rc) return rc;
+    DeviceState* d = nullptr;
+    if ((rc = device_state(&d))) return rc;
+    if ((rc = check_device_status(*d, stream))) return rc;
+    mk::DecodeParams p = make_params(a, *d);
+    p.token_ptr = nullptr; p.token_val = input_token_id; p.out_token = output_token_id;
+    cudaError_t e = mk::launch_decode_kernel(p, decode_grid(*d), stream);
+    if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
+    return MK_OK;
+}
+
+int mk_decode_many_bf16(
+    int* token_buffer, int* output_tokens, int steps,
+    const void* embed_weight, const MkLayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden_buffer,
+    void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch,
+    void* g_alpha_scratch, void* g_normalized,
+    float* seen_token_mask, float repetition_penalty,
+    int position, int max_seq_len, cudaStream_t stream) {
+    DecodeCall a{embed_weight, final_norm_weight, lm_head_weight, layer_weights,
+                 fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden_buffer,
+                 g_qkv_scratch, g_kv_scratch, g_attn_out, g_mlp_inter, g_z_scratch, g_beta_scratch, g_alpha_scratch,
+                 g_normalized, seen_token_mask, repetition_penalty, position, max_seq_len};
+    if (!token_buffer || !output_tokens) return set_err(MK_ERR_BAD_ARG, "null token buffer");
+    if (steps < 0) return set_err(MK_ERR_BAD_ARG, "steps must be non-negative");
+    if (steps == 0) return MK_OK;
+    int rc = validate(a);
+    if (rc) return rc;
+    if (position + steps > max_seq_len) return set_err(MK_ERR_BAD_ARG, "position + steps exceeds max_seq_len");
+    DeviceState* d = nullptr;
+    if ((rc = device_state(&d))) return rc;
+    if ((rc = check_device_status(*d, stream))) return rc;
+    mk::DecodeParams p = make_params(a, *d);
+    const int grid = decode_grid(*d);
+    for (int s = 0; s < steps; ++s) {
+        p.token_ptr = token_buffer; p.token_val = 0;
+        p.out_token = output_tokens + s; p.token_feedback = token_buffer; p.out_tokens_slot = nullptr;
+        p.position = position + s;
+        cudaError_t e = mk::launch_decode_kernel(p, grid, stream);
+        if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
+    }
+    return MK_OK;
+}
+
+void set_decode_blocks_override(int blocks) { g_blocks_override = blocks < 0 ? 0 : blocks; }
+
+int query_max_safe_decode_blocks(void) {
+    DeviceState* d = nullptr;
+    if (device_state(&d)) return 1;
+    return d->max_grid;
+}
+
+int mk_set_model_dims(int num_layers, int vocab) {
+    if (num_layers < 1 || num_layers > mk::MAX_LAYERS) return set_err(MK_ERR_BAD_ARG, "num_layers must be in [1,24]");
+    if (vocab < 1) return set_err(MK_ERR_BAD_ARG, "vocab must be positive");
+    g_num_layers = num_layers;
+    g_vocab = vocab;
+    return MK_OK;
+}
+
+int mk_device_status(void) {
+    DeviceState* d = nullptr;
+    if (device_state(&d)) return -1;
+    return (int)*reinterpret_cast<volatile uint32_t*>(d->host_status);
+}
+
+const char* mk_last_error_string(void) { return g_err; }
+
+void mk_clear_error(void) {
+    DeviceState* d = nullptr;
+    if (device_state(&d)) return;
+    cudaDeviceSynchronize();
+    cudaMemset(d->ws, 0, sizeof(mk::DecodeWorkspace));
+    *d->host_status = 0;
+    g_err[0] = 0;
+}
+
+void mk_set_trace_buffer(unsigned long long* buf, int slots_per_cta) {
+    g_trace = (buf && slots_per_cta > 0) ? buf : nullptr;
+    g_trace_slots = g_trace ? slots_per_cta : 0;
+}
+
+}  // extern "C"

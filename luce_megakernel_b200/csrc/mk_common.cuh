@@ -1,0 +1,153 @@
+// Shared definitions for the sm_100a kernels: model constants, the layer pointer-table
+// layout, PTX wrappers (mbarrier, bulk async copy, acquire/release), small math helpers.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mk {
+
+// ---- model constants (reference: megakernel/kernel.cu:17-45, megakernel/model.py:6-36) ----
+constexpr int HIDDEN = 1024;
+constexpr int INTER = 3584;
+constexpr int MAX_LAYERS = 24;
+constexpr int DEFAULT_VOCAB = 248320;
+constexpr float RMS_EPS = 1e-6f;
+
+constexpr int FA_Q_HEADS = 8;
+constexpr int FA_KV_HEADS = 2;
+constexpr int FA_GQA = FA_Q_HEADS / FA_KV_HEADS;
+constexpr int FA_HEAD_DIM = 256;
+constexpr int FA_Q_SIZE = FA_Q_HEADS * FA_HEAD_DIM;      // 2048
+constexpr int FA_QPROJ = 2 * FA_Q_SIZE;                  // 4096, per head [q | gate]
+constexpr int FA_KV_SIZE = FA_KV_HEADS * FA_HEAD_DIM;    // 512
+constexpr int FA_QKV_ROWS = FA_QPROJ + 2 * FA_KV_SIZE;   // 5120
+constexpr int FA_ROT = 64;
+constexpr double ROPE_THETA = 1.0e7;
+
+constexpr int DN_HEADS = 16;
+constexpr int DN_KEY = 128;
+constexpr int DN_VAL = 128;
+constexpr int DN_QK = DN_HEADS * DN_KEY;                 // 2048
+constexpr int DN_V = DN_HEADS * DN_VAL;                  // 2048
+constexpr int DN_CONV_CH = 2 * DN_QK + DN_V;             // 6144
+constexpr int DN_CONV_K = 4;
+constexpr int DN_IN_ROWS = DN_CONV_CH + DN_V + 2 * DN_HEADS;   // qkv | z | beta | alpha = 8224
+
+// Device pointer table entry, 128 bytes, written by the caller
+// (reference: megakernel/torch_bindings.cpp:30-34, megakernel/model.py:160-177).
+struct LayerWeights {
+    int layer_type;        // 0 = Gated DeltaNet, 1 = full attention
+    int pad[3];
+    const void* ptrs[14];
+};
+static_assert(sizeof(LayerWeights) == 128, "pointer table entry must be 128 bytes");
+
+// pointer slots, DeltaNet layer (reference: megakernel/model.py:117-132)
+enum { DN_IN_NORM = 0, DN_W_QKV, DN_W_Z, DN_W_B, DN_W_A, DN_CONV_W, DN_A_LOG, DN_DT_BIAS,
+       DN_NORM_W, DN_W_OUT, DN_POST_NORM, DN_W_GATE, DN_W_UP, DN_W_DOWN };
+// pointer slots, attention layer (reference: megakernel/model.py:99-111)
+enum { FA_IN_NORM = 0, FA_W_Q, FA_W_K, FA_W_V, FA_Q_NORM, FA_K_NORM, FA_W_O, FA_POST_NORM,
+       FA_W_GATE, FA_W_UP, FA_W_DOWN };
+
+// status codes reported by the device through the status word
+enum { ST_OK = 0, ST_GRID_TIMEOUT = 1, ST_MBAR_TIMEOUT = 2, ST_MISALIGNED = 3 };
+
+// ---- PTX wrappers ------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait: returns false when the limit ran out (the caller records the status).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t n = 0; n < (1u << 22); ++n)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// global -> shared bulk async copy; bytes % 16 == 0, both addresses 16-byte aligned
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---- math helpers ------------------------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
+
+// 8 bf16 weights (one 16-byte word) times 8 f32 activations
+__device__ __forceinline__ float dot8(const uint4& w, const float* x, float acc) {
+    acc = fmaf(bf_lo(w.x), x[0], acc); acc = fmaf(bf_hi(w.x), x[1], acc);
+    acc = fmaf(bf_lo(w.y), x[2], acc); acc = fmaf(bf_hi(w.y), x[3], acc);
+    acc = fmaf(bf_lo(w.z), x[4], acc); acc = fmaf(bf_hi(w.z), x[5], acc);
+    acc = fmaf(bf_lo(w.w), x[6], acc); acc = fmaf(bf_hi(w.w), x[7], acc);
+    return acc;
+}
+__device__ __forceinline__ float dot4(const uint2& w, const float* x, float acc) {
+    acc = fmaf(bf_lo(w.x), x[0], acc); acc = fmaf(bf_hi(w.x), x[1], acc);
+    acc = fmaf(bf_lo(w.y), x[2], acc); acc = fmaf(bf_hi(w.y), x[3], acc);
+    return acc;
+}
+
+}  // namespace mk

@@ -1,0 +1,126 @@
+// PyTorch op surface over the C ABI.  Registers, in the namespace the reference's Python
+// drivers call (torch.ops.qwen35_megakernel_bf16_C), ops with the reference's schemas
+// (reference: megakernel/torch_bindings.cpp:568-601), so megakernel/model.py-style callers run
+// unchanged.  Every op validates its tensors, forwards raw device pointers and the current
+// CUDA stream to libluce_megakernel_b200.so and turns a non-zero status into an exception.
+#include <Python.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/all.h>
+#include <torch/library.h>
+
+#include "../../include/luce_megakernel_b200.h"
+
+namespace {
+
+using torch::Tensor;
+
+void need(const Tensor& t, const char* name, c10::ScalarType dt, int64_t min_numel) {
+    TORCH_CHECK(t.defined(), name, " is undefined");
+    TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+    TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+    TORCH_CHECK(t.scalar_type() == dt, name, " has dtype ", t.scalar_type(), ", expected ", dt);
+    TORCH_CHECK(t.numel() >= min_numel, name, " has ", t.numel(), " elements, needs at least ", min_numel);
+}
+
+void check_status(int rc, const char* op) {
+    TORCH_CHECK(rc == MK_OK, "qwen35_megakernel_bf16_C::", op, " failed (", rc, "): ", mk_last_error_string());
+}
+
+cudaStream_t current_stream(const Tensor& t) { return c10::cuda::getCurrentCUDAStream(t.get_device()).stream(); }
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(const Tensor& t) {
+        cudaGetDevice(&prev);
+        if (prev != t.get_device()) cudaSetDevice(t.get_device());
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (cur != prev && prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+void decode(Tensor output_token, int64_t input_token_id, Tensor embed_weight, Tensor layer_weights_packed,
+            Tensor final_norm_weight, Tensor lm_head_weight, Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states,
+            Tensor conv_bufs, Tensor hidden_buffer, Tensor activations, Tensor residual, Tensor qkv_scratch,
+            Tensor kv_scratch, Tensor attn_out, Tensor mlp_inter, Tensor z_scratch, Tensor beta_scratch,
+            Tensor alpha_scratch, Tensor normalized, Tensor barrier_counter, Tensor barrier_generation,
+            Tensor block_max_vals, Tensor block_max_idxs, Tensor lm_sync_counter, Tensor seen_token_mask,
+            double repetition_penalty, int64_t position, int64_t max_seq_len) {
+    const auto bf16 = torch::kBFloat16;
+    const auto f32 = torch::kFloat32;
+    need(output_token, "output_token", torch::kInt32, 1);
+    need(embed_weight, "embed_weight", bf16, 1024);
+    need(layer_weights_packed, "layer_weights_packed", torch::kUInt8, 128);
+    need(final_norm_weight, "final_norm_weight", bf16, 1024);
+    need(lm_head_weight, "lm_head_weight", bf16, 1024);
+    need(fa_k_cache, "fa_k_cache", bf16, 2 * max_seq_len * 256);
+    need(fa_v_cache, "fa_v_cache", bf16, 2 * max_seq_len * 256);
+    need(dn_states, "dn_states", f32, 16 * 128 * 128);
+    need(conv_bufs, "conv_bufs", f32, 6144 * 4);
+    need(hidden_buffer, "hidden_buffer", bf16, 1024);
+    need(qkv_scratch, "qkv_scratch", f32, 6144);
+    need(kv_scratch, "kv_scratch", f32, 1024);
+    need(attn_out, "attn_out", f32, 2048);
+    need(mlp_inter, "mlp_inter", f32, 3584);
+    need(z_scratch, "z_scratch", f32, 2048);
+    need(beta_scratch, "beta_scratch", f32, 16);
+    need(alpha_scratch, "alpha_scratch", f32, 16);
+    need(normalized, "normalized", f32, 1024);
+    if (repetition_penalty > 1.0) need(seen_token_mask, "seen_token_mask", f32, embed_weight.size(0));
+    TORCH_CHECK(embed_weight.dim() == 2 && embed_weight.size(1) == 1024, "embed_weight must be [vocab, 1024]");
+    TORCH_CHECK(layer_weights_packed.numel() % 128 == 0, "layer_weights_packed must hold 128-byte entries");
+    DeviceGuard guard(embed_weight);
+    check_status(mk_set_model_dims((int)(layer_weights_packed.numel() / 128), (int)embed_weight.size(0)), "decode");
+    const int rc = launch_decode(
+        (int)input_token_id, (int*)output_token.data_ptr(), embed_weight.data_ptr(),
+        (const MkLayerWeights*)layer_weights_packed.data_ptr(), final_norm_weight.data_ptr(),
+        lm_head_weight.data_ptr(), fa_k_cache.data_ptr(), fa_v_cache.data_ptr(), dn_states.data_ptr(),
+        conv_bufs.data_ptr(), hidden_buffer.data_ptr(), activations.defined() ? activations.data_ptr() : nullptr,
+        residual.defined() ? residual.data_ptr() : nullptr, qkv_scratch.data_ptr(), kv_scratch.data_ptr(),
+        attn_out.data_ptr(), mlp_inter.data_ptr(), z_scratch.data_ptr(), beta_scratch.data_ptr(),
+        alpha_scratch.data_ptr(), normalized.data_ptr(), nullptr, nullptr, nullptr, nullptr, nullptr,
+        seen_token_mask.defined() ? (float*)seen_token_mask.data_ptr() : nullptr, (float)repetition_penalty,
+        (int)position, (int)max_seq_len, current_stream(embed_weight));
+    check_status(rc, "decode");
+    (void)barrier_counter; (void)barrier_generation; (void)block_max_vals; (void)block_max_idxs; (void)lm_sync_counter;
+}
+
+int64_t max_safe_decode_blocks() { return query_max_safe_decode_blocks(); }
+
+void set_decode_blocks(int64_t blocks) {
+    TORCH_CHECK(blocks >= 0, "blocks must be non-negative");
+    set_decode_blocks_override((int)blocks);
+}
+
+}  // namespace
+
+TORCH_LIBRARY(qwen35_megakernel_bf16_C, ops) {
+    ops.def("decode(Tensor output_token, int input_token_id, "
+            "Tensor embed_weight, Tensor layer_weights_packed, "
+            "Tensor final_norm_weight, Tensor lm_head_weight, "
+            "Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs, "
+            "Tensor hidden_buffer, Tensor activations, Tensor residual, "
+            "Tensor qkv_scratch, Tensor kv_scratch, Tensor attn_out, "
+            "Tensor mlp_inter, Tensor z_scratch, Tensor beta_scratch, "
+            "Tensor alpha_scratch, Tensor normalized, "
+            "Tensor barrier_counter, Tensor barrier_generation, "
+            "Tensor block_max_vals, Tensor block_max_idxs, Tensor lm_sync_counter, "
+            "Tensor seen_token_mask, float repetition_penalty, "
+            "int position, int max_seq_len) -> ()");
+    ops.impl("decode", torch::kCUDA, &decode);
+
+    ops.def("max_safe_decode_blocks() -> int");
+    ops.impl("max_safe_decode_blocks", &max_safe_decode_blocks);
+
+    ops.def("set_decode_blocks(int blocks) -> ()");
+    ops.impl("set_decode_blocks", &set_decode_blocks);
+}
+
+// Importable as a Python module of the same name, like the reference extension
+// (reference: megakernel/torch_bindings.cpp:23-28,679).
+PyMODINIT_FUNC PyInit_qwen35_megakernel_bf16_C(void) {
+    static struct PyModuleDef module = {PyModuleDef_HEAD_INIT, "qwen35_megakernel_bf16_C", nullptr, 0, nullptr};
+    return PyModule_Create(&module);
+}

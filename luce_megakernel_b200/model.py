@@ -1,0 +1,287 @@
+"""Weight packing and the stateful decoder over the sm_100a ops.
+
+Host-side mirror of the reference's Python driver (reference: megakernel/model.py): the same
+constants, the same 24 x 128-byte layer pointer table, the same state / scratch tensors and
+the same `Decoder.step / reset / generate / alloc_prefill_scratch` interface, so code written
+against the reference driver runs against this one.  The arithmetic lives in the native
+library; nothing here computes on the CPU.
+"""
+import ctypes
+import struct
+
+import torch
+
+NUM_LAYERS = 24
+HIDDEN_SIZE = 1024
+INTERMEDIATE_SIZE = 3584
+VOCAB_SIZE = 248320
+MAX_SEQ_LEN = 2048
+
+FA_NUM_Q_HEADS = 8
+FA_NUM_KV_HEADS = 2
+FA_HEAD_DIM = 256
+FA_Q_SIZE = FA_NUM_Q_HEADS * FA_HEAD_DIM
+FA_QPROJ_SIZE = FA_Q_SIZE * 2
+FA_KV_SIZE = FA_NUM_KV_HEADS * FA_HEAD_DIM
+
+DN_NUM_HEADS = 16
+DN_KEY_DIM = 128
+DN_VALUE_DIM = 128
+DN_QK_SIZE = DN_NUM_HEADS * DN_KEY_DIM
+DN_V_SIZE = DN_NUM_HEADS * DN_VALUE_DIM
+DN_CONV_CHANNELS = DN_QK_SIZE * 2 + DN_V_SIZE
+DN_CONV_KERNEL = 4
+
+
+def layer_types(num_layers=NUM_LAYERS):
+    """0 = Gated DeltaNet, 1 = full attention, pattern [DN, DN, DN, FA]."""
+    return [1 if i % 4 == 3 else 0 for i in range(num_layers)]
+
+
+LAYER_TYPE = layer_types()
+
+_FA_KEYS = ("input_layernorm.weight", "self_attn.q_proj.weight", "self_attn.k_proj.weight",
+            "self_attn.v_proj.weight", "self_attn.q_norm.weight", "self_attn.k_norm.weight",
+            "self_attn.o_proj.weight", "post_attention_layernorm.weight",
+            "mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight")
+_DN_KEYS = ("input_layernorm.weight", "linear_attn.in_proj_qkv.weight", "linear_attn.in_proj_z.weight",
+            "linear_attn.in_proj_b.weight", "linear_attn.in_proj_a.weight", "linear_attn.conv1d.weight",
+            "linear_attn.A_log", "linear_attn.dt_bias", "linear_attn.norm.weight",
+            "linear_attn.out_proj.weight", "post_attention_layernorm.weight",
+            "mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight")
+
+
+def weights_from_state_dict(state, device="cuda", num_layers=None):
+    """Orders a `transformers`-style state dict into the per-layer pointer lists the kernels
+    read: 11 tensors for an attention layer, 14 for a DeltaNet layer
+    (reference: megakernel/model.py:90-148).  Tensors become contiguous bf16 on `device`."""
+    if num_layers is None:
+        num_layers = 1 + max(int(k.split(".")[2]) for k in state if k.startswith("model.layers."))
+
+    def w(key):
+        return state[key].to(device=device, dtype=torch.bfloat16).contiguous()
+
+    layer_data = []
+    for i, lt in enumerate(layer_types(num_layers)):
+        keys = _FA_KEYS if lt == 1 else _DN_KEYS
+        layer_data.append({"type": lt, "ptrs": [w(f"model.layers.{i}.{k}") for k in keys]})
+    embed = w("model.embed_tokens.weight")
+    lm_head = w("lm_head.weight") if "lm_head.weight" in state else embed
+    return {"embed_weight": embed, "final_norm_weight": w("model.norm.weight"),
+            "lm_head_weight": lm_head, "layer_data": layer_data}
+
+
+def load_weights(model_name="Qwen/Qwen3.5-0.8B", verbose=True, seed=None, num_layers=NUM_LAYERS,
+                 vocab=VOCAB_SIZE, norm_init="literal", device_init=False):
+    """Returns (weights, tokenizer).  With `seed` set, seeded random-init weights of the
+    architecture are produced (tokenizer None; drawn on the CPU unless device_init, see
+    weights.random_state_dict); otherwise the checkpoint `model_name` is
+    loaded through transformers, like the reference does (megakernel/model.py:66-157)."""
+    if seed is not None:
+        from .weights import random_state_dict
+        dev = torch.device("cuda", torch.cuda.current_device()) if device_init else "cpu"
+        sd = random_state_dict(seed, num_layers, vocab, norm_init, device=dev)
+        return weights_from_state_dict(sd, device=torch.device("cuda", torch.cuda.current_device()),
+                                       num_layers=num_layers), None
+    from transformers import AutoModelForCausalLM, AutoTokenizer
+    if verbose:
+        print(f"Loading {model_name} (bf16)...")
+    model = AutoModelForCausalLM.from_pretrained(model_name, dtype=torch.bfloat16, device_map="cuda")
+    tokenizer = AutoTokenizer.from_pretrained(model_name)
+    weights = weights_from_state_dict(model.state_dict())
+    del model
+    torch.cuda.empty_cache()
+    return weights, tokenizer
+
+
+def _pack_layer_weights(layer_data):
+    """Device blob of len(layer_data) entries {int type; int pad[3]; void* ptrs[14]} (128 B each),
+    the layout of MkLayerWeights (reference: megakernel/model.py:160-177)."""
+    entry = struct.Struct("<4i14Q")
+    assert entry.size == 128
+    blob = bytearray()
+    for ld in layer_data:
+        ptrs = [t.data_ptr() for t in ld["ptrs"]]
+        blob += entry.pack(ld["type"], 0, 0, 0, *(ptrs + [0] * (14 - len(ptrs))))
+    return torch.frombuffer(blob, dtype=torch.uint8).cuda()
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+class Decoder:
+    """Stateful greedy decoder (reference: megakernel/model.py:180-318).
+
+    `api="ops"` calls torch.ops.qwen35_megakernel_bf16_C.* exactly like the reference
+    driver; `api="cabi"` calls the C ABI of libluce_megakernel_b200.so through ctypes."""
+
+    def __init__(self, weights=None, tokenizer=None, model_name="Qwen/Qwen3.5-0.8B", verbose=True,
+                 max_seq_len=MAX_SEQ_LEN, repetition_penalty=1.0, decode_blocks=None, api="ops"):
+        if max_seq_len <= 0:
+            raise ValueError("max_seq_len must be positive")
+        if repetition_penalty < 1.0:
+            raise ValueError("repetition_penalty must be >= 1.0")
+        if decode_blocks is not None and decode_blocks < 0:
+            raise ValueError("decode_blocks must be non-negative")
+        if api not in ("ops", "cabi"):
+            raise ValueError("api must be 'ops' or 'cabi'")
+        from . import lib, load_ops
+        self._lib = lib()
+        self._ops = load_ops() if api == "ops" else None
+        self.api = api
+        if weights is None:
+            weights, tokenizer = load_weights(model_name, verbose=verbose)
+        self.tokenizer = tokenizer
+        self._position = 0
+        self.max_seq_len = int(max_seq_len)
+        self.repetition_penalty = float(repetition_penalty)
+        self._weights = weights
+        self._embed_weight = weights["embed_weight"]
+        self._final_norm_weight = weights["final_norm_weight"]
+        self._lm_head_weight = weights["lm_head_weight"]
+        layer_data = weights["layer_data"]
+        self.num_layers = len(layer_data)
+        self.vocab = int(self._embed_weight.shape[0])
+        self._layer_weights_packed = _pack_layer_weights(layer_data)
+        self._bind_dims()
+        self._lib.set_decode_blocks_override(0 if decode_blocks is None else int(decode_blocks))
+
+        dev = self._embed_weight.device
+        bf16 = dict(dtype=torch.bfloat16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        u32 = dict(dtype=torch.uint32, device=dev)
+        types = [ld["type"] for ld in layer_data]
+        n_fa, n_dn = sum(types), len(types) - sum(types)
+        self._fa_k_cache = torch.zeros(max(n_fa, 1), FA_NUM_KV_HEADS, self.max_seq_len, FA_HEAD_DIM, **bf16)
+        self._fa_v_cache = torch.zeros_like(self._fa_k_cache)
+        self._dn_states = torch.zeros(max(n_dn, 1), DN_NUM_HEADS, DN_KEY_DIM, DN_VALUE_DIM, **f32)
+        self._conv_bufs = torch.zeros(max(n_dn, 1), DN_CONV_CHANNELS, DN_CONV_KERNEL, **f32)
+        self._hidden = torch.empty(HIDDEN_SIZE, **bf16)
+        self._activations = torch.empty(HIDDEN_SIZE * 8 + INTERMEDIATE_SIZE, **f32)
+        self._residual = torch.empty(HIDDEN_SIZE, **bf16)
+        self._qkv_scratch = torch.empty(max(FA_QPROJ_SIZE, DN_CONV_CHANNELS), **f32)
+        self._kv_scratch = torch.empty(FA_KV_SIZE * 2, **f32)
+        self._attn_out = torch.empty(max(FA_Q_SIZE, DN_V_SIZE), **f32)
+        self._mlp_inter = torch.empty(INTERMEDIATE_SIZE, **f32)
+        self._z_scratch = torch.empty(DN_V_SIZE, **f32)
+        self._beta_scratch = torch.empty(DN_NUM_HEADS, **f32)
+        self._alpha_scratch = torch.empty(DN_NUM_HEADS, **f32)
+        self._normalized = torch.empty(HIDDEN_SIZE, **f32)
+        self._barrier_counter = torch.zeros(1, **u32)
+        self._barrier_generation = torch.zeros(1, **u32)
+        self._block_max_vals = torch.empty(1024, **f32)
+        self._block_max_idxs = torch.empty(1024, **i32)
+        self._lm_sync_counter = torch.zeros(1, **u32)
+        self._seen_token_mask = torch.zeros(self.vocab, **f32)
+        self._out_token = torch.empty(1, **i32)
+        self._token_buffer = torch.empty(1, **i32)
+
+    # ------------------------------------------------------------------------------------
+    def _bind_dims(self):
+        rc = self._lib.mk_set_model_dims(self.num_layers, self.vocab)
+        if rc != 0:
+            raise RuntimeError(self._lib.mk_last_error_string().decode())
+
+    def _check(self, rc):
+        if rc != 0:
+            raise RuntimeError(f"luce_megakernel_b200 error {rc}: {self._lib.mk_last_error_string().decode()}")
+
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream(self._embed_weight.device).cuda_stream)
+
+    def step_async(self, token_id: int):
+        """Enqueue one decode step; the next token lands in self._out_token (no host sync)."""
+        if self._position >= self.max_seq_len:
+            raise ValueError(f"position {self._position} exceeds max_seq_len={self.max_seq_len}")
+        self._bind_dims()
+        if self.api == "ops":
+            self._ops.decode(
+                self._out_token, token_id, self._embed_weight, self._layer_weights_packed,
+                self._final_norm_weight, self._lm_head_weight, self._fa_k_cache, self._fa_v_cache,
+                self._dn_states, self._conv_bufs, self._hidden, self._activations, self._residual,
+                self._qkv_scratch, self._kv_scratch, self._attn_out, self._mlp_inter, self._z_scratch,
+                self._beta_scratch, self._alpha_scratch, self._normalized, self._barrier_counter,
+                self._barrier_generation, self._block_max_vals, self._block_max_idxs, self._lm_sync_counter,
+                self._seen_token_mask, self.repetition_penalty, self._position, self.max_seq_len)
+        else:
+            self._check(self._lib.launch_decode(
+                ctypes.c_int(int(token_id)), _ptr(self._out_token), _ptr(self._embed_weight),
+                _ptr(self._layer_weights_packed), _ptr(self._final_norm_weight), _ptr(self._lm_head_weight),
+                _ptr(self._fa_k_cache), _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs),
+                _ptr(self._hidden), _ptr(self._activations), _ptr(self._residual), _ptr(self._qkv_scratch),
+                _ptr(self._kv_scratch), _ptr(self._attn_out), _ptr(self._mlp_inter), _ptr(self._z_scratch),
+                _ptr(self._beta_scratch), _ptr(self._alpha_scratch), _ptr(self._normalized),
+                _ptr(self._barrier_counter), _ptr(self._barrier_generation), _ptr(self._block_max_vals),
+                _ptr(self._block_max_idxs), _ptr(self._lm_sync_counter), _ptr(self._seen_token_mask),
+                ctypes.c_float(self.repetition_penalty), ctypes.c_int(self._position),
+                ctypes.c_int(self.max_seq_len), self._stream()))
+        self._position += 1
+
+    def step(self, token_id: int) -> int:
+        """Decode one token.  Returns the next token id (synchronises with the device)."""
+        self.step_async(token_id)
+        return int(self._out_token.item())
+
+    def step_many(self, token_id: int, steps: int) -> torch.Tensor:
+        """`steps` greedy steps with the token fed back on the device; returns the int32 device
+        tensor of generated tokens without synchronising (bf16 counterpart of the reference's
+        NVFP4 step_many, megakernel/model_nvfp4.py:742-769)."""
+        if steps <= 0:
+            return torch.empty(0, dtype=torch.int32, device=self._out_token.device)
+        if self._position + steps > self.max_seq_len:
+            raise ValueError("position + steps exceeds max_seq_len")
+        self._bind_dims()
+        out = torch.empty(steps, dtype=torch.int32, device=self._out_token.device)
+        self._token_buffer.fill_(int(token_id))
+        self._check(self._lib.mk_decode_many_bf16(
+            _ptr(self._token_buffer), _ptr(out), ctypes.c_int(steps), _ptr(self._embed_weight),
+            _ptr(self._layer_weights_packed), _ptr(self._final_norm_weight), _ptr(self._lm_head_weight),
+            _ptr(self._fa_k_cache), _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs),
+            _ptr(self._hidden), _ptr(self._qkv_scratch), _ptr(self._kv_scratch), _ptr(self._attn_out),
+            _ptr(self._mlp_inter), _ptr(self._z_scratch), _ptr(self._beta_scratch), _ptr(self._alpha_scratch),
+            _ptr(self._normalized), _ptr(self._seen_token_mask), ctypes.c_float(self.repetition_penalty),
+            ctypes.c_int(self._position), ctypes.c_int(self.max_seq_len), self._stream()))
+        self._position += steps
+        return out
+
+    def reset(self):
+        self._position = 0
+        self._fa_k_cache.zero_()
+        self._fa_v_cache.zero_()
+        self._dn_states.zero_()
+        self._conv_bufs.zero_()
+        self._seen_token_mask.zero_()
+
+    def state_dict(self):
+        """The whole session state (a checkpoint of a generation in flight)."""
+        return {"position": self._position, "fa_k_cache": self._fa_k_cache.clone(),
+                "fa_v_cache": self._fa_v_cache.clone(), "dn_states": self._dn_states.clone(),
+                "conv_bufs": self._conv_bufs.clone(), "seen_token_mask": self._seen_token_mask.clone()}
+
+    def load_state_dict(self, sd):
+        self._position = int(sd["position"])
+        self._fa_k_cache.copy_(sd["fa_k_cache"])
+        self._fa_v_cache.copy_(sd["fa_v_cache"])
+        self._dn_states.copy_(sd["dn_states"])
+        self._conv_bufs.copy_(sd["conv_bufs"])
+        self._seen_token_mask.copy_(sd["seen_token_mask"])
+
+    def generate_ids(self, prompt_ids, max_tokens=100, eos=None):
+        """Token-level generate: feeds the prompt token by token, then decodes greedily."""
+        self.reset()
+        for tid in prompt_ids[:-1]:
+            self.step_async(int(tid))
+        out, nxt = [], int(prompt_ids[-1])
+        for _ in range(max_tokens):
+            nxt = self.step(nxt)
+            if eos is not None and nxt == eos:
+                break
+            out.append(nxt)
+        return out
+
+    def generate(self, prompt: str, max_tokens: int = 100) -> str:
+        ids = self.tokenizer.encode(prompt, add_special_tokens=True)
+        out = self.generate_ids(ids, max_tokens, self.tokenizer.eos_token_id)
+        return self.tokenizer.decode(out, skip_special_tokens=True)

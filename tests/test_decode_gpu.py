@@ -1,0 +1,293 @@
+"""GPU parity of the bf16 decode step against the CPU oracle (same seeded weights, same tokens).
+
+Tolerances (bf16 path, from the acceptance rule of this project):
+  * per-layer hidden states: 2e-2 max-abs for a single token; over a sequence the bound is
+    widened to four bf16 ulps of the layer's largest element where that is larger (the
+    residual stream is stored in bf16, one last-bit flip of a value in [2, 4) is already
+    1.6e-2, and flips made in early layers are carried through the later ones);
+  * logits: 5e-2 max-abs (computed on the CPU from the kernel's final-normed vector);
+  * greedy tokens: identical wherever the oracle's top-1/top-2 margin exceeds 2 x 5e-2;
+    below that margin either of the oracle's two best tokens is accepted.
+"""
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from oracle import qwen35_oracle as O  # noqa: E402
+
+NL, V, MAXSEQ = 8, 2048, 256
+
+
+def bf16_ulp(x: float) -> float:
+    import math
+    return 2.0 ** (math.floor(math.log2(max(x, 1e-30))) - 7)
+
+
+def hidden_tol(ref: torch.Tensor) -> float:
+    return max(2e-2, 4.0 * bf16_ulp(float(ref.abs().max())))
+
+
+@pytest.fixture(scope="module")
+def dec_small(small_model):
+    from luce_megakernel_b200 import model as M
+    sd, _ = small_model("unit", "decode")
+    w = M.weights_from_state_dict(sd)
+    return M.Decoder(weights=w, max_seq_len=MAXSEQ, api="cabi")
+
+
+def seeded_prompt(n, seed=0, vocab=V):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, vocab, (n,), generator=g).tolist()
+
+
+def accept_token(tok, logits_ref):
+    top = torch.topk(logits_ref, 2)
+    margin = float(top.values[0] - top.values[1])
+    if margin > 0.1:
+        return tok == int(top.indices[0])
+    return tok in top.indices.tolist()
+
+
+def test_native_library_loaded():
+    import luce_megakernel_b200 as L
+    lib = L.lib()
+    assert lib.query_max_safe_decode_blocks() >= 100
+    assert lib.mk_device_status() == 0
+
+
+def test_per_layer_hidden_single_token(dec_small, small_model):
+    sd, orc = small_model("unit", "decode")
+    tok = seeded_prompt(1)[0]
+    tr = orc.forward([tok], O.State.new(NL, MAXSEQ, V))
+    for k in range(1, NL + 1):
+        dec_small.reset()
+        dec_small.num_layers = k          # run only the first k layers of the pointer table
+        dec_small.step(tok)
+        got = dec_small._hidden.float().cpu()
+        err = float((got - tr.hidden[k - 1][0]).abs().max())
+        assert err <= 2e-2, f"layer {k}: hidden max-abs error {err}"
+    dec_small.num_layers = NL
+
+
+def test_teacher_forced_sequence(dec_small, small_model):
+    sd, orc = small_model("unit", "decode")
+    dec_small.reset()
+    st = O.State.new(NL, MAXSEQ, V)
+    lm = sd["model.embed_tokens.weight"].float()
+    worst_h = worst_l = 0.0
+    for t in seeded_prompt(48):
+        tok = dec_small.step(t)
+        tr = orc.forward([t], st)
+        ref_h = tr.hidden[-1][0]
+        eh = float((dec_small._hidden.float().cpu() - ref_h).abs().max())
+        assert eh <= hidden_tol(ref_h), f"pos {st.position - 1}: hidden error {eh}"
+        logits = lm @ dec_small._normalized.cpu()
+        el = float((logits - tr.logits).abs().max())
+        assert el <= 5e-2, f"pos {st.position - 1}: logit error {el}"
+        assert accept_token(tok, tr.logits), f"pos {st.position - 1}: token {tok} vs oracle {tr.token}"
+        assert tok == int(torch.argmax(logits)) or float(logits.max() - logits[tok]) < 1e-4
+        worst_h, worst_l = max(worst_h, eh), max(worst_l, el)
+    print(f"worst hidden err {worst_h:.4g}, worst logit err {worst_l:.4g}")
+    # session state in the reference layouts
+    L = st.position
+    assert float((dec_small._dn_states.cpu() - st.dn_states).abs().max()) < 5e-3
+    assert float((dec_small._conv_bufs.cpu() - st.conv_bufs).abs().max()) < 8e-2
+    kerr = float((dec_small._fa_k_cache.float().cpu()[:, :, :L] - st.k_cache[:, :, :L]).abs().max())
+    verr = float((dec_small._fa_v_cache.float().cpu()[:, :, :L] - st.v_cache[:, :, :L]).abs().max())
+    assert kerr <= 0.13 and verr <= 0.13   # bf16 cache entries, a few ulps of values up to ~8
+    assert float(dec_small._fa_k_cache[:, :, L:].abs().max()) == 0.0   # nothing written past the position
+
+
+def test_free_running_greedy_128(dec_small, small_model):
+    """128 greedy steps after a 32-token prompt: tokens must equal the oracle's for as long as
+    the oracle's margins exceed the logit tolerance; the first divergence (if any) is reported
+    together with the margin there and must sit at a low-margin step."""
+    sd, orc = small_model("unit", "decode")
+    prompt = seeded_prompt(32, seed=1)
+    dec_small.reset()
+    for t in prompt[:-1]:
+        dec_small.step_async(t)
+    got = dec_small.step_many(prompt[-1], 128).cpu().tolist()
+    st = O.State.new(NL, MAXSEQ, V)
+    orc.forward(prompt[:-1], st, want_logits=False)
+    t = prompt[-1]
+    for i in range(128):
+        tr = orc.forward([t], st)
+        if got[i] != tr.token:
+            top = torch.topk(tr.logits, 2)
+            margin = float(top.values[0] - top.values[1])
+            print(f"first divergence at step {i}: gpu {got[i]} oracle {tr.token} margin {margin:.4g}")
+            assert margin <= 0.1 and got[i] in top.indices.tolist()
+            return
+        t = tr.token
+    print("128 greedy tokens identical to the oracle")
+
+
+def test_step_many_equals_single_steps_and_is_deterministic(dec_small):
+    prompt = seeded_prompt(20, seed=2)
+    runs = []
+    for mode in ("single", "many", "many"):
+        dec_small.reset()
+        for t in prompt[:-1]:
+            dec_small.step_async(t)
+        if mode == "single":
+            out, t = [], prompt[-1]
+            for _ in range(24):
+                t = dec_small.step(t)
+                out.append(t)
+        else:
+            out = dec_small.step_many(prompt[-1], 24).cpu().tolist()
+        runs.append((out, dec_small._dn_states.clone(), dec_small._fa_k_cache.clone(), dec_small._hidden.clone()))
+    assert runs[0][0] == runs[1][0] == runs[2][0]
+    for a, b in ((0, 1), (1, 2)):      # bit-identical state: any race would show up here
+        assert torch.equal(runs[a][1], runs[b][1]) and torch.equal(runs[a][2], runs[b][2])
+        assert torch.equal(runs[a][3], runs[b][3])
+
+
+def test_grid_override_gives_identical_results(dec_small):
+    import luce_megakernel_b200 as L
+    lib = L.lib()
+    prompt = seeded_prompt(12, seed=4)
+    outs = []
+    for blocks in (0, 64, 37):
+        lib.set_decode_blocks_override(blocks)
+        dec_small.reset()
+        toks = [dec_small.step(t) for t in prompt]
+        outs.append((toks, dec_small._dn_states.clone()))
+    lib.set_decode_blocks_override(0)
+    assert outs[0][0] == outs[1][0] == outs[2][0]
+    assert torch.equal(outs[0][1], outs[1][1]) and torch.equal(outs[0][1], outs[2][1])
+
+
+def test_repetition_penalty(dec_small, small_model):
+    sd, orc = small_model("unit", "decode")
+    prompt = seeded_prompt(10, seed=5)
+    dec_small.reset()
+    dec_small.repetition_penalty = 1.3
+    st = O.State.new(NL, MAXSEQ, V)
+    try:
+        for t in prompt:
+            tok = dec_small.step(t)
+            tr = orc.forward([t], st, repetition_penalty=1.3)
+            assert accept_token(tok, tr.logits)
+        assert torch.equal((dec_small._seen_token_mask.cpu() > 0), (st.seen > 0))
+    finally:
+        dec_small.repetition_penalty = 1.0
+
+
+def test_long_context_attention_chunks(dec_small, small_model):
+    """Positions up to 200 exercise 1..4 KV chunks per KV head and the cross-CTA softmax merge."""
+    sd, orc = small_model("unit", "decode")
+    dec_small.reset()
+    st = O.State.new(NL, MAXSEQ, V)
+    toks = seeded_prompt(200, seed=6)
+    for i, t in enumerate(toks):
+        dec_small.step_async(t)
+        if i in (63, 64, 65, 127, 128, 199):
+            if i > st.position:
+                orc.forward(toks[st.position:i], st, want_logits=False)
+            trs = orc.forward([t], st)
+            ref_h = trs.hidden[-1][0]
+            eh = float((dec_small._hidden.float().cpu() - ref_h).abs().max())
+            assert eh <= hidden_tol(ref_h), f"pos {i}: hidden error {eh}"
+            assert accept_token(int(dec_small._out_token.item()), trs.logits)
+
+
+def test_ops_surface_matches_cabi(dec_small, small_model):
+    from luce_megakernel_b200 import model as M
+    sd, _ = small_model("unit", "decode")
+    dec_ops = M.Decoder(weights=dec_small._weights, max_seq_len=MAXSEQ, api="ops")
+    prompt = seeded_prompt(10, seed=7)
+    dec_small.reset()
+    a = [dec_small.step(t) for t in prompt]
+    b = [dec_ops.step(t) for t in prompt]
+    assert a == b
+    assert torch.equal(dec_small._dn_states, dec_ops._dn_states)
+    import torch as T
+    assert int(T.ops.qwen35_megakernel_bf16_C.max_safe_decode_blocks()) >= 100
+
+
+def test_error_paths(dec_small):
+    import luce_megakernel_b200 as L
+    lib = L.lib()
+    with pytest.raises(ValueError):
+        dec_small._position = MAXSEQ
+        dec_small.step(1)
+    dec_small.reset()
+    # token id out of range and position out of range are refused by the C ABI itself
+    from luce_megakernel_b200.model import _ptr
+    d = dec_small
+    args = [_ptr(d._out_token), _ptr(d._embed_weight), _ptr(d._layer_weights_packed), _ptr(d._final_norm_weight),
+            _ptr(d._lm_head_weight), _ptr(d._fa_k_cache), _ptr(d._fa_v_cache), _ptr(d._dn_states), _ptr(d._conv_bufs),
+            _ptr(d._hidden), _ptr(d._activations), _ptr(d._residual), _ptr(d._qkv_scratch), _ptr(d._kv_scratch),
+            _ptr(d._attn_out), _ptr(d._mlp_inter), _ptr(d._z_scratch), _ptr(d._beta_scratch), _ptr(d._alpha_scratch),
+            _ptr(d._normalized), _ptr(d._barrier_counter), _ptr(d._barrier_generation), _ptr(d._block_max_vals),
+            _ptr(d._block_max_idxs), _ptr(d._lm_sync_counter), _ptr(d._seen_token_mask)]
+    tail = lambda pos: [ctypes.c_float(1.0), ctypes.c_int(pos), ctypes.c_int(MAXSEQ), ctypes.c_void_p(0)]
+    assert lib.launch_decode(ctypes.c_int(V + 5), *args, *tail(0)) == 1
+    assert lib.launch_decode(ctypes.c_int(1), *args, *tail(MAXSEQ)) == 1
+    assert lib.launch_decode(ctypes.c_int(1), *args, *tail(-1)) == 1
+    assert b"position" in lib.mk_last_error_string()
+    torch.cuda.synchronize()
+    assert lib.mk_device_status() == 0
+
+
+def test_session_checkpoint_resume(dec_small):
+    prompt = seeded_prompt(16, seed=8)
+    dec_small.reset()
+    for t in prompt[:-1]:
+        dec_small.step_async(t)
+    ck = dec_small.state_dict()
+    a = dec_small.step_many(prompt[-1], 12).cpu().tolist()
+    dec_small.reset()
+    dec_small.load_state_dict(ck)
+    b = dec_small.step_many(prompt[-1], 12).cpu().tolist()
+    assert a == b
+
+
+@pytest.mark.parametrize("norm_init", ["unit", "literal"])
+def test_full_size_model_prompt32_greedy16(norm_init):
+    """The reference's CPU-runnable configuration: 24 layers, vocabulary 248320, seed 0,
+    32-token prompt then 16 greedy tokens, compared with the oracle step by step (teacher
+    forced).  "unit" reads "norm weights 1" as an effective RMSNorm weight of 1 and is held to
+    the plain bounds.  "literal" sets every norm tensor to 1.0, so each (1+w) norm doubles its
+    input, |hidden| reaches ~20 and one bf16 ulp of the residual stream is 0.125: there the
+    logit bound is the larger of 5e-2 and twice the distance between the oracle with the bf16
+    rounding points and the oracle without them (the noise any bf16 implementation carries)."""
+    from luce_megakernel_b200 import model as M
+    sd = O.init_weights(0, 24, O.VOCAB, norm_init=norm_init)
+    orc = O.Oracle(sd, rounding="decode")
+    o32 = O.Oracle(sd, rounding="none") if norm_init == "literal" else None
+    dec = M.Decoder(weights=M.weights_from_state_dict(sd), max_seq_len=64, api="cabi")
+    prompt = seeded_prompt(32, seed=0, vocab=O.VOCAB)
+    st, st32 = O.State.new(24, 64, O.VOCAB), O.State.new(24, 64, O.VOCAB)
+    for t in prompt[:-1]:
+        dec.step_async(t)
+    orc.forward(prompt[:-1], st, want_logits=False)
+    if o32 is not None:
+        o32.forward(prompt[:-1], st32, want_logits=False)
+    t = prompt[-1]
+    lm = sd["model.embed_tokens.weight"].float()
+    worst = 0.0
+    for i in range(16):
+        tok = dec.step(t)
+        tr = orc.forward([t], st)
+        ref_h = tr.hidden[-1][0]
+        eh = float((dec._hidden.float().cpu() - ref_h).abs().max())
+        assert eh <= hidden_tol(ref_h), f"step {i}: hidden error {eh}"
+        logit_tol = 5e-2
+        if o32 is not None:
+            noise = float((o32.forward([t], st32).logits - tr.logits).abs().max())
+            logit_tol = max(5e-2, 2.0 * noise)
+        el = float((lm @ dec._normalized.cpu() - tr.logits).abs().max())
+        worst = max(worst, el)
+        assert el <= logit_tol, f"step {i}: logit error {el} (bound {logit_tol})"
+        top = torch.topk(tr.logits, 2)
+        margin = float(top.values[0] - top.values[1])
+        assert tok == tr.token or (margin <= 2 * logit_tol and tok in top.indices.tolist()), \
+            f"step {i}: token {tok} vs {tr.token} (margin {margin})"
+        t = tr.token     # teacher forcing
+    print(f"{norm_init}: worst logit error {worst:.4g}")
