@@ -98,6 +98,43 @@ void mk_clear_error(void);
  * and stops at slots_per_cta entries.  Pass NULL to switch it off. */
 void mk_set_trace_buffer(unsigned long long *buf, int slots_per_cta);
 
+/* One greedy decode step that allocates nothing.  No counterpart in the reference.
+ *
+ * For hosts that cannot let a library allocate device memory: a server that gave all free HBM
+ * to its own pool at start-up (a later cudaMalloc fails), or a latency-critical loop that cannot
+ * take the device-wide synchronisation of cudaMalloc / cudaFree.  Same kernel and same results
+ * as launch_decode(), but the barrier words, argmax partials and attention partials live in a
+ * static __device__ array inside the library (about 132 KB on every GPU that loads it, held
+ * until the process exits) instead of a workspace allocated on first use; the call makes no
+ * cudaMalloc / cudaFree / cudaHostAlloc and no allocating library call.  The caller passes all
+ * inputs, outputs and the activation scratch vectors, as for launch_decode(); the model depth
+ * and vocabulary are arguments here instead of mk_set_model_dims() state.
+ *
+ * Limits: the array is sized for grids of at most MK_STATIC_SCRATCH_MAX_CTAS CTAs (one per SM)
+ * and num_layers <= 24; anything beyond is refused with MK_ERR_BAD_ARG and a message from
+ * mk_decode_bf16_static_scratch_error().
+ * First call on a device: resolves the array's device address (cudaGetSymbolAddress) and sizes
+ * the grid, with that device current; make that call before any stream capture.
+ * Sharing: every call on a device uses the same array and finds the previous call's contents
+ * there; the entry point clears the control words it needs at zero on `stream` before the
+ * launch.  Two calls that overlap on the GPU (different streams) race on the array: serialise
+ * them.  A device-side wait that runs out is not reported by this entry point (the status word
+ * of launch_decode() is itself an allocation); the next call re-arms the array. */
+#define MK_STATIC_SCRATCH_MAX_CTAS 256
+int mk_decode_bf16_static_scratch(
+    int input_token_id, int *output_token_id,
+    const void *embed_weight, const MkLayerWeights *layer_weights,
+    const void *final_norm_weight, const void *lm_head_weight,
+    void *fa_k_cache, void *fa_v_cache,
+    void *dn_states, void *conv_bufs,
+    void *hidden_buffer,
+    void *g_qkv_scratch, void *g_kv_scratch, void *g_attn_out,
+    void *g_mlp_inter, void *g_z_scratch, void *g_beta_scratch,
+    void *g_alpha_scratch, void *g_normalized,
+    float *seen_token_mask, float repetition_penalty,
+    int position, int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
+const char *mk_decode_bf16_static_scratch_error(void);
+
 #ifdef __cplusplus
 }
 #endif
