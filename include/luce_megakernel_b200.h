@@ -58,7 +58,8 @@ int launch_decode(
     int position, int max_seq_len, cudaStream_t stream);
 
 /* Resident-block ceiling and decode grid override
- * (reference: megakernel/kernel.cu:1012-1020, megakernel/torch_bindings.cpp:144-145). */
+ * (reference: megakernel/kernel.cu:1012-1020, megakernel/torch_bindings.cpp:144-145).
+ * The kernel runs one CTA per SM; overrides are clamped to [129, ceiling]. */
 void set_decode_blocks_override(int blocks);
 int query_max_safe_decode_blocks(void);
 
@@ -79,6 +80,20 @@ int mk_decode_many_bf16(
     void *g_alpha_scratch, void *g_normalized,
     float *seen_token_mask, float repetition_penalty,
     int position, int max_seq_len, cudaStream_t stream);
+
+/* NVFP4 weight quantisers, bit-exact to the reference's kernels.
+ * launch_quantize_nvfp4_out: layer-weight format (reference: megakernel/kernel_gb10_nvfp4.cu:1778-1817,
+ *   declared at megakernel/torch_bindings.cpp:108-110): weight bf16 [rows, cols] -> packed uint8
+ *   [rows, cols/2] (low nibble = even element) + fp16 scales [rows, cols/group_size].
+ * launch_quantize_nvfp4_lm_out: LM-head / tensor-core format (reference:
+ *   megakernel/kernel_gb10_nvfp4.cu:1373-1437, megakernel/torch_bindings.cpp:112-114): 16-element blocks,
+ *   E4M3 scales in 128-row x 4-column tiles of 512 bytes; rows % 128 == 0, cols % 64 == 0,
+ *   scales_out has (rows/128)*(cols/64)*512 bytes. */
+int launch_quantize_nvfp4_out(const void *weight, int rows, int cols, int group_size,
+                              void *packed_out, void *scales_out, cudaStream_t stream);
+int launch_quantize_nvfp4_lm_out(const void *weight, int rows, int cols,
+                                 void *packed_out, void *scales_out, cudaStream_t stream);
+const char *mk_quantize_error(void);
 
 /* Model depth and vocabulary the entry points assume (defaults 24 and 248320, the
  * compile-time constants of the reference: megakernel/kernel.cu:20,22).  Reduced values let
@@ -103,8 +118,8 @@ void mk_set_trace_buffer(unsigned long long *buf, int slots_per_cta);
  * For hosts that cannot let a library allocate device memory: a server that gave all free HBM
  * to its own pool at start-up (a later cudaMalloc fails), or a latency-critical loop that cannot
  * take the device-wide synchronisation of cudaMalloc / cudaFree.  Same kernel and same results
- * as launch_decode(), but the barrier words, argmax partials and attention partials live in a
- * static __device__ array inside the library (about 132 KB on every GPU that loads it, held
+ * as launch_decode(), but the activation exchange buffers, argmax partials and attention partials
+ * live in a static __device__ array inside the library (about 300 KB on every GPU that loads it, held
  * until the process exits) instead of a workspace allocated on first use; the call makes no
  * cudaMalloc / cudaFree / cudaHostAlloc and no allocating library call.  The caller passes all
  * inputs, outputs and the activation scratch vectors, as for launch_decode(); the model depth

@@ -49,7 +49,7 @@ int device_state(DeviceState** out) {
         e = cudaHostGetDevicePointer(&d.host_status_dev, d.host_status, 0);
         if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaHostGetDevicePointer", e);
         d.max_grid = mk::decode_max_grid();
-        if (d.max_grid <= 0) return set_err(MK_ERR_CUDA, "decode kernel does not fit on this device");
+        if (d.max_grid < mk::MIN_GRID) return set_err(MK_ERR_CUDA, "decode kernel needs at least 129 co-resident CTAs (one per SM)");
     }
     *out = &d;
     return MK_OK;
@@ -60,6 +60,7 @@ bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u)
 int decode_grid(const DeviceState& d) {
     int g = d.max_grid;
     if (g_blocks_override > 0 && g_blocks_override < g) g = g_blocks_override;
+    if (g < mk::MIN_GRID) g = mk::MIN_GRID;    // smaller grids would not fit a phase into the ring bookkeeping
     return g;
 }
 
@@ -146,6 +147,7 @@ int launch_decode(
     if ((rc = check_device_status(*d, stream))) return rc;
     mk::DecodeParams p = make_params(a, *d);
     p.token_ptr = nullptr; p.token_val = input_token_id; p.out_token = output_token_id;
+    mk::fill_rope(p);
     cudaError_t e = mk::launch_decode_kernel(p, decode_grid(*d), stream);
     if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
     return MK_OK;
@@ -181,6 +183,7 @@ int mk_decode_many_bf16(
         p.token_ptr = token_buffer; p.token_val = 0;
         p.out_token = output_tokens + s; p.token_feedback = token_buffer; p.out_tokens_slot = nullptr;
         p.position = position + s;
+        mk::fill_rope(p);
         cudaError_t e = mk::launch_decode_kernel(p, grid, stream);
         if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
     }

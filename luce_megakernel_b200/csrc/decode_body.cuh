@@ -1,0 +1,1061 @@
+// Device code of the decode megakernel.  Included twice by decode_bf16.cu, once per value of
+// MK_TRACE, inside a namespace of its own: the timeline stamps cost instruction-cache space, so
+// the variant without them is the one that normally runs.
+struct Ctx {
+    char* smem;
+    float* xs;            // scratch as floats
+    float* part;          // per-chunk, per-warp partial row sums (half in use by the current phase)
+    float* part_base;
+    uint32_t part_flip;
+    float* red;
+    volatile int* misc;
+    uint32_t full0, empty0, ring0;
+    int tid, warp, lane, cta, G;
+    uint32_t it;          // ring chunk counter (producer and consumers advance it identically)
+    uint32_t seq;         // launches completed before this one
+    uint32_t trace_slot;
+};
+
+// A bounded wait ran out (or another CTA reported one): from here on every wait of this CTA
+// returns at once and the launch drains; the status reaches the host when the kernel ends.
+// Kept tiny and inline: a call here would cost a register save/restore at every wait site.
+__device__ __forceinline__ void fail(const DecodeParams& P, Ctx& c, uint32_t code) {
+    c.misc[MISC_ABORT] = (int)code;
+    P.ws->abort_flag = 1u;
+}
+
+// Optional timeline: thread 0 of each CTA appends the global timer at four points of every phase.
+__device__ __forceinline__ void trace_point(const DecodeParams& P, Ctx& c) {
+    if (MK_TRACE && P.trace) {
+        if (c.tid == 0 && c.trace_slot < (uint32_t)P.trace_slots)
+            P.trace[(size_t)c.cta * P.trace_slots + c.trace_slot] = globaltimer_ns();
+        c.trace_slot++;
+    }
+}
+
+__device__ __forceinline__ void wait_full(const DecodeParams& P, Ctx& c, uint32_t stage, uint32_t parity) {
+    if (mbar_try_wait(c.full0 + stage * 8, parity)) return;
+    if (c.misc[MISC_ABORT]) return;
+    if (!mbar_wait(c.full0 + stage * 8, parity)) fail(P, c, ST_MBAR_TIMEOUT);
+}
+
+__device__ __forceinline__ void release_stage(Ctx& c, uint32_t stage) {
+    __syncwarp();
+    if (c.lane == 0) mbar_arrive(c.empty0 + stage * 8);
+}
+
+// ---- flagged activation words --------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t epoch_of(const Ctx& c, int layer) { return ((c.seq + 1u) << 5) | (uint32_t)(layer + 1); }
+
+__device__ __forceinline__ void st_flagged(unsigned long long* p, float v, uint32_t epoch) {
+    const unsigned long long w = ((unsigned long long)epoch << 32) | (unsigned long long)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_word(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ void ld_word2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Slow path of a poll (every 1024 failed tries): bounded to about 2 s of SM clock, gives up at
+// once if another CTA gave up.
+__device__ __forceinline__ bool poll_give_up(const DecodeParams& P, Ctx& c, uint64_t& t0) {
+    if (c.misc[MISC_ABORT]) return true;
+    const uint64_t now = (uint64_t)clock64();
+    if (t0 == 0) t0 = now;
+    if (now - t0 > 4000000000ull || *((volatile uint32_t*)&P.ws->abort_flag) != 0u) {
+        fail(P, c, ST_GRID_TIMEOUT);
+        return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ float poll1(const DecodeParams& P, Ctx& c, const unsigned long long* p, uint32_t epoch) {
+    unsigned long long w = ld_word(p);
+    if ((uint32_t)(w >> 32) != epoch) {
+        uint64_t t0 = 0;
+        uint32_t n = 0;
+        do {
+            if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
+            MK_POLL_BACKOFF();
+            w = ld_word(p);
+        } while ((uint32_t)(w >> 32) != epoch);
+    }
+    return __uint_as_float((uint32_t)w);
+}
+
+// two consecutive words (p must be 16-byte aligned)
+__device__ __forceinline__ float2 poll2(const DecodeParams& P, Ctx& c, const unsigned long long* p, uint32_t epoch) {
+    unsigned long long a, b;
+    ld_word2(p, a, b);
+    if ((uint32_t)(a >> 32) != epoch || (uint32_t)(b >> 32) != epoch) {
+        uint64_t t0 = 0;
+        uint32_t n = 0;
+        do {
+            if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
+            MK_POLL_BACKOFF();
+            ld_word2(p, a, b);
+        } while ((uint32_t)(a >> 32) != epoch || (uint32_t)(b >> 32) != epoch);
+    }
+    return make_float2(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b));
+}
+
+// Batched polls: all loads are issued before any epoch is checked, so the N words cost one
+// L2 round trip instead of N.  W = words per load (1 or 2); words of one load are consecutive.
+template <int N>
+__device__ __forceinline__ void poll1_batch(const DecodeParams& P, Ctx& c, const unsigned long long* const (&p)[N],
+                                            uint32_t epoch, float (&out)[N]) {
+    unsigned long long w[N];
+    uint64_t t0 = 0;
+    uint32_t n = 0;
+#pragma unroll 1
+    while (true) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) w[i] = ld_word(p[i]);
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(w[i] >> 32) == epoch);
+        if (ok) break;
+        if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
+        MK_POLL_BACKOFF();
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = __uint_as_float((uint32_t)w[i]);
+}
+
+template <int N>
+__device__ __forceinline__ void poll2_batch(const DecodeParams& P, Ctx& c, const unsigned long long* const (&p)[N],
+                                            uint32_t epoch, float2 (&out)[N]) {
+    unsigned long long a[N], b[N];
+    uint64_t t0 = 0;
+    uint32_t n = 0;
+#pragma unroll 1
+    while (true) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) ld_word2(p[i], a[i], b[i]);
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(a[i] >> 32) == epoch) && ((uint32_t)(b[i] >> 32) == epoch);
+        if (ok) break;
+        if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
+        MK_POLL_BACKOFF();
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = make_float2(__uint_as_float((uint32_t)a[i]), __uint_as_float((uint32_t)b[i]));
+}
+
+// ---- producer ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void producer_phase(const DecodeParams& P, Ctx& c, int type, const LayerWeights& lw, int dn_idx,
+                               uint64_t pol_stream, uint64_t pol_keep) {
+    const Geo g = phase_geo(type, c.cta, c.G, P.vocab);
+#pragma unroll 1
+    for (int q = 0; q < g.nchunks; ++q, ++c.it) {
+        if (c.misc[MISC_ABORT]) continue;
+        const uint32_t stage = c.it % NSTAGE, parity = (c.it / NSTAGE) & 1u;
+        if (c.lane == 0 && !mbar_wait(c.empty0 + stage * 8, parity ^ 1u)) fail(P, c, ST_MBAR_TIMEOUT);
+        __syncwarp();
+        const char* src = nullptr;
+        uint32_t dst_off = 0;
+        uint32_t bytes = chunk_slot_src(type, lw, P, g, q, c.lane, c.G, dn_idx, src, dst_off);
+        if (bytes && (((uintptr_t)src) & 15u)) { fail(P, c, ST_MISALIGNED); bytes = 0; }
+        const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
+        if (c.misc[MISC_ABORT]) continue;
+        // Consecutive slots whose sources and destinations are contiguous (consecutive rows of one
+        // matrix) travel as ONE bulk copy: the copy issue rate, not its size, limits a CTA.
+        const unsigned long long prev_src = __shfl_up_sync(0xffffffffu, (unsigned long long)(uintptr_t)src, 1);
+        const uint32_t prev_bytes = __shfl_up_sync(0xffffffffu, bytes, 1);
+        const uint32_t prev_dst = __shfl_up_sync(0xffffffffu, dst_off, 1);
+        const bool head = bytes && (c.lane == 0 || prev_bytes == 0 ||
+                                    prev_src + prev_bytes != (unsigned long long)(uintptr_t)src ||
+                                    prev_dst + prev_bytes != dst_off);
+        const uint32_t heads = __ballot_sync(0xffffffffu, head);
+        const uint32_t valid = __ballot_sync(0xffffffffu, bytes != 0);
+        const uint32_t above = (c.lane == 31) ? 0u : ~((2u << c.lane) - 1u);
+        const uint32_t stop = (heads | ~valid) & above;
+        const int end = stop ? (__ffs(stop) - 1) : 32;
+        if (c.lane == 0) mbar_expect_tx(c.full0 + stage * 8, total);
+        __syncwarp();
+        if (head)
+            bulk_g2s(c.ring0 + stage * STAGE_BYTES + dst_off, src, bytes * (uint32_t)(end - c.lane), c.full0 + stage * 8,
+                     type == T_DN_REC ? pol_keep : pol_stream);
+    }
+}
+
+// ---- tensor-core row products ---------------------------------------------------------------
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// An f32 activation is carried through the bf16 MMA as three bf16 terms that add up to it
+// exactly: each term keeps the next 8 leading mantissa bits (truncation, no rounding), so
+// hi + mid + lo == x.  The terms occupy MMA columns 0, 1, 2; columns 3..7 are zero.
+__device__ __forceinline__ void split3(float x, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+    hi = __float_as_uint(x) & 0xffff0000u;
+    const float r1 = x - __uint_as_float(hi);
+    mid = __float_as_uint(r1) & 0xffff0000u;
+    const float r2 = r1 - __uint_as_float(mid);
+    lo = __float_as_uint(r2) & 0xffff0000u;
+}
+
+// Staging of a warp's K-slice: three planes of XK bf16.  Elements e, e+1 (e even) as one word.
+__device__ __forceinline__ void stage_pair(uint32_t* xw, int e, float x0, float x1) {
+    uint32_t h0, m0, l0, h1, m1, l1;
+    split3(x0, h0, m0, l0);
+    split3(x1, h1, m1, l1);
+    xw[e >> 1] = __byte_perm(h0, h1, 0x7632);
+    xw[(XK >> 1) + (e >> 1)] = __byte_perm(m0, m1, 0x7632);
+    xw[XK + (e >> 1)] = __byte_perm(l0, l1, 0x7632);
+}
+__device__ __forceinline__ void stage_one(uint32_t* xw, int e, float x) {
+    uint32_t h, m, l;
+    split3(x, h, m, l);
+    unsigned short* p = reinterpret_cast<unsigned short*>(xw);
+    p[e] = (unsigned short)(h >> 16);
+    p[XK + e] = (unsigned short)(m >> 16);
+    p[2 * XK + e] = (unsigned short)(l >> 16);
+}
+
+// B fragments of this warp's K-slice.  Thread (g = lane/4, t = lane%4) reads the 16-byte weight
+// chunks t, t+4, ... of a row, i.e. elements 8(t+4i)..+7; chunk i feeds MMA 2i (first four
+// elements) and MMA 2i+1 (last four).  The k order inside an MMA is a permutation shared by both
+// operands, so any consistent assignment is valid: the same 16 bytes of plane g are the B words.
+template <int NLOAD>
+__device__ __forceinline__ void load_bfrags(const uint32_t* xw, int lane, uint32_t (&b)[2 * NLOAD][2]) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t* plane = xw + (g < 3 ? g : 0) * (XK >> 1);
+#pragma unroll
+    for (int i = 0; i < NLOAD; ++i) {
+        uint4 v = *reinterpret_cast<const uint4*>(plane + 4 * (t + 4 * i));
+        if (g >= 3) v = make_uint4(0, 0, 0, 0);
+        b[2 * i][0] = v.x; b[2 * i][1] = v.y;
+        b[2 * i + 1][0] = v.z; b[2 * i + 1][1] = v.w;
+    }
+}
+
+// One ring chunk times the activation: rows of `rowbytes` bytes, this warp's K-slice starting
+// `kofs` bytes into each row.  ROWS = 16: tile rows g and g+8; ROWS = 8: row g; ROWS = 4: rows g < 4.
+// Odd g read their chunks rotated by one so that the two rows of a quarter-warp hit different
+// banks (all rows alias: the row stride is a multiple of 128 bytes).  Writes the warp's partial
+// sums of tile rows into `out[0..15]`.
+template <int NLOAD, int ROWS>
+__device__ __forceinline__ void mma_chunk(const char* stage, int rowbytes, int kofs, int lane,
+                                          const uint32_t (&b)[2 * NLOAD][2], float* out) {
+    const int g = lane >> 2, t = lane & 3, odd = g & 1;
+    const bool live = (ROWS >= 8) || (g < 4);
+    const char* r0 = stage + g * rowbytes + kofs + 16 * t;
+    const char* r1 = r0 + 8 * rowbytes;
+    uint4 A0[NLOAD], A1[NLOAD];
+#pragma unroll
+    for (int s = 0; s < NLOAD; ++s) {
+        int i = s + odd;
+        if (i >= NLOAD) i -= NLOAD;
+        A0[s] = live ? *reinterpret_cast<const uint4*>(r0 + 64 * i) : make_uint4(0, 0, 0, 0);
+        if (ROWS == 16) A1[s] = *reinterpret_cast<const uint4*>(r1 + 64 * i);
+        else A1[s] = make_uint4(0, 0, 0, 0);
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < NLOAD; ++i) {
+        constexpr int N = NLOAD;
+        const int so = (i + N - 1) % N;      // slot holding chunk i for odd g
+        uint4 a, d;
+        a.x = odd ? A0[so].x : A0[i].x; a.y = odd ? A0[so].y : A0[i].y;
+        a.z = odd ? A0[so].z : A0[i].z; a.w = odd ? A0[so].w : A0[i].w;
+        if (ROWS == 16) {
+            d.x = odd ? A1[so].x : A1[i].x; d.y = odd ? A1[so].y : A1[i].y;
+            d.z = odd ? A1[so].z : A1[i].z; d.w = odd ? A1[so].w : A1[i].w;
+        } else {
+            d = make_uint4(0, 0, 0, 0);
+        }
+        mma_bf16_16816(acc, a.x, d.x, a.y, d.y, b[2 * i][0], b[2 * i][1]);
+        mma_bf16_16816(acc2, a.z, d.z, a.w, d.w, b[2 * i + 1][0], b[2 * i + 1][1]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] += acc2[k];
+    // columns 0,1 (hi, mid) sit in the t = 0 lane, column 2 (lo) in the t = 1 lane
+    float s0 = acc[0] + (t == 0 ? acc[1] : 0.f);
+    float s1 = acc[2] + (t == 0 ? acc[3] : 0.f);
+    s0 += __shfl_down_sync(0xffffffffu, s0, 1);
+    s1 += __shfl_down_sync(0xffffffffu, s1, 1);
+    if (t == 0) {
+        out[g] = s0;
+        if (ROWS == 16) out[g + 8] = s1;
+    }
+}
+
+// Runs all chunks of a phase; partial sums land in part[(q * 16 + warp) * 16 + tile_row].
+template <int NLOAD, int ROWS>
+__device__ __forceinline__ void mma_phase(const DecodeParams& P, Ctx& c, int nchunks_in, int rowbytes) {
+    int nchunks = nchunks_in;
+    // alternate halves: a slow warp may still be reading the previous phase's sums in its epilogue
+    c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
+    uint32_t b[2 * NLOAD][2];
+    load_bfrags<NLOAD>(reinterpret_cast<const uint32_t*>(c.xs) + c.warp * XSW, c.lane, b);
+    const int kofs = c.warp * NLOAD * 64;      // 32*NLOAD elements of 2 bytes
+    if (nchunks > 4) { fail(P, c, ST_MISALIGNED); nchunks = 4; }   // never reached for grids >= MIN_GRID
+    if (nchunks > 0) wait_full(P, c, c.it % NSTAGE, (c.it / NSTAGE) & 1u);
+#pragma unroll 1
+    for (int q = 0; q < nchunks; ++q, ++c.it) {
+        const uint32_t stage = c.it % NSTAGE;
+        mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + stage * STAGE_BYTES, rowbytes, kofs, c.lane, b,
+                               c.part + (q * NCW + c.warp) * 16);
+        release_stage(c, stage);
+        // the mbarrier test of the next chunk overlaps the tail of this chunk's MMAs
+        if (q + 1 < nchunks) wait_full(P, c, (c.it + 1) % NSTAGE, ((c.it + 1) / NSTAGE) & 1u);
+    }
+}
+
+__device__ __forceinline__ float part_sum(const Ctx& c, int q, int row) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) s += c.part[(q * NCW + w) * 16 + row];
+    return s;
+}
+
+// ---- activation staging -----------------------------------------------------------------
+
+__device__ __forceinline__ void load_norm_w(const void* w, int tid, float& w0, float& w1) {
+    const uint32_t raw = __ldg(reinterpret_cast<const uint32_t*>(w) + tid);
+    w0 = 1.0f + bf_lo(raw);
+    w1 = 1.0f + bf_hi(raw);
+}
+
+// Thread tid fetches elements (2 tid, 2 tid + 1) of the residual stream: from the embedding row
+// for the first layer, else from the flagged words of the previous down-projection.
+__device__ __forceinline__ float2 fetch_hidden2(const DecodeParams& P, Ctx& c, const __nv_bfloat16* embed_row,
+                                                const unsigned long long* words, uint32_t epoch) {
+    if (embed_row) {
+        const uint32_t raw = __ldg(reinterpret_cast<const uint32_t*>(embed_row) + c.tid);
+        return make_float2(bf_lo(raw), bf_hi(raw));
+    }
+    return poll2(P, c, words + 2 * c.tid, epoch);
+}
+
+// RMSNorm of the 1024-vector held two elements per thread; result (optionally rounded to bf16)
+// goes to this warp's staging slice, whose 64 elements are exactly the warp's K-slice.
+// reference: megakernel/kernel.cu:189-231
+__device__ __forceinline__ float2 rmsnorm_to_slice(Ctx& c, float2 v, float w0, float w1, bool round_to_bf16) {
+    const float ss = warp_sum(v.x * v.x + v.y * v.y);
+    if (c.lane == 0) c.red[c.warp] = ss;
+    named_bar_sync(1, NCT);
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) tot += c.red[i];
+    const float rstd = rsqrtf(tot * (1.0f / HIDDEN) + RMS_EPS);
+    float x0 = v.x * rstd * w0, x1 = v.y * rstd * w1;
+    if (round_to_bf16) { x0 = round_bf16(x0); x1 = round_bf16(x1); }
+    stage_pair(reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW, 2 * c.lane, x0, x1);
+    __syncwarp();
+    return make_float2(x0, x1);
+}
+
+// ---- phases -----------------------------------------------------------------------------
+
+__device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer, int dn_idx,
+                            const __nv_bfloat16* embed_row) {
+    const Geo g = phase_geo(T_DN_IN, c.cta, c.G, P.vocab);
+    const int nloc = g.r1 - g.r0;
+    const uint32_t ep = epoch_of(c, layer);
+    trace_point(P, c);
+    float w0, w1;
+    load_norm_w(lw.ptrs[DN_IN_NORM], c.tid, w0, w1);
+    // epilogue inputs that do not depend on this token: conv window and taps of the row this thread finishes
+    const int r = g.r0 + c.tid;
+    float4 cs = make_float4(0, 0, 0, 0);
+    uint2 cw = make_uint2(0, 0);
+    float a_log = 0.f, dt_b = 0.f;
+    float* conv_row = nullptr;
+    if (c.tid < nloc) {
+        if (r < DN_CONV_CH) {
+            conv_row = P.conv_bufs + ((size_t)dn_idx * DN_CONV_CH + r) * DN_CONV_K;
+            cs = __ldcg(reinterpret_cast<const float4*>(conv_row));
+            cw = __ldg(reinterpret_cast<const uint2*>(lw.ptrs[DN_CONV_W]) + r);
+        } else if (r >= DN_CONV_CH + DN_V + DN_HEADS) {
+            const int h = r - (DN_CONV_CH + DN_V + DN_HEADS);
+            a_log = bf2f(reinterpret_cast<const __nv_bfloat16*>(lw.ptrs[DN_A_LOG])[h]);
+            dt_b = bf2f(reinterpret_cast<const __nv_bfloat16*>(lw.ptrs[DN_DT_BIAS])[h]);
+        }
+    }
+    const float2 v = fetch_hidden2(P, c, embed_row, P.ws->x_hidden[1], epoch_of(c, layer - 1));
+    rmsnorm_to_slice(c, v, w0, w1, true);
+    trace_point(P, c);
+    mma_phase<2, 16>(P, c, g.nchunks, HIDDEN * 2);
+    trace_point(P, c);
+    named_bar_sync(1, NCT);
+    if (c.tid < nloc) {
+        const float val = part_sum(c, c.tid >> 4, c.tid & 15);
+        if (r < DN_CONV_CH) {
+            // shift the 4-tap window, append, dot with the taps, SiLU (reference: megakernel/kernel.cu:640-646)
+            const float4 ns = make_float4(cs.y, cs.z, cs.w, val);
+            *reinterpret_cast<float4*>(conv_row) = ns;
+            const float co = ns.x * bf_lo(cw.x) + ns.y * bf_hi(cw.x) + ns.z * bf_lo(cw.y) + ns.w * bf_hi(cw.y);
+            st_flagged(P.ws->x_dnin + r, silu_f(co), ep);
+        } else if (r < DN_CONV_CH + DN_V) {
+            st_flagged(P.ws->x_dnin + r, val, ep);
+        } else if (r < DN_CONV_CH + DN_V + DN_HEADS) {
+            st_flagged(P.ws->x_dnin + r, 1.0f / (1.0f + expf(-val)), ep);
+        } else {
+            // decay = exp(-exp(A_log) * softplus(a + dt_bias)) (reference: megakernel/kernel.cu:653-657)
+            const float x = val + dt_b;
+            const float sp = (x > 20.0f) ? x : log1pf(expf(x));
+            st_flagged(P.ws->x_dnin + r, expf(-expf(a_log) * sp), ep);
+        }
+    }
+    trace_point(P, c);
+}
+
+// Gated delta rule for one token; unit = (head, 16 value rows), one warp per value row.
+// State row j is contiguous over the key index (reference: megakernel/kernel.cu:686-713).
+// The unit's inputs (q and k of the head, 16 v values, beta, decay) are fetched once per CTA --
+// one word pair per thread -- and shared through shared memory: every REC CTA polling every word
+// with every warp would put thousands of pollers on the same few L2 lines.
+__device__ __forceinline__ void phase_dn_rec(const DecodeParams& P, Ctx& c, int layer, int dn_idx) {
+    const Geo g = phase_geo(T_DN_REC, c.cta, c.G, P.vocab);
+    const uint32_t ep = epoch_of(c, layer);
+    float* sh = c.xs;        // [0,128) q, [128,256) k, [256,272) v, [272] beta, [273] decay
+    trace_point(P, c);
+#pragma unroll 1
+    for (int qi = 0; qi < g.nchunks; ++qi, ++c.it) {
+        const uint32_t stage = c.it % NSTAGE, parity = (c.it / NSTAGE) & 1u;
+        const int u = g.r0 + qi * c.G;
+        const int h = u >> 3, j0 = (u & 7) * 16;
+        const unsigned long long* X = P.ws->x_dnin;
+        if (c.tid < 128) {
+            const unsigned long long* src = (c.tid < 64) ? X + h * DN_KEY + 2 * c.tid
+                                                         : X + DN_QK + h * DN_KEY + 2 * (c.tid - 64);
+            const float2 v = poll2(P, c, src, ep);
+            reinterpret_cast<float2*>(sh)[c.tid] = v;
+        } else if (c.tid < 128 + 18) {
+            const int k = c.tid - 128;
+            const unsigned long long* src = (k < 16) ? X + 2 * DN_QK + h * DN_VAL + j0 + k
+                                           : (k == 16) ? X + DN_CONV_CH + DN_V + h
+                                                       : X + DN_CONV_CH + DN_V + DN_HEADS + h;
+            sh[256 + k] = poll1(P, c, src, ep);
+        }
+        named_bar_sync(1, NCT);
+        const int j = j0 + c.warp;
+        const float4 q4 = reinterpret_cast<const float4*>(sh)[c.lane];
+        const float4 k4 = reinterpret_cast<const float4*>(sh + 128)[c.lane];
+        const float vj = sh[256 + c.warp], beta = sh[272], decay = sh[273];
+        float sq = q4.x * q4.x + q4.y * q4.y + q4.z * q4.z + q4.w * q4.w;
+        float sk = k4.x * k4.x + k4.y * k4.y + k4.z * k4.z + k4.w * k4.w;
+        float kq = q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w;
+        sq = warp_sum(sq); sk = warp_sum(sk); kq = warp_sum(kq);
+        const float qn = rsqrtf(sq + 1e-6f) * 0.08838834764831845f;   // 1/sqrt(128)
+        const float kn = rsqrtf(sk + 1e-6f);
+        kq *= qn * kn;
+        if (qi == 0) trace_point(P, c);
+        wait_full(P, c, stage, parity);
+        const float4 s4 = *reinterpret_cast<const float4*>(c.smem + OFF_RING + stage * STAGE_BYTES +
+                                                           (c.warp * DN_KEY + c.lane * 4) * 4);
+        float stk = (s4.x * k4.x + s4.y * k4.y + s4.z * k4.z + s4.w * k4.w) * kn;
+        float sqv = (s4.x * q4.x + s4.y * q4.y + s4.z * q4.z + s4.w * q4.w) * qn;
+        stk = warp_sum(stk); sqv = warp_sum(sqv);
+        const float err = (vj - decay * stk) * beta;
+        const float ek = err * kn;
+        float4 sn;
+        sn.x = s4.x * decay + k4.x * ek; sn.y = s4.y * decay + k4.y * ek;
+        sn.z = s4.z * decay + k4.z * ek; sn.w = s4.w * decay + k4.w * ek;
+        float* srow = P.dn_states + ((size_t)(dn_idx * DN_HEADS + h) * DN_VAL + j) * DN_KEY;
+        reinterpret_cast<float4*>(srow)[c.lane] = sn;
+        if (c.lane == 0) st_flagged(P.ws->x_o + h * DN_VAL + j, decay * sqv + err * kq, ep);
+        if (qi == 0) trace_point(P, c);
+        release_stage(c, stage);
+        if (qi + 1 < g.nchunks) named_bar_sync(1, NCT);     // the shared inputs are rewritten by the next unit
+    }
+    if (g.nchunks == 0) { trace_point(P, c); trace_point(P, c); }
+    trace_point(P, c);
+}
+
+// out-projection (K = 2048, 8 rows per chunk) + residual -> bf16-rounded hidden words
+__device__ __forceinline__ void outproj_rows(const DecodeParams& P, Ctx& c, const Geo& g, int type, float resid, uint32_t ep) {
+    (void)type;
+    const int nloc = g.r1 - g.r0;
+    mma_phase<4, 8>(P, c, g.nchunks, 2048 * 2);
+    trace_point(P, c);
+    named_bar_sync(1, NCT);
+    if (c.tid < nloc) {
+        const float y = part_sum(c, c.tid >> 3, c.tid & 7) + resid;
+        st_flagged(P.ws->x_hidden[0] + g.r0 + c.tid, round_bf16(y), ep);
+    }
+    trace_point(P, c);
+}
+
+__device__ __forceinline__ float fetch_resid_in(const DecodeParams& P, Ctx& c, const __nv_bfloat16* embed_row, int row,
+                                                int layer) {
+    if (embed_row) return bf2f(embed_row[row]);
+    return poll1(P, c, P.ws->x_hidden[1] + row, epoch_of(c, layer - 1));
+}
+
+// out-proj of a DeltaNet layer; staging fuses the gated RMSNorm (plain weight) * SiLU(z): warp w
+// owns head w, whose 128 values are exactly its K-slice (reference: megakernel/kernel.cu:715-741)
+__device__ __forceinline__ void phase_dn_out(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer,
+                             const __nv_bfloat16* embed_row) {
+    const Geo g = phase_geo(T_DN_OUT, c.cta, c.G, P.vocab);
+    const uint32_t ep = epoch_of(c, layer);
+    trace_point(P, c);
+    const uint2 nwr = __ldg(reinterpret_cast<const uint2*>(lw.ptrs[DN_NORM_W]) + c.lane);
+    float resid = 0.f;
+    if (c.tid < g.r1 - g.r0) resid = fetch_resid_in(P, c, embed_row, g.r0 + c.tid, layer);
+    {
+        const int h = c.warp;
+        const unsigned long long* Z = P.ws->x_dnin + DN_CONV_CH + h * DN_VAL + 4 * c.lane;
+        const unsigned long long* O = P.ws->x_o + h * DN_VAL + 4 * c.lane;
+        const unsigned long long* const p2[4] = {Z, Z + 2, O, O + 2};
+        float2 v2[4];
+        poll2_batch<4>(P, c, p2, ep, v2);
+        const float2 za = v2[0], zb = v2[1], oa = v2[2], ob = v2[3];
+        const float ss = warp_sum(oa.x * oa.x + oa.y * oa.y + ob.x * ob.x + ob.y * ob.y);
+        const float rstd = rsqrtf(ss * (1.0f / DN_VAL) + RMS_EPS);
+        float4 x;
+        x.x = oa.x * rstd * bf_lo(nwr.x) * silu_f(za.x);
+        x.y = oa.y * rstd * bf_hi(nwr.x) * silu_f(za.y);
+        x.z = ob.x * rstd * bf_lo(nwr.y) * silu_f(zb.x);
+        x.w = ob.y * rstd * bf_hi(nwr.y) * silu_f(zb.y);
+        uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
+        stage_pair(xw, 4 * c.lane, x.x, x.y);
+        stage_pair(xw, 4 * c.lane + 2, x.z, x.w);
+        __syncwarp();
+    }
+    trace_point(P, c);
+    outproj_rows(P, c, g, T_DN_OUT, resid, ep);
+}
+
+__device__ __forceinline__ void phase_fa_in(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer,
+                            const __nv_bfloat16* embed_row) {
+    const Geo g = phase_geo(T_FA_IN, c.cta, c.G, P.vocab);
+    const int nloc = g.r1 - g.r0;
+    const uint32_t ep = epoch_of(c, layer);
+    trace_point(P, c);
+    float w0, w1;
+    load_norm_w(lw.ptrs[FA_IN_NORM], c.tid, w0, w1);
+    const float2 v = fetch_hidden2(P, c, embed_row, P.ws->x_hidden[1], epoch_of(c, layer - 1));
+    rmsnorm_to_slice(c, v, w0, w1, true);
+    trace_point(P, c);
+    mma_phase<2, 16>(P, c, g.nchunks, HIDDEN * 2);
+    trace_point(P, c);
+    named_bar_sync(1, NCT);
+    if (c.tid < nloc)      // rows 0..4095: per head [q(256) | gate(256)]; then k[512], v[512]
+        st_flagged(P.ws->x_fain + g.r0 + c.tid, part_sum(c, c.tid >> 4, c.tid & 15), ep);
+    trace_point(P, c);
+}
+
+__device__ __forceinline__ int att_num_chunks(int L) {
+    int nc = (L + ATT_CHUNK_POS - 1) / ATT_CHUNK_POS;
+    return nc < 1 ? 1 : (nc > ATT_MAX_CHUNKS ? ATT_MAX_CHUNKS : nc);
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
+    f[0] = bf_lo(u.x); f[1] = bf_hi(u.x); f[2] = bf_lo(u.y); f[3] = bf_hi(u.y);
+    f[4] = bf_lo(u.z); f[5] = bf_hi(u.z); f[6] = bf_lo(u.w); f[7] = bf_hi(u.w);
+}
+
+// per-head RMSNorm(1+w) + partial RoPE on lane-strided dims d = lane + 32 e
+// (dims i and i+32 of the rotary pair sit in the same lane).  reference: megakernel/kernel.cu:462-499
+__device__ __forceinline__ void head_norm_rope(const DecodeParams& P, Ctx& c, const unsigned long long* src, uint32_t ep,
+                                               const void* wn, int pos, float* n) {
+    float ss = 0.f;
+    {
+        const unsigned long long* b0 = src + c.lane;
+        const unsigned long long* const p1[8] = {b0, b0 + 32, b0 + 64, b0 + 96, b0 + 128, b0 + 160, b0 + 192, b0 + 224};
+        float v[8];
+        poll1_batch<8>(P, c, p1, ep, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { n[e] = v[e]; ss += v[e] * v[e]; }
+    }
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss * (1.0f / FA_HEAD_DIM) + RMS_EPS);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+        n[e] = n[e] * rstd * (1.0f + bf2f(reinterpret_cast<const __nv_bfloat16*>(wn)[c.lane + 32 * e]));
+    (void)pos;
+    const float sn = P.rope_sin[c.lane], cs = P.rope_cos[c.lane];   // host-computed for this position
+    const float a = n[0], b = n[1];
+    n[0] = a * cs - b * sn;
+    n[1] = b * cs + a * sn;
+}
+
+// Split-KV decode attention.  Unit = (KV head, position chunk); the 4 query heads of a KV head
+// share every K/V load.  Each unit leaves (m, l, o[256]) per head in the workspace and then
+// publishes its ready word; the o-proj phase merges the chunks.  reference: megakernel/kernel.cu:506-560
+__device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer, int fa_idx) {
+    const int pos = P.position, L = pos + 1;
+    const int NC = att_num_chunks(L);
+    const int per = (L + NC - 1) / NC;
+    const uint32_t ep = epoch_of(c, layer);
+    float* slots = c.xs;                 // 4 slots x 4 heads x 260 floats
+    float* qs = c.xs + 4160;             // 4 heads x 256 floats
+    trace_point(P, c);
+    trace_point(P, c);
+#pragma unroll 1
+    for (int u = c.cta; u < FA_KV_HEADS * NC; u += c.G) {
+        const int g = u / NC, ch = u % NC;
+        const int p_lo = ch * per, p_hi = min(L, p_lo + per);
+        const bool owner = (pos >= p_lo && pos < p_hi);
+        __nv_bfloat16* Kb = reinterpret_cast<__nv_bfloat16*>(P.k_cache) + (size_t)(fa_idx * FA_KV_HEADS + g) * P.max_seq_len * FA_HEAD_DIM;
+        __nv_bfloat16* Vb = reinterpret_cast<__nv_bfloat16*>(P.v_cache) + (size_t)(fa_idx * FA_KV_HEADS + g) * P.max_seq_len * FA_HEAD_DIM;
+        if (c.warp < 4) {
+            float n[8];
+            head_norm_rope(P, c, P.ws->x_fain + (g * FA_GQA + c.warp) * 2 * FA_HEAD_DIM, ep, lw.ptrs[FA_Q_NORM], pos, n);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qs[c.warp * FA_HEAD_DIM + c.lane + 32 * e] = n[e];
+        } else if (c.warp == 4 && owner) {
+            float n[8];
+            head_norm_rope(P, c, P.ws->x_fain + FA_QPROJ + g * FA_HEAD_DIM, ep, lw.ptrs[FA_K_NORM], pos, n);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) Kb[(size_t)pos * FA_HEAD_DIM + c.lane + 32 * e] = __float2bfloat16_rn(n[e]);
+        } else if (c.warp == 5 && owner) {
+            const unsigned long long* b0 = P.ws->x_fain + FA_QPROJ + FA_KV_SIZE + g * FA_HEAD_DIM + c.lane;
+            const unsigned long long* const p1[8] = {b0, b0 + 32, b0 + 64, b0 + 96, b0 + 128, b0 + 160, b0 + 192, b0 + 224};
+            float v[8];
+            poll1_batch<8>(P, c, p1, ep, v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) Vb[(size_t)pos * FA_HEAD_DIM + c.lane + 32 * e] = __float2bfloat16_rn(v[e]);
+        }
+        __threadfence_block();
+        named_bar_sync(1, NCT);
+
+        float qr[4][8], acc[4][8], m[4], l[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            m[h] = -1e30f; l[h] = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) { qr[h][e] = qs[h * FA_HEAD_DIM + c.lane * 8 + e] * 0.0625f; acc[h][e] = 0.f; }
+        }
+        int p = p_lo + c.warp;
+        uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+        if (p < p_hi) {
+            kk = __ldcg(reinterpret_cast<const uint4*>(Kb + (size_t)p * FA_HEAD_DIM) + c.lane);
+            vv = __ldcg(reinterpret_cast<const uint4*>(Vb + (size_t)p * FA_HEAD_DIM) + c.lane);
+        }
+#pragma unroll 1
+        while (p < p_hi) {
+            const int pn = p + NCW;
+            uint4 kn = make_uint4(0, 0, 0, 0), vn = make_uint4(0, 0, 0, 0);
+            if (pn < p_hi) {
+                kn = __ldcg(reinterpret_cast<const uint4*>(Kb + (size_t)pn * FA_HEAD_DIM) + c.lane);
+                vn = __ldcg(reinterpret_cast<const uint4*>(Vb + (size_t)pn * FA_HEAD_DIM) + c.lane);
+            }
+            float kf[8], vf[8], s[4];
+            unpack8(kk, kf);
+            unpack8(vv, vf);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) d = fmaf(qr[h][e], kf[e], d);
+                s[h] = d;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int h = 0; h < 4; ++h) s[h] += __shfl_xor_sync(0xffffffffu, s[h], o);
+            }
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const float mn = fmaxf(m[h], s[h]);
+                const float corr = __expf(m[h] - mn), pe = __expf(s[h] - mn);
+                l[h] = l[h] * corr + pe;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[h][e] = acc[h][e] * corr + pe * vf[e];
+                m[h] = mn;
+            }
+            kk = kn; vv = vn; p = pn;
+        }
+
+        // merge the 16 warps' partial softmax states: three rounds into warps 0-3, then per head
+#pragma unroll 1
+        for (int r = 1; r <= 3; ++r) {
+            if (c.warp >= 4 * r && c.warp < 4 * r + 4) {
+                const int sl = c.warp - 4 * r;
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    float* d = slots + (sl * 4 + h) * ATT_PART_STRIDE;
+                    if (c.lane == 0) { d[0] = m[h]; d[1] = l[h]; }
+                    *reinterpret_cast<float4*>(d + 4 + c.lane * 8) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+                    *reinterpret_cast<float4*>(d + 8 + c.lane * 8) = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+                }
+            }
+            named_bar_sync(1, NCT);
+            if (c.warp < 4) {
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const float* d = slots + (c.warp * 4 + h) * ATT_PART_STRIDE;
+                    const float m2 = d[0], l2 = d[1];
+                    const float4 a = *reinterpret_cast<const float4*>(d + 4 + c.lane * 8);
+                    const float4 b = *reinterpret_cast<const float4*>(d + 8 + c.lane * 8);
+                    const float mn = fmaxf(m[h], m2);
+                    const float f1 = __expf(m[h] - mn), f2 = __expf(m2 - mn);
+                    l[h] = l[h] * f1 + l2 * f2;
+                    acc[h][0] = acc[h][0] * f1 + a.x * f2; acc[h][1] = acc[h][1] * f1 + a.y * f2;
+                    acc[h][2] = acc[h][2] * f1 + a.z * f2; acc[h][3] = acc[h][3] * f1 + a.w * f2;
+                    acc[h][4] = acc[h][4] * f1 + b.x * f2; acc[h][5] = acc[h][5] * f1 + b.y * f2;
+                    acc[h][6] = acc[h][6] * f1 + b.z * f2; acc[h][7] = acc[h][7] * f1 + b.w * f2;
+                    m[h] = mn;
+                }
+            }
+            named_bar_sync(1, NCT);
+        }
+        if (c.warp < 4) {
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                float* d = slots + (c.warp * 4 + h) * ATT_PART_STRIDE;
+                if (c.lane == 0) { d[0] = m[h]; d[1] = l[h]; }
+                *reinterpret_cast<float4*>(d + 4 + c.lane * 8) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+                *reinterpret_cast<float4*>(d + 8 + c.lane * 8) = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+            }
+        }
+        named_bar_sync(1, NCT);
+        if (c.warp < 4) {
+            const int h = c.warp;
+            float M = -1e30f;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) M = fmaxf(M, slots[(s * 4 + h) * ATT_PART_STRIDE]);
+            float lt = 0.f, o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const float* d = slots + (s * 4 + h) * ATT_PART_STRIDE;
+                const float f = __expf(d[0] - M);
+                lt += d[1] * f;
+                const float4 a = *reinterpret_cast<const float4*>(d + 4 + c.lane * 8);
+                const float4 b = *reinterpret_cast<const float4*>(d + 8 + c.lane * 8);
+                o[0] += a.x * f; o[1] += a.y * f; o[2] += a.z * f; o[3] += a.w * f;
+                o[4] += b.x * f; o[5] += b.y * f; o[6] += b.z * f; o[7] += b.w * f;
+            }
+            float* dst = P.ws->attn_part + ((size_t)(g * FA_GQA + h) * ATT_MAX_CHUNKS + ch) * ATT_PART_STRIDE;
+            if (c.lane == 0) { dst[0] = M; dst[1] = lt; }
+            *reinterpret_cast<float4*>(dst + 4 + c.lane * 8) = make_float4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<float4*>(dst + 8 + c.lane * 8) = make_float4(o[4], o[5], o[6], o[7]);
+        }
+        named_bar_sync(1, NCT);
+        if (c.tid == 0)       // the partials of this unit are complete: publish (release orders the CTA's stores)
+            asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(P.ws->att_ready + u), "r"(ep) : "memory");
+    }
+    trace_point(P, c);
+    trace_point(P, c);
+}
+
+// o-proj of an attention layer; staging waits for the attention units, merges their chunks and
+// applies the sigmoid gate: warp w owns dims (w&1)*128.. of head w/2, which is its K-slice
+// (reference: megakernel/kernel.cu:542-570)
+__device__ __forceinline__ void phase_fa_out(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer,
+                             const __nv_bfloat16* embed_row) {
+    (void)lw;
+    const Geo g = phase_geo(T_FA_OUT, c.cta, c.G, P.vocab);
+    const int NC = att_num_chunks(P.position + 1);
+    const uint32_t ep = epoch_of(c, layer);
+    trace_point(P, c);
+    float resid = 0.f;
+    if (c.tid < g.r1 - g.r0) resid = fetch_resid_in(P, c, embed_row, g.r0 + c.tid, layer);
+    {
+        const int head = c.warp >> 1, d4 = (c.warp & 1) * 128 + 4 * c.lane;
+        const unsigned long long* G4 = P.ws->x_fain + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM + d4;
+        const float2 ga = poll2(P, c, G4, ep), gb = poll2(P, c, G4 + 2, ep);
+        if (c.warp == 0 && c.lane < FA_KV_HEADS * NC) {   // one warp waits for the attention units of this layer
+            uint64_t t0 = 0;
+            uint32_t n = 0;
+            while (ld_acquire_gpu(P.ws->att_ready + c.lane) != ep)
+                if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
+        }
+        named_bar_sync(1, NCT);
+        const float* part = P.ws->attn_part + (size_t)head * ATT_MAX_CHUNKS * ATT_PART_STRIDE;
+        float mv[ATT_MAX_CHUNKS];
+        float M = -1e30f;
+#pragma unroll
+        for (int ch = 0; ch < ATT_MAX_CHUNKS; ++ch) {
+            mv[ch] = (ch < NC) ? __ldcg(part + ch * ATT_PART_STRIDE) : -1e30f;
+            M = fmaxf(M, mv[ch]);
+        }
+        float den = 0.f;
+        float4 o = make_float4(0, 0, 0, 0);
+#pragma unroll
+        for (int ch = 0; ch < ATT_MAX_CHUNKS; ++ch) {
+            if (ch < NC) {
+                const float f = __expf(mv[ch] - M);
+                den += __ldcg(part + ch * ATT_PART_STRIDE + 1) * f;
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(part + ch * ATT_PART_STRIDE + 4 + d4));
+                o.x += a.x * f; o.y += a.y * f; o.z += a.z * f; o.w += a.w * f;
+            }
+        }
+        const float inv = 1.0f / den;
+        float4 x;
+        x.x = o.x * inv * sigmoid_f(ga.x); x.y = o.y * inv * sigmoid_f(ga.y);
+        x.z = o.z * inv * sigmoid_f(gb.x); x.w = o.w * inv * sigmoid_f(gb.y);
+        uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
+        stage_pair(xw, 4 * c.lane, x.x, x.y);
+        stage_pair(xw, 4 * c.lane + 2, x.z, x.w);
+        __syncwarp();
+    }
+    trace_point(P, c);
+    outproj_rows(P, c, g, T_FA_OUT, resid, ep);
+}
+
+// post norm + SiLU(Wg x) * (Wu x): tile rows 0-7 are gate rows, 8-15 the matching up rows
+// (reference: megakernel/kernel.cu:313-347, 572-578)
+__device__ __forceinline__ void phase_gateup(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer) {
+    const Geo g = phase_geo(T_GATEUP, c.cta, c.G, P.vocab);
+    const int nout = g.r1 - g.r0;
+    const uint32_t ep = epoch_of(c, layer);
+    trace_point(P, c);
+    float w0, w1;
+    load_norm_w(lw.ptrs[lw.layer_type == 0 ? (int)DN_POST_NORM : (int)FA_POST_NORM], c.tid, w0, w1);
+    const float2 v = poll2(P, c, P.ws->x_hidden[0] + 2 * c.tid, ep);
+    rmsnorm_to_slice(c, v, w0, w1, true);
+    trace_point(P, c);
+    mma_phase<2, 16>(P, c, g.nchunks, HIDDEN * 2);
+    trace_point(P, c);
+    named_bar_sync(1, NCT);
+    if (c.tid < nout) {
+        const float gv = part_sum(c, c.tid >> 3, c.tid & 7);
+        const float uv = part_sum(c, c.tid >> 3, 8 + (c.tid & 7));
+        st_flagged(P.ws->x_mlp + g.r0 + c.tid, silu_f(gv) * uv, ep);
+    }
+    trace_point(P, c);
+}
+
+// down projection (K = 3584, 4 rows per chunk) + residual (reference: megakernel/kernel.cu:350-384)
+__device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, int layer) {
+    const Geo g = phase_geo(T_DOWN, c.cta, c.G, P.vocab);
+    const int nloc = g.r1 - g.r0;
+    const uint32_t ep = epoch_of(c, layer);
+    trace_point(P, c);
+    float resid = 0.f;
+    if (c.tid < nloc) resid = poll1(P, c, P.ws->x_hidden[0] + g.r0 + c.tid, ep);
+    {
+        float xv[7];
+        const unsigned long long* base = P.ws->x_mlp + c.warp * XK + c.lane;
+        const unsigned long long* const p1[7] = {base, base + 32, base + 64, base + 96, base + 128, base + 160, base + 192};
+        poll1_batch<7>(P, c, p1, ep, xv);
+        uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
+#pragma unroll
+        for (int k = 0; k < 7; ++k) stage_one(xw, c.lane + 32 * k, xv[k]);
+        __syncwarp();
+    }
+    trace_point(P, c);
+    mma_phase<7, 4>(P, c, g.nchunks, INTER * 2);
+    trace_point(P, c);
+    named_bar_sync(1, NCT);
+    if (c.tid < nloc) {
+        const float y = part_sum(c, c.tid >> 2, c.tid & 3) + resid;
+        st_flagged(P.ws->x_hidden[1] + g.r0 + c.tid, round_bf16(y), ep);
+    }
+    trace_point(P, c);
+}
+
+// ---- LM head: scalar streaming rows (one warp per ring slot) --------------------------------
+
+__device__ __forceinline__ float dot_row1024(const char* row, int lane, const float* xr) {
+    const uint4* wp = reinterpret_cast<const uint4*>(row) + lane;
+    const uint4 w0 = wp[0], w1 = wp[32], w2 = wp[64], w3 = wp[96];
+    float a0 = dot8(w0, xr, 0.f), a1 = dot8(w1, xr + 8, 0.f);
+    a0 = dot8(w2, xr + 16, a0); a1 = dot8(w3, xr + 24, a1);
+    return a0 + a1;
+}
+
+// final norm (f32, not rounded) + LM head + argmax, lowest index winning exact ties
+// (reference: megakernel/kernel.cu:763-826, 905-920)
+__device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
+    const Geo g = phase_geo(T_LM, c.cta, c.G, P.vocab);
+    const int nloc = g.r1 - g.r0;
+    trace_point(P, c);
+    float w0, w1;
+    load_norm_w(P.final_norm, c.tid, w0, w1);
+    const float2 v = poll2(P, c, P.ws->x_hidden[1] + 2 * c.tid, epoch_of(c, P.num_layers - 1));
+    {
+        const float ss = warp_sum(v.x * v.x + v.y * v.y);
+        if (c.lane == 0) c.red[c.warp] = ss;
+        named_bar_sync(1, NCT);
+        float tot = 0.f;
+#pragma unroll
+        for (int i = 0; i < NCW; ++i) tot += c.red[i];
+        const float rstd = rsqrtf(tot * (1.0f / HIDDEN) + RMS_EPS);
+        const float2 x = make_float2(v.x * rstd * w0, v.y * rstd * w1);
+        reinterpret_cast<float2*>(c.xs)[c.tid] = x;
+        if (c.cta == 0) {     // outputs of the reference signature: last hidden (bf16) and its final norm (f32)
+            reinterpret_cast<float2*>(P.normalized)[c.tid] = x;
+            reinterpret_cast<__nv_bfloat162*>(P.hidden)[c.tid] = __floats2bfloat162_rn(v.x, v.y);
+        }
+        named_bar_sync(1, NCT);
+    }
+    trace_point(P, c);
+    float xr[32];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const float4 a = *reinterpret_cast<const float4*>(c.xs + it * 256 + c.lane * 8);
+        const float4 b = *reinterpret_cast<const float4*>(c.xs + it * 256 + c.lane * 8 + 4);
+        xr[it * 8 + 0] = a.x; xr[it * 8 + 1] = a.y; xr[it * 8 + 2] = a.z; xr[it * 8 + 3] = a.w;
+        xr[it * 8 + 4] = b.x; xr[it * 8 + 5] = b.y; xr[it * 8 + 6] = b.z; xr[it * 8 + 7] = b.w;
+    }
+    const bool penal = (P.rep_penalty > 1.0f) && (P.seen_mask != nullptr);
+    float bestv = -INFINITY;
+    int besti = 0x7fffffff;
+#pragma unroll 1
+    for (int q = 0; q < g.nchunks; ++q, ++c.it) {
+        const uint32_t stage = c.it % NSTAGE, parity = (c.it / NSTAGE) & 1u;
+        const int row = g.r0 + q * 16 + c.warp;
+        const bool valid = (q * 16 + c.warp) < nloc;
+        float seen = 0.f;
+        if (penal && valid) seen = __ldcg(P.seen_mask + row);
+        wait_full(P, c, stage, parity);
+        float acc = 0.f;
+        if (valid) acc = dot_row1024(c.smem + OFF_RING + stage * STAGE_BYTES + c.warp * 2048, c.lane, xr);
+        acc = warp_sum(acc);
+        if (valid) {
+            if (seen > 0.f) acc = (acc > 0.f) ? acc / P.rep_penalty : acc * P.rep_penalty;
+            if (acc > bestv) { bestv = acc; besti = row; }
+        }
+        release_stage(c, stage);
+    }
+    trace_point(P, c);
+    c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
+    int* resi = reinterpret_cast<int*>(c.part) + 32;
+    if (c.lane == 0) { c.part[c.warp] = bestv; resi[c.warp] = besti; }
+    named_bar_sync(1, NCT);
+    if (c.warp == 0) {
+        float bv = (c.lane < NCW) ? c.part[c.lane] : -INFINITY;
+        int bi = (c.lane < NCW) ? resi[c.lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (c.lane == 0) {
+            P.ws->argmax_val[c.cta] = bv;
+            P.ws->argmax_idx[c.cta] = bi;
+            __threadfence();
+            const uint32_t old = atomicAdd(&P.ws->lm_count, 1u);
+            c.misc[MISC_LAST] = (old == (uint32_t)c.G - 1u) ? 1 : 0;
+        }
+    }
+    named_bar_sync(1, NCT);
+    if (c.misc[MISC_LAST] && c.warp == 0) {
+        __threadfence();
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int b = c.lane; b < c.G; b += 32) {
+            const float ov = __ldcg(P.ws->argmax_val + b);
+            const int oi = __ldcg(P.ws->argmax_idx + b);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (c.lane == 0) {
+            *P.out_token = bi;
+            if (P.token_feedback) *P.token_feedback = bi;
+            if (P.out_tokens_slot) *P.out_tokens_slot = bi;
+            // every CTA has finished: re-arm the workspace for the next launch
+            P.ws->lm_count = 0u;
+            P.ws->seq = c.seq + 1u;
+        }
+    }
+    trace_point(P, c);
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __grid_constant__ DecodeParams P) {
+    extern __shared__ __align__(1024) char smem[];
+    Ctx c;
+    c.smem = smem;
+    c.xs = reinterpret_cast<float*>(smem + OFF_SCRATCH);
+    c.part_base = reinterpret_cast<float*>(smem + OFF_PART);
+    c.part = c.part_base;
+    c.part_flip = 0;
+    c.red = reinterpret_cast<float*>(smem + OFF_RED);
+    c.misc = reinterpret_cast<volatile int*>(smem + OFF_MISC);
+    c.ring0 = smem_u32(smem + OFF_RING);
+    c.full0 = smem_u32(smem + OFF_BAR);
+    c.empty0 = c.full0 + NSTAGE * 8;
+    c.tid = threadIdx.x; c.warp = threadIdx.x >> 5; c.lane = threadIdx.x & 31;
+    c.cta = blockIdx.x; c.G = gridDim.x;
+    c.it = 0; c.trace_slot = 0;
+    c.seq = __ldcg(&P.ws->seq);
+
+    // The pointer table is read on every chunk; keep it in shared memory.
+    LayerWeights* s_layers = reinterpret_cast<LayerWeights*>(smem + OFF_LAYERS);
+    for (int i = threadIdx.x; i < P.num_layers * (int)(sizeof(LayerWeights) / 16); i += NTHREADS)
+        reinterpret_cast<uint4*>(s_layers)[i] = __ldg(reinterpret_cast<const uint4*>(P.layers) + i);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSTAGE; ++s) {
+            mbar_init(c.full0 + s * 8, 1);
+            mbar_init(c.empty0 + s * 8, NCW);
+        }
+        c.misc[MISC_ABORT] = 0;
+        c.misc[MISC_LAST] = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    int token = P.token_ptr ? __ldcg(P.token_ptr) : P.token_val;
+    token = token < 0 ? 0 : (token >= P.vocab ? P.vocab - 1 : token);
+    const __nv_bfloat16* embed_row = reinterpret_cast<const __nv_bfloat16*>(P.embed) + (size_t)token * HIDDEN;
+
+    if (c.warp == NCW) {
+        // ===== producer warp =====
+        const uint64_t pol_stream = l2_policy_evict_first();
+        const uint64_t pol_keep = l2_policy_evict_last();
+        // one copy of the issue code: the phase type is a run-time value here
+        int dn_idx = 0;
+        for (int layer = 0; layer <= P.num_layers; ++layer) {
+            const bool lm = (layer == P.num_layers);
+            const LayerWeights& lw = s_layers[lm ? 0 : layer];
+            const bool dn = (lw.layer_type == 0);
+            const int nph = lm ? 1 : (dn ? 5 : 4);
+#pragma unroll 1
+            for (int ph = 0; ph < nph; ++ph) {
+                int type;
+                if (lm) type = T_LM;
+                else if (dn) type = (ph == 0) ? T_DN_IN : (ph == 1) ? T_DN_REC : (ph == 2) ? T_DN_OUT : (ph == 3) ? T_GATEUP : T_DOWN;
+                else type = (ph == 0) ? T_FA_IN : (ph == 1) ? T_FA_OUT : (ph == 2) ? T_GATEUP : T_DOWN;
+                producer_phase(P, c, type, lw, dn_idx, pol_stream, pol_keep);
+            }
+            if (!lm && dn) ++dn_idx;
+        }
+    } else {
+        // ===== consumer warps =====
+        if (c.cta == 0 && c.tid == 0 && P.seen_mask && P.rep_penalty > 1.0f) P.seen_mask[token] = 1.0f;
+        int dn_idx = 0, fa_idx = 0;
+        for (int layer = 0; layer < P.num_layers; ++layer) {
+            const LayerWeights& lw = s_layers[layer];
+            const __nv_bfloat16* erow = (layer == 0) ? embed_row : nullptr;
+            if (lw.layer_type == 0) {
+                phase_dn_in(P, c, lw, layer, dn_idx, erow);
+                phase_dn_rec(P, c, layer, dn_idx);
+                phase_dn_out(P, c, lw, layer, erow);
+                ++dn_idx;
+            } else {
+                phase_fa_in(P, c, lw, layer, erow);
+                phase_fa_att(P, c, lw, layer, fa_idx);
+                phase_fa_out(P, c, lw, layer, erow);
+                ++fa_idx;
+            }
+            phase_gateup(P, c, lw, layer);
+            phase_down(P, c, layer);
+        }
+        phase_lm(P, c);
+    }
+    __syncthreads();
+    if (c.misc[MISC_ABORT]) {
+        if (threadIdx.x == 0 && P.host_status) {
+            *((volatile uint32_t*)P.host_status) = (uint32_t)c.misc[MISC_ABORT];
+            __threadfence_system();
+        }
+        // a wait ran out: give bulk copies that are still in flight time to land before the CTA exits
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 50000ull) {}
+    }
+}
+

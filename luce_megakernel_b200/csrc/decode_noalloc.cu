@@ -3,12 +3,12 @@
 // Some hosts of this library cannot let it call cudaMalloc: an inference server that hands all
 // free HBM to its own pool at start-up (a later cudaMalloc from a library then fails), or a
 // latency-critical decode loop that cannot accept the device-wide synchronisation cudaMalloc and
-// cudaFree imply.  launch_decode() keeps its barrier words, argmax partials and attention
-// partials in a workspace it allocates on first use; the entry point below runs the same kernel
+// cudaFree imply.  launch_decode() keeps its activation exchange buffers, argmax partials and
+// attention partials in a workspace it allocates on first use; the entry point below runs the same kernel
 // with that scratch placed in a file-scope __device__ array instead, so it allocates nothing:
 // no cudaMalloc / cudaFree / cudaHostAlloc and no allocating library call.
 //
-// The array costs sizeof(DecodeWorkspace) (about 132 KB) on every GPU that loads the library,
+// The array costs sizeof(DecodeWorkspace) (about 300 KB) on every GPU that loads the library,
 // until the process exits, and is sized for grids of at most MK_STATIC_SCRATCH_MAX_CTAS CTAs.
 #include <stdio.h>
 #include <string.h>
@@ -87,7 +87,7 @@ extern "C" int mk_decode_bf16_static_scratch(
         e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return fail_with(MK_ERR_CUDA, "cudaDeviceGetAttribute", e);
         const int grid = mk::decode_max_grid();
-        if (grid <= 0) return fail_with(MK_ERR_CUDA, "decode kernel does not fit on this device");
+        if (grid < mk::MIN_GRID) return fail_with(MK_ERR_CUDA, "decode kernel needs at least 129 co-resident CTAs (one per SM)");
         if (sms > MK_STATIC_SCRATCH_MAX_CTAS) {
             snprintf(g_static_err, sizeof(g_static_err),
                      "this device runs %d CTAs; the static scratch holds partial results for at most %d", sms,
@@ -100,9 +100,10 @@ extern "C" int mk_decode_bf16_static_scratch(
     }
 
     // Every call shares the array and finds the previous call's contents in it.  Only the
-    // control words (barrier count, argmax arrival count, abort flag: the first 128 bytes) have
-    // to start at zero; partial results are always written before they are read.
-    e = cudaMemsetAsync(s.scratch, 0, 128, stream);
+    // control words (argmax arrival count and abort flag: the first 64 bytes) have to start at
+    // zero; the launch counter that follows them must persist, and every exchanged value and
+    // partial result is written before it is read.
+    e = cudaMemsetAsync(s.scratch, 0, 64, stream);
     if (e != cudaSuccess) return fail_with(MK_ERR_CUDA, "cudaMemsetAsync(static scratch)", e);
 
     mk::DecodeParams p;
@@ -120,6 +121,7 @@ extern "C" int mk_decode_bf16_static_scratch(
     p.ws = s.scratch;
     p.host_status = nullptr;   // the mapped status word of launch_decode would be an allocation
     p.trace = nullptr; p.trace_slots = 0;
+    mk::fill_rope(p);
     e = mk::launch_decode_kernel(p, s.grid, stream);
     if (e != cudaSuccess) return fail_with(MK_ERR_CUDA, "decode launch", e);
     return MK_OK;

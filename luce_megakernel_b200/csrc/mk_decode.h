@@ -12,15 +12,29 @@ constexpr int ATT_MAX_CHUNKS = 16;     // KV chunks per KV head in one decode st
 constexpr int ATT_CHUNK_POS = 64;      // target positions per chunk
 constexpr int ATT_PART_STRIDE = 260;   // floats per (head, chunk) partial: m, l, 2 pad, o[256]
 constexpr int MAX_GRID = 256;
+// Smallest grid the kernel accepts: every phase must fit its rows of one CTA into four ring
+// chunks (8224 in-projection rows / 129 CTAs = 64 rows = 4 chunks of 16).
+constexpr int MIN_GRID = 129;
 
-// Library-owned scratch in global memory, zero on entry to every launch.
+// Library-owned scratch in global memory.  Activation vectors travel between CTAs as 64-bit
+// words {f32 value, epoch}: a reader spins on the word itself until the epoch matches, so no
+// grid barrier and no separate flag are needed.  The epoch is unique per launch and layer
+// (derived from `seq`, which the last CTA of every launch increments), so nothing has to be
+// cleared between launches; only `lm_count` and `abort_flag` must be zero on entry.
 struct DecodeWorkspace {
-    uint32_t bar;        // grid-barrier arrivals of the current launch
-    uint32_t lm_count;   // CTAs that have published their argmax partial
-    uint32_t abort_flag; // set by the first CTA whose bounded wait ran out
-    uint32_t pad[29];
+    uint32_t lm_count;    // CTAs that have published their argmax partial
+    uint32_t abort_flag;  // set by the first CTA whose bounded wait ran out
+    uint32_t pad0[14];
+    uint32_t seq;         // launches completed on this workspace
+    uint32_t pad1[15];
     float argmax_val[MAX_GRID];
     int argmax_idx[MAX_GRID];
+    uint32_t att_ready[32];                 // per attention unit: epoch once its partials are written
+    unsigned long long x_hidden[2][1024];   // residual stream after out-proj [0] / after down-proj [1]
+    unsigned long long x_dnin[8224];        // DeltaNet: q|k|v after conv+SiLU, z, beta, decay
+    unsigned long long x_o[2048];           // DeltaNet recurrence output
+    unsigned long long x_mlp[3584];         // SwiGLU output
+    unsigned long long x_fain[5120];        // attention: per head [q|gate], k, v
     float attn_part[8 * ATT_MAX_CHUNKS * ATT_PART_STRIDE];
 };
 
@@ -33,14 +47,14 @@ struct DecodeParams {
     void* v_cache;
     float* dn_states;             // f32 [n_dn, 16, 128(value), 128(key)]
     float* conv_bufs;             // f32 [n_dn, 6144, 4]
-    void* hidden;                 // bf16 [1024] residual stream between phases
-    float* qkv;                   // f32 [6144]: DeltaNet q|k|v after conv, or attention per-head [q|gate] (4096)
-    float* kv;                    // f32 [1024]
-    float* attn_out;              // f32 [2048]
-    float* mlp_inter;             // f32 [3584]
-    float* z;                     // f32 [2048]
-    float* beta;                  // f32 [16]
-    float* alpha;                 // f32 [16]
+    void* hidden;                 // bf16 [1024]: receives the last layer's output
+    float* qkv;                   // caller scratch of the reference signature (unused by the kernel)
+    float* kv;
+    float* attn_out;
+    float* mlp_inter;
+    float* z;
+    float* beta;
+    float* alpha;
     float* normalized;            // f32 [1024] final-normed hidden (output)
     float* seen_mask;             // f32 [vocab] or null
     float rep_penalty;
@@ -50,6 +64,8 @@ struct DecodeParams {
     int* token_feedback;          // optional: also receives the new token
     int* out_tokens_slot;         // optional: also receives the new token
     int position;
+    float rope_cos[32];           // cos / sin of position * inv_freq_i, filled by fill_rope()
+    float rope_sin[32];
     int max_seq_len;
     int num_layers;
     int vocab;
@@ -59,6 +75,8 @@ struct DecodeParams {
     int trace_slots;              // entries per CTA in `trace`
 };
 
+// Fills rope_cos / rope_sin for p.position (call after setting the position).
+void fill_rope(DecodeParams& p);
 // Launches the persistent decode kernel (cooperative launch, `grid` CTAs of 544 threads).
 cudaError_t launch_decode_kernel(const DecodeParams& p, int grid, cudaStream_t stream);
 // Largest grid that is guaranteed co-resident on the current device.

@@ -1,0 +1,147 @@
+// NVFP4 weight quantisers for sm_100a, bit-exact to the reference's two formats.
+//
+//  format A (layer weights; reference: megakernel/kernel_gb10_nvfp4.cu:1764-1817)
+//    groups of `group_size` along K, scale = amax/6 as fp16 (1 for an all-zero group), code by the
+//    thresholds .25/.75/1.25/1.75/2.5/3.5/5 on x * (1/scale) with the unrounded f32 scale.
+//  format B (LM head / tensor-core layout; reference: megakernel/kernel_gb10_nvfp4.cu:1373-1437)
+//    blocks of 16, scale = max(amax/6, 2^-28) in E4M3, values rounded to e2m1 (nearest even),
+//    scales in 128-row x 4-column tiles of 512 bytes.
+//
+// Both are HBM-bound byte work: one thread per group/block, 128-bit loads of the bf16 row,
+// 64/128-bit stores of the packed nibbles; consecutive threads take consecutive groups of a row.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/luce_megakernel_b200.h"
+
+namespace {
+
+__device__ __forceinline__ float bf_at(const uint4& v, int i) {
+    const uint32_t w = (i < 2) ? v.x : (i < 4) ? v.y : (i < 6) ? v.z : v.w;
+    return __uint_as_float((i & 1) ? (w & 0xffff0000u) : (w << 16));
+}
+
+__device__ __forceinline__ unsigned code_thresholds(float x) {
+    const float ax = fabsf(x);
+    const unsigned mag = ax < 0.25f ? 0u : ax < 0.75f ? 1u : ax < 1.25f ? 2u : ax < 1.75f ? 3u
+                       : ax < 2.5f ? 4u : ax < 3.5f ? 5u : ax < 5.0f ? 6u : 7u;
+    return (x < 0.0f) ? (mag | 8u) : mag;
+}
+
+__global__ void quantize_a_kernel(const __nv_bfloat16* __restrict__ w, uint8_t* __restrict__ packed,
+                                  __half* __restrict__ scales, long long total_groups, int groups_per_row, int group) {
+    const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= total_groups) return;
+    const long long row = gid / groups_per_row;
+    const int g = (int)(gid - row * groups_per_row);
+    const size_t cols = (size_t)groups_per_row * group;
+    const __nv_bfloat16* src = w + row * cols + (size_t)g * group;
+    uint8_t* dst = packed + row * (cols / 2) + (size_t)g * (group / 2);
+    float amax = 0.0f;
+    const bool vec = (group % 8 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+    if (vec) {
+        for (int i = 0; i < group; i += 8) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + i));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(bf_at(v, e)));
+        }
+    } else {
+        for (int i = 0; i < group; ++i) amax = fmaxf(amax, fabsf(__bfloat162float(src[i])));
+    }
+    const float scale = (amax > 0.0f) ? __fdiv_rn(amax, 6.0f) : 1.0f;
+    scales[gid] = __float2half_rn(scale);
+    if (amax == 0.0f) {
+        for (int i = 0; i < group / 2; ++i) dst[i] = 0;
+        return;
+    }
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (vec) {
+        for (int i = 0; i < group; i += 8) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + i));
+            uint32_t out = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) out |= code_thresholds(__fmul_rn(bf_at(v, e), inv)) << (4 * e);
+            if ((reinterpret_cast<uintptr_t>(dst + i / 2) & 3u) == 0) *reinterpret_cast<uint32_t*>(dst + i / 2) = out;
+            else for (int b = 0; b < 4; ++b) dst[i / 2 + b] = (uint8_t)(out >> (8 * b));
+        }
+    } else {
+        for (int i = 0; i < group; i += 2) {
+            const unsigned lo = code_thresholds(__fmul_rn(__bfloat162float(src[i]), inv));
+            const unsigned hi = code_thresholds(__fmul_rn(__bfloat162float(src[i + 1]), inv));
+            dst[i / 2] = (uint8_t)(lo | (hi << 4));
+        }
+    }
+}
+
+__global__ void quantize_b_kernel(const __nv_bfloat16* __restrict__ w, uint8_t* __restrict__ packed,
+                                  uint8_t* __restrict__ scales, int rows, int cols) {
+    const int blocks_per_row = cols / 16;
+    const long long bid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (bid >= (long long)rows * blocks_per_row) return;
+    const int row = (int)(bid / blocks_per_row), sc = (int)(bid % blocks_per_row);
+    const uint4* src = reinterpret_cast<const uint4*>(w + (size_t)row * cols + (size_t)sc * 16);
+    const uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fmaxf(fabsf(bf_at(v0, e)), fabsf(bf_at(v1, e))));
+    const float scale_f = fmaxf(__fmul_rn(amax, 1.0f / 6.0f), 1.0f / (float)(1 << 28));
+    const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale_f, __NV_SATFINITE, __NV_E4M3);
+    const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
+    const float dec = __half2float(*reinterpret_cast<const __half*>(&hr));
+    const float inv = (dec > 0.0f) ? __fdiv_rn(1.0f, dec) : 0.0f;
+    unsigned long long out = 0;
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+        const uint4& v = (p < 4) ? v0 : v1;
+        const float2 f = make_float2(__fmul_rn(bf_at(v, (2 * p) & 7), inv), __fmul_rn(bf_at(v, (2 * p + 1) & 7), inv));
+        const __nv_fp4x2_storage_t q = __nv_cvt_float2_to_fp4x2(f, __NV_E2M1, cudaRoundNearest);
+        out |= (unsigned long long)(uint8_t)q << (8 * p);
+    }
+    *reinterpret_cast<unsigned long long*>(packed + (size_t)row * (cols / 2) + (size_t)sc * 8) = out;
+    const size_t tile = (size_t)(row >> 7) * (cols / 64) + (sc >> 2);
+    scales[tile * 512 + (size_t)(row & 31) * 16 + (size_t)((row & 127) >> 5) * 4 + (sc & 3)] = (uint8_t)s8;
+}
+
+thread_local char g_qerr[160] = "";
+int qfail(const char* m) { snprintf(g_qerr, sizeof(g_qerr), "%s", m); return MK_ERR_BAD_ARG; }
+
+}  // namespace
+
+extern "C" const char* mk_quantize_error(void) { return g_qerr; }
+
+extern "C" int launch_quantize_nvfp4_out(const void* weight, int rows, int cols, int group_size, void* packed_out,
+                                         void* scales_out, cudaStream_t stream) {
+    if (!weight || !packed_out || !scales_out) return qfail("null pointer argument");
+    if (rows <= 0 || cols <= 0) return qfail("rows and cols must be positive");
+    if (group_size <= 0 || (group_size & 1) || cols % group_size) return qfail("group_size must be even and divide cols");
+    const int gpr = cols / group_size;
+    const long long total = (long long)rows * gpr;
+    const int threads = 256;
+    const unsigned blocks = (unsigned)((total + threads - 1) / threads);
+    quantize_a_kernel<<<blocks, threads, 0, stream>>>((const __nv_bfloat16*)weight, (uint8_t*)packed_out,
+                                                      (__half*)scales_out, total, gpr, group_size);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_qerr, sizeof(g_qerr), "quantize launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
+    return MK_OK;
+}
+
+extern "C" int launch_quantize_nvfp4_lm_out(const void* weight, int rows, int cols, void* packed_out, void* scales_out,
+                                            cudaStream_t stream) {
+    if (!weight || !packed_out || !scales_out) return qfail("null pointer argument");
+    if (rows <= 0 || rows % 128) return qfail("rows must be a positive multiple of 128");
+    if (cols <= 0 || cols % 64) return qfail("cols must be a positive multiple of 64");
+    if ((reinterpret_cast<uintptr_t>(weight) & 15u) || (reinterpret_cast<uintptr_t>(packed_out) & 7u))
+        return qfail("weight must be 16-byte aligned and packed_out 8-byte aligned");
+    const long long total = (long long)rows * (cols / 16);
+    const int threads = 256;
+    const unsigned blocks = (unsigned)((total + threads - 1) / threads);
+    quantize_b_kernel<<<blocks, threads, 0, stream>>>((const __nv_bfloat16*)weight, (uint8_t*)packed_out,
+                                                      (uint8_t*)scales_out, rows, cols);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_qerr, sizeof(g_qerr), "quantize launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
+    return MK_OK;
+}

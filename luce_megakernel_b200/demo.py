@@ -1,0 +1,42 @@
+"""Minimal end-to-end example: a random-init model of the architecture decodes a few tokens.
+
+    python -m luce_megakernel_b200.demo [--steps 8] [--context 520] [--layers 24] [--vocab 248320]
+
+Also the small, bounded workload used for profiler captures of the decode kernel (few launches,
+about 1.6 GB on the device).
+"""
+import argparse
+import time
+
+import torch
+
+from . import lib
+from . import model as M
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--context", type=int, default=520)
+    ap.add_argument("--layers", type=int, default=M.NUM_LAYERS)
+    ap.add_argument("--vocab", type=int, default=M.VOCAB_SIZE)
+    args = ap.parse_args()
+    weights, _ = M.load_weights(seed=0, num_layers=args.layers, vocab=args.vocab, device_init=True)
+    dec = M.Decoder(weights=weights, max_seq_len=max(2048, args.context + args.steps + 8), api="cabi")
+    tok = 11
+    for _ in range(4):                      # a short prompt through the decode kernel
+        tok = dec.step(tok)
+    dec._position = args.context            # continue at the requested context length
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    out = dec.step_many(tok, args.steps)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    status = lib().mk_device_status()
+    if status != 0:
+        raise SystemExit(f"device-side wait timed out (status {status})")
+    print(f"{args.steps} tokens in {dt * 1e3:.2f} ms ({args.steps / dt:.0f} tok/s): {out.tolist()[:8]}")
+
+
+if __name__ == "__main__":
+    main()
