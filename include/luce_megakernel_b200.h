@@ -95,11 +95,52 @@ int launch_quantize_nvfp4_lm_out(const void *weight, int rows, int cols,
                                  void *packed_out, void *scales_out, cudaStream_t stream);
 const char *mk_quantize_error(void);
 
+/* Prefill of a prompt of seq_len tokens from position 0: fills the KV caches for positions
+ * 0..seq_len-1, advances the DeltaNet and conv state from their current content (callers zero
+ * them first), writes the first generated token to output_token, the last row's final-normed
+ * vector to final_normed (bf16 [1024]) and its pre-norm hidden to hidden_bf16_out (bf16 [1024]).
+ * Replaces launch_prefill_bf16 (reference: megakernel/prefill.cu:1559-1793, declared at
+ * megakernel/torch_bindings.cpp:354-368) with the same argument list; the scratch buffers of that
+ * signature are accepted and ignored (the library keeps its own workspace, grown on demand:
+ * about 45 KB per prompt token).  token_ids is a device pointer.  fused_fa_qkv_base is
+ * [n_fa, 5120, 1024] (q|k|v rows) and fused_gate_up_base [num_layers, 7168, 1024] (gate|up rows),
+ * as the reference driver packs them (megakernel/model.py:245-260).
+ * mk_prefill_bf16 is the same call without the unused scratch arguments and with explicit depth
+ * and vocabulary. */
+int launch_prefill_bf16(
+    const int *token_ids, int seq_len, int *output_token,
+    const void *embed_weight, const MkLayerWeights *layers,
+    const void *final_norm_w, const void *lm_head_w,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *hidden, void *residual, void *normalized,
+    void *proj_buf, void *proj_buf2, void *attn_buf, void *mlp_buf,
+    void *dn_out_buf, void *beta_buf, void *alpha_buf, void *dn_pre_qkv,
+    void *dn_u_scratch, void *dn_w_scratch, void *dn_cs_scratch,
+    const void *fused_fa_qkv_base, const void *fused_gate_up_base,
+    void *final_normed, void *hidden_bf16_out,
+    void *lm_bmv, void *lm_bmi,
+    int max_seq_len, cudaStream_t stream);
+int mk_prefill_bf16(
+    const int *token_ids, int seq_len, int *output_token,
+    const void *embed_weight, const MkLayerWeights *layers, const void *final_norm_w, const void *lm_head_w,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    const void *fused_fa_qkv_base, const void *fused_gate_up_base,
+    void *final_normed, void *hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
+const char *mk_prefill_error(void);
+
+/* The prefill projection GEMM on its own: C[M,N] = A[M,K] . W[N,K]^T (+ residual[M,N]), bf16 row-major,
+ * f32 accumulation (tcgen05 / TMEM / TMA).  Replaces the cublasGemmEx call of the reference prefill
+ * (reference: megakernel/prefill.cu:1526-1534).  N % 128 == 0, K % 64 == 0, 16-byte aligned pointers. */
+int mk_gemm_bf16_tn(const void *A, const void *W, void *C, const void *residual, int M, int N, int K,
+                    cudaStream_t stream);
+
 /* Model depth and vocabulary the entry points assume (defaults 24 and 248320, the
  * compile-time constants of the reference: megakernel/kernel.cu:20,22).  Reduced values let
  * the parity tests run the same kernels on a small model.  num_layers in [1,24]; the layer
  * types are read from the pointer table. */
 int mk_set_model_dims(int num_layers, int vocab);
+void mk_get_model_dims(int *num_layers, int *vocab);
 
 /* Status of the last device-side failure on the current device (0 = none) and a text for the
  * last error returned on this thread.  mk_clear_error() re-arms the library after a timeout. */

@@ -5,6 +5,7 @@
 #include "../../include/luce_megakernel_b200.h"
 #include "mk_common.cuh"
 #include "mk_decode.h"
+#include "mk_prefill.h"
 
 namespace {
 
@@ -206,6 +207,11 @@ int mk_set_model_dims(int num_layers, int vocab) {
     return MK_OK;
 }
 
+void mk_get_model_dims(int* num_layers, int* vocab) {
+    if (num_layers) *num_layers = g_num_layers;
+    if (vocab) *vocab = g_vocab;
+}
+
 int mk_device_status(void) {
     DeviceState* d = nullptr;
     if (device_state(&d)) return -1;
@@ -221,6 +227,21 @@ void mk_clear_error(void) {
     cudaMemset(d->ws, 0, sizeof(mk::DecodeWorkspace));
     *d->host_status = 0;
     g_err[0] = 0;
+}
+
+int mk_gemm_bf16_tn(const void* A, const void* W, void* C, const void* residual, int M, int N, int K,
+                    cudaStream_t stream) {
+    if (!A || !W || !C) return set_err(MK_ERR_BAD_ARG, "null pointer argument");
+    static int* err_flag = nullptr;
+    if (!err_flag) {
+        cudaError_t e0 = cudaMalloc(&err_flag, sizeof(int));
+        if (e0 != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaMalloc(gemm status)", e0);
+        cudaMemset(err_flag, 0, sizeof(int));
+    }
+    cudaError_t e = mk::gemm_bf16_tn(A, W, C, residual, M, N, K, K, N, err_flag, stream);
+    if (e == cudaErrorInvalidValue) return set_err(MK_ERR_BAD_ARG, "gemm shape or alignment not supported (N % 128, K % 64, 16-byte pointers)");
+    if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "gemm launch", e);
+    return MK_OK;
 }
 
 void mk_set_trace_buffer(unsigned long long* buf, int slots_per_cta) {

@@ -1,0 +1,234 @@
+// bf16 GEMM for the prefill projections on the 5th-generation tensor cores (sm_100a):
+//   C[M, N] = A[M, K] . W[N, K]^T     A, W, C bf16 row-major (both operands K-major), f32 accumulate
+// optionally C += R (residual, bf16 [M, N]) before the bf16 rounding.
+//
+// One 128 x 128 output tile per CTA.  Warp 0 streams A and W tiles (128 rows x 64 k, 128-byte
+// swizzle) with TMA into a 4-stage shared-memory ring; one thread of warp 1 issues
+// tcgen05.mma (M128 N128 K16, cta_group::1) with the accumulator in tensor memory; warps 2-5
+// read the accumulator back with tcgen05.ld (each warp its own 32-lane quadrant) and store bf16.
+// M is the token dimension: rows beyond M are zero-filled by TMA and not stored.
+// Every wait is bounded; on expiry the kernel sets *err and leaves.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "mk_common.cuh"
+#include "mk_prefill.h"
+
+namespace mk {
+
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 64;
+constexpr int STAGES = 4;
+constexpr int TILE_A_BYTES = BM * BK * 2;                 // 16 KB
+constexpr int TILE_B_BYTES = BN * BK * 2;                 // 16 KB
+constexpr int GEMM_SMEM = STAGES * (TILE_A_BYTES + TILE_B_BYTES) + 1024 /*align slack*/ + 256;
+constexpr int GEMM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 128;
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 bytes,
+// 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3ffffu) >> 4);             // start address, 16-byte units
+    d |= (uint64_t)1 << 16;                               // leading-dimension byte offset (unused with swizzle)
+    d |= (uint64_t)(1024 >> 4) << 32;                     // stride-dimension byte offset: 8 rows x 128 B
+    d |= (uint64_t)1 << 46;                               // descriptor version of sm_100
+    d |= (uint64_t)2 << 61;                               // layout: 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor of tcgen05.mma.kind::f16: bf16 x bf16 -> f32, both operands K-major.
+__device__ __forceinline__ uint32_t idesc_bf16(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, int* err) {
+    for (uint32_t n = 0; n < (1u << 24); ++n)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicExch(err, 1);
+    return false;
+}
+
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                    __nv_bfloat16* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc,
+                    int* err) {
+    extern __shared__ char smem_raw[];
+    char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t a0 = sbase, b0 = sbase + STAGES * TILE_A_BYTES;
+    const uint32_t bars = sbase + STAGES * (TILE_A_BYTES + TILE_B_BYTES);
+    const uint32_t full0 = bars, empty0 = bars + 8 * STAGES, tfull = bars + 16 * STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * (TILE_A_BYTES + TILE_B_BYTES) + 16 * STAGES + 16);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int nk = K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(full0 + 8 * s, 1); mbar_init(empty0 + 8 * s, 1); }
+        mbar_init(tfull, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {   // one warp allocates the accumulator columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = 0; kb < nk && ok; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t par = (kb / STAGES) & 1u;
+                ok = wait_bounded(empty0 + 8 * s, par ^ 1u, err);
+                if (!ok) break;
+                mbar_expect_tx(full0 + 8 * s, TILE_A_BYTES + TILE_B_BYTES);
+                tma_load_2d(a0 + s * TILE_A_BYTES, &map_a, kb * BK, m0, full0 + 8 * s);
+                tma_load_2d(b0 + s * TILE_B_BYTES, &map_w, kb * BK, n0, full0 + 8 * s);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_bf16(BM, BN);
+            for (int kb = 0; kb < nk && ok; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t par = (kb / STAGES) & 1u;
+                ok = wait_bounded(full0 + 8 * s, par, err);
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint64_t ad = smem_desc_sw128(a0 + s * TILE_A_BYTES), bd = smem_desc_sw128(b0 + s * TILE_B_BYTES);
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)   // 16 bf16 = 32 bytes = 2 descriptor units per step
+                    umma(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) ? 1u : 0u);
+                umma_commit(empty0 + 8 * s);        // frees the stage once these MMAs have read it
+            }
+            umma_commit(tfull);                     // accumulator complete
+        }
+    } else {
+        // epilogue warps 2..5: warp w may touch TMEM lanes 32*(w%4) .. +31
+        const int quad = warp & 3;
+        ok = wait_bounded(tfull, 0, err);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int row = m0 + quad * 32 + lane;
+        if (ok) {
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t v[32];
+                const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0;
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                    "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+                      "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+                      "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                    : "r"(taddr) : "memory");
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (row < M) {
+                    __nv_bfloat16* dst = C + (size_t)row * ldc + n0 + c0;
+                    const __nv_bfloat16* res = R ? R + (size_t)row * ldc + n0 + c0 : nullptr;
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        float f[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j + e]);
+                        if (res) {
+                            const uint4 r4 = *reinterpret_cast<const uint4*>(res + j);
+                            f[0] += bf_lo(r4.x); f[1] += bf_hi(r4.x); f[2] += bf_lo(r4.y); f[3] += bf_hi(r4.y);
+                            f[4] += bf_lo(r4.z); f[5] += bf_hi(r4.z); f[6] += bf_lo(r4.w); f[7] += bf_hi(r4.w);
+                        }
+                        uint4 o;
+                        __nv_bfloat162 p0 = __floats2bfloat162_rn(f[0], f[1]), p1 = __floats2bfloat162_rn(f[2], f[3]);
+                        __nv_bfloat162 p2 = __floats2bfloat162_rn(f[4], f[5]), p3 = __floats2bfloat162_rn(f[6], f[7]);
+                        o.x = *reinterpret_cast<uint32_t*>(&p0); o.y = *reinterpret_cast<uint32_t*>(&p1);
+                        o.z = *reinterpret_cast<uint32_t*>(&p2); o.w = *reinterpret_cast<uint32_t*>(&p3);
+                        *reinterpret_cast<uint4*>(dst + j) = o;
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                  const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess) fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+// rows x k bf16 matrix with row pitch `ld` elements; box = 64 k x 128 rows, 128-byte swizzle
+bool make_map(CUtensorMap* map, const void* base, int rows, int k, int ld) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
+                         int* err_flag, cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || N % BN || K % BK) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(C)) & 15u)
+        return cudaErrorInvalidValue;
+    if ((lda % 8) || (ldc % 8)) return cudaErrorInvalidValue;
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM);
+        if (e != cudaSuccess) return e;
+        attr_done = true;
+    }
+    CUtensorMap ma, mw;
+    if (!make_map(&ma, A, M, K, lda) || !make_map(&mw, W, N, K, K)) return cudaErrorInvalidValue;
+    dim3 grid(N / BN, (M + BM - 1) / BM);
+    gemm_bf16_tn_kernel<<<grid, GEMM_THREADS, GEMM_SMEM, stream>>>(ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K,
+                                                                   ldc, err_flag);
+    return cudaGetLastError();
+}
+
+}  // namespace mk

@@ -1,0 +1,546 @@
+// bf16 prefill of the Qwen3.5-0.8B hybrid for sm_100a: prompt of S tokens from position 0.
+//
+// The dense projections and the MLP run as tcgen05 / TMEM GEMMs fed by TMA (gemm_tcgen05.cu); the
+// kernels in this file are the pieces between them.  Arithmetic follows the reference prefill
+// (megakernel/prefill.cu:1559-1793) and, token by token, the decode kernel: bf16 activations
+// between GEMMs, f32 inside every kernel, f32 DeltaNet state.
+//
+// First version of this path: the DeltaNet scan is token-serial per (head, 16 value rows) and the
+// causal attention is a scalar online-softmax warp per (query, head).  Both are correct for any S
+// and are the parts a later version replaces with the chunked scan / tensor-core flash attention.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/luce_megakernel_b200.h"
+#include "mk_common.cuh"
+#include "mk_prefill.h"
+
+namespace mk {
+namespace {
+
+__constant__ float c_pf_inv_freq[FA_ROT / 2];
+
+__device__ __forceinline__ float ld_bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+// ---- embedding + RMSNorm -------------------------------------------------------------------
+
+__global__ void k_embed(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ embed,
+                        __nv_bfloat16* __restrict__ hidden, int S, int vocab) {
+    const int t = blockIdx.x;
+    int id = tok[t];
+    id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+    const uint4* src = reinterpret_cast<const uint4*>(embed + (size_t)id * HIDDEN);
+    uint4* dst = reinterpret_cast<uint4*>(hidden + (size_t)t * HIDDEN);
+    for (int i = threadIdx.x; i < HIDDEN / 8; i += blockDim.x) dst[i] = __ldg(src + i);
+}
+
+// one warp per row: out = bf16( x * rsqrt(mean x^2 + eps) * (1 + w) )   (reference: prefill.cu:72-88)
+__global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                          __nv_bfloat16* __restrict__ out, int S) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= S) return;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)row * HIDDEN);
+    float v[32];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 u = src[i * 32 + lane];
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) { v[i * 8 + 2 * e] = bf_lo(q[e]); v[i * 8 + 2 * e + 1] = bf_hi(q[e]); }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss * (1.0f / HIDDEN) + RMS_EPS);
+    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * HIDDEN);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 wu = __ldg(reinterpret_cast<const uint4*>(w) + i * 32 + lane);
+        const uint32_t wq[4] = {wu.x, wu.y, wu.z, wu.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 p = __floats2bfloat162_rn(v[i * 8 + 2 * e] * rstd * (1.0f + bf_lo(wq[e])),
+                                                           v[i * 8 + 2 * e + 1] * rstd * (1.0f + bf_hi(wq[e])));
+            o[e] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+        dst[i * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// ---- DeltaNet pieces ---------------------------------------------------------------------------
+
+// beta = sigmoid(Wb x), decay = exp(-exp(A_log) softplus(Wa x + dt_bias)); one warp per (t, output)
+// (reference: prefill.cu:91-99, 400-412)
+__global__ void k_dn_gates(const __nv_bfloat16* __restrict__ xn, const __nv_bfloat16* __restrict__ Wb,
+                           const __nv_bfloat16* __restrict__ Wa, const __nv_bfloat16* __restrict__ a_log,
+                           const __nv_bfloat16* __restrict__ dt_bias, float* __restrict__ beta, float* __restrict__ decay, int S) {
+    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (wid >= S * 32) return;
+    const int t = wid >> 5, o = wid & 31, h = o & 15;
+    const __nv_bfloat16* wrow = (o < 16 ? Wb : Wa) + (size_t)h * HIDDEN;
+    const uint4* xa = reinterpret_cast<const uint4*>(xn + (size_t)t * HIDDEN);
+    const uint4* wa = reinterpret_cast<const uint4*>(wrow);
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 xv = xa[i * 32 + lane], wv = __ldg(wa + i * 32 + lane);
+        acc += bf_lo(xv.x) * bf_lo(wv.x) + bf_hi(xv.x) * bf_hi(wv.x) + bf_lo(xv.y) * bf_lo(wv.y) + bf_hi(xv.y) * bf_hi(wv.y) +
+               bf_lo(xv.z) * bf_lo(wv.z) + bf_hi(xv.z) * bf_hi(wv.z) + bf_lo(xv.w) * bf_lo(wv.w) + bf_hi(xv.w) * bf_hi(wv.w);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+        if (o < 16) beta[t * 16 + h] = 1.0f / (1.0f + expf(-acc));
+        else {
+            const float x = acc + ld_bf(dt_bias + h);
+            const float sp = (x > 20.0f) ? x : log1pf(expf(x));
+            decay[t * 16 + h] = expf(-expf(ld_bf(a_log + h)) * sp);
+        }
+    }
+}
+
+// causal depthwise conv (k=4) + SiLU over all t in parallel, then per-head L2 norm of q (x 1/sqrt(128))
+// and k; block = (t, head), thread c = channel c of q, k and v of that head.  Inputs for t < 3 come
+// from the stored conv window.  Also leaves q.k per (t, head).  (reference: prefill.cu:1281-1368)
+__global__ void k_dn_preproject(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ conv_w,
+                                const float* __restrict__ conv_state, float* __restrict__ pre, float* __restrict__ kq, int S) {
+    const int t = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
+    __shared__ float red[3][4];
+    float val[3];
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+        const int ch = r * DN_QK + h * DN_KEY + c;
+        const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + ch);
+        const float w4[4] = {bf_lo(wr.x), bf_hi(wr.x), bf_lo(wr.y), bf_hi(wr.y)};
+        float co = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int tt = t - 3 + k;
+            const float x = (tt >= 0) ? ld_bf(qkv + (size_t)tt * DN_CONV_CH + ch) : conv_state[ch * 4 + 4 + tt];
+            co += x * w4[k];
+        }
+        val[r] = silu_f(co);
+    }
+    float sq = warp_sum(val[0] * val[0]), sk = warp_sum(val[1] * val[1]), sqk = warp_sum(val[0] * val[1]);
+    if ((c & 31) == 0) { red[0][c >> 5] = sq; red[1][c >> 5] = sk; red[2][c >> 5] = sqk; }
+    __syncthreads();
+    sq = red[0][0] + red[0][1] + red[0][2] + red[0][3];
+    sk = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+    sqk = red[2][0] + red[2][1] + red[2][2] + red[2][3];
+    const float qn = rsqrtf(sq + 1e-6f) * 0.08838834764831845f, kn = rsqrtf(sk + 1e-6f);
+    float* dst = pre + (size_t)t * DN_CONV_CH + h * DN_KEY + c;
+    dst[0] = val[0] * qn;
+    dst[DN_QK] = val[1] * kn;
+    dst[2 * DN_QK] = val[2];
+    if (c == 0) kq[t * 16 + h] = sqk * qn * kn;
+}
+
+// conv window after the prompt: the last four pre-activation inputs (reference: prefill.cu:1373-1395)
+__global__ void k_dn_conv_state(const __nv_bfloat16* __restrict__ qkv, float* __restrict__ conv_state, int S) {
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    if (ch >= DN_CONV_CH) return;
+    float old[4], nw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) old[k] = conv_state[ch * 4 + k];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int tt = S - 4 + k;
+        nw[k] = (tt >= 0) ? ld_bf(qkv + (size_t)tt * DN_CONV_CH + ch) : old[4 + tt];
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) conv_state[ch * 4 + k] = nw[k];
+}
+
+// Gated delta rule, token-serial; block = (head, 16 value rows), warp = one value row, lane = 4 keys.
+// The state row lives in registers across the whole prompt.  (reference: prefill.cu:114-221)
+__global__ void __launch_bounds__(512) k_dn_scan(const float* __restrict__ pre, const float* __restrict__ beta,
+                                                 const float* __restrict__ decay, const float* __restrict__ kq,
+                                                 float* __restrict__ state, float* __restrict__ o, int S) {
+    const int h = blockIdx.x >> 3, j = (blockIdx.x & 7) * 16 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    float* srow = state + ((size_t)h * DN_VAL + j) * DN_KEY;
+    float4 s = reinterpret_cast<const float4*>(srow)[lane];
+    const float* qp = pre + h * DN_KEY + 4 * lane;
+    float4 q4 = *reinterpret_cast<const float4*>(qp), k4 = *reinterpret_cast<const float4*>(qp + DN_QK);
+    float vj = pre[2 * DN_QK + h * DN_VAL + j], b = beta[h], g = decay[h], qk = kq[h];
+    for (int t = 0; t < S; ++t) {
+        float4 qn = q4, kn = k4;
+        float vn = vj, bn = b, gn = g, qkn = qk;
+        if (t + 1 < S) {                      // prefetch the next token's inputs
+            const float* np = qp + (size_t)(t + 1) * DN_CONV_CH;
+            qn = *reinterpret_cast<const float4*>(np);
+            kn = *reinterpret_cast<const float4*>(np + DN_QK);
+            vn = pre[(size_t)(t + 1) * DN_CONV_CH + 2 * DN_QK + h * DN_VAL + j];
+            bn = beta[(t + 1) * 16 + h]; gn = decay[(t + 1) * 16 + h]; qkn = kq[(t + 1) * 16 + h];
+        }
+        float stk = s.x * k4.x + s.y * k4.y + s.z * k4.z + s.w * k4.w;
+        float sqv = s.x * q4.x + s.y * q4.y + s.z * q4.z + s.w * q4.w;
+#pragma unroll
+        for (int of = 16; of > 0; of >>= 1) {
+            stk += __shfl_xor_sync(0xffffffffu, stk, of);
+            sqv += __shfl_xor_sync(0xffffffffu, sqv, of);
+        }
+        const float err = (vj - g * stk) * b;
+        s.x = s.x * g + k4.x * err; s.y = s.y * g + k4.y * err; s.z = s.z * g + k4.z * err; s.w = s.w * g + k4.w * err;
+        if (lane == 0) o[(size_t)t * DN_V + h * DN_VAL + j] = g * sqv + err * qk;
+        q4 = qn; k4 = kn; vj = vn; b = bn; g = gn; qk = qkn;
+    }
+    reinterpret_cast<float4*>(srow)[lane] = s;
+}
+
+// y = o * rsqrt(mean o^2 + eps) * w * silu(z), one warp per (t, head) (reference: prefill.cu:1493-1523)
+__global__ void k_dn_gated_norm(const float* __restrict__ o, const __nv_bfloat16* __restrict__ z,
+                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int S) {
+    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (wid >= S * DN_HEADS) return;
+    const float4 o4 = reinterpret_cast<const float4*>(o + (size_t)wid * DN_VAL)[lane];
+    const uint2 z2 = reinterpret_cast<const uint2*>(z + (size_t)wid * DN_VAL)[lane];
+    const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(w) + lane);
+    const float ss = warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w);
+    const float rstd = rsqrtf(ss * (1.0f / DN_VAL) + RMS_EPS);
+    const __nv_bfloat162 p0 = __floats2bfloat162_rn(o4.x * rstd * bf_lo(w2.x) * silu_f(bf_lo(z2.x)),
+                                                    o4.y * rstd * bf_hi(w2.x) * silu_f(bf_hi(z2.x)));
+    const __nv_bfloat162 p1 = __floats2bfloat162_rn(o4.z * rstd * bf_lo(w2.y) * silu_f(bf_lo(z2.y)),
+                                                    o4.w * rstd * bf_hi(w2.y) * silu_f(bf_hi(z2.y)));
+    uint2 r;
+    r.x = *reinterpret_cast<const uint32_t*>(&p0); r.y = *reinterpret_cast<const uint32_t*>(&p1);
+    reinterpret_cast<uint2*>(out + (size_t)wid * DN_VAL)[lane] = r;
+}
+
+// ---- attention pieces ------------------------------------------------------------------------------
+
+// per-head RMSNorm(1+w) + partial RoPE; q rewritten in place (bf16), K and V appended to the caches.
+// warp per (t, slot): slots 0-7 = q heads, 8-9 = k heads, 10-11 = v heads.  Row layout of the fused
+// projection: 8 x [q(256) | gate(256)], k(512), v(512).  (reference: prefill.cu:1041-1087)
+__global__ void k_fa_norm_rope(__nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ q_norm,
+                               const __nv_bfloat16* __restrict__ k_norm, __nv_bfloat16* __restrict__ kc,
+                               __nv_bfloat16* __restrict__ vc, int S, int max_seq) {
+    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (wid >= S * 12) return;
+    const int t = wid / 12, slot = wid % 12;
+    __nv_bfloat16* row = qkv + (size_t)t * FA_QKV_ROWS;
+    if (slot >= 10) {
+        const int g = slot - 10;
+        const uint4* src = reinterpret_cast<const uint4*>(row + FA_QPROJ + FA_KV_SIZE + g * FA_HEAD_DIM);
+        reinterpret_cast<uint4*>(vc + ((size_t)g * max_seq + t) * FA_HEAD_DIM)[lane] = src[lane];
+        return;
+    }
+    const bool isq = slot < 8;
+    __nv_bfloat16* src = isq ? row + slot * 2 * FA_HEAD_DIM : row + FA_QPROJ + (slot - 8) * FA_HEAD_DIM;
+    const __nv_bfloat16* wn = isq ? q_norm : k_norm;
+    float n[8], ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { n[e] = ld_bf(src + lane + 32 * e); ss += n[e] * n[e]; }
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss * (1.0f / FA_HEAD_DIM) + RMS_EPS);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) n[e] = n[e] * rstd * (1.0f + ld_bf(wn + lane + 32 * e));
+    float sn, cs;
+    sincosf((float)t * c_pf_inv_freq[lane], &sn, &cs);
+    const float a = n[0], b = n[1];
+    n[0] = a * cs - b * sn;
+    n[1] = b * cs + a * sn;
+    __nv_bfloat16* dst = isq ? src : kc + ((size_t)(slot - 8) * max_seq + t) * FA_HEAD_DIM;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dst[lane + 32 * e] = __float2bfloat16_rn(n[e]);
+}
+
+// causal attention, online softmax, one warp per (query t, head); out = softmax(q k / 16) v * sigmoid(gate)
+// (reference: prefill.cu:270-294, 1182-1200)
+__global__ void k_fa_attention(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ kc,
+                               const __nv_bfloat16* __restrict__ vc, __nv_bfloat16* __restrict__ out, int S, int max_seq) {
+    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (wid >= S * FA_Q_HEADS) return;
+    const int t = wid >> 3, h = wid & 7, g = h / FA_GQA;
+    const __nv_bfloat16* qrow = qkv + (size_t)t * FA_QKV_ROWS + h * 2 * FA_HEAD_DIM;
+    float q[8], acc[8], m = -1e30f, l = 0.f;
+    {
+        const uint4 u = reinterpret_cast<const uint4*>(qrow)[lane];
+        q[0] = bf_lo(u.x); q[1] = bf_hi(u.x); q[2] = bf_lo(u.y); q[3] = bf_hi(u.y);
+        q[4] = bf_lo(u.z); q[5] = bf_hi(u.z); q[6] = bf_lo(u.w); q[7] = bf_hi(u.w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { q[e] *= 0.0625f; acc[e] = 0.f; }
+    }
+    const __nv_bfloat16* K = kc + (size_t)g * max_seq * FA_HEAD_DIM;
+    const __nv_bfloat16* V = vc + (size_t)g * max_seq * FA_HEAD_DIM;
+    for (int p = 0; p <= t; ++p) {
+        const uint4 ku = reinterpret_cast<const uint4*>(K + (size_t)p * FA_HEAD_DIM)[lane];
+        const uint4 vu = reinterpret_cast<const uint4*>(V + (size_t)p * FA_HEAD_DIM)[lane];
+        float s = q[0] * bf_lo(ku.x) + q[1] * bf_hi(ku.x) + q[2] * bf_lo(ku.y) + q[3] * bf_hi(ku.y) +
+                  q[4] * bf_lo(ku.z) + q[5] * bf_hi(ku.z) + q[6] * bf_lo(ku.w) + q[7] * bf_hi(ku.w);
+        s = warp_sum(s);
+        const float mn = fmaxf(m, s), corr = __expf(m - mn), pe = __expf(s - mn);
+        l = l * corr + pe;
+        acc[0] = acc[0] * corr + pe * bf_lo(vu.x); acc[1] = acc[1] * corr + pe * bf_hi(vu.x);
+        acc[2] = acc[2] * corr + pe * bf_lo(vu.y); acc[3] = acc[3] * corr + pe * bf_hi(vu.y);
+        acc[4] = acc[4] * corr + pe * bf_lo(vu.z); acc[5] = acc[5] * corr + pe * bf_hi(vu.z);
+        acc[6] = acc[6] * corr + pe * bf_lo(vu.w); acc[7] = acc[7] * corr + pe * bf_hi(vu.w);
+        m = mn;
+    }
+    const uint4 gu = reinterpret_cast<const uint4*>(qrow + FA_HEAD_DIM)[lane];
+    const float gt[8] = {bf_lo(gu.x), bf_hi(gu.x), bf_lo(gu.y), bf_hi(gu.y), bf_lo(gu.z), bf_hi(gu.z), bf_lo(gu.w), bf_hi(gu.w)};
+    const float inv = 1.0f / l;
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 p2 = __floats2bfloat162_rn(acc[2 * e] * inv * sigmoid_f(gt[2 * e]),
+                                                        acc[2 * e + 1] * inv * sigmoid_f(gt[2 * e + 1]));
+        o[e] = *reinterpret_cast<const uint32_t*>(&p2);
+    }
+    reinterpret_cast<uint4*>(out + (size_t)t * FA_Q_SIZE + h * FA_HEAD_DIM)[lane] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ---- MLP glue, final norm, LM head -------------------------------------------------------------------
+
+// act[t, i] = silu(gu[t, i]) * gu[t, 3584 + i]   (reference: prefill.cu:1239-1247)
+__global__ void k_silu_mul(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ act, int S) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;     // one thread per 8 outputs
+    if (i >= (size_t)S * (INTER / 8)) return;
+    const size_t t = i / (INTER / 8), c = (i % (INTER / 8)) * 8;
+    const uint4 gv = *reinterpret_cast<const uint4*>(gu + t * (2 * INTER) + c);
+    const uint4 uv = *reinterpret_cast<const uint4*>(gu + t * (2 * INTER) + INTER + c);
+    const uint32_t ga[4] = {gv.x, gv.y, gv.z, gv.w}, ua[4] = {uv.x, uv.y, uv.z, uv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 p = __floats2bfloat162_rn(silu_f(bf_lo(ga[e])) * bf_lo(ua[e]), silu_f(bf_hi(ga[e])) * bf_hi(ua[e]));
+        o[e] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    *reinterpret_cast<uint4*>(act + t * INTER + c) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// last row: final norm (f32 for the LM head, bf16 copy for the caller) (reference: prefill.cu:297-311)
+__global__ void k_final_norm(const __nv_bfloat16* __restrict__ hidden_last, const __nv_bfloat16* __restrict__ w,
+                             float* __restrict__ normed_f32, __nv_bfloat16* __restrict__ normed_bf16,
+                             __nv_bfloat16* __restrict__ hidden_out) {
+    __shared__ float red[32];
+    float v[2], ss = 0.f;
+    for (int i = 0; i < 2; ++i) { v[i] = ld_bf(hidden_last + threadIdx.x + 512 * i); ss += v[i] * v[i]; }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < 16; ++i) tot += red[i];
+    const float rstd = rsqrtf(tot * (1.0f / HIDDEN) + RMS_EPS);
+    for (int i = 0; i < 2; ++i) {
+        const int c = threadIdx.x + 512 * i;
+        const float x = v[i] * rstd * (1.0f + ld_bf(w + c));
+        normed_f32[c] = x;
+        if (normed_bf16) normed_bf16[c] = __float2bfloat16_rn(x);
+        if (hidden_out) hidden_out[c] = hidden_last[c];
+    }
+}
+
+// logits = W x, per-block argmax (lowest index on ties) (reference: prefill.cu:314-339)
+__global__ void __launch_bounds__(256) k_lm_head(const float* __restrict__ x, const __nv_bfloat16* __restrict__ W, int vocab,
+                                                 float* __restrict__ bval, int* __restrict__ bidx) {
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float xr[32];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xr[i * 8 + e] = x[i * 256 + lane * 8 + e];
+    }
+    float best = -INFINITY;
+    int besti = 0x7fffffff;
+    for (int row = blockIdx.x * 8 + warp; row < vocab; row += gridDim.x * 8) {
+        const uint4* wp = reinterpret_cast<const uint4*>(W + (size_t)row * HIDDEN) + lane;
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc = dot8(__ldg(wp + i * 32), xr + i * 8, acc);
+        acc = warp_sum(acc);
+        if (acc > best) { best = acc; besti = row; }
+    }
+    if (lane == 0) { sv[warp] = best; si[warp] = besti; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w)
+            if (sv[w] > best || (sv[w] == best && si[w] < besti)) { best = sv[w]; besti = si[w]; }
+        bval[blockIdx.x] = best;
+        bidx[blockIdx.x] = besti;
+    }
+}
+
+__global__ void k_lm_reduce(const float* __restrict__ bval, const int* __restrict__ bidx, int n, int* __restrict__ out) {
+    float best = -INFINITY;
+    int besti = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += 32) {
+        const float v = bval[i];
+        const int ix = bidx[i];
+        if (v > best || (v == best && ix < besti)) { best = v; besti = ix; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+        if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+    }
+    if (threadIdx.x == 0) *out = besti;
+}
+
+// ---- workspace -----------------------------------------------------------------------------------------
+
+struct PrefillWs {
+    int cap = 0;                    // tokens the buffers are sized for
+    __nv_bfloat16 *hidden = nullptr, *normed = nullptr, *wide = nullptr, *z = nullptr, *act = nullptr;
+    float *pre = nullptr, *o = nullptr, *beta = nullptr, *decay = nullptr, *kq = nullptr, *normed_f32 = nullptr, *bval = nullptr;
+    int *bidx = nullptr, *err = nullptr;
+};
+PrefillWs g_pws[64];
+constexpr int LM_BLOCKS = 1184;     // 8 resident blocks of 256 threads on each of 148 SMs
+
+cudaError_t ensure_ws(PrefillWs& w, int S) {
+    if (S <= w.cap) return cudaSuccess;
+    void** ptrs[] = {(void**)&w.hidden, (void**)&w.normed, (void**)&w.wide, (void**)&w.z, (void**)&w.act, (void**)&w.pre,
+                     (void**)&w.o, (void**)&w.beta, (void**)&w.decay, (void**)&w.kq};
+    for (void** p : ptrs) { if (*p) cudaFree(*p); *p = nullptr; }
+    const size_t s = (size_t)S;
+    const size_t sizes[] = {s * HIDDEN * 2, s * HIDDEN * 2, s * 2 * INTER * 2, s * DN_V * 2, s * INTER * 2,
+                            s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 4, s * 16 * 4, s * 16 * 4};
+    for (int i = 0; i < 10; ++i) {
+        cudaError_t e = cudaMalloc(ptrs[i], sizes[i]);
+        if (e != cudaSuccess) { w.cap = 0; return e; }
+    }
+    if (!w.normed_f32) {
+        cudaError_t e = cudaMalloc((void**)&w.normed_f32, HIDDEN * 4);
+        if (e == cudaSuccess) e = cudaMalloc((void**)&w.bval, LM_BLOCKS * 4);
+        if (e == cudaSuccess) e = cudaMalloc((void**)&w.bidx, LM_BLOCKS * 4);
+        if (e == cudaSuccess) e = cudaMalloc((void**)&w.err, 4);
+        if (e == cudaSuccess) e = cudaMemset(w.err, 0, 4);
+        if (e != cudaSuccess) return e;
+        float tab[FA_ROT / 2];
+        for (int i = 0; i < FA_ROT / 2; ++i) tab[i] = (float)(1.0 / pow(ROPE_THETA, (2.0 * i) / FA_ROT));
+        e = cudaMemcpyToSymbol(c_pf_inv_freq, tab, sizeof(tab));
+        if (e != cudaSuccess) return e;
+    }
+    w.cap = S;
+    return cudaSuccess;
+}
+
+thread_local char g_perr[200] = "";
+int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
+    if (e != cudaSuccess) snprintf(g_perr, sizeof(g_perr), "%s: %s", what, cudaGetErrorString(e));
+    else snprintf(g_perr, sizeof(g_perr), "%s", what);
+    return code;
+}
+
+#define PF_CHECK(call, what)                                     \
+    do {                                                         \
+        cudaError_t e_ = (call);                                 \
+        if (e_ != cudaSuccess) return pfail(MK_ERR_CUDA, what, e_); \
+    } while (0)
+
+}  // namespace
+}  // namespace mk
+
+extern "C" const char* mk_prefill_error(void) { return mk::g_perr; }
+
+extern "C" int mk_prefill_bf16(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const MkLayerWeights* layers, const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    const void* fused_fa_qkv_base, const void* fused_gate_up_base,
+    void* final_normed, void* hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream) {
+    using namespace mk;
+    if (!token_ids || !output_token || !embed_weight || !layers || !final_norm_w || !lm_head_w || !fa_k_cache ||
+        !fa_v_cache || !dn_states || !conv_bufs || !fused_fa_qkv_base || !fused_gate_up_base)
+        return pfail(MK_ERR_BAD_ARG, "null pointer argument");
+    if (seq_len <= 0 || seq_len > max_seq_len) return pfail(MK_ERR_BAD_ARG, "seq_len must be in [1, max_seq_len]");
+    if (num_layers < 1 || num_layers > MAX_LAYERS || vocab < 1) return pfail(MK_ERR_BAD_ARG, "bad model dimensions");
+    int dev = 0;
+    PF_CHECK(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return pfail(MK_ERR_BAD_ARG, "device index out of range");
+    PrefillWs& w = g_pws[dev];
+    PF_CHECK(ensure_ws(w, seq_len), "prefill workspace");
+
+    // the pointer table lives on the device; the launches below need its entries on the host
+    LayerWeights hl[MAX_LAYERS];
+    PF_CHECK(cudaMemcpyAsync(hl, layers, (size_t)num_layers * sizeof(LayerWeights), cudaMemcpyDeviceToHost, stream), "table copy");
+    PF_CHECK(cudaStreamSynchronize(stream), "table copy sync");
+
+    const int S = seq_len;
+    typedef __nv_bfloat16 bf;
+    auto gemm = [&](const void* A, const void* W, void* C, const void* R, int N, int K) {
+        return gemm_bf16_tn(A, W, C, R, S, N, K, K, N, w.err, stream);
+    };
+    const int wpb = 8;                                            // warps per 256-thread block
+    auto blocks_for_warps = [&](long long nw) { return (unsigned)((nw + wpb - 1) / wpb); };
+
+    k_embed<<<S, 128, 0, stream>>>(token_ids, (const bf*)embed_weight, w.hidden, S, vocab);
+    int dn_idx = 0, fa_idx = 0;
+    for (int li = 0; li < num_layers; ++li) {
+        const LayerWeights& lw = hl[li];
+        const bool dn = (lw.layer_type == 0);
+        k_rmsnorm<<<blocks_for_warps(S), 256, 0, stream>>>(w.hidden, (const bf*)lw.ptrs[0], w.normed, S);
+        if (dn) {
+            float* state = (float*)dn_states + (size_t)dn_idx * DN_HEADS * DN_VAL * DN_KEY;
+            float* cstate = (float*)conv_bufs + (size_t)dn_idx * DN_CONV_CH * DN_CONV_K;
+            PF_CHECK(gemm(w.normed, lw.ptrs[DN_W_QKV], w.wide, nullptr, DN_CONV_CH, HIDDEN), "gemm qkv");
+            PF_CHECK(gemm(w.normed, lw.ptrs[DN_W_Z], w.z, nullptr, DN_V, HIDDEN), "gemm z");
+            k_dn_gates<<<blocks_for_warps((long long)S * 32), 256, 0, stream>>>(
+                w.normed, (const bf*)lw.ptrs[DN_W_B], (const bf*)lw.ptrs[DN_W_A], (const bf*)lw.ptrs[DN_A_LOG],
+                (const bf*)lw.ptrs[DN_DT_BIAS], w.beta, w.decay, S);
+            k_dn_preproject<<<dim3(S, DN_HEADS), 128, 0, stream>>>(w.wide, (const bf*)lw.ptrs[DN_CONV_W], cstate, w.pre, w.kq, S);
+            k_dn_scan<<<128, 512, 0, stream>>>(w.pre, w.beta, w.decay, w.kq, state, w.o, S);
+            k_dn_conv_state<<<(DN_CONV_CH + 255) / 256, 256, 0, stream>>>(w.wide, cstate, S);
+            k_dn_gated_norm<<<blocks_for_warps((long long)S * DN_HEADS), 256, 0, stream>>>(w.o, w.z, (const bf*)lw.ptrs[DN_NORM_W], w.act, S);
+            PF_CHECK(gemm(w.act, lw.ptrs[DN_W_OUT], w.hidden, w.hidden, HIDDEN, DN_V), "gemm out");
+            ++dn_idx;
+        } else {
+            bf* kc = (bf*)fa_k_cache + (size_t)fa_idx * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;
+            bf* vc = (bf*)fa_v_cache + (size_t)fa_idx * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;
+            const bf* wqkv = (const bf*)fused_fa_qkv_base + (size_t)fa_idx * FA_QKV_ROWS * HIDDEN;
+            PF_CHECK(gemm(w.normed, wqkv, w.wide, nullptr, FA_QKV_ROWS, HIDDEN), "gemm fa qkv");
+            k_fa_norm_rope<<<blocks_for_warps((long long)S * 12), 256, 0, stream>>>(
+                w.wide, (const bf*)lw.ptrs[FA_Q_NORM], (const bf*)lw.ptrs[FA_K_NORM], kc, vc, S, max_seq_len);
+            k_fa_attention<<<blocks_for_warps((long long)S * FA_Q_HEADS), 256, 0, stream>>>(w.wide, kc, vc, w.act, S, max_seq_len);
+            PF_CHECK(gemm(w.act, lw.ptrs[FA_W_O], w.hidden, w.hidden, HIDDEN, FA_Q_SIZE), "gemm o");
+            ++fa_idx;
+        }
+        k_rmsnorm<<<blocks_for_warps(S), 256, 0, stream>>>(w.hidden, (const bf*)lw.ptrs[dn ? (int)DN_POST_NORM : (int)FA_POST_NORM], w.normed, S);
+        const bf* wgu = (const bf*)fused_gate_up_base + (size_t)li * 2 * INTER * HIDDEN;
+        PF_CHECK(gemm(w.normed, wgu, w.wide, nullptr, 2 * INTER, HIDDEN), "gemm gate_up");
+        k_silu_mul<<<(unsigned)(((size_t)S * (INTER / 8) + 255) / 256), 256, 0, stream>>>(w.wide, w.act, S);
+        PF_CHECK(gemm(w.act, lw.ptrs[dn ? (int)DN_W_DOWN : (int)FA_W_DOWN], w.hidden, w.hidden, HIDDEN, INTER), "gemm down");
+    }
+    k_final_norm<<<1, 512, 0, stream>>>(w.hidden + (size_t)(S - 1) * HIDDEN, (const bf*)final_norm_w, w.normed_f32,
+                                        (bf*)final_normed, (bf*)hidden_bf16_out);
+    k_lm_head<<<LM_BLOCKS, 256, 0, stream>>>(w.normed_f32, (const bf*)lm_head_w, vocab, w.bval, w.bidx);
+    k_lm_reduce<<<1, 32, 0, stream>>>(w.bval, w.bidx, LM_BLOCKS, output_token);
+    PF_CHECK(cudaGetLastError(), "prefill launch");
+    return MK_OK;
+}
+
+// Reference-compatible entry (reference: megakernel/prefill.cu:1559-1576, declared at
+// megakernel/torch_bindings.cpp:354-368).  The caller's scratch buffers are accepted and ignored:
+// the library sizes its own workspace (the reference's scratch layout overruns proj_buf for the
+// fused gate/up tile and cannot hold S x 7168).
+extern "C" int launch_prefill_bf16(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const MkLayerWeights* layers,
+    const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden, void* residual, void* normalized,
+    void* proj_buf, void* proj_buf2, void* attn_buf, void* mlp_buf,
+    void* dn_out_buf, void* beta_buf, void* alpha_buf, void* dn_pre_qkv,
+    void* dn_u_scratch, void* dn_w_scratch, void* dn_cs_scratch,
+    const void* fused_fa_qkv_base, const void* fused_gate_up_base,
+    void* final_normed, void* hidden_bf16_out,
+    void* lm_bmv, void* lm_bmi,
+    int max_seq_len, cudaStream_t stream) {
+    (void)hidden; (void)residual; (void)normalized; (void)proj_buf; (void)proj_buf2; (void)attn_buf; (void)mlp_buf;
+    (void)dn_out_buf; (void)beta_buf; (void)alpha_buf; (void)dn_pre_qkv; (void)dn_u_scratch; (void)dn_w_scratch;
+    (void)dn_cs_scratch; (void)lm_bmv; (void)lm_bmi;
+    int nl = 0, vocab = 0;
+    mk_get_model_dims(&nl, &vocab);
+    return mk_prefill_bf16(token_ids, seq_len, output_token, embed_weight, layers, final_norm_w, lm_head_w, fa_k_cache,
+                           fa_v_cache, dn_states, conv_bufs, fused_fa_qkv_base, fused_gate_up_base, final_normed,
+                           hidden_bf16_out, max_seq_len, nl, vocab, stream);
+}

@@ -87,6 +87,46 @@ void decode(Tensor output_token, int64_t input_token_id, Tensor embed_weight, Te
     (void)barrier_counter; (void)barrier_generation; (void)block_max_vals; (void)block_max_idxs; (void)lm_sync_counter;
 }
 
+void prefill_bf16(Tensor output_token, Tensor token_ids, Tensor embed_weight, Tensor layer_weights_packed,
+                  Tensor final_norm_weight, Tensor lm_head_weight, Tensor fa_k_cache, Tensor fa_v_cache,
+                  Tensor dn_states, Tensor conv_bufs, Tensor hidden, Tensor residual, Tensor normalized,
+                  Tensor proj_buf, Tensor proj_buf2, Tensor attn_buf, Tensor mlp_buf, Tensor dn_out_buf,
+                  Tensor beta_buf, Tensor alpha_buf, Tensor dn_pre_qkv, Tensor dn_u_scratch, Tensor dn_w_scratch,
+                  Tensor dn_cs_scratch, Tensor fused_fa_qkv, Tensor fused_gate_up, Tensor final_normed,
+                  Tensor hidden_bf16_out, Tensor lm_bmv, Tensor lm_bmi, int64_t max_seq_len) {
+    const auto bf16 = torch::kBFloat16;
+    const auto f32 = torch::kFloat32;
+    need(output_token, "output_token", torch::kInt32, 1);
+    need(token_ids, "token_ids", torch::kInt32, 1);
+    TORCH_CHECK(token_ids.dim() == 1, "token_ids must be 1-D");
+    need(embed_weight, "embed_weight", bf16, 1024);
+    need(layer_weights_packed, "layer_weights_packed", torch::kUInt8, 128);
+    need(final_norm_weight, "final_norm_weight", bf16, 1024);
+    need(lm_head_weight, "lm_head_weight", bf16, 1024);
+    need(fa_k_cache, "fa_k_cache", bf16, 2 * max_seq_len * 256);
+    need(fa_v_cache, "fa_v_cache", bf16, 2 * max_seq_len * 256);
+    need(dn_states, "dn_states", f32, 16 * 128 * 128);
+    need(conv_bufs, "conv_bufs", f32, 6144 * 4);
+    need(fused_fa_qkv, "fused_fa_qkv", bf16, 5120 * 1024);
+    need(fused_gate_up, "fused_gate_up", bf16, 7168 * 1024);
+    need(final_normed, "final_normed", bf16, 1024);
+    need(hidden_bf16_out, "hidden_bf16_out", bf16, 1024);
+    TORCH_CHECK(token_ids.size(0) <= max_seq_len, "prompt longer than max_seq_len");
+    DeviceGuard guard(embed_weight);
+    check_status(mk_set_model_dims((int)(layer_weights_packed.numel() / 128), (int)embed_weight.size(0)), "prefill_bf16");
+    const int rc = launch_prefill_bf16(
+        (const int*)token_ids.data_ptr(), (int)token_ids.size(0), (int*)output_token.data_ptr(), embed_weight.data_ptr(),
+        (const MkLayerWeights*)layer_weights_packed.data_ptr(), final_norm_weight.data_ptr(), lm_head_weight.data_ptr(),
+        fa_k_cache.data_ptr(), fa_v_cache.data_ptr(), dn_states.data_ptr(), conv_bufs.data_ptr(), nullptr, nullptr,
+        nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+        fused_fa_qkv.data_ptr(), fused_gate_up.data_ptr(), final_normed.data_ptr(), hidden_bf16_out.data_ptr(), nullptr,
+        nullptr, (int)max_seq_len, current_stream(embed_weight));
+    TORCH_CHECK(rc == MK_OK, "qwen35_megakernel_bf16_C::prefill_bf16 failed (", rc, "): ", mk_prefill_error());
+    (void)hidden; (void)residual; (void)normalized; (void)proj_buf; (void)proj_buf2; (void)attn_buf; (void)mlp_buf;
+    (void)dn_out_buf; (void)beta_buf; (void)alpha_buf; (void)dn_pre_qkv; (void)dn_u_scratch; (void)dn_w_scratch;
+    (void)dn_cs_scratch; (void)lm_bmv; (void)lm_bmi;
+}
+
 int64_t max_safe_decode_blocks() { return query_max_safe_decode_blocks(); }
 
 void set_decode_blocks(int64_t blocks) {
@@ -110,6 +150,20 @@ TORCH_LIBRARY(qwen35_megakernel_bf16_C, ops) {
             "Tensor seen_token_mask, float repetition_penalty, "
             "int position, int max_seq_len) -> ()");
     ops.impl("decode", torch::kCUDA, &decode);
+
+    ops.def("prefill_bf16(Tensor output_token, Tensor token_ids, "
+            "Tensor embed_weight, Tensor layer_weights_packed, "
+            "Tensor final_norm_weight, Tensor lm_head_weight, "
+            "Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs, "
+            "Tensor hidden, Tensor residual, Tensor normalized, "
+            "Tensor proj_buf, Tensor proj_buf2, Tensor attn_buf, Tensor mlp_buf, "
+            "Tensor dn_out_buf, Tensor beta_buf, Tensor alpha_buf, "
+            "Tensor dn_pre_qkv, "
+            "Tensor dn_u_scratch, Tensor dn_w_scratch, Tensor dn_cs_scratch, "
+            "Tensor fused_fa_qkv, Tensor fused_gate_up, "
+            "Tensor final_normed, Tensor hidden_bf16_out, "
+            "Tensor lm_bmv, Tensor lm_bmi, int max_seq_len) -> ()");
+    ops.impl("prefill_bf16", torch::kCUDA, &prefill_bf16);
 
     ops.def("max_safe_decode_blocks() -> int");
     ops.impl("max_safe_decode_blocks", &max_safe_decode_blocks);

@@ -177,6 +177,17 @@ class Decoder:
         self._seen_token_mask = torch.zeros(self.vocab, **f32)
         self._out_token = torch.empty(1, **i32)
         self._token_buffer = torch.empty(1, **i32)
+        self._final_normed = torch.empty(HIDDEN_SIZE, **bf16)
+        self._hidden_bf16_out = torch.empty(HIDDEN_SIZE, **bf16)
+
+        # fused weights for the prefill GEMMs: q|k|v rows of every attention layer and gate|up rows
+        # of every layer (reference: megakernel/model.py:242-260)
+        fa = [torch.cat([ld["ptrs"][1], ld["ptrs"][2], ld["ptrs"][3]], dim=0) for ld in layer_data if ld["type"] == 1]
+        self._fused_fa_qkv = (torch.stack(fa, dim=0).contiguous() if fa
+                              else torch.zeros(1, FA_QPROJ_SIZE + 2 * FA_KV_SIZE, HIDDEN_SIZE, **bf16))
+        gu = [torch.cat([ld["ptrs"][11], ld["ptrs"][12]] if ld["type"] == 0 else [ld["ptrs"][8], ld["ptrs"][9]], dim=0)
+              for ld in layer_data]
+        self._fused_gate_up = torch.stack(gu, dim=0).contiguous()
 
     # ------------------------------------------------------------------------------------
     def _bind_dims(self):
@@ -245,6 +256,46 @@ class Decoder:
             ctypes.c_int(self._position), ctypes.c_int(self.max_seq_len), self._stream()))
         self._position += steps
         return out
+
+    def alloc_prefill_scratch(self, S: int):
+        """Scratch tensors of the reference's prefill signature (reference: megakernel/model.py:262-272).
+        The sm_100a prefill keeps its own workspace, so these are minimal placeholders."""
+        f32 = dict(dtype=torch.float32, device=self._embed_weight.device)
+        return dict(dn_pre_qkv=torch.empty(1, **f32), dn_u_scratch=torch.empty(1, **f32),
+                    dn_w_scratch=torch.empty(1, **f32), dn_cs_scratch=torch.empty(1, **f32))
+
+    def prefill(self, token_ids) -> int:
+        """Process a whole prompt from position 0 (state must be reset); returns the first generated
+        token.  Afterwards step()/step_many() continue from position len(token_ids)."""
+        ids = torch.as_tensor(token_ids, dtype=torch.int32).to(self._embed_weight.device).contiguous()
+        S = int(ids.numel())
+        if S < 1 or S > self.max_seq_len:
+            raise ValueError("prompt length must be in [1, max_seq_len]")
+        if self._position != 0:
+            raise ValueError("prefill starts at position 0: call reset() first")
+        self._bind_dims()
+        if self.api == "ops":
+            e = torch.empty(1, dtype=torch.bfloat16, device=ids.device)
+            f = torch.empty(1, dtype=torch.float32, device=ids.device)
+            i = torch.empty(1, dtype=torch.int32, device=ids.device)
+            self._ops.prefill_bf16(
+                self._out_token, ids, self._embed_weight, self._layer_weights_packed, self._final_norm_weight,
+                self._lm_head_weight, self._fa_k_cache, self._fa_v_cache, self._dn_states, self._conv_bufs,
+                e, e, e, e, e, e, e, e, f, f, f, f, f, f, self._fused_fa_qkv, self._fused_gate_up,
+                self._final_normed, self._hidden_bf16_out, f, i, self.max_seq_len)
+        else:
+            self._lib.mk_prefill_error.restype = ctypes.c_char_p
+            rc = self._lib.mk_prefill_bf16(
+                _ptr(ids), ctypes.c_int(S), _ptr(self._out_token), _ptr(self._embed_weight),
+                _ptr(self._layer_weights_packed), _ptr(self._final_norm_weight), _ptr(self._lm_head_weight),
+                _ptr(self._fa_k_cache), _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs),
+                _ptr(self._fused_fa_qkv), _ptr(self._fused_gate_up), _ptr(self._final_normed),
+                _ptr(self._hidden_bf16_out), ctypes.c_int(self.max_seq_len), ctypes.c_int(self.num_layers),
+                ctypes.c_int(self.vocab), self._stream())
+            if rc != 0:
+                raise RuntimeError(f"prefill failed ({rc}): {self._lib.mk_prefill_error().decode()}")
+        self._position = S
+        return int(self._out_token.item())
 
     def reset(self):
         self._position = 0
