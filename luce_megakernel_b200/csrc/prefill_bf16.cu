@@ -95,11 +95,11 @@ __global__ void k_dn_gates(const __nv_bfloat16* __restrict__ xn, const __nv_bflo
     }
     acc = warp_sum(acc);
     if (lane == 0) {
-        if (o < 16) beta[t * 16 + h] = 1.0f / (1.0f + expf(-acc));
+        if (o < 16) beta[(t * 16 + h) * 4] = 1.0f / (1.0f + expf(-acc));
         else {
             const float x = acc + ld_bf(dt_bias + h);
             const float sp = (x > 20.0f) ? x : log1pf(expf(x));
-            decay[t * 16 + h] = expf(-expf(ld_bf(a_log + h)) * sp);
+            decay[(t * 16 + h) * 4 + 1] = expf(-expf(ld_bf(a_log + h)) * sp);
         }
     }
 }
@@ -137,7 +137,7 @@ __global__ void k_dn_preproject(const __nv_bfloat16* __restrict__ qkv, const __n
     dst[0] = val[0] * qn;
     dst[DN_QK] = val[1] * kn;
     dst[2 * DN_QK] = val[2];
-    if (c == 0) kq[t * 16 + h] = sqk * qn * kn;
+    if (c == 0) kq[(t * 16 + h) * 4 + 2] = sqk * qn * kn;
 }
 
 // conv window after the prompt: the last four pre-activation inputs (reference: prefill.cu:1373-1395)
@@ -156,38 +156,76 @@ __global__ void k_dn_conv_state(const __nv_bfloat16* __restrict__ qkv, float* __
     for (int k = 0; k < 4; ++k) conv_state[ch * 4 + k] = nw[k];
 }
 
-// Gated delta rule, token-serial; block = (head, 16 value rows), warp = one value row, lane = 4 keys.
-// The state row lives in registers across the whole prompt.  (reference: prefill.cu:114-221)
-__global__ void __launch_bounds__(512) k_dn_scan(const float* __restrict__ pre, const float* __restrict__ beta,
-                                                 const float* __restrict__ decay, const float* __restrict__ kq,
+// Gated delta rule, token-serial.  Block = (head, 16 value rows), 16 warps; warp = one value row,
+// lane = 4 keys, the state row stays in registers for the whole prompt.  The per-token inputs
+// (q and k of the head, the 16 v values, beta / decay / q.k) are staged through shared memory in
+// tiles of 32 tokens with cp.async double buffering, so a step costs shared-memory latency plus
+// the two warp reductions instead of an L2 round trip.  (reference: prefill.cu:114-221)
+constexpr int SCAN_TT = 32;                       // tokens per staged tile
+constexpr int SCAN_TOK_FLOATS = 256 + 16 + 4;     // q[128] | k[128] | v[16 rows of this block] | beta, decay, q.k, pad
+constexpr int SCAN_TILE_FLOATS = SCAN_TT * SCAN_TOK_FLOATS;
+constexpr int SCAN_SMEM = 2 * SCAN_TILE_FLOATS * 4;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// gates: [t][head][4] = beta, decay, q.k, unused
+__global__ void __launch_bounds__(512) k_dn_scan(const float* __restrict__ pre, const float* __restrict__ gates,
                                                  float* __restrict__ state, float* __restrict__ o, int S) {
-    const int h = blockIdx.x >> 3, j = (blockIdx.x & 7) * 16 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    float* srow = state + ((size_t)h * DN_VAL + j) * DN_KEY;
+    extern __shared__ __align__(16) float scan_sm[];
+    const int h = blockIdx.x >> 3, slice = blockIdx.x & 7;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = slice * 16 + warp;
+    float* srow = state + ((size_t)h * DN_VAL + row) * DN_KEY;
     float4 s = reinterpret_cast<const float4*>(srow)[lane];
-    const float* qp = pre + h * DN_KEY + 4 * lane;
-    float4 q4 = *reinterpret_cast<const float4*>(qp), k4 = *reinterpret_cast<const float4*>(qp + DN_QK);
-    float vj = pre[2 * DN_QK + h * DN_VAL + j], b = beta[h], g = decay[h], qk = kq[h];
-    for (int t = 0; t < S; ++t) {
-        float4 qn = q4, kn = k4;
-        float vn = vj, bn = b, gn = g, qkn = qk;
-        if (t + 1 < S) {                      // prefetch the next token's inputs
-            const float* np = qp + (size_t)(t + 1) * DN_CONV_CH;
-            qn = *reinterpret_cast<const float4*>(np);
-            kn = *reinterpret_cast<const float4*>(np + DN_QK);
-            vn = pre[(size_t)(t + 1) * DN_CONV_CH + 2 * DN_QK + h * DN_VAL + j];
-            bn = beta[(t + 1) * 16 + h]; gn = decay[(t + 1) * 16 + h]; qkn = kq[(t + 1) * 16 + h];
+    const int ntiles = (S + SCAN_TT - 1) / SCAN_TT;
+    auto stage = [&](int tile, int buf) {
+        // per token 69 16-byte pieces: 32 of q, 32 of k, 4 of v, 1 of gates
+        float* dst = scan_sm + buf * SCAN_TILE_FLOATS;
+        for (int i = threadIdx.x; i < SCAN_TT * 69; i += 512) {
+            const int tt = i / 69, piece = i - tt * 69;
+            const int t = tile * SCAN_TT + tt;
+            if (t < S) {
+                const float* src;
+                if (piece < 32) src = pre + (size_t)t * DN_CONV_CH + h * DN_KEY + piece * 4;
+                else if (piece < 64) src = pre + (size_t)t * DN_CONV_CH + DN_QK + h * DN_KEY + (piece - 32) * 4;
+                else if (piece < 68) src = pre + (size_t)t * DN_CONV_CH + 2 * DN_QK + h * DN_VAL + slice * 16 + (piece - 64) * 4;
+                else src = gates + ((size_t)t * 16 + h) * 4;
+                cp_async16(dst + tt * SCAN_TOK_FLOATS + piece * 4, src);
+            }
         }
-        float stk = s.x * k4.x + s.y * k4.y + s.z * k4.z + s.w * k4.w;
-        float sqv = s.x * q4.x + s.y * q4.y + s.z * q4.z + s.w * q4.w;
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    stage(0, 0);
+    for (int tile = 0; tile < ntiles; ++tile) {
+        const int buf = tile & 1;
+        if (tile + 1 < ntiles) stage(tile + 1, buf ^ 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();
+        const float* tb = scan_sm + buf * SCAN_TILE_FLOATS;
+        const int t0 = tile * SCAN_TT, tn = min(SCAN_TT, S - t0);
+#pragma unroll 2
+        for (int tt = 0; tt < tn; ++tt) {
+            const float* tok = tb + tt * SCAN_TOK_FLOATS;
+            const float4 q4 = reinterpret_cast<const float4*>(tok)[lane];
+            const float4 k4 = reinterpret_cast<const float4*>(tok + 128)[lane];
+            const float vj = tok[256 + warp];
+            const float4 gt = *reinterpret_cast<const float4*>(tok + 272);     // beta, decay, q.k
+            float stk = s.x * k4.x + s.y * k4.y + s.z * k4.z + s.w * k4.w;
+            float sqv = s.x * q4.x + s.y * q4.y + s.z * q4.z + s.w * q4.w;
 #pragma unroll
-        for (int of = 16; of > 0; of >>= 1) {
-            stk += __shfl_xor_sync(0xffffffffu, stk, of);
-            sqv += __shfl_xor_sync(0xffffffffu, sqv, of);
+            for (int of = 16; of > 0; of >>= 1) {
+                stk += __shfl_xor_sync(0xffffffffu, stk, of);
+                sqv += __shfl_xor_sync(0xffffffffu, sqv, of);
+            }
+            const float err = (vj - gt.y * stk) * gt.x;
+            s.x = fmaf(s.x, gt.y, k4.x * err); s.y = fmaf(s.y, gt.y, k4.y * err);
+            s.z = fmaf(s.z, gt.y, k4.z * err); s.w = fmaf(s.w, gt.y, k4.w * err);
+            if (lane == 0) o[(size_t)(t0 + tt) * DN_V + h * DN_VAL + row] = gt.y * sqv + err * gt.z;
         }
-        const float err = (vj - g * stk) * b;
-        s.x = s.x * g + k4.x * err; s.y = s.y * g + k4.y * err; s.z = s.z * g + k4.z * err; s.w = s.w * g + k4.w * err;
-        if (lane == 0) o[(size_t)t * DN_V + h * DN_VAL + j] = g * sqv + err * qk;
-        q4 = qn; k4 = kn; vj = vn; b = bn; g = gn; qk = qkn;
+        __syncthreads();
     }
     reinterpret_cast<float4*>(srow)[lane] = s;
 }
@@ -402,7 +440,7 @@ cudaError_t ensure_ws(PrefillWs& w, int S) {
     for (void** p : ptrs) { if (*p) cudaFree(*p); *p = nullptr; }
     const size_t s = (size_t)S;
     const size_t sizes[] = {s * HIDDEN * 2, s * HIDDEN * 2, s * 2 * INTER * 2, s * DN_V * 2, s * INTER * 2,
-                            s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 4, s * 16 * 4, s * 16 * 4};
+                            s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 16, 16, 16};
     for (int i = 0; i < 10; ++i) {
         cudaError_t e = cudaMalloc(ptrs[i], sizes[i]);
         if (e != cudaSuccess) { w.cap = 0; return e; }
@@ -459,6 +497,11 @@ extern "C" int mk_prefill_bf16(
     if (dev < 0 || dev >= 64) return pfail(MK_ERR_BAD_ARG, "device index out of range");
     PrefillWs& w = g_pws[dev];
     PF_CHECK(ensure_ws(w, seq_len), "prefill workspace");
+    static bool scan_attr[64] = {false};
+    if (!scan_attr[dev]) {
+        PF_CHECK(cudaFuncSetAttribute(k_dn_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM), "scan smem");
+        scan_attr[dev] = true;
+    }
 
     // the pointer table lives on the device; the launches below need its entries on the host
     LayerWeights hl[MAX_LAYERS];
@@ -486,9 +529,9 @@ extern "C" int mk_prefill_bf16(
             PF_CHECK(gemm(w.normed, lw.ptrs[DN_W_Z], w.z, nullptr, DN_V, HIDDEN), "gemm z");
             k_dn_gates<<<blocks_for_warps((long long)S * 32), 256, 0, stream>>>(
                 w.normed, (const bf*)lw.ptrs[DN_W_B], (const bf*)lw.ptrs[DN_W_A], (const bf*)lw.ptrs[DN_A_LOG],
-                (const bf*)lw.ptrs[DN_DT_BIAS], w.beta, w.decay, S);
-            k_dn_preproject<<<dim3(S, DN_HEADS), 128, 0, stream>>>(w.wide, (const bf*)lw.ptrs[DN_CONV_W], cstate, w.pre, w.kq, S);
-            k_dn_scan<<<128, 512, 0, stream>>>(w.pre, w.beta, w.decay, w.kq, state, w.o, S);
+                (const bf*)lw.ptrs[DN_DT_BIAS], w.beta, w.beta, S);
+            k_dn_preproject<<<dim3(S, DN_HEADS), 128, 0, stream>>>(w.wide, (const bf*)lw.ptrs[DN_CONV_W], cstate, w.pre, w.beta, S);
+            k_dn_scan<<<128, 512, SCAN_SMEM, stream>>>(w.pre, w.beta, state, w.o, S);
             k_dn_conv_state<<<(DN_CONV_CH + 255) / 256, 256, 0, stream>>>(w.wide, cstate, S);
             k_dn_gated_norm<<<blocks_for_warps((long long)S * DN_HEADS), 256, 0, stream>>>(w.o, w.z, (const bf*)lw.ptrs[DN_NORM_W], w.act, S);
             PF_CHECK(gemm(w.act, lw.ptrs[DN_W_OUT], w.hidden, w.hidden, HIDDEN, DN_V), "gemm out");

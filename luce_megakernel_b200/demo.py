@@ -20,13 +20,25 @@ def main():
     ap.add_argument("--context", type=int, default=520)
     ap.add_argument("--layers", type=int, default=M.NUM_LAYERS)
     ap.add_argument("--vocab", type=int, default=M.VOCAB_SIZE)
+    ap.add_argument("--prefill", type=int, default=0, help="prompt length processed by the prefill op instead of the decode kernel")
     args = ap.parse_args()
     weights, _ = M.load_weights(seed=0, num_layers=args.layers, vocab=args.vocab, device_init=True)
     dec = M.Decoder(weights=weights, max_seq_len=max(2048, args.context + args.steps + 8), api="cabi")
-    tok = 11
-    for _ in range(4):                      # a short prompt through the decode kernel
-        tok = dec.step(tok)
-    dec._position = args.context            # continue at the requested context length
+    if args.prefill > 0:
+        g = torch.Generator().manual_seed(0)
+        ids = torch.randint(0, args.vocab, (args.prefill,), generator=g)
+        dec.prefill(ids)                    # warm-up (sizes the workspace)
+        dec.reset()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        tok = dec.prefill(ids)
+        dt = time.perf_counter() - t0
+        print(f"prefill of {args.prefill} tokens in {dt * 1e3:.2f} ms ({args.prefill / dt:.0f} tok/s)")
+    else:
+        tok = 11
+        for _ in range(4):                  # a short prompt through the decode kernel
+            tok = dec.step(tok)
+        dec._position = args.context        # continue at the requested context length
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     out = dec.step_many(tok, args.steps)
