@@ -95,6 +95,18 @@ int launch_quantize_nvfp4_lm_out(const void *weight, int rows, int cols,
                                  void *packed_out, void *scales_out, cudaStream_t stream);
 const char *mk_quantize_error(void);
 
+/* NVFP4 weights dequantised in registers.  format 0 = layer-weight format (fp16 scales per 32),
+ * format 1 = LM-head format (E4M3 scales per 16, tiled); value = e2m1(code) * scale
+ * (reference: megakernel/kernel_gb10_nvfp4.cu:80-83, 528-552, 682-856, 1439-1530).
+ * mk_matvec_nvfp4: y[rows] = dequant(W)[rows, cols] . x[cols], f32 in and out (the streaming
+ *   row product of the reference's matvec_nvfp4 / lm_head_kernel_nvfp4).
+ * mk_dequantize_nvfp4: out[rows, cols] f32 = dequantised weights, bit-exact to the reference's LUT * scale. */
+int mk_matvec_nvfp4(int format, const void *packed, const void *scales, const float *x, float *y,
+                    int rows, int cols, int group_size, cudaStream_t stream);
+int mk_dequantize_nvfp4(int format, const void *packed, const void *scales, float *out,
+                        int rows, int cols, int group_size, cudaStream_t stream);
+const char *mk_nvfp4_error(void);
+
 /* Prefill of a prompt of seq_len tokens from position 0: fills the KV caches for positions
  * 0..seq_len-1, advances the DeltaNet and conv state from their current content (callers zero
  * them first), writes the first generated token to output_token, the last row's final-normed

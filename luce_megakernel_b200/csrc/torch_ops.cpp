@@ -127,6 +127,38 @@ void prefill_bf16(Tensor output_token, Tensor token_ids, Tensor embed_weight, Te
     (void)dn_cs_scratch; (void)lm_bmv; (void)lm_bmi;
 }
 
+// NVFP4 quantisers (reference: megakernel/torch_bindings.cpp:272-337): same checks, same outputs.
+void quantize_nvfp4_out(Tensor packed_out, Tensor scales_out, Tensor weight, int64_t group_size) {
+    TORCH_CHECK(weight.is_cuda() && weight.is_contiguous() && weight.dim() == 2, "weight must be a contiguous 2-D CUDA tensor");
+    TORCH_CHECK(weight.scalar_type() == torch::kBFloat16, "weight must be bfloat16");
+    TORCH_CHECK(group_size > 0 && (group_size % 2) == 0, "group_size must be a positive even integer");
+    const int rows = (int)weight.size(0), cols = (int)weight.size(1);
+    TORCH_CHECK((cols % 2) == 0 && (cols % group_size) == 0, "in_dim must be divisible by 2 and by group_size");
+    need(packed_out, "packed_out", torch::kUInt8, (int64_t)rows * (cols / 2));
+    need(scales_out, "scales_out", torch::kFloat16, (int64_t)rows * (cols / group_size));
+    TORCH_CHECK(packed_out.numel() == (int64_t)rows * (cols / 2), "packed_out has the wrong size");
+    TORCH_CHECK(scales_out.numel() == (int64_t)rows * (cols / group_size), "scales_out has the wrong size");
+    DeviceGuard guard(weight);
+    const int rc = launch_quantize_nvfp4_out(weight.data_ptr(), rows, cols, (int)group_size, packed_out.data_ptr(),
+                                             scales_out.data_ptr(), current_stream(weight));
+    TORCH_CHECK(rc == MK_OK, "quantize_nvfp4_out failed: ", mk_quantize_error());
+}
+
+void quantize_nvfp4_lm_out(Tensor packed_out, Tensor scales_out, Tensor weight) {
+    TORCH_CHECK(weight.is_cuda() && weight.is_contiguous() && weight.dim() == 2, "weight must be a contiguous 2-D CUDA tensor");
+    TORCH_CHECK(weight.scalar_type() == torch::kBFloat16, "weight must be bfloat16");
+    const int rows = (int)weight.size(0), cols = (int)weight.size(1);
+    TORCH_CHECK((rows % 128) == 0, "out_dim must be divisible by 128");
+    TORCH_CHECK((cols % 64) == 0, "in_dim must be divisible by 64");
+    need(packed_out, "packed_out", torch::kUInt8, (int64_t)rows * (cols / 2));
+    need(scales_out, "scales_out", torch::kUInt8, (int64_t)(rows / 128) * (cols / 64) * 512);
+    TORCH_CHECK(scales_out.numel() == (int64_t)(rows / 128) * (cols / 64) * 512, "scales_out has the wrong size");
+    DeviceGuard guard(weight);
+    const int rc = launch_quantize_nvfp4_lm_out(weight.data_ptr(), rows, cols, packed_out.data_ptr(), scales_out.data_ptr(),
+                                                current_stream(weight));
+    TORCH_CHECK(rc == MK_OK, "quantize_nvfp4_lm_out failed: ", mk_quantize_error());
+}
+
 int64_t max_safe_decode_blocks() { return query_max_safe_decode_blocks(); }
 
 void set_decode_blocks(int64_t blocks) {
@@ -170,6 +202,12 @@ TORCH_LIBRARY(qwen35_megakernel_bf16_C, ops) {
 
     ops.def("set_decode_blocks(int blocks) -> ()");
     ops.impl("set_decode_blocks", &set_decode_blocks);
+
+    ops.def("quantize_nvfp4_out(Tensor packed_out, Tensor scales_out, Tensor weight, int group_size) -> ()");
+    ops.impl("quantize_nvfp4_out", torch::kCUDA, &quantize_nvfp4_out);
+
+    ops.def("quantize_nvfp4_lm_out(Tensor packed_out, Tensor scales_out, Tensor weight) -> ()");
+    ops.impl("quantize_nvfp4_lm_out", torch::kCUDA, &quantize_nvfp4_lm_out);
 }
 
 // Importable as a Python module of the same name, like the reference extension

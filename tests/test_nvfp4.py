@@ -125,3 +125,67 @@ def test_gpu_quantizer_rejects_bad_shapes():
     assert lib.launch_quantize_nvfp4_out(p, 4, 100, 32, p, p, None) == 1
     assert lib.launch_quantize_nvfp4_lm_out(p, 100, 64, p, p, None) == 1
     assert lib.launch_quantize_nvfp4_lm_out(p, 128, 100, p, p, None) == 1
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt,shape", [(0, (256, 1024)), (0, (1024, 3584)), (1, (256, 1024)), (1, (2048, 1024))])
+def test_gpu_dequant_bit_exact_and_matvec(fmt, shape):
+    """Dequantised weights are bit-identical to the C oracle; the in-register dequantising row
+    product agrees with a float64 product of those weights to f32 rounding."""
+    import luce_megakernel_b200 as L
+    lib = L.lib()
+    lib.mk_nvfp4_error.restype = ctypes.c_char_p
+    rows, cols = shape
+    w = _rand_bf16(rows, cols, 7 + fmt)
+    if fmt == 0:
+        packed, scales = nvfp4.quantize_a(w, 32)
+        ref = nvfp4.dequantize_a(packed, scales, 32)
+        sc_t = torch.from_numpy(scales.view(np.int16)).cuda()
+    else:
+        packed, scales = nvfp4.quantize_b(w)
+        ref = nvfp4.dequantize_b(packed, scales)
+        sc_t = torch.from_numpy(scales).cuda()
+    pk_t = torch.from_numpy(packed).cuda()
+    out = torch.empty(rows, cols, dtype=torch.float32, device="cuda")
+    rc = lib.mk_dequantize_nvfp4(fmt, ctypes.c_void_p(pk_t.data_ptr()), ctypes.c_void_p(sc_t.data_ptr()),
+                                 ctypes.c_void_p(out.data_ptr()), rows, cols, 32, _stream())
+    assert rc == 0, lib.mk_nvfp4_error().decode()
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))      # bit-exact
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(cols, generator=g)
+    y = torch.empty(rows, dtype=torch.float32, device="cuda")
+    xd = x.cuda()
+    rc = lib.mk_matvec_nvfp4(fmt, ctypes.c_void_p(pk_t.data_ptr()), ctypes.c_void_p(sc_t.data_ptr()),
+                             ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(y.data_ptr()), rows, cols, 32, _stream())
+    assert rc == 0, lib.mk_nvfp4_error().decode()
+    torch.cuda.synchronize()
+    yref = ref.astype(np.float64) @ x.numpy().astype(np.float64)
+    err = np.abs(y.cpu().numpy() - yref).max()
+    assert err <= 1e-5 * max(1.0, np.abs(yref).max()) + 1e-6, err
+
+
+@pytest.mark.gpu
+def test_quantize_ops_surface():
+    """The torch ops of the reference's names and schemas give the oracle's bytes."""
+    import luce_megakernel_b200 as L
+    ops = L.load_ops()
+    w = _rand_bf16(256, 1024, 9)
+    wd = w.cuda()
+    packed = torch.empty(256, 512, dtype=torch.uint8, device="cuda")
+    scales = torch.empty(256, 32, dtype=torch.float16, device="cuda")
+    ops.quantize_nvfp4_out(packed, scales, wd, 32)
+    rp, rs = nvfp4.quantize_a(w, 32)
+    assert np.array_equal(packed.cpu().numpy(), rp)
+    assert np.array_equal(scales.cpu().view(torch.int16).numpy().view(np.uint16), rs)
+    packed_b = torch.empty(256, 512, dtype=torch.uint8, device="cuda")
+    scales_b = torch.zeros(2 * 16 * 512, dtype=torch.uint8, device="cuda")
+    ops.quantize_nvfp4_lm_out(packed_b, scales_b, wd)
+    bp, bs = nvfp4.quantize_b(w)
+    assert np.array_equal(packed_b.cpu().numpy(), bp) and np.array_equal(scales_b.cpu().numpy(), bs)
+    with pytest.raises(RuntimeError):
+        ops.quantize_nvfp4_out(packed, scales, wd, 48)
