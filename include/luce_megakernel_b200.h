@@ -57,6 +57,42 @@ int launch_decode(
     float repetition_penalty,
     int position, int max_seq_len, cudaStream_t stream);
 
+/* NVFP4 decode step and multi-step decode with device token feedback.  Replace launch_decode_nvfp4
+ * and launch_decode_many_nvfp4 (reference: megakernel/kernel_gb10_nvfp4.cu:2068-2257, declared at
+ * megakernel/torch_bindings.cpp:74-106) with the same argument lists.  layer_weights is the 24 x
+ * 208-byte table {int type; int group_size; int pad[2]; void *ptrs[24]} of the reference's NVFP4
+ * driver (megakernel/model_nvfp4.py:274-311, 456-473): quantised matrices as (packed e2m1, fp16
+ * scales per 32) pairs, norms / conv / beta / alpha in bf16; the LM head is the packed 16-block
+ * E4M3 format of launch_quantize_nvfp4_lm_out.  input_token_ptr / token_buffer are device
+ * pointers.  group_size must be 32.  The lm_hidden_* / lm_logits_f16 and the other scratch
+ * arguments are accepted and ignored. */
+int launch_decode_nvfp4(
+    const int *input_token_ptr, int *output_token_id,
+    const void *embed_weight, const void *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight_packed, const void *lm_head_scales,
+    void *lm_hidden_bf16, void *lm_hidden_packed, void *lm_hidden_scales, void *lm_logits_f16,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *hidden_buffer, void *g_activations, void *g_residual,
+    void *g_qkv_scratch, void *g_kv_scratch, void *g_attn_out,
+    void *g_mlp_inter, void *g_z_scratch, void *g_beta_scratch,
+    void *g_alpha_scratch, void *g_normalized,
+    unsigned int *barrier_counter, unsigned int *barrier_generation,
+    float *block_max_vals, int *block_max_idxs, unsigned int *lm_sync_counter,
+    int position, int max_seq_len, int group_size, cudaStream_t stream);
+int launch_decode_many_nvfp4(
+    int *token_buffer, int *output_tokens, int steps,
+    const void *embed_weight, const void *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight_packed, const void *lm_head_scales,
+    void *lm_hidden_bf16, void *lm_hidden_packed, void *lm_hidden_scales, void *lm_logits_f16,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *hidden_buffer, void *g_activations, void *g_residual,
+    void *g_qkv_scratch, void *g_kv_scratch, void *g_attn_out,
+    void *g_mlp_inter, void *g_z_scratch, void *g_beta_scratch,
+    void *g_alpha_scratch, void *g_normalized,
+    unsigned int *barrier_counter, unsigned int *barrier_generation,
+    float *block_max_vals, int *block_max_idxs, unsigned int *lm_sync_counter,
+    int position, int max_seq_len, int group_size, cudaStream_t stream);
+
 /* Resident-block ceiling and decode grid override
  * (reference: megakernel/kernel.cu:1012-1020, megakernel/torch_bindings.cpp:144-145).
  * The kernel runs one CTA per SM; overrides are clamped to [129, ceiling]. */

@@ -102,7 +102,7 @@ int validate(const DecodeCall& a) {
 mk::DecodeParams make_params(const DecodeCall& a, DeviceState& d) {
     mk::DecodeParams p;
     memset(&p, 0, sizeof(p));
-    p.embed = a.embed; p.layers = reinterpret_cast<const mk::LayerWeights*>(a.layers);
+    p.embed = a.embed; p.layers = a.layers;
     p.final_norm = a.final_norm; p.lm_head = a.lm_head;
     p.k_cache = a.k_cache; p.v_cache = a.v_cache;
     p.dn_states = (float*)a.dn_states; p.conv_bufs = (float*)a.conv_bufs;
@@ -187,6 +187,96 @@ int mk_decode_many_bf16(
         mk::fill_rope(p);
         cudaError_t e = mk::launch_decode_kernel(p, grid, stream);
         if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
+    }
+    return MK_OK;
+}
+
+// NVFP4 decode step: same kernel schedule with packed e2m1 layer weights (fp16 scales per 32) and
+// the LM head in the 16-block E4M3 format; the token is read from device memory.
+static int decode_nvfp4_common(const int* token_in, int* token_out, int* token_feedback, const void* embed_weight,
+                               const void* layer_weights, const void* final_norm_weight, const void* lm_packed,
+                               const void* lm_scales, void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+                               void* hidden_buffer, void* g_normalized, int position, int max_seq_len, int group_size,
+                               cudaStream_t stream) {
+    if (!token_in || !token_out || !embed_weight || !layer_weights || !final_norm_weight || !lm_packed || !lm_scales ||
+        !fa_k_cache || !fa_v_cache || !dn_states || !conv_bufs || !hidden_buffer || !g_normalized)
+        return set_err(MK_ERR_BAD_ARG, "null pointer argument");
+    if (group_size != 32) return set_err(MK_ERR_BAD_ARG, "the NVFP4 decode kernel is built for group_size 32");
+    if (g_vocab % 128) return set_err(MK_ERR_BAD_ARG, "the NVFP4 LM-head format needs a vocabulary divisible by 128");
+    if (max_seq_len <= 0 || position < 0 || position >= max_seq_len) return set_err(MK_ERR_BAD_ARG, "position out of range");
+    const void* al[] = {embed_weight, layer_weights, final_norm_weight, lm_packed, fa_k_cache, fa_v_cache, dn_states,
+                        conv_bufs, hidden_buffer, g_normalized};
+    for (const void* q : al)
+        if (misaligned16(q)) return set_err(MK_ERR_BAD_ARG, "pointer argument is not 16-byte aligned");
+    DeviceState* d = nullptr;
+    int rc = device_state(&d);
+    if (rc) return rc;
+    if ((rc = check_device_status(*d, stream))) return rc;
+    mk::DecodeParams p;
+    memset(&p, 0, sizeof(p));
+    p.embed = embed_weight; p.layers = layer_weights; p.final_norm = final_norm_weight;
+    p.lm_head = lm_packed; p.lm_scales = lm_scales; p.wfmt = 1;
+    p.k_cache = fa_k_cache; p.v_cache = fa_v_cache; p.dn_states = (float*)dn_states; p.conv_bufs = (float*)conv_bufs;
+    p.hidden = hidden_buffer; p.normalized = (float*)g_normalized;
+    p.seen_mask = nullptr; p.rep_penalty = 1.0f;
+    p.token_ptr = token_in; p.token_val = 0; p.out_token = token_out; p.token_feedback = token_feedback;
+    p.position = position; p.max_seq_len = max_seq_len; p.num_layers = g_num_layers; p.vocab = g_vocab;
+    p.ws = d->ws; p.host_status = d->host_status_dev; p.trace = nullptr; p.trace_slots = 0;
+    mk::fill_rope(p);
+    cudaError_t e = mk::launch_decode_kernel(p, decode_grid(*d), stream);
+    if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
+    return MK_OK;
+}
+
+int launch_decode_nvfp4(
+    const int* input_token_ptr, int* output_token_id,
+    const void* embed_weight, const void* layer_weights, const void* final_norm_weight,
+    const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* lm_hidden_bf16, void* lm_hidden_packed, void* lm_hidden_scales, void* lm_logits_f16,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden_buffer, void* g_activations, void* g_residual,
+    void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch,
+    void* g_alpha_scratch, void* g_normalized,
+    unsigned int* barrier_counter, unsigned int* barrier_generation,
+    float* block_max_vals, int* block_max_idxs, unsigned int* lm_sync_counter,
+    int position, int max_seq_len, int group_size, cudaStream_t stream) {
+    (void)lm_hidden_bf16; (void)lm_hidden_packed; (void)lm_hidden_scales; (void)lm_logits_f16; (void)g_activations;
+    (void)g_residual; (void)g_qkv_scratch; (void)g_kv_scratch; (void)g_attn_out; (void)g_mlp_inter; (void)g_z_scratch;
+    (void)g_beta_scratch; (void)g_alpha_scratch; (void)barrier_counter; (void)barrier_generation; (void)block_max_vals;
+    (void)block_max_idxs; (void)lm_sync_counter;
+    return decode_nvfp4_common(input_token_ptr, output_token_id, nullptr, embed_weight, layer_weights, final_norm_weight,
+                               lm_head_weight_packed, lm_head_scales, fa_k_cache, fa_v_cache, dn_states, conv_bufs,
+                               hidden_buffer, g_normalized, position, max_seq_len, group_size, stream);
+}
+
+int launch_decode_many_nvfp4(
+    int* token_buffer, int* output_tokens, int steps,
+    const void* embed_weight, const void* layer_weights, const void* final_norm_weight,
+    const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* lm_hidden_bf16, void* lm_hidden_packed, void* lm_hidden_scales, void* lm_logits_f16,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden_buffer, void* g_activations, void* g_residual,
+    void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch,
+    void* g_alpha_scratch, void* g_normalized,
+    unsigned int* barrier_counter, unsigned int* barrier_generation,
+    float* block_max_vals, int* block_max_idxs, unsigned int* lm_sync_counter,
+    int position, int max_seq_len, int group_size, cudaStream_t stream) {
+    (void)lm_hidden_bf16; (void)lm_hidden_packed; (void)lm_hidden_scales; (void)lm_logits_f16; (void)g_activations;
+    (void)g_residual; (void)g_qkv_scratch; (void)g_kv_scratch; (void)g_attn_out; (void)g_mlp_inter; (void)g_z_scratch;
+    (void)g_beta_scratch; (void)g_alpha_scratch; (void)barrier_counter; (void)barrier_generation; (void)block_max_vals;
+    (void)block_max_idxs; (void)lm_sync_counter;
+    if (!output_tokens) return set_err(MK_ERR_BAD_ARG, "null output_tokens");
+    if (steps < 0) return set_err(MK_ERR_BAD_ARG, "steps must be non-negative");
+    if (position + steps > max_seq_len) return set_err(MK_ERR_BAD_ARG, "position + steps exceeds max_seq_len");
+    for (int s = 0; s < steps; ++s) {
+        // the kernel writes the new token to output_tokens[s] and back into token_buffer
+        const int rc = decode_nvfp4_common(token_buffer, output_tokens + s, token_buffer, embed_weight, layer_weights,
+                                           final_norm_weight, lm_head_weight_packed, lm_head_scales, fa_k_cache, fa_v_cache,
+                                           dn_states, conv_bufs, hidden_buffer, g_normalized, position + s, max_seq_len,
+                                           group_size, stream);
+        if (rc) return rc;
     }
     return MK_OK;
 }

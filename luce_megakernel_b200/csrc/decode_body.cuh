@@ -1,6 +1,153 @@
 // Device code of the decode megakernel.  Included twice by decode_bf16.cu, once per value of
 // MK_TRACE, inside a namespace of its own: the timeline stamps cost instruction-cache space, so
 // the variant without them is the one that normally runs.
+// ---- weight format of this variant -----------------------------------------------------------
+// MK_WFMT 0: bf16 rows of K*2 bytes, contiguous in the ring stage.
+// MK_WFMT 1: NVFP4 layer weights: packed rows of K/2 bytes placed at a stride of K/2+16 bytes (so
+//            that the 8 rows a quarter-warp reads hit different banks), followed by the fp16 group
+//            scales of the chunk's rows (K/16 bytes per row); lanes 0-15 of the producer issue the
+//            data rows, lanes 16-31 the scale rows.  beta / alpha projections stay bf16 and are
+//            computed outside the ring; the LM head uses the 16-block E4M3 format.
+#if MK_WFMT == 0
+typedef LayerWeights LW;
+constexpr int IN_ROWS_DN = DN_IN_ROWS;                  // qkv | z | beta | alpha
+constexpr int LM_RPC = 16;                              // LM-head rows per ring chunk
+__device__ __forceinline__ constexpr int row_bytes(int K) { return K * 2; }
+__device__ __forceinline__ constexpr int row_stride(int K) { return K * 2; }
+#else
+typedef LayerWeightsNVFP4 LW;
+// slots of the NVFP4 table: a quantised matrix takes (data, scales) (reference: megakernel/model_nvfp4.py:274-311)
+enum { DN_IN_NORM = 0, DN_W_QKV = 1, DN_W_Z = 3, DN_W_B = 5, DN_W_A = 6, DN_CONV_W = 7, DN_A_LOG = 8, DN_DT_BIAS = 9,
+       DN_NORM_W = 10, DN_W_OUT = 11, DN_POST_NORM = 13, DN_W_GATE = 14, DN_W_UP = 16, DN_W_DOWN = 18 };
+enum { FA_IN_NORM = 0, FA_W_Q = 1, FA_W_K = 3, FA_W_V = 5, FA_Q_NORM = 7, FA_K_NORM = 8, FA_W_O = 9, FA_POST_NORM = 11,
+       FA_W_GATE = 12, FA_W_UP = 14, FA_W_DOWN = 16 };
+constexpr int IN_ROWS_DN = DN_CONV_CH + DN_V;           // qkv | z
+constexpr int LM_RPC = 64;
+__device__ __forceinline__ constexpr int row_bytes(int K) { return K / 2; }
+__device__ __forceinline__ constexpr int row_stride(int K) { return K / 2 + 16; }
+__device__ __forceinline__ constexpr int scale_bytes(int K) { return K / 16; }
+#endif
+
+struct Geo {
+    int r0, r1;       // rows (or outputs for gate/up, first unit for the recurrence)
+    int nchunks;
+};
+
+__device__ __forceinline__ void split_rows(int n, int G, int c, int& a, int& b) {
+    // n <= 248320 rows (or whatever the vocabulary is) times at most 256 CTAs fits 32 bits
+    a = (int)(((unsigned)n * (unsigned)c) / (unsigned)G);
+    b = (int)(((unsigned)n * (unsigned)(c + 1)) / (unsigned)G);
+}
+
+__device__ __forceinline__ Geo phase_geo(int type, int cta, int G, int vocab) {
+    Geo g;
+    g.r0 = g.r1 = 0;
+    g.nchunks = 0;
+    switch (type) {
+        case T_DN_IN:  split_rows(IN_ROWS_DN, G, cta, g.r0, g.r1);  g.nchunks = (g.r1 - g.r0 + 15) >> 4; break;
+        case T_FA_IN:  split_rows(FA_QKV_ROWS, G, cta, g.r0, g.r1); g.nchunks = (g.r1 - g.r0 + 15) >> 4; break;
+        case T_DN_OUT:
+        case T_FA_OUT: split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = (g.r1 - g.r0 + 7) >> 3; break;
+        case T_GATEUP: split_rows(INTER, G, cta, g.r0, g.r1);       g.nchunks = (g.r1 - g.r0 + 7) >> 3; break;
+        case T_DOWN:   split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = (g.r1 - g.r0 + 3) >> 2; break;
+        case T_LM:     split_rows(vocab, G, cta, g.r0, g.r1);       g.nchunks = (g.r1 - g.r0 + LM_RPC - 1) / LM_RPC; break;
+        case T_DN_REC: g.r0 = cta; g.nchunks = (cta < 128) ? (128 - cta + G - 1) / G : 0; break;
+        default: break;
+    }
+    return g;
+}
+
+// Source of what producer lane `lane` copies for chunk q: returns bytes (0 = nothing) and the
+// ring offset.  bf16: lane = row slot.  NVFP4: lanes 0-15 = packed rows, lanes 16-31 = their scales.
+__device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const DecodeParams& P,
+                                                   const Geo& g, int q, int lane, int G, int dn_idx,
+                                                   const char*& src, uint32_t& dst_off) {
+#if MK_WFMT == 0
+    const int slot = lane, kind = 0;
+#else
+    const int slot = lane & 15, kind = lane >> 4;
+#endif
+    int K = HIDDEN, rpc = 16, idx = -1, rr = 0;     // matrix slot index in the table and row inside it
+    switch (type) {
+        case T_DN_IN: {
+            const int r = g.r0 + q * 16 + slot;
+            if (slot >= 16 || r >= g.r1) return 0;
+            if (r < DN_CONV_CH) { idx = DN_W_QKV; rr = r; }
+            else if (r < DN_CONV_CH + DN_V) { idx = DN_W_Z; rr = r - DN_CONV_CH; }
+            else if (r < DN_CONV_CH + DN_V + DN_HEADS) { idx = DN_W_B; rr = r - DN_CONV_CH - DN_V; }
+            else { idx = DN_W_A; rr = r - DN_CONV_CH - DN_V - DN_HEADS; }
+            break;
+        }
+        case T_FA_IN: {
+            const int r = g.r0 + q * 16 + slot;
+            if (slot >= 16 || r >= g.r1) return 0;
+            if (r < FA_QPROJ) { idx = FA_W_Q; rr = r; }
+            else if (r < FA_QPROJ + FA_KV_SIZE) { idx = FA_W_K; rr = r - FA_QPROJ; }
+            else { idx = FA_W_V; rr = r - FA_QPROJ - FA_KV_SIZE; }
+            break;
+        }
+        case T_DN_OUT:
+        case T_FA_OUT: {
+            const int r = g.r0 + q * 8 + slot;
+            if (slot >= 8 || r >= g.r1) return 0;
+            idx = (type == T_DN_OUT) ? (int)DN_W_OUT : (int)FA_W_O; rr = r; K = 2048; rpc = 8;
+            break;
+        }
+        case T_GATEUP: {
+            const int o = g.r0 + q * 8 + (slot & 7);
+            if (slot >= 16 || o >= g.r1) return 0;
+            const bool dn = (lw.layer_type == 0);
+            idx = slot < 8 ? (dn ? (int)DN_W_GATE : (int)FA_W_GATE) : (dn ? (int)DN_W_UP : (int)FA_W_UP); rr = o;
+            break;
+        }
+        case T_DOWN: {
+            const int r = g.r0 + q * 4 + slot;
+            if (slot >= 4 || r >= g.r1) return 0;
+            idx = (lw.layer_type == 0) ? (int)DN_W_DOWN : (int)FA_W_DOWN; rr = r; K = INTER; rpc = 4;
+            break;
+        }
+        case T_LM: {
+#if MK_WFMT == 0
+            const int r = g.r0 + q * 16 + slot;
+            if (slot >= 16 || r >= g.r1) return 0;
+            src = (const char*)P.lm_head + (size_t)r * (HIDDEN * 2); dst_off = slot * (HIDDEN * 2);
+            return HIDDEN * 2;
+#else
+            // packed LM-head rows are read one row per warp step: no padding, one copy per chunk
+            if (lane != 0) return 0;
+            const int r = g.r0 + q * LM_RPC;
+            const int n = min(LM_RPC, g.r1 - r);
+            src = (const char*)P.lm_head + (size_t)r * (HIDDEN / 2); dst_off = 0;
+            return (uint32_t)n * (HIDDEN / 2);
+#endif
+        }
+        case T_DN_REC: {
+            if (lane != 0) return 0;
+            const int u = g.r0 + q * G;           // unit = (head, 16-row value slice)
+            const int h = u >> 3, sl = u & 7;
+            src = (const char*)(P.dn_states + ((size_t)(dn_idx * DN_HEADS + h) * DN_VAL + sl * 16) * DN_KEY);
+            dst_off = 0;
+            return 16 * DN_KEY * 4;
+        }
+        default: return 0;
+    }
+#if MK_WFMT == 0
+    (void)rpc; (void)kind;
+    src = (const char*)lw.ptrs[idx] + (size_t)rr * row_bytes(K);
+    dst_off = slot * row_stride(K);
+    return row_bytes(K);
+#else
+    if (kind == 0) {
+        src = (const char*)lw.ptrs[idx] + (size_t)rr * row_bytes(K);
+        dst_off = slot * row_stride(K);
+        return row_bytes(K);
+    }
+    src = (const char*)lw.ptrs[idx + 1] + (size_t)rr * scale_bytes(K);
+    dst_off = rpc * row_stride(K) + slot * scale_bytes(K);
+    return scale_bytes(K);
+#endif
+}
+
 struct Ctx {
     char* smem;
     float* xs;            // scratch as floats
@@ -150,7 +297,7 @@ __device__ __forceinline__ void poll2_batch(const DecodeParams& P, Ctx& c, const
 
 // ---- producer ---------------------------------------------------------------------------
 
-__device__ __forceinline__ void producer_phase(const DecodeParams& P, Ctx& c, int type, const LayerWeights& lw, int dn_idx,
+__device__ __forceinline__ void producer_phase(const DecodeParams& P, Ctx& c, int type, const LW& lw, int dn_idx,
                                uint64_t pol_stream, uint64_t pol_keep) {
     const Geo g = phase_geo(type, c.cta, c.G, P.vocab);
 #pragma unroll 1
@@ -188,8 +335,9 @@ __device__ __forceinline__ void producer_phase(const DecodeParams& P, Ctx& c, in
 
 // ---- tensor-core row products ---------------------------------------------------------------
 
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                               uint32_t b0, uint32_t b1) {
+#if MK_WFMT == 0
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -206,6 +354,36 @@ __device__ __forceinline__ void split3(float x, uint32_t& hi, uint32_t& mid, uin
     const float r2 = r1 - __uint_as_float(mid);
     lo = __float_as_uint(r2) & 0xffff0000u;
 }
+#else
+// NVFP4 weights are exact in f16 (e2m1 codes 0..6), so this variant multiplies in f16: the
+// activation is split into three f16 terms (round to nearest; the sum reproduces x to about
+// 2^-30 relative unless a term underflows below 6e-8, far under the bf16 tolerances).
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// terms returned in the upper 16 bits, like the bf16 variant
+__device__ __forceinline__ void split3(float x, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+    const __half h = __float2half_rn(x);
+    const float r1 = x - __half2float(h);
+    const __half m = __float2half_rn(r1);
+    const float r2 = r1 - __half2float(m);
+    const __half l = __float2half_rn(r2);
+    hi = (uint32_t)__half_as_ushort(h) << 16;
+    mid = (uint32_t)__half_as_ushort(m) << 16;
+    lo = (uint32_t)__half_as_ushort(l) << 16;
+}
+
+// two e2m1 codes (one byte, low nibble first) -> f16x2
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+    const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)(byte & 0xffu), __NV_E2M1);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+#endif
 
 // Staging of a warp's K-slice: three planes of XK bf16.  Elements e, e+1 (e even) as one word.
 __device__ __forceinline__ void stage_pair(uint32_t* xw, int e, float x0, float x1) {
@@ -242,15 +420,17 @@ __device__ __forceinline__ void load_bfrags(const uint32_t* xw, int lane, uint32
     }
 }
 
+#if MK_WFMT == 0
 // One ring chunk times the activation: rows of `rowbytes` bytes, this warp's K-slice starting
 // `kofs` bytes into each row.  ROWS = 16: tile rows g and g+8; ROWS = 8: row g; ROWS = 4: rows g < 4.
 // Odd g read their chunks rotated by one so that the two rows of a quarter-warp hit different
 // banks (all rows alias: the row stride is a multiple of 128 bytes).  Writes the warp's partial
 // sums of tile rows into `out[0..15]`.
 template <int NLOAD, int ROWS>
-__device__ __forceinline__ void mma_chunk(const char* stage, int rowbytes, int kofs, int lane,
+__device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, int lane,
                                           const uint32_t (&b)[2 * NLOAD][2], float* out) {
     const int g = lane >> 2, t = lane & 3, odd = g & 1;
+    const int rowbytes = row_stride(K), kofs = warp * NLOAD * 64;      // 32*NLOAD elements of 2 bytes per warp
     const bool live = (ROWS >= 8) || (g < 4);
     const char* r0 = stage + g * rowbytes + kofs + 16 * t;
     const char* r1 = r0 + 8 * rowbytes;
@@ -277,8 +457,8 @@ __device__ __forceinline__ void mma_chunk(const char* stage, int rowbytes, int k
         } else {
             d = make_uint4(0, 0, 0, 0);
         }
-        mma_bf16_16816(acc, a.x, d.x, a.y, d.y, b[2 * i][0], b[2 * i][1]);
-        mma_bf16_16816(acc2, a.z, d.z, a.w, d.w, b[2 * i + 1][0], b[2 * i + 1][1]);
+        mma_16816(acc, a.x, d.x, a.y, d.y, b[2 * i][0], b[2 * i][1]);
+        mma_16816(acc2, a.z, d.z, a.w, d.w, b[2 * i + 1][0], b[2 * i + 1][1]);
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) acc[k] += acc2[k];
@@ -293,21 +473,73 @@ __device__ __forceinline__ void mma_chunk(const char* stage, int rowbytes, int k
     }
 }
 
+#else
+// NVFP4 version of the chunk product.  Stage: packed rows at a stride of K/2+16 bytes, then the
+// fp16 scales of the chunk's rows.  The 16-byte weight chunk i of the bf16 layout (8 elements) is
+// one 32-bit word of nibbles here; the 32 elements the four lanes of a row cover in chunk i are
+// exactly quantisation group warp*NLOAD+i, so the two MMAs of a chunk go into a fresh accumulator
+// that is then scaled by the group's scale of each row: the dequantised value never has to be
+// rounded.  The row stride keeps the 8 rows of a quarter-warp on different banks.
+template <int NLOAD, int ROWS>
+__device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, int lane,
+                                          const uint32_t (&b)[2 * NLOAD][2], float* out) {
+    const int g = lane >> 2, t = lane & 3;
+    const bool live = (ROWS >= 8) || (g < 4);
+    const int stride = row_stride(K);
+    const char* r0 = stage + g * stride + warp * (NLOAD * 16) + 4 * t;
+    const char* r1 = r0 + 8 * stride;
+    const unsigned short* sc0 = reinterpret_cast<const unsigned short*>(stage + ROWS * stride + g * scale_bytes(K)) + warp * NLOAD;
+    const unsigned short* sc1 = sc0 + 8 * (scale_bytes(K) / 2);
+    uint32_t w0[NLOAD], w1[NLOAD];
+    float s0[NLOAD], s1[NLOAD];
+#pragma unroll
+    for (int i = 0; i < NLOAD; ++i) {
+        w0[i] = live ? *reinterpret_cast<const uint32_t*>(r0 + 16 * i) : 0u;
+        s0[i] = live ? __half2float(__ushort_as_half(sc0[i])) : 0.f;
+        if (ROWS == 16) { w1[i] = *reinterpret_cast<const uint32_t*>(r1 + 16 * i); s1[i] = __half2float(__ushort_as_half(sc1[i])); }
+        else { w1[i] = 0u; s1[i] = 0.f; }
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < NLOAD; ++i) {
+        float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t a0 = e2m1x2_to_f16x2(w0[i]), a2 = e2m1x2_to_f16x2(w0[i] >> 8);
+        const uint32_t c0 = e2m1x2_to_f16x2(w0[i] >> 16), c2 = e2m1x2_to_f16x2(w0[i] >> 24);
+        uint32_t a1 = 0u, a3 = 0u, c1 = 0u, c3 = 0u;
+        if (ROWS == 16) {
+            a1 = e2m1x2_to_f16x2(w1[i]); a3 = e2m1x2_to_f16x2(w1[i] >> 8);
+            c1 = e2m1x2_to_f16x2(w1[i] >> 16); c3 = e2m1x2_to_f16x2(w1[i] >> 24);
+        }
+        mma_16816(tmp, a0, a1, a2, a3, b[2 * i][0], b[2 * i][1]);
+        mma_16816(tmp, c0, c1, c2, c3, b[2 * i + 1][0], b[2 * i + 1][1]);
+        acc[0] = fmaf(s0[i], tmp[0], acc[0]); acc[1] = fmaf(s0[i], tmp[1], acc[1]);
+        acc[2] = fmaf(s1[i], tmp[2], acc[2]); acc[3] = fmaf(s1[i], tmp[3], acc[3]);
+    }
+    float q0 = acc[0] + (t == 0 ? acc[1] : 0.f);
+    float q1 = acc[2] + (t == 0 ? acc[3] : 0.f);
+    q0 += __shfl_down_sync(0xffffffffu, q0, 1);
+    q1 += __shfl_down_sync(0xffffffffu, q1, 1);
+    if (t == 0) {
+        out[g] = q0;
+        if (ROWS == 16) out[g + 8] = q1;
+    }
+}
+#endif
+
 // Runs all chunks of a phase; partial sums land in part[(q * 16 + warp) * 16 + tile_row].
 template <int NLOAD, int ROWS>
-__device__ __forceinline__ void mma_phase(const DecodeParams& P, Ctx& c, int nchunks_in, int rowbytes) {
+__device__ __forceinline__ void mma_phase(const DecodeParams& P, Ctx& c, int nchunks_in, int K) {
     int nchunks = nchunks_in;
     // alternate halves: a slow warp may still be reading the previous phase's sums in its epilogue
     c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
     uint32_t b[2 * NLOAD][2];
     load_bfrags<NLOAD>(reinterpret_cast<const uint32_t*>(c.xs) + c.warp * XSW, c.lane, b);
-    const int kofs = c.warp * NLOAD * 64;      // 32*NLOAD elements of 2 bytes
     if (nchunks > 4) { fail(P, c, ST_MISALIGNED); nchunks = 4; }   // never reached for grids >= MIN_GRID
     if (nchunks > 0) wait_full(P, c, c.it % NSTAGE, (c.it / NSTAGE) & 1u);
 #pragma unroll 1
     for (int q = 0; q < nchunks; ++q, ++c.it) {
         const uint32_t stage = c.it % NSTAGE;
-        mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + stage * STAGE_BYTES, rowbytes, kofs, c.lane, b,
+        mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + stage * STAGE_BYTES, K, c.warp, c.lane, b,
                                c.part + (q * NCW + c.warp) * 16);
         release_stage(c, stage);
         // the mbarrier test of the next chunk overlaps the tail of this chunk's MMAs
@@ -361,7 +593,7 @@ __device__ __forceinline__ float2 rmsnorm_to_slice(Ctx& c, float2 v, float w0, f
 
 // ---- phases -----------------------------------------------------------------------------
 
-__device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer, int dn_idx,
+__device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const LW& lw, int layer, int dn_idx,
                             const __nv_bfloat16* embed_row) {
     const Geo g = phase_geo(T_DN_IN, c.cta, c.G, P.vocab);
     const int nloc = g.r1 - g.r0;
@@ -386,12 +618,46 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
             dt_b = bf2f(reinterpret_cast<const __nv_bfloat16*>(lw.ptrs[DN_DT_BIAS])[h]);
         }
     }
+#if MK_WFMT == 1
+    // beta / alpha projections are bf16 rows outside the ring: CTA c < 32 owns row c of [Wb; Wa];
+    // every thread multiplies its two activations with its two weights (fetched before the wait)
+    uint32_t ba_w = 0u;
+    if (c.cta < 2 * DN_HEADS)
+        ba_w = __ldg(reinterpret_cast<const uint32_t*>(lw.ptrs[c.cta < DN_HEADS ? (int)DN_W_B : (int)DN_W_A]) +
+                     (size_t)(c.cta & (DN_HEADS - 1)) * (HIDDEN / 2) + c.tid);
+    if (c.tid == NCT - 1 && c.cta >= DN_HEADS && c.cta < 2 * DN_HEADS) {
+        a_log = bf2f(reinterpret_cast<const __nv_bfloat16*>(lw.ptrs[DN_A_LOG])[c.cta - DN_HEADS]);
+        dt_b = bf2f(reinterpret_cast<const __nv_bfloat16*>(lw.ptrs[DN_DT_BIAS])[c.cta - DN_HEADS]);
+    }
+#endif
     const float2 v = fetch_hidden2(P, c, embed_row, P.ws->x_hidden[1], epoch_of(c, layer - 1));
-    rmsnorm_to_slice(c, v, w0, w1, true);
+    const float2 xn = rmsnorm_to_slice(c, v, w0, w1, true);
+#if MK_WFMT == 1
+    if (c.cta < 2 * DN_HEADS) {
+        const float pd = warp_sum(bf_lo(ba_w) * xn.x + bf_hi(ba_w) * xn.y);
+        if (c.lane == 0) c.red[16 + c.warp] = pd;
+    }
+#else
+    (void)xn;
+#endif
     trace_point(P, c);
-    mma_phase<2, 16>(P, c, g.nchunks, HIDDEN * 2);
+    mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
     trace_point(P, c);
     named_bar_sync(1, NCT);
+#if MK_WFMT == 1
+    if (c.tid == NCT - 1 && c.cta < 2 * DN_HEADS) {
+        float val = 0.f;
+#pragma unroll
+        for (int i = 0; i < NCW; ++i) val += c.red[16 + i];
+        if (c.cta < DN_HEADS) {
+            st_flagged(P.ws->x_dnin + DN_CONV_CH + DN_V + c.cta, 1.0f / (1.0f + expf(-val)), ep);
+        } else {
+            const float x = val + dt_b;
+            const float sp = (x > 20.0f) ? x : log1pf(expf(x));
+            st_flagged(P.ws->x_dnin + DN_CONV_CH + DN_V + c.cta, expf(-expf(a_log) * sp), ep);
+        }
+    }
+#endif
     if (c.tid < nloc) {
         const float val = part_sum(c, c.tid >> 4, c.tid & 15);
         if (r < DN_CONV_CH) {
@@ -402,7 +668,9 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
             st_flagged(P.ws->x_dnin + r, silu_f(co), ep);
         } else if (r < DN_CONV_CH + DN_V) {
             st_flagged(P.ws->x_dnin + r, val, ep);
-        } else if (r < DN_CONV_CH + DN_V + DN_HEADS) {
+        }
+#if MK_WFMT == 0
+        else if (r < DN_CONV_CH + DN_V + DN_HEADS) {
             st_flagged(P.ws->x_dnin + r, 1.0f / (1.0f + expf(-val)), ep);
         } else {
             // decay = exp(-exp(A_log) * softplus(a + dt_bias)) (reference: megakernel/kernel.cu:653-657)
@@ -410,6 +678,7 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
             const float sp = (x > 20.0f) ? x : log1pf(expf(x));
             st_flagged(P.ws->x_dnin + r, expf(-expf(a_log) * sp), ep);
         }
+#endif
     }
     trace_point(P, c);
 }
@@ -481,7 +750,7 @@ __device__ __forceinline__ void phase_dn_rec(const DecodeParams& P, Ctx& c, int 
 __device__ __forceinline__ void outproj_rows(const DecodeParams& P, Ctx& c, const Geo& g, int type, float resid, uint32_t ep) {
     (void)type;
     const int nloc = g.r1 - g.r0;
-    mma_phase<4, 8>(P, c, g.nchunks, 2048 * 2);
+    mma_phase<4, 8>(P, c, g.nchunks, 2048);
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nloc) {
@@ -499,7 +768,7 @@ __device__ __forceinline__ float fetch_resid_in(const DecodeParams& P, Ctx& c, c
 
 // out-proj of a DeltaNet layer; staging fuses the gated RMSNorm (plain weight) * SiLU(z): warp w
 // owns head w, whose 128 values are exactly its K-slice (reference: megakernel/kernel.cu:715-741)
-__device__ __forceinline__ void phase_dn_out(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer,
+__device__ __forceinline__ void phase_dn_out(const DecodeParams& P, Ctx& c, const LW& lw, int layer,
                              const __nv_bfloat16* embed_row) {
     const Geo g = phase_geo(T_DN_OUT, c.cta, c.G, P.vocab);
     const uint32_t ep = epoch_of(c, layer);
@@ -531,7 +800,7 @@ __device__ __forceinline__ void phase_dn_out(const DecodeParams& P, Ctx& c, cons
     outproj_rows(P, c, g, T_DN_OUT, resid, ep);
 }
 
-__device__ __forceinline__ void phase_fa_in(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer,
+__device__ __forceinline__ void phase_fa_in(const DecodeParams& P, Ctx& c, const LW& lw, int layer,
                             const __nv_bfloat16* embed_row) {
     const Geo g = phase_geo(T_FA_IN, c.cta, c.G, P.vocab);
     const int nloc = g.r1 - g.r0;
@@ -542,7 +811,7 @@ __device__ __forceinline__ void phase_fa_in(const DecodeParams& P, Ctx& c, const
     const float2 v = fetch_hidden2(P, c, embed_row, P.ws->x_hidden[1], epoch_of(c, layer - 1));
     rmsnorm_to_slice(c, v, w0, w1, true);
     trace_point(P, c);
-    mma_phase<2, 16>(P, c, g.nchunks, HIDDEN * 2);
+    mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nloc)      // rows 0..4095: per head [q(256) | gate(256)]; then k[512], v[512]
@@ -588,7 +857,7 @@ __device__ __forceinline__ void head_norm_rope(const DecodeParams& P, Ctx& c, co
 // Split-KV decode attention.  Unit = (KV head, position chunk); the 4 query heads of a KV head
 // share every K/V load.  Each unit leaves (m, l, o[256]) per head in the workspace and then
 // publishes its ready word; the o-proj phase merges the chunks.  reference: megakernel/kernel.cu:506-560
-__device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer, int fa_idx) {
+__device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, const LW& lw, int layer, int fa_idx) {
     const int pos = P.position, L = pos + 1;
     const int NC = att_num_chunks(L);
     const int per = (L + NC - 1) / NC;
@@ -748,7 +1017,7 @@ __device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, cons
 // o-proj of an attention layer; staging waits for the attention units, merges their chunks and
 // applies the sigmoid gate: warp w owns dims (w&1)*128.. of head w/2, which is its K-slice
 // (reference: megakernel/kernel.cu:542-570)
-__device__ __forceinline__ void phase_fa_out(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer,
+__device__ __forceinline__ void phase_fa_out(const DecodeParams& P, Ctx& c, const LW& lw, int layer,
                              const __nv_bfloat16* embed_row) {
     (void)lw;
     const Geo g = phase_geo(T_FA_OUT, c.cta, c.G, P.vocab);
@@ -802,7 +1071,7 @@ __device__ __forceinline__ void phase_fa_out(const DecodeParams& P, Ctx& c, cons
 
 // post norm + SiLU(Wg x) * (Wu x): tile rows 0-7 are gate rows, 8-15 the matching up rows
 // (reference: megakernel/kernel.cu:313-347, 572-578)
-__device__ __forceinline__ void phase_gateup(const DecodeParams& P, Ctx& c, const LayerWeights& lw, int layer) {
+__device__ __forceinline__ void phase_gateup(const DecodeParams& P, Ctx& c, const LW& lw, int layer) {
     const Geo g = phase_geo(T_GATEUP, c.cta, c.G, P.vocab);
     const int nout = g.r1 - g.r0;
     const uint32_t ep = epoch_of(c, layer);
@@ -812,7 +1081,7 @@ __device__ __forceinline__ void phase_gateup(const DecodeParams& P, Ctx& c, cons
     const float2 v = poll2(P, c, P.ws->x_hidden[0] + 2 * c.tid, ep);
     rmsnorm_to_slice(c, v, w0, w1, true);
     trace_point(P, c);
-    mma_phase<2, 16>(P, c, g.nchunks, HIDDEN * 2);
+    mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nout) {
@@ -842,7 +1111,7 @@ __device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, int la
         __syncwarp();
     }
     trace_point(P, c);
-    mma_phase<7, 4>(P, c, g.nchunks, INTER * 2);
+    mma_phase<7, 4>(P, c, g.nchunks, INTER);
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nloc) {
@@ -888,6 +1157,9 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
         named_bar_sync(1, NCT);
     }
     trace_point(P, c);
+    float bestv = -INFINITY;
+    int besti = 0x7fffffff;
+#if MK_WFMT == 0
     float xr[32];
 #pragma unroll
     for (int it = 0; it < 4; ++it) {
@@ -897,8 +1169,6 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
         xr[it * 8 + 4] = b.x; xr[it * 8 + 5] = b.y; xr[it * 8 + 6] = b.z; xr[it * 8 + 7] = b.w;
     }
     const bool penal = (P.rep_penalty > 1.0f) && (P.seen_mask != nullptr);
-    float bestv = -INFINITY;
-    int besti = 0x7fffffff;
 #pragma unroll 1
     for (int q = 0; q < g.nchunks; ++q, ++c.it) {
         const uint32_t stage = c.it % NSTAGE, parity = (c.it / NSTAGE) & 1u;
@@ -916,6 +1186,65 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
         }
         release_stage(c, stage);
     }
+#else
+    // LM head in the 16-block E4M3 format: a chunk is 64 packed rows (512 bytes each); a warp takes
+    // rows warp, warp+16, ...; a lane owns 32 weights = two blocks, whose scales are adjacent
+    // bytes of the tiled scale array and are fetched from global memory ahead of the ring wait.
+    float xr[32];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const float4 a = *reinterpret_cast<const float4*>(c.xs + 32 * c.lane + 4 * j);
+        xr[4 * j] = a.x; xr[4 * j + 1] = a.y; xr[4 * j + 2] = a.z; xr[4 * j + 3] = a.w;
+    }
+    const uint8_t* lm_scales = reinterpret_cast<const uint8_t*>(P.lm_scales);
+#pragma unroll 1
+    for (int q = 0; q < g.nchunks; ++q, ++c.it) {
+        const uint32_t stage = c.it % NSTAGE, parity = (c.it / NSTAGE) & 1u;
+        unsigned short sc[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int lr = q * LM_RPC + c.warp + 16 * k;
+            const int row = g.r0 + lr;
+            sc[k] = 0;
+            if (lr < nloc) {
+                const size_t idx = ((size_t)(row >> 7) * (HIDDEN >> 6) + (c.lane >> 1)) * 512 + (size_t)(row & 31) * 16 +
+                                   (size_t)((row & 127) >> 5) * 4 + ((2 * c.lane) & 3);
+                sc[k] = __ldg(reinterpret_cast<const unsigned short*>(lm_scales + idx));
+            }
+        }
+        wait_full(P, c, stage, parity);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int lr = q * LM_RPC + c.warp + 16 * k;
+            const bool valid = lr < nloc;
+            float acc = 0.f;
+            if (valid) {
+                const uint4 pk = *(reinterpret_cast<const uint4*>(c.smem + OFF_RING + stage * STAGE_BYTES + (c.warp + 16 * k) * (HIDDEN / 2)) + c.lane);
+                const __half_raw h0 = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)(sc[k] & 0xff), __NV_E4M3);
+                const __half_raw h1 = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)(sc[k] >> 8), __NV_E4M3);
+                const float s0 = __half2float(*reinterpret_cast<const __half*>(&h0)), s1 = __half2float(*reinterpret_cast<const __half*>(&h1));
+                const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
+                float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float part = 0.f;
+#pragma unroll
+                    for (int bb = 0; bb < 4; ++bb) {
+                        const uint32_t hh = e2m1x2_to_f16x2(wv[i] >> (8 * bb));
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hh));
+                        part = fmaf(f.x, xr[8 * i + 2 * bb], part);
+                        part = fmaf(f.y, xr[8 * i + 2 * bb + 1], part);
+                    }
+                    if (i < 2) a0 += part; else a1 += part;
+                }
+                acc = a0 * s0 + a1 * s1;
+            }
+            acc = warp_sum(acc);
+            if (valid && acc > bestv) { bestv = acc; besti = g.r0 + lr; }
+        }
+        release_stage(c, stage);
+    }
+#endif
     trace_point(P, c);
     c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
     int* resi = reinterpret_cast<int*>(c.part) + 32;
@@ -985,8 +1314,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
     c.seq = __ldcg(&P.ws->seq);
 
     // The pointer table is read on every chunk; keep it in shared memory.
-    LayerWeights* s_layers = reinterpret_cast<LayerWeights*>(smem + OFF_LAYERS);
-    for (int i = threadIdx.x; i < P.num_layers * (int)(sizeof(LayerWeights) / 16); i += NTHREADS)
+    LW* s_layers = reinterpret_cast<LW*>(smem + OFF_LAYERS);
+    for (int i = threadIdx.x; i < P.num_layers * (int)(sizeof(LW) / 16); i += NTHREADS)
         reinterpret_cast<uint4*>(s_layers)[i] = __ldg(reinterpret_cast<const uint4*>(P.layers) + i);
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSTAGE; ++s) {
@@ -1011,7 +1340,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
         int dn_idx = 0;
         for (int layer = 0; layer <= P.num_layers; ++layer) {
             const bool lm = (layer == P.num_layers);
-            const LayerWeights& lw = s_layers[lm ? 0 : layer];
+            const LW& lw = s_layers[lm ? 0 : layer];
             const bool dn = (lw.layer_type == 0);
             const int nph = lm ? 1 : (dn ? 5 : 4);
 #pragma unroll 1
@@ -1029,7 +1358,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
         if (c.cta == 0 && c.tid == 0 && P.seen_mask && P.rep_penalty > 1.0f) P.seen_mask[token] = 1.0f;
         int dn_idx = 0, fa_idx = 0;
         for (int layer = 0; layer < P.num_layers; ++layer) {
-            const LayerWeights& lw = s_layers[layer];
+            const LW& lw = s_layers[layer];
             const __nv_bfloat16* erow = (layer == 0) ? embed_row : nullptr;
             if (lw.layer_type == 0) {
                 phase_dn_in(P, c, lw, layer, dn_idx, erow);

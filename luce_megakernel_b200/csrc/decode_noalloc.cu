@@ -108,7 +108,7 @@ extern "C" int mk_decode_bf16_static_scratch(
 
     mk::DecodeParams p;
     memset(&p, 0, sizeof(p));
-    p.embed = embed_weight; p.layers = reinterpret_cast<const mk::LayerWeights*>(layer_weights);
+    p.embed = embed_weight; p.layers = layer_weights;
     p.final_norm = final_norm_weight; p.lm_head = lm_head_weight;
     p.k_cache = fa_k_cache; p.v_cache = fa_v_cache;
     p.dn_states = (float*)dn_states; p.conv_bufs = (float*)conv_bufs; p.hidden = hidden_buffer;

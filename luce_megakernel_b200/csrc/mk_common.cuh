@@ -44,6 +44,17 @@ struct LayerWeights {
 };
 static_assert(sizeof(LayerWeights) == 128, "pointer table entry must be 128 bytes");
 
+// Pointer table entry of the NVFP4 decode path, 208 bytes: quantised matrices take two slots
+// (packed data, fp16 group scales) (reference: megakernel/torch_bindings.cpp:37-42,
+// megakernel/kernel_gb10_nvfp4.cu:156-203, megakernel/model_nvfp4.py:274-311).
+struct LayerWeightsNVFP4 {
+    int layer_type;
+    int group_size;
+    int pad[2];
+    const void* ptrs[24];
+};
+static_assert(sizeof(LayerWeightsNVFP4) == 208, "NVFP4 pointer table entry must be 208 bytes");
+
 // pointer slots, DeltaNet layer (reference: megakernel/model.py:117-132)
 enum { DN_IN_NORM = 0, DN_W_QKV, DN_W_Z, DN_W_B, DN_W_A, DN_CONV_W, DN_A_LOG, DN_DT_BIAS,
        DN_NORM_W, DN_W_OUT, DN_POST_NORM, DN_W_GATE, DN_W_UP, DN_W_DOWN };

@@ -40,9 +40,11 @@ struct DecodeWorkspace {
 
 struct DecodeParams {
     const void* embed;            // bf16 [vocab, 1024]
-    const LayerWeights* layers;   // device pointer table
+    const void* layers;           // device pointer table: LayerWeights[] (bf16) or LayerWeightsNVFP4[] (wfmt 1)
     const void* final_norm;       // bf16 [1024]
-    const void* lm_head;          // bf16 [vocab, 1024]
+    const void* lm_head;          // bf16 [vocab, 1024], or packed e2m1 [vocab, 512] when wfmt is 1
+    const void* lm_scales;        // wfmt 1: E4M3 block scales of the LM head (128 x 4 tiles)
+    int wfmt;                     // 0 = bf16 weights, 1 = NVFP4 (layer format A, LM head format B)
     void* k_cache;                // bf16 [n_fa, 2, max_seq, 256]
     void* v_cache;
     float* dn_states;             // f32 [n_dn, 16, 128(value), 128(key)]

@@ -127,6 +127,78 @@ void prefill_bf16(Tensor output_token, Tensor token_ids, Tensor embed_weight, Te
     (void)dn_cs_scratch; (void)lm_bmv; (void)lm_bmi;
 }
 
+// NVFP4 decode ops (reference: megakernel/torch_bindings.cpp:182-270): the token is seeded into
+// device memory on the current stream, then the C ABI is called with the reference's argument list.
+static void seed_token(const Tensor& buf, int token_id) {
+    const cudaError_t e = cudaMemcpyAsync(buf.data_ptr(), &token_id, sizeof(int), cudaMemcpyHostToDevice,
+                                          current_stream(buf));
+    TORCH_CHECK(e == cudaSuccess, "cudaMemcpyAsync(token) failed: ", cudaGetErrorString(e));
+}
+
+#define MK_NVFP4_TENSOR_ARGS                                                                                       \
+    Tensor embed_weight, Tensor layer_weights_packed, Tensor final_norm_weight, Tensor lm_head_weight_packed,      \
+    Tensor lm_head_scales, Tensor lm_hidden_bf16, Tensor lm_hidden_packed, Tensor lm_hidden_scales,                \
+    Tensor lm_logits_f16, Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs,                \
+    Tensor hidden_buffer, Tensor activations, Tensor residual, Tensor qkv_scratch, Tensor kv_scratch,              \
+    Tensor attn_out, Tensor mlp_inter, Tensor z_scratch, Tensor beta_scratch, Tensor alpha_scratch,                \
+    Tensor normalized, Tensor barrier_counter, Tensor barrier_generation, Tensor block_max_vals,                   \
+    Tensor block_max_idxs, Tensor lm_sync_counter, int64_t position, int64_t max_seq_len, int64_t group_size
+
+static void check_nvfp4_common(const Tensor& embed_weight, const Tensor& layer_weights_packed, const Tensor& final_norm_weight,
+                               const Tensor& lm_packed, const Tensor& lm_scales, const Tensor& fa_k_cache,
+                               const Tensor& fa_v_cache, const Tensor& dn_states, const Tensor& conv_bufs,
+                               const Tensor& hidden_buffer, const Tensor& normalized, int64_t max_seq_len, const char* op) {
+    need(embed_weight, "embed_weight", torch::kBFloat16, 1024);
+    need(layer_weights_packed, "layer_weights_packed", torch::kUInt8, 208);
+    TORCH_CHECK(layer_weights_packed.numel() % 208 == 0, "layer_weights_packed must hold 208-byte entries");
+    need(final_norm_weight, "final_norm_weight", torch::kBFloat16, 1024);
+    need(lm_packed, "lm_head_weight_packed", torch::kUInt8, 512);
+    need(lm_scales, "lm_head_scales", torch::kUInt8, 512);
+    need(fa_k_cache, "fa_k_cache", torch::kBFloat16, 2 * max_seq_len * 256);
+    need(fa_v_cache, "fa_v_cache", torch::kBFloat16, 2 * max_seq_len * 256);
+    need(dn_states, "dn_states", torch::kFloat32, 16 * 128 * 128);
+    need(conv_bufs, "conv_bufs", torch::kFloat32, 6144 * 4);
+    need(hidden_buffer, "hidden_buffer", torch::kBFloat16, 1024);
+    need(normalized, "normalized", torch::kFloat32, 1024);
+    check_status(mk_set_model_dims((int)(layer_weights_packed.numel() / 208), (int)embed_weight.size(0)), op);
+}
+
+void decode_nvfp4(Tensor output_token, int64_t input_token_id, MK_NVFP4_TENSOR_ARGS) {
+    need(output_token, "output_token", torch::kInt32, 1);
+    DeviceGuard guard(embed_weight);
+    check_nvfp4_common(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight_packed, lm_head_scales,
+                       fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden_buffer, normalized, max_seq_len, "decode_nvfp4");
+    seed_token(output_token, (int)input_token_id);
+    const int rc = launch_decode_nvfp4(
+        (const int*)output_token.data_ptr(), (int*)output_token.data_ptr(), embed_weight.data_ptr(),
+        layer_weights_packed.data_ptr(), final_norm_weight.data_ptr(), lm_head_weight_packed.data_ptr(),
+        lm_head_scales.data_ptr(), nullptr, nullptr, nullptr, nullptr, fa_k_cache.data_ptr(), fa_v_cache.data_ptr(),
+        dn_states.data_ptr(), conv_bufs.data_ptr(), hidden_buffer.data_ptr(), nullptr, nullptr, nullptr, nullptr, nullptr,
+        nullptr, nullptr, nullptr, nullptr, normalized.data_ptr(), nullptr, nullptr, nullptr, nullptr, nullptr,
+        (int)position, (int)max_seq_len, (int)group_size, current_stream(embed_weight));
+    check_status(rc, "decode_nvfp4");
+}
+
+void decode_many_nvfp4(Tensor output_tokens, Tensor token_buffer, int64_t input_token_id, MK_NVFP4_TENSOR_ARGS) {
+    need(output_tokens, "output_tokens", torch::kInt32, 0);
+    TORCH_CHECK(output_tokens.dim() == 1, "output_tokens must be 1D");
+    need(token_buffer, "token_buffer", torch::kInt32, 1);
+    TORCH_CHECK(token_buffer.numel() == 1, "token_buffer must contain exactly one int32 token");
+    DeviceGuard guard(embed_weight);
+    check_nvfp4_common(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight_packed, lm_head_scales,
+                       fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden_buffer, normalized, max_seq_len,
+                       "decode_many_nvfp4");
+    seed_token(token_buffer, (int)input_token_id);
+    const int rc = launch_decode_many_nvfp4(
+        (int*)token_buffer.data_ptr(), (int*)output_tokens.data_ptr(), (int)output_tokens.numel(), embed_weight.data_ptr(),
+        layer_weights_packed.data_ptr(), final_norm_weight.data_ptr(), lm_head_weight_packed.data_ptr(),
+        lm_head_scales.data_ptr(), nullptr, nullptr, nullptr, nullptr, fa_k_cache.data_ptr(), fa_v_cache.data_ptr(),
+        dn_states.data_ptr(), conv_bufs.data_ptr(), hidden_buffer.data_ptr(), nullptr, nullptr, nullptr, nullptr, nullptr,
+        nullptr, nullptr, nullptr, nullptr, normalized.data_ptr(), nullptr, nullptr, nullptr, nullptr, nullptr,
+        (int)position, (int)max_seq_len, (int)group_size, current_stream(embed_weight));
+    check_status(rc, "decode_many_nvfp4");
+}
+
 // NVFP4 quantisers (reference: megakernel/torch_bindings.cpp:272-337): same checks, same outputs.
 void quantize_nvfp4_out(Tensor packed_out, Tensor scales_out, Tensor weight, int64_t group_size) {
     TORCH_CHECK(weight.is_cuda() && weight.is_contiguous() && weight.dim() == 2, "weight must be a contiguous 2-D CUDA tensor");
@@ -202,6 +274,34 @@ TORCH_LIBRARY(qwen35_megakernel_bf16_C, ops) {
 
     ops.def("set_decode_blocks(int blocks) -> ()");
     ops.impl("set_decode_blocks", &set_decode_blocks);
+
+    ops.def("decode_nvfp4(Tensor output_token, int input_token_id, "
+            "Tensor embed_weight, Tensor layer_weights_packed, "
+            "Tensor final_norm_weight, Tensor lm_head_weight_packed, Tensor lm_head_scales, "
+            "Tensor lm_hidden_bf16, Tensor lm_hidden_packed, Tensor lm_hidden_scales, Tensor lm_logits_f16, "
+            "Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs, "
+            "Tensor hidden_buffer, Tensor activations, Tensor residual, "
+            "Tensor qkv_scratch, Tensor kv_scratch, Tensor attn_out, "
+            "Tensor mlp_inter, Tensor z_scratch, Tensor beta_scratch, "
+            "Tensor alpha_scratch, Tensor normalized, "
+            "Tensor barrier_counter, Tensor barrier_generation, "
+            "Tensor block_max_vals, Tensor block_max_idxs, Tensor lm_sync_counter, "
+            "int position, int max_seq_len, int group_size) -> ()");
+    ops.impl("decode_nvfp4", torch::kCUDA, &decode_nvfp4);
+
+    ops.def("decode_many_nvfp4(Tensor output_tokens, Tensor token_buffer, int input_token_id, "
+            "Tensor embed_weight, Tensor layer_weights_packed, "
+            "Tensor final_norm_weight, Tensor lm_head_weight_packed, Tensor lm_head_scales, "
+            "Tensor lm_hidden_bf16, Tensor lm_hidden_packed, Tensor lm_hidden_scales, Tensor lm_logits_f16, "
+            "Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs, "
+            "Tensor hidden_buffer, Tensor activations, Tensor residual, "
+            "Tensor qkv_scratch, Tensor kv_scratch, Tensor attn_out, "
+            "Tensor mlp_inter, Tensor z_scratch, Tensor beta_scratch, "
+            "Tensor alpha_scratch, Tensor normalized, "
+            "Tensor barrier_counter, Tensor barrier_generation, "
+            "Tensor block_max_vals, Tensor block_max_idxs, Tensor lm_sync_counter, "
+            "int position, int max_seq_len, int group_size) -> ()");
+    ops.impl("decode_many_nvfp4", torch::kCUDA, &decode_many_nvfp4);
 
     ops.def("quantize_nvfp4_out(Tensor packed_out, Tensor scales_out, Tensor weight, int group_size) -> ()");
     ops.impl("quantize_nvfp4_out", torch::kCUDA, &quantize_nvfp4_out);

@@ -1,0 +1,156 @@
+"""NVFP4 decode driver: quantises the bf16 weights with the library's quantisers, packs the
+24 x 208-byte pointer table and drives launch_decode_nvfp4 / launch_decode_many_nvfp4.
+
+Host-side mirror of the reference's NVFP4 driver (reference: megakernel/model_nvfp4.py:126-160,
+249-337, 456-473, 704-769): layer matrices in the 32-group / fp16-scale format, the LM head as its
+own packed copy in the 16-block / E4M3 format (even when it is tied to the embedding), norms, conv,
+beta / alpha projections and the embedding gather table in bf16.
+"""
+import ctypes
+import struct
+
+import torch
+
+from .model import (DN_CONV_CHANNELS, DN_CONV_KERNEL, DN_KEY_DIM, DN_NUM_HEADS, DN_VALUE_DIM, FA_HEAD_DIM,
+                    FA_NUM_KV_HEADS, HIDDEN_SIZE, _ptr)
+
+NVFP4_GROUP_SIZE = 32
+NVFP4_LM_GROUP_SIZE = 16
+
+
+def _quantize_matrix_nvfp4(lib, w, group_size=NVFP4_GROUP_SIZE):
+    rows, cols = w.shape
+    packed = torch.empty(rows, cols // 2, dtype=torch.uint8, device=w.device)
+    scales = torch.empty(rows, cols // group_size, dtype=torch.float16, device=w.device)
+    rc = lib.launch_quantize_nvfp4_out(_ptr(w), rows, cols, group_size, _ptr(packed), _ptr(scales),
+                                       ctypes.c_void_p(torch.cuda.current_stream(w.device).cuda_stream))
+    if rc != 0:
+        raise RuntimeError("quantize_nvfp4_out failed")
+    return {"packed": packed, "scales": scales}
+
+
+def _quantize_matrix_nvfp4_lm(lib, w):
+    rows, cols = w.shape
+    if rows % 128 or cols % 64:
+        raise ValueError("LM head needs rows % 128 == 0 and cols % 64 == 0")
+    packed = torch.empty(rows, cols // 2, dtype=torch.uint8, device=w.device)
+    scales = torch.zeros((rows // 128) * (cols // 64) * 512, dtype=torch.uint8, device=w.device)
+    rc = lib.launch_quantize_nvfp4_lm_out(_ptr(w), rows, cols, _ptr(packed), _ptr(scales),
+                                          ctypes.c_void_p(torch.cuda.current_stream(w.device).cuda_stream))
+    if rc != 0:
+        raise RuntimeError("quantize_nvfp4_lm_out failed")
+    return {"packed": packed, "scales": scales}
+
+
+def attach_nvfp4_weights(weights, group_size=NVFP4_GROUP_SIZE):
+    """Adds weights["nvfp4"] (reference: megakernel/model_nvfp4.py:249-337)."""
+    from . import lib as _lib
+    lib = _lib()
+    if "nvfp4" in weights and weights["nvfp4"]["group_size"] == group_size:
+        return weights
+    layers = []
+    for ld in weights["layer_data"]:
+        p = ld["ptrs"]
+        q = lambda i: _quantize_matrix_nvfp4(lib, p[i], group_size)
+        if ld["type"] == 1:
+            qq, kk, vv, oo, gg, uu, dd = q(1), q(2), q(3), q(6), q(8), q(9), q(10)
+            ptrs = [p[0], qq["packed"], qq["scales"], kk["packed"], kk["scales"], vv["packed"], vv["scales"], p[4], p[5],
+                    oo["packed"], oo["scales"], p[7], gg["packed"], gg["scales"], uu["packed"], uu["scales"],
+                    dd["packed"], dd["scales"]]
+        else:
+            qkv, zz, oo, gg, uu, dd = q(1), q(2), q(9), q(11), q(12), q(13)
+            ptrs = [p[0], qkv["packed"], qkv["scales"], zz["packed"], zz["scales"], p[3], p[4], p[5], p[6], p[7], p[8],
+                    oo["packed"], oo["scales"], p[10], gg["packed"], gg["scales"], uu["packed"], uu["scales"],
+                    dd["packed"], dd["scales"]]
+        layers.append({"type": ld["type"], "ptrs": ptrs})
+    lm = _quantize_matrix_nvfp4_lm(lib, weights["lm_head_weight"])
+    weights["nvfp4"] = {"group_size": group_size, "lm_group_size": NVFP4_LM_GROUP_SIZE, "layer_data": layers,
+                        "lm_head_weight_packed": lm["packed"], "lm_head_scales": lm["scales"]}
+    return weights
+
+
+def _pack_layer_weights_nvfp4(layer_data, group_size):
+    """Device blob of 208-byte entries {int type; int group_size; int pad[2]; void* ptrs[24]}
+    (reference: megakernel/model_nvfp4.py:456-473)."""
+    entry = struct.Struct("<4i24Q")
+    assert entry.size == 208
+    blob = bytearray()
+    for ld in layer_data:
+        ptrs = [t.data_ptr() for t in ld["ptrs"]]
+        blob += entry.pack(ld["type"], group_size, 0, 0, *(ptrs + [0] * (24 - len(ptrs))))
+    return torch.frombuffer(blob, dtype=torch.uint8).cuda()
+
+
+class Decoder:
+    """Stateful greedy decoder over the NVFP4 weights (reference: megakernel/model_nvfp4.py:499-769)."""
+
+    def __init__(self, weights, max_seq_len=2048, group_size=NVFP4_GROUP_SIZE):
+        from . import lib as _lib
+        self._lib = _lib()
+        self._weights = attach_nvfp4_weights(weights, group_size)
+        nv = self._weights["nvfp4"]
+        self.group_size = group_size
+        self.max_seq_len = int(max_seq_len)
+        self._embed_weight = weights["embed_weight"]
+        self._final_norm_weight = weights["final_norm_weight"]
+        self._lm_packed, self._lm_scales = nv["lm_head_weight_packed"], nv["lm_head_scales"]
+        self.num_layers = len(nv["layer_data"])
+        self.vocab = int(self._embed_weight.shape[0])
+        self._layer_weights_packed = _pack_layer_weights_nvfp4(nv["layer_data"], group_size)
+        dev = self._embed_weight.device
+        types = [ld["type"] for ld in nv["layer_data"]]
+        n_fa, n_dn = sum(types), len(types) - sum(types)
+        self._fa_k_cache = torch.zeros(max(n_fa, 1), FA_NUM_KV_HEADS, self.max_seq_len, FA_HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        self._fa_v_cache = torch.zeros_like(self._fa_k_cache)
+        self._dn_states = torch.zeros(max(n_dn, 1), DN_NUM_HEADS, DN_KEY_DIM, DN_VALUE_DIM, dtype=torch.float32, device=dev)
+        self._conv_bufs = torch.zeros(max(n_dn, 1), DN_CONV_CHANNELS, DN_CONV_KERNEL, dtype=torch.float32, device=dev)
+        self._hidden = torch.empty(HIDDEN_SIZE, dtype=torch.bfloat16, device=dev)
+        self._normalized = torch.empty(HIDDEN_SIZE, dtype=torch.float32, device=dev)
+        self._out_token = torch.empty(1, dtype=torch.int32, device=dev)
+        self._token_buffer = torch.empty(1, dtype=torch.int32, device=dev)
+        self._position = 0
+
+    def _common_args(self):
+        z = ctypes.c_void_p(0)
+        return [_ptr(self._embed_weight), _ptr(self._layer_weights_packed), _ptr(self._final_norm_weight),
+                _ptr(self._lm_packed), _ptr(self._lm_scales), z, z, z, z, _ptr(self._fa_k_cache), _ptr(self._fa_v_cache),
+                _ptr(self._dn_states), _ptr(self._conv_bufs), _ptr(self._hidden), z, z, z, z, z, z, z, z, z,
+                _ptr(self._normalized), z, z, z, z, z]
+
+    def _check(self, rc):
+        if rc != 0:
+            raise RuntimeError(f"luce_megakernel_b200 error {rc}: {self._lib.mk_last_error_string().decode()}")
+
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream(self._embed_weight.device).cuda_stream)
+
+    def step_async(self, token_id: int):
+        if self._position >= self.max_seq_len:
+            raise ValueError("position exceeds max_seq_len")
+        self._check(self._lib.mk_set_model_dims(self.num_layers, self.vocab))
+        self._out_token.fill_(int(token_id))       # the token travels through device memory, as in the reference op
+        self._check(self._lib.launch_decode_nvfp4(
+            _ptr(self._out_token), _ptr(self._out_token), *self._common_args(), ctypes.c_int(self._position),
+            ctypes.c_int(self.max_seq_len), ctypes.c_int(self.group_size), self._stream()))
+        self._position += 1
+
+    def step(self, token_id: int) -> int:
+        self.step_async(token_id)
+        return int(self._out_token.item())
+
+    def step_many(self, token_id: int, steps: int) -> torch.Tensor:
+        if self._position + steps > self.max_seq_len:
+            raise ValueError("position + steps exceeds max_seq_len")
+        self._check(self._lib.mk_set_model_dims(self.num_layers, self.vocab))
+        out = torch.empty(steps, dtype=torch.int32, device=self._out_token.device)
+        self._token_buffer.fill_(int(token_id))
+        self._check(self._lib.launch_decode_many_nvfp4(
+            _ptr(self._token_buffer), _ptr(out), ctypes.c_int(steps), *self._common_args(),
+            ctypes.c_int(self._position), ctypes.c_int(self.max_seq_len), ctypes.c_int(self.group_size), self._stream()))
+        self._position += steps
+        return out
+
+    def reset(self):
+        self._position = 0
+        for t in (self._fa_k_cache, self._fa_v_cache, self._dn_states, self._conv_bufs):
+            t.zero_()
