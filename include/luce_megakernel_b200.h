@@ -176,6 +176,10 @@ int mk_prefill_bf16(
     void *final_normed, void *hidden_bf16_out,
     int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
 const char *mk_prefill_error(void);
+/* Which form of the gated delta rule the prefill uses: 1 (default) = chunks of 64 tokens on the tensor cores
+ * (reference: the chunked kernels megakernel/prefill.cu:355-680), 0 = token-serial recurrence
+ * (reference: megakernel/prefill.cu:114-221).  Both give the same result up to rounding. */
+void mk_prefill_set_scan_mode(int chunked);
 
 /* The prefill projection GEMM on its own: C[M,N] = A[M,K] . W[N,K]^T (+ residual[M,N]), bf16 row-major,
  * f32 accumulation (tcgen05 / TMEM / TMA).  Replaces the cublasGemmEx call of the reference prefill

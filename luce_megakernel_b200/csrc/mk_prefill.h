@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <stddef.h>
 
 namespace mk {
 
@@ -10,5 +11,17 @@ namespace mk {
 // err_flag: device int, set to 1 if a bounded wait ran out inside the kernel.
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
                          int* err_flag, cudaStream_t stream);
+
+// Gated delta rule over a prompt in chunks of 64 tokens (all 16 heads of one layer).
+// pre: f32 [S][6144] = q | k | v (q, k normalised); gates: f32 [S][16][4] = beta, decay, q.k, log decay;
+// state: f32 [16][128 value][128 key], updated in place; o: f32 [S][2048]; scratch: dn_chunked_scratch_bytes(S).
+size_t dn_chunked_scratch_bytes(int S);
+cudaError_t dn_chunked(const float* pre, const float* gates, float* state, float* o, int S, void* scratch, int* err,
+                       cudaStream_t stream);
+
+// Causal GQA attention over a prompt (one layer): qkv bf16 [S][5120] = 8 x [q | gate] | k | v with q normalised
+// and rotated; kc, vc: bf16 [2][max_seq][256] (already holding the prompt's keys / values); out bf16 [S][2048]
+// = softmax(q k^T / 16) v * sigmoid(gate).
+cudaError_t fa_prefill(const void* qkv, const void* kc, const void* vc, void* out, int S, int max_seq, cudaStream_t stream);
 
 }  // namespace mk

@@ -99,7 +99,9 @@ __global__ void k_dn_gates(const __nv_bfloat16* __restrict__ xn, const __nv_bflo
         else {
             const float x = acc + ld_bf(dt_bias + h);
             const float sp = (x > 20.0f) ? x : log1pf(expf(x));
-            decay[(t * 16 + h) * 4 + 1] = expf(-expf(ld_bf(a_log + h)) * sp);
+            const float g = -expf(ld_bf(a_log + h)) * sp;
+            decay[(t * 16 + h) * 4 + 1] = expf(g);
+            decay[(t * 16 + h) * 4 + 3] = g;
         }
     }
 }
@@ -170,7 +172,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
-// gates: [t][head][4] = beta, decay, q.k, unused
+// gates: [t][head][4] = beta, decay, q.k, log decay
 __global__ void __launch_bounds__(512) k_dn_scan(const float* __restrict__ pre, const float* __restrict__ gates,
                                                  float* __restrict__ state, float* __restrict__ o, int S) {
     extern __shared__ __align__(16) float scan_sm[];
@@ -287,51 +289,6 @@ __global__ void k_fa_norm_rope(__nv_bfloat16* __restrict__ qkv, const __nv_bfloa
     for (int e = 0; e < 8; ++e) dst[lane + 32 * e] = __float2bfloat16_rn(n[e]);
 }
 
-// causal attention, online softmax, one warp per (query t, head); out = softmax(q k / 16) v * sigmoid(gate)
-// (reference: prefill.cu:270-294, 1182-1200)
-__global__ void k_fa_attention(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ kc,
-                               const __nv_bfloat16* __restrict__ vc, __nv_bfloat16* __restrict__ out, int S, int max_seq) {
-    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (wid >= S * FA_Q_HEADS) return;
-    const int t = wid >> 3, h = wid & 7, g = h / FA_GQA;
-    const __nv_bfloat16* qrow = qkv + (size_t)t * FA_QKV_ROWS + h * 2 * FA_HEAD_DIM;
-    float q[8], acc[8], m = -1e30f, l = 0.f;
-    {
-        const uint4 u = reinterpret_cast<const uint4*>(qrow)[lane];
-        q[0] = bf_lo(u.x); q[1] = bf_hi(u.x); q[2] = bf_lo(u.y); q[3] = bf_hi(u.y);
-        q[4] = bf_lo(u.z); q[5] = bf_hi(u.z); q[6] = bf_lo(u.w); q[7] = bf_hi(u.w);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) { q[e] *= 0.0625f; acc[e] = 0.f; }
-    }
-    const __nv_bfloat16* K = kc + (size_t)g * max_seq * FA_HEAD_DIM;
-    const __nv_bfloat16* V = vc + (size_t)g * max_seq * FA_HEAD_DIM;
-    for (int p = 0; p <= t; ++p) {
-        const uint4 ku = reinterpret_cast<const uint4*>(K + (size_t)p * FA_HEAD_DIM)[lane];
-        const uint4 vu = reinterpret_cast<const uint4*>(V + (size_t)p * FA_HEAD_DIM)[lane];
-        float s = q[0] * bf_lo(ku.x) + q[1] * bf_hi(ku.x) + q[2] * bf_lo(ku.y) + q[3] * bf_hi(ku.y) +
-                  q[4] * bf_lo(ku.z) + q[5] * bf_hi(ku.z) + q[6] * bf_lo(ku.w) + q[7] * bf_hi(ku.w);
-        s = warp_sum(s);
-        const float mn = fmaxf(m, s), corr = __expf(m - mn), pe = __expf(s - mn);
-        l = l * corr + pe;
-        acc[0] = acc[0] * corr + pe * bf_lo(vu.x); acc[1] = acc[1] * corr + pe * bf_hi(vu.x);
-        acc[2] = acc[2] * corr + pe * bf_lo(vu.y); acc[3] = acc[3] * corr + pe * bf_hi(vu.y);
-        acc[4] = acc[4] * corr + pe * bf_lo(vu.z); acc[5] = acc[5] * corr + pe * bf_hi(vu.z);
-        acc[6] = acc[6] * corr + pe * bf_lo(vu.w); acc[7] = acc[7] * corr + pe * bf_hi(vu.w);
-        m = mn;
-    }
-    const uint4 gu = reinterpret_cast<const uint4*>(qrow + FA_HEAD_DIM)[lane];
-    const float gt[8] = {bf_lo(gu.x), bf_hi(gu.x), bf_lo(gu.y), bf_hi(gu.y), bf_lo(gu.z), bf_hi(gu.z), bf_lo(gu.w), bf_hi(gu.w)};
-    const float inv = 1.0f / l;
-    uint32_t o[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat162 p2 = __floats2bfloat162_rn(acc[2 * e] * inv * sigmoid_f(gt[2 * e]),
-                                                        acc[2 * e + 1] * inv * sigmoid_f(gt[2 * e + 1]));
-        o[e] = *reinterpret_cast<const uint32_t*>(&p2);
-    }
-    reinterpret_cast<uint4*>(out + (size_t)t * FA_Q_SIZE + h * FA_HEAD_DIM)[lane] = make_uint4(o[0], o[1], o[2], o[3]);
-}
-
 // ---- MLP glue, final norm, LM head -------------------------------------------------------------------
 
 // act[t, i] = silu(gu[t, i]) * gu[t, 3584 + i]   (reference: prefill.cu:1239-1247)
@@ -429,6 +386,7 @@ struct PrefillWs {
     __nv_bfloat16 *hidden = nullptr, *normed = nullptr, *wide = nullptr, *z = nullptr, *act = nullptr;
     float *pre = nullptr, *o = nullptr, *beta = nullptr, *decay = nullptr, *kq = nullptr, *normed_f32 = nullptr, *bval = nullptr;
     int *bidx = nullptr, *err = nullptr;
+    void* chunk_scratch = nullptr;
 };
 PrefillWs g_pws[64];
 constexpr int LM_BLOCKS = 1184;     // 8 resident blocks of 256 threads on each of 148 SMs
@@ -436,12 +394,12 @@ constexpr int LM_BLOCKS = 1184;     // 8 resident blocks of 256 threads on each 
 cudaError_t ensure_ws(PrefillWs& w, int S) {
     if (S <= w.cap) return cudaSuccess;
     void** ptrs[] = {(void**)&w.hidden, (void**)&w.normed, (void**)&w.wide, (void**)&w.z, (void**)&w.act, (void**)&w.pre,
-                     (void**)&w.o, (void**)&w.beta, (void**)&w.decay, (void**)&w.kq};
+                     (void**)&w.o, (void**)&w.beta, (void**)&w.decay, (void**)&w.kq, &w.chunk_scratch};
     for (void** p : ptrs) { if (*p) cudaFree(*p); *p = nullptr; }
     const size_t s = (size_t)S;
     const size_t sizes[] = {s * HIDDEN * 2, s * HIDDEN * 2, s * 2 * INTER * 2, s * DN_V * 2, s * INTER * 2,
-                            s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 16, 16, 16};
-    for (int i = 0; i < 10; ++i) {
+                            s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 16, 16, 16, dn_chunked_scratch_bytes(S)};
+    for (int i = 0; i < 11; ++i) {
         cudaError_t e = cudaMalloc(ptrs[i], sizes[i]);
         if (e != cudaSuccess) { w.cap = 0; return e; }
     }
@@ -462,6 +420,7 @@ cudaError_t ensure_ws(PrefillWs& w, int S) {
 }
 
 thread_local char g_perr[200] = "";
+int g_scan_mode = 1;              // 1 = chunks of 64 on the tensor cores, 0 = token-serial recurrence
 int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
     if (e != cudaSuccess) snprintf(g_perr, sizeof(g_perr), "%s: %s", what, cudaGetErrorString(e));
     else snprintf(g_perr, sizeof(g_perr), "%s", what);
@@ -478,6 +437,7 @@ int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
 }  // namespace mk
 
 extern "C" const char* mk_prefill_error(void) { return mk::g_perr; }
+extern "C" void mk_prefill_set_scan_mode(int chunked) { mk::g_scan_mode = chunked ? 1 : 0; }
 
 extern "C" int mk_prefill_bf16(
     const int* token_ids, int seq_len, int* output_token,
@@ -531,7 +491,8 @@ extern "C" int mk_prefill_bf16(
                 w.normed, (const bf*)lw.ptrs[DN_W_B], (const bf*)lw.ptrs[DN_W_A], (const bf*)lw.ptrs[DN_A_LOG],
                 (const bf*)lw.ptrs[DN_DT_BIAS], w.beta, w.beta, S);
             k_dn_preproject<<<dim3(S, DN_HEADS), 128, 0, stream>>>(w.wide, (const bf*)lw.ptrs[DN_CONV_W], cstate, w.pre, w.beta, S);
-            k_dn_scan<<<128, 512, SCAN_SMEM, stream>>>(w.pre, w.beta, state, w.o, S);
+            if (g_scan_mode == 0) k_dn_scan<<<128, 512, SCAN_SMEM, stream>>>(w.pre, w.beta, state, w.o, S);
+            else PF_CHECK(dn_chunked(w.pre, w.beta, state, w.o, S, w.chunk_scratch, w.err, stream), "chunked scan");
             k_dn_conv_state<<<(DN_CONV_CH + 255) / 256, 256, 0, stream>>>(w.wide, cstate, S);
             k_dn_gated_norm<<<blocks_for_warps((long long)S * DN_HEADS), 256, 0, stream>>>(w.o, w.z, (const bf*)lw.ptrs[DN_NORM_W], w.act, S);
             PF_CHECK(gemm(w.act, lw.ptrs[DN_W_OUT], w.hidden, w.hidden, HIDDEN, DN_V), "gemm out");
@@ -543,7 +504,7 @@ extern "C" int mk_prefill_bf16(
             PF_CHECK(gemm(w.normed, wqkv, w.wide, nullptr, FA_QKV_ROWS, HIDDEN), "gemm fa qkv");
             k_fa_norm_rope<<<blocks_for_warps((long long)S * 12), 256, 0, stream>>>(
                 w.wide, (const bf*)lw.ptrs[FA_Q_NORM], (const bf*)lw.ptrs[FA_K_NORM], kc, vc, S, max_seq_len);
-            k_fa_attention<<<blocks_for_warps((long long)S * FA_Q_HEADS), 256, 0, stream>>>(w.wide, kc, vc, w.act, S, max_seq_len);
+            PF_CHECK(fa_prefill(w.wide, kc, vc, w.act, S, max_seq_len, stream), "attention");
             PF_CHECK(gemm(w.act, lw.ptrs[FA_W_O], w.hidden, w.hidden, HIDDEN, FA_Q_SIZE), "gemm o");
             ++fa_idx;
         }

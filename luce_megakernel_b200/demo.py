@@ -23,7 +23,7 @@ def main():
     ap.add_argument("--prefill", type=int, default=0, help="prompt length processed by the prefill op instead of the decode kernel")
     args = ap.parse_args()
     weights, _ = M.load_weights(seed=0, num_layers=args.layers, vocab=args.vocab, device_init=True)
-    dec = M.Decoder(weights=weights, max_seq_len=max(2048, args.context + args.steps + 8), api="cabi")
+    dec = M.Decoder(weights=weights, max_seq_len=max(2048, args.context + args.steps + 8, args.prefill + args.steps + 8), api="cabi")
     if args.prefill > 0:
         g = torch.Generator().manual_seed(0)
         ids = torch.randint(0, args.vocab, (args.prefill,), generator=g)

@@ -1,8 +1,10 @@
 """GPU parity of the bf16 prefill against the CPU oracle, and the prefill -> decode handoff.
 
 Bounds as for decode (see tests/test_decode_gpu.py): last-row hidden within 2e-2 or four bf16
-ulps of its largest element, logits within 5e-2, first token identical where the oracle margin
-allows; session state (KV cache, DeltaNet state, conv window) compared in the op layouts.
+ulps of its largest element, or twice the distance between the oracle with the decode kernel's bf16
+rounding points and the oracle without any (the noise a bf16 implementation with other rounding
+points carries: the prefill rounds projections and softmax weights to bf16, the decode path does
+not); logits within 5e-2, first token identical where the oracle margin allows; session state (KV cache, DeltaNet state, conv window) compared in the op layouts.
 The prefill rounds the projection outputs to bf16 between kernels (as the reference prefill does,
 megakernel/prefill.cu:1615-1616), which the oracle does not: conv windows and keys carry that
 rounding, hence their looser bounds.
@@ -43,8 +45,11 @@ def test_prefill_matches_oracle(dec, small_model, S):
     st = O.State.new(NL, MAXSEQ, V)
     tr = orc.forward(toks, st)
     ref_h = tr.hidden[-1][-1]
+    _, o32 = small_model("unit", "none")
+    h32 = o32.forward(toks, O.State.new(NL, MAXSEQ, V), want_logits=False).hidden[-1][-1]
     eh = float((dec._hidden_bf16_out.float().cpu() - ref_h).abs().max())
-    assert eh <= max(2e-2, 4 * bf16_ulp(float(ref_h.abs().max()))), f"hidden error {eh}"
+    tol = max(2e-2, 4 * bf16_ulp(float(ref_h.abs().max())), 2.0 * float((h32 - ref_h).abs().max()))
+    assert eh <= tol, f"hidden error {eh} (bound {tol})"
     lm = sd["model.embed_tokens.weight"].float()
     logits = lm @ dec._final_normed.float().cpu()
     assert float((logits - tr.logits).abs().max()) <= 6e-2       # final_normed is returned in bf16
