@@ -180,6 +180,9 @@ const char *mk_prefill_error(void);
  * (reference: the chunked kernels megakernel/prefill.cu:355-680), 0 = token-serial recurrence
  * (reference: megakernel/prefill.cu:114-221).  Both give the same result up to rounding. */
 void mk_prefill_set_scan_mode(int chunked);
+/* The prefill keeps a host copy of each layer pointer table it has seen (keyed by device and table address), as
+ * the reference does (megakernel/prefill.cu:1578-1584).  Call this after rewriting a table in place. */
+void mk_prefill_forget_tables(void);
 
 /* The prefill projection GEMM on its own: C[M,N] = A[M,K] . W[N,K]^T (+ residual[M,N]), bf16 row-major,
  * f32 accumulation (tcgen05 / TMEM / TMA).  Replaces the cublasGemmEx call of the reference prefill

@@ -2,10 +2,13 @@
 //   C[M, N] = A[M, K] . W[N, K]^T     A, W, C bf16 row-major (both operands K-major), f32 accumulate
 // optionally C += R (residual, bf16 [M, N]) before the bf16 rounding.
 //
-// One 128 x 128 output tile per CTA.  Warp 0 streams A and W tiles (128 rows x 64 k, 128-byte
-// swizzle) with TMA into a 4-stage shared-memory ring; one thread of warp 1 issues
-// tcgen05.mma (M128 N128 K16, cta_group::1) with the accumulator in tensor memory; warps 2-5
-// read the accumulator back with tcgen05.ld (each warp its own 32-lane quadrant) and store bf16.
+// Persistent kernel, one CTA per SM, each walking 128 x BN output tiles (BN = 256, or 128 for small
+// problems).  Warp 0 streams A and W tiles (rows x 64 k, 128-byte swizzle) with TMA into a
+// shared-memory ring; one thread of warp 1 issues tcgen05.mma (M128 x BN x K16, cta_group::1) into one
+// of two accumulator buffers in tensor memory; warps 2-5 read a finished accumulator back with
+// tcgen05.ld (each warp its own 32-lane quadrant), add the residual and store bf16 while the MMA
+// thread is already working on the next tile.  With BN = 256 an MMA reads 12 KB of shared memory per
+// 128 tensor-core cycles, which stays under the shared-memory bandwidth; 128-wide tiles sit at it.
 // M is the token dimension: rows beyond M are zero-filled by TMA and not stored.
 // Every wait is bounded; on expiry the kernel sets *err and leaves.
 #include <cuda.h>
@@ -21,13 +24,16 @@ namespace mk {
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64;
-constexpr int STAGES = 4;
+constexpr int BM = 128, BK = 64;
 constexpr int TILE_A_BYTES = BM * BK * 2;                 // 16 KB
-constexpr int TILE_B_BYTES = BN * BK * 2;                 // 16 KB
-constexpr int GEMM_SMEM = STAGES * (TILE_A_BYTES + TILE_B_BYTES) + 1024 /*align slack*/ + 256;
 constexpr int GEMM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 128;
+template <int BN> struct Cfg {
+    static constexpr int STAGES = (BN == 256) ? 4 : 6;
+    static constexpr int TILE_B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = TILE_A_BYTES + TILE_B_BYTES;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;         // two accumulator buffers
+};
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
     asm volatile(
@@ -70,28 +76,31 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, int*
     return false;
 }
 
+template <int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                     __nv_bfloat16* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc,
                     int* err) {
+    typedef Cfg<BN> G;
+    constexpr int STAGES = G::STAGES;
     extern __shared__ char smem_raw[];
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t a0 = sbase, b0 = sbase + STAGES * TILE_A_BYTES;
-    const uint32_t bars = sbase + STAGES * (TILE_A_BYTES + TILE_B_BYTES);
-    const uint32_t full0 = bars, empty0 = bars + 8 * STAGES, tfull = bars + 16 * STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * (TILE_A_BYTES + TILE_B_BYTES) + 16 * STAGES + 16);
+    const uint32_t bars = sbase + STAGES * G::STAGE_BYTES;
+    const uint32_t full0 = bars, empty0 = bars + 8 * STAGES, tfull0 = bars + 16 * STAGES, tempty0 = tfull0 + 16;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * G::STAGE_BYTES + 16 * STAGES + 32);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int nk = K / BK;
+    const int mt = (M + BM - 1) / BM, ntiles = mt * (N / BN);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(full0 + 8 * s, 1); mbar_init(empty0 + 8 * s, 1); }
-        mbar_init(tfull, 1);
+        for (int b = 0; b < 2; ++b) { mbar_init(tfull0 + 8 * b, 1); mbar_init(tempty0 + 8 * b, 4); }
         fence_mbar_init();
     }
     if (warp == 1) {   // one warp allocates the accumulator columns
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(G::TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -102,44 +111,58 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int kb = 0; kb < nk && ok; ++kb) {
-                const int s = kb % STAGES;
-                const uint32_t par = (kb / STAGES) & 1u;
-                ok = wait_bounded(empty0 + 8 * s, par ^ 1u, err);
-                if (!ok) break;
-                mbar_expect_tx(full0 + 8 * s, TILE_A_BYTES + TILE_B_BYTES);
-                tma_load_2d(a0 + s * TILE_A_BYTES, &map_a, kb * BK, m0, full0 + 8 * s);
-                tma_load_2d(b0 + s * TILE_B_BYTES, &map_w, kb * BK, n0, full0 + 8 * s);
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+                const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const uint32_t s = it % STAGES, par = (it / STAGES) & 1u;
+                    ok = wait_bounded(empty0 + 8 * s, par ^ 1u, err);
+                    if (!ok) break;
+                    mbar_expect_tx(full0 + 8 * s, G::STAGE_BYTES);
+                    tma_load_2d(a0 + s * TILE_A_BYTES, &map_a, kb * BK, m0, full0 + 8 * s);
+                    tma_load_2d(b0 + s * G::TILE_B_BYTES, &map_w, kb * BK, n0, full0 + 8 * s);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = idesc_bf16(BM, BN);
-            for (int kb = 0; kb < nk && ok; ++kb) {
-                const int s = kb % STAGES;
-                const uint32_t par = (kb / STAGES) & 1u;
-                ok = wait_bounded(full0 + 8 * s, par, err);
+            uint32_t it = 0, local = 0;
+            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++local) {
+                const uint32_t buf = local & 1u, use = local >> 1;
+                ok = wait_bounded(tempty0 + 8 * buf, (use & 1u) ^ 1u, err);     // epilogue has drained this buffer
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint64_t ad = smem_desc_sw128(a0 + s * TILE_A_BYTES), bd = smem_desc_sw128(b0 + s * TILE_B_BYTES);
+                const uint32_t acc = tmem + buf * BN;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const uint32_t s = it % STAGES, par = (it / STAGES) & 1u;
+                    ok = wait_bounded(full0 + 8 * s, par, err);
+                    if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint64_t ad = smem_desc_sw128(a0 + s * TILE_A_BYTES), bd = smem_desc_sw128(b0 + s * G::TILE_B_BYTES);
 #pragma unroll
-                for (int k = 0; k < BK / 16; ++k)   // 16 bf16 = 32 bytes = 2 descriptor units per step
-                    umma(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) ? 1u : 0u);
-                umma_commit(empty0 + 8 * s);        // frees the stage once these MMAs have read it
+                    for (int k = 0; k < BK / 16; ++k)   // 16 bf16 = 32 bytes = 2 descriptor units per step
+                        umma(acc, ad + 2 * k, bd + 2 * k, idesc, (kb | k) ? 1u : 0u);
+                    umma_commit(empty0 + 8 * s);        // frees the stage once these MMAs have read it
+                }
+                if (ok) umma_commit(tfull0 + 8 * buf);  // accumulator complete
             }
-            umma_commit(tfull);                     // accumulator complete
         }
     } else {
         // epilogue warps 2..5: warp w may touch TMEM lanes 32*(w%4) .. +31
         const int quad = warp & 3;
-        ok = wait_bounded(tfull, 0, err);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int row = m0 + quad * 32 + lane;
-        if (ok) {
+        uint32_t local = 0;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++local) {
+            const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
+            const uint32_t buf = local & 1u, use = local >> 1;
+            ok = wait_bounded(tfull0 + 8 * buf, use & 1u, err);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int row = m0 + quad * 32 + lane;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 uint32_t v[32];
-                const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0;
+                const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * BN + (uint32_t)c0;
                 asm volatile(
                     "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
                     "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -172,13 +195,17 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
                     }
                 }
             }
+            // hand the accumulator buffer back to the MMA thread
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::TMEM_COLS) : "memory");
     }
 }
 
@@ -196,39 +223,55 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// rows x k bf16 matrix with row pitch `ld` elements; box = 64 k x 128 rows, 128-byte swizzle
-bool make_map(CUtensorMap* map, const void* base, int rows, int k, int ld) {
+// rows x k bf16 matrix with row pitch `ld` elements; box = 64 k x box_rows rows, 128-byte swizzle
+bool make_map(CUtensorMap* map, const void* base, int rows, int k, int ld, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-}  // namespace
-
-cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
-                         int* err_flag, cudaStream_t stream) {
-    if (M <= 0 || N <= 0 || K <= 0 || N % BN || K % BK) return cudaErrorInvalidValue;
-    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(C)) & 15u)
-        return cudaErrorInvalidValue;
-    if ((lda % 8) || (ldc % 8)) return cudaErrorInvalidValue;
+template <int BN>
+cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc, int* err_flag,
+                        int sms, cudaStream_t stream) {
     static bool attr_done = false;
     if (!attr_done) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM);
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
         if (e != cudaSuccess) return e;
         attr_done = true;
     }
     CUtensorMap ma, mw;
-    if (!make_map(&ma, A, M, K, lda) || !make_map(&mw, W, N, K, K)) return cudaErrorInvalidValue;
-    dim3 grid(N / BN, (M + BM - 1) / BM);
-    gemm_bf16_tn_kernel<<<grid, GEMM_THREADS, GEMM_SMEM, stream>>>(ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K,
-                                                                   ldc, err_flag);
+    if (!make_map(&ma, A, M, K, lda, BM) || !make_map(&mw, W, N, K, K, BN)) return cudaErrorInvalidValue;
+    const int ntiles = ((M + BM - 1) / BM) * (N / BN);
+    gemm_bf16_tn_kernel<BN><<<ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(
+        ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K, ldc, err_flag);
     return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
+                         int* err_flag, cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % BK) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(C)) & 15u)
+        return cudaErrorInvalidValue;
+    if ((lda % 8) || (ldc % 8)) return cudaErrorInvalidValue;
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+    }
+    // 256-wide tiles once they fill the machine; 128-wide tiles keep more SMs busy on small problems
+    const int mt = (M + BM - 1) / BM;
+    if (N % 256 == 0 && mt * (N / 256) >= sms) return launch_gemm<256>(A, W, C, R, M, N, K, lda, ldc, err_flag, sms, stream);
+    return launch_gemm<128>(A, W, C, R, M, N, K, lda, ldc, err_flag, sms, stream);
 }
 
 }  // namespace mk

@@ -419,6 +419,8 @@ cudaError_t ensure_ws(PrefillWs& w, int S) {
     return cudaSuccess;
 }
 
+struct HostTable { const void* src = nullptr; int n = 0; LayerWeights rows[MAX_LAYERS]; };
+HostTable g_tables[64];
 thread_local char g_perr[200] = "";
 int g_scan_mode = 1;              // 1 = chunks of 64 on the tensor cores, 0 = token-serial recurrence
 int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
@@ -437,6 +439,7 @@ int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
 }  // namespace mk
 
 extern "C" const char* mk_prefill_error(void) { return mk::g_perr; }
+extern "C" void mk_prefill_forget_tables(void) { for (auto& t : mk::g_tables) { t.src = nullptr; t.n = 0; } }
 extern "C" void mk_prefill_set_scan_mode(int chunked) { mk::g_scan_mode = chunked ? 1 : 0; }
 
 extern "C" int mk_prefill_bf16(
@@ -463,10 +466,18 @@ extern "C" int mk_prefill_bf16(
         scan_attr[dev] = true;
     }
 
-    // the pointer table lives on the device; the launches below need its entries on the host
-    LayerWeights hl[MAX_LAYERS];
-    PF_CHECK(cudaMemcpyAsync(hl, layers, (size_t)num_layers * sizeof(LayerWeights), cudaMemcpyDeviceToHost, stream), "table copy");
-    PF_CHECK(cudaStreamSynchronize(stream), "table copy sync");
+    // The pointer table lives on the device; the launches below need its entries on the host.  The
+    // host copy is kept per device and table address, as the reference keeps its own
+    // (megakernel/prefill.cu:1578-1584): a caller that rewrites a table in place must call
+    // mk_prefill_forget_tables() first.  With the copy cached the call enqueues work only (no
+    // synchronisation), so a whole prefill can be captured into a CUDA graph.
+    HostTable& ht = g_tables[dev];
+    if (ht.src != (const void*)layers || ht.n != num_layers) {
+        PF_CHECK(cudaMemcpyAsync(ht.rows, layers, (size_t)num_layers * sizeof(LayerWeights), cudaMemcpyDeviceToHost, stream), "table copy");
+        PF_CHECK(cudaStreamSynchronize(stream), "table copy sync");
+        ht.src = layers; ht.n = num_layers;
+    }
+    const LayerWeights* hl = ht.rows;
 
     const int S = seq_len;
     typedef __nv_bfloat16 bf;

@@ -103,6 +103,8 @@ def _pack_layer_weights(layer_data):
     for ld in layer_data:
         ptrs = [t.data_ptr() for t in ld["ptrs"]]
         blob += entry.pack(ld["type"], 0, 0, 0, *(ptrs + [0] * (14 - len(ptrs))))
+    from . import lib
+    lib().mk_prefill_forget_tables()      # a new table may reuse the address of a freed one
     return torch.frombuffer(blob, dtype=torch.uint8).cuda()
 
 
@@ -267,6 +269,12 @@ class Decoder:
     def prefill(self, token_ids) -> int:
         """Process a whole prompt from position 0 (state must be reset); returns the first generated
         token.  Afterwards step()/step_many() continue from position len(token_ids)."""
+        return int(self.prefill_async(token_ids).item())
+
+    def prefill_async(self, token_ids):
+        """prefill() without the device-to-host read: returns the int32[1] device tensor that will hold
+        the first generated token.  After the first call for a given weight table this only enqueues
+        work, so it can be captured into a CUDA graph (pass a device int32 tensor of ids)."""
         ids = torch.as_tensor(token_ids, dtype=torch.int32).to(self._embed_weight.device).contiguous()
         S = int(ids.numel())
         if S < 1 or S > self.max_seq_len:
@@ -295,7 +303,7 @@ class Decoder:
             if rc != 0:
                 raise RuntimeError(f"prefill failed ({rc}): {self._lib.mk_prefill_error().decode()}")
         self._position = S
-        return int(self._out_token.item())
+        return self._out_token
 
     def reset(self):
         self._position = 0
