@@ -211,9 +211,17 @@ def _rms(x: torch.Tensor, w1p: torch.Tensor) -> torch.Tensor:
 class Oracle:
     """fp32 restatement of the reference decode arithmetic, usable for T>=1 consecutive tokens."""
 
-    def __init__(self, weights: Dict[str, torch.Tensor], rounding: str = "decode"):
+    def __init__(self, weights: Dict[str, torch.Tensor], rounding: str = "decode", ref_q_rope_in_place: bool = False):
+        """ref_q_rope_in_place reproduces what the reference decode kernel actually computes for the
+        query's rotary dims 32..63: it rotates q in place (kernel.cu:487-497), so by the time a lane
+        reaches dim i+32 its partner dim i already holds the rotated value, which is then normalised
+        a second time.  At position 0 the rotation is the identity and nothing changes; from position
+        1 on the result differs from the reference's own PyTorch baseline (transformers' rotate_half).
+        This library follows the baseline; the flag exists only so that the tests can pin this
+        restatement against the reference kernels themselves, run on a GPU."""
         assert rounding in ("decode", "none")
         self.rounding = rounding
+        self.ref_q_rope_in_place = ref_q_rope_in_place
         self.w = {k: v.to(torch.float32) for k, v in weights.items()}
         self.num_layers = 1 + max(int(k.split(".")[2]) for k in weights if k.startswith("model.layers."))
         self.types = layer_types(self.num_layers)
@@ -269,6 +277,7 @@ class Oracle:
         q, gate = qg[..., :FA_HEAD_DIM], qg[..., FA_HEAD_DIM:]
         k = (x @ w[p + "k_proj.weight"].T).reshape(T, FA_KV_HEADS, FA_HEAD_DIM)
         v = (x @ w[p + "v_proj.weight"].T).reshape(T, FA_KV_HEADS, FA_HEAD_DIM)
+        q_scale = torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + RMS_EPS)
         q = _rms(q, 1.0 + w[p + "q_norm.weight"])                                       # kernel.cu:487-491
         k = _rms(k, 1.0 + w[p + "k_norm.weight"])                                       # kernel.cu:462-466
         pos = torch.arange(pos0, pos0 + T, dtype=torch.float32)
@@ -279,7 +288,15 @@ class Oracle:
             lo, hi, rest = t[..., :32], t[..., 32:64], t[..., 64:]
             return torch.cat([lo * cos - hi * sin, hi * cos + lo * sin, rest], dim=-1)
 
-        q, k = rope(q), rope(k)
+        if self.ref_q_rope_in_place:
+            w1p = 1.0 + w[p + "q_norm.weight"]
+            lo, hi, rest = q[..., :32], q[..., 32:64], q[..., 64:]
+            lo_out = lo * cos - hi * sin
+            partner = lo_out * q_scale * w1p[:32]          # the already rotated value, normalised again
+            q = torch.cat([lo_out, partner * sin + hi * cos, rest], dim=-1)
+        else:
+            q = rope(q)
+        k = rope(k)
         st.k_cache[idx, :, pos0:pos0 + T] = self._r(k).transpose(0, 1)                   # kernel.cu:474-476
         st.v_cache[idx, :, pos0:pos0 + T] = self._r(v).transpose(0, 1)
         L = pos0 + T
