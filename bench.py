@@ -34,7 +34,16 @@ def algorithmic_bytes_per_token(context_len: float) -> float:
     return WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POS * context_len
 
 
-PREFILL_TFLOP_PP520 = 0.539        # GEMMs + attention + scan + one LM-head pass at S = 520
+def prefill_tflop(S: int) -> float:
+    """Algorithmic FLOPs of a dense prefill of S tokens, in TFLOP: all per-token linear layers, causal
+    attention (6 layers, 8 heads, head_dim 256), the gated delta rule in its recurrent-form count, one LM-head pass."""
+    gemm = 2.0 * 497_614_848 * S
+    attn = 6 * 8 * (4 * 256) * S * (S + 1) / 2.0
+    scan = 18 * 16 * (6 * 128 * 128) * S
+    return (gemm + attn + scan + 2.0 * 254_279_680) / 1e12
+
+
+PREFILL_TFLOP_PP520 = prefill_tflop(520)        # 0.539
 
 
 def measured_bf16_peak():
@@ -162,6 +171,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-long-prefill", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -249,6 +259,25 @@ def main():
     barrier()
     pp_ms = p0.elapsed_time(p1) / 10
 
+    # dense prefill at 8192 and 32768 tokens, single GPU only: 1 warm-up + 2 timed calls
+    long_pp = []
+    if world == 1 and not args.no_long_prefill:
+        for S_ in (8192, 32768):
+            d2 = M.Decoder(weights=weights, max_seq_len=S_ + 8, api="cabi")
+            ids = torch.randint(0, M.VOCAB_SIZE, (S_,), generator=g).to(torch.int32).cuda()
+            d2.prefill(ids)
+            torch.cuda.synchronize()
+            p0.record()
+            for _ in range(2):
+                d2._position = 0
+                d2.prefill_async(ids)
+            p1.record()
+            torch.cuda.synchronize()
+            long_pp.append((S_, p0.elapsed_time(p1) / 2))
+            del d2
+        if lib().mk_device_status() != 0:
+            raise SystemExit("device-side wait timed out during the long prefill")
+
     t_all = torch.tensor([ms, e2e_s, pp_ms], dtype=torch.float64, device="cuda")
     if use_dist:
         dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
@@ -276,10 +305,15 @@ def main():
             "prefill": {"prompt_len": PROMPT_LEN, "ms": pp_max, "tok_s": world * PROMPT_LEN / (pp_max * 1e-3),
                         "tflops_algorithmic": PREFILL_TFLOP_PP520 / (pp_max * 1e-3),
                         "frac_of_bf16_peak": PREFILL_TFLOP_PP520 / (pp_max * 1e-3) / measured_bf16_peak(),
-                        "note": "prefill_bf16 op, tcgen05 GEMMs + token-serial DeltaNet scan + scalar attention"},
+                        "note": "prefill_bf16 op: persistent tcgen05/TMEM GEMMs fed by TMA, chunk-64 DeltaNet scan and "
+                                "causal GQA flash attention on mma.sync"},
             "gpu_launches": world * tokens,
             "clocks": clocks,
         }
+        if world == 1 and long_pp:
+            out["prefill_long"] = [
+                {"prompt_len": S_, "ms": ms_, "tok_s": S_ / (ms_ * 1e-3), "tflops_algorithmic": prefill_tflop(S_) / (ms_ * 1e-3),
+                 "frac_of_bf16_peak": prefill_tflop(S_) / (ms_ * 1e-3) / measured_bf16_peak()} for S_, ms_ in long_pp]
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
             sd = {k: v for k, v in cpu_state_dict(weights).items()}
