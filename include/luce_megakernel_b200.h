@@ -184,6 +184,23 @@ void mk_prefill_set_scan_mode(int chunked);
  * the reference does (megakernel/prefill.cu:1578-1584).  Call this after rewriting a table in place. */
 void mk_prefill_forget_tables(void);
 
+/* Block-sparse attention for long prompts (off by default: dense causal attention).  Attention runs over
+ * 128 x 128 blocks; per query head and query block the kept key blocks are the first `sink` blocks, the `window`
+ * most recent ones (the diagonal included) and the ceil(top_frac * causal blocks) best by
+ * mean-pooled q . mean-pooled k (ties to the lower index).  Structure after the reference's selection
+ * (reference: dflash/src/flashprefill_select.cpp:27-84, dflash/src/flashprefill_kernels.cu:57-90,130-219);
+ * the benchmark's rule is sink 1, window 4, top_frac 0.10. */
+int mk_prefill_set_block_sparse(int enable, double top_frac, int window, int sink);
+/* The two building blocks on their own.  qkv: bf16 [S][5120] = 8 x [q | gate] | k | v with q normalised and
+ * rotated; k_cache / v_cache: bf16 [2][max_seq_len][256]; mask: uint32 [8][B][ceil(B/32)], B = ceil(S/128), one bit per
+ * key block (null in mk_attention_prefill = dense); out: bf16 [S][2048] = softmax(q k^T / 16) v * sigmoid(gate);
+ * scratch: mk_block_select_scratch_bytes(S) bytes of device memory. */
+int mk_block_select(const void *qkv, const void *k_cache, int seq_len, int max_seq_len, double top_frac, int window,
+                    int sink, unsigned int *mask_out, void *scratch, cudaStream_t stream);
+size_t mk_block_select_scratch_bytes(int seq_len);
+int mk_attention_prefill(const void *qkv, const void *k_cache, const void *v_cache, void *out, int seq_len,
+                         int max_seq_len, const unsigned int *mask, cudaStream_t stream);
+
 /* The prefill projection GEMM on its own: C[M,N] = A[M,K] . W[N,K]^T (+ residual[M,N]), bf16 row-major,
  * f32 accumulation (tcgen05 / TMEM / TMA).  Replaces the cublasGemmEx call of the reference prefill
  * (reference: megakernel/prefill.cu:1526-1534).  N % 128 == 0, K % 64 == 0, 16-byte aligned pointers. */

@@ -45,11 +45,17 @@ __device__ __forceinline__ void cp16(uint32_t dst, const void* src, int bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
 }
 
+constexpr int MAX_KEY_BLOCKS = 1024;          // block-sparse mode: prompts of up to 131072 tokens
+constexpr int FA_SMEM_SPARSE = FA_SMEM + MAX_KEY_BLOCKS * 4 + 16;   // + list of up to 2048 tile ids + count
+
 // qkv: [S][5120] = 8 x [q(256) | gate(256)] | k(512) | v(512), q already normalised and rotated;
-// kc, vc: [2][max_seq][256]; out: [S][2048]
+// kc, vc: [2][max_seq][256]; out: [S][2048].
+// SPARSE: mask[head][query block of 128][word] holds one bit per key block of 128; a CTA walks the union
+// of the kept key blocks of its four heads and each warp skips the blocks its own head dropped.
+template <bool SPARSE>
 __global__ void __launch_bounds__(256, 1) k_fa_prefill(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ kc,
                                                        const __nv_bfloat16* __restrict__ vc, __nv_bfloat16* __restrict__ out,
-                                                       int S, int max_seq) {
+                                                       int S, int max_seq, const uint32_t* __restrict__ mask, int nblk, int nwords) {
     extern __shared__ __align__(128) unsigned char sm[];
     const int qblk = gridDim.x - 1 - blockIdx.x;          // longest rows first
     const int g = blockIdx.y;
@@ -66,8 +72,35 @@ __global__ void __launch_bounds__(256, 1) k_fa_prefill(const __nv_bfloat16* __re
         cp16(sQ + swz512(row, chunk), src, t < S ? 16 : 0);
     }
     const int last_q = min(q0 + QB, S) - 1;
-    const int ntiles = last_q / KB + 1;
-    auto load_kv = [&](int j, int buf) {
+    int ntiles = last_q / KB + 1;
+    // tile list (sparse): 64-key tiles of the kept 128-key blocks, in ascending order
+    unsigned short* tlist = reinterpret_cast<unsigned short*>(sm + FA_SMEM);
+    const uint32_t* hmask = nullptr;         // mask row of this warp's head
+    if (SPARSE) {
+        const int qb = q0 >> 7;
+        const uint32_t* m0 = mask + ((size_t)(g * FA_GQA) * nblk + qb) * nwords;
+        const size_t hstride = (size_t)nblk * nwords;
+        hmask = m0 + (size_t)(warp >> 1) * hstride;
+        if (tid == 0) {
+            int n = 0;
+            for (int w = 0; w < nwords; ++w) {
+                uint32_t u = m0[w] | m0[w + hstride] | m0[w + 2 * hstride] | m0[w + 3 * hstride];
+                while (u) {
+                    const int b = __ffs(u) - 1;
+                    u &= u - 1;
+                    const int t0 = (w * 32 + b) * 2;
+                    if (t0 * KB <= last_q) tlist[n++] = (unsigned short)t0;
+                    if ((t0 + 1) * KB <= last_q) tlist[n++] = (unsigned short)(t0 + 1);
+                }
+            }
+            *reinterpret_cast<int*>(sm + FA_SMEM + MAX_KEY_BLOCKS * 4) = n;
+        }
+        __syncthreads();
+        ntiles = *reinterpret_cast<const int*>(sm + FA_SMEM + MAX_KEY_BLOCKS * 4);
+    }
+    auto tile_of = [&](int it) { return SPARSE ? (int)tlist[it] : it; };
+    auto load_kv = [&](int it, int buf) {
+        const int j = tile_of(it);
         for (int i = tid; i < KB * 32; i += 256) {
             const int row = i >> 5, chunk = i & 31, key = j * KB + row;
             const int ok = key <= last_q ? 16 : 0;
@@ -90,12 +123,14 @@ __global__ void __launch_bounds__(256, 1) k_fa_prefill(const __nv_bfloat16* __re
     const int brow = (lane & 7) + (lane >> 4) * 8, bchunk = (lane >> 3) & 1;
     const int trow = (lane & 7) + ((lane >> 3) & 1) * 8, tchunk = lane >> 4;
 
-    for (int j = 0; j < ntiles; ++j) {
-        const int buf = j & 1;
-        if (j + 1 < ntiles) load_kv(j + 1, buf ^ 1);
+    for (int it = 0; it < ntiles; ++it) {
+        const int buf = it & 1;
+        const int j = tile_of(it);
+        if (it + 1 < ntiles) load_kv(it + 1, buf ^ 1);
         else asm volatile("cp.async.commit_group;" ::: "memory");
         asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncthreads();
+        if (SPARSE && !((hmask[j >> 6] >> ((j >> 1) & 31)) & 1u)) { __syncthreads(); continue; }   // this head dropped the block
         const uint32_t kb = sK + buf * FA_KV_BYTES, vb = sV + buf * FA_KV_BYTES;
         float s[8][4];
 #pragma unroll
@@ -193,18 +228,105 @@ __global__ void __launch_bounds__(256, 1) k_fa_prefill(const __nv_bfloat16* __re
 
 }  // namespace
 
-cudaError_t fa_prefill(const void* qkv, const void* kc, const void* vc, void* out, int S, int max_seq, cudaStream_t stream) {
+namespace {
+
+// ---- block selection ----------------------------------------------------------------------------------
+// Mean over the (up to) 128 positions of a block, sequentially in f32; slots 0-7 = query heads, 8-9 = key heads.
+__global__ void __launch_bounds__(256) k_bs_pool(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ kc,
+                                                 float* __restrict__ means, int S, int max_seq, int nblk) {
+    const int b = blockIdx.x, slot = blockIdx.y, d = threadIdx.x;
+    const int lo = b * 128, hi = min(S, lo + 128);
+    float acc = 0.f;
+    if (slot < 8) {
+        const __nv_bfloat16* src = qkv + (size_t)lo * FA_QKV_ROWS + slot * 2 * FA_HEAD_DIM + d;
+        for (int p = lo; p < hi; ++p, src += FA_QKV_ROWS) acc = __fadd_rn(acc, bf2f(*src));
+    } else {
+        const __nv_bfloat16* src = kc + ((size_t)(slot - 8) * max_seq + lo) * FA_HEAD_DIM + d;
+        for (int p = lo; p < hi; ++p, src += FA_HEAD_DIM) acc = __fadd_rn(acc, bf2f(*src));
+    }
+    means[((size_t)slot * nblk + b) * FA_HEAD_DIM + d] = __fmul_rn(acc, 1.0f / (float)(hi - lo));
+}
+
+// One CTA per (query block i, head): scores against all causal key blocks, then keep the sink blocks, the
+// local window and the `topk` best by score (ties to the lower index).  Every add and multiply is rounded
+// on its own and in a fixed order, so the scores can be reproduced bit for bit on a CPU.
+__global__ void __launch_bounds__(256) k_bs_select(const float* __restrict__ means, uint32_t* __restrict__ mask, int nblk, int nwords,
+                                                   double top_frac, int window, int sink) {
+    extern __shared__ float sc[];                           // nblk scores, then nwords mask words
+    uint32_t* words = reinterpret_cast<uint32_t*>(sc + nblk);
+    const int i = blockIdx.x, h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = i + 1;
+    const float* qm = means + ((size_t)h * nblk + i) * FA_HEAD_DIM + lane * 8;
+    float q[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = qm[e];
+    for (int j = warp; j < n; j += 8) {
+        const float* km = means + ((size_t)(8 + h / FA_GQA) * nblk + j) * FA_HEAD_DIM + lane * 8;
+        float part = __fmul_rn(q[0], km[0]);
+#pragma unroll
+        for (int e = 1; e < 8; ++e) part = __fadd_rn(part, __fmul_rn(q[e], km[e]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
+        if (lane == 0) sc[j] = part;
+    }
+    for (int w = threadIdx.x; w < nwords; w += 256) words[w] = 0u;
+    __syncthreads();
+    const int topk = (int)ceil(top_frac * (double)n);
+    for (int j = threadIdx.x; j < n; j += 256) {
+        bool keep = j < sink || j > i - window;
+        if (!keep) {
+            const float s = sc[j];
+            int rank = 0;
+            for (int o = 0; o < n; ++o) { const float t = sc[o]; rank += (t > s) || (t == s && o < j); }
+            keep = rank < topk;
+        }
+        if (keep) atomicOr(&words[j >> 5], 1u << (j & 31));
+    }
+    __syncthreads();
+    for (int w = threadIdx.x; w < nwords; w += 256) mask[((size_t)h * nblk + i) * nwords + w] = words[w];
+}
+
+}  // namespace
+
+size_t block_select_scratch_bytes(int S) {
+    const int nblk = (S + 127) / 128, nwords = (nblk + 31) / 32;
+    return (size_t)10 * nblk * FA_HEAD_DIM * 4 + (size_t)8 * nblk * nwords * 4;
+}
+
+cudaError_t block_select(const void* qkv, const void* kc, int S, int max_seq, double top_frac, int window, int sink,
+                         void* scratch, uint32_t** mask_out, cudaStream_t stream) {
+    const int nblk = (S + 127) / 128, nwords = (nblk + 31) / 32;
+    if (nblk > MAX_KEY_BLOCKS) return cudaErrorInvalidValue;
+    float* means = (float*)scratch;
+    uint32_t* mask = (uint32_t*)((char*)scratch + (size_t)10 * nblk * FA_HEAD_DIM * 4);
+    k_bs_pool<<<dim3(nblk, 10), 256, 0, stream>>>((const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc, means, S, max_seq, nblk);
+    k_bs_select<<<dim3(nblk, 8), 256, (nblk + nwords) * 4, stream>>>(means, mask, nblk, nwords, top_frac, window, sink);
+    *mask_out = mask;
+    return cudaGetLastError();
+}
+
+cudaError_t fa_prefill(const void* qkv, const void* kc, const void* vc, void* out, int S, int max_seq, const uint32_t* mask,
+                       cudaStream_t stream) {
     static bool attr[64] = {false};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64 && !attr[dev]) {
-        e = cudaFuncSetAttribute(k_fa_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
+        e = cudaFuncSetAttribute(k_fa_prefill<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_fa_prefill<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM_SPARSE);
         if (e != cudaSuccess) return e;
         attr[dev] = true;
     }
-    k_fa_prefill<<<dim3((S + QB - 1) / QB, FA_KV_HEADS), 256, FA_SMEM, stream>>>(
-        (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, (__nv_bfloat16*)out, S, max_seq);
+    const dim3 grid((S + QB - 1) / QB, FA_KV_HEADS);
+    if (mask) {
+        const int nblk = (S + 127) / 128, nwords = (nblk + 31) / 32;
+        if (nblk > MAX_KEY_BLOCKS) return cudaErrorInvalidValue;
+        k_fa_prefill<true><<<grid, 256, FA_SMEM_SPARSE, stream>>>((const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc,
+                                                                   (const __nv_bfloat16*)vc, (__nv_bfloat16*)out, S, max_seq, mask, nblk, nwords);
+    } else {
+        k_fa_prefill<false><<<grid, 256, FA_SMEM, stream>>>((const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc,
+                                                            (__nv_bfloat16*)out, S, max_seq, nullptr, 0, 0);
+    }
     return cudaGetLastError();
 }
 

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <stddef.h>
+#include <stdint.h>
 
 namespace mk {
 
@@ -22,6 +23,16 @@ cudaError_t dn_chunked(const float* pre, const float* gates, float* state, float
 // Causal GQA attention over a prompt (one layer): qkv bf16 [S][5120] = 8 x [q | gate] | k | v with q normalised
 // and rotated; kc, vc: bf16 [2][max_seq][256] (already holding the prompt's keys / values); out bf16 [S][2048]
 // = softmax(q k^T / 16) v * sigmoid(gate).
-cudaError_t fa_prefill(const void* qkv, const void* kc, const void* vc, void* out, int S, int max_seq, cudaStream_t stream);
+// mask: null = dense; else the block mask written by block_select (one bit per 128-key block, per head and
+// 128-query block).
+cudaError_t fa_prefill(const void* qkv, const void* kc, const void* vc, void* out, int S, int max_seq, const uint32_t* mask,
+                       cudaStream_t stream);
+
+// Block selection for sparse attention over 128 x 128 blocks: keep the first `sink` key blocks, the `window`
+// most recent ones and the ceil(top_frac * causal blocks) best by mean-pooled q . mean-pooled k, per query head.
+// scratch: block_select_scratch_bytes(S); *mask_out points into it: uint32 [8][blocks][ceil(blocks / 32)].
+size_t block_select_scratch_bytes(int S);
+cudaError_t block_select(const void* qkv, const void* kc, int S, int max_seq, double top_frac, int window, int sink,
+                         void* scratch, uint32_t** mask_out, cudaStream_t stream);
 
 }  // namespace mk

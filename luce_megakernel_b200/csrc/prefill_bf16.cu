@@ -387,6 +387,7 @@ struct PrefillWs {
     float *pre = nullptr, *o = nullptr, *beta = nullptr, *decay = nullptr, *kq = nullptr, *normed_f32 = nullptr, *bval = nullptr;
     int *bidx = nullptr, *err = nullptr;
     void* chunk_scratch = nullptr;
+    void* select_scratch = nullptr;
 };
 PrefillWs g_pws[64];
 constexpr int LM_BLOCKS = 1184;     // 8 resident blocks of 256 threads on each of 148 SMs
@@ -394,12 +395,12 @@ constexpr int LM_BLOCKS = 1184;     // 8 resident blocks of 256 threads on each 
 cudaError_t ensure_ws(PrefillWs& w, int S) {
     if (S <= w.cap) return cudaSuccess;
     void** ptrs[] = {(void**)&w.hidden, (void**)&w.normed, (void**)&w.wide, (void**)&w.z, (void**)&w.act, (void**)&w.pre,
-                     (void**)&w.o, (void**)&w.beta, (void**)&w.decay, (void**)&w.kq, &w.chunk_scratch};
+                     (void**)&w.o, (void**)&w.beta, (void**)&w.decay, (void**)&w.kq, &w.chunk_scratch, &w.select_scratch};
     for (void** p : ptrs) { if (*p) cudaFree(*p); *p = nullptr; }
     const size_t s = (size_t)S;
     const size_t sizes[] = {s * HIDDEN * 2, s * HIDDEN * 2, s * 2 * INTER * 2, s * DN_V * 2, s * INTER * 2,
-                            s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 16, 16, 16, dn_chunked_scratch_bytes(S)};
-    for (int i = 0; i < 11; ++i) {
+                            s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 16, 16, 16, dn_chunked_scratch_bytes(S), block_select_scratch_bytes(S)};
+    for (int i = 0; i < 12; ++i) {
         cudaError_t e = cudaMalloc(ptrs[i], sizes[i]);
         if (e != cudaSuccess) { w.cap = 0; return e; }
     }
@@ -422,6 +423,8 @@ cudaError_t ensure_ws(PrefillWs& w, int S) {
 struct HostTable { const void* src = nullptr; int n = 0; LayerWeights rows[MAX_LAYERS]; };
 HostTable g_tables[64];
 thread_local char g_perr[200] = "";
+struct SparseCfg { bool enabled = false; double top_frac = 0.10; int window = 4, sink = 1; };
+SparseCfg g_sparse;
 int g_scan_mode = 1;              // 1 = chunks of 64 on the tensor cores, 0 = token-serial recurrence
 int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
     if (e != cudaSuccess) snprintf(g_perr, sizeof(g_perr), "%s: %s", what, cudaGetErrorString(e));
@@ -440,6 +443,12 @@ int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
 
 extern "C" const char* mk_prefill_error(void) { return mk::g_perr; }
 extern "C" void mk_prefill_forget_tables(void) { for (auto& t : mk::g_tables) { t.src = nullptr; t.n = 0; } }
+extern "C" int mk_prefill_set_block_sparse(int enable, double top_frac, int window, int sink) {
+    if (enable && (!(top_frac >= 0.0 && top_frac <= 1.0) || window < 1 || sink < 0)) return MK_ERR_BAD_ARG;
+    mk::g_sparse.enabled = enable != 0;
+    if (enable) { mk::g_sparse.top_frac = top_frac; mk::g_sparse.window = window; mk::g_sparse.sink = sink; }
+    return MK_OK;
+}
 extern "C" void mk_prefill_set_scan_mode(int chunked) { mk::g_scan_mode = chunked ? 1 : 0; }
 
 extern "C" int mk_prefill_bf16(
@@ -515,7 +524,14 @@ extern "C" int mk_prefill_bf16(
             PF_CHECK(gemm(w.normed, wqkv, w.wide, nullptr, FA_QKV_ROWS, HIDDEN), "gemm fa qkv");
             k_fa_norm_rope<<<blocks_for_warps((long long)S * 12), 256, 0, stream>>>(
                 w.wide, (const bf*)lw.ptrs[FA_Q_NORM], (const bf*)lw.ptrs[FA_K_NORM], kc, vc, S, max_seq_len);
-            PF_CHECK(fa_prefill(w.wide, kc, vc, w.act, S, max_seq_len, stream), "attention");
+            const uint32_t* bmask = nullptr;
+            if (g_sparse.enabled) {
+                uint32_t* m = nullptr;
+                PF_CHECK(block_select(w.wide, kc, S, max_seq_len, g_sparse.top_frac, g_sparse.window, g_sparse.sink,
+                                      w.select_scratch, &m, stream), "block selection");
+                bmask = m;
+            }
+            PF_CHECK(fa_prefill(w.wide, kc, vc, w.act, S, max_seq_len, bmask, stream), "attention");
             PF_CHECK(gemm(w.act, lw.ptrs[FA_W_O], w.hidden, w.hidden, HIDDEN, FA_Q_SIZE), "gemm o");
             ++fa_idx;
         }
@@ -558,4 +574,25 @@ extern "C" int launch_prefill_bf16(
     return mk_prefill_bf16(token_ids, seq_len, output_token, embed_weight, layers, final_norm_w, lm_head_w, fa_k_cache,
                            fa_v_cache, dn_states, conv_bufs, fused_fa_qkv_base, fused_gate_up_base, final_normed,
                            hidden_bf16_out, max_seq_len, nl, vocab, stream);
+}
+
+// The attention building blocks on their own (tests call these through the C ABI).
+extern "C" int mk_block_select(const void* qkv, const void* k_cache, int seq_len, int max_seq_len, double top_frac, int window,
+                               int sink, unsigned int* mask_out, void* scratch, cudaStream_t stream) {
+    using namespace mk;
+    if (!qkv || !k_cache || !mask_out || !scratch || seq_len < 1 || seq_len > max_seq_len || window < 1 || sink < 0)
+        return pfail(MK_ERR_BAD_ARG, "bad argument");
+    uint32_t* m = nullptr;
+    PF_CHECK(block_select(qkv, k_cache, seq_len, max_seq_len, top_frac, window, sink, scratch, &m, stream), "block selection");
+    const int nblk = (seq_len + 127) / 128, nwords = (nblk + 31) / 32;
+    PF_CHECK(cudaMemcpyAsync(mask_out, m, (size_t)8 * nblk * nwords * 4, cudaMemcpyDeviceToDevice, stream), "mask copy");
+    return MK_OK;
+}
+extern "C" size_t mk_block_select_scratch_bytes(int seq_len) { return mk::block_select_scratch_bytes(seq_len); }
+extern "C" int mk_attention_prefill(const void* qkv, const void* k_cache, const void* v_cache, void* out, int seq_len, int max_seq_len,
+                                    const unsigned int* mask, cudaStream_t stream) {
+    using namespace mk;
+    if (!qkv || !k_cache || !v_cache || !out || seq_len < 1 || seq_len > max_seq_len) return pfail(MK_ERR_BAD_ARG, "bad argument");
+    PF_CHECK(fa_prefill(qkv, k_cache, v_cache, out, seq_len, max_seq_len, mask, stream), "attention");
+    return MK_OK;
 }

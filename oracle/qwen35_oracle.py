@@ -211,7 +211,8 @@ def _rms(x: torch.Tensor, w1p: torch.Tensor) -> torch.Tensor:
 class Oracle:
     """fp32 restatement of the reference decode arithmetic, usable for T>=1 consecutive tokens."""
 
-    def __init__(self, weights: Dict[str, torch.Tensor], rounding: str = "decode", ref_q_rope_in_place: bool = False):
+    def __init__(self, weights: Dict[str, torch.Tensor], rounding: str = "decode", ref_q_rope_in_place: bool = False,
+                 block_sparse: Optional[dict] = None):
         """ref_q_rope_in_place reproduces what the reference decode kernel actually computes for the
         query's rotary dims 32..63: it rotates q in place (kernel.cu:487-497), so by the time a lane
         reaches dim i+32 its partner dim i already holds the rotated value, which is then normalised
@@ -222,6 +223,9 @@ class Oracle:
         assert rounding in ("decode", "none")
         self.rounding = rounding
         self.ref_q_rope_in_place = ref_q_rope_in_place
+        # block_sparse = {"top_frac": .., "window": .., "sink": ..}: prompts processed from position 0 attend
+        # only to the key blocks oracle/block_sparse.py selects (bf16-rounded q and k feed the selection)
+        self.block_sparse = block_sparse
         self.w = {k: v.to(torch.float32) for k, v in weights.items()}
         self.num_layers = 1 + max(int(k.split(".")[2]) for k in weights if k.startswith("model.layers."))
         self.types = layer_types(self.num_layers)
@@ -305,6 +309,11 @@ class Oracle:
         s = torch.einsum("thd,hld->htl", q, K) / math.sqrt(FA_HEAD_DIM)                  # kernel.cu:509,528-529
         causal = torch.arange(L)[None, :] <= (pos0 + torch.arange(T))[:, None]
         s = s.masked_fill(~causal[None], float("-inf"))
+        if self.block_sparse is not None and pos0 == 0 and T > 1:
+            from . import block_sparse as BS
+            keep = BS.select_for_heads(_bf(q).permute(1, 0, 2).numpy(), st.k_cache[idx, :, :L].numpy(), **self.block_sparse)
+            for hh in range(FA_Q_HEADS):
+                s[hh] = s[hh].masked_fill(~torch.from_numpy(BS.token_mask(keep[hh], L)), float("-inf"))
         o = torch.einsum("htl,hld->thd", torch.softmax(s, dim=-1), V)
         o = o * torch.sigmoid(gate)                                                      # kernel.cu:551-556
         return o.reshape(T, FA_Q_SIZE)
