@@ -34,11 +34,20 @@ def algorithmic_bytes_per_token(context_len: float) -> float:
     return WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POS * context_len
 
 
-def prefill_tflop(S: int) -> float:
-    """Algorithmic FLOPs of a dense prefill of S tokens, in TFLOP: all per-token linear layers, causal
-    attention (6 layers, 8 heads, head_dim 256), the gated delta rule in its recurrent-form count, one LM-head pass."""
+def kept_block_fraction(S: int, top_frac=0.10, window=4, sink=1) -> float:
+    """Upper bound on the fraction of causal 128 x 128 blocks the sparse rule keeps (overlaps not subtracted)."""
+    import math
+    nb = (S + 127) // 128
+    kept = sum(min(i + 1, sink + window + math.ceil(top_frac * (i + 1))) for i in range(nb))
+    return kept / (nb * (nb + 1) / 2.0)
+
+
+def prefill_tflop(S: int, sparse: bool = False) -> float:
+    """Algorithmic FLOPs of a prefill of S tokens, in TFLOP: all per-token linear layers, causal attention
+    (6 layers, 8 heads, head_dim 256; only the kept blocks when sparse), the gated delta rule in its
+    recurrent-form count, one LM-head pass."""
     gemm = 2.0 * 497_614_848 * S
-    attn = 6 * 8 * (4 * 256) * S * (S + 1) / 2.0
+    attn = 6 * 8 * (4 * 256) * S * (S + 1) / 2.0 * (kept_block_fraction(S) if sparse else 1.0)
     scan = 18 * 16 * (6 * 128 * 128) * S
     return (gemm + attn + scan + 2.0 * 254_279_680) / 1e12
 
@@ -262,18 +271,24 @@ def main():
     # dense prefill at 8192 and 32768 tokens, single GPU only: 1 warm-up + 2 timed calls
     long_pp = []
     if world == 1 and not args.no_long_prefill:
-        for S_ in (8192, 32768):
+        import ctypes
+        for S_, sparse in ((8192, False), (32768, False), (65536, True)):
             d2 = M.Decoder(weights=weights, max_seq_len=S_ + 8, api="cabi")
             ids = torch.randint(0, M.VOCAB_SIZE, (S_,), generator=g).to(torch.int32).cuda()
-            d2.prefill(ids)
-            torch.cuda.synchronize()
-            p0.record()
-            for _ in range(2):
-                d2._position = 0
-                d2.prefill_async(ids)
-            p1.record()
-            torch.cuda.synchronize()
-            long_pp.append((S_, p0.elapsed_time(p1) / 2))
+            # 128 x 128 blocks, sink block 0, 4-block window, top 10 % by pooled q.k
+            lib().mk_prefill_set_block_sparse(1 if sparse else 0, ctypes.c_double(0.10), 4, 1)
+            try:
+                d2.prefill(ids)
+                torch.cuda.synchronize()
+                p0.record()
+                for _ in range(2):
+                    d2._position = 0
+                    d2.prefill_async(ids)
+                p1.record()
+                torch.cuda.synchronize()
+            finally:
+                lib().mk_prefill_set_block_sparse(0, ctypes.c_double(0.10), 4, 1)
+            long_pp.append((S_, p0.elapsed_time(p1) / 2, sparse))
             del d2
         if lib().mk_device_status() != 0:
             raise SystemExit("device-side wait timed out during the long prefill")
@@ -312,8 +327,11 @@ def main():
         }
         if world == 1 and long_pp:
             out["prefill_long"] = [
-                {"prompt_len": S_, "ms": ms_, "tok_s": S_ / (ms_ * 1e-3), "tflops_algorithmic": prefill_tflop(S_) / (ms_ * 1e-3),
-                 "frac_of_bf16_peak": prefill_tflop(S_) / (ms_ * 1e-3) / measured_bf16_peak()} for S_, ms_ in long_pp]
+                {"prompt_len": S_, "attention": "block-sparse 128x128: sink 1 + window 4 + top 10%" if sp_ else "dense causal",
+                 "ms": ms_, "tok_s": S_ / (ms_ * 1e-3),
+                 "tflops_algorithmic": prefill_tflop(S_, sp_) / (ms_ * 1e-3),
+                 "frac_of_bf16_peak": prefill_tflop(S_, sp_) / (ms_ * 1e-3) / measured_bf16_peak(),
+                 "tflops_dense_equivalent": prefill_tflop(S_) / (ms_ * 1e-3)} for S_, ms_, sp_ in long_pp]
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
             sd = {k: v for k, v in cpu_state_dict(weights).items()}
