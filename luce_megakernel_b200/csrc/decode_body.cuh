@@ -39,7 +39,21 @@ __device__ __forceinline__ void split_rows(int n, int G, int c, int& a, int& b) 
     b = (int)(((unsigned)n * (unsigned)(c + 1)) / (unsigned)G);
 }
 
-__device__ __forceinline__ Geo phase_geo(int type, int cta, int G, int vocab) {
+// attention units: (KV head, chunk of positions); a unit's K and V rows travel through the ring in tiles of
+// 64 positions, four ring chunks per tile: K rows 0-31, K rows 32-63, V rows 0-31, V rows 32-63, each row
+// at a stride of ATT_ROW_STRIDE bytes so that the 8 rows an ldmatrix reads fall in different banks
+constexpr int ATT_ROW_STRIDE = FA_HEAD_DIM * 2 + 16;
+__device__ __forceinline__ int att_num_chunks(int L) {
+    int nc = (L + ATT_CHUNK_POS - 1) / ATT_CHUNK_POS;
+    return nc < 1 ? 1 : (nc > ATT_MAX_CHUNKS ? ATT_MAX_CHUNKS : nc);
+}
+__device__ __forceinline__ void att_unit_range(int L, int u, int& g, int& ch, int& p_lo, int& p_hi) {
+    const int NC = att_num_chunks(L), per = (L + NC - 1) / NC;
+    g = u / NC; ch = u % NC;
+    p_lo = ch * per; p_hi = min(L, p_lo + per);
+}
+
+__device__ __forceinline__ Geo phase_geo(int type, int cta, int G, int vocab, int pos = 0) {
     Geo g;
     g.r0 = g.r1 = 0;
     g.nchunks = 0;
@@ -52,6 +66,16 @@ __device__ __forceinline__ Geo phase_geo(int type, int cta, int G, int vocab) {
         case T_DOWN:   split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = (g.r1 - g.r0 + 3) >> 2; break;
         case T_LM:     split_rows(vocab, G, cta, g.r0, g.r1);       g.nchunks = (g.r1 - g.r0 + LM_RPC - 1) / LM_RPC; break;
         case T_DN_REC: g.r0 = cta; g.nchunks = (cta < 128) ? (128 - cta + G - 1) / G : 0; break;
+        case T_FA_ATT: {
+            const int L = pos + 1;
+            if (cta < FA_KV_HEADS * att_num_chunks(L)) {      // at most one unit per CTA (grids hold >= 129 CTAs)
+                int gg, ch, lo, hi;
+                att_unit_range(L, cta, gg, ch, lo, hi);
+                g.r0 = lo; g.r1 = hi;
+                g.nchunks = 4 * ((hi - lo + 63) >> 6);
+            }
+            break;
+        }
         default: break;
     }
     return g;
@@ -61,7 +85,19 @@ __device__ __forceinline__ Geo phase_geo(int type, int cta, int G, int vocab) {
 // ring offset.  bf16: lane = row slot.  NVFP4: lanes 0-15 = packed rows, lanes 16-31 = their scales.
 __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const DecodeParams& P,
                                                    const Geo& g, int q, int lane, int G, int dn_idx,
-                                                   const char*& src, uint32_t& dst_off) {
+                                                   const char*& src, uint32_t& dst_off, int cta_of_geo) {
+    if (type == T_FA_ATT) {
+        // dn_idx carries the attention layer index here; chunk q = tile * 4 + {K lo, K hi, V lo, V hi}
+        const int u = cta_of_geo;
+        const int NC = att_num_chunks(P.position + 1);
+        const int kvh = u / NC, part = q & 3;
+        const int p = g.r0 + (q >> 2) * 64 + (part & 1) * 32 + lane;
+        if (p >= g.r1) return 0;
+        const char* base = (const char*)((part & 2) ? P.v_cache : P.k_cache);
+        src = base + ((size_t)(dn_idx * FA_KV_HEADS + kvh) * P.max_seq_len + p) * (FA_HEAD_DIM * 2);
+        dst_off = lane * ATT_ROW_STRIDE;
+        return FA_HEAD_DIM * 2;
+    }
 #if MK_WFMT == 0
     const int slot = lane, kind = 0;
 #else
@@ -299,7 +335,7 @@ __device__ __forceinline__ void poll2_batch(const DecodeParams& P, Ctx& c, const
 
 __device__ __forceinline__ void producer_phase(const DecodeParams& P, Ctx& c, int type, const LW& lw, int dn_idx,
                                uint64_t pol_stream, uint64_t pol_keep) {
-    const Geo g = phase_geo(type, c.cta, c.G, P.vocab);
+    const Geo g = phase_geo(type, c.cta, c.G, P.vocab, P.position);
 #pragma unroll 1
     for (int q = 0; q < g.nchunks; ++q, ++c.it) {
         if (c.misc[MISC_ABORT]) continue;
@@ -308,7 +344,7 @@ __device__ __forceinline__ void producer_phase(const DecodeParams& P, Ctx& c, in
         __syncwarp();
         const char* src = nullptr;
         uint32_t dst_off = 0;
-        uint32_t bytes = chunk_slot_src(type, lw, P, g, q, c.lane, c.G, dn_idx, src, dst_off);
+        uint32_t bytes = chunk_slot_src(type, lw, P, g, q, c.lane, c.G, dn_idx, src, dst_off, c.cta);
         if (bytes && (((uintptr_t)src) & 15u)) { fail(P, c, ST_MISALIGNED); bytes = 0; }
         const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
         if (c.misc[MISC_ABORT]) continue;
@@ -329,7 +365,7 @@ __device__ __forceinline__ void producer_phase(const DecodeParams& P, Ctx& c, in
         __syncwarp();
         if (head)
             bulk_g2s(c.ring0 + stage * STAGE_BYTES + dst_off, src, bytes * (uint32_t)(end - c.lane), c.full0 + stage * 8,
-                     type == T_DN_REC ? pol_keep : pol_stream);
+                     (type == T_DN_REC || type == T_FA_ATT) ? pol_keep : pol_stream);
     }
 }
 
@@ -819,11 +855,6 @@ __device__ __forceinline__ void phase_fa_in(const DecodeParams& P, Ctx& c, const
     trace_point(P, c);
 }
 
-__device__ __forceinline__ int att_num_chunks(int L) {
-    int nc = (L + ATT_CHUNK_POS - 1) / ATT_CHUNK_POS;
-    return nc < 1 ? 1 : (nc > ATT_MAX_CHUNKS ? ATT_MAX_CHUNKS : nc);
-}
-
 __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
     f[0] = bf_lo(u.x); f[1] = bf_hi(u.x); f[2] = bf_lo(u.y); f[3] = bf_hi(u.y);
     f[4] = bf_lo(u.z); f[5] = bf_hi(u.z); f[6] = bf_lo(u.w); f[7] = bf_hi(u.w);
@@ -854,163 +885,211 @@ __device__ __forceinline__ void head_norm_rope(const DecodeParams& P, Ctx& c, co
     n[1] = b * cs + a * sn;
 }
 
-// Split-KV decode attention.  Unit = (KV head, position chunk); the 4 query heads of a KV head
-// share every K/V load.  Each unit leaves (m, l, o[256]) per head in the workspace and then
-// publishes its ready word; the o-proj phase merges the chunks.  reference: megakernel/kernel.cu:506-560
+// Split-KV decode attention.  Unit = (KV head, chunk of positions), one unit per CTA at most.  The unit's
+// K and V rows arrive through the weight ring (issued by the producer warp long before the query exists),
+// the row of the current position is patched in shared memory by the unit that owns it (and appended to the
+// cache).  The 4 query heads of the KV head are rows of one MMA tile: rows 0-3 carry the bf16 head of each
+// (scaled) query, rows 4-7 the bf16 remainder, so q . k keeps ~16 mantissa bits; the softmax weights take the
+// same two-row form into P . V.  Warps 0-3 each compute all scores and 64 of the 256 output dims; there is no
+// cross-warp merge.  Each unit leaves (m, l, o[256]) per head in the workspace and publishes its ready word;
+// the o-proj phase merges the chunks.  reference: megakernel/kernel.cu:506-560
+__device__ __forceinline__ void att_mma(float (&c4)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c4[0]), "+f"(c4[1]), "+f"(c4[2]), "+f"(c4[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void att_ldsm4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void att_ldsm4t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+// x as a pair (bf16 head, bf16 remainder); `lo_part` selects which one this lane carries
+__device__ __forceinline__ uint32_t att_pack(float x, float y, bool lo_part) {
+    const __nv_bfloat16 xh = __float2bfloat16_rn(x), yh = __float2bfloat16_rn(y);
+    __nv_bfloat162 r = lo_part ? __floats2bfloat162_rn(x - __bfloat162float(xh), y - __bfloat162float(yh))
+                               : __halves2bfloat162(xh, yh);
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+
 __device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, const LW& lw, int layer, int fa_idx) {
     const int pos = P.position, L = pos + 1;
-    const int NC = att_num_chunks(L);
-    const int per = (L + NC - 1) / NC;
     const uint32_t ep = epoch_of(c, layer);
-    float* slots = c.xs;                 // 4 slots x 4 heads x 260 floats
-    float* qs = c.xs + 4160;             // 4 heads x 256 floats
+    const Geo geo = phase_geo(T_FA_ATT, c.cta, c.G, P.vocab, pos);
+    // scratch: query tile [8 rows][264] bf16 (rows 0-3 heads, 4-7 remainders), probability tile [8][72] bf16,
+    // the current position's key / value row, per-warp row maxima and sums
+    constexpr int QROW = FA_HEAD_DIM + 8, PROW = 64 + 8;
+    __nv_bfloat16* qt = reinterpret_cast<__nv_bfloat16*>(c.xs);
+    __nv_bfloat16* pt = qt + 8 * QROW;
+    __nv_bfloat16* krow = pt + 8 * PROW;
+    __nv_bfloat16* vrow = krow + FA_HEAD_DIM;
+    float* smax = reinterpret_cast<float*>(vrow + FA_HEAD_DIM);      // [4 warps][4 heads]
+    float* ssum = smax + 16;
     trace_point(P, c);
-    trace_point(P, c);
-#pragma unroll 1
-    for (int u = c.cta; u < FA_KV_HEADS * NC; u += c.G) {
-        const int g = u / NC, ch = u % NC;
-        const int p_lo = ch * per, p_hi = min(L, p_lo + per);
+    if (geo.nchunks == 0) { trace_point(P, c); trace_point(P, c); }
+    if (geo.nchunks > 0) {
+        const int u = c.cta;
+        int g, ch, p_lo, p_hi;
+        att_unit_range(L, u, g, ch, p_lo, p_hi);
         const bool owner = (pos >= p_lo && pos < p_hi);
-        __nv_bfloat16* Kb = reinterpret_cast<__nv_bfloat16*>(P.k_cache) + (size_t)(fa_idx * FA_KV_HEADS + g) * P.max_seq_len * FA_HEAD_DIM;
-        __nv_bfloat16* Vb = reinterpret_cast<__nv_bfloat16*>(P.v_cache) + (size_t)(fa_idx * FA_KV_HEADS + g) * P.max_seq_len * FA_HEAD_DIM;
         if (c.warp < 4) {
             float n[8];
             head_norm_rope(P, c, P.ws->x_fain + (g * FA_GQA + c.warp) * 2 * FA_HEAD_DIM, ep, lw.ptrs[FA_Q_NORM], pos, n);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) qs[c.warp * FA_HEAD_DIM + c.lane + 32 * e] = n[e];
+            for (int e = 0; e < 8; ++e) {
+                const float x = n[e] * 0.0625f;                       // 1 / sqrt(head_dim), exact
+                const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+                qt[c.warp * QROW + c.lane + 32 * e] = hi;
+                qt[(c.warp + 4) * QROW + c.lane + 32 * e] = __float2bfloat16_rn(x - __bfloat162float(hi));
+            }
         } else if (c.warp == 4 && owner) {
             float n[8];
             head_norm_rope(P, c, P.ws->x_fain + FA_QPROJ + g * FA_HEAD_DIM, ep, lw.ptrs[FA_K_NORM], pos, n);
+            __nv_bfloat16* Kb = reinterpret_cast<__nv_bfloat16*>(P.k_cache) + ((size_t)(fa_idx * FA_KV_HEADS + g) * P.max_seq_len + pos) * FA_HEAD_DIM;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) Kb[(size_t)pos * FA_HEAD_DIM + c.lane + 32 * e] = __float2bfloat16_rn(n[e]);
+            for (int e = 0; e < 8; ++e) {
+                const __nv_bfloat16 v = __float2bfloat16_rn(n[e]);
+                Kb[c.lane + 32 * e] = v;
+                krow[c.lane + 32 * e] = v;
+            }
         } else if (c.warp == 5 && owner) {
             const unsigned long long* b0 = P.ws->x_fain + FA_QPROJ + FA_KV_SIZE + g * FA_HEAD_DIM + c.lane;
             const unsigned long long* const p1[8] = {b0, b0 + 32, b0 + 64, b0 + 96, b0 + 128, b0 + 160, b0 + 192, b0 + 224};
             float v[8];
             poll1_batch<8>(P, c, p1, ep, v);
+            __nv_bfloat16* Vb = reinterpret_cast<__nv_bfloat16*>(P.v_cache) + ((size_t)(fa_idx * FA_KV_HEADS + g) * P.max_seq_len + pos) * FA_HEAD_DIM;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) Vb[(size_t)pos * FA_HEAD_DIM + c.lane + 32 * e] = __float2bfloat16_rn(v[e]);
+            for (int e = 0; e < 8; ++e) {
+                const __nv_bfloat16 b = __float2bfloat16_rn(v[e]);
+                Vb[c.lane + 32 * e] = b;
+                vrow[c.lane + 32 * e] = b;
+            }
         }
-        __threadfence_block();
         named_bar_sync(1, NCT);
+        trace_point(P, c);                 // query / key / value of this position ready
 
-        float qr[4][8], acc[4][8], m[4], l[4];
+        const int g8 = c.lane >> 2, t4 = c.lane & 3;
+        const bool lo_part = g8 >= 4;
+        float oacc[4][4];                  // warps 0-7: output dims [32 warp, 32 warp + 32)
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-            m[h] = -1e30f; l[h] = 0.f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) { qr[h][e] = qs[h * FA_HEAD_DIM + c.lane * 8 + e] * 0.0625f; acc[h][e] = 0.f; }
-        }
-        int p = p_lo + c.warp;
-        uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-        if (p < p_hi) {
-            kk = __ldcg(reinterpret_cast<const uint4*>(Kb + (size_t)p * FA_HEAD_DIM) + c.lane);
-            vv = __ldcg(reinterpret_cast<const uint4*>(Vb + (size_t)p * FA_HEAD_DIM) + c.lane);
-        }
+        for (int n = 0; n < 4; ++n) { oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.f; }
+        float mrun = -1e30f, lrun = 0.f;
+        const int ntile = geo.nchunks >> 2;
 #pragma unroll 1
-        while (p < p_hi) {
-            const int pn = p + NCW;
-            uint4 kn = make_uint4(0, 0, 0, 0), vn = make_uint4(0, 0, 0, 0);
-            if (pn < p_hi) {
-                kn = __ldcg(reinterpret_cast<const uint4*>(Kb + (size_t)pn * FA_HEAD_DIM) + c.lane);
-                vn = __ldcg(reinterpret_cast<const uint4*>(Vb + (size_t)pn * FA_HEAD_DIM) + c.lane);
+        for (int tile = 0; tile < ntile; ++tile) {
+            uint32_t stg[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t itk = c.it + k;
+                wait_full(P, c, itk % NSTAGE, (itk / NSTAGE) & 1u);
+                stg[k] = smem_u32(c.smem + OFF_RING + (itk % NSTAGE) * STAGE_BYTES);
             }
-            float kf[8], vf[8], s[4];
-            unpack8(kk, kf);
-            unpack8(vv, vf);
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                float d = 0.f;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) d = fmaf(qr[h][e], kf[e], d);
-                s[h] = d;
+            const int tbase = p_lo + tile * 64, nvalid = min(64, p_hi - tbase);
+            // patch the row of the current position, zero the value rows past the end of the chunk
+            if (owner && pos >= tbase && pos < tbase + 64 && c.warp >= 4 && c.warp < 6) {
+                const int r = pos - tbase;
+                char* dst = c.smem + OFF_RING + ((c.it + (c.warp == 4 ? 0 : 2) + (r >> 5)) % NSTAGE) * STAGE_BYTES + (r & 31) * ATT_ROW_STRIDE;
+                const uint4* srcv = reinterpret_cast<const uint4*>(c.warp == 4 ? krow : vrow);
+                reinterpret_cast<uint4*>(dst)[c.lane] = srcv[c.lane];
+                fence_proxy_async();      // the stage is refilled by bulk copies later
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-                for (int h = 0; h < 4; ++h) s[h] += __shfl_xor_sync(0xffffffffu, s[h], o);
-            }
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                const float mn = fmaxf(m[h], s[h]);
-                const float corr = __expf(m[h] - mn), pe = __expf(s[h] - mn);
-                l[h] = l[h] * corr + pe;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) acc[h][e] = acc[h][e] * corr + pe * vf[e];
-                m[h] = mn;
-            }
-            kk = kn; vv = vn; p = pn;
-        }
-
-        // merge the 16 warps' partial softmax states: three rounds into warps 0-3, then per head
-#pragma unroll 1
-        for (int r = 1; r <= 3; ++r) {
-            if (c.warp >= 4 * r && c.warp < 4 * r + 4) {
-                const int sl = c.warp - 4 * r;
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    float* d = slots + (sl * 4 + h) * ATT_PART_STRIDE;
-                    if (c.lane == 0) { d[0] = m[h]; d[1] = l[h]; }
-                    *reinterpret_cast<float4*>(d + 4 + c.lane * 8) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-                    *reinterpret_cast<float4*>(d + 8 + c.lane * 8) = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+            if (nvalid < 64 && c.warp >= 6) {
+                for (int r = nvalid + (c.warp - 6); r < 64; r += NCW - 6) {
+                    char* dst = c.smem + OFF_RING + ((c.it + 2 + (r >> 5)) % NSTAGE) * STAGE_BYTES + (r & 31) * ATT_ROW_STRIDE;
+                    reinterpret_cast<uint4*>(dst)[c.lane] = make_uint4(0, 0, 0, 0);
                 }
+                fence_proxy_async();
             }
             named_bar_sync(1, NCT);
+            if (tile == 0) trace_point(P, c);      // first K/V tile landed and patched
+            float sc[2][2];
             if (c.warp < 4) {
+                // scores of keys [16 warp, 16 warp + 16): rows = (head, part)
+                float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                const int brow = (c.lane & 7) + (c.lane >> 4) * 8, bcol = ((c.lane >> 3) & 1) * 16;
+                const uint32_t kb = stg[c.warp >> 1] + ((c.warp & 1) * 16 + brow) * ATT_ROW_STRIDE + bcol;
+                const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qt + g8 * QROW) + t4;
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    const float* d = slots + (c.warp * 4 + h) * ATT_PART_STRIDE;
-                    const float m2 = d[0], l2 = d[1];
-                    const float4 a = *reinterpret_cast<const float4*>(d + 4 + c.lane * 8);
-                    const float4 b = *reinterpret_cast<const float4*>(d + 8 + c.lane * 8);
-                    const float mn = fmaxf(m[h], m2);
-                    const float f1 = __expf(m[h] - mn), f2 = __expf(m2 - mn);
-                    l[h] = l[h] * f1 + l2 * f2;
-                    acc[h][0] = acc[h][0] * f1 + a.x * f2; acc[h][1] = acc[h][1] * f1 + a.y * f2;
-                    acc[h][2] = acc[h][2] * f1 + a.z * f2; acc[h][3] = acc[h][3] * f1 + a.w * f2;
-                    acc[h][4] = acc[h][4] * f1 + b.x * f2; acc[h][5] = acc[h][5] * f1 + b.y * f2;
-                    acc[h][6] = acc[h][6] * f1 + b.z * f2; acc[h][7] = acc[h][7] * f1 + b.w * f2;
-                    m[h] = mn;
+                for (int ks = 0; ks < 16; ++ks) {
+                    uint32_t b0, b1, b2, b3;
+                    att_ldsm4(kb + ks * 32, b0, b1, b2, b3);
+                    const uint32_t a0 = qrow[ks * 8], a2 = qrow[ks * 8 + 4];
+                    att_mma(acc[0], a0, a2, b0, b1);
+                    att_mma(acc[1], a0, a2, b2, b3);
+                }
+                float tmax = -1e30f;
+#pragma unroll
+                for (int n = 0; n < 2; ++n) {
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        float v = acc[n][e] + __shfl_xor_sync(0xffffffffu, acc[n][e], 16);   // head + remainder rows
+                        if (c.warp * 16 + n * 8 + 2 * t4 + e >= nvalid) v = -1e30f;
+                        sc[n][e] = v;
+                        tmax = fmaxf(tmax, v);
+                    }
+                }
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+                if (!lo_part && t4 == 0) smax[c.warp * 4 + g8] = tmax;
+                named_bar_sync(2, 128);
+                const int h = g8 & 3;
+                const float mn = fmaxf(fmaxf(fmaxf(smax[h], smax[4 + h]), fmaxf(smax[8 + h], smax[12 + h])), mrun);
+                float rs = 0.f;
+#pragma unroll
+                for (int n = 0; n < 2; ++n) {
+                    const float p0 = __expf(sc[n][0] - mn), p1 = __expf(sc[n][1] - mn);
+                    rs += p0 + p1;
+                    *reinterpret_cast<uint32_t*>(pt + g8 * PROW + c.warp * 16 + n * 8 + 2 * t4) = att_pack(p0, p1, lo_part);
+                }
+                rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+                rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+                if (!lo_part && t4 == 0) ssum[c.warp * 4 + g8] = rs;
+            }
+            if (c.warp < 8) {
+                named_bar_sync(3, 256);
+                const int h = g8 & 3;
+                const float mn = fmaxf(fmaxf(fmaxf(smax[h], smax[4 + h]), fmaxf(smax[8 + h], smax[12 + h])), mrun);
+                const float corr = __expf(mrun - mn);
+                lrun = lrun * corr + (ssum[h] + ssum[4 + h]) + (ssum[8 + h] + ssum[12 + h]);
+                mrun = mn;
+#pragma unroll
+                for (int n = 0; n < 4; ++n) { oacc[n][0] *= corr; oacc[n][1] *= corr; }
+                const int trow = (c.lane & 7) + ((c.lane >> 3) & 1) * 8, tcol = (c.lane >> 4) * 16;
+                const uint32_t* prow = reinterpret_cast<const uint32_t*>(pt + g8 * PROW) + t4;
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint32_t a0 = prow[ks * 8], a2 = prow[ks * 8 + 4];
+#pragma unroll
+                    for (int np = 0; np < 2; ++np) {
+                        uint32_t b0, b1, b2, b3;
+                        att_ldsm4t(stg[2 + (ks >> 1)] + ((ks & 1) * 16 + trow) * ATT_ROW_STRIDE + (c.warp * 32 + np * 16) * 2 + tcol, b0, b1, b2, b3);
+                        att_mma(oacc[2 * np], a0, a2, b0, b1);
+                        att_mma(oacc[2 * np + 1], a0, a2, b2, b3);
+                    }
                 }
             }
             named_bar_sync(1, NCT);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) release_stage(c, (c.it + k) % NSTAGE);
+            c.it += 4;
         }
-        if (c.warp < 4) {
+        if (c.warp < 8) {
+            float* dst = P.ws->attn_part + ((size_t)(g * FA_GQA + (g8 & 3)) * ATT_MAX_CHUNKS + ch) * ATT_PART_STRIDE;
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                float* d = slots + (c.warp * 4 + h) * ATT_PART_STRIDE;
-                if (c.lane == 0) { d[0] = m[h]; d[1] = l[h]; }
-                *reinterpret_cast<float4*>(d + 4 + c.lane * 8) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-                *reinterpret_cast<float4*>(d + 8 + c.lane * 8) = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+            for (int n = 0; n < 4; ++n) {
+                const float o0 = oacc[n][0] + __shfl_xor_sync(0xffffffffu, oacc[n][0], 16);
+                const float o1 = oacc[n][1] + __shfl_xor_sync(0xffffffffu, oacc[n][1], 16);
+                if (!lo_part) *reinterpret_cast<float2*>(dst + 4 + c.warp * 32 + n * 8 + 2 * t4) = make_float2(o0, o1);
             }
-        }
-        named_bar_sync(1, NCT);
-        if (c.warp < 4) {
-            const int h = c.warp;
-            float M = -1e30f;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) M = fmaxf(M, slots[(s * 4 + h) * ATT_PART_STRIDE]);
-            float lt = 0.f, o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const float* d = slots + (s * 4 + h) * ATT_PART_STRIDE;
-                const float f = __expf(d[0] - M);
-                lt += d[1] * f;
-                const float4 a = *reinterpret_cast<const float4*>(d + 4 + c.lane * 8);
-                const float4 b = *reinterpret_cast<const float4*>(d + 8 + c.lane * 8);
-                o[0] += a.x * f; o[1] += a.y * f; o[2] += a.z * f; o[3] += a.w * f;
-                o[4] += b.x * f; o[5] += b.y * f; o[6] += b.z * f; o[7] += b.w * f;
-            }
-            float* dst = P.ws->attn_part + ((size_t)(g * FA_GQA + h) * ATT_MAX_CHUNKS + ch) * ATT_PART_STRIDE;
-            if (c.lane == 0) { dst[0] = M; dst[1] = lt; }
-            *reinterpret_cast<float4*>(dst + 4 + c.lane * 8) = make_float4(o[0], o[1], o[2], o[3]);
-            *reinterpret_cast<float4*>(dst + 8 + c.lane * 8) = make_float4(o[4], o[5], o[6], o[7]);
+            if (c.warp == 0 && !lo_part && t4 == 0) { dst[0] = mrun; dst[1] = lrun; }
         }
         named_bar_sync(1, NCT);
         if (c.tid == 0)       // the partials of this unit are complete: publish (release orders the CTA's stores)
             asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(P.ws->att_ready + u), "r"(ep) : "memory");
     }
-    trace_point(P, c);
     trace_point(P, c);
 }
 
@@ -1337,21 +1416,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
         const uint64_t pol_stream = l2_policy_evict_first();
         const uint64_t pol_keep = l2_policy_evict_last();
         // one copy of the issue code: the phase type is a run-time value here
-        int dn_idx = 0;
+        int dn_idx = 0, fa_idx = 0;
         for (int layer = 0; layer <= P.num_layers; ++layer) {
             const bool lm = (layer == P.num_layers);
             const LW& lw = s_layers[lm ? 0 : layer];
             const bool dn = (lw.layer_type == 0);
-            const int nph = lm ? 1 : (dn ? 5 : 4);
+            const int nph = 5 - (lm ? 4 : 0);
 #pragma unroll 1
             for (int ph = 0; ph < nph; ++ph) {
                 int type;
                 if (lm) type = T_LM;
                 else if (dn) type = (ph == 0) ? T_DN_IN : (ph == 1) ? T_DN_REC : (ph == 2) ? T_DN_OUT : (ph == 3) ? T_GATEUP : T_DOWN;
-                else type = (ph == 0) ? T_FA_IN : (ph == 1) ? T_FA_OUT : (ph == 2) ? T_GATEUP : T_DOWN;
-                producer_phase(P, c, type, lw, dn_idx, pol_stream, pol_keep);
+                else type = (ph == 0) ? T_FA_IN : (ph == 1) ? T_FA_ATT : (ph == 2) ? T_FA_OUT : (ph == 3) ? T_GATEUP : T_DOWN;
+                producer_phase(P, c, type, lw, dn ? dn_idx : fa_idx, pol_stream, pol_keep);
             }
-            if (!lm && dn) ++dn_idx;
+            if (!lm) { if (dn) ++dn_idx; else ++fa_idx; }
         }
     } else {
         // ===== consumer warps =====
