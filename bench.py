@@ -346,7 +346,7 @@ def main():
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch, from the ncu capture
 # summarised under profiles/ (None until a capture exists).
-TRAFFIC_BYTES_PER_LAUNCH = 1_540_186_920   # profiles/decode_megakernel_bf16_ctx520.md
+TRAFFIC_BYTES_PER_LAUNCH = 1_537_192_800   # profiles/decode_megakernel_bf16_ctx520.md
 
 
 def cpu_state_dict(weights):
