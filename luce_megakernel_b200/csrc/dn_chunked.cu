@@ -87,20 +87,26 @@ constexpr int PREP_VB = PREP_KG + CH * PADROW * 2;        // fp16 beta v
 constexpr int PREP_A = PREP_VB + CH * PADROW * 2;         // f32 A
 constexpr int PREP_TH = PREP_A + CH * AROW * 4;           // fp16 T hi
 constexpr int PREP_TL = PREP_TH + CH * TROW * 2;          // fp16 T lo
-constexpr int PREP_OUT = PREP_TL + CH * TROW * 2;         // the shared block being assembled
-constexpr int PREP_G = PREP_OUT + BLK_BYTES;              // f32 G[64], beta[64]
-constexpr int PREP_SMEM = PREP_G + 2 * CH * 4;
+constexpr int PREP_G = PREP_TL + CH * TROW * 2;           // f32 G[64], beta[64]
+constexpr int PREP_SMEM = PREP_G + 2 * CH * 4;            // 105 984 bytes: two CTAs per SM
+constexpr int PREP_KDT = PREP_A;                          // staging of the decayed, transposed keys (16 KB), flushed
+                                                          // to global memory before A is written
 
-// gates: [t][head][4] = beta, decay, q.k, log decay;  pre: [t][6144] = q | k | v (f32, q and k normalised)
-__global__ void __launch_bounds__(256) k_dn_chunk_prepare(const float* __restrict__ pre, const float* __restrict__ gates,
-                                                          unsigned char* __restrict__ scratch, int S) {
+// qkv: bf16 [t][6144] projection outputs (q | k | v before the convolution); conv_w: bf16 [6144][4];
+// conv_state: f32 [6144][4], the four inputs before the prompt; gates: [t][head][4] = beta, decay, -, log decay.
+// The causal depthwise convolution (k = 4), SiLU and the L2 norms of q (x 1/sqrt(128)) and k
+// (reference: megakernel/prefill.cu:1281-1368) are computed here, one warp per 8 consecutive tokens with the
+// convolution window sliding through registers.
+__global__ void __launch_bounds__(256, 2) k_dn_chunk_prepare(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ conv_w,
+                                                             const float* __restrict__ conv_state, const float* __restrict__ gates,
+                                                             unsigned char* __restrict__ scratch, int S) {
     extern __shared__ __align__(128) unsigned char sm[];
     const int chunk = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = chunk * CH;
     float* sG = reinterpret_cast<float*>(sm + PREP_G);
     float* sBeta = sG + CH;
     float* sA = reinterpret_cast<float*>(sm + PREP_A);
-    unsigned char* outb = sm + PREP_OUT;
+    unsigned char* outg = scratch + pair_offset(chunk, h);          // the shared block in global memory
 
     // cumulative log-decay of the chunk (tokens past the prompt: beta 0, g 0)
     if (warp < 2) {
@@ -118,33 +124,88 @@ __global__ void __launch_bounds__(256) k_dn_chunk_prepare(const float* __restric
     __syncthreads();
     const float Glast = sG[CH - 1];
 
-    // q, k, v of the chunk -> bf16 operand tiles, and the two scaled copies that go straight to the shared block
-    for (int i = tid; i < CH * 32; i += 256) {
-        const int r = i >> 5, c4 = (i & 31) * 4;
-        const int t = t0 + r;
-        float4 q = make_float4(0.f, 0.f, 0.f, 0.f), k = q, v = q;
-        if (t < S) {
-            const float* row = pre + (size_t)t * DN_CONV_CH + h * DN_KEY + c4;
-            q = *reinterpret_cast<const float4*>(row);
-            k = *reinterpret_cast<const float4*>(row + DN_QK);
-            v = *reinterpret_cast<const float4*>(row + 2 * DN_QK);
+    {
+        // convolution + SiLU + L2 norms, then the fp16 operand tiles and the two scaled copies of the shared block
+        const int c4 = lane * 4;
+        float wq[3][4][4];                                  // [q|k|v][channel][tap]
+        int chan[3];
+#pragma unroll
+        for (int m = 0; m < 3; ++m) {
+            chan[m] = m * DN_QK + h * DN_KEY + c4;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + chan[m] + e);
+                wq[m][e][0] = bf_lo(wr.x); wq[m][e][1] = bf_hi(wr.x); wq[m][e][2] = bf_lo(wr.y); wq[m][e][3] = bf_hi(wr.y);
+            }
         }
-        const float G = sG[r], b = sBeta[r], gam = __expf(G), bg = b * gam, kd = __expf(Glast - G);
-        *reinterpret_cast<uint2*>(sm + PREP_KB + (r * PADROW + c4) * 2) = make_uint2(pack_h(k.x, k.y), pack_h(k.z, k.w));
-        *reinterpret_cast<uint2*>(sm + PREP_QB + (r * PADROW + c4) * 2) = make_uint2(pack_h(q.x, q.y), pack_h(q.z, q.w));
-        *reinterpret_cast<uint2*>(sm + PREP_KG + (r * PADROW + c4) * 2) =
-            make_uint2(pack_h(bg * k.x, bg * k.y), pack_h(bg * k.z, bg * k.w));
-        *reinterpret_cast<uint2*>(sm + PREP_VB + (r * PADROW + c4) * 2) =
-            make_uint2(pack_h(b * v.x, b * v.y), pack_h(b * v.z, b * v.w));
-        *reinterpret_cast<uint2*>(outb + OFF_QG + swz256(r, c4)) =
-            make_uint2(pack_h(gam * q.x, gam * q.y), pack_h(gam * q.z, gam * q.w));
-        __half* kdt = reinterpret_cast<__half*>(outb + OFF_KD);
-        kdt[swz128(c4 + 0, r) >> 1] = __float2half_rn(kd * k.x);
-        kdt[swz128(c4 + 1, r) >> 1] = __float2half_rn(kd * k.y);
-        kdt[swz128(c4 + 2, r) >> 1] = __float2half_rn(kd * k.z);
-        kdt[swz128(c4 + 3, r) >> 1] = __float2half_rn(kd * k.w);
+        // x[m][e][tap]: the last three inputs before the current token
+        float win[3][4][3];
+        auto load_row = [&](int tt, int m, float (&dst)[4]) {
+            if (tt >= 0) {
+                if (tt < S) {
+                    const uint2 u = *reinterpret_cast<const uint2*>(qkv + (size_t)tt * DN_CONV_CH + chan[m]);
+                    dst[0] = bf_lo(u.x); dst[1] = bf_hi(u.x); dst[2] = bf_lo(u.y); dst[3] = bf_hi(u.y);
+                } else { dst[0] = dst[1] = dst[2] = dst[3] = 0.f; }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dst[e] = conv_state[(chan[m] + e) * 4 + 4 + tt];
+            }
+        };
+        const int tb = t0 + warp * 8;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+#pragma unroll
+            for (int m = 0; m < 3; ++m) {
+                float tmp[4];
+                load_row(tb - 3 + k, m, tmp);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) win[m][e][k] = tmp[e];
+            }
+        }
+        __half* kdt = reinterpret_cast<__half*>(sm + PREP_KDT);
+#pragma unroll 1
+        for (int i = 0; i < 8; ++i) {
+            const int r = warp * 8 + i, t = t0 + r;
+            float val[3][4];
+#pragma unroll
+            for (int m = 0; m < 3; ++m) {
+                float cur[4];
+                load_row(t, m, cur);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float co = win[m][e][0] * wq[m][e][0] + win[m][e][1] * wq[m][e][1] + win[m][e][2] * wq[m][e][2] + cur[e] * wq[m][e][3];
+                    val[m][e] = (t < S) ? silu_f(co) : 0.f;
+                    win[m][e][0] = win[m][e][1]; win[m][e][1] = win[m][e][2]; win[m][e][2] = cur[e];
+                }
+            }
+            const float sq = warp_sum(val[0][0] * val[0][0] + val[0][1] * val[0][1] + val[0][2] * val[0][2] + val[0][3] * val[0][3]);
+            const float sk = warp_sum(val[1][0] * val[1][0] + val[1][1] * val[1][1] + val[1][2] * val[1][2] + val[1][3] * val[1][3]);
+            const float qn = rsqrtf(sq + 1e-6f) * 0.08838834764831845f, kn = rsqrtf(sk + 1e-6f);
+            const float4 q = make_float4(val[0][0] * qn, val[0][1] * qn, val[0][2] * qn, val[0][3] * qn);
+            const float4 k = make_float4(val[1][0] * kn, val[1][1] * kn, val[1][2] * kn, val[1][3] * kn);
+            const float4 v = make_float4(val[2][0], val[2][1], val[2][2], val[2][3]);
+            const float G = sG[r], b = sBeta[r], gam = __expf(G), bg = b * gam, kd = __expf(Glast - G);
+            *reinterpret_cast<uint2*>(sm + PREP_KB + (r * PADROW + c4) * 2) = make_uint2(pack_h(k.x, k.y), pack_h(k.z, k.w));
+            *reinterpret_cast<uint2*>(sm + PREP_QB + (r * PADROW + c4) * 2) = make_uint2(pack_h(q.x, q.y), pack_h(q.z, q.w));
+            *reinterpret_cast<uint2*>(sm + PREP_KG + (r * PADROW + c4) * 2) =
+                make_uint2(pack_h(bg * k.x, bg * k.y), pack_h(bg * k.z, bg * k.w));
+            *reinterpret_cast<uint2*>(sm + PREP_VB + (r * PADROW + c4) * 2) =
+                make_uint2(pack_h(b * v.x, b * v.y), pack_h(b * v.z, b * v.w));
+            *reinterpret_cast<uint2*>(outg + OFF_QG + swz256(r, c4)) =
+                make_uint2(pack_h(gam * q.x, gam * q.y), pack_h(gam * q.z, gam * q.w));
+            kdt[swz128(c4 + 0, r) >> 1] = __float2half_rn(kd * k.x);
+            kdt[swz128(c4 + 1, r) >> 1] = __float2half_rn(kd * k.y);
+            kdt[swz128(c4 + 2, r) >> 1] = __float2half_rn(kd * k.z);
+            kdt[swz128(c4 + 3, r) >> 1] = __float2half_rn(kd * k.w);
+        }
     }
-    if (tid == 0) *reinterpret_cast<float4*>(outb + OFF_GL) = make_float4(__expf(Glast), 0.f, 0.f, 0.f);
+    if (tid == 0) *reinterpret_cast<float4*>(outg + OFF_GL) = make_float4(__expf(Glast), 0.f, 0.f, 0.f);
+    __syncthreads();
+    {   // flush the transposed keys (their staging area is reused for A below)
+        const uint4* src = reinterpret_cast<const uint4*>(sm + PREP_KDT);
+        uint4* dst = reinterpret_cast<uint4*>(outg + OFF_KD);
+        for (int i = tid; i < 128 * 128 / 16; i += 256) dst[i] = src[i];
+    }
     __syncthreads();
 
     const int g8 = lane >> 2, t4 = lane & 3;
@@ -181,8 +242,8 @@ __global__ void __launch_bounds__(256) k_dn_chunk_prepare(const float* __restric
             }
             if (isq) {
                 const int c = n * 8 + 2 * t4;
-                *reinterpret_cast<uint32_t*>(outb + OFF_P + swz128(mt * 16 + g8, c)) = pack_h(acc[n][0], acc[n][1]);
-                *reinterpret_cast<uint32_t*>(outb + OFF_P + swz128(mt * 16 + g8 + 8, c)) = pack_h(acc[n][2], acc[n][3]);
+                *reinterpret_cast<uint32_t*>(outg + OFF_P + swz128(mt * 16 + g8, c)) = pack_h(acc[n][0], acc[n][1]);
+                *reinterpret_cast<uint32_t*>(outg + OFF_P + swz128(mt * 16 + g8 + 8, c)) = pack_h(acc[n][2], acc[n][3]);
             }
         }
     }
@@ -223,7 +284,7 @@ __global__ void __launch_bounds__(256) k_dn_chunk_prepare(const float* __restric
             ldsm4(th + (arow * TROW + ks * 16 + acol) * 2, ah[ks][0], ah[ks][1], ah[ks][2], ah[ks][3]);
             ldsm4(tl + (arow * TROW + ks * 16 + acol) * 2, al[ks][0], al[ks][1], al[ks][2], al[ks][3]);
         }
-        float* Uout = reinterpret_cast<float*>(scratch + pair_offset(chunk, h) + BLK_BYTES);
+        float* Uout = reinterpret_cast<float*>(outg + BLK_BYTES);
 #pragma unroll 2
         for (int np = 0; np < 8; ++np) {                 // pairs of 8-column tiles
             float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
@@ -238,10 +299,10 @@ __global__ void __launch_bounds__(256) k_dn_chunk_prepare(const float* __restric
             }
             const int r = mt * 16 + g8, col = np * 16 + 2 * t4;
             if (!isu) {
-                *reinterpret_cast<uint32_t*>(outb + OFF_W + swz256(r, col)) = pack_h(c0[0], c0[1]);
-                *reinterpret_cast<uint32_t*>(outb + OFF_W + swz256(r + 8, col)) = pack_h(c0[2], c0[3]);
-                *reinterpret_cast<uint32_t*>(outb + OFF_W + swz256(r, col + 8)) = pack_h(c1[0], c1[1]);
-                *reinterpret_cast<uint32_t*>(outb + OFF_W + swz256(r + 8, col + 8)) = pack_h(c1[2], c1[3]);
+                *reinterpret_cast<uint32_t*>(outg + OFF_W + swz256(r, col)) = pack_h(c0[0], c0[1]);
+                *reinterpret_cast<uint32_t*>(outg + OFF_W + swz256(r + 8, col)) = pack_h(c0[2], c0[3]);
+                *reinterpret_cast<uint32_t*>(outg + OFF_W + swz256(r, col + 8)) = pack_h(c1[0], c1[1]);
+                *reinterpret_cast<uint32_t*>(outg + OFF_W + swz256(r + 8, col + 8)) = pack_h(c1[2], c1[3]);
             } else {
                 // U[slice][token][32 values]
                 auto uaddr = [&](int row, int j) { return Uout + ((size_t)(j >> 5) * CH + row) * 32 + (j & 31); };
@@ -252,10 +313,6 @@ __global__ void __launch_bounds__(256) k_dn_chunk_prepare(const float* __restric
             }
         }
     }
-    __syncthreads();
-    uint4* dst = reinterpret_cast<uint4*>(scratch + pair_offset(chunk, h));
-    const uint4* src = reinterpret_cast<const uint4*>(outb);
-    for (int i = tid; i < BLK_BYTES / 16; i += 256) dst[i] = src[i];
 }
 
 // ---- serial pass: one CTA per (head, 32 value rows), 256 threads ------------------------------------------
@@ -414,8 +471,8 @@ __global__ void __launch_bounds__(256, 1) k_dn_chunk_scan(const unsigned char* _
 
 size_t dn_chunked_scratch_bytes(int S) { return (size_t)((S + CH - 1) / CH) * DN_HEADS * PAIR_BYTES; }
 
-cudaError_t dn_chunked(const float* pre, const float* gates, float* state, float* o, int S, void* scratch, int* err,
-                       cudaStream_t stream) {
+cudaError_t dn_chunked(const void* qkv, const void* conv_w, const float* conv_state, const float* gates, float* state, float* o,
+                       int S, void* scratch, int* err, cudaStream_t stream) {
     static bool attr[64] = {false};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -428,7 +485,8 @@ cudaError_t dn_chunked(const float* pre, const float* gates, float* state, float
         attr[dev] = true;
     }
     const int nchunks = (S + CH - 1) / CH;
-    k_dn_chunk_prepare<<<dim3(nchunks, DN_HEADS), 256, PREP_SMEM, stream>>>(pre, gates, (unsigned char*)scratch, S);
+    k_dn_chunk_prepare<<<dim3(nchunks, DN_HEADS), 256, PREP_SMEM, stream>>>((const __nv_bfloat16*)qkv, (const __nv_bfloat16*)conv_w, conv_state,
+                                                                         gates, (unsigned char*)scratch, S);
     k_dn_chunk_scan<<<DN_HEADS * 4, 256, SCAN2_SMEM, stream>>>((const unsigned char*)scratch, state, o, S, nchunks, err);
     return cudaGetLastError();
 }

@@ -14,11 +14,13 @@ cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, i
                          int* err_flag, cudaStream_t stream);
 
 // Gated delta rule over a prompt in chunks of 64 tokens (all 16 heads of one layer).
-// pre: f32 [S][6144] = q | k | v (q, k normalised); gates: f32 [S][16][4] = beta, decay, q.k, log decay;
-// state: f32 [16][128 value][128 key], updated in place; o: f32 [S][2048]; scratch: dn_chunked_scratch_bytes(S).
+// qkv: bf16 [S][6144] projection outputs q | k | v (the causal conv1d + SiLU and the L2 norms are applied inside);
+// conv_w: bf16 [6144][4]; conv_state: f32 [6144][4], the four inputs before the prompt (read only);
+// gates: f32 [S][16][4] = beta, decay, -, log decay; state: f32 [16][128 value][128 key], updated in place;
+// o: f32 [S][2048]; scratch: dn_chunked_scratch_bytes(S).
 size_t dn_chunked_scratch_bytes(int S);
-cudaError_t dn_chunked(const float* pre, const float* gates, float* state, float* o, int S, void* scratch, int* err,
-                       cudaStream_t stream);
+cudaError_t dn_chunked(const void* qkv, const void* conv_w, const float* conv_state, const float* gates, float* state, float* o,
+                       int S, void* scratch, int* err, cudaStream_t stream);
 
 // Causal GQA attention over a prompt (one layer): qkv bf16 [S][5120] = 8 x [q | gate] | k | v with q normalised
 // and rotated; kc, vc: bf16 [2][max_seq][256] (already holding the prompt's keys / values); out bf16 [S][2048]

@@ -510,9 +510,12 @@ extern "C" int mk_prefill_bf16(
             k_dn_gates<<<blocks_for_warps((long long)S * 32), 256, 0, stream>>>(
                 w.normed, (const bf*)lw.ptrs[DN_W_B], (const bf*)lw.ptrs[DN_W_A], (const bf*)lw.ptrs[DN_A_LOG],
                 (const bf*)lw.ptrs[DN_DT_BIAS], w.beta, w.beta, S);
-            k_dn_preproject<<<dim3(S, DN_HEADS), 128, 0, stream>>>(w.wide, (const bf*)lw.ptrs[DN_CONV_W], cstate, w.pre, w.beta, S);
-            if (g_scan_mode == 0) k_dn_scan<<<128, 512, SCAN_SMEM, stream>>>(w.pre, w.beta, state, w.o, S);
-            else PF_CHECK(dn_chunked(w.pre, w.beta, state, w.o, S, w.chunk_scratch, w.err, stream), "chunked scan");
+            if (g_scan_mode == 0) {
+                k_dn_preproject<<<dim3(S, DN_HEADS), 128, 0, stream>>>(w.wide, (const bf*)lw.ptrs[DN_CONV_W], cstate, w.pre, w.beta, S);
+                k_dn_scan<<<128, 512, SCAN_SMEM, stream>>>(w.pre, w.beta, state, w.o, S);
+            } else {
+                PF_CHECK(dn_chunked(w.wide, lw.ptrs[DN_CONV_W], cstate, w.beta, state, w.o, S, w.chunk_scratch, w.err, stream), "chunked scan");
+            }
             k_dn_conv_state<<<(DN_CONV_CH + 255) / 256, 256, 0, stream>>>(w.wide, cstate, S);
             k_dn_gated_norm<<<blocks_for_warps((long long)S * DN_HEADS), 256, 0, stream>>>(w.o, w.z, (const bf*)lw.ptrs[DN_NORM_W], w.act, S);
             PF_CHECK(gemm(w.act, lw.ptrs[DN_W_OUT], w.hidden, w.hidden, HIDDEN, DN_V), "gemm out");
