@@ -172,10 +172,64 @@ int mk_prefill_bf16(
     const int *token_ids, int seq_len, int *output_token,
     const void *embed_weight, const MkLayerWeights *layers, const void *final_norm_w, const void *lm_head_w,
     void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
-    const void *fused_fa_qkv_base, const void *fused_gate_up_base,
+    const void *fused_fa_qkv_base, const void *fused_gate_up_base,   /* either may be null: per-matrix GEMMs */
     void *final_normed, void *hidden_bf16_out,
     int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
 const char *mk_prefill_error(void);
+
+/* The reference's other prefill entry points, with their argument lists: launch_prefill_bf16_mega (bf16, per-matrix
+ * weights from the 128-byte table only; reference: megakernel/prefill_megakernel.cu:1031-1045),
+ * launch_prefill_bf16_nvfp4_lm (bf16 layers, NVFP4 LM head; megakernel/prefill_bw.cu:1486-1503) and
+ * launch_prefill_megakernel_nvfp4 (NVFP4 layer weights from the 208-byte table, NVFP4 LM head;
+ * megakernel/kernel_gb10_nvfp4.cu:2127-2145).  All run the same kernels as launch_prefill_bf16; NVFP4 layer
+ * matrices are dequantised to bf16 scratch one layer ahead of their GEMMs (that rounding to bf16 is the one
+ * place where the prefill is less exact than the NVFP4 decode kernel).  Scratch arguments are accepted and
+ * ignored.  The first two carry no max_seq_len: the cache stride comes from mk_set_prefill_max_seq_len
+ * (default 2048).  The mk_* forms take the model dimensions explicitly. */
+void mk_set_prefill_max_seq_len(int max_seq_len);
+int launch_prefill_bf16_mega(
+    const int *token_ids, int seq_len, int *output_token,
+    const void *embed_weight, const MkLayerWeights *layers, const void *final_norm_w, const void *lm_head_w,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *hidden, void *residual, void *normalized, void *proj_buf, void *proj_buf2, void *attn_buf, void *mlp_buf,
+    void *dn_out_buf, void *beta_buf, void *alpha_buf, void *final_normed, void *hidden_bf16_out,
+    void *lm_bmv, void *lm_bmi, cudaStream_t stream);
+int launch_prefill_bf16_nvfp4_lm(
+    const int *token_ids, int seq_len, int *output_token,
+    const void *embed_weight, const MkLayerWeights *layers, const void *fused_layers,
+    const void *final_norm_w, const void *lm_head_w, const void *lm_head_weight_packed, const void *lm_head_scales,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *hidden, void *residual, void *normalized,
+    void *proj_buf, void *proj_buf2, void *proj_buf_half, void *proj_act_packed, void *proj_act_scales,
+    void *attn_buf, void *mlp_buf, void *dn_out_buf, void *beta_buf, void *alpha_buf,
+    void *final_normed, void *hidden_bf16_out, void *lm_bmv, void *lm_bmi,
+    void *lm_hidden_bf16, void *lm_hidden_packed, void *lm_hidden_scales, void *lm_logits_f16, cudaStream_t stream);
+int launch_prefill_megakernel_nvfp4(
+    const int *token_ids, int seq_len, int *output_token_id,
+    const void *embed_weight, const void *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight_packed, const void *lm_head_scales,
+    void *lm_hidden_bf16, void *lm_hidden_packed, void *lm_hidden_scales, void *lm_logits_f16,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *hidden_buffer, void *g_activations, void *g_residual,
+    void *g_qkv_scratch, void *g_kv_scratch, void *g_attn_out,
+    void *g_mlp_inter, void *g_z_scratch, void *g_beta_scratch, void *g_alpha_scratch, void *g_normalized,
+    unsigned int *barrier_counter, unsigned int *barrier_generation,
+    float *block_max_vals, int *block_max_idxs, unsigned int *lm_sync_counter,
+    int max_seq_len, int group_size, cudaStream_t stream);
+int mk_prefill_bf16_nvfp4_lm(
+    const int *token_ids, int seq_len, int *output_token,
+    const void *embed_weight, const MkLayerWeights *layers, const void *final_norm_w,
+    const void *lm_head_weight_packed, const void *lm_head_scales,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *final_normed, void *hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
+int mk_prefill_nvfp4(
+    const int *token_ids, int seq_len, int *output_token,
+    const void *embed_weight, const void *layers, const void *final_norm_w,
+    const void *lm_head_weight_packed, const void *lm_head_scales,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *final_normed, void *hidden_bf16_out,
+    int max_seq_len, int group_size, int num_layers, int vocab, cudaStream_t stream);
 /* Which form of the gated delta rule the prefill uses: 1 (default) = chunks of 64 tokens on the tensor cores
  * (reference: the chunked kernels megakernel/prefill.cu:355-680), 0 = token-serial recurrence
  * (reference: megakernel/prefill.cu:114-221).  Both give the same result up to rounding. */

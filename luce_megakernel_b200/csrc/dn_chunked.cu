@@ -88,7 +88,7 @@ constexpr int PREP_A = PREP_VB + CH * PADROW * 2;         // f32 A
 constexpr int PREP_TH = PREP_A + CH * AROW * 4;           // fp16 T hi
 constexpr int PREP_TL = PREP_TH + CH * TROW * 2;          // fp16 T lo
 constexpr int PREP_G = PREP_TL + CH * TROW * 2;           // f32 G[64], beta[64]
-constexpr int PREP_SMEM = PREP_G + 2 * CH * 4;            // 105 984 bytes: two CTAs per SM
+constexpr int PREP_SMEM = PREP_G + 2 * CH * 4 + 16 * 17 * 4;   // 107 072 bytes: two CTAs per SM
 constexpr int PREP_KDT = PREP_A;                          // staging of the decayed, transposed keys (16 KB), flushed
                                                           // to global memory before A is written
 
@@ -162,15 +162,27 @@ __global__ void __launch_bounds__(256, 2) k_dn_chunk_prepare(const __nv_bfloat16
                 for (int e = 0; e < 4; ++e) win[m][e][k] = tmp[e];
             }
         }
+        // raw rows of the next two tokens are in flight while the current one is processed
+        auto fetch = [&](int t, uint2 (&dst)[3]) {
+#pragma unroll
+            for (int m = 0; m < 3; ++m)
+                dst[m] = (t < S) ? *reinterpret_cast<const uint2*>(qkv + (size_t)t * DN_CONV_CH + chan[m]) : make_uint2(0u, 0u);
+        };
+        uint2 nx0[3], nx1[3];
+        fetch(tb, nx0);
+        fetch(tb + 1, nx1);
         __half* kdt = reinterpret_cast<__half*>(sm + PREP_KDT);
-#pragma unroll 1
+#pragma unroll 2
         for (int i = 0; i < 8; ++i) {
             const int r = warp * 8 + i, t = t0 + r;
+            uint2 raw[3] = {nx0[0], nx0[1], nx0[2]};
+#pragma unroll
+            for (int m = 0; m < 3; ++m) nx0[m] = nx1[m];
+            if (i + 2 < 8) fetch(t + 2, nx1);
             float val[3][4];
 #pragma unroll
             for (int m = 0; m < 3; ++m) {
-                float cur[4];
-                load_row(t, m, cur);
+                const float cur[4] = {bf_lo(raw[m].x), bf_hi(raw[m].x), bf_lo(raw[m].y), bf_hi(raw[m].y)};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const float co = win[m][e][0] * wq[m][e][0] + win[m][e][1] * wq[m][e][1] + win[m][e][2] * wq[m][e][2] + cur[e] * wq[m][e][3];
@@ -249,29 +261,60 @@ __global__ void __launch_bounds__(256, 2) k_dn_chunk_prepare(const __nv_bfloat16
     }
     __syncthreads();
 
-    // T = (I + A)^-1 by forward substitution: thread c owns column c, the column stays in registers
-    if (warp < 2) {
-        float x[CH];
-        const int c = tid;
+    // T = (I + A)^-1, A strictly lower triangular, in 16 x 16 blocks: the four diagonal blocks by forward
+    // substitution (one thread per column), then each block row i from right to left,
+    //   T_ij = -(sum_{k=j+1..i} T_ik A_kj) T_jj,
+    // one thread per element.  T is kept as fp16 head + remainder (the form the products below read).
+    {
+        __half* TH = reinterpret_cast<__half*>(sm + PREP_TH);
+        __half* TL = reinterpret_cast<__half*>(sm + PREP_TL);
+        auto put = [&](int r, int c, float v) {
+            const __half hi = __float2half_rn(v);
+            TH[r * TROW + c] = hi;
+            TL[r * TROW + c] = __float2half_rn(v - __half2float(hi));
+        };
+        auto get = [&](int r, int c) { return __half2float(TH[r * TROW + c]) + __half2float(TL[r * TROW + c]); };
+        if (tid < 64) {
+            const int bb = (tid >> 4) * 16, c = tid & 15;
+            float x[16];
 #pragma unroll
-        for (int s = 0; s < CH; ++s) {
-            float p0 = (s == c) ? 1.f : 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+            for (int s = 0; s < 16; ++s) {
+                float acc = (s == c) ? 1.f : 0.f;
 #pragma unroll
-            for (int u4 = 0; u4 < (s + 3) / 4; ++u4) {
-                const float4 a = *reinterpret_cast<const float4*>(sA + s * AROW + u4 * 4);
-                if (u4 * 4 + 0 < s) p0 = fmaf(-a.x, x[u4 * 4 + 0], p0);
-                if (u4 * 4 + 1 < s) p1 = fmaf(-a.y, x[u4 * 4 + 1], p1);
-                if (u4 * 4 + 2 < s) p2 = fmaf(-a.z, x[u4 * 4 + 2], p2);
-                if (u4 * 4 + 3 < s) p3 = fmaf(-a.w, x[u4 * 4 + 3], p3);
+                for (int u = 0; u < s; ++u) acc = fmaf(-sA[(bb + s) * AROW + bb + u], x[u], acc);
+                x[s] = acc;
+                put(bb + s, bb + c, acc);
             }
-            x[s] = (p0 + p1) + (p2 + p3);
-            const __half hi = __float2half_rn(x[s]);
-            reinterpret_cast<__half*>(sm + PREP_TH)[s * TROW + c] = hi;
-            reinterpret_cast<__half*>(sm + PREP_TL)[s * TROW + c] = __float2half_rn(x[s] - __half2float(hi));
+        }
+        // zero the blocks above the diagonal
+        for (int i = tid; i < 6 * 256; i += 256) {
+            const int blk = i >> 8, r = (i >> 4) & 15, c = i & 15;
+            const int bi = (blk < 3) ? 0 : (blk < 5 ? 1 : 2), bj = (blk < 3) ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+            put(bi * 16 + r, bj * 16 + c, 0.f);
+        }
+        __syncthreads();
+        float* Ms = sG + 2 * CH;                 // 16 x 17 floats of scratch after G and beta
+        const int r = tid >> 4, c = tid & 15;
+#pragma unroll 1
+        for (int bi = 3; bi >= 1; --bi) {
+#pragma unroll 1
+            for (int bj = bi - 1; bj >= 0; --bj) {
+                float m[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int k = bj + 1; k <= bi; ++k) {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        m[e & 3] = fmaf(get(bi * 16 + r, k * 16 + e), sA[(k * 16 + e) * AROW + bj * 16 + c], m[e & 3]);
+                }
+                Ms[r * 17 + c] = (m[0] + m[1]) + (m[2] + m[3]);
+                __syncthreads();
+                float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e & 3] = fmaf(Ms[r * 17 + e], get(bj * 16 + e, bj * 16 + c), v[e & 3]);
+                put(bi * 16 + r, bj * 16 + c, -((v[0] + v[1]) + (v[2] + v[3])));
+                __syncthreads();
+            }
         }
     }
-    __syncthreads();
-
     {
         // warps 0-3: W = T (beta Gam k), warps 4-7: U = T (beta v); each warp one 16-row tile, 128 columns
         const int mt = warp & 3, isu = warp >> 2;
@@ -284,12 +327,14 @@ __global__ void __launch_bounds__(256, 2) k_dn_chunk_prepare(const __nv_bfloat16
             ldsm4(th + (arow * TROW + ks * 16 + acol) * 2, ah[ks][0], ah[ks][1], ah[ks][2], ah[ks][3]);
             ldsm4(tl + (arow * TROW + ks * 16 + acol) * 2, al[ks][0], al[ks][1], al[ks][2], al[ks][3]);
         }
+        // block row mt of T is zero right of block column mt: k-steps beyond it are skipped
         float* Uout = reinterpret_cast<float*>(outg + BLK_BYTES);
 #pragma unroll 2
         for (int np = 0; np < 8; ++np) {                 // pairs of 8-column tiles
             float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
+                if (ks > mt) continue;
                 uint32_t b0, b1, b2, b3;                  // operand stored [k][n]: transposing load
                 ldsm4t(bbase + ((ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * PADROW + np * 16 + (lane >> 4) * 8) * 2, b0, b1, b2, b3);
                 mma_h(c0, ah[ks][0], ah[ks][1], ah[ks][2], ah[ks][3], b0, b1);

@@ -9,6 +9,7 @@
 // causal attention is a scalar online-softmax warp per (query, head).  Both are correct for any S
 // and are the parts a later version replaces with the chunked scan / tensor-core flash attention.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -420,7 +421,7 @@ cudaError_t ensure_ws(PrefillWs& w, int S) {
     return cudaSuccess;
 }
 
-struct HostTable { const void* src = nullptr; int n = 0; LayerWeights rows[MAX_LAYERS]; };
+struct HostTable { const void* src = nullptr; int n = 0; size_t entry = 0; unsigned char rows[MAX_LAYERS * sizeof(LayerWeightsNVFP4)]; };
 HostTable g_tables[64];
 thread_local char g_perr[200] = "";
 struct SparseCfg { bool enabled = false; double top_frac = 0.10; int window = 4, sink = 1; };
@@ -451,22 +452,105 @@ extern "C" int mk_prefill_set_block_sparse(int enable, double top_frac, int wind
 }
 extern "C" void mk_prefill_set_scan_mode(int chunked) { mk::g_scan_mode = chunked ? 1 : 0; }
 
-extern "C" int mk_prefill_bf16(
-    const int* token_ids, int seq_len, int* output_token,
-    const void* embed_weight, const MkLayerWeights* layers, const void* final_norm_w, const void* lm_head_w,
-    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
-    const void* fused_fa_qkv_base, const void* fused_gate_up_base,
-    void* final_normed, void* hidden_bf16_out,
-    int max_seq_len, int num_layers, int vocab, cudaStream_t stream) {
-    using namespace mk;
-    if (!token_ids || !output_token || !embed_weight || !layers || !final_norm_w || !lm_head_w || !fa_k_cache ||
-        !fa_v_cache || !dn_states || !conv_bufs || !fused_fa_qkv_base || !fused_gate_up_base)
-        return pfail(MK_ERR_BAD_ARG, "null pointer argument");
-    if (seq_len <= 0 || seq_len > max_seq_len) return pfail(MK_ERR_BAD_ARG, "seq_len must be in [1, max_seq_len]");
-    if (num_layers < 1 || num_layers > MAX_LAYERS || vocab < 1) return pfail(MK_ERR_BAD_ARG, "bad model dimensions");
-    int dev = 0;
-    PF_CHECK(cudaGetDevice(&dev), "cudaGetDevice");
-    if (dev < 0 || dev >= 64) return pfail(MK_ERR_BAD_ARG, "device index out of range");
+namespace mk {
+namespace {
+
+// One layer's device pointers as the prefill uses them (bf16 unless noted).  Fused pointers ([q|k|v] rows and
+// [gate|up] rows in one matrix) take precedence; otherwise the separate matrices are multiplied into column
+// slices of the same activation buffers.
+struct LayerView {
+    int type = 0;
+    const void *in_norm = nullptr, *post_norm = nullptr;
+    const void *w_qkv = nullptr, *w_z = nullptr, *w_b = nullptr, *w_a = nullptr, *conv_w = nullptr, *a_log = nullptr,
+               *dt_bias = nullptr, *dn_norm = nullptr, *w_out = nullptr;                       // DeltaNet
+    const void *w_faqkv = nullptr, *w_q = nullptr, *w_k = nullptr, *w_v = nullptr, *q_norm = nullptr, *k_norm = nullptr,
+               *w_o = nullptr;                                                                  // attention
+    const void *w_gateup = nullptr, *w_gate = nullptr, *w_up = nullptr, *w_down = nullptr;      // MLP
+};
+struct LmView { const void* bf16 = nullptr; const void* packed = nullptr; const void* scales = nullptr; };
+
+LayerView view_of(const LayerWeights& lw, const void* fused_faqkv, const void* fused_gateup) {
+    LayerView v;
+    v.type = lw.layer_type;
+    v.in_norm = lw.ptrs[0];
+    if (lw.layer_type == 0) {
+        v.w_qkv = lw.ptrs[DN_W_QKV]; v.w_z = lw.ptrs[DN_W_Z]; v.w_b = lw.ptrs[DN_W_B]; v.w_a = lw.ptrs[DN_W_A];
+        v.conv_w = lw.ptrs[DN_CONV_W]; v.a_log = lw.ptrs[DN_A_LOG]; v.dt_bias = lw.ptrs[DN_DT_BIAS];
+        v.dn_norm = lw.ptrs[DN_NORM_W]; v.w_out = lw.ptrs[DN_W_OUT]; v.post_norm = lw.ptrs[DN_POST_NORM];
+        v.w_gate = lw.ptrs[DN_W_GATE]; v.w_up = lw.ptrs[DN_W_UP]; v.w_down = lw.ptrs[DN_W_DOWN];
+    } else {
+        v.w_q = lw.ptrs[FA_W_Q]; v.w_k = lw.ptrs[FA_W_K]; v.w_v = lw.ptrs[FA_W_V]; v.q_norm = lw.ptrs[FA_Q_NORM];
+        v.k_norm = lw.ptrs[FA_K_NORM]; v.w_o = lw.ptrs[FA_W_O]; v.post_norm = lw.ptrs[FA_POST_NORM];
+        v.w_gate = lw.ptrs[FA_W_GATE]; v.w_up = lw.ptrs[FA_W_UP]; v.w_down = lw.ptrs[FA_W_DOWN];
+        v.w_faqkv = fused_faqkv;
+    }
+    v.w_gateup = fused_gateup;
+    return v;
+}
+
+// greedy argmax over a logit vector, lowest index on ties (one block)
+__global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logits, int n, int* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += 1024) {
+        const float v = logits[i];
+        if (v > best) { best = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = sv[threadIdx.x]; bi = si[threadIdx.x];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+        }
+        if (threadIdx.x == 0) *out = bi;
+    }
+}
+
+// NVFP4 layer-weight format (groups of 32 along K, fp16 scales) -> bf16 matrix for the tensor-core GEMMs.
+// One thread per 8 weights.  value = e2m1(code) * scale in f32, rounded to bf16 (the GEMM operand type):
+// unlike the decode kernel, which multiplies the exact dequantised value, the prefill carries this rounding.
+__global__ void k_dequant_a_bf16(const uint8_t* __restrict__ packed, const __half* __restrict__ scales,
+                                 __nv_bfloat16* __restrict__ out, size_t n8, int cols) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n8) return;
+    const size_t e0 = i * 8, row = e0 / cols;
+    const int col = (int)(e0 - row * cols);
+    const float sc = __half2float(scales[row * (cols / 32) + col / 32]);
+    const uint32_t w = reinterpret_cast<const uint32_t*>(packed)[i];
+    const float lut[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t b = (w >> (8 * k)) & 0xffu;
+        const float lo = (b & 0x8u) ? -lut[b & 7u] : lut[b & 7u];
+        const float hi = (b & 0x80u) ? -lut[(b >> 4) & 7u] : lut[(b >> 4) & 7u];
+        const __nv_bfloat162 p2 = __floats2bfloat162_rn(lo * sc, hi * sc);
+        o[k] = *reinterpret_cast<const uint32_t*>(&p2);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+struct NvScratch { __nv_bfloat16 *qkv = nullptr, *z = nullptr, *out = nullptr, *gateup = nullptr, *down = nullptr; float* logits = nullptr; };
+NvScratch g_nvs[64];
+float* g_logits[64] = {nullptr};
+
+template <typename LayerSource>
+int prefill_core(const int* token_ids, int seq_len, int* output_token, const void* embed_weight, LayerSource source,
+                 int num_layers, const void* final_norm_w, LmView lm, void* fa_k_cache, void* fa_v_cache, void* dn_states,
+                 void* conv_bufs, void* final_normed, void* hidden_bf16_out, int max_seq_len, int vocab, int dev,
+                 cudaStream_t stream) {
     PrefillWs& w = g_pws[dev];
     PF_CHECK(ensure_ws(w, seq_len), "prefill workspace");
     static bool scan_attr[64] = {false};
@@ -474,24 +558,10 @@ extern "C" int mk_prefill_bf16(
         PF_CHECK(cudaFuncSetAttribute(k_dn_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM), "scan smem");
         scan_attr[dev] = true;
     }
-
-    // The pointer table lives on the device; the launches below need its entries on the host.  The
-    // host copy is kept per device and table address, as the reference keeps its own
-    // (megakernel/prefill.cu:1578-1584): a caller that rewrites a table in place must call
-    // mk_prefill_forget_tables() first.  With the copy cached the call enqueues work only (no
-    // synchronisation), so a whole prefill can be captured into a CUDA graph.
-    HostTable& ht = g_tables[dev];
-    if (ht.src != (const void*)layers || ht.n != num_layers) {
-        PF_CHECK(cudaMemcpyAsync(ht.rows, layers, (size_t)num_layers * sizeof(LayerWeights), cudaMemcpyDeviceToHost, stream), "table copy");
-        PF_CHECK(cudaStreamSynchronize(stream), "table copy sync");
-        ht.src = layers; ht.n = num_layers;
-    }
-    const LayerWeights* hl = ht.rows;
-
     const int S = seq_len;
     typedef __nv_bfloat16 bf;
-    auto gemm = [&](const void* A, const void* W, void* C, const void* R, int N, int K) {
-        return gemm_bf16_tn(A, W, C, R, S, N, K, K, N, w.err, stream);
+    auto gemm = [&](const void* A, const void* W, void* C, const void* R, int N, int K, int ldc) {
+        return gemm_bf16_tn(A, W, C, R, S, N, K, K, ldc, w.err, stream);
     };
     const int wpb = 8;                                            // warps per 256-thread block
     auto blocks_for_warps = [&](long long nw) { return (unsigned)((nw + wpb - 1) / wpb); };
@@ -499,34 +569,40 @@ extern "C" int mk_prefill_bf16(
     k_embed<<<S, 128, 0, stream>>>(token_ids, (const bf*)embed_weight, w.hidden, S, vocab);
     int dn_idx = 0, fa_idx = 0;
     for (int li = 0; li < num_layers; ++li) {
-        const LayerWeights& lw = hl[li];
-        const bool dn = (lw.layer_type == 0);
-        k_rmsnorm<<<blocks_for_warps(S), 256, 0, stream>>>(w.hidden, (const bf*)lw.ptrs[0], w.normed, S);
+        LayerView lv;
+        const int rc = source(li, lv);
+        if (rc != MK_OK) return rc;
+        const bool dn = (lv.type == 0);
+        k_rmsnorm<<<blocks_for_warps(S), 256, 0, stream>>>(w.hidden, (const bf*)lv.in_norm, w.normed, S);
         if (dn) {
             float* state = (float*)dn_states + (size_t)dn_idx * DN_HEADS * DN_VAL * DN_KEY;
             float* cstate = (float*)conv_bufs + (size_t)dn_idx * DN_CONV_CH * DN_CONV_K;
-            PF_CHECK(gemm(w.normed, lw.ptrs[DN_W_QKV], w.wide, nullptr, DN_CONV_CH, HIDDEN), "gemm qkv");
-            PF_CHECK(gemm(w.normed, lw.ptrs[DN_W_Z], w.z, nullptr, DN_V, HIDDEN), "gemm z");
+            PF_CHECK(gemm(w.normed, lv.w_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
+            PF_CHECK(gemm(w.normed, lv.w_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
             k_dn_gates<<<blocks_for_warps((long long)S * 32), 256, 0, stream>>>(
-                w.normed, (const bf*)lw.ptrs[DN_W_B], (const bf*)lw.ptrs[DN_W_A], (const bf*)lw.ptrs[DN_A_LOG],
-                (const bf*)lw.ptrs[DN_DT_BIAS], w.beta, w.beta, S);
+                w.normed, (const bf*)lv.w_b, (const bf*)lv.w_a, (const bf*)lv.a_log, (const bf*)lv.dt_bias, w.beta, w.beta, S);
             if (g_scan_mode == 0) {
-                k_dn_preproject<<<dim3(S, DN_HEADS), 128, 0, stream>>>(w.wide, (const bf*)lw.ptrs[DN_CONV_W], cstate, w.pre, w.beta, S);
+                k_dn_preproject<<<dim3(S, DN_HEADS), 128, 0, stream>>>(w.wide, (const bf*)lv.conv_w, cstate, w.pre, w.beta, S);
                 k_dn_scan<<<128, 512, SCAN_SMEM, stream>>>(w.pre, w.beta, state, w.o, S);
             } else {
-                PF_CHECK(dn_chunked(w.wide, lw.ptrs[DN_CONV_W], cstate, w.beta, state, w.o, S, w.chunk_scratch, w.err, stream), "chunked scan");
+                PF_CHECK(dn_chunked(w.wide, lv.conv_w, cstate, w.beta, state, w.o, S, w.chunk_scratch, w.err, stream), "chunked scan");
             }
             k_dn_conv_state<<<(DN_CONV_CH + 255) / 256, 256, 0, stream>>>(w.wide, cstate, S);
-            k_dn_gated_norm<<<blocks_for_warps((long long)S * DN_HEADS), 256, 0, stream>>>(w.o, w.z, (const bf*)lw.ptrs[DN_NORM_W], w.act, S);
-            PF_CHECK(gemm(w.act, lw.ptrs[DN_W_OUT], w.hidden, w.hidden, HIDDEN, DN_V), "gemm out");
+            k_dn_gated_norm<<<blocks_for_warps((long long)S * DN_HEADS), 256, 0, stream>>>(w.o, w.z, (const bf*)lv.dn_norm, w.act, S);
+            PF_CHECK(gemm(w.act, lv.w_out, w.hidden, w.hidden, HIDDEN, DN_V, HIDDEN), "gemm out");
             ++dn_idx;
         } else {
             bf* kc = (bf*)fa_k_cache + (size_t)fa_idx * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;
             bf* vc = (bf*)fa_v_cache + (size_t)fa_idx * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;
-            const bf* wqkv = (const bf*)fused_fa_qkv_base + (size_t)fa_idx * FA_QKV_ROWS * HIDDEN;
-            PF_CHECK(gemm(w.normed, wqkv, w.wide, nullptr, FA_QKV_ROWS, HIDDEN), "gemm fa qkv");
+            if (lv.w_faqkv) {
+                PF_CHECK(gemm(w.normed, lv.w_faqkv, w.wide, nullptr, FA_QKV_ROWS, HIDDEN, FA_QKV_ROWS), "gemm fa qkv");
+            } else {
+                PF_CHECK(gemm(w.normed, lv.w_q, w.wide, nullptr, FA_QPROJ, HIDDEN, FA_QKV_ROWS), "gemm q");
+                PF_CHECK(gemm(w.normed, lv.w_k, w.wide + FA_QPROJ, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm k");
+                PF_CHECK(gemm(w.normed, lv.w_v, w.wide + FA_QPROJ + FA_KV_SIZE, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm v");
+            }
             k_fa_norm_rope<<<blocks_for_warps((long long)S * 12), 256, 0, stream>>>(
-                w.wide, (const bf*)lw.ptrs[FA_Q_NORM], (const bf*)lw.ptrs[FA_K_NORM], kc, vc, S, max_seq_len);
+                w.wide, (const bf*)lv.q_norm, (const bf*)lv.k_norm, kc, vc, S, max_seq_len);
             const uint32_t* bmask = nullptr;
             if (g_sparse.enabled) {
                 uint32_t* m = nullptr;
@@ -535,27 +611,189 @@ extern "C" int mk_prefill_bf16(
                 bmask = m;
             }
             PF_CHECK(fa_prefill(w.wide, kc, vc, w.act, S, max_seq_len, bmask, stream), "attention");
-            PF_CHECK(gemm(w.act, lw.ptrs[FA_W_O], w.hidden, w.hidden, HIDDEN, FA_Q_SIZE), "gemm o");
+            PF_CHECK(gemm(w.act, lv.w_o, w.hidden, w.hidden, HIDDEN, FA_Q_SIZE, HIDDEN), "gemm o");
             ++fa_idx;
         }
-        k_rmsnorm<<<blocks_for_warps(S), 256, 0, stream>>>(w.hidden, (const bf*)lw.ptrs[dn ? (int)DN_POST_NORM : (int)FA_POST_NORM], w.normed, S);
-        const bf* wgu = (const bf*)fused_gate_up_base + (size_t)li * 2 * INTER * HIDDEN;
-        PF_CHECK(gemm(w.normed, wgu, w.wide, nullptr, 2 * INTER, HIDDEN), "gemm gate_up");
+        k_rmsnorm<<<blocks_for_warps(S), 256, 0, stream>>>(w.hidden, (const bf*)lv.post_norm, w.normed, S);
+        if (lv.w_gateup) {
+            PF_CHECK(gemm(w.normed, lv.w_gateup, w.wide, nullptr, 2 * INTER, HIDDEN, 2 * INTER), "gemm gate_up");
+        } else {
+            PF_CHECK(gemm(w.normed, lv.w_gate, w.wide, nullptr, INTER, HIDDEN, 2 * INTER), "gemm gate");
+            PF_CHECK(gemm(w.normed, lv.w_up, w.wide + INTER, nullptr, INTER, HIDDEN, 2 * INTER), "gemm up");
+        }
         k_silu_mul<<<(unsigned)(((size_t)S * (INTER / 8) + 255) / 256), 256, 0, stream>>>(w.wide, w.act, S);
-        PF_CHECK(gemm(w.act, lw.ptrs[dn ? (int)DN_W_DOWN : (int)FA_W_DOWN], w.hidden, w.hidden, HIDDEN, INTER), "gemm down");
+        PF_CHECK(gemm(w.act, lv.w_down, w.hidden, w.hidden, HIDDEN, INTER, HIDDEN), "gemm down");
     }
     k_final_norm<<<1, 512, 0, stream>>>(w.hidden + (size_t)(S - 1) * HIDDEN, (const bf*)final_norm_w, w.normed_f32,
                                         (bf*)final_normed, (bf*)hidden_bf16_out);
-    k_lm_head<<<LM_BLOCKS, 256, 0, stream>>>(w.normed_f32, (const bf*)lm_head_w, vocab, w.bval, w.bidx);
-    k_lm_reduce<<<1, 32, 0, stream>>>(w.bval, w.bidx, LM_BLOCKS, output_token);
+    if (lm.packed) {
+        // NVFP4 LM head (16-block / E4M3 format): logits by the in-register dequantising row product, then argmax
+        if (!g_logits[dev]) PF_CHECK(cudaMalloc((void**)&g_logits[dev], (size_t)DEFAULT_VOCAB * 4 * 2), "logits buffer");
+        if (vocab > 2 * DEFAULT_VOCAB) return pfail(MK_ERR_BAD_ARG, "vocabulary too large for the logits buffer");
+        if (mk_matvec_nvfp4(1, lm.packed, lm.scales, w.normed_f32, g_logits[dev], vocab, HIDDEN, 16, stream) != MK_OK)
+            return pfail(MK_ERR_BAD_ARG, mk_nvfp4_error());
+        k_argmax<<<1, 1024, 0, stream>>>(g_logits[dev], vocab, output_token);
+    } else {
+        k_lm_head<<<LM_BLOCKS, 256, 0, stream>>>(w.normed_f32, (const bf*)lm.bf16, vocab, w.bval, w.bidx);
+        k_lm_reduce<<<1, 32, 0, stream>>>(w.bval, w.bidx, LM_BLOCKS, output_token);
+    }
     PF_CHECK(cudaGetLastError(), "prefill launch");
     return MK_OK;
 }
 
-// Reference-compatible entry (reference: megakernel/prefill.cu:1559-1576, declared at
-// megakernel/torch_bindings.cpp:354-368).  The caller's scratch buffers are accepted and ignored:
-// the library sizes its own workspace (the reference's scratch layout overruns proj_buf for the
-// fused gate/up tile and cannot hold S x 7168).
+int check_common(const void* const* req, int nreq, int seq_len, int max_seq_len, int num_layers, int vocab, int& dev) {
+    for (int i = 0; i < nreq; ++i) if (!req[i]) return pfail(MK_ERR_BAD_ARG, "null pointer argument");
+    if (seq_len <= 0 || seq_len > max_seq_len) return pfail(MK_ERR_BAD_ARG, "seq_len must be in [1, max_seq_len]");
+    if (num_layers < 1 || num_layers > MAX_LAYERS || vocab < 1) return pfail(MK_ERR_BAD_ARG, "bad model dimensions");
+    PF_CHECK(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return pfail(MK_ERR_BAD_ARG, "device index out of range");
+    return MK_OK;
+}
+
+// host copy of a pointer table (kept per device and table address, see mk_prefill_forget_tables)
+int host_table(int dev, const void* layers, int num_layers, size_t entry, cudaStream_t stream, const unsigned char*& rows) {
+    HostTable& ht = g_tables[dev];
+    if (ht.src != layers || ht.n != num_layers || ht.entry != entry) {
+        PF_CHECK(cudaMemcpyAsync(ht.rows, layers, (size_t)num_layers * entry, cudaMemcpyDeviceToHost, stream), "table copy");
+        PF_CHECK(cudaStreamSynchronize(stream), "table copy sync");
+        ht.src = layers; ht.n = num_layers; ht.entry = entry;
+    }
+    rows = ht.rows;
+    return MK_OK;
+}
+
+}  // namespace
+}  // namespace mk
+
+// The host copy of the pointer table is kept per device and table address, as the reference keeps its own
+// (megakernel/prefill.cu:1578-1584): a caller that rewrites a table in place must call
+// mk_prefill_forget_tables() first.  With the copy cached a call enqueues work only (no synchronisation), so a
+// whole prefill can be captured into a CUDA graph.
+extern "C" int mk_prefill_bf16(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const MkLayerWeights* layers, const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    const void* fused_fa_qkv_base, const void* fused_gate_up_base,
+    void* final_normed, void* hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream) {
+    using namespace mk;
+    const void* req[] = {token_ids, output_token, embed_weight, layers, final_norm_w, lm_head_w, fa_k_cache, fa_v_cache, dn_states, conv_bufs};
+    int dev = 0;
+    int rc = check_common(req, 10, seq_len, max_seq_len, num_layers, vocab, dev);
+    if (rc != MK_OK) return rc;
+    const unsigned char* rows = nullptr;
+    rc = host_table(dev, layers, num_layers, sizeof(LayerWeights), stream, rows);
+    if (rc != MK_OK) return rc;
+    const LayerWeights* hl = reinterpret_cast<const LayerWeights*>(rows);
+    int fa_seen = 0;
+    auto source = [&](int li, LayerView& lv) {
+        const bool fa = hl[li].layer_type != 0;
+        lv = view_of(hl[li],
+                     (fa && fused_fa_qkv_base) ? (const __nv_bfloat16*)fused_fa_qkv_base + (size_t)fa_seen * FA_QKV_ROWS * HIDDEN : nullptr,
+                     fused_gate_up_base ? (const __nv_bfloat16*)fused_gate_up_base + (size_t)li * 2 * INTER * HIDDEN : nullptr);
+        if (fa) ++fa_seen;
+        return (int)MK_OK;
+    };
+    LmView lm;
+    lm.bf16 = lm_head_w;
+    return prefill_core(token_ids, seq_len, output_token, embed_weight, source, num_layers, final_norm_w, lm, fa_k_cache,
+                        fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out, max_seq_len, vocab, dev, stream);
+}
+
+// bf16 layers, NVFP4 LM head (16-block / E4M3 format) for the first generated token
+// (reference: launch_prefill_bf16_nvfp4_lm, megakernel/prefill_bw.cu:1486-1530).
+extern "C" int mk_prefill_bf16_nvfp4_lm(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const MkLayerWeights* layers, const void* final_norm_w,
+    const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* final_normed, void* hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream) {
+    using namespace mk;
+    const void* req[] = {token_ids, output_token, embed_weight, layers, final_norm_w, lm_head_weight_packed, lm_head_scales,
+                         fa_k_cache, fa_v_cache, dn_states, conv_bufs};
+    int dev = 0;
+    int rc = check_common(req, 11, seq_len, max_seq_len, num_layers, vocab, dev);
+    if (rc != MK_OK) return rc;
+    if (vocab % 128) return pfail(MK_ERR_BAD_ARG, "the NVFP4 LM head needs a vocabulary that is a multiple of 128");
+    const unsigned char* rows = nullptr;
+    rc = host_table(dev, layers, num_layers, sizeof(LayerWeights), stream, rows);
+    if (rc != MK_OK) return rc;
+    const LayerWeights* hl = reinterpret_cast<const LayerWeights*>(rows);
+    auto source = [&](int li, LayerView& lv) { lv = view_of(hl[li], nullptr, nullptr); return (int)MK_OK; };
+    LmView lm;
+    lm.packed = lm_head_weight_packed; lm.scales = lm_head_scales;
+    return prefill_core(token_ids, seq_len, output_token, embed_weight, source, num_layers, final_norm_w, lm, fa_k_cache,
+                        fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out, max_seq_len, vocab, dev, stream);
+}
+
+// Prefill on NVFP4 weights (208-byte table): every quantised matrix of a layer is dequantised into bf16 scratch
+// right before the layer runs, then the bf16 pipeline is used; NVFP4 LM head.
+// (reference: launch_prefill_megakernel_nvfp4, megakernel/kernel_gb10_nvfp4.cu:2127-2190)
+extern "C" int mk_prefill_nvfp4(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const void* layers, const void* final_norm_w,
+    const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* final_normed, void* hidden_bf16_out,
+    int max_seq_len, int group_size, int num_layers, int vocab, cudaStream_t stream) {
+    using namespace mk;
+    const void* req[] = {token_ids, output_token, embed_weight, layers, final_norm_w, lm_head_weight_packed, lm_head_scales,
+                         fa_k_cache, fa_v_cache, dn_states, conv_bufs};
+    int dev = 0;
+    int rc = check_common(req, 11, seq_len, max_seq_len, num_layers, vocab, dev);
+    if (rc != MK_OK) return rc;
+    if (group_size != 32) return pfail(MK_ERR_BAD_ARG, "group_size must be 32");
+    if (vocab % 128) return pfail(MK_ERR_BAD_ARG, "the NVFP4 LM head needs a vocabulary that is a multiple of 128");
+    const unsigned char* rows = nullptr;
+    rc = host_table(dev, layers, num_layers, sizeof(LayerWeightsNVFP4), stream, rows);
+    if (rc != MK_OK) return rc;
+    const LayerWeightsNVFP4* hl = reinterpret_cast<const LayerWeightsNVFP4*>(rows);
+    NvScratch& ns = g_nvs[dev];
+    if (!ns.qkv) {
+        PF_CHECK(cudaMalloc((void**)&ns.qkv, (size_t)DN_CONV_CH * HIDDEN * 2), "dequant scratch");
+        PF_CHECK(cudaMalloc((void**)&ns.z, (size_t)DN_V * HIDDEN * 2), "dequant scratch");
+        PF_CHECK(cudaMalloc((void**)&ns.out, (size_t)HIDDEN * DN_V * 2), "dequant scratch");
+        PF_CHECK(cudaMalloc((void**)&ns.gateup, (size_t)2 * INTER * HIDDEN * 2), "dequant scratch");
+        PF_CHECK(cudaMalloc((void**)&ns.down, (size_t)HIDDEN * INTER * 2), "dequant scratch");
+    }
+    auto deq = [&](const void* packed, const void* scales, __nv_bfloat16* out, int rws, int cols) {
+        const size_t n8 = (size_t)rws * cols / 8;
+        k_dequant_a_bf16<<<(unsigned)((n8 + 255) / 256), 256, 0, stream>>>((const uint8_t*)packed, (const __half*)scales, out, n8, cols);
+    };
+    // slots of the 208-byte table (reference: megakernel/model_nvfp4.py:274-311)
+    auto source = [&](int li, LayerView& lv) {
+        const LayerWeightsNVFP4& t = hl[li];
+        lv.type = t.layer_type;
+        lv.in_norm = t.ptrs[0];
+        if (t.layer_type == 0) {
+            deq(t.ptrs[1], t.ptrs[2], ns.qkv, DN_CONV_CH, HIDDEN);
+            deq(t.ptrs[3], t.ptrs[4], ns.z, DN_V, HIDDEN);
+            deq(t.ptrs[11], t.ptrs[12], ns.out, HIDDEN, DN_V);
+            deq(t.ptrs[14], t.ptrs[15], ns.gateup, INTER, HIDDEN);
+            deq(t.ptrs[16], t.ptrs[17], ns.gateup + (size_t)INTER * HIDDEN, INTER, HIDDEN);
+            deq(t.ptrs[18], t.ptrs[19], ns.down, HIDDEN, INTER);
+            lv.w_qkv = ns.qkv; lv.w_z = ns.z; lv.w_b = t.ptrs[5]; lv.w_a = t.ptrs[6]; lv.conv_w = t.ptrs[7];
+            lv.a_log = t.ptrs[8]; lv.dt_bias = t.ptrs[9]; lv.dn_norm = t.ptrs[10]; lv.w_out = ns.out; lv.post_norm = t.ptrs[13];
+        } else {
+            deq(t.ptrs[1], t.ptrs[2], ns.qkv, FA_QPROJ, HIDDEN);
+            deq(t.ptrs[3], t.ptrs[4], ns.qkv + (size_t)FA_QPROJ * HIDDEN, FA_KV_SIZE, HIDDEN);
+            deq(t.ptrs[5], t.ptrs[6], ns.qkv + (size_t)(FA_QPROJ + FA_KV_SIZE) * HIDDEN, FA_KV_SIZE, HIDDEN);
+            deq(t.ptrs[9], t.ptrs[10], ns.out, HIDDEN, FA_Q_SIZE);
+            deq(t.ptrs[12], t.ptrs[13], ns.gateup, INTER, HIDDEN);
+            deq(t.ptrs[14], t.ptrs[15], ns.gateup + (size_t)INTER * HIDDEN, INTER, HIDDEN);
+            deq(t.ptrs[16], t.ptrs[17], ns.down, HIDDEN, INTER);
+            lv.w_faqkv = ns.qkv; lv.q_norm = t.ptrs[7]; lv.k_norm = t.ptrs[8]; lv.w_o = ns.out; lv.post_norm = t.ptrs[11];
+        }
+        lv.w_gateup = ns.gateup; lv.w_down = ns.down;
+        return cudaGetLastError() == cudaSuccess ? (int)MK_OK : pfail(MK_ERR_CUDA, "dequantise launch");
+    };
+    LmView lm;
+    lm.packed = lm_head_weight_packed; lm.scales = lm_head_scales;
+    return prefill_core(token_ids, seq_len, output_token, embed_weight, source, num_layers, final_norm_w, lm, fa_k_cache,
+                        fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out, max_seq_len, vocab, dev, stream);
+}
+
 extern "C" int launch_prefill_bf16(
     const int* token_ids, int seq_len, int* output_token,
     const void* embed_weight, const MkLayerWeights* layers,
@@ -577,6 +815,79 @@ extern "C" int launch_prefill_bf16(
     return mk_prefill_bf16(token_ids, seq_len, output_token, embed_weight, layers, final_norm_w, lm_head_w, fa_k_cache,
                            fa_v_cache, dn_states, conv_bufs, fused_fa_qkv_base, fused_gate_up_base, final_normed,
                            hidden_bf16_out, max_seq_len, nl, vocab, stream);
+}
+
+// ---- the reference's other prefill entry points, same argument lists ---------------------------------------
+// Two of them carry no max_seq_len (the reference compiles the cache stride in): the stride is taken from
+// mk_set_prefill_max_seq_len (default 2048, the reference's MAX_SEQ_LEN); the torch ops set it from the cache
+// tensor's shape.
+namespace mk { namespace { int g_default_max_seq = 2048; } }
+extern "C" void mk_set_prefill_max_seq_len(int max_seq_len) { if (max_seq_len > 0) mk::g_default_max_seq = max_seq_len; }
+
+extern "C" int launch_prefill_bf16_mega(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const MkLayerWeights* layers,
+    const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden, void* residual, void* normalized,
+    void* proj_buf, void* proj_buf2, void* attn_buf, void* mlp_buf,
+    void* dn_out_buf, void* beta_buf, void* alpha_buf,
+    void* final_normed, void* hidden_bf16_out,
+    void* lm_bmv, void* lm_bmi, cudaStream_t stream) {
+    (void)hidden; (void)residual; (void)normalized; (void)proj_buf; (void)proj_buf2; (void)attn_buf; (void)mlp_buf;
+    (void)dn_out_buf; (void)beta_buf; (void)alpha_buf; (void)lm_bmv; (void)lm_bmi;
+    int nl = 0, vocab = 0;
+    mk_get_model_dims(&nl, &vocab);
+    return mk_prefill_bf16(token_ids, seq_len, output_token, embed_weight, layers, final_norm_w, lm_head_w, fa_k_cache,
+                           fa_v_cache, dn_states, conv_bufs, nullptr, nullptr, final_normed, hidden_bf16_out,
+                           mk::g_default_max_seq, nl, vocab, stream);
+}
+
+extern "C" int launch_prefill_bf16_nvfp4_lm(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const MkLayerWeights* layers, const void* fused_layers,
+    const void* final_norm_w, const void* lm_head_w,
+    const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden, void* residual, void* normalized,
+    void* proj_buf, void* proj_buf2, void* proj_buf_half, void* proj_act_packed, void* proj_act_scales,
+    void* attn_buf, void* mlp_buf, void* dn_out_buf, void* beta_buf, void* alpha_buf,
+    void* final_normed, void* hidden_bf16_out, void* lm_bmv, void* lm_bmi,
+    void* lm_hidden_bf16, void* lm_hidden_packed, void* lm_hidden_scales, void* lm_logits_f16, cudaStream_t stream) {
+    (void)fused_layers; (void)lm_head_w; (void)hidden; (void)residual; (void)normalized; (void)proj_buf; (void)proj_buf2;
+    (void)proj_buf_half; (void)proj_act_packed; (void)proj_act_scales; (void)attn_buf; (void)mlp_buf; (void)dn_out_buf;
+    (void)beta_buf; (void)alpha_buf; (void)lm_bmv; (void)lm_bmi; (void)lm_hidden_bf16; (void)lm_hidden_packed;
+    (void)lm_hidden_scales; (void)lm_logits_f16;
+    int nl = 0, vocab = 0;
+    mk_get_model_dims(&nl, &vocab);
+    return mk_prefill_bf16_nvfp4_lm(token_ids, seq_len, output_token, embed_weight, layers, final_norm_w, lm_head_weight_packed,
+                                    lm_head_scales, fa_k_cache, fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out,
+                                    mk::g_default_max_seq, nl, vocab, stream);
+}
+
+extern "C" int launch_prefill_megakernel_nvfp4(
+    const int* token_ids, int seq_len, int* output_token_id,
+    const void* embed_weight, const void* layer_weights, const void* final_norm_weight,
+    const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* lm_hidden_bf16, void* lm_hidden_packed, void* lm_hidden_scales, void* lm_logits_f16,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden_buffer, void* g_activations, void* g_residual,
+    void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch,
+    void* g_alpha_scratch, void* g_normalized,
+    unsigned int* barrier_counter, unsigned int* barrier_generation,
+    float* block_max_vals, int* block_max_idxs, unsigned int* lm_sync_counter,
+    int max_seq_len, int group_size, cudaStream_t stream) {
+    (void)lm_hidden_bf16; (void)lm_hidden_packed; (void)lm_hidden_scales; (void)lm_logits_f16; (void)g_activations;
+    (void)g_residual; (void)g_qkv_scratch; (void)g_kv_scratch; (void)g_attn_out; (void)g_mlp_inter; (void)g_z_scratch;
+    (void)g_beta_scratch; (void)g_alpha_scratch; (void)g_normalized; (void)barrier_counter; (void)barrier_generation;
+    (void)block_max_vals; (void)block_max_idxs; (void)lm_sync_counter;
+    int nl = 0, vocab = 0;
+    mk_get_model_dims(&nl, &vocab);
+    // the reference leaves the last row of the residual stream in hidden_buffer for the decode steps that follow
+    return mk_prefill_nvfp4(token_ids, seq_len, output_token_id, embed_weight, layer_weights, final_norm_weight,
+                            lm_head_weight_packed, lm_head_scales, fa_k_cache, fa_v_cache, dn_states, conv_bufs, nullptr,
+                            hidden_buffer, max_seq_len, group_size, nl, vocab, stream);
 }
 
 // The attention building blocks on their own (tests call these through the C ABI).

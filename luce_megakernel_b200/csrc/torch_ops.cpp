@@ -199,6 +199,112 @@ void decode_many_nvfp4(Tensor output_tokens, Tensor token_buffer, int64_t input_
     check_status(rc, "decode_many_nvfp4");
 }
 
+// The reference's other prefill ops (reference: megakernel/torch_bindings.cpp:409-565, schemas :632-670).
+void prefill_bf16_mega(Tensor output_token, Tensor token_ids, Tensor embed_weight, Tensor layer_weights_packed,
+                       Tensor final_norm_weight, Tensor lm_head_weight, Tensor fa_k_cache, Tensor fa_v_cache,
+                       Tensor dn_states, Tensor conv_bufs, Tensor hidden, Tensor residual, Tensor normalized,
+                       Tensor proj_buf, Tensor proj_buf2, Tensor attn_buf, Tensor mlp_buf, Tensor dn_out_buf,
+                       Tensor beta_buf, Tensor alpha_buf, Tensor final_normed, Tensor hidden_bf16_out, Tensor lm_bmv,
+                       Tensor lm_bmi) {
+    need(output_token, "output_token", torch::kInt32, 1);
+    need(token_ids, "token_ids", torch::kInt32, 1);
+    TORCH_CHECK(token_ids.dim() == 1, "token_ids must be 1-D");
+    need(embed_weight, "embed_weight", torch::kBFloat16, 1024);
+    need(layer_weights_packed, "layer_weights_packed", torch::kUInt8, 128);
+    need(lm_head_weight, "lm_head_weight", torch::kBFloat16, 1024);
+    TORCH_CHECK(fa_k_cache.dim() == 4 && fa_k_cache.size(3) == 256, "fa_k_cache must be [layers, 2, max_seq_len, 256]");
+    const int64_t max_seq_len = fa_k_cache.size(2);
+    need(fa_k_cache, "fa_k_cache", torch::kBFloat16, 2 * max_seq_len * 256);
+    need(fa_v_cache, "fa_v_cache", torch::kBFloat16, 2 * max_seq_len * 256);
+    need(dn_states, "dn_states", torch::kFloat32, 16 * 128 * 128);
+    need(conv_bufs, "conv_bufs", torch::kFloat32, 6144 * 4);
+    need(final_normed, "final_normed", torch::kBFloat16, 1024);
+    need(hidden_bf16_out, "hidden_bf16_out", torch::kBFloat16, 1024);
+    TORCH_CHECK(token_ids.size(0) <= max_seq_len, "prompt longer than the cache");
+    DeviceGuard guard(embed_weight);
+    check_status(mk_set_model_dims((int)(layer_weights_packed.numel() / 128), (int)embed_weight.size(0)), "prefill_bf16_mega");
+    mk_set_prefill_max_seq_len((int)max_seq_len);
+    const int rc = launch_prefill_bf16_mega(
+        (const int*)token_ids.data_ptr(), (int)token_ids.size(0), (int*)output_token.data_ptr(), embed_weight.data_ptr(),
+        (const MkLayerWeights*)layer_weights_packed.data_ptr(), final_norm_weight.data_ptr(), lm_head_weight.data_ptr(),
+        fa_k_cache.data_ptr(), fa_v_cache.data_ptr(), dn_states.data_ptr(), conv_bufs.data_ptr(), nullptr, nullptr, nullptr,
+        nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, final_normed.data_ptr(), hidden_bf16_out.data_ptr(),
+        nullptr, nullptr, current_stream(embed_weight));
+    TORCH_CHECK(rc == MK_OK, "qwen35_megakernel_bf16_C::prefill_bf16_mega failed (", rc, "): ", mk_prefill_error());
+    (void)hidden; (void)residual; (void)normalized; (void)proj_buf; (void)proj_buf2; (void)attn_buf; (void)mlp_buf;
+    (void)dn_out_buf; (void)beta_buf; (void)alpha_buf; (void)lm_bmv; (void)lm_bmi;
+}
+
+void prefill_megakernel_nvfp4(Tensor output_token, Tensor token_ids, Tensor embed_weight, Tensor layer_weights_packed,
+                              Tensor final_norm_weight, Tensor lm_head_weight_packed, Tensor lm_head_scales,
+                              Tensor lm_hidden_bf16, Tensor lm_hidden_packed, Tensor lm_hidden_scales, Tensor lm_logits_f16,
+                              Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs, Tensor hidden_buffer,
+                              Tensor activations, Tensor residual, Tensor qkv_scratch, Tensor kv_scratch, Tensor attn_out,
+                              Tensor mlp_inter, Tensor z_scratch, Tensor beta_scratch, Tensor alpha_scratch, Tensor normalized,
+                              Tensor barrier_counter, Tensor barrier_generation, Tensor block_max_vals, Tensor block_max_idxs,
+                              Tensor lm_sync_counter, int64_t max_seq_len, int64_t group_size) {
+    need(output_token, "output_token", torch::kInt32, 1);
+    need(token_ids, "token_ids", torch::kInt32, 1);
+    TORCH_CHECK(token_ids.dim() == 1, "token_ids must be 1-D");
+    TORCH_CHECK(token_ids.size(0) <= max_seq_len, "prompt longer than max_seq_len");
+    DeviceGuard guard(embed_weight);
+    check_nvfp4_common(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight_packed, lm_head_scales, fa_k_cache,
+                       fa_v_cache, dn_states, conv_bufs, hidden_buffer, normalized, max_seq_len, "prefill_megakernel_nvfp4");
+    const int rc = launch_prefill_megakernel_nvfp4(
+        (const int*)token_ids.data_ptr(), (int)token_ids.size(0), (int*)output_token.data_ptr(), embed_weight.data_ptr(),
+        layer_weights_packed.data_ptr(), final_norm_weight.data_ptr(), lm_head_weight_packed.data_ptr(), lm_head_scales.data_ptr(),
+        nullptr, nullptr, nullptr, nullptr, fa_k_cache.data_ptr(), fa_v_cache.data_ptr(), dn_states.data_ptr(),
+        conv_bufs.data_ptr(), hidden_buffer.data_ptr(), nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+        nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, (int)max_seq_len, (int)group_size,
+        current_stream(embed_weight));
+    TORCH_CHECK(rc == MK_OK, "qwen35_megakernel_bf16_C::prefill_megakernel_nvfp4 failed (", rc, "): ", mk_prefill_error());
+    (void)lm_hidden_bf16; (void)lm_hidden_packed; (void)lm_hidden_scales; (void)lm_logits_f16; (void)activations; (void)residual;
+    (void)qkv_scratch; (void)kv_scratch; (void)attn_out; (void)mlp_inter; (void)z_scratch; (void)beta_scratch;
+    (void)alpha_scratch; (void)barrier_counter; (void)barrier_generation; (void)block_max_vals; (void)block_max_idxs;
+    (void)lm_sync_counter;
+}
+
+void prefill_bf16_nvfp4_lm(Tensor output_token, Tensor token_ids, Tensor embed_weight, Tensor layer_weights_packed,
+                           Tensor prefill_fused_weights_packed, Tensor final_norm_weight, Tensor lm_head_weight,
+                           Tensor lm_head_weight_packed, Tensor lm_head_scales, Tensor fa_k_cache, Tensor fa_v_cache,
+                           Tensor dn_states, Tensor conv_bufs, Tensor hidden, Tensor residual, Tensor normalized,
+                           Tensor proj_buf, Tensor proj_buf2, Tensor proj_buf_half, Tensor proj_act_packed,
+                           Tensor proj_act_scales, Tensor attn_buf, Tensor mlp_buf, Tensor dn_out_buf, Tensor beta_buf,
+                           Tensor alpha_buf, Tensor final_normed, Tensor hidden_bf16_out, Tensor lm_bmv, Tensor lm_bmi,
+                           Tensor lm_hidden_bf16, Tensor lm_hidden_packed, Tensor lm_hidden_scales, Tensor lm_logits_f16) {
+    need(output_token, "output_token", torch::kInt32, 1);
+    need(token_ids, "token_ids", torch::kInt32, 1);
+    TORCH_CHECK(token_ids.dim() == 1, "token_ids must be 1-D");
+    need(embed_weight, "embed_weight", torch::kBFloat16, 1024);
+    need(layer_weights_packed, "layer_weights_packed", torch::kUInt8, 128);
+    need(lm_head_weight_packed, "lm_head_weight_packed", torch::kUInt8, 512);
+    need(lm_head_scales, "lm_head_scales", torch::kUInt8, 512);
+    TORCH_CHECK(fa_k_cache.dim() == 4 && fa_k_cache.size(3) == 256, "fa_k_cache must be [layers, 2, max_seq_len, 256]");
+    const int64_t max_seq_len = fa_k_cache.size(2);
+    need(fa_k_cache, "fa_k_cache", torch::kBFloat16, 2 * max_seq_len * 256);
+    need(fa_v_cache, "fa_v_cache", torch::kBFloat16, 2 * max_seq_len * 256);
+    need(dn_states, "dn_states", torch::kFloat32, 16 * 128 * 128);
+    need(conv_bufs, "conv_bufs", torch::kFloat32, 6144 * 4);
+    need(final_normed, "final_normed", torch::kBFloat16, 1024);
+    need(hidden_bf16_out, "hidden_bf16_out", torch::kBFloat16, 1024);
+    TORCH_CHECK(token_ids.size(0) <= max_seq_len, "prompt longer than the cache");
+    DeviceGuard guard(embed_weight);
+    check_status(mk_set_model_dims((int)(layer_weights_packed.numel() / 128), (int)embed_weight.size(0)), "prefill_bf16_nvfp4_lm");
+    mk_set_prefill_max_seq_len((int)max_seq_len);
+    const int rc = launch_prefill_bf16_nvfp4_lm(
+        (const int*)token_ids.data_ptr(), (int)token_ids.size(0), (int*)output_token.data_ptr(), embed_weight.data_ptr(),
+        (const MkLayerWeights*)layer_weights_packed.data_ptr(), nullptr, final_norm_weight.data_ptr(), nullptr,
+        lm_head_weight_packed.data_ptr(), lm_head_scales.data_ptr(), fa_k_cache.data_ptr(), fa_v_cache.data_ptr(),
+        dn_states.data_ptr(), conv_bufs.data_ptr(), nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+        nullptr, nullptr, nullptr, nullptr, final_normed.data_ptr(), hidden_bf16_out.data_ptr(), nullptr, nullptr, nullptr, nullptr,
+        nullptr, nullptr, current_stream(embed_weight));
+    TORCH_CHECK(rc == MK_OK, "qwen35_megakernel_bf16_C::prefill_bf16_nvfp4_lm failed (", rc, "): ", mk_prefill_error());
+    (void)prefill_fused_weights_packed; (void)lm_head_weight; (void)hidden; (void)residual; (void)normalized; (void)proj_buf;
+    (void)proj_buf2; (void)proj_buf_half; (void)proj_act_packed; (void)proj_act_scales; (void)attn_buf; (void)mlp_buf;
+    (void)dn_out_buf; (void)beta_buf; (void)alpha_buf; (void)lm_bmv; (void)lm_bmi; (void)lm_hidden_bf16; (void)lm_hidden_packed;
+    (void)lm_hidden_scales; (void)lm_logits_f16;
+}
+
 // NVFP4 quantisers (reference: megakernel/torch_bindings.cpp:272-337): same checks, same outputs.
 void quantize_nvfp4_out(Tensor packed_out, Tensor scales_out, Tensor weight, int64_t group_size) {
     TORCH_CHECK(weight.is_cuda() && weight.is_contiguous() && weight.dim() == 2, "weight must be a contiguous 2-D CUDA tensor");
@@ -302,6 +408,45 @@ TORCH_LIBRARY(qwen35_megakernel_bf16_C, ops) {
             "Tensor block_max_vals, Tensor block_max_idxs, Tensor lm_sync_counter, "
             "int position, int max_seq_len, int group_size) -> ()");
     ops.impl("decode_many_nvfp4", torch::kCUDA, &decode_many_nvfp4);
+
+    ops.def("prefill_bf16_mega(Tensor output_token, Tensor token_ids, "
+            "Tensor embed_weight, Tensor layer_weights_packed, "
+            "Tensor final_norm_weight, Tensor lm_head_weight, "
+            "Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs, "
+            "Tensor hidden, Tensor residual, Tensor normalized, "
+            "Tensor proj_buf, Tensor proj_buf2, Tensor attn_buf, Tensor mlp_buf, "
+            "Tensor dn_out_buf, Tensor beta_buf, Tensor alpha_buf, "
+            "Tensor final_normed, Tensor hidden_bf16_out, "
+            "Tensor lm_bmv, Tensor lm_bmi) -> ()");
+    ops.impl("prefill_bf16_mega", torch::kCUDA, &prefill_bf16_mega);
+
+    ops.def("prefill_megakernel_nvfp4(Tensor output_token, Tensor token_ids, "
+            "Tensor embed_weight, Tensor layer_weights_packed, "
+            "Tensor final_norm_weight, Tensor lm_head_weight_packed, Tensor lm_head_scales, "
+            "Tensor lm_hidden_bf16, Tensor lm_hidden_packed, Tensor lm_hidden_scales, Tensor lm_logits_f16, "
+            "Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs, "
+            "Tensor hidden_buffer, Tensor activations, Tensor residual, "
+            "Tensor qkv_scratch, Tensor kv_scratch, Tensor attn_out, "
+            "Tensor mlp_inter, Tensor z_scratch, Tensor beta_scratch, "
+            "Tensor alpha_scratch, Tensor normalized, "
+            "Tensor barrier_counter, Tensor barrier_generation, "
+            "Tensor block_max_vals, Tensor block_max_idxs, Tensor lm_sync_counter, "
+            "int max_seq_len, int group_size) -> ()");
+    ops.impl("prefill_megakernel_nvfp4", torch::kCUDA, &prefill_megakernel_nvfp4);
+
+    ops.def("prefill_bf16_nvfp4_lm(Tensor output_token, Tensor token_ids, "
+            "Tensor embed_weight, Tensor layer_weights_packed, Tensor prefill_fused_weights_packed, "
+            "Tensor final_norm_weight, Tensor lm_head_weight, "
+            "Tensor lm_head_weight_packed, Tensor lm_head_scales, "
+            "Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs, "
+            "Tensor hidden, Tensor residual, Tensor normalized, "
+            "Tensor proj_buf, Tensor proj_buf2, Tensor proj_buf_half, Tensor proj_act_packed, Tensor proj_act_scales, "
+            "Tensor attn_buf, Tensor mlp_buf, "
+            "Tensor dn_out_buf, Tensor beta_buf, Tensor alpha_buf, "
+            "Tensor final_normed, Tensor hidden_bf16_out, "
+            "Tensor lm_bmv, Tensor lm_bmi, "
+            "Tensor lm_hidden_bf16, Tensor lm_hidden_packed, Tensor lm_hidden_scales, Tensor lm_logits_f16) -> ()");
+    ops.impl("prefill_bf16_nvfp4_lm", torch::kCUDA, &prefill_bf16_nvfp4_lm);
 
     ops.def("quantize_nvfp4_out(Tensor packed_out, Tensor scales_out, Tensor weight, int group_size) -> ()");
     ops.impl("quantize_nvfp4_out", torch::kCUDA, &quantize_nvfp4_out);

@@ -150,6 +150,42 @@ class Decoder:
         self._position += steps
         return out
 
+    def prefill_tokens(self, token_ids, mode: str = "raw") -> int:
+        """Run prompt prefill from position 0 and return the first generated token id
+        (reference: megakernel/model_nvfp4.py:771-825).  mode "raw": NVFP4 layer weights
+        (launch_prefill_megakernel_nvfp4); mode "bf16": bf16 layer weights with the NVFP4 LM head
+        (launch_prefill_bf16_nvfp4_lm's arithmetic)."""
+        ids = torch.as_tensor(token_ids, dtype=torch.int32).to(self._embed_weight.device).contiguous()
+        S = int(ids.numel())
+        if S < 1 or S > self.max_seq_len:
+            raise ValueError("prompt length must be in [1, max_seq_len]")
+        self.reset()
+        self._check(self._lib.mk_set_model_dims(self.num_layers, self.vocab))
+        z = ctypes.c_void_p(0)
+        if mode == "raw":
+            rc = self._lib.mk_prefill_nvfp4(
+                _ptr(ids), ctypes.c_int(S), _ptr(self._out_token), _ptr(self._embed_weight), _ptr(self._layer_weights_packed),
+                _ptr(self._final_norm_weight), _ptr(self._lm_packed), _ptr(self._lm_scales), _ptr(self._fa_k_cache),
+                _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs), z, _ptr(self._hidden),
+                ctypes.c_int(self.max_seq_len), ctypes.c_int(self.group_size), ctypes.c_int(self.num_layers),
+                ctypes.c_int(self.vocab), self._stream())
+        elif mode == "bf16":
+            if not hasattr(self, "_bf16_table"):
+                from .model import _pack_layer_weights
+                self._bf16_table = _pack_layer_weights(self._weights["layer_data"])
+            rc = self._lib.mk_prefill_bf16_nvfp4_lm(
+                _ptr(ids), ctypes.c_int(S), _ptr(self._out_token), _ptr(self._embed_weight), _ptr(self._bf16_table),
+                _ptr(self._final_norm_weight), _ptr(self._lm_packed), _ptr(self._lm_scales), _ptr(self._fa_k_cache),
+                _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs), z, _ptr(self._hidden),
+                ctypes.c_int(self.max_seq_len), ctypes.c_int(self.num_layers), ctypes.c_int(self.vocab), self._stream())
+        else:
+            raise ValueError("mode must be 'raw' or 'bf16'")
+        if rc != 0:
+            self._lib.mk_prefill_error.restype = ctypes.c_char_p
+            raise RuntimeError(f"prefill failed ({rc}): {self._lib.mk_prefill_error().decode()}")
+        self._position = S
+        return int(self._out_token.item())
+
     def reset(self):
         self._position = 0
         for t in (self._fa_k_cache, self._fa_v_cache, self._dn_states, self._conv_bufs):

@@ -46,13 +46,17 @@ def test_prefill_matches_oracle(dec, small_model, S):
     tr = orc.forward(toks, st)
     ref_h = tr.hidden[-1][-1]
     _, o32 = small_model("unit", "none")
-    h32 = o32.forward(toks, O.State.new(NL, MAXSEQ, V), want_logits=False).hidden[-1][-1]
+    tr32 = o32.forward(toks, O.State.new(NL, MAXSEQ, V))
+    h32 = tr32.hidden[-1][-1]
     eh = float((dec._hidden_bf16_out.float().cpu() - ref_h).abs().max())
     tol = max(2e-2, 4 * bf16_ulp(float(ref_h.abs().max())), 2.0 * float((h32 - ref_h).abs().max()))
     assert eh <= tol, f"hidden error {eh} (bound {tol})"
     lm = sd["model.embed_tokens.weight"].float()
     logits = lm @ dec._final_normed.float().cpu()
-    assert float((logits - tr.logits).abs().max()) <= 6e-2       # final_normed is returned in bf16
+    # final_normed is returned in bf16; like the hidden bound, the logit bound admits twice the distance
+    # between the oracle with and without the decode kernel's rounding points
+    logit_tol = max(6e-2, 2.0 * float((tr32.logits - tr.logits).abs().max()))
+    assert float((logits - tr.logits).abs().max()) <= logit_tol
     top = torch.topk(tr.logits, 2)
     margin = float(top.values[0] - top.values[1])
     assert tok == tr.token or (margin <= 0.1 and tok in top.indices.tolist())
