@@ -76,11 +76,14 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, int*
     return false;
 }
 
-template <int BN>
+// SPLIT: the K range is cut into `ks` parts, a work item is (tile, part) and leaves its f32 partial tile in
+// `partial` ([part][M][N]); gemm_splitk_reduce adds the parts (and the residual) and rounds to bf16.  Used when
+// a problem has far fewer tiles than the machine has SMs (the K = 2048 / 3584 projections of a short prompt).
+template <int BN, bool SPLIT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                     __nv_bfloat16* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc,
-                    int* err) {
+                    int* err, float* __restrict__ partial, int ks) {
     typedef Cfg<BN> G;
     constexpr int STAGES = G::STAGES;
     extern __shared__ char smem_raw[];
@@ -91,8 +94,16 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     const uint32_t full0 = bars, empty0 = bars + 8 * STAGES, tfull0 = bars + 16 * STAGES, tempty0 = tfull0 + 16;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * G::STAGE_BYTES + 16 * STAGES + 32);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nk = K / BK;
-    const int mt = (M + BM - 1) / BM, ntiles = mt * (N / BN);
+    const int nk_all = K / BK;
+    const int mt = (M + BM - 1) / BM, ntiles = mt * (N / BN) * (SPLIT ? ks : 1);
+    // work item -> (tile, K part); part p covers k-steps [p nk / ks, (p + 1) nk / ks)
+    auto item = [&](int it_, int& m0, int& n0, int& kb0, int& kb1, int& part) {
+        const int tile = SPLIT ? it_ / ks : it_;
+        part = SPLIT ? it_ - tile * ks : 0;
+        m0 = (tile % mt) * BM; n0 = (tile / mt) * BN;
+        kb0 = SPLIT ? (part * nk_all) / ks : 0;
+        kb1 = SPLIT ? ((part + 1) * nk_all) / ks : nk_all;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) { mbar_init(full0 + 8 * s, 1); mbar_init(empty0 + 8 * s, 1); }
@@ -113,8 +124,9 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         if (lane == 0) {
             uint32_t it = 0;
             for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-                const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                int m0, n0, kb0, kb1, part;
+                item(tile, m0, n0, kb0, kb1, part);
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const uint32_t s = it % STAGES, par = (it / STAGES) & 1u;
                     ok = wait_bounded(empty0 + 8 * s, par ^ 1u, err);
                     if (!ok) break;
@@ -134,7 +146,9 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t acc = tmem + buf * BN;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                int m0, n0, kb0, kb1, part;
+                item(tile, m0, n0, kb0, kb1, part);
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const uint32_t s = it % STAGES, par = (it / STAGES) & 1u;
                     ok = wait_bounded(full0 + 8 * s, par, err);
                     if (!ok) break;
@@ -142,7 +156,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
                     const uint64_t ad = smem_desc_sw128(a0 + s * TILE_A_BYTES), bd = smem_desc_sw128(b0 + s * G::TILE_B_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)   // 16 bf16 = 32 bytes = 2 descriptor units per step
-                        umma(acc, ad + 2 * k, bd + 2 * k, idesc, (kb | k) ? 1u : 0u);
+                        umma(acc, ad + 2 * k, bd + 2 * k, idesc, ((kb - kb0) | k) ? 1u : 0u);
                     umma_commit(empty0 + 8 * s);        // frees the stage once these MMAs have read it
                 }
                 if (ok) umma_commit(tfull0 + 8 * buf);  // accumulator complete
@@ -153,7 +167,8 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         const int quad = warp & 3;
         uint32_t local = 0;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++local) {
-            const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
+            int m0, n0, kb0, kb1, part;
+            item(tile, m0, n0, kb0, kb1, part);
             const uint32_t buf = local & 1u, use = local >> 1;
             ok = wait_bounded(tfull0 + 8 * buf, use & 1u, err);
             if (!ok) break;
@@ -173,7 +188,15 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
                       "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
                     : "r"(taddr) : "memory");
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (row < M) {
+                if (SPLIT) {
+                    if (row < M) {
+                        float4* dst = reinterpret_cast<float4*>(partial + ((size_t)part * M + row) * N + n0 + c0);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                                 __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+                    }
+                } else if (row < M) {
                     __nv_bfloat16* dst = C + (size_t)row * ldc + n0 + c0;
                     const __nv_bfloat16* res = R ? R + (size_t)row * ldc + n0 + c0 : nullptr;
 #pragma unroll
@@ -209,6 +232,32 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     }
 }
 
+// C[row][col] = bf16(sum over parts + residual), 8 columns per thread
+__global__ void gemm_splitk_reduce(const float* __restrict__ partial, int ks, const __nv_bfloat16* __restrict__ R,
+                                   __nv_bfloat16* __restrict__ C, int M, int N, int ldc) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int n8 = N / 8;
+    if (i >= (size_t)M * n8) return;
+    const int row = (int)(i / n8), col = (int)(i - (size_t)row * n8) * 8;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int p = 0; p < ks; ++p) {
+        const float4* src = reinterpret_cast<const float4*>(partial + ((size_t)p * M + row) * N + col);
+        const float4 a = src[0], b = src[1];
+        f[0] += a.x; f[1] += a.y; f[2] += a.z; f[3] += a.w; f[4] += b.x; f[5] += b.y; f[6] += b.z; f[7] += b.w;
+    }
+    if (R) {
+        const uint4 r4 = *reinterpret_cast<const uint4*>(R + (size_t)row * ldc + col);
+        f[0] += bf_lo(r4.x); f[1] += bf_hi(r4.x); f[2] += bf_lo(r4.y); f[3] += bf_hi(r4.y);
+        f[4] += bf_lo(r4.z); f[5] += bf_hi(r4.z); f[6] += bf_lo(r4.w); f[7] += bf_hi(r4.w);
+    }
+    uint4 o;
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(f[0], f[1]), p1 = __floats2bfloat162_rn(f[2], f[3]);
+    __nv_bfloat162 p2 = __floats2bfloat162_rn(f[4], f[5]), p3 = __floats2bfloat162_rn(f[6], f[7]);
+    o.x = *reinterpret_cast<uint32_t*>(&p0); o.y = *reinterpret_cast<uint32_t*>(&p1);
+    o.z = *reinterpret_cast<uint32_t*>(&p2); o.w = *reinterpret_cast<uint32_t*>(&p3);
+    *reinterpret_cast<uint4*>(C + (size_t)row * ldc + col) = o;
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
                                   const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -241,15 +290,39 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
                         int sms, cudaStream_t stream) {
     static bool attr_done = false;
     if (!attr_done) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
         if (e != cudaSuccess) return e;
         attr_done = true;
     }
     CUtensorMap ma, mw;
     if (!make_map(&ma, A, M, K, lda, BM) || !make_map(&mw, W, N, K, K, BN)) return cudaErrorInvalidValue;
     const int ntiles = ((M + BM - 1) / BM) * (N / BN);
-    gemm_bf16_tn_kernel<BN><<<ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(
-        ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K, ldc, err_flag);
+    // split K when the tiles would leave most SMs idle and every part still has a few k-steps
+    int ks = sms / ntiles;
+    if (ks > 4) ks = 4;
+    while (ks > 1 && (K / BK) / ks < 4) --ks;
+    if (BN == 128 && ks >= 2 && K >= 2048) {      // only the long-K projections: K = 1024 products keep one summation order
+        static float* ws = nullptr;
+        static size_t ws_bytes = 0;
+        const size_t need = (size_t)ks * M * N * sizeof(float);
+        if (need > ws_bytes) {
+            if (ws) cudaFree(ws);
+            ws = nullptr; ws_bytes = 0;
+            cudaError_t e = cudaMalloc((void**)&ws, need);
+            if (e != cudaSuccess) return e;
+            ws_bytes = need;
+        }
+        const int items = ntiles * ks;
+        gemm_bf16_tn_kernel<BN, true><<<items < sms ? items : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(
+            ma, mw, nullptr, nullptr, M, N, K, ldc, err_flag, ws, ks);
+        const size_t n = (size_t)M * (N / 8);
+        gemm_splitk_reduce<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(ws, ks, (const __nv_bfloat16*)R, (__nv_bfloat16*)C, M, N, ldc);
+        return cudaGetLastError();
+    }
+    gemm_bf16_tn_kernel<BN, false><<<ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(
+        ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K, ldc, err_flag, nullptr, 1);
     return cudaGetLastError();
 }
 
