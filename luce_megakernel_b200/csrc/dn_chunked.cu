@@ -100,6 +100,7 @@ constexpr int PREP_KDT = PREP_A;                          // staging of the deca
 __global__ void __launch_bounds__(256, 2) k_dn_chunk_prepare(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ conv_w,
                                                              const float* __restrict__ conv_state, const float* __restrict__ gates,
                                                              unsigned char* __restrict__ scratch, int S) {
+    pdl_enter();
     extern __shared__ __align__(128) unsigned char sm[];
     const int chunk = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = chunk * CH;
@@ -373,6 +374,7 @@ constexpr int SCAN2_SMEM = SC_BAR + 16;
 
 __global__ void __launch_bounds__(256, 1) k_dn_chunk_scan(const unsigned char* __restrict__ scratch, float* __restrict__ state,
                                                           float* __restrict__ o, int S, int nchunks, int* __restrict__ err) {
+    pdl_enter();
     extern __shared__ __align__(128) unsigned char sm[];
     const int h = blockIdx.x >> 2, slice = blockIdx.x & 3;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -530,9 +532,9 @@ cudaError_t dn_chunked(const void* qkv, const void* conv_w, const float* conv_st
         attr[dev] = true;
     }
     const int nchunks = (S + CH - 1) / CH;
-    k_dn_chunk_prepare<<<dim3(nchunks, DN_HEADS), 256, PREP_SMEM, stream>>>((const __nv_bfloat16*)qkv, (const __nv_bfloat16*)conv_w, conv_state,
+    launch_pdl(k_dn_chunk_prepare, dim3(nchunks, DN_HEADS), 256, PREP_SMEM, stream, (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)conv_w, conv_state,
                                                                          gates, (unsigned char*)scratch, S);
-    k_dn_chunk_scan<<<DN_HEADS * 4, 256, SCAN2_SMEM, stream>>>((const unsigned char*)scratch, state, o, S, nchunks, err);
+    launch_pdl(k_dn_chunk_scan, DN_HEADS * 4, 256, SCAN2_SMEM, stream, (const unsigned char*)scratch, state, o, S, nchunks, err);
     return cudaGetLastError();
 }
 

@@ -56,6 +56,7 @@ template <bool SPARSE>
 __global__ void __launch_bounds__(256, 1) k_fa_prefill(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ kc,
                                                        const __nv_bfloat16* __restrict__ vc, __nv_bfloat16* __restrict__ out,
                                                        int S, int max_seq, const uint32_t* __restrict__ mask, int nblk, int nwords) {
+    pdl_enter();
     extern __shared__ __align__(128) unsigned char sm[];
     const int qblk = gridDim.x - 1 - blockIdx.x;          // longest rows first
     const int g = blockIdx.y;
@@ -234,6 +235,7 @@ namespace {
 // Mean over the (up to) 128 positions of a block, sequentially in f32; slots 0-7 = query heads, 8-9 = key heads.
 __global__ void __launch_bounds__(256) k_bs_pool(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ kc,
                                                  float* __restrict__ means, int S, int max_seq, int nblk) {
+    pdl_enter();
     const int b = blockIdx.x, slot = blockIdx.y, d = threadIdx.x;
     const int lo = b * 128, hi = min(S, lo + 128);
     float acc = 0.f;
@@ -252,6 +254,7 @@ __global__ void __launch_bounds__(256) k_bs_pool(const __nv_bfloat16* __restrict
 // on its own and in a fixed order, so the scores can be reproduced bit for bit on a CPU.
 __global__ void __launch_bounds__(256) k_bs_select(const float* __restrict__ means, uint32_t* __restrict__ mask, int nblk, int nwords,
                                                    double top_frac, int window, int sink) {
+    pdl_enter();
     extern __shared__ float sc[];                           // nblk scores, then nwords mask words
     uint32_t* words = reinterpret_cast<uint32_t*>(sc + nblk);
     const int i = blockIdx.x, h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -299,8 +302,8 @@ cudaError_t block_select(const void* qkv, const void* kc, int S, int max_seq, do
     if (nblk > MAX_KEY_BLOCKS) return cudaErrorInvalidValue;
     float* means = (float*)scratch;
     uint32_t* mask = (uint32_t*)((char*)scratch + (size_t)10 * nblk * FA_HEAD_DIM * 4);
-    k_bs_pool<<<dim3(nblk, 10), 256, 0, stream>>>((const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc, means, S, max_seq, nblk);
-    k_bs_select<<<dim3(nblk, 8), 256, (nblk + nwords) * 4, stream>>>(means, mask, nblk, nwords, top_frac, window, sink);
+    launch_pdl(k_bs_pool, dim3(nblk, 10), 256, 0, stream, (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc, means, S, max_seq, nblk);
+    launch_pdl(k_bs_select, dim3(nblk, 8), 256, (nblk + nwords) * 4, stream, means, mask, nblk, nwords, top_frac, window, sink);
     *mask_out = mask;
     return cudaGetLastError();
 }
@@ -321,10 +324,10 @@ cudaError_t fa_prefill(const void* qkv, const void* kc, const void* vc, void* ou
     if (mask) {
         const int nblk = (S + 127) / 128, nwords = (nblk + 31) / 32;
         if (nblk > MAX_KEY_BLOCKS) return cudaErrorInvalidValue;
-        k_fa_prefill<true><<<grid, 256, FA_SMEM_SPARSE, stream>>>((const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc,
+        launch_pdl(k_fa_prefill<true>, grid, 256, FA_SMEM_SPARSE, stream, (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc,
                                                                    (const __nv_bfloat16*)vc, (__nv_bfloat16*)out, S, max_seq, mask, nblk, nwords);
     } else {
-        k_fa_prefill<false><<<grid, 256, FA_SMEM, stream>>>((const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc,
+        launch_pdl(k_fa_prefill<false>, grid, 256, FA_SMEM, stream, (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc,
                                                             (__nv_bfloat16*)out, S, max_seq, nullptr, 0, 0);
     }
     return cudaGetLastError();

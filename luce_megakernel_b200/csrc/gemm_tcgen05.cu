@@ -84,6 +84,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                     __nv_bfloat16* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc,
                     int* err, float* __restrict__ partial, int ks) {
+    // the next kernel may be scheduled now; this one sets up barriers and tensor memory while its predecessor
+    // drains and waits for it (griddepcontrol.wait below) before the first operand is read
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     typedef Cfg<BN> G;
     constexpr int STAGES = G::STAGES;
     extern __shared__ char smem_raw[];
@@ -119,6 +122,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
     bool ok = true;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == 0) {
         if (lane == 0) {
@@ -235,6 +239,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 // C[row][col] = bf16(sum over parts + residual), 8 columns per thread
 __global__ void gemm_splitk_reduce(const float* __restrict__ partial, int ks, const __nv_bfloat16* __restrict__ R,
                                    __nv_bfloat16* __restrict__ C, int M, int N, int ldc) {
+    pdl_enter();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int n8 = N / 8;
     if (i >= (size_t)M * n8) return;
@@ -315,14 +320,12 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
             ws_bytes = need;
         }
         const int items = ntiles * ks;
-        gemm_bf16_tn_kernel<BN, true><<<items < sms ? items : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(
-            ma, mw, nullptr, nullptr, M, N, K, ldc, err_flag, ws, ks);
+        launch_pdl(gemm_bf16_tn_kernel<BN, true>, items < sms ? items : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, nullptr, nullptr, M, N, K, ldc, err_flag, ws, ks);
         const size_t n = (size_t)M * (N / 8);
-        gemm_splitk_reduce<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(ws, ks, (const __nv_bfloat16*)R, (__nv_bfloat16*)C, M, N, ldc);
+        launch_pdl(gemm_splitk_reduce, (unsigned)((n + 255) / 256), 256, 0, stream, ws, ks, (const __nv_bfloat16*)R, (__nv_bfloat16*)C, M, N, ldc);
         return cudaGetLastError();
     }
-    gemm_bf16_tn_kernel<BN, false><<<ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream>>>(
-        ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K, ldc, err_flag, nullptr, 1);
+    launch_pdl(gemm_bf16_tn_kernel<BN, false>, ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K, ldc, err_flag, nullptr, 1);
     return cudaGetLastError();
 }
 

@@ -133,6 +133,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// Programmatic dependent launch: a kernel launched with the stream-serialisation attribute may start while
+// its predecessor drains.  pdl_enter() is the first statement of every prefill kernel: it lets the next kernel
+// in the stream be scheduled early and then waits until the predecessor has completed and its writes are
+// visible, so no kernel touches its inputs before they exist.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---- math helpers ------------------------------------------------------------------------
 
 __device__ __forceinline__ float warp_sum(float v) {

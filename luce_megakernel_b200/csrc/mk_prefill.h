@@ -7,6 +7,19 @@
 
 namespace mk {
 
+// Launch with programmatic stream serialisation (the kernels call pdl_enter() first): launch latency and the
+// next kernel's set-up overlap the tail of the previous kernel.  A prompt of 520 tokens is ~310 short kernels.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid; cfg.blockDim = block; cfg.dynamicSmemBytes = smem; cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // C[M,N] = A[M,K] . W[N,K]^T (+ R[M,N]); bf16 row-major, f32 accumulate; tcgen05 / TMEM / TMA.
 // N % 128 == 0, K % 64 == 0, lda and ldc multiples of 8 elements, pointers 16-byte aligned.
 // err_flag: device int, set to 1 if a bounded wait ran out inside the kernel.

@@ -31,6 +31,7 @@ __device__ __forceinline__ float ld_bf(const __nv_bfloat16* p) { return __bfloat
 
 __global__ void k_embed(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ embed,
                         __nv_bfloat16* __restrict__ hidden, int S, int vocab) {
+    pdl_enter();
     const int t = blockIdx.x;
     int id = tok[t];
     id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
@@ -42,6 +43,7 @@ __global__ void k_embed(const int* __restrict__ tok, const __nv_bfloat16* __rest
 // one warp per row: out = bf16( x * rsqrt(mean x^2 + eps) * (1 + w) )   (reference: prefill.cu:72-88)
 __global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                           __nv_bfloat16* __restrict__ out, int S) {
+    pdl_enter();
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= S) return;
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)row * HIDDEN);
@@ -81,6 +83,7 @@ __global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bfloat
 __global__ void k_dn_gates(const __nv_bfloat16* __restrict__ xn, const __nv_bfloat16* __restrict__ Wb,
                            const __nv_bfloat16* __restrict__ Wa, const __nv_bfloat16* __restrict__ a_log,
                            const __nv_bfloat16* __restrict__ dt_bias, float* __restrict__ beta, float* __restrict__ decay, int S) {
+    pdl_enter();
     const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (wid >= S * 32) return;
     const int t = wid >> 5, o = wid & 31, h = o & 15;
@@ -112,6 +115,7 @@ __global__ void k_dn_gates(const __nv_bfloat16* __restrict__ xn, const __nv_bflo
 // from the stored conv window.  Also leaves q.k per (t, head).  (reference: prefill.cu:1281-1368)
 __global__ void k_dn_preproject(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ conv_w,
                                 const float* __restrict__ conv_state, float* __restrict__ pre, float* __restrict__ kq, int S) {
+    pdl_enter();
     const int t = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
     __shared__ float red[3][4];
     float val[3];
@@ -145,6 +149,7 @@ __global__ void k_dn_preproject(const __nv_bfloat16* __restrict__ qkv, const __n
 
 // conv window after the prompt: the last four pre-activation inputs (reference: prefill.cu:1373-1395)
 __global__ void k_dn_conv_state(const __nv_bfloat16* __restrict__ qkv, float* __restrict__ conv_state, int S) {
+    pdl_enter();
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     if (ch >= DN_CONV_CH) return;
     float old[4], nw[4];
@@ -176,6 +181,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 // gates: [t][head][4] = beta, decay, q.k, log decay
 __global__ void __launch_bounds__(512) k_dn_scan(const float* __restrict__ pre, const float* __restrict__ gates,
                                                  float* __restrict__ state, float* __restrict__ o, int S) {
+    pdl_enter();
     extern __shared__ __align__(16) float scan_sm[];
     const int h = blockIdx.x >> 3, slice = blockIdx.x & 7;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -236,6 +242,7 @@ __global__ void __launch_bounds__(512) k_dn_scan(const float* __restrict__ pre, 
 // y = o * rsqrt(mean o^2 + eps) * w * silu(z), one warp per (t, head) (reference: prefill.cu:1493-1523)
 __global__ void k_dn_gated_norm(const float* __restrict__ o, const __nv_bfloat16* __restrict__ z,
                                 const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int S) {
+    pdl_enter();
     const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (wid >= S * DN_HEADS) return;
     const float4 o4 = reinterpret_cast<const float4*>(o + (size_t)wid * DN_VAL)[lane];
@@ -260,6 +267,7 @@ __global__ void k_dn_gated_norm(const float* __restrict__ o, const __nv_bfloat16
 __global__ void k_fa_norm_rope(__nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ q_norm,
                                const __nv_bfloat16* __restrict__ k_norm, __nv_bfloat16* __restrict__ kc,
                                __nv_bfloat16* __restrict__ vc, int S, int max_seq) {
+    pdl_enter();
     const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (wid >= S * 12) return;
     const int t = wid / 12, slot = wid % 12;
@@ -294,6 +302,7 @@ __global__ void k_fa_norm_rope(__nv_bfloat16* __restrict__ qkv, const __nv_bfloa
 
 // act[t, i] = silu(gu[t, i]) * gu[t, 3584 + i]   (reference: prefill.cu:1239-1247)
 __global__ void k_silu_mul(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ act, int S) {
+    pdl_enter();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;     // one thread per 8 outputs
     if (i >= (size_t)S * (INTER / 8)) return;
     const size_t t = i / (INTER / 8), c = (i % (INTER / 8)) * 8;
@@ -313,6 +322,7 @@ __global__ void k_silu_mul(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* 
 __global__ void k_final_norm(const __nv_bfloat16* __restrict__ hidden_last, const __nv_bfloat16* __restrict__ w,
                              float* __restrict__ normed_f32, __nv_bfloat16* __restrict__ normed_bf16,
                              __nv_bfloat16* __restrict__ hidden_out) {
+    pdl_enter();
     __shared__ float red[32];
     float v[2], ss = 0.f;
     for (int i = 0; i < 2; ++i) { v[i] = ld_bf(hidden_last + threadIdx.x + 512 * i); ss += v[i] * v[i]; }
@@ -334,6 +344,7 @@ __global__ void k_final_norm(const __nv_bfloat16* __restrict__ hidden_last, cons
 // logits = W x, per-block argmax (lowest index on ties) (reference: prefill.cu:314-339)
 __global__ void __launch_bounds__(256) k_lm_head(const float* __restrict__ x, const __nv_bfloat16* __restrict__ W, int vocab,
                                                  float* __restrict__ bval, int* __restrict__ bidx) {
+    pdl_enter();
     __shared__ float sv[8];
     __shared__ int si[8];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -364,6 +375,7 @@ __global__ void __launch_bounds__(256) k_lm_head(const float* __restrict__ x, co
 }
 
 __global__ void k_lm_reduce(const float* __restrict__ bval, const int* __restrict__ bidx, int n, int* __restrict__ out) {
+    pdl_enter();
     float best = -INFINITY;
     int besti = 0x7fffffff;
     for (int i = threadIdx.x; i < n; i += 32) {
@@ -490,6 +502,7 @@ LayerView view_of(const LayerWeights& lw, const void* fused_faqkv, const void* f
 
 // greedy argmax over a logit vector, lowest index on ties (one block)
 __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logits, int n, int* __restrict__ out) {
+    pdl_enter();
     __shared__ float sv[32];
     __shared__ int si[32];
     float best = -INFINITY;
@@ -523,6 +536,7 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
 // unlike the decode kernel, which multiplies the exact dequantised value, the prefill carries this rounding.
 __global__ void k_dequant_a_bf16(const uint8_t* __restrict__ packed, const __half* __restrict__ scales,
                                  __nv_bfloat16* __restrict__ out, size_t n8, int cols) {
+    pdl_enter();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n8) return;
     const size_t e0 = i * 8, row = e0 / cols;
@@ -566,29 +580,28 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
     const int wpb = 8;                                            // warps per 256-thread block
     auto blocks_for_warps = [&](long long nw) { return (unsigned)((nw + wpb - 1) / wpb); };
 
-    k_embed<<<S, 128, 0, stream>>>(token_ids, (const bf*)embed_weight, w.hidden, S, vocab);
+    launch_pdl(k_embed, S, 128, 0, stream, token_ids, (const bf*)embed_weight, w.hidden, S, vocab);
     int dn_idx = 0, fa_idx = 0;
     for (int li = 0; li < num_layers; ++li) {
         LayerView lv;
         const int rc = source(li, lv);
         if (rc != MK_OK) return rc;
         const bool dn = (lv.type == 0);
-        k_rmsnorm<<<blocks_for_warps(S), 256, 0, stream>>>(w.hidden, (const bf*)lv.in_norm, w.normed, S);
+        launch_pdl(k_rmsnorm, blocks_for_warps(S), 256, 0, stream, w.hidden, (const bf*)lv.in_norm, w.normed, S);
         if (dn) {
             float* state = (float*)dn_states + (size_t)dn_idx * DN_HEADS * DN_VAL * DN_KEY;
             float* cstate = (float*)conv_bufs + (size_t)dn_idx * DN_CONV_CH * DN_CONV_K;
             PF_CHECK(gemm(w.normed, lv.w_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
             PF_CHECK(gemm(w.normed, lv.w_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
-            k_dn_gates<<<blocks_for_warps((long long)S * 32), 256, 0, stream>>>(
-                w.normed, (const bf*)lv.w_b, (const bf*)lv.w_a, (const bf*)lv.a_log, (const bf*)lv.dt_bias, w.beta, w.beta, S);
+            launch_pdl(k_dn_gates, blocks_for_warps((long long)S * 32), 256, 0, stream, w.normed, (const bf*)lv.w_b, (const bf*)lv.w_a, (const bf*)lv.a_log, (const bf*)lv.dt_bias, w.beta, w.beta, S);
             if (g_scan_mode == 0) {
-                k_dn_preproject<<<dim3(S, DN_HEADS), 128, 0, stream>>>(w.wide, (const bf*)lv.conv_w, cstate, w.pre, w.beta, S);
-                k_dn_scan<<<128, 512, SCAN_SMEM, stream>>>(w.pre, w.beta, state, w.o, S);
+                launch_pdl(k_dn_preproject, dim3(S, DN_HEADS), 128, 0, stream, w.wide, (const bf*)lv.conv_w, cstate, w.pre, w.beta, S);
+                launch_pdl(k_dn_scan, 128, 512, SCAN_SMEM, stream, w.pre, w.beta, state, w.o, S);
             } else {
                 PF_CHECK(dn_chunked(w.wide, lv.conv_w, cstate, w.beta, state, w.o, S, w.chunk_scratch, w.err, stream), "chunked scan");
             }
-            k_dn_conv_state<<<(DN_CONV_CH + 255) / 256, 256, 0, stream>>>(w.wide, cstate, S);
-            k_dn_gated_norm<<<blocks_for_warps((long long)S * DN_HEADS), 256, 0, stream>>>(w.o, w.z, (const bf*)lv.dn_norm, w.act, S);
+            launch_pdl(k_dn_conv_state, (DN_CONV_CH + 255) / 256, 256, 0, stream, w.wide, cstate, S);
+            launch_pdl(k_dn_gated_norm, blocks_for_warps((long long)S * DN_HEADS), 256, 0, stream, w.o, w.z, (const bf*)lv.dn_norm, w.act, S);
             PF_CHECK(gemm(w.act, lv.w_out, w.hidden, w.hidden, HIDDEN, DN_V, HIDDEN), "gemm out");
             ++dn_idx;
         } else {
@@ -601,8 +614,7 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
                 PF_CHECK(gemm(w.normed, lv.w_k, w.wide + FA_QPROJ, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm k");
                 PF_CHECK(gemm(w.normed, lv.w_v, w.wide + FA_QPROJ + FA_KV_SIZE, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm v");
             }
-            k_fa_norm_rope<<<blocks_for_warps((long long)S * 12), 256, 0, stream>>>(
-                w.wide, (const bf*)lv.q_norm, (const bf*)lv.k_norm, kc, vc, S, max_seq_len);
+            launch_pdl(k_fa_norm_rope, blocks_for_warps((long long)S * 12), 256, 0, stream, w.wide, (const bf*)lv.q_norm, (const bf*)lv.k_norm, kc, vc, S, max_seq_len);
             const uint32_t* bmask = nullptr;
             if (g_sparse.enabled) {
                 uint32_t* m = nullptr;
@@ -614,17 +626,17 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
             PF_CHECK(gemm(w.act, lv.w_o, w.hidden, w.hidden, HIDDEN, FA_Q_SIZE, HIDDEN), "gemm o");
             ++fa_idx;
         }
-        k_rmsnorm<<<blocks_for_warps(S), 256, 0, stream>>>(w.hidden, (const bf*)lv.post_norm, w.normed, S);
+        launch_pdl(k_rmsnorm, blocks_for_warps(S), 256, 0, stream, w.hidden, (const bf*)lv.post_norm, w.normed, S);
         if (lv.w_gateup) {
             PF_CHECK(gemm(w.normed, lv.w_gateup, w.wide, nullptr, 2 * INTER, HIDDEN, 2 * INTER), "gemm gate_up");
         } else {
             PF_CHECK(gemm(w.normed, lv.w_gate, w.wide, nullptr, INTER, HIDDEN, 2 * INTER), "gemm gate");
             PF_CHECK(gemm(w.normed, lv.w_up, w.wide + INTER, nullptr, INTER, HIDDEN, 2 * INTER), "gemm up");
         }
-        k_silu_mul<<<(unsigned)(((size_t)S * (INTER / 8) + 255) / 256), 256, 0, stream>>>(w.wide, w.act, S);
+        launch_pdl(k_silu_mul, (unsigned)(((size_t)S * (INTER / 8) + 255) / 256), 256, 0, stream, w.wide, w.act, S);
         PF_CHECK(gemm(w.act, lv.w_down, w.hidden, w.hidden, HIDDEN, INTER, HIDDEN), "gemm down");
     }
-    k_final_norm<<<1, 512, 0, stream>>>(w.hidden + (size_t)(S - 1) * HIDDEN, (const bf*)final_norm_w, w.normed_f32,
+    launch_pdl(k_final_norm, 1, 512, 0, stream, w.hidden + (size_t)(S - 1) * HIDDEN, (const bf*)final_norm_w, w.normed_f32,
                                         (bf*)final_normed, (bf*)hidden_bf16_out);
     if (lm.packed) {
         // NVFP4 LM head (16-block / E4M3 format): logits by the in-register dequantising row product, then argmax
@@ -632,10 +644,10 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
         if (vocab > 2 * DEFAULT_VOCAB) return pfail(MK_ERR_BAD_ARG, "vocabulary too large for the logits buffer");
         if (mk_matvec_nvfp4(1, lm.packed, lm.scales, w.normed_f32, g_logits[dev], vocab, HIDDEN, 16, stream) != MK_OK)
             return pfail(MK_ERR_BAD_ARG, mk_nvfp4_error());
-        k_argmax<<<1, 1024, 0, stream>>>(g_logits[dev], vocab, output_token);
+        launch_pdl(k_argmax, 1, 1024, 0, stream, g_logits[dev], vocab, output_token);
     } else {
-        k_lm_head<<<LM_BLOCKS, 256, 0, stream>>>(w.normed_f32, (const bf*)lm.bf16, vocab, w.bval, w.bidx);
-        k_lm_reduce<<<1, 32, 0, stream>>>(w.bval, w.bidx, LM_BLOCKS, output_token);
+        launch_pdl(k_lm_head, LM_BLOCKS, 256, 0, stream, w.normed_f32, (const bf*)lm.bf16, vocab, w.bval, w.bidx);
+        launch_pdl(k_lm_reduce, 1, 32, 0, stream, w.bval, w.bidx, LM_BLOCKS, output_token);
     }
     PF_CHECK(cudaGetLastError(), "prefill launch");
     return MK_OK;
@@ -759,7 +771,7 @@ extern "C" int mk_prefill_nvfp4(
     }
     auto deq = [&](const void* packed, const void* scales, __nv_bfloat16* out, int rws, int cols) {
         const size_t n8 = (size_t)rws * cols / 8;
-        k_dequant_a_bf16<<<(unsigned)((n8 + 255) / 256), 256, 0, stream>>>((const uint8_t*)packed, (const __half*)scales, out, n8, cols);
+        launch_pdl(k_dequant_a_bf16, (unsigned)((n8 + 255) / 256), 256, 0, stream, (const uint8_t*)packed, (const __half*)scales, out, n8, cols);
     };
     // slots of the 208-byte table (reference: megakernel/model_nvfp4.py:274-311)
     auto source = [&](int li, LayerView& lv) {
