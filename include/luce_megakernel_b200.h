@@ -234,6 +234,9 @@ int mk_prefill_nvfp4(
  * (reference: the chunked kernels megakernel/prefill.cu:355-680), 0 = token-serial recurrence
  * (reference: megakernel/prefill.cu:114-221).  Both give the same result up to rounding. */
 void mk_prefill_set_scan_mode(int chunked);
+/* Dense prefill attention kernel: 1 = tcgen05 / TMEM kernel, 0 = mma.sync kernel (the block-sparse mode always
+ * uses the mma.sync kernel).  Both compute softmax(q k^T / 16) v * sigmoid(gate). */
+void mk_prefill_set_attention_impl(int tcgen05);
 /* The prefill keeps a host copy of each layer pointer table it has seen (keyed by device and table address), as
  * the reference does (megakernel/prefill.cu:1578-1584).  Call this after rewriting a table in place. */
 void mk_prefill_forget_tables(void);

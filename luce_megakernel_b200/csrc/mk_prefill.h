@@ -43,6 +43,11 @@ cudaError_t dn_chunked(const void* qkv, const void* conv_w, const float* conv_st
 cudaError_t fa_prefill(const void* qkv, const void* kc, const void* vc, void* out, int S, int max_seq, const uint32_t* mask,
                        cudaStream_t stream);
 
+// The same attention (dense, or block-sparse with a mask) on tcgen05 / TMEM (TMA-fed, scores and P.V as tcgen05.mma, softmax one thread per row).
+// err: device int, set to 3 if a bounded wait ran out.
+cudaError_t fa_prefill_tcgen05(const void* qkv, const void* kc, const void* vc, void* out, int S, int max_seq, int* err,
+                               const uint32_t* mask, cudaStream_t stream);
+
 // Block selection for sparse attention over 128 x 128 blocks: keep the first `sink` key blocks, the `window`
 // most recent ones and the ceil(top_frac * causal blocks) best by mean-pooled q . mean-pooled k, per query head.
 // scratch: block_select_scratch_bytes(S); *mask_out points into it: uint32 [8][blocks][ceil(blocks / 32)].

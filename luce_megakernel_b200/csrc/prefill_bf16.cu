@@ -438,6 +438,7 @@ HostTable g_tables[64];
 thread_local char g_perr[200] = "";
 struct SparseCfg { bool enabled = false; double top_frac = 0.10; int window = 4, sink = 1; };
 SparseCfg g_sparse;
+int g_attn_impl = 1;              // attention kernel: 1 = tcgen05 / TMEM (default), 0 = mma.sync
 int g_scan_mode = 1;              // 1 = chunks of 64 on the tensor cores, 0 = token-serial recurrence
 int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
     if (e != cudaSuccess) snprintf(g_perr, sizeof(g_perr), "%s: %s", what, cudaGetErrorString(e));
@@ -462,6 +463,7 @@ extern "C" int mk_prefill_set_block_sparse(int enable, double top_frac, int wind
     if (enable) { mk::g_sparse.top_frac = top_frac; mk::g_sparse.window = window; mk::g_sparse.sink = sink; }
     return MK_OK;
 }
+extern "C" void mk_prefill_set_attention_impl(int tcgen05) { mk::g_attn_impl = tcgen05 ? 1 : 0; }
 extern "C" void mk_prefill_set_scan_mode(int chunked) { mk::g_scan_mode = chunked ? 1 : 0; }
 
 namespace mk {
@@ -622,7 +624,8 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
                                       w.select_scratch, &m, stream), "block selection");
                 bmask = m;
             }
-            PF_CHECK(fa_prefill(w.wide, kc, vc, w.act, S, max_seq_len, bmask, stream), "attention");
+            if (g_attn_impl == 1) PF_CHECK(fa_prefill_tcgen05(w.wide, kc, vc, w.act, S, max_seq_len, w.err, bmask, stream), "attention");
+            else PF_CHECK(fa_prefill(w.wide, kc, vc, w.act, S, max_seq_len, bmask, stream), "attention");
             PF_CHECK(gemm(w.act, lv.w_o, w.hidden, w.hidden, HIDDEN, FA_Q_SIZE, HIDDEN), "gemm o");
             ++fa_idx;
         }
@@ -919,6 +922,14 @@ extern "C" int mk_attention_prefill(const void* qkv, const void* k_cache, const 
                                     const unsigned int* mask, cudaStream_t stream) {
     using namespace mk;
     if (!qkv || !k_cache || !v_cache || !out || seq_len < 1 || seq_len > max_seq_len) return pfail(MK_ERR_BAD_ARG, "bad argument");
-    PF_CHECK(fa_prefill(qkv, k_cache, v_cache, out, seq_len, max_seq_len, mask, stream), "attention");
+    if (g_attn_impl == 1) {
+        int dev = 0;
+        PF_CHECK(cudaGetDevice(&dev), "cudaGetDevice");
+        PrefillWs& w = g_pws[dev < 0 || dev >= 64 ? 0 : dev];
+        PF_CHECK(ensure_ws(w, 1), "prefill workspace");
+        PF_CHECK(fa_prefill_tcgen05(qkv, k_cache, v_cache, out, seq_len, max_seq_len, w.err, mask, stream), "attention");
+    } else {
+        PF_CHECK(fa_prefill(qkv, k_cache, v_cache, out, seq_len, max_seq_len, mask, stream), "attention");
+    }
     return MK_OK;
 }

@@ -129,6 +129,34 @@ def test_attention_matches_torch(S, sparse):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("impl", [0, 1])
+def test_attention_with_growing_scores(impl):
+    """Scores that grow along the sequence force the running maximum up tile after tile: the tensor-memory
+    kernel rescales its output accumulator (a warp-wide TMEM round trip) every few tiles."""
+    import luce_megakernel_b200 as L
+    lib = L.lib()
+    S = 1100
+    qkv, kc, vc = _make(S, 31)
+    ramp = (torch.arange(S, dtype=torch.float32) / S * 6.0)[:, None]
+    qkv[:, :4096] = (qkv[:, :4096].float() * 0.2 + 0.5).to(torch.bfloat16)             # queries with a common direction
+    kc[:, :S] = (kc[:, :S].float() * 0.2 + ramp[None]).to(torch.bfloat16)               # keys growing with position
+    qkv[:, 4096:4608] = kc[:, :S].transpose(0, 1).reshape(S, 512)
+    dq, dk, dv = qkv.cuda(), kc.cuda(), vc.cuda()
+    out = torch.empty(S, 2048, dtype=torch.bfloat16, device="cuda")
+    lib.mk_prefill_set_attention_impl(impl)
+    try:
+        rc = lib.mk_attention_prefill(_ptr(dq), _ptr(dk), _ptr(dv), _ptr(out), S, S, _ptr(None),
+                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+    finally:
+        lib.mk_prefill_set_attention_impl(1)
+    assert rc == 0 and lib.mk_device_status() == 0
+    ref = _torch_attention(qkv, kc, vc, S)
+    err = float((out.float().cpu() - ref).abs().max())
+    assert err <= 3e-2, f"attention error {err}"
+
+
+@pytest.mark.gpu
 def test_keeping_every_block_equals_dense():
     import luce_megakernel_b200 as L
     lib = L.lib()
