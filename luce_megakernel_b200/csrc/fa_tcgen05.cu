@@ -5,8 +5,9 @@
 //   warp 1      one thread issues tcgen05.mma: S = Q K^T (M128 N64, K = 256 in 16 steps) into one of two score
 //               buffers in tensor memory, and O += P V (M128 N256, K = 64 in 4 steps; V is read MN-major, i.e.
 //               as it lies in the cache: keys x dims)
-//   warps 2-5   softmax, one thread per row: tcgen05.ld the 64 scores, running maximum and sum, probabilities
-//               rounded to bf16 into shared memory (the A operand of P V), and the epilogue
+//   warps 2-9   softmax, two threads per row (warps 2-5 take score columns 0-31, warps 6-9 columns 32-63 of the
+//               same TMEM lanes): tcgen05.ld the scores, running maximum (exchanged through shared memory) and
+//               sum, probabilities rounded to bf16 into shared memory (the A operand of P V), and the epilogue
 // The score MMA of tile j+1 is issued before the P V MMA of tile j, so the tensor pipe works while the softmax
 // threads process tile j.  The output accumulator is rescaled only when a row maximum grows by more than 2^8
 // since the last rescale (probabilities then stay below 2^8, exact enough in bf16/f32): with a causal mask the
@@ -34,7 +35,8 @@ constexpr int OFF_K = OFF_Q + Q_BYTES;                     // 2 stages
 constexpr int OFF_V = OFF_K + 2 * KV_BYTES;                // 2 stages
 constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
 constexpr int OFF_BARS = OFF_P + P_BYTES;
-constexpr int OFF_LIST = OFF_BARS + 256;                   // block-sparse mode: up to 2048 tile ids (u16)
+constexpr int OFF_LIST = OFF_BARS + 160 + 2048;            // after the barriers and the 2 x 2 x 128 floats of row-maximum exchange;
+                                                           // block-sparse mode: up to 2048 tile ids (u16)
 constexpr int FA5_SMEM = OFF_LIST + 4096 + 1024;           // + alignment slack
 constexpr uint32_t TM_COLS = 512;
 constexpr uint32_t TM_S0 = 0, TM_O = 128;                  // score buffers at columns 0 and 64, output at 128..383
@@ -94,10 +96,19 @@ __device__ __forceinline__ bool waitb(uint32_t bar, uint32_t parity, int* err) {
                    "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]), "r"(v[55]), "r"(v[56]), "r"(v[57]), "r"(v[58]), "r"(v[59]),  \
                    "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63]), "r"(taddr) : "memory")
 
+#define TM_LD32(taddr, v)                                                                                              \
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "                                                            \
+                 "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];" \
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]),   \
+                   "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),    \
+                   "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),   \
+                   "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])                                                                      \
+                 : "r"(taddr) : "memory")
+
 // map_q: 2-D view of the qkv buffer restricted to the query heads: (dims 0..4095, tokens), box 64 x 32;
 // map_k0/1, map_v0/1: 2-D views of the two KV heads of one layer's cache: (256 dims, S rows), box 64 x 64; rows
 // past the prompt read as zeros, so stale cache contents never meet a zero probability.
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
 k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k0,
              const __grid_constant__ CUtensorMap map_k1, const __grid_constant__ CUtensorMap map_v0,
              const __grid_constant__ CUtensorMap map_v1, const __nv_bfloat16* __restrict__ qkv,
@@ -145,9 +156,9 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
         mbar_init(q_full, 1);
         for (int s = 0; s < 2; ++s) {
             mbar_init(kv_full0 + 8 * s, 1); mbar_init(kv_empty0 + 8 * s, 1);
-            mbar_init(s_full0 + 8 * s, 1); mbar_init(s_empty0 + 8 * s, 128);
+            mbar_init(s_full0 + 8 * s, 1); mbar_init(s_empty0 + 8 * s, 256);
         }
-        mbar_init(p_full, 128); mbar_init(pv_done, 1);
+        mbar_init(p_full, 256); mbar_init(pv_done, 1);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -222,89 +233,104 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
         }
     } else {
         const int r = (warp & 3) * 32 + lane;                 // row = TMEM lane
+        const int half = (warp - 2) >> 2;                      // which 32 of the tile's 64 score columns
         const int hh = r >> 5, qi = r & 31, qpos = q0 + qi;
         const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const float sc = 0.0625f * 1.4426950408889634f;       // 1/sqrt(256) * log2(e)
+        float* xbuf = reinterpret_cast<float*>(smem + OFF_BARS + 160);      // [tile parity][2 halves][128 rows]
         float m_ref = -1e30f, lsum = 0.f;
-        for (int j = 0; j < ntiles && ok; ++j) {
+        // A wait that ran out must not make one warp leave the loop while the others sit in the named barrier
+        // below: from then on this warp skips every wait (its results are garbage, *err is set) but keeps step.
+        bool dead = false;
+        auto wait_all = [&](uint32_t bar, uint32_t parity) {
+            if (!dead && !__all_sync(0xffffffffu, waitb(bar, parity, err))) dead = true;
+        };
+        for (int j = 0; j < ntiles; ++j) {
             const int s = j & 1;
-            ok = __all_sync(0xffffffffu, waitb(s_full0 + 8 * s, (j >> 1) & 1, err));
-            if (!ok) break;
+            float* xmax = xbuf + (j & 1) * 256;
+            wait_all(s_full0 + 8 * s, (j >> 1) & 1);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            uint32_t v[64];
-            TM_LD64(lane_addr + TM_S0 + s * TK, v);
+            uint32_t v[32];
+            TM_LD32(lane_addr + TM_S0 + s * TK + half * 32, v);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(s_empty0 + 8 * s);
-            const int tj = tile_of(j), key0 = tj * TK;
+            const int tj = tile_of(j), key0 = tj * TK + half * 32;
             const bool dropped = mask && !((m0[hh * hstride + (tj >> 6)] >> ((tj >> 1) & 31)) & 1u);   // this head dropped the block
-            float tmax = -1e30f;
+            float hmax = -1e30f;
 #pragma unroll
-            for (int k = 0; k < 64; ++k) {
+            for (int k = 0; k < 32; ++k) {
                 float x = __uint_as_float(v[k]) * sc;
                 if (key0 + k > qpos || dropped) x = -1e30f;
                 v[k] = __float_as_uint(x);
-                tmax = fmaxf(tmax, x);
+                hmax = fmaxf(hmax, x);
             }
+            // row maximum over both halves
+            xmax[half * 128 + r] = hmax;
+            named_bar_sync(1, 256);
+            const float tmax = fmaxf(hmax, xmax[(half ^ 1) * 128 + r]);
             // the previous P V must be complete before P is overwritten or O rescaled
             if (j >= 1) {
-                ok = __all_sync(0xffffffffu, waitb(pv_done, (j - 1) & 1, err));
-                if (!ok) break;
+                wait_all(pv_done, (j - 1) & 1);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             }
             // tcgen05.ld / st are warp-wide: the decision to rescale is taken per warp, every lane takes part
-            // with its own factor (1 for a row whose maximum did not move)
+            // with its own factor (1 for a row whose maximum did not move); each half rescales 128 output columns
             const bool grow = tmax > m_ref + 8.0f;
             if (__any_sync(0xffffffffu, grow)) {
                 if (j >= 1) {
                     const float f = grow ? exp2f(m_ref - tmax) : 1.0f;
                     lsum *= f;
 #pragma unroll 1
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < 2; ++c) {
                         uint32_t o[64];
-                        TM_LD64(lane_addr + TM_O + c * 64, o);
+                        TM_LD64(lane_addr + TM_O + half * 128 + c * 64, o);
                         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
                         for (int k = 0; k < 64; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
-                        TM_ST64(lane_addr + TM_O + c * 64, o);
+                        TM_ST64(lane_addr + TM_O + half * 128 + c * 64, o);
                     }
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 }
                 if (grow) m_ref = tmax;
             }
-            // probabilities -> bf16 row of the P tile (128-byte rows, 16-byte pieces xor (row & 7))
+            // probabilities -> bf16 half row of the P tile (128-byte rows, 16-byte pieces xor (row & 7))
             char* prow = smem + OFF_P + r * 128;
 #pragma unroll
-            for (int c8 = 0; c8 < 8; ++c8) {
+            for (int c4 = 0; c4 < 4; ++c4) {
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float p0 = dropped ? 0.f : exp2f(__uint_as_float(v[c8 * 8 + 2 * e]) - m_ref);
-                    const float p1 = dropped ? 0.f : exp2f(__uint_as_float(v[c8 * 8 + 2 * e + 1]) - m_ref);
+                    const float p0 = exp2f(__uint_as_float(v[c4 * 8 + 2 * e]) - m_ref);
+                    const float p1 = exp2f(__uint_as_float(v[c4 * 8 + 2 * e + 1]) - m_ref);
                     const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
                     w[e] = *reinterpret_cast<const uint32_t*>(&pp);
                     lsum += bf_lo(w[e]) + bf_hi(w[e]);
                 }
-                *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(prow + (((half * 4 + c4) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
             fence_proxy_async();
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(p_full);
         }
-        // epilogue: O / l * sigmoid(gate) -> bf16
-        if (ok) ok = __all_sync(0xffffffffu, waitb(pv_done, (ntiles - 1) & 1, err));
-        if (ok) {
+        // epilogue: O / l * sigmoid(gate) -> bf16; the row sum is the two halves' sums
+        wait_all(pv_done, (ntiles - 1) & 1);
+        float* xsum = xbuf + (ntiles & 1) * 256;
+        xsum[half * 128 + r] = lsum;
+        named_bar_sync(1, 256);
+        if (!dead) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const float inv = 1.0f / lsum;
+            const float inv = 1.0f / (lsum + xsum[(half ^ 1) * 128 + r]);
             const int head = g * 4 + hh;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t o[64];
-                TM_LD64(lane_addr + TM_O + c * 64, o);
+                const int col0 = half * 128 + c * 64;
+                TM_LD64(lane_addr + TM_O + col0, o);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (qpos < S) {
-                    const __nv_bfloat16* gate = qkv + (size_t)qpos * FA_QKV_ROWS + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM + c * 64;
-                    __nv_bfloat16* dst = out + (size_t)qpos * FA_Q_SIZE + head * FA_HEAD_DIM + c * 64;
+                    const __nv_bfloat16* gate = qkv + (size_t)qpos * FA_QKV_ROWS + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM + col0;
+                    __nv_bfloat16* dst = out + (size_t)qpos * FA_Q_SIZE + head * FA_HEAD_DIM + col0;
 #pragma unroll
                     for (int k8 = 0; k8 < 8; ++k8) {
                         const uint4 gu = *reinterpret_cast<const uint4*>(gate + k8 * 8);
@@ -377,7 +403,7 @@ cudaError_t fa_prefill_tcgen05(const void* qkv, const void* kc, const void* vc, 
         !map2d(&k1, K + head, FA_HEAD_DIM, (uint64_t)S, FA_HEAD_DIM, TK) || !map2d(&v0, V, FA_HEAD_DIM, (uint64_t)S, FA_HEAD_DIM, TK) ||
         !map2d(&v1, V + head, FA_HEAD_DIM, (uint64_t)S, FA_HEAD_DIM, TK))
         return cudaErrorInvalidValue;
-    return launch_pdl(k_fa_tcgen05, dim3((S + TQ - 1) / TQ, FA_KV_HEADS), 192, FA5_SMEM, stream, mq, k0, k1, v0, v1,
+    return launch_pdl(k_fa_tcgen05, dim3((S + TQ - 1) / TQ, FA_KV_HEADS), 320, FA5_SMEM, stream, mq, k0, k1, v0, v1,
                       (const __nv_bfloat16*)qkv, (__nv_bfloat16*)out, S, err, mask, nblk, nwords);
 }
 
