@@ -290,7 +290,7 @@ def main():
                 lib().mk_prefill_set_block_sparse(0, ctypes.c_double(0.10), 4, 1)
             long_pp.append((S_, p0.elapsed_time(p1) / 2, sparse))
             del d2
-        if lib().mk_device_status() != 0:
+        if lib().mk_device_status() != 0 or lib().mk_prefill_status() != 0:
             raise SystemExit("device-side wait timed out during the long prefill")
 
     t_all = torch.tensor([ms, e2e_s, pp_ms], dtype=torch.float64, device="cuda")

@@ -237,6 +237,10 @@ void mk_prefill_set_scan_mode(int chunked);
 /* Dense prefill attention kernel: 1 = tcgen05 / TMEM kernel, 0 = mma.sync kernel (the block-sparse mode always
  * uses the mma.sync kernel).  Both compute softmax(q k^T / 16) v * sigmoid(gate). */
 void mk_prefill_set_attention_impl(int tcgen05);
+/* Status word of the prefill kernels on the current device (synchronises the device): 0 = every bounded wait
+ * inside the kernels completed; 1 / 2 / 3 = a wait ran out in a GEMM / the chunk scan / the attention kernel
+ * (the affected prefill's results are invalid). */
+int mk_prefill_status(void);
 /* The prefill keeps a host copy of each layer pointer table it has seen (keyed by device and table address), as
  * the reference does (megakernel/prefill.cu:1578-1584).  Call this after rewriting a table in place. */
 void mk_prefill_forget_tables(void);

@@ -463,6 +463,17 @@ extern "C" int mk_prefill_set_block_sparse(int enable, double top_frac, int wind
     if (enable) { mk::g_sparse.top_frac = top_frac; mk::g_sparse.window = window; mk::g_sparse.sink = sink; }
     return MK_OK;
 }
+// Status word of the prefill kernels on the current device: 0 = no bounded wait has run out; 1 = a GEMM wait,
+// 2 = a chunk-scan wait, 3 = an attention wait.  Synchronises the device (it reads device memory).
+extern "C" int mk_prefill_status(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    mk::PrefillWs& w = mk::g_pws[dev];
+    if (!w.err) return 0;
+    int v = 0;
+    if (cudaMemcpy(&v, w.err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    return v;
+}
 extern "C" void mk_prefill_set_attention_impl(int tcgen05) { mk::g_attn_impl = tcgen05 ? 1 : 0; }
 extern "C" void mk_prefill_set_scan_mode(int chunked) { mk::g_scan_mode = chunked ? 1 : 0; }
 

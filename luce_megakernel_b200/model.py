@@ -269,7 +269,11 @@ class Decoder:
     def prefill(self, token_ids) -> int:
         """Process a whole prompt from position 0 (state must be reset); returns the first generated
         token.  Afterwards step()/step_many() continue from position len(token_ids)."""
-        return int(self.prefill_async(token_ids).item())
+        tok = int(self.prefill_async(token_ids).item())
+        st = self._lib.mk_prefill_status()
+        if st != 0:
+            raise RuntimeError(f"a bounded wait ran out inside a prefill kernel (status {st})")
+        return tok
 
     def prefill_async(self, token_ids):
         """prefill() without the device-to-host read: returns the int32[1] device tensor that will hold
