@@ -128,3 +128,31 @@ def test_gemm_against_torch():
         assert err <= 2 * bf16_ulp(float(ref.abs().max())), (M_, N_, K_, err)
     assert lib.mk_gemm_bf16_tn(ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(W.data_ptr()), ctypes.c_void_p(C.data_ptr()),
                                ctypes.c_void_p(0), 8, 100, 64, None) == 1
+
+
+def test_decode_after_long_prefill(small_model):
+    """Context beyond 1024 positions: the decode kernel's attention units then hold more than one 64-key tile
+    (online softmax across tiles inside a unit, 16 units per KV head).  The prompt goes through the prefill,
+    then three decode steps are compared with the oracle run over the whole sequence."""
+    from luce_megakernel_b200 import model as M
+    sd, orc = small_model("unit", "decode")
+    _, o32 = small_model("unit", "none")
+    S, steps, maxseq = 1500, 3, 1600
+    dec = M.Decoder(weights=M.weights_from_state_dict(sd), max_seq_len=maxseq, api="cabi")
+    toks = prompt(S, 77)
+    tok = dec.prefill(toks)
+    st, st32 = O.State.new(NL, maxseq, V), O.State.new(NL, maxseq, V)
+    tr = orc.forward(toks, st)
+    tr32 = o32.forward(toks, st32)
+    feed = tr.token
+    for i in range(steps):
+        got = dec.step(feed)
+        tr = orc.forward([feed], st)
+        tr32 = o32.forward([feed], st32)
+        ref_h = tr.hidden[-1][0]
+        eh = float((dec._hidden.float().cpu() - ref_h).abs().max())
+        tol = max(2e-2, 4 * bf16_ulp(float(ref_h.abs().max())), 2.0 * float((tr32.hidden[-1][0] - ref_h).abs().max()))
+        assert eh <= tol, f"step {i} at position {S + i}: hidden error {eh} (bound {tol})"
+        top = torch.topk(tr.logits, 2)
+        assert got == tr.token or (float(top.values[0] - top.values[1]) <= 0.1 and got in top.indices.tolist())
+        feed = tr.token
