@@ -15,7 +15,7 @@
 //   S1 = Gam_last S0 + D^T (exp(G_last - G_s) k_s)
 //
 // k_dn_chunk_prepare computes everything that does not depend on S0 for all (chunk, head) pairs in
-// parallel; k_dn_chunk_scan walks the chunks of one head serially, one CTA per (head, 32 value
+// parallel; k_dn_chunk_scan walks the chunks of one head serially, one CTA per (head, 16 value
 // rows), state in f32 accumulator registers, every product on mma.sync (fp16 operands: all of them
 // are bounded by construction and fp16 carries three more mantissa bits than bf16; f32 accumulate;
 // T and the state enter as two fp16 terms hi + lo).  The serial pass computes D, O
@@ -39,8 +39,10 @@ constexpr int OFF_KD = OFF_QG + CH * 256;                 // fp16 [128 keys][64 
 constexpr int OFF_P = OFF_KD + 128 * 128;                 // fp16 [64][64], 128-byte rows, swizzled
 constexpr int OFF_GL = OFF_P + CH * 128;                  // f32 Gam_last (+ pad to 16 bytes)
 constexpr int BLK_BYTES = OFF_GL + 16;                    // 57360
-constexpr int U_BYTES = CH * 128 * 4;                     // f32 [4 slices][64][32]
-constexpr int U_SLICE_BYTES = CH * 32 * 4;                // 8192
+constexpr int SCAN_GROUPS = 1;                            // groups of 16 value rows per CTA of the serial pass
+constexpr int SCAN_ROWS = 16 * SCAN_GROUPS;               // value rows per CTA: 128 / SCAN_ROWS CTAs per head
+constexpr int U_BYTES = CH * 128 * 4;                     // f32 [slices][64][SCAN_ROWS]
+constexpr int U_SLICE_BYTES = CH * SCAN_ROWS * 4;
 constexpr int PAIR_BYTES = BLK_BYTES + U_BYTES;           // per (chunk, head)
 
 __host__ __device__ inline size_t pair_offset(int chunk, int head) { return ((size_t)chunk * DN_HEADS + head) * PAIR_BYTES; }
@@ -350,8 +352,8 @@ __global__ void __launch_bounds__(256, 2) k_dn_chunk_prepare(const __nv_bfloat16
                 *reinterpret_cast<uint32_t*>(outg + OFF_W + swz256(r, col + 8)) = pack_h(c1[0], c1[1]);
                 *reinterpret_cast<uint32_t*>(outg + OFF_W + swz256(r + 8, col + 8)) = pack_h(c1[2], c1[3]);
             } else {
-                // U[slice][token][32 values]
-                auto uaddr = [&](int row, int j) { return Uout + ((size_t)(j >> 5) * CH + row) * 32 + (j & 31); };
+                // U[slice][token][SCAN_ROWS values]
+                auto uaddr = [&](int row, int j) { return Uout + ((size_t)(j / SCAN_ROWS) * CH + row) * SCAN_ROWS + (j % SCAN_ROWS); };
                 *reinterpret_cast<float2*>(uaddr(r, col)) = make_float2(c0[0], c0[1]);
                 *reinterpret_cast<float2*>(uaddr(r + 8, col)) = make_float2(c0[2], c0[3]);
                 *reinterpret_cast<float2*>(uaddr(r, col + 8)) = make_float2(c1[0], c1[1]);
@@ -361,7 +363,7 @@ __global__ void __launch_bounds__(256, 2) k_dn_chunk_prepare(const __nv_bfloat16
     }
 }
 
-// ---- serial pass: one CTA per (head, 32 value rows), 256 threads ------------------------------------------
+// ---- serial pass: one CTA per (head, SCAN_ROWS value rows), 128 threads per group of 16 rows ------------------------------------------
 
 constexpr int STAGE_BYTES_DN = BLK_BYTES + U_SLICE_BYTES;         // 65552
 constexpr int SC_STAGE0 = 0;
@@ -372,11 +374,12 @@ constexpr int SC_D = SC_S_LO + 32 * 256;                          // fp16 [32 va
 constexpr int SC_BAR = SC_D + 32 * DROW * 2;
 constexpr int SCAN2_SMEM = SC_BAR + 16;
 
-__global__ void __launch_bounds__(256, 1) k_dn_chunk_scan(const unsigned char* __restrict__ scratch, float* __restrict__ state,
+__global__ void __launch_bounds__(128 * SCAN_GROUPS, 1) k_dn_chunk_scan(const unsigned char* __restrict__ scratch, float* __restrict__ state,
                                                           float* __restrict__ o, int S, int nchunks, int* __restrict__ err) {
     pdl_enter();
     extern __shared__ __align__(128) unsigned char sm[];
-    const int h = blockIdx.x >> 2, slice = blockIdx.x & 3;
+    constexpr int SLICES = DN_VAL / SCAN_ROWS;
+    const int h = blockIdx.x / SLICES, slice = blockIdx.x % SLICES;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int grp = warp >> 2, wq = warp & 3;                     // grp: 16 value rows; wq: quarter of the columns
     const int g8 = lane >> 2, t4 = lane & 3;
@@ -394,7 +397,7 @@ __global__ void __launch_bounds__(256, 1) k_dn_chunk_scan(const unsigned char* _
     if (tid == 0) { issue(0); if (nchunks > 1) issue(1); }
 
     // state rows of this warp group: accumulator layout, this warp holds key columns [32 wq, 32 wq + 32)
-    const int jrow = slice * 32 + grp * 16;                       // first value row of the group within the head
+    const int jrow = slice * SCAN_ROWS + grp * 16;                // first value row of the group within the head
     float sacc[4][4];
     float* sg = state + ((size_t)h * DN_VAL + jrow) * DN_KEY;
 #pragma unroll
@@ -457,13 +460,13 @@ __global__ void __launch_bounds__(256, 1) k_dn_chunk_scan(const unsigned char* _
             mma_h(oi[1], sl[ks][0], sl[ks][1], sl[ks][2], sl[ks][3], b2, b3);
         }
         {
-            const float* U = reinterpret_cast<const float*>(st + BLK_BYTES);       // [token][32 values of this slice]
+            const float* U = reinterpret_cast<const float*>(st + BLK_BYTES);       // [token][SCAN_ROWS values of this slice]
             __half* D = reinterpret_cast<__half*>(sm + SC_D);
 #pragma unroll
             for (int n = 0; n < 2; ++n) {
                 const int tok = wq * 16 + n * 8 + 2 * t4, j = grp * 16 + g8;
-                const float d0 = U[tok * 32 + j] - d[n][0], d1 = U[(tok + 1) * 32 + j] - d[n][1];
-                const float d2 = U[tok * 32 + j + 8] - d[n][2], d3 = U[(tok + 1) * 32 + j + 8] - d[n][3];
+                const float d0 = U[tok * SCAN_ROWS + j] - d[n][0], d1 = U[(tok + 1) * SCAN_ROWS + j] - d[n][1];
+                const float d2 = U[tok * SCAN_ROWS + j + 8] - d[n][2], d3 = U[(tok + 1) * SCAN_ROWS + j + 8] - d[n][3];
                 *reinterpret_cast<uint32_t*>(D + j * DROW + tok) = pack_h(d0, d1);
                 *reinterpret_cast<uint32_t*>(D + (j + 8) * DROW + tok) = pack_h(d2, d3);
             }
@@ -534,7 +537,7 @@ cudaError_t dn_chunked(const void* qkv, const void* conv_w, const float* conv_st
     const int nchunks = (S + CH - 1) / CH;
     launch_pdl(k_dn_chunk_prepare, dim3(nchunks, DN_HEADS), 256, PREP_SMEM, stream, (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)conv_w, conv_state,
                                                                          gates, (unsigned char*)scratch, S);
-    launch_pdl(k_dn_chunk_scan, DN_HEADS * 4, 256, SCAN2_SMEM, stream, (const unsigned char*)scratch, state, o, S, nchunks, err);
+    launch_pdl(k_dn_chunk_scan, DN_HEADS * (DN_VAL / SCAN_ROWS), 128 * SCAN_GROUPS, SCAN2_SMEM, stream, (const unsigned char*)scratch, state, o, S, nchunks, err);
     return cudaGetLastError();
 }
 
