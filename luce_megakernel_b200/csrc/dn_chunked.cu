@@ -128,90 +128,74 @@ __global__ void __launch_bounds__(256, 2) k_dn_chunk_prepare(const __nv_bfloat16
     const float Glast = sG[CH - 1];
 
     {
-        // convolution + SiLU + L2 norms, then the fp16 operand tiles and the two scaled copies of the shared block
+        // convolution + SiLU + L2 norms, then the fp16 operand tiles and the two scaled copies of the shared block.
+        // One warp = 8 consecutive tokens, lane = 4 channels; q, k and v are processed one after the other so that
+        // all 11 input rows of a pass (8 tokens + 3 of history) can be in flight at once.
         const int c4 = lane * 4;
-        float wq[3][4][4];                                  // [q|k|v][channel][tap]
-        int chan[3];
-#pragma unroll
+        const int tb = t0 + warp * 8;
+        __half* kdt = reinterpret_cast<__half*>(sm + PREP_KDT);
+#pragma unroll 1
         for (int m = 0; m < 3; ++m) {
-            chan[m] = m * DN_QK + h * DN_KEY + c4;
+            const int chan = m * DN_QK + h * DN_KEY + c4;
+            float wq[4][4];                                 // [channel][tap]
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + chan[m] + e);
-                wq[m][e][0] = bf_lo(wr.x); wq[m][e][1] = bf_hi(wr.x); wq[m][e][2] = bf_lo(wr.y); wq[m][e][3] = bf_hi(wr.y);
+                const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + chan + e);
+                wq[e][0] = bf_lo(wr.x); wq[e][1] = bf_hi(wr.x); wq[e][2] = bf_lo(wr.y); wq[e][3] = bf_hi(wr.y);
             }
-        }
-        // x[m][e][tap]: the last three inputs before the current token
-        float win[3][4][3];
-        auto load_row = [&](int tt, int m, float (&dst)[4]) {
-            if (tt >= 0) {
-                if (tt < S) {
-                    const uint2 u = *reinterpret_cast<const uint2*>(qkv + (size_t)tt * DN_CONV_CH + chan[m]);
-                    dst[0] = bf_lo(u.x); dst[1] = bf_hi(u.x); dst[2] = bf_lo(u.y); dst[3] = bf_hi(u.y);
-                } else { dst[0] = dst[1] = dst[2] = dst[3] = 0.f; }
-            } else {
+            uint2 raw[11];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) dst[e] = conv_state[(chan[m] + e) * 4 + 4 + tt];
+            for (int i = 0; i < 11; ++i) {
+                const int tt = tb - 3 + i;
+                raw[i] = (tt >= 0 && tt < S) ? *reinterpret_cast<const uint2*>(qkv + (size_t)tt * DN_CONV_CH + chan) : make_uint2(0u, 0u);
             }
-        };
-        const int tb = t0 + warp * 8;
+            float x[11][4];
 #pragma unroll
-        for (int k = 0; k < 3; ++k) {
+            for (int i = 0; i < 11; ++i) { x[i][0] = bf_lo(raw[i].x); x[i][1] = bf_hi(raw[i].x); x[i][2] = bf_lo(raw[i].y); x[i][3] = bf_hi(raw[i].y); }
+            if (tb < 3) {                                   // the first rows of the prompt: history from the stored window
 #pragma unroll
-            for (int m = 0; m < 3; ++m) {
-                float tmp[4];
-                load_row(tb - 3 + k, m, tmp);
+                for (int i = 0; i < 3; ++i) {
+                    const int tt = tb - 3 + i;
+                    if (tt < 0) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) win[m][e][k] = tmp[e];
-            }
-        }
-        // raw rows of the next two tokens are in flight while the current one is processed
-        auto fetch = [&](int t, uint2 (&dst)[3]) {
-#pragma unroll
-            for (int m = 0; m < 3; ++m)
-                dst[m] = (t < S) ? *reinterpret_cast<const uint2*>(qkv + (size_t)t * DN_CONV_CH + chan[m]) : make_uint2(0u, 0u);
-        };
-        uint2 nx0[3], nx1[3];
-        fetch(tb, nx0);
-        fetch(tb + 1, nx1);
-        __half* kdt = reinterpret_cast<__half*>(sm + PREP_KDT);
-#pragma unroll 2
-        for (int i = 0; i < 8; ++i) {
-            const int r = warp * 8 + i, t = t0 + r;
-            uint2 raw[3] = {nx0[0], nx0[1], nx0[2]};
-#pragma unroll
-            for (int m = 0; m < 3; ++m) nx0[m] = nx1[m];
-            if (i + 2 < 8) fetch(t + 2, nx1);
-            float val[3][4];
-#pragma unroll
-            for (int m = 0; m < 3; ++m) {
-                const float cur[4] = {bf_lo(raw[m].x), bf_hi(raw[m].x), bf_lo(raw[m].y), bf_hi(raw[m].y)};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float co = win[m][e][0] * wq[m][e][0] + win[m][e][1] * wq[m][e][1] + win[m][e][2] * wq[m][e][2] + cur[e] * wq[m][e][3];
-                    val[m][e] = (t < S) ? silu_f(co) : 0.f;
-                    win[m][e][0] = win[m][e][1]; win[m][e][1] = win[m][e][2]; win[m][e][2] = cur[e];
+                        for (int e = 0; e < 4; ++e) x[i][e] = conv_state[(chan + e) * 4 + 4 + tt];
+                    }
                 }
             }
-            const float sq = warp_sum(val[0][0] * val[0][0] + val[0][1] * val[0][1] + val[0][2] * val[0][2] + val[0][3] * val[0][3]);
-            const float sk = warp_sum(val[1][0] * val[1][0] + val[1][1] * val[1][1] + val[1][2] * val[1][2] + val[1][3] * val[1][3]);
-            const float qn = rsqrtf(sq + 1e-6f) * 0.08838834764831845f, kn = rsqrtf(sk + 1e-6f);
-            const float4 q = make_float4(val[0][0] * qn, val[0][1] * qn, val[0][2] * qn, val[0][3] * qn);
-            const float4 k = make_float4(val[1][0] * kn, val[1][1] * kn, val[1][2] * kn, val[1][3] * kn);
-            const float4 v = make_float4(val[2][0], val[2][1], val[2][2], val[2][3]);
-            const float G = sG[r], b = sBeta[r], gam = __expf(G), bg = b * gam, kd = __expf(Glast - G);
-            *reinterpret_cast<uint2*>(sm + PREP_KB + (r * PADROW + c4) * 2) = make_uint2(pack_h(k.x, k.y), pack_h(k.z, k.w));
-            *reinterpret_cast<uint2*>(sm + PREP_QB + (r * PADROW + c4) * 2) = make_uint2(pack_h(q.x, q.y), pack_h(q.z, q.w));
-            *reinterpret_cast<uint2*>(sm + PREP_KG + (r * PADROW + c4) * 2) =
-                make_uint2(pack_h(bg * k.x, bg * k.y), pack_h(bg * k.z, bg * k.w));
-            *reinterpret_cast<uint2*>(sm + PREP_VB + (r * PADROW + c4) * 2) =
-                make_uint2(pack_h(b * v.x, b * v.y), pack_h(b * v.z, b * v.w));
-            *reinterpret_cast<uint2*>(outg + OFF_QG + swz256(r, c4)) =
-                make_uint2(pack_h(gam * q.x, gam * q.y), pack_h(gam * q.z, gam * q.w));
-            kdt[swz128(c4 + 0, r) >> 1] = __float2half_rn(kd * k.x);
-            kdt[swz128(c4 + 1, r) >> 1] = __float2half_rn(kd * k.y);
-            kdt[swz128(c4 + 2, r) >> 1] = __float2half_rn(kd * k.z);
-            kdt[swz128(c4 + 3, r) >> 1] = __float2half_rn(kd * k.w);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = warp * 8 + i, t = t0 + r;
+                float val[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float co = x[i][e] * wq[e][0] + x[i + 1][e] * wq[e][1] + x[i + 2][e] * wq[e][2] + x[i + 3][e] * wq[e][3];
+                    val[e] = (t < S) ? silu_f(co) : 0.f;
+                }
+                const float G = sG[r], bta = sBeta[r];
+                if (m == 2) {                               // values: beta v
+                    *reinterpret_cast<uint2*>(sm + PREP_VB + (r * PADROW + c4) * 2) =
+                        make_uint2(pack_h(bta * val[0], bta * val[1]), pack_h(bta * val[2], bta * val[3]));
+                } else {
+                    const float ss = warp_sum(val[0] * val[0] + val[1] * val[1] + val[2] * val[2] + val[3] * val[3]);
+                    const float nrm = rsqrtf(ss + 1e-6f) * (m == 0 ? 0.08838834764831845f : 1.0f);
+                    const float v0 = val[0] * nrm, v1 = val[1] * nrm, v2 = val[2] * nrm, v3 = val[3] * nrm;
+                    const float gam = __expf(G);
+                    if (m == 0) {                           // queries: q and Gam q
+                        *reinterpret_cast<uint2*>(sm + PREP_QB + (r * PADROW + c4) * 2) = make_uint2(pack_h(v0, v1), pack_h(v2, v3));
+                        *reinterpret_cast<uint2*>(outg + OFF_QG + swz256(r, c4)) =
+                            make_uint2(pack_h(gam * v0, gam * v1), pack_h(gam * v2, gam * v3));
+                    } else {                                // keys: k, beta Gam k, and the decayed transposed copy
+                        const float bg = bta * gam, kd = __expf(Glast - G);
+                        *reinterpret_cast<uint2*>(sm + PREP_KB + (r * PADROW + c4) * 2) = make_uint2(pack_h(v0, v1), pack_h(v2, v3));
+                        *reinterpret_cast<uint2*>(sm + PREP_KG + (r * PADROW + c4) * 2) =
+                            make_uint2(pack_h(bg * v0, bg * v1), pack_h(bg * v2, bg * v3));
+                        kdt[swz128(c4 + 0, r) >> 1] = __float2half_rn(kd * v0);
+                        kdt[swz128(c4 + 1, r) >> 1] = __float2half_rn(kd * v1);
+                        kdt[swz128(c4 + 2, r) >> 1] = __float2half_rn(kd * v2);
+                        kdt[swz128(c4 + 3, r) >> 1] = __float2half_rn(kd * v3);
+                    }
+                }
+            }
         }
     }
     if (tid == 0) *reinterpret_cast<float4*>(outg + OFF_GL) = make_float4(__expf(Glast), 0.f, 0.f, 0.f);
@@ -267,16 +251,19 @@ __global__ void __launch_bounds__(256, 2) k_dn_chunk_prepare(const __nv_bfloat16
     // T = (I + A)^-1, A strictly lower triangular, in 16 x 16 blocks: the four diagonal blocks by forward
     // substitution (one thread per column), then each block row i from right to left,
     //   T_ij = -(sum_{k=j+1..i} T_ik A_kj) T_jj,
-    // one thread per element.  T is kept as fp16 head + remainder (the form the products below read).
+    // one thread per element.  T is written as fp16 head + remainder (the form the products below read).
     {
         __half* TH = reinterpret_cast<__half*>(sm + PREP_TH);
         __half* TL = reinterpret_cast<__half*>(sm + PREP_TL);
+        // f32 working copy of T in the (now unused) q tile: the block products read it with one load per term
+        float* Tf = reinterpret_cast<float*>(sm + PREP_QB);
         auto put = [&](int r, int c, float v) {
             const __half hi = __float2half_rn(v);
             TH[r * TROW + c] = hi;
             TL[r * TROW + c] = __float2half_rn(v - __half2float(hi));
+            Tf[r * AROW + c] = v;
         };
-        auto get = [&](int r, int c) { return __half2float(TH[r * TROW + c]) + __half2float(TL[r * TROW + c]); };
+        auto get = [&](int r, int c) { return Tf[r * AROW + c]; };
         if (tid < 64) {
             const int bb = (tid >> 4) * 16, c = tid & 15;
             float x[16];
