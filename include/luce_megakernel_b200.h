@@ -177,6 +177,31 @@ int mk_prefill_bf16(
     int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
 const char *mk_prefill_error(void);
 
+/* Batched decode: `batch` (1..16) independent sequences advance by one token each and share every weight pass.
+ * The reference has no batched op (all of megakernel/torch_bindings.cpp:569-675 are batch 1); these calls keep the
+ * reference's per-sequence layouts and put a leading batch dimension on them:
+ *   tokens, positions, output_tokens: device int32 [batch] (positions[b] = index the new token of sequence b is
+ *   written at = tokens of b already in its cache; every sequence has its own length, all < max_seq_len),
+ *   fa_k_cache / fa_v_cache bf16 [batch][n_fa][2][max_seq_len][256], dn_states f32 [batch][n_dn][16][128][128],
+ *   conv_bufs f32 [batch][n_dn][6144][4]  (slice b is exactly what mk_prefill_bf16 / decode take for one sequence),
+ *   final_normed / hidden_bf16_out: bf16 [batch][1024] or null.
+ * mk_decode_batch runs one step and leaves tokens / positions untouched; mk_decode_batch_many runs `steps` steps
+ * with the chosen tokens fed back on the device: tokens and positions are updated in place and tokens_log
+ * [steps][batch] receives every step's tokens.  Enqueue only (no synchronisation once the pointer table is cached):
+ * capturable into a CUDA graph.  Rounding points are those of the prompt path. */
+int mk_decode_batch(
+    const int *tokens, const int *positions, int *output_tokens, int batch,
+    const void *embed_weight, const MkLayerWeights *layers, const void *final_norm_w, const void *lm_head_w,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    const void *fused_fa_qkv_base, const void *fused_gate_up_base, void *final_normed, void *hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
+int mk_decode_batch_many(
+    int steps, int *tokens, int *positions, int *tokens_log, int batch,
+    const void *embed_weight, const MkLayerWeights *layers, const void *final_norm_w, const void *lm_head_w,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    const void *fused_fa_qkv_base, const void *fused_gate_up_base,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
+
 /* The reference's other prefill entry points, with their argument lists: launch_prefill_bf16_mega (bf16, per-matrix
  * weights from the 128-byte table only; reference: megakernel/prefill_megakernel.cu:1031-1045),
  * launch_prefill_bf16_nvfp4_lm (bf16 layers, NVFP4 LM head; megakernel/prefill_bw.cu:1486-1503) and

@@ -292,12 +292,20 @@ __global__ void k_dn_gated_norm(const float* __restrict__ o, const __nv_bfloat16
 // projection: 8 x [q(256) | gate(256)], k(512), v(512).  (reference: prefill.cu:1041-1087)
 __global__ void k_fa_norm_rope(__nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ q_norm,
                                const __nv_bfloat16* __restrict__ k_norm, __nv_bfloat16* __restrict__ kc,
-                               __nv_bfloat16* __restrict__ vc, int S, int max_seq) {
+                               __nv_bfloat16* __restrict__ vc, int S, int max_seq,
+                               const int* __restrict__ row_pos, size_t row_cache_stride) {
     pdl_enter();
     const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (wid >= S * 12) return;
-    const int t = wid / 12, slot = wid % 12;
-    __nv_bfloat16* row = qkv + (size_t)t * FA_QKV_ROWS;
+    const int r = wid / 12, slot = wid % 12;
+    __nv_bfloat16* row = qkv + (size_t)r * FA_QKV_ROWS;
+    // prompt: row r is position r of one sequence; batched step: row r is sequence r at position row_pos[r]
+    int t = r;
+    if (row_pos) {
+        t = min(max(row_pos[r], 0), max_seq - 1);
+        kc += (size_t)r * row_cache_stride;
+        vc += (size_t)r * row_cache_stride;
+    }
     if (slot >= 10) {
         const int g = slot - 10;
         const uint4* src = reinterpret_cast<const uint4*>(row + FA_QPROJ + FA_KV_SIZE + g * FA_HEAD_DIM);
@@ -350,6 +358,10 @@ __global__ void k_final_norm(const __nv_bfloat16* __restrict__ hidden_last, cons
                              __nv_bfloat16* __restrict__ hidden_out) {
     pdl_enter();
     __shared__ float red[32];
+    const size_t off = (size_t)blockIdx.x * HIDDEN;            // one block per row (the prompt's last row: one block)
+    hidden_last += off; normed_f32 += off;
+    if (normed_bf16) normed_bf16 += off;
+    if (hidden_out) hidden_out += off;
     float v[2], ss = 0.f;
     for (int i = 0; i < 2; ++i) { v[i] = ld_bf(hidden_last + threadIdx.x + 512 * i); ss += v[i] * v[i]; }
     ss = warp_sum(ss);
@@ -402,6 +414,7 @@ __global__ void __launch_bounds__(256) k_lm_head(const float* __restrict__ x, co
 
 __global__ void k_lm_reduce(const float* __restrict__ bval, const int* __restrict__ bidx, int n, int* __restrict__ out) {
     pdl_enter();
+    bval += (size_t)blockIdx.x * n; bidx += (size_t)blockIdx.x * n; out += blockIdx.x;     // one block per row of logits
     float best = -INFINITY;
     int besti = 0x7fffffff;
     for (int i = threadIdx.x; i < n; i += 32) {
@@ -654,7 +667,8 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
                 PF_CHECK(gemm(w.normed, lv.w_k, w.wide + FA_QPROJ, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm k");
                 PF_CHECK(gemm(w.normed, lv.w_v, w.wide + FA_QPROJ + FA_KV_SIZE, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm v");
             }
-            launch_pdl(k_fa_norm_rope, blocks_for_warps((long long)S * 12), 256, 0, stream, w.wide, (const bf*)lv.q_norm, (const bf*)lv.k_norm, kc, vc, S, max_seq_len);
+            launch_pdl(k_fa_norm_rope, blocks_for_warps((long long)S * 12), 256, 0, stream, w.wide, (const bf*)lv.q_norm, (const bf*)lv.k_norm, kc, vc, S, max_seq_len,
+                       (const int*)nullptr, (size_t)0);
             const uint32_t* bmask = nullptr;
             if (g_sparse.enabled) {
                 uint32_t* m = nullptr;
@@ -714,6 +728,8 @@ int host_table(int dev, const void* layers, int num_layers, size_t entry, cudaSt
     rows = ht.rows;
     return MK_OK;
 }
+
+#include "decode_batch.cuh"
 
 }  // namespace
 }  // namespace mk
@@ -970,4 +986,79 @@ extern "C" int mk_attention_prefill(const void* qkv, const void* k_cache, const 
         PF_CHECK(fa_prefill(qkv, k_cache, v_cache, out, seq_len, max_seq_len, mask, stream), "attention");
     }
     return MK_OK;
+}
+
+// ---- batched decode (no counterpart in the reference: every op of megakernel/torch_bindings.cpp:569-675 is batch 1) ----
+namespace mk {
+namespace {
+int decode_batch_entry(int steps, int* tokens, int* positions, int* output_tokens, int* tokens_log, int batch,
+                       const void* embed_weight, const MkLayerWeights* layers, const void* final_norm_w, const void* lm_head_w,
+                       void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+                       const void* fused_fa_qkv_base, const void* fused_gate_up_base, void* final_normed,
+                       void* hidden_bf16_out, int max_seq_len, int num_layers, int vocab, cudaStream_t stream) {
+    const void* req[] = {tokens, positions, embed_weight, layers, final_norm_w, lm_head_w, fa_k_cache, fa_v_cache, dn_states, conv_bufs};
+    int dev = 0;
+    int rc = check_common(req, 10, 1, max_seq_len, num_layers, vocab, dev);
+    if (rc != MK_OK) return rc;
+    if (batch < 1 || batch > BATCH_MAX) return pfail(MK_ERR_BAD_ARG, "batch must be in [1, 16]");
+    if (steps < 1 || (steps > 1 && !tokens_log) || (steps == 1 && !output_tokens && !tokens_log))
+        return pfail(MK_ERR_BAD_ARG, "bad step count or missing output");
+    const unsigned char* rows = nullptr;
+    rc = host_table(dev, layers, num_layers, sizeof(LayerWeights), stream, rows);
+    if (rc != MK_OK) return rc;
+    const LayerWeights* hl = reinterpret_cast<const LayerWeights*>(rows);
+    int n_fa = 0;
+    for (int li = 0; li < num_layers; ++li) n_fa += hl[li].layer_type != 0;
+    const int n_dn = num_layers - n_fa;
+    int fa_seen = 0;
+    auto source = [&](int li, LayerView& lv) {
+        const bool fa = hl[li].layer_type != 0;
+        lv = view_of(hl[li],
+                     (fa && fused_fa_qkv_base) ? (const __nv_bfloat16*)fused_fa_qkv_base + (size_t)fa_seen * FA_QKV_ROWS * HIDDEN : nullptr,
+                     fused_gate_up_base ? (const __nv_bfloat16*)fused_gate_up_base + (size_t)li * 2 * INTER * HIDDEN : nullptr);
+        if (fa) ++fa_seen;
+        return (int)MK_OK;
+    };
+    if (steps == 1 && output_tokens)
+        return decode_batch_core(tokens, positions, output_tokens, batch, embed_weight, source, num_layers, n_fa, n_dn, final_norm_w,
+                                 lm_head_w, fa_k_cache, fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out,
+                                 max_seq_len, vocab, dev, stream);
+    PF_CHECK(ensure_batch_ws(g_bws[dev]), "batch workspace");
+    for (int s = 0; s < steps; ++s) {
+        fa_seen = 0;
+        rc = decode_batch_core(tokens, positions, g_bws[dev].chosen, batch, embed_weight, source, num_layers, n_fa, n_dn,
+                               final_norm_w, lm_head_w, fa_k_cache, fa_v_cache, dn_states, conv_bufs, final_normed,
+                               hidden_bf16_out, max_seq_len, vocab, dev, stream);
+        if (rc != MK_OK) return rc;
+        launch_pdl(k_batch_advance, 1, 32, 0, stream, tokens, (const int*)g_bws[dev].chosen, positions, tokens_log + (size_t)s * batch, batch);
+    }
+    PF_CHECK(cudaGetLastError(), "batched steps launch");
+    return MK_OK;
+}
+}  // namespace
+}  // namespace mk
+
+extern "C" int mk_decode_batch(
+    const int* tokens, const int* positions, int* output_tokens, int batch,
+    const void* embed_weight, const MkLayerWeights* layers, const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    const void* fused_fa_qkv_base, const void* fused_gate_up_base, void* final_normed, void* hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream) {
+    if (!output_tokens) return mk::pfail(MK_ERR_BAD_ARG, "null pointer argument");
+    return mk::decode_batch_entry(1, const_cast<int*>(tokens), const_cast<int*>(positions), output_tokens, nullptr, batch,
+                                  embed_weight, layers, final_norm_w, lm_head_w, fa_k_cache, fa_v_cache, dn_states, conv_bufs,
+                                  fused_fa_qkv_base, fused_gate_up_base, final_normed, hidden_bf16_out, max_seq_len, num_layers,
+                                  vocab, stream);
+}
+
+extern "C" int mk_decode_batch_many(
+    int steps, int* tokens, int* positions, int* tokens_log, int batch,
+    const void* embed_weight, const MkLayerWeights* layers, const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    const void* fused_fa_qkv_base, const void* fused_gate_up_base,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream) {
+    if (!tokens_log) return mk::pfail(MK_ERR_BAD_ARG, "null pointer argument");
+    return mk::decode_batch_entry(steps, tokens, positions, nullptr, tokens_log, batch, embed_weight, layers, final_norm_w,
+                                  lm_head_w, fa_k_cache, fa_v_cache, dn_states, conv_bufs, fused_fa_qkv_base,
+                                  fused_gate_up_base, nullptr, nullptr, max_seq_len, num_layers, vocab, stream);
 }

@@ -235,6 +235,44 @@ void prefill_bf16_mega(Tensor output_token, Tensor token_ids, Tensor embed_weigh
     (void)dn_out_buf; (void)beta_buf; (void)alpha_buf; (void)lm_bmv; (void)lm_bmi;
 }
 
+// Batched decode step: no counterpart in the reference (megakernel/torch_bindings.cpp:569-675 are all batch 1).
+// State tensors are the reference's with a leading batch dimension; tokens, positions, output_tokens: int32 [batch].
+void decode_batch(Tensor output_tokens, Tensor tokens, Tensor positions, Tensor embed_weight, Tensor layer_weights_packed,
+                  Tensor final_norm_weight, Tensor lm_head_weight, Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states,
+                  Tensor conv_bufs, Tensor fused_fa_qkv, Tensor fused_gate_up, Tensor final_normed, Tensor hidden_bf16_out) {
+    need(tokens, "tokens", torch::kInt32, 1);
+    const int64_t batch = tokens.numel();
+    TORCH_CHECK(batch >= 1 && batch <= 16, "batch must be in [1, 16]");
+    need(output_tokens, "output_tokens", torch::kInt32, batch);
+    need(positions, "positions", torch::kInt32, batch);
+    need(embed_weight, "embed_weight", torch::kBFloat16, 1024);
+    need(layer_weights_packed, "layer_weights_packed", torch::kUInt8, 128);
+    need(lm_head_weight, "lm_head_weight", torch::kBFloat16, 1024);
+    TORCH_CHECK(fa_k_cache.dim() == 5 && fa_k_cache.size(0) == batch && fa_k_cache.size(4) == 256,
+                "fa_k_cache must be [batch, layers, 2, max_seq_len, 256]");
+    const int64_t max_seq_len = fa_k_cache.size(3);
+    need(fa_k_cache, "fa_k_cache", torch::kBFloat16, batch * 2 * max_seq_len * 256);
+    need(fa_v_cache, "fa_v_cache", torch::kBFloat16, batch * 2 * max_seq_len * 256);
+    TORCH_CHECK(fa_v_cache.numel() == fa_k_cache.numel(), "fa_v_cache must have the shape of fa_k_cache");
+    TORCH_CHECK(dn_states.dim() == 5 && dn_states.size(0) == batch, "dn_states must be [batch, layers, 16, 128, 128]");
+    TORCH_CHECK(conv_bufs.dim() == 4 && conv_bufs.size(0) == batch, "conv_bufs must be [batch, layers, 6144, 4]");
+    need(dn_states, "dn_states", torch::kFloat32, batch * 16 * 128 * 128);
+    need(conv_bufs, "conv_bufs", torch::kFloat32, batch * 6144 * 4);
+    need(fused_fa_qkv, "fused_fa_qkv", torch::kBFloat16, 5120 * 1024);
+    need(fused_gate_up, "fused_gate_up", torch::kBFloat16, 7168 * 1024);
+    need(final_normed, "final_normed", torch::kBFloat16, batch * 1024);
+    need(hidden_bf16_out, "hidden_bf16_out", torch::kBFloat16, batch * 1024);
+    DeviceGuard guard(embed_weight);
+    const int num_layers = (int)(layer_weights_packed.numel() / 128);
+    const int rc = mk_decode_batch(
+        (const int*)tokens.data_ptr(), (const int*)positions.data_ptr(), (int*)output_tokens.data_ptr(), (int)batch,
+        embed_weight.data_ptr(), (const MkLayerWeights*)layer_weights_packed.data_ptr(), final_norm_weight.data_ptr(),
+        lm_head_weight.data_ptr(), fa_k_cache.data_ptr(), fa_v_cache.data_ptr(), dn_states.data_ptr(), conv_bufs.data_ptr(),
+        fused_fa_qkv.data_ptr(), fused_gate_up.data_ptr(), final_normed.data_ptr(), hidden_bf16_out.data_ptr(), (int)max_seq_len,
+        num_layers, (int)embed_weight.size(0), current_stream(embed_weight));
+    TORCH_CHECK(rc == MK_OK, "qwen35_megakernel_bf16_C::decode_batch failed (", rc, "): ", mk_prefill_error());
+}
+
 void prefill_megakernel_nvfp4(Tensor output_token, Tensor token_ids, Tensor embed_weight, Tensor layer_weights_packed,
                               Tensor final_norm_weight, Tensor lm_head_weight_packed, Tensor lm_head_scales,
                               Tensor lm_hidden_bf16, Tensor lm_hidden_packed, Tensor lm_hidden_scales, Tensor lm_logits_f16,
@@ -419,6 +457,14 @@ TORCH_LIBRARY(qwen35_megakernel_bf16_C, ops) {
             "Tensor final_normed, Tensor hidden_bf16_out, "
             "Tensor lm_bmv, Tensor lm_bmi) -> ()");
     ops.impl("prefill_bf16_mega", torch::kCUDA, &prefill_bf16_mega);
+
+    ops.def("decode_batch(Tensor output_tokens, Tensor tokens, Tensor positions, "
+            "Tensor embed_weight, Tensor layer_weights_packed, "
+            "Tensor final_norm_weight, Tensor lm_head_weight, "
+            "Tensor fa_k_cache, Tensor fa_v_cache, Tensor dn_states, Tensor conv_bufs, "
+            "Tensor fused_fa_qkv, Tensor fused_gate_up, "
+            "Tensor final_normed, Tensor hidden_bf16_out) -> ()");
+    ops.impl("decode_batch", torch::kCUDA, &decode_batch);
 
     ops.def("prefill_megakernel_nvfp4(Tensor output_token, Tensor token_ids, "
             "Tensor embed_weight, Tensor layer_weights_packed, "

@@ -348,3 +348,125 @@ class Decoder:
         ids = self.tokenizer.encode(prompt, add_special_tokens=True)
         out = self.generate_ids(ids, max_tokens, self.tokenizer.eos_token_id)
         return self.tokenizer.decode(out, skip_special_tokens=True)
+
+
+class BatchDecoder:
+    """`batch` independent greedy sequences decoded together: every step reads each weight matrix once for all of
+    them.  The reference has no batched op (megakernel/torch_bindings.cpp:569-675 are all batch 1); the state
+    tensors are the reference's per-sequence layouts (megakernel/model.py:200-214) with a leading batch
+    dimension, so slice b is exactly the state of a batch-1 Decoder.  Weights are shared with `decoder`.
+
+    Sequences may have different lengths: prefill() takes one prompt per sequence and runs the prompt path on
+    each slice; step()/step_many() then advance all sequences by one token per step."""
+
+    MAX_BATCH = 16
+
+    def __init__(self, decoder: Decoder, batch: int):
+        if not 1 <= batch <= self.MAX_BATCH:
+            raise ValueError(f"batch must be in [1, {self.MAX_BATCH}]")
+        self._d = decoder
+        self._lib = decoder._lib
+        self.batch = int(batch)
+        self.max_seq_len = decoder.max_seq_len
+        dev = decoder._embed_weight.device
+        types = [ld["type"] for ld in decoder._weights["layer_data"]]
+        n_fa, n_dn = sum(types), len(types) - sum(types)
+        B = self.batch
+        self._fa_k_cache = torch.zeros(B, max(n_fa, 1), FA_NUM_KV_HEADS, self.max_seq_len, FA_HEAD_DIM,
+                                       dtype=torch.bfloat16, device=dev)
+        self._fa_v_cache = torch.zeros_like(self._fa_k_cache)
+        self._dn_states = torch.zeros(B, max(n_dn, 1), DN_NUM_HEADS, DN_KEY_DIM, DN_VALUE_DIM, dtype=torch.float32, device=dev)
+        self._conv_bufs = torch.zeros(B, max(n_dn, 1), DN_CONV_CHANNELS, DN_CONV_KERNEL, dtype=torch.float32, device=dev)
+        self._tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self._positions = torch.zeros(B, dtype=torch.int32, device=dev)
+        self._out_tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self._final_normed = torch.empty(B, HIDDEN_SIZE, dtype=torch.bfloat16, device=dev)
+        self._hidden_bf16_out = torch.empty(B, HIDDEN_SIZE, dtype=torch.bfloat16, device=dev)
+        self._host_positions = [0] * B
+
+    def reset(self):
+        for t in (self._fa_k_cache, self._fa_v_cache, self._dn_states, self._conv_bufs, self._tokens, self._positions):
+            t.zero_()
+        self._host_positions = [0] * self.batch
+
+    def _fail(self, rc, what):
+        self._lib.mk_prefill_error.restype = ctypes.c_char_p
+        raise RuntimeError(f"{what} failed ({rc}): {self._lib.mk_prefill_error().decode()}")
+
+    def _status(self):
+        st = self._lib.mk_prefill_status()
+        if st != 0:
+            raise RuntimeError(f"a bounded wait ran out inside a kernel (status {st})")
+
+    def prefill(self, prompts):
+        """One prompt (list of ids) per sequence, from position 0.  Returns the first generated token of each;
+        they are also the inputs of the next step()."""
+        d = self._d
+        if len(prompts) != self.batch:
+            raise ValueError("one prompt per sequence")
+        if any(p != 0 for p in self._host_positions):
+            raise ValueError("prefill starts at position 0: call reset() first")
+        d._bind_dims()
+        for b, prompt in enumerate(prompts):
+            ids = torch.as_tensor(prompt, dtype=torch.int32).to(self._tokens.device).contiguous()
+            S = int(ids.numel())
+            if S < 1 or S >= self.max_seq_len:
+                raise ValueError("prompt length must be in [1, max_seq_len)")
+            rc = self._lib.mk_prefill_bf16(
+                _ptr(ids), ctypes.c_int(S), _ptr(self._tokens[b:b + 1]), _ptr(d._embed_weight), _ptr(d._layer_weights_packed),
+                _ptr(d._final_norm_weight), _ptr(d._lm_head_weight), _ptr(self._fa_k_cache[b]), _ptr(self._fa_v_cache[b]),
+                _ptr(self._dn_states[b]), _ptr(self._conv_bufs[b]), _ptr(d._fused_fa_qkv), _ptr(d._fused_gate_up),
+                _ptr(self._final_normed[b]), _ptr(self._hidden_bf16_out[b]), ctypes.c_int(self.max_seq_len),
+                ctypes.c_int(d.num_layers), ctypes.c_int(d.vocab), d._stream())
+            if rc != 0:
+                self._fail(rc, "prefill")
+            self._host_positions[b] = S
+        self._positions.copy_(torch.tensor(self._host_positions, dtype=torch.int32))
+        first = self._tokens.cpu().tolist()
+        self._status()
+        return first
+
+    def _args(self):
+        d = self._d
+        return (_ptr(d._embed_weight), _ptr(d._layer_weights_packed), _ptr(d._final_norm_weight), _ptr(d._lm_head_weight),
+                _ptr(self._fa_k_cache), _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs),
+                _ptr(d._fused_fa_qkv), _ptr(d._fused_gate_up))
+
+    def step_async(self, tokens=None):
+        """Enqueue one step for all sequences (inputs: `tokens`, or the tokens of the previous step / prefill).
+        Returns the device int32[batch] tensor that will hold the chosen tokens.  Capturable into a CUDA graph
+        when `tokens` is None or a device tensor."""
+        d = self._d
+        if max(self._host_positions) >= self.max_seq_len:
+            raise ValueError("a sequence has reached max_seq_len")
+        if tokens is not None:
+            self._tokens.copy_(torch.as_tensor(tokens, dtype=torch.int32), non_blocking=True)
+        rc = self._lib.mk_decode_batch(
+            _ptr(self._tokens), _ptr(self._positions), _ptr(self._out_tokens), ctypes.c_int(self.batch), *self._args(),
+            _ptr(self._final_normed), _ptr(self._hidden_bf16_out), ctypes.c_int(self.max_seq_len),
+            ctypes.c_int(d.num_layers), ctypes.c_int(d.vocab), d._stream())
+        if rc != 0:
+            self._fail(rc, "batched step")
+        self._positions += 1
+        self._tokens.copy_(self._out_tokens)
+        self._host_positions = [p + 1 for p in self._host_positions]
+        return self._out_tokens
+
+    def step(self, tokens=None):
+        out = self.step_async(tokens).cpu().tolist()
+        self._status()
+        return out
+
+    def step_many(self, steps: int) -> torch.Tensor:
+        """`steps` greedy steps with the chosen tokens fed back on the device; returns int32 [steps][batch]."""
+        d = self._d
+        if steps < 1 or max(self._host_positions) + steps > self.max_seq_len:
+            raise ValueError("steps must be positive and stay within max_seq_len")
+        log = torch.empty(steps, self.batch, dtype=torch.int32, device=self._tokens.device)
+        rc = self._lib.mk_decode_batch_many(
+            ctypes.c_int(steps), _ptr(self._tokens), _ptr(self._positions), _ptr(log), ctypes.c_int(self.batch), *self._args(),
+            ctypes.c_int(self.max_seq_len), ctypes.c_int(d.num_layers), ctypes.c_int(d.vocab), d._stream())
+        if rc != 0:
+            self._fail(rc, "batched steps")
+        self._host_positions = [p + steps for p in self._host_positions]
+        return log
