@@ -28,10 +28,16 @@ GEN_LEN = 128
 MAX_SEQ = 2048
 WEIGHT_BYTES_PER_TOKEN = 1_546_073_728      # weights + DeltaNet state r/w + conv state r/w
 KV_BYTES_PER_POS = 12_288                   # K and V rows read per cached position, 6 layers
+STATE_BYTES_PER_SEQ = 41_287_680            # DeltaNet state and conv window, read + written once per token
 
 
 def algorithmic_bytes_per_token(context_len: float) -> float:
     return WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POS * context_len
+
+
+def batch_step_bytes(batch: int, context_len: float) -> float:
+    """Algorithmic HBM bytes of one batched step: the weights once, state and cache rows once per sequence."""
+    return (WEIGHT_BYTES_PER_TOKEN - STATE_BYTES_PER_SEQ) + batch * (STATE_BYTES_PER_SEQ + KV_BYTES_PER_POS * context_len)
 
 
 def kept_block_fraction(S: int, top_frac=0.10, window=4, sink=1) -> float:
@@ -181,6 +187,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-long-prefill", action="store_true")
+    ap.add_argument("--no-batch", action="store_true", help="skip the batch 8 / batch 16 decode figures")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -293,10 +300,33 @@ def main():
         if lib().mk_device_status() != 0 or lib().mk_prefill_status() != 0:
             raise SystemExit("device-side wait timed out during the long prefill")
 
-    t_all = torch.tensor([ms, e2e_s, pp_ms], dtype=torch.float64, device="cuda")
+    # batched decode (BASELINE configs[3] and [4]): batch 8 and 16 per GPU, a pp520 prompt per sequence, then tg128
+    # with the tokens fed back on the device; 1 warm-up run + 2 timed runs of 128 steps
+    batch_ms = []
+    if not args.no_batch:
+        for B_ in (8, 16):
+            bd = M.BatchDecoder(dec, B_)
+            prompts = [torch.randint(0, M.VOCAB_SIZE, (PROMPT_LEN,), generator=g).tolist() for _ in range(B_)]
+            runs = []
+            for r in range(3):
+                bd.reset()
+                bd.prefill(prompts)
+                barrier()
+                p0.record()
+                bd.step_many(GEN_LEN)
+                p1.record()
+                barrier()
+                runs.append(p0.elapsed_time(p1))
+            batch_ms.append(sum(runs[1:]) / 2 / GEN_LEN)
+            del bd
+        if lib().mk_prefill_status() != 0:
+            raise SystemExit("device-side wait timed out during the batched decode")
+
+    t_all = torch.tensor([ms, e2e_s, pp_ms] + (batch_ms or [0.0, 0.0]), dtype=torch.float64, device="cuda")
     if use_dist:
         dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
     ms_max, e2e_max, pp_max = float(t_all[0]), float(t_all[1]), float(t_all[2])
+    batch_max = [float(t_all[3]), float(t_all[4])]
 
     if rank == 0:
         tokens = GEN_LEN * args.steps
@@ -325,6 +355,14 @@ def main():
             "gpu_launches": world * tokens,
             "clocks": clocks,
         }
+        if batch_ms:
+            hbm, _ = measured_hbm_peak()
+            out["decode_batch"] = [
+                {"batch_per_gpu": B_, "ms_per_step": t_, "tok_s": world * B_ / (t_ * 1e-3),
+                 "hbm_gbs_algorithmic": batch_step_bytes(B_, avg_ctx) / (t_ * 1e-3) / 1e9,
+                 "frac_of_hbm_peak": batch_step_bytes(B_, avg_ctx) / (t_ * 1e-3) / 1e9 / hbm,
+                 "note": "mk_decode_batch_many: every sequence has its own pp520 prompt and state; kernel sequence per step"}
+                for B_, t_ in zip((8, 16), batch_max)]
         if world == 1 and long_pp:
             out["prefill_long"] = [
                 {"prompt_len": S_, "attention": "block-sparse 128x128: sink 1 + window 4 + top 10%" if sp_ else "dense causal",

@@ -195,6 +195,8 @@ int mk_decode_batch(
     void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
     const void *fused_fa_qkv_base, const void *fused_gate_up_base, void *final_normed, void *hidden_bf16_out,
     int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
+/* LM head of the batched step: 1 (default) = tensor cores with the f32 activations as two bf16 terms, 0 = f32 FMAs. */
+void mk_decode_batch_set_lm_head(int tensor_cores);
 int mk_decode_batch_many(
     int steps, int *tokens, int *positions, int *tokens_log, int batch,
     const void *embed_weight, const MkLayerWeights *layers, const void *final_norm_w, const void *lm_head_w,

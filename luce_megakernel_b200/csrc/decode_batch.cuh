@@ -6,78 +6,105 @@
 //   tokens int32 [B], positions int32 [B] (each sequence has its own length),
 //   fa_k_cache / fa_v_cache bf16 [B][n_fa][2][max_seq][256], dn_states f32 [B][n_dn][16][128][128],
 //   conv_bufs f32 [B][n_dn][6144][4].
-// Row-wise work (norms, projections as tcgen05 GEMMs with M = B, gates, SwiGLU) treats the batch as B rows; the
+// Row-wise work (norms, gates, SwiGLU) treats the batch as B rows, the projections stream each matrix once; the
 // kernels below do the per-sequence work: conv window, recurrent state update, attention over each sequence's own
 // cache, and the LM head with one argmax per sequence.  Rounding points are those of the prompt path.
 
 constexpr int BATCH_MAX = 16;
 
-// Causal conv1d (window of four inputs) + SiLU + L2 norms for the new token of every sequence, and the shifted
-// window written back.  Block = (sequence, head), thread c = channel c of q, k and v of that head.
-// Same arithmetic as k_dn_preproject at t = 0 followed by k_dn_conv_state with S = 1.
-__global__ void k_dnb_conv(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ conv_w,
-                           float* __restrict__ conv_state, size_t seq_stride, float* __restrict__ pre, float* __restrict__ kq) {
+// The whole token mixer of a Gated DeltaNet layer for one (sequence, head) per block, 32 warps:
+//   gates from the raw beta / alpha products, causal conv1d (window of four inputs) + SiLU + L2 norms with the
+//   shifted window written back, one gated-delta-rule step on the head's 128 x 128 state (warp = four value rows,
+//   lane = four keys; the rows are requested before anything else so that their latency hides the rest), and the
+//   gated RMSNorm of the head's output, written as bf16 for the out projection.
+// Arithmetic: k_dn_gates_mma's epilogue, k_dn_preproject at t = 0 + k_dn_conv_state with S = 1, one iteration of
+// k_dn_scan, k_dn_gated_norm.  The step is bound by the state traffic (2 x 64 KB per block).
+// qkv, z: bf16 [B][6144], [B][2048]; graw: f32 [B][32] = W_b x | W_a x; act: bf16 [B][2048].
+__global__ void __launch_bounds__(1024) k_dnb_layer(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ z,
+                                                    const float* __restrict__ graw, const __nv_bfloat16* __restrict__ conv_w,
+                                                    const __nv_bfloat16* __restrict__ a_log, const __nv_bfloat16* __restrict__ dt_bias,
+                                                    const __nv_bfloat16* __restrict__ norm_w, float* __restrict__ conv_state,
+                                                    size_t conv_seq_stride, float* __restrict__ state, size_t state_seq_stride,
+                                                    __nv_bfloat16* __restrict__ act) {
     pdl_enter();
-    const int b = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
-    float* cs = conv_state + (size_t)b * seq_stride;
-    __shared__ float red[3][4];
-    float val[3];
-#pragma unroll
-    for (int r = 0; r < 3; ++r) {
-        const int ch = r * DN_QK + h * DN_KEY + c;
-        const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + ch);
-        const float w4[4] = {bf_lo(wr.x), bf_hi(wr.x), bf_lo(wr.y), bf_hi(wr.y)};
-        const float4 old = *reinterpret_cast<const float4*>(cs + ch * 4);
-        const float x[4] = {old.y, old.z, old.w, ld_bf(qkv + (size_t)b * DN_CONV_CH + ch)};
-        float co = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) co += x[k] * w4[k];
-        val[r] = silu_f(co);
-        *reinterpret_cast<float4*>(cs + ch * 4) = make_float4(x[0], x[1], x[2], x[3]);
-    }
-    float sq = warp_sum(val[0] * val[0]), sk = warp_sum(val[1] * val[1]), sqk = warp_sum(val[0] * val[1]);
-    if ((c & 31) == 0) { red[0][c >> 5] = sq; red[1][c >> 5] = sk; red[2][c >> 5] = sqk; }
-    __syncthreads();
-    sq = red[0][0] + red[0][1] + red[0][2] + red[0][3];
-    sk = red[1][0] + red[1][1] + red[1][2] + red[1][3];
-    sqk = red[2][0] + red[2][1] + red[2][2] + red[2][3];
-    const float qn = rsqrtf(sq + 1e-6f) * 0.08838834764831845f, kn = rsqrtf(sk + 1e-6f);
-    float* dst = pre + (size_t)b * DN_CONV_CH + h * DN_KEY + c;
-    dst[0] = val[0] * qn;
-    dst[DN_QK] = val[1] * kn;
-    dst[2 * DN_QK] = val[2];
-    if (c == 0) kq[(b * 16 + h) * 4 + 2] = sqk * qn * kn;
-}
-
-// One gated-delta-rule step per sequence.  Block = (sequence, head, 16 value rows), warp = one value row, lane =
-// four keys: the state row is read once, updated and written back (the step is bound by that traffic:
-// 2 x 1 MB per sequence and layer).  Arithmetic as one iteration of k_dn_scan.
-__global__ void __launch_bounds__(512) k_dnb_step(const float* __restrict__ pre, const float* __restrict__ gates,
-                                                  float* __restrict__ state, size_t seq_stride, float* __restrict__ o) {
-    pdl_enter();
-    const int b = blockIdx.x >> 7, hb = blockIdx.x & 127;
-    const int h = hb >> 3, slice = hb & 7;
+    const int b = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = slice * 16 + warp;
-    float* srow = state + (size_t)b * seq_stride + ((size_t)h * DN_VAL + row) * DN_KEY;
-    float4 s = reinterpret_cast<const float4*>(srow)[lane];
-    const float* tok = pre + (size_t)b * DN_CONV_CH;
-    const float4 q4 = reinterpret_cast<const float4*>(tok + h * DN_KEY)[lane];
-    const float4 k4 = reinterpret_cast<const float4*>(tok + DN_QK + h * DN_KEY)[lane];
-    const float vj = tok[2 * DN_QK + h * DN_VAL + row];
-    const float4 gt = *reinterpret_cast<const float4*>(gates + ((size_t)b * 16 + h) * 4);     // beta, decay, q.k
-    float stk = s.x * k4.x + s.y * k4.y + s.z * k4.z + s.w * k4.w;
-    float sqv = s.x * q4.x + s.y * q4.y + s.z * q4.z + s.w * q4.w;
+    __shared__ __align__(16) float qs[DN_KEY], ks[DN_KEY], vs[DN_VAL], os[DN_VAL];
+    __shared__ float red[3][4];
+    __shared__ float gate[4];                                 // beta, decay, q.k
+    float* sbase = state + (size_t)b * state_seq_stride + ((size_t)h * DN_VAL + warp * 4) * DN_KEY;
+    float4 s[4];
 #pragma unroll
-    for (int of = 16; of > 0; of >>= 1) {
-        stk += __shfl_xor_sync(0xffffffffu, stk, of);
-        sqv += __shfl_xor_sync(0xffffffffu, sqv, of);
+    for (int r = 0; r < 4; ++r) s[r] = reinterpret_cast<const float4*>(sbase + r * DN_KEY)[lane];
+    if (threadIdx.x < 128) {
+        const int c = threadIdx.x;
+        float* cs = conv_state + (size_t)b * conv_seq_stride;
+        float val[3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+            const int ch = r * DN_QK + h * DN_KEY + c;
+            const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + ch);
+            const float w4[4] = {bf_lo(wr.x), bf_hi(wr.x), bf_lo(wr.y), bf_hi(wr.y)};
+            const float4 old = *reinterpret_cast<const float4*>(cs + ch * 4);
+            const float x[4] = {old.y, old.z, old.w, ld_bf(qkv + (size_t)b * DN_CONV_CH + ch)};
+            float co = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) co += x[k] * w4[k];
+            val[r] = silu_f(co);
+            *reinterpret_cast<float4*>(cs + ch * 4) = make_float4(x[0], x[1], x[2], x[3]);
+        }
+        float sq = warp_sum(val[0] * val[0]), sk = warp_sum(val[1] * val[1]), sqk = warp_sum(val[0] * val[1]);
+        if ((c & 31) == 0) { red[0][c >> 5] = sq; red[1][c >> 5] = sk; red[2][c >> 5] = sqk; }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        sq = red[0][0] + red[0][1] + red[0][2] + red[0][3];
+        sk = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+        sqk = red[2][0] + red[2][1] + red[2][2] + red[2][3];
+        const float qn = rsqrtf(sq + 1e-6f) * 0.08838834764831845f, kn = rsqrtf(sk + 1e-6f);
+        qs[c] = val[0] * qn;
+        ks[c] = val[1] * kn;
+        vs[c] = val[2];
+        if (c == 0) gate[2] = sqk * qn * kn;
+    } else if (threadIdx.x == 128) {
+        gate[0] = 1.0f / (1.0f + expf(-graw[b * 32 + h]));
+        const float x = graw[b * 32 + 16 + h] + ld_bf(dt_bias + h);
+        const float sp = (x > 20.0f) ? x : log1pf(expf(x));
+        gate[1] = expf(-expf(ld_bf(a_log + h)) * sp);
     }
-    const float err = (vj - gt.y * stk) * gt.x;
-    s.x = fmaf(s.x, gt.y, k4.x * err); s.y = fmaf(s.y, gt.y, k4.y * err);
-    s.z = fmaf(s.z, gt.y, k4.z * err); s.w = fmaf(s.w, gt.y, k4.w * err);
-    if (lane == 0) o[(size_t)b * DN_V + h * DN_VAL + row] = gt.y * sqv + err * gt.z;
-    reinterpret_cast<float4*>(srow)[lane] = s;
+    __syncthreads();
+    const float4 q4 = reinterpret_cast<const float4*>(qs)[lane], k4 = reinterpret_cast<const float4*>(ks)[lane];
+    const float beta = gate[0], decay = gate[1], qk = gate[2];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int row = warp * 4 + r;
+        float stk = s[r].x * k4.x + s[r].y * k4.y + s[r].z * k4.z + s[r].w * k4.w;
+        float sqv = s[r].x * q4.x + s[r].y * q4.y + s[r].z * q4.z + s[r].w * q4.w;
+#pragma unroll
+        for (int of = 16; of > 0; of >>= 1) {
+            stk += __shfl_xor_sync(0xffffffffu, stk, of);
+            sqv += __shfl_xor_sync(0xffffffffu, sqv, of);
+        }
+        const float err = (vs[row] - decay * stk) * beta;
+        s[r].x = fmaf(s[r].x, decay, k4.x * err); s[r].y = fmaf(s[r].y, decay, k4.y * err);
+        s[r].z = fmaf(s[r].z, decay, k4.z * err); s[r].w = fmaf(s[r].w, decay, k4.w * err);
+        if (lane == 0) os[row] = decay * sqv + err * qk;
+        reinterpret_cast<float4*>(sbase + r * DN_KEY)[lane] = s[r];
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const size_t off = (size_t)b * DN_V + h * DN_VAL;
+        const float4 o4 = reinterpret_cast<const float4*>(os)[lane];
+        const uint2 z2 = reinterpret_cast<const uint2*>(z + off)[lane];
+        const uint2 w2 = __ldg(reinterpret_cast<const uint2*>(norm_w) + lane);
+        const float ss = warp_sum(o4.x * o4.x + o4.y * o4.y + o4.z * o4.z + o4.w * o4.w);
+        const float rstd = rsqrtf(ss * (1.0f / DN_VAL) + RMS_EPS);
+        const __nv_bfloat162 p0 = __floats2bfloat162_rn(o4.x * rstd * bf_lo(w2.x) * silu_f(bf_lo(z2.x)),
+                                                        o4.y * rstd * bf_hi(w2.x) * silu_f(bf_hi(z2.x)));
+        const __nv_bfloat162 p1 = __floats2bfloat162_rn(o4.z * rstd * bf_lo(w2.y) * silu_f(bf_lo(z2.y)),
+                                                        o4.w * rstd * bf_hi(w2.y) * silu_f(bf_hi(z2.y)));
+        uint2 r;
+        r.x = *reinterpret_cast<const uint32_t*>(&p0); r.y = *reinterpret_cast<const uint32_t*>(&p1);
+        reinterpret_cast<uint2*>(act + off)[lane] = r;
+    }
 }
 
 // Attention of one new query per sequence over that sequence's cache (positions 0 .. pos[b], the new key and
@@ -231,6 +258,338 @@ __global__ void __launch_bounds__(256) k_lm_head_batch(const float* __restrict__
     }
 }
 
+// ---- projections of a batched step ---------------------------------------------------------------------------
+// C[b][n] = sum_k A[b][k] W[n][k] (+ R[b][n]) for B <= 16 rows of activations: pure weight streaming, so the kernel is
+// built around reading W once at full rate, not around the tensor cores' peak.  One CTA per 16 rows of W, its eight
+// warps split K; W goes straight from global memory into mma.sync A fragments (the k order inside a fragment is
+// permuted so that a lane reads 16 contiguous bytes of a row: a dot product does not care, and the activations are
+// permuted the same way), the activations sit in shared memory as the B operand (batch = the n8 columns), f32
+// partial sums of the warps meet in shared memory.  Several matrices that share A (the input projections of a
+// layer) run as segments of one launch.
+// kind: 0 = bf16 output (+ residual R), 1 = f32 output, 2 = SwiGLU pair: C = bf16(silu(bf16(W x)) * bf16(W2 x)), the
+// rounding points of a bf16 gate | up projection followed by k_silu_mul.
+struct SkinnySeg { const __nv_bfloat16* W; const __nv_bfloat16* W2; void* C; const __nv_bfloat16* R; int N; int ldc; int kind; };
+struct SkinnyArgs { SkinnySeg seg[4]; int nseg; };
+
+// norm_w != null: A is the residual stream [B][1024] and the staged activations are its RMSNorm (weights norm_w),
+// exactly k_rmsnorm's arithmetic; every CTA normalises for itself (B x 1024 values: less than a launch costs) and
+// keeps the result in shared memory.  norm_w == null: every lane reads its B fragments straight from A (L2
+// hits), together with the weights of the same k steps.
+// ks > 1 (single plain segment with few rows): ks CTAs share a row group, each takes a slice of K and leaves f32
+// partial sums in `part`; the CTA that arrives last at the group's counter adds them in slice order (same result
+// whichever CTA that is), applies the residual and writes.  The counter resets itself.
+// Persistent: a CTA walks over its share of the (row group, K slice) items; the activations are staged once and the
+// weight stream of the next item is already in flight while the current one is reduced and written.
+template <int NT>      // n8 tiles over the batch: 1 for B <= 8, 2 for B <= 16
+__global__ void __launch_bounds__(256, 2) k_skinny_proj(const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* __restrict__ norm_w,
+                                                                      int B, int K, int lda, SkinnyArgs args, int items, int ks,
+                                                                      float* __restrict__ part, int* __restrict__ counters) {
+    pdl_enter();
+    extern __shared__ __align__(16) uint4 as[];              // norm mode: [NT * 8][K / 8 + 4] activations, rows >= B zero
+    __shared__ float red[8][NT * 8][17];
+    __shared__ int s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    const int rs = K / 8 + 4;                                // row stride in 16-byte units (+64 B: no bank conflicts)
+    const int nst_all = K / 32;                              // a step = 32 k: 64 contiguous bytes of each of 16 rows
+    const bool direct = norm_w == nullptr;
+    const bool pair = args.seg[0].kind == 2;                 // a pair launch has a single segment
+    // a pair splits the warps: 0-3 stream the 16 rows of W, 4-7 the 16 rows of W2, each group splits K four ways
+    const int kw = pair ? (warp & 3) : warp, nkw = pair ? 4 : 8;
+    const int FG = ((nst_all + ks - 1) / ks + 4 * nkw - 1) / (4 * nkw);      // fetches (of four k steps per warp) per item
+    const int mine = (items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+
+    struct Item { const uint4 *w0, *w1; int st_lo, nst, n0, si, kp, ggrp; };
+    auto locate = [&](int j) {
+        Item it;
+        const int gg = blockIdx.x + j * gridDim.x;
+        it.kp = gg % ks; it.ggrp = gg / ks;
+        int grp = it.ggrp, si = 0;
+        while (si + 1 < args.nseg && grp >= args.seg[si].N / 16) { grp -= args.seg[si].N / 16; ++si; }
+        it.si = si; it.n0 = grp * 16;
+        const __nv_bfloat16* Wm = (pair && warp >= 4) ? args.seg[si].W2 : args.seg[si].W;
+        it.w0 = reinterpret_cast<const uint4*>(Wm + (size_t)(it.n0 + g) * K) + tig;
+        it.w1 = reinterpret_cast<const uint4*>(Wm + (size_t)(it.n0 + g + 8) * K) + tig;
+        it.st_lo = (it.kp * nst_all) / ks; it.nst = ((it.kp + 1) * nst_all) / ks;
+        return it;
+    };
+    const uint4* arow[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) arow[t] = reinterpret_cast<const uint4*>(A + (size_t)min(t * 8 + g, B - 1) * lda) + tig;
+    uint4 lo[4], hi[4], bfr[NT][4];
+    auto fetch = [&](int q) {                                // q-th fetch of this warp's stream
+        const Item it = locate(q / FG);
+        const int st0 = it.st_lo + kw + (q % FG) * 4 * nkw;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int st = st0 + nkw * u;
+            if (st < it.nst) { lo[u] = __ldcs(it.w0 + st * 4); hi[u] = __ldcs(it.w1 + st * 4); }
+            else { lo[u] = make_uint4(0, 0, 0, 0); hi[u] = make_uint4(0, 0, 0, 0); }
+            if (direct) {
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+                    bfr[t][u] = (st < it.nst && t * 8 + g < B) ? __ldg(arow[t] + st * 4) : make_uint4(0, 0, 0, 0);
+            }
+        }
+    };
+    if (mine > 0) fetch(0);                                  // weights are on their way while the activations are staged
+    if (!direct) {
+        for (int b = warp; b < NT * 8; b += 8) {
+            if (b < B) rmsnorm_row(reinterpret_cast<const uint4*>(A + (size_t)b * lda), norm_w, as + b * rs, lane);
+            else { for (int i = lane; i < K / 8; i += 32) as[b * rs + i] = make_uint4(0, 0, 0, 0); }
+        }
+        __syncthreads();                                     // activations staged
+    }
+    const int b = threadIdx.x >> 4, n = threadIdx.x & 15;    // epilogue: 256 threads = 16 batch columns x 16 rows
+    const bool writer = threadIdx.x < NT * 8 * 16 && b < B;
+    for (int j = 0; j < mine; ++j) {
+        const Item it = locate(j);
+        float acc[NT][4];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) { acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f; }
+        for (int f = 0; f < FG; ++f) {
+            const int q = j * FG + f;
+            uint4 clo[4], chi[4], cb[NT][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                clo[u] = lo[u]; chi[u] = hi[u];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) cb[t][u] = bfr[t][u];
+            }
+            if (q + 1 < mine * FG) fetch(q + 1);             // next fetch in flight while this one is multiplied
+            const int st0 = it.st_lo + kw + f * 4 * nkw;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int st = st0 + nkw * u;
+                if (st < it.nst) {
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        const uint4 bb = direct ? cb[t][u] : as[(t * 8 + g) * rs + st * 4 + tig];
+                        asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                                     : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                                     : "r"(clo[u].x), "r"(chi[u].x), "r"(clo[u].y), "r"(chi[u].y), "r"(bb.x), "r"(bb.y));
+                        asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                                     : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                                     : "r"(clo[u].z), "r"(chi[u].z), "r"(clo[u].w), "r"(chi[u].w), "r"(bb.z), "r"(bb.w));
+                    }
+                }
+            }
+        }
+        // accumulator element e of tile t: W row g + 8 (e >> 1), batch column 8 t + 2 tig + (e & 1)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) red[warp][t * 8 + 2 * tig + (e & 1)][g + 8 * (e >> 1)] = acc[t][e];
+        }
+        __syncthreads();
+        const SkinnySeg& sg = args.seg[it.si];
+        const size_t o = (size_t)b * sg.ldc + it.n0 + n;
+        const int bc = b & (NT * 8 - 1);
+        if (ks > 1) {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) v += red[w][bc][n];
+            float* mypart = part + ((size_t)it.ggrp * ks) * 256;
+            if (writer) mypart[it.kp * 256 + threadIdx.x] = v;
+            __threadfence();
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                const int old = atomicAdd(counters + it.ggrp, 1);
+                s_last = (old == ks - 1);
+                if (old == ks - 1) counters[it.ggrp] = 0;
+            }
+            __syncthreads();
+            if (s_last && writer) {
+                __threadfence();
+                float tot = 0.f;
+                for (int p = 0; p < ks; ++p) tot += __ldcg(mypart + p * 256 + threadIdx.x);
+                if (sg.R) tot += ld_bf(sg.R + o);
+                reinterpret_cast<__nv_bfloat16*>(sg.C)[o] = __float2bfloat16_rn(tot);
+            }
+        } else if (writer) {
+            if (pair) {
+                const float gsum = (red[0][bc][n] + red[1][bc][n]) + (red[2][bc][n] + red[3][bc][n]);
+                const float usum = (red[4][bc][n] + red[5][bc][n]) + (red[6][bc][n] + red[7][bc][n]);
+                const float gv = __bfloat162float(__float2bfloat16_rn(gsum)), uv = __bfloat162float(__float2bfloat16_rn(usum));
+                reinterpret_cast<__nv_bfloat16*>(sg.C)[o] = __float2bfloat16_rn(silu_f(gv) * uv);
+            } else {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) v += red[w][bc][n];
+                if (sg.R) v += ld_bf(sg.R + o);
+                if (sg.kind == 1) reinterpret_cast<float*>(sg.C)[o] = v;
+                else reinterpret_cast<__nv_bfloat16*>(sg.C)[o] = __float2bfloat16_rn(v);
+            }
+        }
+        __syncthreads();                                     // red and s_last are reused by the next item
+    }
+}
+
+// host side: launch the segments (all N multiples of 16, K a multiple of 32, at most 4 segments)
+constexpr int SKINNY_MAX_GROUPS = 1024;      // row groups a K-split launch may have (counters, partial sums)
+struct SkinnyWs { float* part = nullptr; int* counters = nullptr; bool attr = false; };
+SkinnyWs g_skinny[64];
+
+inline cudaError_t skinny_proj(const void* A, const void* norm_w, int B, int K, int lda, const SkinnyArgs& args, cudaStream_t stream) {
+    int groups = 0;
+    for (int i = 0; i < args.nseg; ++i) {
+        if (args.seg[i].N % 16) return cudaErrorInvalidValue;
+        groups += args.seg[i].N / 16;
+    }
+    if (K % 32 || lda % 8 || B < 1 || B > 16 || groups == 0 || K > INTER || (norm_w && K != HIDDEN)) return cudaErrorInvalidValue;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    SkinnyWs& ws = g_skinny[dev];
+    if (!ws.attr) {
+        cudaError_t e = cudaFuncSetAttribute(k_skinny_proj<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * (HIDDEN / 8 + 4) * 16);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_skinny_proj<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 16 * (HIDDEN / 8 + 4) * 16);
+        if (e == cudaSuccess) e = cudaMalloc((void**)&ws.part, (size_t)SKINNY_MAX_GROUPS * 256 * 4);
+        if (e == cudaSuccess) e = cudaMalloc((void**)&ws.counters, SKINNY_MAX_GROUPS * 4);
+        if (e == cudaSuccess) e = cudaMemset(ws.counters, 0, SKINNY_MAX_GROUPS * 4);
+        if (e != cudaSuccess) return e;
+        ws.attr = true;
+    }
+    // few row groups (the 1024-row out / o / down projections): split K over CTAs until about 256 of them stream
+    int ks = 1;
+    if (args.nseg == 1 && args.seg[0].kind == 0 && !norm_w) {
+        ks = 256 / groups;
+        const int max_ks = (K / 32) / 8;                     // at least eight k steps (one per warp) per CTA
+        if (ks > max_ks) ks = max_ks;
+        if (ks < 1) ks = 1;
+        if (groups * ks > SKINNY_MAX_GROUPS) ks = 1;
+    }
+    const int nt = B <= 8 ? 1 : 2;
+    const size_t smem = norm_w ? (size_t)nt * 8 * (K / 8 + 4) * 16 : 0;
+    static int sms = 0;
+    if (!sms && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    const int items = groups * ks, slots = sms * 2;
+    const int grid = items < slots ? items : slots;
+    if (nt == 1) return launch_pdl(k_skinny_proj<1>, grid, 256, smem, stream, (const __nv_bfloat16*)A, (const __nv_bfloat16*)norm_w, B, K, lda, args, items, ks, ws.part, ws.counters);
+    return launch_pdl(k_skinny_proj<2>, grid, 256, smem, stream, (const __nv_bfloat16*)A, (const __nv_bfloat16*)norm_w, B, K, lda, args, items, ks, ws.part, ws.counters);
+}
+
+// LM head of a batched step on the tensor cores: the same fragment scheme as k_skinny_proj, but a warp keeps a
+// 16-row group of the vocabulary to itself over all of K = 1024 (no cross-warp sum), the f32 activations enter as two
+// bf16 terms (x = hi + lo, relative error 2^-16) accumulated into the same f32 sums, and the epilogue is a running
+// argmax per sequence (lowest index on ties).  Persistent: the warps stride over the 16-row groups, the weight
+// stream is prefetched across group boundaries.  Per block and sequence the best logit goes to bval / bidx [B][grid].
+template <int NT>
+__global__ void __launch_bounds__(256, 2) k_lm_head_mma(const float* __restrict__ x, int B, const __nv_bfloat16* __restrict__ W,
+                                                        int vocab, float* __restrict__ bval, int* __restrict__ bidx) {
+    pdl_enter();
+    constexpr int RS = HIDDEN / 8 + 4;                        // row stride in 16-byte units (+64 B: no bank conflicts)
+    extern __shared__ __align__(16) uint4 xh[];               // hi [NT * 8][RS], then lo [NT * 8][RS]
+    __shared__ float sv[8][NT * 8];
+    __shared__ int si[8][NT * 8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    uint4* xlo = xh + NT * 8 * RS;
+    for (int i = threadIdx.x; i < NT * 8 * (HIDDEN / 8); i += 256) {
+        const int b = i / (HIDDEN / 8), c = i - b * (HIDDEN / 8);
+        uint32_t h[4] = {0, 0, 0, 0}, l[4] = {0, 0, 0, 0};
+        if (b < B) {
+            const float4 a = *reinterpret_cast<const float4*>(x + (size_t)b * HIDDEN + c * 8);
+            const float4 d = *reinterpret_cast<const float4*>(x + (size_t)b * HIDDEN + c * 8 + 4);
+            const float v[8] = {a.x, a.y, a.z, a.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+                const __nv_bfloat162 ll = __floats2bfloat162_rn(v[2 * e] - __low2float(hh), v[2 * e + 1] - __high2float(hh));
+                h[e] = *reinterpret_cast<const uint32_t*>(&hh);
+                l[e] = *reinterpret_cast<const uint32_t*>(&ll);
+            }
+        }
+        xh[b * RS + c] = make_uint4(h[0], h[1], h[2], h[3]);
+        xlo[b * RS + c] = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+    const int ngroups = (vocab + 15) / 16, nwarps = gridDim.x * 8, wg = blockIdx.x * 8 + warp;
+    const int mine = wg < ngroups ? (ngroups - wg + nwarps - 1) / nwarps : 0;       // groups of this warp
+    constexpr int FG = HIDDEN / 32 / 4;                       // fetches of four k steps per group: 8
+    uint4 lo[4], hi[4];
+    auto fetch = [&](int q) {                                 // q-th fetch of this warp's stream
+        const int n0 = (wg + (q / FG) * nwarps) * 16, st0 = (q % FG) * 4;
+        const uint4* w0 = reinterpret_cast<const uint4*>(W + (size_t)min(n0 + g, vocab - 1) * HIDDEN) + tig;
+        const uint4* w1 = reinterpret_cast<const uint4*>(W + (size_t)min(n0 + g + 8, vocab - 1) * HIDDEN) + tig;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { lo[u] = __ldcs(w0 + (st0 + u) * 4); hi[u] = __ldcs(w1 + (st0 + u) * 4); }
+    };
+    if (mine > 0) fetch(0);
+    __syncthreads();
+    float best[NT][2];
+    int besti[NT][2];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) { best[t][0] = best[t][1] = -INFINITY; besti[t][0] = besti[t][1] = 0x7fffffff; }
+    float acc[NT][4];
+    for (int q = 0; q < mine * FG; ++q) {
+        const int st0 = (q % FG) * 4;
+        if (st0 == 0) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) { acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f; }
+        }
+        uint4 clo[4], chi[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { clo[u] = lo[u]; chi[u] = hi[u]; }
+        if (q + 1 < mine * FG) fetch(q + 1);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const int off = (t * 8 + g) * RS + (st0 + u) * 4 + tig;
+                const uint4 bh = xh[off], bl = xlo[off];
+                asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                             : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                             : "r"(clo[u].x), "r"(chi[u].x), "r"(clo[u].y), "r"(chi[u].y), "r"(bh.x), "r"(bh.y));
+                asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                             : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                             : "r"(clo[u].z), "r"(chi[u].z), "r"(clo[u].w), "r"(chi[u].w), "r"(bh.z), "r"(bh.w));
+                asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                             : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                             : "r"(clo[u].x), "r"(chi[u].x), "r"(clo[u].y), "r"(chi[u].y), "r"(bl.x), "r"(bl.y));
+                asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                             : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                             : "r"(clo[u].z), "r"(chi[u].z), "r"(clo[u].w), "r"(chi[u].w), "r"(bl.z), "r"(bl.w));
+            }
+        }
+        if (st0 == (FG - 1) * 4) {
+            // group done: element e of tile t = logit of row n0 + g + 8 (e >> 1) for sequence 8 t + 2 tig + (e & 1)
+            const int n0 = (wg + (q / FG) * nwarps) * 16;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const int r0 = n0 + g, r1 = n0 + g + 8;
+                    float v = r0 < vocab ? acc[t][c] : -INFINITY;
+                    int ix = r0;
+                    const float v1 = r1 < vocab ? acc[t][2 + c] : -INFINITY;
+                    if (v1 > v) { v = v1; ix = r1; }
+#pragma unroll
+                    for (int of = 4; of < 32; of <<= 1) {
+                        const float ov = __shfl_xor_sync(0xffffffffu, v, of);
+                        const int oi = __shfl_xor_sync(0xffffffffu, ix, of);
+                        if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
+                    }
+                    if (v > best[t][c] || (v == best[t][c] && ix < besti[t][c])) { best[t][c] = v; besti[t][c] = ix; }
+                }
+            }
+        }
+    }
+    if (g == 0) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) { sv[warp][t * 8 + 2 * tig + c] = best[t][c]; si[warp][t * 8 + 2 * tig + c] = besti[t][c]; }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < NT * 8 && threadIdx.x < B) {
+        const int b = threadIdx.x;
+        float bv = sv[0][b];
+        int bi = si[0][b];
+        for (int w = 1; w < 8; ++w)
+            if (sv[w][b] > bv || (sv[w][b] == bv && si[w][b] < bi)) { bv = sv[w][b]; bi = si[w][b]; }
+        bval[(size_t)b * gridDim.x + blockIdx.x] = bv;
+        bidx[(size_t)b * gridDim.x + blockIdx.x] = bi;
+    }
+}
+
 // After a step of a multi-step run: the chosen tokens become the next inputs, every sequence moves on by one.
 __global__ void k_batch_advance(int* __restrict__ tokens, const int* __restrict__ chosen, int* __restrict__ positions,
                                 int* __restrict__ log_row, int B) {
@@ -243,7 +602,8 @@ __global__ void k_batch_advance(int* __restrict__ tokens, const int* __restrict_
     if (log_row) log_row[b] = t;
 }
 
-struct BatchWs { float *normed_f32 = nullptr, *bval = nullptr; int *bidx = nullptr, *chosen = nullptr; };
+int g_batch_lm_mma = 1;            // LM head of the batched step: 1 = tensor cores (bf16 hi + lo), 0 = f32 CUDA cores
+struct BatchWs { float *normed_f32 = nullptr, *bval = nullptr, *graw = nullptr; int *bidx = nullptr, *chosen = nullptr; };
 BatchWs g_bws[64];
 
 cudaError_t ensure_batch_ws(BatchWs& w) {
@@ -252,6 +612,7 @@ cudaError_t ensure_batch_ws(BatchWs& w) {
     if (e == cudaSuccess) e = cudaMalloc((void**)&w.bval, (size_t)BATCH_MAX * LM_BLOCKS * 4);
     if (e == cudaSuccess) e = cudaMalloc((void**)&w.bidx, (size_t)BATCH_MAX * LM_BLOCKS * 4);
     if (e == cudaSuccess) e = cudaMalloc((void**)&w.chosen, BATCH_MAX * 4);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&w.graw, BATCH_MAX * 32 * 4);
     return e;
 }
 
@@ -268,14 +629,16 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
     static bool attr[64] = {false};
     if (!attr[dev]) {
         PF_CHECK(cudaFuncSetAttribute(k_lm_head_batch<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 16 * 256 * 16), "lm head smem");
+        PF_CHECK(cudaFuncSetAttribute(k_lm_head_mma<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * 8 * (HIDDEN / 8 + 4) * 16), "lm head smem");
         attr[dev] = true;
     }
     typedef __nv_bfloat16 bf;
-    auto gemm = [&](const void* A, const void* W, void* C, const void* R, int N, int K, int ldc) {
-        gemm_set_small_m_split(true);
-        const cudaError_t e = gemm_bf16_tn(A, W, C, R, B, N, K, K, ldc, w.err, stream);
-        gemm_set_small_m_split(false);
-        return e;
+    // projections: up to four matrices that share the activations per launch
+    auto proj = [&](const void* A, const void* norm_w, int K, std::initializer_list<SkinnySeg> segs) {
+        SkinnyArgs a;
+        a.nseg = 0;
+        for (const SkinnySeg& sg : segs) a.seg[a.nseg++] = sg;
+        return skinny_proj(A, norm_w, B, K, K, a, stream);
     };
     auto blocks_for_warps = [&](long long nw) { return (unsigned)((nw + 7) / 8); };
     const size_t kv_seq = (size_t)n_fa * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;          // elements per sequence
@@ -287,50 +650,58 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
         LayerView lv;
         const int rc = source(li, lv);
         if (rc != MK_OK) return rc;
-        launch_pdl(k_rmsnorm, blocks_for_warps(B), 256, 0, stream, w.hidden, (const bf*)lv.in_norm, w.normed, B);
+        // every input projection normalises the residual stream itself (lv.in_norm / lv.post_norm)
         if (lv.type == 0) {
             float* state = (float*)dn_states + (size_t)dn_idx * DN_HEADS * DN_VAL * DN_KEY;
             float* cstate = (float*)conv_bufs + (size_t)dn_idx * DN_CONV_CH * DN_CONV_K;
-            PF_CHECK(gemm(w.normed, lv.w_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
-            PF_CHECK(gemm(w.normed, lv.w_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
-            launch_pdl(k_dn_gates_mma, (unsigned)((B + 15) / 16), 128, 0, stream, w.normed, (const bf*)lv.w_b, (const bf*)lv.w_a,
-                       (const bf*)lv.a_log, (const bf*)lv.dt_bias, w.beta, B);
-            launch_pdl(k_dnb_conv, dim3(B, DN_HEADS), 128, 0, stream, w.wide, (const bf*)lv.conv_w, cstate, cv_seq, w.pre, w.beta);
-            launch_pdl(k_dnb_step, (unsigned)(B * 128), 512, 0, stream, w.pre, w.beta, state, st_seq, w.o);
-            launch_pdl(k_dn_gated_norm, blocks_for_warps((long long)B * DN_HEADS), 256, 0, stream, w.o, w.z, (const bf*)lv.dn_norm, w.act, B);
-            PF_CHECK(gemm(w.act, lv.w_out, w.hidden, w.hidden, HIDDEN, DN_V, HIDDEN), "gemm out");
+            PF_CHECK(proj(w.hidden, lv.in_norm, HIDDEN, {{(const bf*)lv.w_qkv, nullptr, w.wide, nullptr, DN_CONV_CH, DN_CONV_CH, 0},
+                                                         {(const bf*)lv.w_z, nullptr, w.z, nullptr, DN_V, DN_V, 0},
+                                                         {(const bf*)lv.w_b, nullptr, bw.graw, nullptr, 16, 32, 1},
+                                                         {(const bf*)lv.w_a, nullptr, bw.graw + 16, nullptr, 16, 32, 1}}),
+                     "DeltaNet input projections");
+            launch_pdl(k_dnb_layer, dim3(B, DN_HEADS), 1024, 0, stream, (const bf*)w.wide, (const bf*)w.z, (const float*)bw.graw,
+                       (const bf*)lv.conv_w, (const bf*)lv.a_log, (const bf*)lv.dt_bias, (const bf*)lv.dn_norm, cstate, cv_seq, state,
+                       st_seq, w.act);
+            PF_CHECK(proj(w.act, nullptr, DN_V, {{(const bf*)lv.w_out, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "out projection");
             ++dn_idx;
         } else {
             bf* kc = (bf*)fa_k_cache + (size_t)fa_idx * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;
             bf* vc = (bf*)fa_v_cache + (size_t)fa_idx * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;
             if (lv.w_faqkv) {
-                PF_CHECK(gemm(w.normed, lv.w_faqkv, w.wide, nullptr, FA_QKV_ROWS, HIDDEN, FA_QKV_ROWS), "gemm fa qkv");
+                PF_CHECK(proj(w.hidden, lv.in_norm, HIDDEN, {{(const bf*)lv.w_faqkv, nullptr, w.wide, nullptr, FA_QKV_ROWS, FA_QKV_ROWS, 0}}),
+                         "q, k, v projections");
             } else {
-                PF_CHECK(gemm(w.normed, lv.w_q, w.wide, nullptr, FA_QPROJ, HIDDEN, FA_QKV_ROWS), "gemm q");
-                PF_CHECK(gemm(w.normed, lv.w_k, w.wide + FA_QPROJ, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm k");
-                PF_CHECK(gemm(w.normed, lv.w_v, w.wide + FA_QPROJ + FA_KV_SIZE, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm v");
+                PF_CHECK(proj(w.hidden, lv.in_norm, HIDDEN,
+                              {{(const bf*)lv.w_q, nullptr, w.wide, nullptr, FA_QPROJ, FA_QKV_ROWS, 0},
+                               {(const bf*)lv.w_k, nullptr, w.wide + FA_QPROJ, nullptr, FA_KV_SIZE, FA_QKV_ROWS, 0},
+                               {(const bf*)lv.w_v, nullptr, w.wide + FA_QPROJ + FA_KV_SIZE, nullptr, FA_KV_SIZE, FA_QKV_ROWS, 0}}),
+                         "q, k, v projections");
             }
             launch_pdl(k_fa_norm_rope, blocks_for_warps((long long)B * 12), 256, 0, stream, w.wide, (const bf*)lv.q_norm,
                        (const bf*)lv.k_norm, kc, vc, B, max_seq_len, positions, kv_seq);
             launch_pdl(k_fab_attention, dim3(B, FA_Q_HEADS), 256, 0, stream, (const bf*)w.wide, (const bf*)kc, (const bf*)vc, kv_seq,
                        positions, max_seq_len, w.act);
-            PF_CHECK(gemm(w.act, lv.w_o, w.hidden, w.hidden, HIDDEN, FA_Q_SIZE, HIDDEN), "gemm o");
+            PF_CHECK(proj(w.act, nullptr, FA_Q_SIZE, {{(const bf*)lv.w_o, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "o projection");
             ++fa_idx;
         }
-        launch_pdl(k_rmsnorm, blocks_for_warps(B), 256, 0, stream, w.hidden, (const bf*)lv.post_norm, w.normed, B);
-        if (lv.w_gateup) {
-            PF_CHECK(gemm(w.normed, lv.w_gateup, w.wide, nullptr, 2 * INTER, HIDDEN, 2 * INTER), "gemm gate_up");
-        } else {
-            PF_CHECK(gemm(w.normed, lv.w_gate, w.wide, nullptr, INTER, HIDDEN, 2 * INTER), "gemm gate");
-            PF_CHECK(gemm(w.normed, lv.w_up, w.wide + INTER, nullptr, INTER, HIDDEN, 2 * INTER), "gemm up");
-        }
-        launch_pdl(k_silu_mul, (unsigned)(((size_t)B * (INTER / 8) + 255) / 256), 256, 0, stream, w.wide, w.act, B);
-        PF_CHECK(gemm(w.act, lv.w_down, w.hidden, w.hidden, HIDDEN, INTER, HIDDEN), "gemm down");
+        // gate and up rows meet in one CTA, which applies SwiGLU before it writes
+        const bf* wg = lv.w_gateup ? (const bf*)lv.w_gateup : (const bf*)lv.w_gate;
+        const bf* wu = lv.w_gateup ? (const bf*)lv.w_gateup + (size_t)INTER * HIDDEN : (const bf*)lv.w_up;
+        PF_CHECK(proj(w.hidden, lv.post_norm, HIDDEN, {{wg, wu, w.act, nullptr, INTER, INTER, 2}}), "gate and up projections");
+        PF_CHECK(proj(w.act, nullptr, INTER, {{(const bf*)lv.w_down, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "down projection");
     }
     launch_pdl(k_final_norm, B, 512, 0, stream, w.hidden, (const bf*)final_norm_w, bw.normed_f32, (bf*)final_normed, (bf*)hidden_bf16_out);
-    if (B <= 8) launch_pdl(k_lm_head_batch<8>, LM_BLOCKS, 256, 8 * 256 * 16, stream, bw.normed_f32, B, (const bf*)lm_head_w, vocab, bw.bval, bw.bidx);
-    else launch_pdl(k_lm_head_batch<16>, LM_BLOCKS / 2, 256, 16 * 256 * 16, stream, bw.normed_f32, B, (const bf*)lm_head_w, vocab, bw.bval, bw.bidx);
-    launch_pdl(k_lm_reduce, B, 32, 0, stream, bw.bval, bw.bidx, B <= 8 ? LM_BLOCKS : LM_BLOCKS / 2, output_tokens);
+    constexpr int LMB = 296;                                  // two persistent blocks per SM
+    constexpr int LM_SMEM1 = 2 * 8 * (HIDDEN / 8 + 4) * 16, LM_SMEM2 = 2 * LM_SMEM1;
+    if (g_batch_lm_mma) {
+        if (B <= 8) launch_pdl(k_lm_head_mma<1>, LMB, 256, LM_SMEM1, stream, (const float*)bw.normed_f32, B, (const bf*)lm_head_w, vocab, bw.bval, bw.bidx);
+        else launch_pdl(k_lm_head_mma<2>, LMB, 256, LM_SMEM2, stream, (const float*)bw.normed_f32, B, (const bf*)lm_head_w, vocab, bw.bval, bw.bidx);
+        launch_pdl(k_lm_reduce, B, 32, 0, stream, bw.bval, bw.bidx, LMB, output_tokens);
+    } else {
+        if (B <= 8) launch_pdl(k_lm_head_batch<8>, LM_BLOCKS, 256, 8 * 256 * 16, stream, bw.normed_f32, B, (const bf*)lm_head_w, vocab, bw.bval, bw.bidx);
+        else launch_pdl(k_lm_head_batch<16>, LM_BLOCKS / 2, 256, 16 * 256 * 16, stream, bw.normed_f32, B, (const bf*)lm_head_w, vocab, bw.bval, bw.bidx);
+        launch_pdl(k_lm_reduce, B, 32, 0, stream, bw.bval, bw.bidx, B <= 8 ? LM_BLOCKS : LM_BLOCKS / 2, output_tokens);
+    }
     PF_CHECK(cudaGetLastError(), "batched step launch");
     return MK_OK;
 }

@@ -290,8 +290,6 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int k, int ld, int b
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool g_small_m_split = false;
-
 template <int BN>
 cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc, int* err_flag,
                         int sms, cudaStream_t stream) {
@@ -307,12 +305,10 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
     if (!make_map(&ma, A, M, K, lda, BM) || !make_map(&mw, W, N, K, K, BN)) return cudaErrorInvalidValue;
     const int ntiles = ((M + BM - 1) / BM) * (N / BN);
     // split K when the tiles would leave most SMs idle and every part still has a few k-steps
-    // A batched decode step (M <= 16) is weight streaming: split K further so that every SM pulls weights.
-    const bool stream_w = g_small_m_split && M <= 16;
     int ks = sms / ntiles;
-    if (ks > (stream_w ? 16 : 4)) ks = stream_w ? 16 : 4;
-    while (ks > 1 && (K / BK) / ks < (stream_w ? 2 : 4)) --ks;
-    if (BN == 128 && ks >= 2 && (K >= 2048 || stream_w)) {      // only the long-K projections: K = 1024 products keep one summation order
+    if (ks > 4) ks = 4;
+    while (ks > 1 && (K / BK) / ks < 4) --ks;
+    if (BN == 128 && ks >= 2 && K >= 2048) {      // only the long-K projections: K = 1024 products keep one summation order
         static float* ws = nullptr;
         static size_t ws_bytes = 0;
         const size_t need = (size_t)ks * M * N * sizeof(float);
@@ -334,8 +330,6 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
 }
 
 }  // namespace
-
-void gemm_set_small_m_split(bool on) { g_small_m_split = on; }
 
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
                          int* err_flag, cudaStream_t stream) {

@@ -25,10 +25,6 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 // err_flag: device int, set to 1 if a bounded wait ran out inside the kernel.
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
                          int* err_flag, cudaStream_t stream);
-// Host-side switch for the calls that follow: with it on, products with M <= 16 (a batched decode step, bound by
-// reading W once) split K over up to 16 CTAs per tile so that every SM streams weights.  Off by default: the
-// prompt path keeps one summation order per (N, K).
-void gemm_set_small_m_split(bool on);
 
 // Gated delta rule over a prompt in chunks of 64 tokens (all 16 heads of one layer).
 // qkv: bf16 [S][6144] projection outputs q | k | v (the causal conv1d + SiLU and the L2 norms are applied inside);

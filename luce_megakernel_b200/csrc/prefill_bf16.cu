@@ -41,12 +41,8 @@ __global__ void k_embed(const int* __restrict__ tok, const __nv_bfloat16* __rest
 }
 
 // one warp per row: out = bf16( x * rsqrt(mean x^2 + eps) * (1 + w) )   (reference: prefill.cu:72-88)
-__global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
-                          __nv_bfloat16* __restrict__ out, int S) {
-    pdl_enter();
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (row >= S) return;
-    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)row * HIDDEN);
+// dst may be global or shared memory (the batched step normalises while it stages its activations).
+__device__ __forceinline__ void rmsnorm_row(const uint4* __restrict__ src, const __nv_bfloat16* __restrict__ w, uint4* dst, int lane) {
     float v[32];
     float ss = 0.f;
 #pragma unroll
@@ -60,7 +56,6 @@ __global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bfloat
     for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
     ss = warp_sum(ss);
     const float rstd = rsqrtf(ss * (1.0f / HIDDEN) + RMS_EPS);
-    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * HIDDEN);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const uint4 wu = __ldg(reinterpret_cast<const uint4*>(w) + i * 32 + lane);
@@ -74,6 +69,14 @@ __global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bfloat
         }
         dst[i * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
     }
+}
+
+__global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                          __nv_bfloat16* __restrict__ out, int S) {
+    pdl_enter();
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= S) return;
+    rmsnorm_row(reinterpret_cast<const uint4*>(x + (size_t)row * HIDDEN), w, reinterpret_cast<uint4*>(out + (size_t)row * HIDDEN), lane);
 }
 
 // ---- DeltaNet pieces ---------------------------------------------------------------------------
@@ -1037,6 +1040,8 @@ int decode_batch_entry(int steps, int* tokens, int* positions, int* output_token
 }
 }  // namespace
 }  // namespace mk
+
+extern "C" void mk_decode_batch_set_lm_head(int tensor_cores) { mk::g_batch_lm_mma = tensor_cores ? 1 : 0; }
 
 extern "C" int mk_decode_batch(
     const int* tokens, const int* positions, int* output_tokens, int batch,
