@@ -12,30 +12,35 @@
 
 constexpr int BATCH_MAX = 16;
 
-// The whole token mixer of a Gated DeltaNet layer for one (sequence, head) per block, 32 warps:
+// The whole token mixer of a Gated DeltaNet layer for one (sequence, head) per block, 16 warps (two blocks per SM):
 //   gates from the raw beta / alpha products, causal conv1d (window of four inputs) + SiLU + L2 norms with the
-//   shifted window written back, one gated-delta-rule step on the head's 128 x 128 state (warp = four value rows,
+//   shifted window written back, one gated-delta-rule step on the head's 128 x 128 state (warp = eight value rows,
 //   lane = four keys; the rows are requested before anything else so that their latency hides the rest), and the
 //   gated RMSNorm of the head's output, written as bf16 for the out projection.
 // Arithmetic: k_dn_gates_mma's epilogue, k_dn_preproject at t = 0 + k_dn_conv_state with S = 1, one iteration of
 // k_dn_scan, k_dn_gated_norm.  The step is bound by the state traffic (2 x 64 KB per block).
 // qkv, z: bf16 [B][6144], [B][2048]; graw: f32 [B][32] = W_b x | W_a x; act: bf16 [B][2048].
-__global__ void __launch_bounds__(1024) k_dnb_layer(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ z,
+__global__ void __launch_bounds__(512, 2) k_dnb_layer(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ z,
                                                     const float* __restrict__ graw, const __nv_bfloat16* __restrict__ conv_w,
                                                     const __nv_bfloat16* __restrict__ a_log, const __nv_bfloat16* __restrict__ dt_bias,
                                                     const __nv_bfloat16* __restrict__ norm_w, float* __restrict__ conv_state,
                                                     size_t conv_seq_stride, float* __restrict__ state, size_t state_seq_stride,
                                                     __nv_bfloat16* __restrict__ act) {
-    pdl_enter();
+    pdl_launch_next();
+    // the head's state (64 KB, contiguous) is not written by the projection kernel before this one
+    if (threadIdx.x == 0)
+        l2_prefetch(state + (size_t)blockIdx.x * state_seq_stride + (size_t)blockIdx.y * DN_VAL * DN_KEY, DN_VAL * DN_KEY * 4);
+    pdl_wait_prior();
     const int b = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ __align__(16) float qs[DN_KEY], ks[DN_KEY], vs[DN_VAL], os[DN_VAL];
     __shared__ float red[3][4];
     __shared__ float gate[4];                                 // beta, decay, q.k
-    float* sbase = state + (size_t)b * state_seq_stride + ((size_t)h * DN_VAL + warp * 4) * DN_KEY;
-    float4 s[4];
+    constexpr int RW = 8;                                     // value rows per warp
+    float* sbase = state + (size_t)b * state_seq_stride + ((size_t)h * DN_VAL + warp * RW) * DN_KEY;
+    float4 s[RW];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) s[r] = reinterpret_cast<const float4*>(sbase + r * DN_KEY)[lane];
+    for (int r = 0; r < RW; ++r) s[r] = reinterpret_cast<const float4*>(sbase + r * DN_KEY)[lane];
     if (threadIdx.x < 128) {
         const int c = threadIdx.x;
         float* cs = conv_state + (size_t)b * conv_seq_stride;
@@ -74,8 +79,8 @@ __global__ void __launch_bounds__(1024) k_dnb_layer(const __nv_bfloat16* __restr
     const float4 q4 = reinterpret_cast<const float4*>(qs)[lane], k4 = reinterpret_cast<const float4*>(ks)[lane];
     const float beta = gate[0], decay = gate[1], qk = gate[2];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int row = warp * 4 + r;
+    for (int r = 0; r < RW; ++r) {
+        const int row = warp * RW + r;
         float stk = s[r].x * k4.x + s[r].y * k4.y + s[r].z * k4.z + s[r].w * k4.w;
         float sqv = s[r].x * q4.x + s[r].y * q4.y + s[r].z * q4.z + s[r].w * q4.w;
 #pragma unroll
@@ -284,7 +289,21 @@ template <int NT>      // n8 tiles over the batch: 1 for B <= 8, 2 for B <= 16
 __global__ void __launch_bounds__(256, 2) k_skinny_proj(const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* __restrict__ norm_w,
                                                                       int B, int K, int lda, SkinnyArgs args, int items, int ks,
                                                                       float* __restrict__ part, int* __restrict__ counters) {
-    pdl_enter();
+    pdl_launch_next();
+    // The weights do not depend on the previous kernel: ask for this CTA's row groups (16 rows x K, contiguous)
+    // to be brought into L2 while the predecessor is still finishing.
+    if (threadIdx.x < 32) {
+        const int mine_ = (items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+        for (int j = threadIdx.x; j < mine_; j += 32) {
+            const int gg = blockIdx.x + j * gridDim.x;
+            if (gg % ks) continue;                           // one CTA of a K-split group asks for the whole group
+            int grp = gg / ks, si = 0;
+            while (si + 1 < args.nseg && grp >= args.seg[si].N / 16) { grp -= args.seg[si].N / 16; ++si; }
+            l2_prefetch(args.seg[si].W + (size_t)grp * 16 * K, 16u * K * 2u);
+            if (args.seg[si].kind == 2) l2_prefetch(args.seg[si].W2 + (size_t)grp * 16 * K, 16u * K * 2u);
+        }
+    }
+    pdl_wait_prior();
     extern __shared__ __align__(16) uint4 as[];              // norm mode: [NT * 8][K / 8 + 4] activations, rows >= B zero
     __shared__ float red[8][NT * 8][17];
     __shared__ int s_last;
@@ -424,6 +443,81 @@ __global__ void __launch_bounds__(256, 2) k_skinny_proj(const __nv_bfloat16* __r
     }
 }
 
+// Projections that read the residual stream (K = 1024: DeltaNet / attention input matrices, gate and up): the same
+// fragment scheme as k_skinny_proj, one item per CTA and no loop at all: a warp's share of K is four k steps, whose
+// weights are requested before the kernel even waits for its predecessor (weights are constants), the RMSNorm of the
+// B rows (k_rmsnorm's arithmetic) is staged in shared memory meanwhile.  Three CTAs per SM, so nearly
+// every item of the largest launch is resident at once.  A SwiGLU pair puts 8 gate rows and the matching 8 up rows
+// into one 16-row tile, so silu(g) * u happens in the epilogue of the thread that owns both.
+template <int NT>
+__global__ void __launch_bounds__(256, 3) k_skinny_norm(const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* __restrict__ norm_w,
+                                                                      int B, SkinnyArgs args) {
+    pdl_launch_next();
+    constexpr int K = HIDDEN, RS = K / 8 + 4;
+    extern __shared__ __align__(16) uint4 as[];              // [NT * 8][RS] normalised activations, rows >= B zero
+    __shared__ float red[8][NT * 8][17];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    const bool pair = args.seg[0].kind == 2;                 // a pair launch has a single segment
+    const int rows = pair ? 8 : 16;
+    int grp = blockIdx.x, si = 0;
+    while (si + 1 < args.nseg && grp >= args.seg[si].N / rows) { grp -= args.seg[si].N / rows; ++si; }
+    const SkinnySeg& sg = args.seg[si];
+    const int n0 = grp * rows;
+    const uint4* w0 = reinterpret_cast<const uint4*>(sg.W + (size_t)(n0 + g) * K) + tig;
+    const uint4* w1 = reinterpret_cast<const uint4*>(pair ? sg.W2 + (size_t)(n0 + g) * K : sg.W + (size_t)(n0 + g + 8) * K) + tig;
+    uint4 lo[4], hi[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) { lo[u] = __ldcs(w0 + (warp + 8 * u) * 4); hi[u] = __ldcs(w1 + (warp + 8 * u) * 4); }
+    pdl_wait_prior();
+    for (int b = warp; b < NT * 8; b += 8) {
+        if (b < B) rmsnorm_row(reinterpret_cast<const uint4*>(A + (size_t)b * K), norm_w, as + b * RS, lane);
+        else { for (int i = lane; i < K / 8; i += 32) as[b * RS + i] = make_uint4(0, 0, 0, 0); }
+    }
+    __syncthreads();
+    float acc[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) { acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f; }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const uint4 bb = as[(t * 8 + g) * RS + (warp + 8 * u) * 4 + tig];
+            asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                         : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                         : "r"(lo[u].x), "r"(hi[u].x), "r"(lo[u].y), "r"(hi[u].y), "r"(bb.x), "r"(bb.y));
+            asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                         : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                         : "r"(lo[u].z), "r"(hi[u].z), "r"(lo[u].w), "r"(hi[u].w), "r"(bb.z), "r"(bb.w));
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[warp][t * 8 + 2 * tig + (e & 1)][g + 8 * (e >> 1)] = acc[t][e];
+    }
+    __syncthreads();
+    const int b = threadIdx.x >> 4, n = threadIdx.x & 15;
+    if (threadIdx.x < NT * 8 * 16 && b < B) {
+        if (pair) {
+            if (n < 8) {
+                float gsum = 0.f, usum = 0.f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) { gsum += red[w][b][n]; usum += red[w][b][n + 8]; }
+                const float gv = __bfloat162float(__float2bfloat16_rn(gsum)), uv = __bfloat162float(__float2bfloat16_rn(usum));
+                reinterpret_cast<__nv_bfloat16*>(sg.C)[(size_t)b * sg.ldc + n0 + n] = __float2bfloat16_rn(silu_f(gv) * uv);
+            }
+        } else {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) v += red[w][b][n];
+            const size_t o = (size_t)b * sg.ldc + n0 + n;
+            if (sg.R) v += ld_bf(sg.R + o);
+            if (sg.kind == 1) reinterpret_cast<float*>(sg.C)[o] = v;
+            else reinterpret_cast<__nv_bfloat16*>(sg.C)[o] = __float2bfloat16_rn(v);
+        }
+    }
+}
+
 // host side: launch the segments (all N multiples of 16, K a multiple of 32, at most 4 segments)
 constexpr int SKINNY_MAX_GROUPS = 1024;      // row groups a K-split launch may have (counters, partial sums)
 struct SkinnyWs { float* part = nullptr; int* counters = nullptr; bool attr = false; };
@@ -442,6 +536,8 @@ inline cudaError_t skinny_proj(const void* A, const void* norm_w, int B, int K, 
     if (!ws.attr) {
         cudaError_t e = cudaFuncSetAttribute(k_skinny_proj<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * (HIDDEN / 8 + 4) * 16);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_skinny_proj<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 16 * (HIDDEN / 8 + 4) * 16);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_skinny_norm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 16 * (HIDDEN / 8 + 4) * 16);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_skinny_norm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 16 * (HIDDEN / 8 + 4) * 16);
         if (e == cudaSuccess) e = cudaMalloc((void**)&ws.part, (size_t)SKINNY_MAX_GROUPS * 256 * 4);
         if (e == cudaSuccess) e = cudaMalloc((void**)&ws.counters, SKINNY_MAX_GROUPS * 4);
         if (e == cudaSuccess) e = cudaMemset(ws.counters, 0, SKINNY_MAX_GROUPS * 4);
@@ -458,7 +554,15 @@ inline cudaError_t skinny_proj(const void* A, const void* norm_w, int B, int K, 
         if (groups * ks > SKINNY_MAX_GROUPS) ks = 1;
     }
     const int nt = B <= 8 ? 1 : 2;
-    const size_t smem = norm_w ? (size_t)nt * 8 * (K / 8 + 4) * 16 : 0;
+    if (norm_w) {
+        const bool pair = args.seg[0].kind == 2;
+        if (pair && args.nseg != 1) return cudaErrorInvalidValue;
+        const int ctas = pair ? args.seg[0].N / 8 : groups;
+        const size_t sm = (size_t)nt * 8 * (HIDDEN / 8 + 4) * 16;
+        if (nt == 1) return launch_pdl(k_skinny_norm<1>, ctas, 256, sm, stream, (const __nv_bfloat16*)A, (const __nv_bfloat16*)norm_w, B, args);
+        return launch_pdl(k_skinny_norm<2>, ctas, 256, sm, stream, (const __nv_bfloat16*)A, (const __nv_bfloat16*)norm_w, B, args);
+    }
+    const size_t smem = 0;
     static int sms = 0;
     if (!sms && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return cudaErrorInvalidDevice;
     const int items = groups * ks, slots = sms * 2;
@@ -659,7 +763,7 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
                                                          {(const bf*)lv.w_b, nullptr, bw.graw, nullptr, 16, 32, 1},
                                                          {(const bf*)lv.w_a, nullptr, bw.graw + 16, nullptr, 16, 32, 1}}),
                      "DeltaNet input projections");
-            launch_pdl(k_dnb_layer, dim3(B, DN_HEADS), 1024, 0, stream, (const bf*)w.wide, (const bf*)w.z, (const float*)bw.graw,
+            launch_pdl(k_dnb_layer, dim3(B, DN_HEADS), 512, 0, stream, (const bf*)w.wide, (const bf*)w.z, (const float*)bw.graw,
                        (const bf*)lv.conv_w, (const bf*)lv.a_log, (const bf*)lv.dt_bias, (const bf*)lv.dn_norm, cstate, cv_seq, state,
                        st_seq, w.act);
             PF_CHECK(proj(w.act, nullptr, DN_V, {{(const bf*)lv.w_out, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "out projection");

@@ -142,6 +142,15 @@ __device__ __forceinline__ void pdl_enter() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// The two halves of pdl_enter(), for kernels that have something useful to do before their inputs exist: between
+// them only memory that no kernel of the stream writes (weights) or that the predecessor does not write may be
+// touched.  l2_prefetch asks for `bytes` (multiple of 16, 16-byte aligned start) to be brought into L2.
+__device__ __forceinline__ void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_prior() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void l2_prefetch(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // ---- math helpers ------------------------------------------------------------------------
 
 __device__ __forceinline__ float warp_sum(float v) {
