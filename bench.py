@@ -350,8 +350,8 @@ def main():
             "prefill": {"prompt_len": PROMPT_LEN, "ms": pp_max, "tok_s": world * PROMPT_LEN / (pp_max * 1e-3),
                         "tflops_algorithmic": PREFILL_TFLOP_PP520 / (pp_max * 1e-3),
                         "frac_of_bf16_peak": PREFILL_TFLOP_PP520 / (pp_max * 1e-3) / measured_bf16_peak(),
-                        "note": "prefill_bf16 op: persistent tcgen05/TMEM GEMMs fed by TMA, chunk-64 DeltaNet scan and "
-                                "causal GQA flash attention on mma.sync"},
+                        "note": "prefill_bf16 op: persistent tcgen05/TMEM GEMMs fed by TMA, chunk-64 DeltaNet scan on "
+                                "mma.sync, causal GQA flash attention on tcgen05/TMEM"},
             "gpu_launches": world * tokens,
             "clocks": clocks,
         }
@@ -361,7 +361,7 @@ def main():
                 {"batch_per_gpu": B_, "ms_per_step": t_, "tok_s": world * B_ / (t_ * 1e-3),
                  "hbm_gbs_algorithmic": batch_step_bytes(B_, avg_ctx) / (t_ * 1e-3) / 1e9,
                  "frac_of_hbm_peak": batch_step_bytes(B_, avg_ctx) / (t_ * 1e-3) / 1e9 / hbm,
-                 "note": "mk_decode_batch_many: every sequence has its own pp520 prompt and state; kernel sequence per step"}
+                 "note": "mk_decode_batch_many: every sequence has its own pp520 prompt and state; 130 kernels per step"}
                 for B_, t_ in zip((8, 16), batch_max)]
         if world == 1 and long_pp:
             out["prefill_long"] = [

@@ -113,10 +113,11 @@ __global__ void __launch_bounds__(512, 2) k_dnb_layer(const __nv_bfloat16* __res
 }
 
 // Attention of one new query per sequence over that sequence's cache (positions 0 .. pos[b], the new key and
-// value already appended).  Block = (sequence, query head), eight warps stride over the keys four at a time with an
+// value already appended).  Block = (sequence, query head), sixteen warps stride over the keys eight at a time with an
 // online softmax each (lane = 8 of the 256 dimensions), then merge through shared memory.
 // out[b][head][256] = softmax(q k^T / 16) v * sigmoid(gate), bf16.
-__global__ void __launch_bounds__(256) k_fab_attention(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ kc,
+constexpr int FAB_WARPS = 16, FAB_UN = 8;      // the kernel is a chain of cache-row round trips: keep many rows in flight
+__global__ void __launch_bounds__(FAB_WARPS * 32) k_fab_attention(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ kc,
                                                        const __nv_bfloat16* __restrict__ vc, size_t seq_stride,
                                                        const int* __restrict__ pos, int max_seq, __nv_bfloat16* __restrict__ out) {
     pdl_enter();
@@ -133,27 +134,27 @@ __global__ void __launch_bounds__(256) k_fab_attention(const __nv_bfloat16* __re
         q[4] = bf_lo(u.z); q[5] = bf_hi(u.z); q[6] = bf_lo(u.w); q[7] = bf_hi(u.w);
     }
     float m = -INFINITY, l = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j0 = warp; j0 < n; j0 += 32) {
-        uint4 ku[4], vu[4];
-        float s[4];
+    for (int j0 = warp; j0 < n; j0 += FAB_WARPS * FAB_UN) {
+        uint4 ku[FAB_UN], vu[FAB_UN];
+        float s[FAB_UN];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int j = j0 + 8 * u;
+        for (int u = 0; u < FAB_UN; ++u) {
+            const int j = j0 + FAB_WARPS * u;
             const bool in = j < n;
             ku[u] = in ? __ldg(reinterpret_cast<const uint4*>(kb + (size_t)j * FA_HEAD_DIM) + lane) : make_uint4(0, 0, 0, 0);
             vu[u] = in ? __ldg(reinterpret_cast<const uint4*>(vb + (size_t)j * FA_HEAD_DIM) + lane) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) s[u] = dot8(ku[u], q, 0.f);
+        for (int u = 0; u < FAB_UN; ++u) s[u] = dot8(ku[u], q, 0.f);
 #pragma unroll
         for (int of = 16; of > 0; of >>= 1) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], of);
+            for (int u = 0; u < FAB_UN; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], of);
         }
         float mn = m;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            s[u] = (j0 + 8 * u < n) ? s[u] * 0.0625f : -INFINITY;
+        for (int u = 0; u < FAB_UN; ++u) {
+            s[u] = (j0 + FAB_WARPS * u < n) ? s[u] * 0.0625f : -INFINITY;
             mn = fmaxf(mn, s[u]);
         }
         const float corr = __expf(m - mn);          // first pass: exp(-inf) = 0
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(256) k_fab_attention(const __nv_bfloat16* __re
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] *= corr;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < FAB_UN; ++u) {
             const float p = __expf(s[u] - mn);
             l += p;
             const uint32_t w[4] = {vu[u].x, vu[u].y, vu[u].z, vu[u].w};
@@ -173,19 +174,20 @@ __global__ void __launch_bounds__(256) k_fab_attention(const __nv_bfloat16* __re
         }
         m = mn;
     }
-    __shared__ float sm_m[8], sm_l[8];
-    __shared__ float sm_acc[8][FA_HEAD_DIM];
+    __shared__ float sm_m[FAB_WARPS], sm_l[FAB_WARPS];
+    __shared__ float sm_acc[FAB_WARPS][FA_HEAD_DIM];
     if (lane == 0) { sm_m[warp] = m; sm_l[warp] = l; }
 #pragma unroll
     for (int e = 0; e < 8; ++e) sm_acc[warp][lane * 8 + e] = acc[e];
     __syncthreads();
-    const int d = threadIdx.x;                       // one output dimension per thread
+    const int d = threadIdx.x;                       // one output dimension per thread (the first 256)
+    if (d >= FA_HEAD_DIM) return;
     float mm = sm_m[0];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) mm = fmaxf(mm, sm_m[w]);
+    for (int w = 1; w < FAB_WARPS; ++w) mm = fmaxf(mm, sm_m[w]);
     float tot = 0.f, ov = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
+    for (int w = 0; w < FAB_WARPS; ++w) {
         const float f = (sm_m[w] == -INFINITY) ? 0.f : __expf(sm_m[w] - mm);
         tot += sm_l[w] * f;
         ov += sm_acc[w][d] * f;
@@ -783,7 +785,7 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
             }
             launch_pdl(k_fa_norm_rope, blocks_for_warps((long long)B * 12), 256, 0, stream, w.wide, (const bf*)lv.q_norm,
                        (const bf*)lv.k_norm, kc, vc, B, max_seq_len, positions, kv_seq);
-            launch_pdl(k_fab_attention, dim3(B, FA_Q_HEADS), 256, 0, stream, (const bf*)w.wide, (const bf*)kc, (const bf*)vc, kv_seq,
+            launch_pdl(k_fab_attention, dim3(B, FA_Q_HEADS), FAB_WARPS * 32, 0, stream, (const bf*)w.wide, (const bf*)kc, (const bf*)vc, kv_seq,
                        positions, max_seq_len, w.act);
             PF_CHECK(proj(w.act, nullptr, FA_Q_SIZE, {{(const bf*)lv.w_o, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "o projection");
             ++fa_idx;
