@@ -361,7 +361,7 @@ def main():
                 {"batch_per_gpu": B_, "ms_per_step": t_, "tok_s": world * B_ / (t_ * 1e-3),
                  "hbm_gbs_algorithmic": batch_step_bytes(B_, avg_ctx) / (t_ * 1e-3) / 1e9,
                  "frac_of_hbm_peak": batch_step_bytes(B_, avg_ctx) / (t_ * 1e-3) / 1e9 / hbm,
-                 "note": "mk_decode_batch_many: every sequence has its own pp520 prompt and state; 130 kernels per step"}
+                 "note": "mk_decode_batch_many: every sequence has its own pp520 prompt and state; 131 kernels per step"}
                 for B_, t_ in zip((8, 16), batch_max)]
         if world == 1 and long_pp:
             out["prefill_long"] = [

@@ -143,6 +143,18 @@ int mk_dequantize_nvfp4(int format, const void *packed, const void *scales, floa
                         int rows, int cols, int group_size, cudaStream_t stream);
 const char *mk_nvfp4_error(void);
 
+/* The NVFP4 format with an fp32 per-tensor scale: e2m1 values in 16-element blocks, E4M3 block scales in the tiling
+ * of the LM-head format, and s_t = amax(tensor) / (6 * 448) (1 for an all-zero tensor); block scale =
+ * E4M3(max((amax(block) / 6) / s_t, 2^-28)), code = e2m1_rne(x / (block * s_t)), value = e2m1(code) * (block * s_t).
+ * The reference's 16-block quantiser has no tensor scale (megakernel/kernel_gb10_nvfp4.cu:1373-1437, alpha = 1 at
+ * :451); this is an additional format next to its two.  rows % 128 == 0, cols % 64 == 0;
+ * packed_out uint8 [rows][cols / 2], scales_out uint8 [(rows / 128) * (cols / 64) * 512], tensor_scale device float[1].
+ * Dequantised f32 values are bit-exact to the CPU restatement; out_is_bf16 = 1 rounds them to bf16. */
+int mk_quantize_nvfp4_tensor_scale(const void *weight, int rows, int cols, void *packed_out, void *scales_out,
+                                   float *tensor_scale_out, cudaStream_t stream);
+int mk_dequantize_nvfp4_tensor_scale(const void *packed, const void *scales, const float *tensor_scale, void *out,
+                                     int out_is_bf16, int rows, int cols, cudaStream_t stream);
+
 /* Prefill of a prompt of seq_len tokens from position 0: fills the KV caches for positions
  * 0..seq_len-1, advances the DeltaNet and conv state from their current content (callers zero
  * them first), writes the first generated token to output_token, the last row's final-normed

@@ -9,6 +9,7 @@
 // step with one 128-bit load, converts nibble pairs with the e2m1x2 -> f16x2 hardware conversion
 // and accumulates in f32 against the activation kept in shared memory; 4 rows per warp are in
 // flight.  Grid = 8 resident CTAs of 256 threads per SM.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp4.h>
 #include <cuda_fp8.h>
@@ -95,6 +96,19 @@ __global__ void dequant_nvfp4_kernel(const uint8_t* __restrict__ packed, const v
     out[(size_t)row * K + c + 1] = v.y * s;
 }
 
+// format B with a per-tensor scale: value = e2m1(code) * (E4M3 block scale * tensor scale); f32 or bf16 output
+template <typename OUT>
+__global__ void dequant_nvfp4_ts_kernel(const uint8_t* __restrict__ packed, const uint8_t* __restrict__ scales,
+                                        const float* __restrict__ tensor_scale, OUT* __restrict__ out, int N, int K) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;      // one thread per packed byte
+    if (i >= (size_t)N * (K >> 1)) return;
+    const int row = (int)(i / (K >> 1)), c = (int)(i % (K >> 1)) * 2;
+    const float2 v = e2m1x2_to_float2(packed[i]);
+    const float s = __fmul_rn(e4m3_to_float(scales[scale_index_b(row, c >> 4, K)]), *tensor_scale);
+    out[(size_t)row * K + c] = (OUT)__fmul_rn(v.x, s);
+    out[(size_t)row * K + c + 1] = (OUT)__fmul_rn(v.y, s);
+}
+
 thread_local char g_merr[160] = "";
 int mfail(const char* m) { snprintf(g_merr, sizeof(g_merr), "%s", m); return MK_ERR_BAD_ARG; }
 
@@ -133,6 +147,22 @@ extern "C" int mk_dequantize_nvfp4(int format, const void* packed, const void* s
     const unsigned blocks = (unsigned)((n + 255) / 256);
     if (format == 0) dequant_nvfp4_kernel<0><<<blocks, 256, 0, stream>>>((const uint8_t*)packed, scales, out, rows, cols, group_size);
     else dequant_nvfp4_kernel<1><<<blocks, 256, 0, stream>>>((const uint8_t*)packed, scales, out, rows, cols, 16);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_merr, sizeof(g_merr), "dequantize launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
+    return MK_OK;
+}
+
+// 16-block / E4M3 / fp32 per-tensor scale (mk_quantize_nvfp4_tensor_scale).  out_is_bf16: 0 = f32 [rows][cols] (exact
+// values), 1 = bf16 (what a bf16 GEMM consumes; e2m1 x E4M3 has at most 5 significant bits, the tensor scale adds
+// up to 24, so this rounds).
+extern "C" int mk_dequantize_nvfp4_tensor_scale(const void* packed, const void* scales, const float* tensor_scale, void* out,
+                                                int out_is_bf16, int rows, int cols, cudaStream_t stream) {
+    if (!packed || !scales || !tensor_scale || !out) return mfail("null pointer argument");
+    if (rows <= 0 || cols <= 0 || rows % 128 || cols % 64) return mfail("needs rows % 128 == 0 and cols % 64 == 0");
+    const size_t n = (size_t)rows * (cols / 2);
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    if (out_is_bf16) dequant_nvfp4_ts_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>((const uint8_t*)packed, (const uint8_t*)scales, tensor_scale, (__nv_bfloat16*)out, rows, cols);
+    else dequant_nvfp4_ts_kernel<float><<<blocks, 256, 0, stream>>>((const uint8_t*)packed, (const uint8_t*)scales, tensor_scale, (float*)out, rows, cols);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_merr, sizeof(g_merr), "dequantize launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
     return MK_OK;

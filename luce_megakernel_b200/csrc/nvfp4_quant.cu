@@ -106,6 +106,58 @@ __global__ void quantize_b_kernel(const __nv_bfloat16* __restrict__ w, uint8_t* 
     scales[tile * 512 + (size_t)(row & 31) * 16 + (size_t)((row & 127) >> 5) * 4 + (sc & 3)] = (uint8_t)s8;
 }
 
+// ---- format B with a per-tensor scale ------------------------------------------------------------------------
+// s_t = amax(tensor) / (6 * 448) (1 for an all-zero tensor); block scale = E4M3(max((amax(block) / 6) / s_t, 2^-28));
+// code = e2m1_rne(x / (dec * s_t)).  The reference stores block scales without a tensor scale
+// (megakernel/kernel_gb10_nvfp4.cu:1373-1437, alpha = 1 at :451); this is the format of the NVFP4 recipe with an
+// fp32 per-tensor scale, same packing and scale tiling as format B.
+__global__ void tensor_amax_kernel(const __nv_bfloat16* __restrict__ w, size_t n8, unsigned* __restrict__ amax_bits) {
+    float amax = 0.0f;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(w) + i);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(bf_at(v, e)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(amax));     // non-negative floats order like their bits
+}
+
+__global__ void tensor_scale_kernel(unsigned* __restrict__ amax_bits_to_scale) {
+    const float amax = __uint_as_float(*amax_bits_to_scale);
+    *reinterpret_cast<float*>(amax_bits_to_scale) = amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
+}
+
+__global__ void quantize_ts_kernel(const __nv_bfloat16* __restrict__ w, uint8_t* __restrict__ packed,
+                                   uint8_t* __restrict__ scales, const float* __restrict__ tensor_scale, int rows, int cols) {
+    const int blocks_per_row = cols / 16;
+    const long long bid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (bid >= (long long)rows * blocks_per_row) return;
+    const float st = *tensor_scale;
+    const int row = (int)(bid / blocks_per_row), sc = (int)(bid % blocks_per_row);
+    const uint4* src = reinterpret_cast<const uint4*>(w + (size_t)row * cols + (size_t)sc * 16);
+    const uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fmaxf(fabsf(bf_at(v0, e)), fabsf(bf_at(v1, e))));
+    const float rel = __fdiv_rn(__fmul_rn(amax, 1.0f / 6.0f), st);
+    const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(fmaxf(rel, 1.0f / (float)(1 << 28)), __NV_SATFINITE, __NV_E4M3);
+    const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
+    const float eff = __fmul_rn(__half2float(*reinterpret_cast<const __half*>(&hr)), st);
+    const float inv = (eff > 0.0f) ? __fdiv_rn(1.0f, eff) : 0.0f;
+    unsigned long long out = 0;
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+        const uint4& v = (p < 4) ? v0 : v1;
+        const float2 f = make_float2(__fmul_rn(bf_at(v, (2 * p) & 7), inv), __fmul_rn(bf_at(v, (2 * p + 1) & 7), inv));
+        const __nv_fp4x2_storage_t q = __nv_cvt_float2_to_fp4x2(f, __NV_E2M1, cudaRoundNearest);
+        out |= (unsigned long long)(uint8_t)q << (8 * p);
+    }
+    *reinterpret_cast<unsigned long long*>(packed + (size_t)row * (cols / 2) + (size_t)sc * 8) = out;
+    const size_t tile = (size_t)(row >> 7) * (cols / 64) + (sc >> 2);
+    scales[tile * 512 + (size_t)(row & 31) * 16 + (size_t)((row & 127) >> 5) * 4 + (sc & 3)] = (uint8_t)s8;
+}
+
 thread_local char g_qerr[160] = "";
 int qfail(const char* m) { snprintf(g_qerr, sizeof(g_qerr), "%s", m); return MK_ERR_BAD_ARG; }
 
@@ -142,6 +194,28 @@ extern "C" int launch_quantize_nvfp4_lm_out(const void* weight, int rows, int co
     quantize_b_kernel<<<blocks, threads, 0, stream>>>((const __nv_bfloat16*)weight, (uint8_t*)packed_out,
                                                       (uint8_t*)scales_out, rows, cols);
     const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_qerr, sizeof(g_qerr), "quantize launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
+    return MK_OK;
+}
+
+// 16-block / E4M3 / fp32 per-tensor scale.  tensor_scale_out: device float[1].
+extern "C" int mk_quantize_nvfp4_tensor_scale(const void* weight, int rows, int cols, void* packed_out, void* scales_out,
+                                              float* tensor_scale_out, cudaStream_t stream) {
+    if (!weight || !packed_out || !scales_out || !tensor_scale_out) return qfail("null pointer argument");
+    if (rows <= 0 || rows % 128) return qfail("rows must be a positive multiple of 128");
+    if (cols <= 0 || cols % 64) return qfail("cols must be a positive multiple of 64");
+    if ((reinterpret_cast<uintptr_t>(weight) & 15u) || (reinterpret_cast<uintptr_t>(packed_out) & 7u))
+        return qfail("weight must be 16-byte aligned and packed_out 8-byte aligned");
+    cudaError_t e = cudaMemsetAsync(tensor_scale_out, 0, 4, stream);
+    if (e == cudaSuccess) {
+        const size_t n8 = (size_t)rows * cols / 8;
+        tensor_amax_kernel<<<592, 256, 0, stream>>>((const __nv_bfloat16*)weight, n8, reinterpret_cast<unsigned*>(tensor_scale_out));
+        tensor_scale_kernel<<<1, 1, 0, stream>>>(reinterpret_cast<unsigned*>(tensor_scale_out));
+        const long long total = (long long)rows * (cols / 16);
+        quantize_ts_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>((const __nv_bfloat16*)weight, (uint8_t*)packed_out,
+                                                                             (uint8_t*)scales_out, tensor_scale_out, rows, cols);
+        e = cudaGetLastError();
+    }
     if (e != cudaSuccess) { snprintf(g_qerr, sizeof(g_qerr), "quantize launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
     return MK_OK;
 }

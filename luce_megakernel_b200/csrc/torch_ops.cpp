@@ -375,6 +375,23 @@ void quantize_nvfp4_lm_out(Tensor packed_out, Tensor scales_out, Tensor weight) 
     TORCH_CHECK(rc == MK_OK, "quantize_nvfp4_lm_out failed: ", mk_quantize_error());
 }
 
+// 16-block / E4M3 / fp32 per-tensor scale: an additional format, the reference's 16-block quantiser has no tensor
+// scale (megakernel/kernel_gb10_nvfp4.cu:1373-1437).  Argument order follows quantize_nvfp4_lm_out.
+void quantize_nvfp4_tensor_scale_out(Tensor packed_out, Tensor scales_out, Tensor tensor_scale_out, Tensor weight) {
+    TORCH_CHECK(weight.is_cuda() && weight.is_contiguous() && weight.dim() == 2, "weight must be a contiguous 2-D CUDA tensor");
+    TORCH_CHECK(weight.scalar_type() == torch::kBFloat16, "weight must be bfloat16");
+    const int rows = (int)weight.size(0), cols = (int)weight.size(1);
+    TORCH_CHECK((rows % 128) == 0, "out_dim must be divisible by 128");
+    TORCH_CHECK((cols % 64) == 0, "in_dim must be divisible by 64");
+    need(packed_out, "packed_out", torch::kUInt8, (int64_t)rows * (cols / 2));
+    need(scales_out, "scales_out", torch::kUInt8, (int64_t)(rows / 128) * (cols / 64) * 512);
+    need(tensor_scale_out, "tensor_scale_out", torch::kFloat32, 1);
+    DeviceGuard guard(weight);
+    const int rc = mk_quantize_nvfp4_tensor_scale(weight.data_ptr(), rows, cols, packed_out.data_ptr(), scales_out.data_ptr(),
+                                                  (float*)tensor_scale_out.data_ptr(), current_stream(weight));
+    TORCH_CHECK(rc == MK_OK, "quantize_nvfp4_tensor_scale_out failed: ", mk_quantize_error());
+}
+
 int64_t max_safe_decode_blocks() { return query_max_safe_decode_blocks(); }
 
 void set_decode_blocks(int64_t blocks) {
@@ -499,6 +516,9 @@ TORCH_LIBRARY(qwen35_megakernel_bf16_C, ops) {
 
     ops.def("quantize_nvfp4_lm_out(Tensor packed_out, Tensor scales_out, Tensor weight) -> ()");
     ops.impl("quantize_nvfp4_lm_out", torch::kCUDA, &quantize_nvfp4_lm_out);
+
+    ops.def("quantize_nvfp4_tensor_scale_out(Tensor packed_out, Tensor scales_out, Tensor tensor_scale_out, Tensor weight) -> ()");
+    ops.impl("quantize_nvfp4_tensor_scale_out", torch::kCUDA, &quantize_nvfp4_tensor_scale_out);
 }
 
 // Importable as a Python module of the same name, like the reference extension

@@ -70,3 +70,23 @@ def dequantize_b(packed, scales):
     out = np.zeros((rows, half * 2), np.float32)
     lib().mk_oracle_dequantize_b(_p(np.ascontiguousarray(packed)), _p(np.ascontiguousarray(scales)), rows, half * 2, _p(out))
     return out
+
+
+def quantize_ts(w):
+    """16-blocks, E4M3 block scales (layout of format B), f32 per-tensor scale.  Returns packed, scales, scale."""
+    bits = _bf16_bits(w)
+    rows, cols = bits.shape
+    assert rows % 128 == 0 and cols % 64 == 0
+    packed = np.zeros((rows, cols // 2), np.uint8)
+    scales = np.zeros((rows // 128) * (cols // 64) * 512, np.uint8)
+    ts = np.zeros(1, np.float32)
+    lib().mk_oracle_quantize_ts(_p(bits), rows, cols, _p(packed), _p(scales), _p(ts))
+    return packed, scales, ts
+
+
+def dequantize_ts(packed, scales, tensor_scale):
+    rows, half = packed.shape
+    out = np.zeros((rows, half * 2), np.float32)
+    lib().mk_oracle_dequantize_ts(_p(np.ascontiguousarray(packed)), _p(np.ascontiguousarray(scales)),
+                                  ctypes.c_float(float(np.asarray(tensor_scale).reshape(-1)[0])), rows, half * 2, _p(out))
+    return out

@@ -174,5 +174,51 @@ void mk_oracle_dequantize_b(const uint8_t* packed, const uint8_t* scales, int ro
         }
 }
 
+/* Format B with a per-tensor scale (the "e2m1 values in 16-element blocks, FP8 E4M3 block scales, fp32 per-tensor
+ * scale" format).  The reference has no per-tensor scale (its 16-block quantiser, kernel_gb10_nvfp4.cu:1373-1437,
+ * stores block scales directly; alpha = 1 at :451): parity unpinned, this restatement is the definition the CUDA
+ * kernels are held to bit for bit.
+ *   s_t   = amax(tensor) / (6 * 448)   (1 for an all-zero tensor)      -- the largest block scale lands on 448
+ *   block = E4M3( max((amax(block) / 6) / s_t, 2^-28) ),  dec = decoded block scale
+ *   code  = e2m1_rne( x * (1 / (dec * s_t)) ),  value = e2m1(code) * (dec * s_t)
+ * every operation a single IEEE f32 operation in the order written. */
+float mk_oracle_tensor_scale(const uint16_t* w, int rows, int cols) {
+    float amax = 0.0f;
+    for (size_t i = 0; i < (size_t)rows * cols; ++i) amax = fmaxf(amax, fabsf(bf16_to_f32(w[i])));
+    return amax > 0.0f ? amax / 2688.0f : 1.0f;
+}
+
+void mk_oracle_quantize_ts(const uint16_t* w, int rows, int cols, uint8_t* packed, uint8_t* scales, float* tensor_scale) {
+    const float sixth = 1.0f / 6.0f, floor_s = 1.0f / (float)(1 << 28);
+    const float st = mk_oracle_tensor_scale(w, rows, cols);
+    *tensor_scale = st;
+    for (int r = 0; r < rows; ++r)
+        for (int b = 0; b < cols / 16; ++b) {
+            const uint16_t* src = w + (size_t)r * cols + (size_t)b * 16;
+            float amax = 0.0f;
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(bf16_to_f32(src[i])));
+            float rel = (amax * sixth) / st;
+            uint8_t sc = mk_oracle_f32_to_e4m3(fmaxf(rel, floor_s));
+            float eff = mk_oracle_e4m3_to_f32(sc) * st;
+            float inv = (eff > 0.0f) ? (1.0f / eff) : 0.0f;
+            uint8_t* dst = packed + (size_t)r * (cols / 2) + (size_t)b * 8;
+            for (int i = 0; i < 16; i += 2) {
+                unsigned lo = mk_oracle_f32_to_e2m1(bf16_to_f32(src[i]) * inv);
+                unsigned hi = mk_oracle_f32_to_e2m1(bf16_to_f32(src[i + 1]) * inv);
+                dst[i / 2] = (uint8_t)(lo | (hi << 4));
+            }
+            scales[mk_oracle_scale_index_b(r, b, cols)] = sc;
+        }
+}
+
+void mk_oracle_dequantize_ts(const uint8_t* packed, const uint8_t* scales, float tensor_scale, int rows, int cols, float* out) {
+    for (int r = 0; r < rows; ++r)
+        for (int c = 0; c < cols; ++c) {
+            uint8_t byte = packed[(size_t)r * (cols / 2) + c / 2];
+            unsigned code = (c & 1) ? (byte >> 4) : (byte & 15u);
+            out[(size_t)r * cols + c] = deq(code, mk_oracle_e4m3_to_f32(scales[mk_oracle_scale_index_b(r, c / 16, cols)]) * tensor_scale);
+        }
+}
+
 uint16_t mk_oracle_f32_to_f16(float f) { return f32_to_f16(f); }
 float mk_oracle_f16_to_f32(uint16_t h) { return f16_to_f32(h); }

@@ -189,3 +189,61 @@ def test_quantize_ops_surface():
     assert np.array_equal(packed_b.cpu().numpy(), bp) and np.array_equal(scales_b.cpu().numpy(), bs)
     with pytest.raises(RuntimeError):
         ops.quantize_nvfp4_out(packed, scales, wd, 48)
+
+
+def test_tensor_scale_format_properties():
+    """CPU: the largest block scale is E4M3's 448, dequantised values stay within half an e2m1 step of the block
+    scale, an all-zero tensor quantises to zeros with scale 1."""
+    w = _rand_bf16(256, 512, 21) * 3.0
+    packed, scales, ts = nvfp4.quantize_ts(w.to(torch.bfloat16))
+    amax = float(w.to(torch.bfloat16).float().abs().max())
+    assert np.float32(ts[0]) == np.float32(amax) / np.float32(2688.0)
+    dec = np.array([nvfp4.lib().mk_oracle_e4m3_to_f32(int(c)) for c in np.unique(scales)])
+    assert dec.max() == 448.0
+    deq = nvfp4.dequantize_ts(packed, scales, ts)
+    ref = w.to(torch.bfloat16).float().numpy()
+    blk_amax = np.abs(ref).reshape(256, -1, 16).max(-1, keepdims=True)
+    # e2m1 steps are at most 2 (between 4 and 6) in units of the block scale ~ amax / 6, E4M3 adds up to 1/16
+    assert (np.abs(deq - ref).reshape(256, -1, 16) <= blk_amax * (1.0 / 6.0 + 1.0 / 16.0) + 1e-12).all()
+    z = torch.zeros(128, 64, dtype=torch.bfloat16)
+    zp, zs, zt = nvfp4.quantize_ts(z)
+    assert zt[0] == 1.0 and not zp.any()
+    assert not nvfp4.dequantize_ts(zp, zs, zt).any()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape,gain", [((256, 1024), 1.0), ((1024, 3584), 0.02), ((128, 64), 300.0)])
+def test_gpu_tensor_scale_format_bit_exact(shape, gain):
+    """Quantiser (codes, block scales, tensor scale) and dequantised weights bit-identical to the C restatement."""
+    import luce_megakernel_b200 as L
+    lib = L.lib()
+    lib.mk_quantize_error.restype = ctypes.c_char_p
+    rows, cols = shape
+    w = (_rand_bf16(rows, cols, 5).float() * gain).to(torch.bfloat16)
+    rp, rs, rt = nvfp4.quantize_ts(w)
+    wd = w.cuda()
+    pk = torch.zeros(rows, cols // 2, dtype=torch.uint8, device="cuda")
+    sc = torch.zeros(rs.size, dtype=torch.uint8, device="cuda")
+    ts = torch.zeros(1, dtype=torch.float32, device="cuda")
+    rc = lib.mk_quantize_nvfp4_tensor_scale(ctypes.c_void_p(wd.data_ptr()), rows, cols, ctypes.c_void_p(pk.data_ptr()),
+                                            ctypes.c_void_p(sc.data_ptr()), ctypes.c_void_p(ts.data_ptr()), _stream())
+    assert rc == 0, lib.mk_quantize_error().decode()
+    torch.cuda.synchronize()
+    assert np.array_equal(ts.cpu().numpy().view(np.uint32), rt.view(np.uint32))
+    assert np.array_equal(sc.cpu().numpy(), rs)
+    assert np.array_equal(pk.cpu().numpy(), rp)
+    out = torch.empty(rows, cols, dtype=torch.float32, device="cuda")
+    rc = lib.mk_dequantize_nvfp4_tensor_scale(ctypes.c_void_p(pk.data_ptr()), ctypes.c_void_p(sc.data_ptr()),
+                                              ctypes.c_void_p(ts.data_ptr()), ctypes.c_void_p(out.data_ptr()), 0, rows, cols, _stream())
+    assert rc == 0
+    ob = torch.empty(rows, cols, dtype=torch.bfloat16, device="cuda")
+    rc = lib.mk_dequantize_nvfp4_tensor_scale(ctypes.c_void_p(pk.data_ptr()), ctypes.c_void_p(sc.data_ptr()),
+                                              ctypes.c_void_p(ts.data_ptr()), ctypes.c_void_p(ob.data_ptr()), 1, rows, cols, _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    ref = nvfp4.dequantize_ts(rp, rs, rt)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))       # bit-exact
+    assert torch.equal(ob.cpu(), torch.from_numpy(ref).to(torch.bfloat16))
+    # and close to the original weights: relative error of a 4-bit format
+    err = np.abs(ref - w.float().numpy()).max() / float(w.float().abs().max())
+    assert err <= 0.2
