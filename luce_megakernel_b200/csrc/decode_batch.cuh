@@ -27,10 +27,6 @@ __global__ void __launch_bounds__(512, 2) k_dnb_layer(const __nv_bfloat16* __res
                                                     size_t conv_seq_stride, float* __restrict__ state, size_t state_seq_stride,
                                                     __nv_bfloat16* __restrict__ act) {
     pdl_launch_next();
-    // the head's state (64 KB, contiguous) is not written by the projection kernel before this one
-    if (threadIdx.x == 0)
-        l2_prefetch(state + (size_t)blockIdx.x * state_seq_stride + (size_t)blockIdx.y * DN_VAL * DN_KEY, DN_VAL * DN_KEY * 4);
-    pdl_wait_prior();
     const int b = blockIdx.x, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ __align__(16) float qs[DN_KEY], ks[DN_KEY], vs[DN_VAL], os[DN_VAL];
@@ -41,6 +37,8 @@ __global__ void __launch_bounds__(512, 2) k_dnb_layer(const __nv_bfloat16* __res
     float4 s[RW];
 #pragma unroll
     for (int r = 0; r < RW; ++r) s[r] = reinterpret_cast<const float4*>(sbase + r * DN_KEY)[lane];
+    // the state is not written by the projection kernel before this one: its rows are requested above, ahead of the wait
+    pdl_wait_prior();
     if (threadIdx.x < 128) {
         const int c = threadIdx.x;
         float* cs = conv_state + (size_t)b * conv_seq_stride;
@@ -573,6 +571,83 @@ inline cudaError_t skinny_proj(const void* A, const void* norm_w, int B, int K, 
     return launch_pdl(k_skinny_proj<2>, grid, 256, smem, stream, (const __nv_bfloat16*)A, (const __nv_bfloat16*)norm_w, B, K, lda, args, items, ks, ws.part, ws.counters);
 }
 
+// The 1024-row projections back into the residual stream (out / o: K = 2048, down: K = 3584): few rows, long K.
+// One CTA per 8 rows of W (the other half of the m16 tile stays zero: the tensor cores are nowhere near the
+// limit, parallelism is), eight warps split K, and the whole kernel is straight-line: every weight a lane will ever
+// need (STEPS x 16 bytes) is requested before the kernel waits for its predecessor, the activations are staged in
+// shared memory after the wait while those loads land, then MMAs, one shared-memory sum, residual add, store.
+// With 128 CTAs the entire matrix is in flight at once.  C doubles as the residual (read and written in place).
+template <int NT, int STEPS>   // K = 256 * STEPS
+__global__ void __launch_bounds__(256, 2) k_skinny_res(const __nv_bfloat16* __restrict__ A, int B, const __nv_bfloat16* __restrict__ W,
+                                                       __nv_bfloat16* C, int ldc) {
+    pdl_launch_next();
+    constexpr int K = 256 * STEPS, RS = K / 8 + 4;
+    extern __shared__ __align__(16) uint4 as[];              // [NT * 8][RS] activations, rows >= B zero
+    __shared__ float red[8][NT * 8][9];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    const int n0 = blockIdx.x * 8;
+    const uint4* w0 = reinterpret_cast<const uint4*>(W + (size_t)(n0 + g) * K) + tig;
+    uint4 lo[STEPS];
+#pragma unroll
+    for (int u = 0; u < STEPS; ++u) lo[u] = __ldcs(w0 + (warp + 8 * u) * 4);
+    pdl_wait_prior();
+    for (int i = threadIdx.x; i < NT * 8 * (K / 8); i += 256) {
+        const int b = i / (K / 8), c = i - b * (K / 8);
+        as[b * RS + c] = (b < B) ? *reinterpret_cast<const uint4*>(A + (size_t)b * K + c * 8) : make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    float acc[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) { acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f; }
+#pragma unroll
+    for (int u = 0; u < STEPS; ++u) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const uint4 bb = as[(t * 8 + g) * RS + (warp + 8 * u) * 4 + tig];
+            asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                         : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                         : "r"(lo[u].x), "r"(0u), "r"(lo[u].y), "r"(0u), "r"(bb.x), "r"(bb.y));
+            asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                         : "+f"(acc[t][0]), "+f"(acc[t][1]), "+f"(acc[t][2]), "+f"(acc[t][3])
+                         : "r"(lo[u].z), "r"(0u), "r"(lo[u].w), "r"(0u), "r"(bb.z), "r"(bb.w));
+        }
+    }
+    // accumulator elements 0, 1 of tile t: W row g, batch columns 8 t + 2 tig, + 1 (elements 2, 3 belong to the zero rows)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) { red[warp][t * 8 + 2 * tig][g] = acc[t][0]; red[warp][t * 8 + 2 * tig + 1][g] = acc[t][1]; }
+    __syncthreads();
+    const int b = threadIdx.x >> 3, n = threadIdx.x & 7;
+    if (threadIdx.x < NT * 8 * 8 && b < B) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) v += red[w][b][n];
+        const size_t o = (size_t)b * ldc + n0 + n;
+        C[o] = __float2bfloat16_rn(v + ld_bf(C + o));
+    }
+}
+
+template <int NT, int STEPS>
+inline cudaError_t launch_skinny_res(const void* A, int B, const void* W, void* C, int N, int ldc, cudaStream_t stream) {
+    constexpr size_t smem = (size_t)NT * 8 * (256 * STEPS / 8 + 4) * 16;
+    static bool attr[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(k_skinny_res<NT, STEPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr[dev] = true;
+    }
+    return launch_pdl(k_skinny_res<NT, STEPS>, N / 8, 256, smem, stream, (const __nv_bfloat16*)A, B, (const __nv_bfloat16*)W,
+                      (__nv_bfloat16*)C, ldc);
+}
+
+// C[b][n] += sum_k A[b][k] W[n][k] for K = 2048 or 3584, N a multiple of 8
+inline cudaError_t skinny_res(const void* A, int B, int K, const void* W, void* C, int N, int ldc, cudaStream_t stream) {
+    if (B < 1 || B > 16 || N % 8 || (K != 2048 && K != 3584)) return cudaErrorInvalidValue;
+    if (B <= 8) return K == 2048 ? launch_skinny_res<1, 8>(A, B, W, C, N, ldc, stream) : launch_skinny_res<1, 14>(A, B, W, C, N, ldc, stream);
+    return K == 2048 ? launch_skinny_res<2, 8>(A, B, W, C, N, ldc, stream) : launch_skinny_res<2, 14>(A, B, W, C, N, ldc, stream);
+}
+
 // LM head of a batched step on the tensor cores: the same fragment scheme as k_skinny_proj, but a warp keeps a
 // 16-row group of the vocabulary to itself over all of K = 1024 (no cross-warp sum), the f32 activations enter as two
 // bf16 terms (x = hi + lo, relative error 2^-16) accumulated into the same f32 sums, and the epilogue is a running
@@ -581,12 +656,25 @@ inline cudaError_t skinny_proj(const void* A, const void* norm_w, int B, int K, 
 template <int NT>
 __global__ void __launch_bounds__(256, 2) k_lm_head_mma(const float* __restrict__ x, int B, const __nv_bfloat16* __restrict__ W,
                                                         int vocab, float* __restrict__ bval, int* __restrict__ bidx) {
-    pdl_enter();
+    pdl_launch_next();
     constexpr int RS = HIDDEN / 8 + 4;                        // row stride in 16-byte units (+64 B: no bank conflicts)
     extern __shared__ __align__(16) uint4 xh[];               // hi [NT * 8][RS], then lo [NT * 8][RS]
     __shared__ float sv[8][NT * 8];
     __shared__ int si[8][NT * 8];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
+    const int ngroups = (vocab + 15) / 16, nwarps = gridDim.x * 8, wg = blockIdx.x * 8 + warp;
+    const int mine = wg < ngroups ? (ngroups - wg + nwarps - 1) / nwarps : 0;       // groups of this warp
+    constexpr int FG = HIDDEN / 32 / 4;                       // fetches of four k steps per group: 8
+    uint4 lo[4], hi[4];
+    auto fetch = [&](int q) {                                 // q-th fetch of this warp's stream
+        const int n0 = (wg + (q / FG) * nwarps) * 16, st0 = (q % FG) * 4;
+        const uint4* w0 = reinterpret_cast<const uint4*>(W + (size_t)min(n0 + g, vocab - 1) * HIDDEN) + tig;
+        const uint4* w1 = reinterpret_cast<const uint4*>(W + (size_t)min(n0 + g + 8, vocab - 1) * HIDDEN) + tig;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { lo[u] = __ldcs(w0 + (st0 + u) * 4); hi[u] = __ldcs(w1 + (st0 + u) * 4); }
+    };
+    if (mine > 0) fetch(0);                                  // weights first: they do not depend on the previous kernel
+    pdl_wait_prior();
     uint4* xlo = xh + NT * 8 * RS;
     for (int i = threadIdx.x; i < NT * 8 * (HIDDEN / 8); i += 256) {
         const int b = i / (HIDDEN / 8), c = i - b * (HIDDEN / 8);
@@ -606,18 +694,6 @@ __global__ void __launch_bounds__(256, 2) k_lm_head_mma(const float* __restrict_
         xh[b * RS + c] = make_uint4(h[0], h[1], h[2], h[3]);
         xlo[b * RS + c] = make_uint4(l[0], l[1], l[2], l[3]);
     }
-    const int ngroups = (vocab + 15) / 16, nwarps = gridDim.x * 8, wg = blockIdx.x * 8 + warp;
-    const int mine = wg < ngroups ? (ngroups - wg + nwarps - 1) / nwarps : 0;       // groups of this warp
-    constexpr int FG = HIDDEN / 32 / 4;                       // fetches of four k steps per group: 8
-    uint4 lo[4], hi[4];
-    auto fetch = [&](int q) {                                 // q-th fetch of this warp's stream
-        const int n0 = (wg + (q / FG) * nwarps) * 16, st0 = (q % FG) * 4;
-        const uint4* w0 = reinterpret_cast<const uint4*>(W + (size_t)min(n0 + g, vocab - 1) * HIDDEN) + tig;
-        const uint4* w1 = reinterpret_cast<const uint4*>(W + (size_t)min(n0 + g + 8, vocab - 1) * HIDDEN) + tig;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) { lo[u] = __ldcs(w0 + (st0 + u) * 4); hi[u] = __ldcs(w1 + (st0 + u) * 4); }
-    };
-    if (mine > 0) fetch(0);
     __syncthreads();
     float best[NT][2];
     int besti[NT][2];
@@ -708,6 +784,7 @@ __global__ void k_batch_advance(int* __restrict__ tokens, const int* __restrict_
     if (log_row) log_row[b] = t;
 }
 
+int g_batch_res_kernel = 1;        // projections into the residual stream: 0 = K split over CTAs, 2 = straight-line 8-row kernel, 1 = by batch size
 int g_batch_lm_mma = 1;            // LM head of the batched step: 1 = tensor cores (bf16 hi + lo), 0 = f32 CUDA cores
 struct BatchWs { float *normed_f32 = nullptr, *bval = nullptr, *graw = nullptr; int *bidx = nullptr, *chosen = nullptr; };
 BatchWs g_bws[64];
@@ -750,6 +827,9 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
     const size_t kv_seq = (size_t)n_fa * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;          // elements per sequence
     const size_t st_seq = (size_t)n_dn * DN_HEADS * DN_VAL * DN_KEY, cv_seq = (size_t)n_dn * DN_CONV_CH * DN_CONV_K;
 
+    // out / o / down: the straight-line kernel stages all B activation rows in each of its 128 CTAs, which pays up to
+    // B = 8; beyond, 64 row groups with K split over four CTAs each read less
+    const bool res_kernel = g_batch_res_kernel == 1 ? B <= 8 : g_batch_res_kernel == 2;
     launch_pdl(k_embed, B, 128, 0, stream, tokens, (const bf*)embed_weight, w.hidden, B, vocab);
     int dn_idx = 0, fa_idx = 0;
     for (int li = 0; li < num_layers; ++li) {
@@ -768,7 +848,8 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
             launch_pdl(k_dnb_layer, dim3(B, DN_HEADS), 512, 0, stream, (const bf*)w.wide, (const bf*)w.z, (const float*)bw.graw,
                        (const bf*)lv.conv_w, (const bf*)lv.a_log, (const bf*)lv.dt_bias, (const bf*)lv.dn_norm, cstate, cv_seq, state,
                        st_seq, w.act);
-            PF_CHECK(proj(w.act, nullptr, DN_V, {{(const bf*)lv.w_out, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "out projection");
+            if (res_kernel) PF_CHECK(skinny_res(w.act, B, DN_V, lv.w_out, w.hidden, HIDDEN, HIDDEN, stream), "out projection");
+            else PF_CHECK(proj(w.act, nullptr, DN_V, {{(const bf*)lv.w_out, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "out projection");
             ++dn_idx;
         } else {
             bf* kc = (bf*)fa_k_cache + (size_t)fa_idx * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;
@@ -787,14 +868,16 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
                        (const bf*)lv.k_norm, kc, vc, B, max_seq_len, positions, kv_seq);
             launch_pdl(k_fab_attention, dim3(B, FA_Q_HEADS), FAB_WARPS * 32, 0, stream, (const bf*)w.wide, (const bf*)kc, (const bf*)vc, kv_seq,
                        positions, max_seq_len, w.act);
-            PF_CHECK(proj(w.act, nullptr, FA_Q_SIZE, {{(const bf*)lv.w_o, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "o projection");
+            if (res_kernel) PF_CHECK(skinny_res(w.act, B, FA_Q_SIZE, lv.w_o, w.hidden, HIDDEN, HIDDEN, stream), "o projection");
+            else PF_CHECK(proj(w.act, nullptr, FA_Q_SIZE, {{(const bf*)lv.w_o, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "o projection");
             ++fa_idx;
         }
         // gate and up rows meet in one CTA, which applies SwiGLU before it writes
         const bf* wg = lv.w_gateup ? (const bf*)lv.w_gateup : (const bf*)lv.w_gate;
         const bf* wu = lv.w_gateup ? (const bf*)lv.w_gateup + (size_t)INTER * HIDDEN : (const bf*)lv.w_up;
         PF_CHECK(proj(w.hidden, lv.post_norm, HIDDEN, {{wg, wu, w.act, nullptr, INTER, INTER, 2}}), "gate and up projections");
-        PF_CHECK(proj(w.act, nullptr, INTER, {{(const bf*)lv.w_down, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "down projection");
+        if (res_kernel) PF_CHECK(skinny_res(w.act, B, INTER, lv.w_down, w.hidden, HIDDEN, HIDDEN, stream), "down projection");
+        else PF_CHECK(proj(w.act, nullptr, INTER, {{(const bf*)lv.w_down, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "down projection");
     }
     launch_pdl(k_final_norm, B, 512, 0, stream, w.hidden, (const bf*)final_norm_w, bw.normed_f32, (bf*)final_normed, (bf*)hidden_bf16_out);
     constexpr int LMB = 296;                                  // two persistent blocks per SM

@@ -1042,6 +1042,7 @@ int decode_batch_entry(int steps, int* tokens, int* positions, int* output_token
 }  // namespace
 }  // namespace mk
 
+extern "C" void mk_decode_batch_set_residual_kernel(int mode) { mk::g_batch_res_kernel = (mode >= 0 && mode <= 2) ? mode : 1; }
 extern "C" void mk_decode_batch_set_lm_head(int tensor_cores) { mk::g_batch_lm_mma = tensor_cores ? 1 : 0; }
 
 extern "C" int mk_decode_batch(

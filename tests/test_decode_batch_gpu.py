@@ -144,3 +144,16 @@ def test_lm_head_variants_agree(dec):
         finally:
             lib().mk_decode_batch_set_lm_head(1)
     assert torch.equal(runs[0], runs[1])
+
+
+@pytest.mark.parametrize("mode", [0, 2])
+def test_residual_projection_kernels_follow_oracle(dec, small_model, mode):
+    """Both kernels for the out / o / down projections (0: K split over CTAs, partial sums added by the last CTA to
+    arrive; 2: straight-line, 8 rows per CTA) at a batch size where the default would pick the other one."""
+    from luce_megakernel_b200 import lib
+    lib().mk_decode_batch_set_residual_kernel(mode)
+    try:
+        lengths = [7, 30, 12, 5, 21] if mode == 0 else [7, 30, 12, 5, 5, 21, 9, 16, 4, 11]
+        test_batch_follows_oracle_per_sequence(dec, small_model, lengths)
+    finally:
+        lib().mk_decode_batch_set_residual_kernel(1)
