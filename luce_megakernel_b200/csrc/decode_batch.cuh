@@ -118,13 +118,21 @@ constexpr int FAB_WARPS = 16, FAB_UN = 8;      // the kernel is a chain of cache
 __global__ void __launch_bounds__(FAB_WARPS * 32) k_fab_attention(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ kc,
                                                        const __nv_bfloat16* __restrict__ vc, size_t seq_stride,
                                                        const int* __restrict__ pos, int max_seq, __nv_bfloat16* __restrict__ out) {
-    pdl_enter();
+    pdl_launch_next();
     const int b = blockIdx.x, hq = blockIdx.y, g = hq >> 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = min(max(pos[b], 0), max_seq - 1) + 1;
+    const int n = min(max(pos[b], 0), max_seq - 1) + 1;       // positions were advanced a whole step ago
     const __nv_bfloat16* qrow = qkv + (size_t)b * FA_QKV_ROWS + hq * 2 * FA_HEAD_DIM;
     const __nv_bfloat16* kb = kc + (size_t)b * seq_stride + (size_t)g * max_seq * FA_HEAD_DIM;
     const __nv_bfloat16* vb = vc + (size_t)b * seq_stride + (size_t)g * max_seq * FA_HEAD_DIM;
+    // Rows 0 .. n-2 of the cache are older than this step (the kernel before this one appends row n-1 only): ask for
+    // them to be brought into L2 while that kernel runs.  One block per KV head does it, at most 1 MB per tensor.
+    if (threadIdx.x == 0 && (hq & 3) == 0 && n > 1) {
+        const uint32_t bytes = (uint32_t)min(n - 1, 2048) * FA_HEAD_DIM * 2;
+        l2_prefetch(kb, bytes);
+        l2_prefetch(vb, bytes);
+    }
+    pdl_wait_prior();
     float q[8];
     {
         const uint4 u = reinterpret_cast<const uint4*>(qrow)[lane];
