@@ -117,7 +117,19 @@ class ClockSampler:
             for n, v in zip(names, f[2:6]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons)}
+        res = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons)}
+        if not sm:
+            # nvidia-smi had not produced a line yet: one query right after the timed region (clocks are still up)
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits"],
+                                     capture_output=True, text=True, timeout=20).stdout
+                f = [x.strip() for x in out.strip().splitlines()[0].split(",")]
+                res = {"sm_mhz": float(f[0]), "sm_max_mhz": float(f[1]),
+                       "reasons": sorted(n for n, v in zip(names, f[2:6]) if v.lower().startswith("active")),
+                       "sampled": "once, right after the timed region"}
+            except Exception:
+                pass
+        return res
 
 
 class CpuDecodeBaseline:
@@ -163,20 +175,39 @@ def run_reference(args):
             rates.append(r)
     value = statistics.mean(rates)
     sample = f"{per_step} greedy decode tokens per step after a {context}-token prompt, fp32, all host threads"
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": "decode_tokens_per_s_tg128", "value": value, "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * per_step / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }))
+    })
 
 
 def workload_config(n_gpus):
     return {"workload": "configs[1]: 24-layer bf16 hybrid decode, batch 1, 520-token prompt then tg128 greedy",
             "prompt_len": PROMPT_LEN, "gen_len": GEN_LEN, "weights": "random-init seed 0 (drawn on the device)",
             "replicas": n_gpus, "l2": "inputs larger than L2 (1.5 GB of weights streamed per token)"}
+
+
+_RESULT_FD = None
+
+
+def protect_stdout():
+    """Libraries print to stdout from native code (NCCL's version banner): keep fd 1 for the one JSON line and send
+    everything else to stderr."""
+    global _RESULT_FD
+    if _RESULT_FD is None:
+        sys.stdout.flush()
+        _RESULT_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit(obj):
+    line = (json.dumps(obj) + "\n").encode()
+    sys.stdout.flush()
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, line)
 
 
 def main():
@@ -189,6 +220,7 @@ def main():
     ap.add_argument("--no-long-prefill", action="store_true")
     ap.add_argument("--no-batch", action="store_true", help="skip the batch 8 / batch 16 decode figures")
     args = ap.parse_args()
+    protect_stdout()
     if args.impl == "reference":
         return run_reference(args)
 
@@ -232,11 +264,13 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    # the sampler starts with the warm-up (the same workload as the timed region) so that short runs, and runs where
+    # eight ranks start nvidia-smi at once, still collect samples under load
+    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else 0)
+    sampler.start()
     for _ in range(max(args.warmup, 3)):
         tg128_device()
-    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else 0)
     barrier()
-    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
@@ -377,7 +411,7 @@ def main():
             v = CpuDecodeBaseline(sd, 64, threads).tokens_per_s(n_tok)
             out["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
                                    "sample": f"{n_tok} greedy decode tokens after a 64-token prompt, fp32 oracle port"}
-        print(json.dumps(out))
+        emit(out)
     if use_dist:
         dist.destroy_process_group()
 
