@@ -37,18 +37,29 @@ __global__ void __launch_bounds__(512, 2) k_dnb_layer(const __nv_bfloat16* __res
     float4 s[RW];
 #pragma unroll
     for (int r = 0; r < RW; ++r) s[r] = reinterpret_cast<const float4*>(sbase + r * DN_KEY)[lane];
-    // the state is not written by the projection kernel before this one: its rows are requested above, ahead of the wait
+    // neither the state nor the conv window is written by the projection kernel before this one: both are requested
+    // here, ahead of the wait
+    float* cs = conv_state + (size_t)b * conv_seq_stride;
+    float4 win[3];
+    uint2 cw[3];
+    if (threadIdx.x < 128) {
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+            const int ch = r * DN_QK + h * DN_KEY + threadIdx.x;
+            win[r] = *reinterpret_cast<const float4*>(cs + ch * 4);
+            cw[r] = __ldg(reinterpret_cast<const uint2*>(conv_w) + ch);
+        }
+    }
     pdl_wait_prior();
     if (threadIdx.x < 128) {
         const int c = threadIdx.x;
-        float* cs = conv_state + (size_t)b * conv_seq_stride;
         float val[3];
 #pragma unroll
         for (int r = 0; r < 3; ++r) {
             const int ch = r * DN_QK + h * DN_KEY + c;
-            const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + ch);
+            const uint2 wr = cw[r];
             const float w4[4] = {bf_lo(wr.x), bf_hi(wr.x), bf_lo(wr.y), bf_hi(wr.y)};
-            const float4 old = *reinterpret_cast<const float4*>(cs + ch * 4);
+            const float4 old = win[r];
             const float x[4] = {old.y, old.z, old.w, ld_bf(qkv + (size_t)b * DN_CONV_CH + ch)};
             float co = 0.f;
 #pragma unroll
