@@ -309,14 +309,14 @@ def main():
     barrier()
     pp_ms = p0.elapsed_time(p1) / 10
 
-    # dense prefill at 8192 and 32768 tokens (BASELINE configs[2]), single GPU only: 1 warm-up + 2 timed calls
+    # dense prefill at 8192 and 32768 tokens (BASELINE.json configs[2]), single GPU only: 1 warm-up + 2 timed calls
     long_pp = []
     if world == 1 and not args.no_long_prefill:
         import ctypes
         for S_, sparse in ((8192, False), (32768, False), (65536, True)):
             d2 = M.Decoder(weights=weights, max_seq_len=S_ + 8, api="cabi")
             ids = torch.randint(0, M.VOCAB_SIZE, (S_,), generator=g).to(torch.int32).cuda()
-            # BASELINE configs[4]: 128 x 128 blocks, sink block 0, 4-block window, top 10 % by pooled q.k
+            # BASELINE.json configs[4]: 128 x 128 blocks, sink block 0, 4-block window, top 10 % by pooled q.k
             lib().mk_prefill_set_block_sparse(1 if sparse else 0, ctypes.c_double(0.10), 4, 1)
             try:
                 d2.prefill(ids)
@@ -334,7 +334,7 @@ def main():
         if lib().mk_device_status() != 0 or lib().mk_prefill_status() != 0:
             raise SystemExit("device-side wait timed out during the long prefill")
 
-    # batched decode (BASELINE configs[3] and [4]): batch 8 and 16 per GPU, a pp520 prompt per sequence, then tg128
+    # batched decode (BASELINE.json configs[3] and [4]): batch 8 and 16 per GPU, a pp520 prompt per sequence, then tg128
     # with the tokens fed back on the device; 1 warm-up run + 2 timed runs of 128 steps
     batch_ms = []
     if not args.no_batch:
