@@ -598,23 +598,33 @@ inline cudaError_t skinny_proj(const void* A, const void* norm_w, int B, int K, 
 // With 128 CTAs the entire matrix is in flight at once.  C doubles as the residual (read and written in place).
 template <int NT, int STEPS>   // K = 256 * STEPS
 __global__ void __launch_bounds__(256, 2) k_skinny_res(const __nv_bfloat16* __restrict__ A, int B, const __nv_bfloat16* __restrict__ W,
-                                                       __nv_bfloat16* C, int ldc) {
+                                                       __nv_bfloat16* C, int ldc, int* __restrict__ err) {
     pdl_launch_next();
     constexpr int K = 256 * STEPS, RS = K / 8 + 4;
     extern __shared__ __align__(16) uint4 as[];              // [NT * 8][RS] activations, rows >= B zero
     __shared__ float red[8][NT * 8][9];
+    __shared__ __align__(8) unsigned long long bar_mem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
     const int n0 = blockIdx.x * 8;
     const uint4* w0 = reinterpret_cast<const uint4*>(W + (size_t)(n0 + g) * K) + tig;
     uint4 lo[STEPS];
 #pragma unroll
     for (int u = 0; u < STEPS; ++u) lo[u] = __ldcs(w0 + (warp + 8 * u) * 4);
-    pdl_wait_prior();
-    for (int i = threadIdx.x; i < NT * 8 * (K / 8); i += 256) {
-        const int b = i / (K / 8), c = i - b * (K / 8);
-        as[b * RS + c] = (b < B) ? *reinterpret_cast<const uint4*>(A + (size_t)b * K + c * 8) : make_uint4(0, 0, 0, 0);
+    const uint32_t bar = smem_u32(&bar_mem);
+    if (threadIdx.x == 0) { mbar_init(bar, 1); fence_mbar_init(); }
+    for (int i = threadIdx.x; i < (NT * 8 - B) * (K / 8); i += 256) {
+        const int b = B + i / (K / 8), c = i % (K / 8);
+        as[b * RS + c] = make_uint4(0, 0, 0, 0);
     }
-    __syncthreads();
+    __syncthreads();                                         // barrier initialised, padding rows written
+    pdl_wait_prior();
+    // the B activation rows arrive as B bulk copies (one thread issues them; no per-thread load / store round trips)
+    if (threadIdx.x == 0) {
+        mbar_expect_tx(bar, (uint32_t)B * K * 2);
+        const uint64_t pol = l2_policy_evict_last();
+        for (int b = 0; b < B; ++b) bulk_g2s(smem_u32(as + b * RS), A + (size_t)b * K, K * 2, bar, pol);
+    }
+    if (!mbar_wait(bar, 0) && threadIdx.x == 0) *err = 5;    // bounded: gives up and reports instead of hanging
     float acc[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; ++t) { acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f; }
@@ -646,7 +656,7 @@ __global__ void __launch_bounds__(256, 2) k_skinny_res(const __nv_bfloat16* __re
 }
 
 template <int NT, int STEPS>
-inline cudaError_t launch_skinny_res(const void* A, int B, const void* W, void* C, int N, int ldc, cudaStream_t stream) {
+inline cudaError_t launch_skinny_res(const void* A, int B, const void* W, void* C, int N, int ldc, int* err, cudaStream_t stream) {
     constexpr size_t smem = (size_t)NT * 8 * (256 * STEPS / 8 + 4) * 16;
     static bool attr[64] = {false};
     int dev = 0;
@@ -657,14 +667,14 @@ inline cudaError_t launch_skinny_res(const void* A, int B, const void* W, void* 
         attr[dev] = true;
     }
     return launch_pdl(k_skinny_res<NT, STEPS>, N / 8, 256, smem, stream, (const __nv_bfloat16*)A, B, (const __nv_bfloat16*)W,
-                      (__nv_bfloat16*)C, ldc);
+                      (__nv_bfloat16*)C, ldc, err);
 }
 
 // C[b][n] += sum_k A[b][k] W[n][k] for K = 2048 or 3584, N a multiple of 8
-inline cudaError_t skinny_res(const void* A, int B, int K, const void* W, void* C, int N, int ldc, cudaStream_t stream) {
-    if (B < 1 || B > 16 || N % 8 || (K != 2048 && K != 3584)) return cudaErrorInvalidValue;
-    if (B <= 8) return K == 2048 ? launch_skinny_res<1, 8>(A, B, W, C, N, ldc, stream) : launch_skinny_res<1, 14>(A, B, W, C, N, ldc, stream);
-    return K == 2048 ? launch_skinny_res<2, 8>(A, B, W, C, N, ldc, stream) : launch_skinny_res<2, 14>(A, B, W, C, N, ldc, stream);
+inline cudaError_t skinny_res(const void* A, int B, int K, const void* W, void* C, int N, int ldc, int* err, cudaStream_t stream) {
+    if (B < 1 || B > 16 || N % 8 || (K != 2048 && K != 3584) || !err) return cudaErrorInvalidValue;
+    if (B <= 8) return K == 2048 ? launch_skinny_res<1, 8>(A, B, W, C, N, ldc, err, stream) : launch_skinny_res<1, 14>(A, B, W, C, N, ldc, err, stream);
+    return K == 2048 ? launch_skinny_res<2, 8>(A, B, W, C, N, ldc, err, stream) : launch_skinny_res<2, 14>(A, B, W, C, N, ldc, err, stream);
 }
 
 // LM head of a batched step on the tensor cores: the same fragment scheme as k_skinny_proj, but a warp keeps a
@@ -867,7 +877,7 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
             launch_pdl(k_dnb_layer, dim3(B, DN_HEADS), 512, 0, stream, (const bf*)w.wide, (const bf*)w.z, (const float*)bw.graw,
                        (const bf*)lv.conv_w, (const bf*)lv.a_log, (const bf*)lv.dt_bias, (const bf*)lv.dn_norm, cstate, cv_seq, state,
                        st_seq, w.act);
-            if (res_kernel) PF_CHECK(skinny_res(w.act, B, DN_V, lv.w_out, w.hidden, HIDDEN, HIDDEN, stream), "out projection");
+            if (res_kernel) PF_CHECK(skinny_res(w.act, B, DN_V, lv.w_out, w.hidden, HIDDEN, HIDDEN, w.err, stream), "out projection");
             else PF_CHECK(proj(w.act, nullptr, DN_V, {{(const bf*)lv.w_out, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "out projection");
             ++dn_idx;
         } else {
@@ -887,7 +897,7 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
                        (const bf*)lv.k_norm, kc, vc, B, max_seq_len, positions, kv_seq);
             launch_pdl(k_fab_attention, dim3(B, FA_Q_HEADS), FAB_WARPS * 32, 0, stream, (const bf*)w.wide, (const bf*)kc, (const bf*)vc, kv_seq,
                        positions, max_seq_len, w.act);
-            if (res_kernel) PF_CHECK(skinny_res(w.act, B, FA_Q_SIZE, lv.w_o, w.hidden, HIDDEN, HIDDEN, stream), "o projection");
+            if (res_kernel) PF_CHECK(skinny_res(w.act, B, FA_Q_SIZE, lv.w_o, w.hidden, HIDDEN, HIDDEN, w.err, stream), "o projection");
             else PF_CHECK(proj(w.act, nullptr, FA_Q_SIZE, {{(const bf*)lv.w_o, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "o projection");
             ++fa_idx;
         }
@@ -895,7 +905,7 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
         const bf* wg = lv.w_gateup ? (const bf*)lv.w_gateup : (const bf*)lv.w_gate;
         const bf* wu = lv.w_gateup ? (const bf*)lv.w_gateup + (size_t)INTER * HIDDEN : (const bf*)lv.w_up;
         PF_CHECK(proj(w.hidden, lv.post_norm, HIDDEN, {{wg, wu, w.act, nullptr, INTER, INTER, 2}}), "gate and up projections");
-        if (res_kernel) PF_CHECK(skinny_res(w.act, B, INTER, lv.w_down, w.hidden, HIDDEN, HIDDEN, stream), "down projection");
+        if (res_kernel) PF_CHECK(skinny_res(w.act, B, INTER, lv.w_down, w.hidden, HIDDEN, HIDDEN, w.err, stream), "down projection");
         else PF_CHECK(proj(w.act, nullptr, INTER, {{(const bf*)lv.w_down, nullptr, w.hidden, w.hidden, HIDDEN, HIDDEN, 0}}), "down projection");
     }
     launch_pdl(k_final_norm, B, 512, 0, stream, w.hidden, (const bf*)final_norm_w, bw.normed_f32, (bf*)final_normed, (bf*)hidden_bf16_out);
