@@ -209,9 +209,9 @@ int mk_decode_batch(
     int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
 /* LM head of the batched step: 1 (default) = tensor cores with the f32 activations as two bf16 terms, 0 = f32 FMAs. */
 void mk_decode_batch_set_lm_head(int tensor_cores);
-/* Projections back into the residual stream (out / o / down): 2 = straight-line kernel, 8 rows per CTA, all weights
- * requested before the dependency wait; 0 = 16 rows per CTA with K split over 4 CTAs; 1 (default) = the first up to
- * batch 8, the second beyond. */
+/* Projections back into the residual stream (out / o / down): 1 or 2 (default) = straight-line kernel, 8 rows per CTA,
+ * all weights requested before the dependency wait, activations staged by bulk async copies; 0 = 16 rows per CTA with K
+ * split over 4 CTAs. */
 void mk_decode_batch_set_residual_kernel(int mode);
 int mk_decode_batch_many(
     int steps, int *tokens, int *positions, int *tokens_log, int batch,

@@ -813,7 +813,7 @@ __global__ void k_batch_advance(int* __restrict__ tokens, const int* __restrict_
     if (log_row) log_row[b] = t;
 }
 
-int g_batch_res_kernel = 1;        // projections into the residual stream: 0 = K split over CTAs, 2 = straight-line 8-row kernel, 1 = by batch size
+int g_batch_res_kernel = 1;        // projections into the residual stream: 0 = K split over CTAs, otherwise the straight-line 8-row kernel
 int g_batch_lm_mma = 1;            // LM head of the batched step: 1 = tensor cores (bf16 hi + lo), 0 = f32 CUDA cores
 struct BatchWs { float *normed_f32 = nullptr, *bval = nullptr, *graw = nullptr; int *bidx = nullptr, *chosen = nullptr; };
 BatchWs g_bws[64];
@@ -856,9 +856,7 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
     const size_t kv_seq = (size_t)n_fa * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;          // elements per sequence
     const size_t st_seq = (size_t)n_dn * DN_HEADS * DN_VAL * DN_KEY, cv_seq = (size_t)n_dn * DN_CONV_CH * DN_CONV_K;
 
-    // out / o / down: the straight-line kernel stages all B activation rows in each of its 128 CTAs, which pays up to
-    // B = 8; beyond, 64 row groups with K split over four CTAs each read less
-    const bool res_kernel = g_batch_res_kernel == 1 ? B <= 8 : g_batch_res_kernel == 2;
+    const bool res_kernel = g_batch_res_kernel != 0;          // out / o / down: straight-line kernel unless switched off
     launch_pdl(k_embed, B, 128, 0, stream, tokens, (const bf*)embed_weight, w.hidden, B, vocab);
     int dn_idx = 0, fa_idx = 0;
     for (int li = 0; li < num_layers; ++li) {

@@ -149,7 +149,7 @@ def test_lm_head_variants_agree(dec):
 @pytest.mark.parametrize("mode", [0, 2])
 def test_residual_projection_kernels_follow_oracle(dec, small_model, mode):
     """Both kernels for the out / o / down projections (0: K split over CTAs, partial sums added by the last CTA to
-    arrive; 2: straight-line, 8 rows per CTA) at a batch size where the default would pick the other one."""
+    arrive; 2: straight-line, 8 rows per CTA, the default), with one and with two batch tiles."""
     from luce_megakernel_b200 import lib
     lib().mk_decode_batch_set_residual_kernel(mode)
     try:
