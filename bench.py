@@ -2,10 +2,11 @@
 """Headline benchmark: batch-1 greedy decode (tg128 after a 520-token prompt) of the 24-layer
 Qwen3.5-0.8B-architecture hybrid in bf16 on B200, random-init weights, synthetic token ids.
 
-    python bench.py --gpus N --steps K --warmup W            # this repo's kernels
-    python bench.py --impl reference --gpus N --steps K ...  # CPU baseline arm (rank 0 only)
+    python bench.py --gpus N --steps K --warmup W                # this repo's kernels
+    python bench.py --impl reference --gpus N --steps K ...      # CPU baseline arm (rank 0 only)
+    python bench.py --impl reference_gpu --steps K ...           # the reference's own CUDA kernels, same GPU (rank 0 only)
 
-One "step" is one tg128 pass: 128 decode launches with the token fed back on the device.
+One "step" is one tg128 pass: 128 greedy decode steps with the token fed back on the device.
 Multi-GPU runs are independent replicas (one process per GPU, no data-path collective); the
 reported value is the aggregate over all ranks divided by the slowest rank's time.
 Prints ONE JSON line on rank 0.
@@ -26,13 +27,16 @@ sys.path.insert(0, ROOT)
 PROMPT_LEN = 520
 GEN_LEN = 128
 MAX_SEQ = 2048
-WEIGHT_BYTES_PER_TOKEN = 1_546_073_728      # weights + DeltaNet state r/w + conv state r/w
+WEIGHT_BYTES_PER_TOKEN = 1_546_073_728      # bf16 weights + DeltaNet state r/w + conv state r/w
+NVFP4_BYTES_PER_TOKEN = 466_073_216         # the same with every linear layer and the LM head at 0.5625 bytes per weight
 KV_BYTES_PER_POS = 12_288                   # K and V rows read per cached position, 6 layers
 STATE_BYTES_PER_SEQ = 41_287_680            # DeltaNet state and conv window, read + written once per token
+# dram__bytes_read.sum + dram__bytes_write.sum of one bf16 decode launch (ncu capture at context 520)
+TRAFFIC_BYTES_PER_LAUNCH = 1_537_192_800
 
 
-def algorithmic_bytes_per_token(context_len: float) -> float:
-    return WEIGHT_BYTES_PER_TOKEN + KV_BYTES_PER_POS * context_len
+def algorithmic_bytes_per_token(context_len: float, nvfp4: bool = False) -> float:
+    return (NVFP4_BYTES_PER_TOKEN if nvfp4 else WEIGHT_BYTES_PER_TOKEN) + KV_BYTES_PER_POS * context_len
 
 
 def batch_step_bytes(batch: int, context_len: float) -> float:
@@ -132,9 +136,51 @@ class ClockSampler:
         return res
 
 
-class CpuDecodeBaseline:
-    """The CPU oracle (fp32 port of the reference decode arithmetic) as a timed baseline:
-    an untimed `context`-token prefill, then timed greedy decode steps on all host threads."""
+# ---- CPU baselines ---------------------------------------------------------------------------------------------
+
+class HfCpuBaseline:
+    """The reference's PyTorch path on the host cores: `transformers`' Qwen3_5ForCausalLM (the class the reference
+    loads in megakernel/final_bench.py:117-149), fp32, eager, with the benchmark's seeded weights: an untimed
+    `context`-token prefill, then timed greedy decode steps on all host threads."""
+    kind = "hf"
+
+    def __init__(self, state_dict, context, threads):
+        from transformers import AutoModelForCausalLM, Qwen3_5TextConfig
+        torch.set_num_threads(threads)
+        vocab = state_dict["model.embed_tokens.weight"].shape[0]
+        n_layers = 1 + max(int(k.split(".")[2]) for k in state_dict if k.startswith("model.layers."))
+        cfg = Qwen3_5TextConfig(
+            vocab_size=vocab, hidden_size=1024, intermediate_size=3584, num_hidden_layers=n_layers,
+            num_attention_heads=8, num_key_value_heads=2, head_dim=256, linear_num_key_heads=16, linear_num_value_heads=16,
+            linear_key_head_dim=128, linear_value_head_dim=128, linear_conv_kernel_dim=4, tie_word_embeddings=True,
+            max_position_embeddings=max(4096, context + 4096), rms_norm_eps=1e-6,
+            rope_parameters={"rope_theta": 1.0e7, "partial_rotary_factor": 0.25, "rope_type": "default"})
+        with torch.device("meta"):                      # no random init of 0.75 B parameters that are overwritten anyway
+            model = AutoModelForCausalLM.from_config(cfg, dtype=torch.float32)
+        model = model.to_empty(device="cpu")
+        model.model.rotary_emb = type(model.model.rotary_emb)(config=cfg)       # its buffers are not in the state dict
+        sd = {k: v.to(torch.float32) for k, v in state_dict.items()}
+        sd["lm_head.weight"] = sd["model.embed_tokens.weight"]
+        model.load_state_dict(sd, strict=True, assign=True)
+        self.model = model.eval()
+        g = torch.Generator().manual_seed(0)
+        prompt = torch.randint(0, vocab, (context,), generator=g)
+        with torch.no_grad():
+            r = self.model(input_ids=prompt[None], use_cache=True)
+        self.cache, self.tok = r.past_key_values, int(r.logits[0, -1].argmax())
+
+    def tokens_per_s(self, n_tokens):
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            for _ in range(n_tokens):
+                r = self.model(input_ids=torch.tensor([[self.tok]]), past_key_values=self.cache, use_cache=True)
+                self.cache, self.tok = r.past_key_values, int(r.logits[0, -1].argmax())
+        return n_tokens / (time.perf_counter() - t0)
+
+
+class PortCpuBaseline:
+    """Fallback when `transformers` cannot be imported: the CPU oracle (fp32 port of the reference decode arithmetic)."""
+    kind = "port"
 
     def __init__(self, state_dict, context, threads):
         from oracle import qwen35_oracle as O      # the checker, timed here only as the CPU baseline
@@ -152,6 +198,20 @@ class CpuDecodeBaseline:
         return n_tokens / (time.perf_counter() - t0)
 
 
+def make_cpu_baseline(state_dict, context, threads):
+    try:
+        return HfCpuBaseline(state_dict, context, threads)
+    except Exception as e:                      # transformers missing or without this model class
+        sys.stderr.write(f"transformers path unavailable ({e!r}); timing the oracle port instead\n")
+        return PortCpuBaseline(state_dict, context, threads)
+
+
+def cpu_sample_text(base, n_tokens, context):
+    what = ("transformers Qwen3_5ForCausalLM, fp32 eager (the reference's PyTorch path)" if base.kind == "hf"
+            else "fp32 oracle port of the reference decode arithmetic")
+    return f"{n_tokens} greedy decode tokens after a {context}-token prompt; {what}; all host threads"
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -159,36 +219,99 @@ def dist_env():
     return rank, local, world
 
 
+def workload_config(n_gpus):
+    return {"workload": "configs[1]: 24-layer bf16 hybrid decode, batch 1, 520-token prompt then tg128 greedy",
+            "prompt_len": PROMPT_LEN, "gen_len": GEN_LEN, "weights": "random-init seed 0 (drawn on the device)",
+            "replicas": n_gpus, "l2": "inputs larger than L2 (1.5 GB of weights streamed per token)"}
+
+
 def run_reference(args):
-    rank, _, world = dist_env()
+    """CPU arm: the reference's PyTorch path on this box's host cores, same model, same context, bounded sample."""
+    rank, _, _ = dist_env()
     if rank != 0:
         return
     from luce_megakernel_b200.weights import random_state_dict
     threads = os.cpu_count() or 1
-    sd = random_state_dict(0)
-    context, per_step = 64, 4
-    base = CpuDecodeBaseline(sd, context, threads)
+    per_step = 4
+    base = make_cpu_baseline(random_state_dict(0), PROMPT_LEN, threads)
     rates = []
     for i in range(args.warmup + args.steps):
         r = base.tokens_per_s(per_step)
         if i >= args.warmup:
             rates.append(r)
     value = statistics.mean(rates)
-    sample = f"{per_step} greedy decode tokens per step after a {context}-token prompt, fp32, all host threads"
+    cfg = workload_config(args.gpus)
+    cfg.update({"weights": "random-init seed 0 (drawn on the host)", "replicas": 1,
+                "sample_per_step": f"{per_step} decode tokens per step (of the 128 of a tg128 pass), context {PROMPT_LEN}+",
+                "l2": "n/a (host memory)"})
     emit({
         "impl": "reference", "metric": "decode_tokens_per_s_tg128", "value": value, "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * per_step / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(args.gpus),
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "config": cfg,
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": base.kind,
+                         "sample": cpu_sample_text(base, per_step, PROMPT_LEN) + ", per step"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
 
 
-def workload_config(n_gpus):
-    return {"workload": "configs[1]: 24-layer bf16 hybrid decode, batch 1, 520-token prompt then tg128 greedy",
-            "prompt_len": PROMPT_LEN, "gen_len": GEN_LEN, "weights": "random-init seed 0 (drawn on the device)",
-            "replicas": n_gpus, "l2": "inputs larger than L2 (1.5 GB of weights streamed per token)"}
+def run_reference_gpu(args):
+    """The reference's own decode / prefill kernels (megakernel/kernel.cu, prefill.cu, compiled unmodified for sm_100a by
+    oracle/build_oracle.py) through their stock launch_decode / launch_prefill_bf16 entry points on this GPU: pp520, then
+    tg128 with the host token loop the reference's driver uses (megakernel/model.py:278-293)."""
+    rank, local, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle.ref_kernels import RefDecoder, load_ref_lib      # test infrastructure, executed only by this arm
+    lib = load_ref_lib()
+    if lib is None or not torch.cuda.is_available():
+        emit({"impl": "reference_gpu", "unavailable": "oracle/_ref/libref_megakernel.so was not built (needs the reference checkout at build time) or no GPU"})
+        return
+    torch.cuda.set_device(local)
+    from luce_megakernel_b200 import model as M
+    weights, _ = M.load_weights(seed=0, device_init=True)
+    mine = M.Decoder(weights=weights, max_seq_len=MAX_SEQ, api="cabi")     # holds the weights and the pointer table only
+    ref = RefDecoder(lib, mine, MAX_SEQ)
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, M.VOCAB_SIZE, (PROMPT_LEN,), generator=g).to(torch.int32).cuda()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def tg128():
+        ref.pos = PROMPT_LEN
+        t = first
+        for _ in range(GEN_LEN):
+            t = ref.step(t)
+
+    ref.reset()
+    first = ref.prefill(ids)
+    for _ in range(max(args.warmup, 1)):
+        tg128()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        tg128()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    ref.reset(); ref.prefill(ids)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(5):
+        ref.reset(); ref.prefill(ids)
+    e1.record()
+    torch.cuda.synchronize()
+    pp_ms = e0.elapsed_time(e1) / 5
+    value = GEN_LEN * args.steps / (ms * 1e-3)
+    emit({
+        "impl": "reference_gpu", "metric": "decode_tokens_per_s_tg128", "value": value, "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(args.warmup, 1), "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(1),
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 4 * GEN_LEN, "d2h_bytes_per_step": 4 * GEN_LEN,
+                "api": "launch_decode per token with a host round trip, as the reference's Decoder.step() does"},
+        "prefill": {"prompt_len": PROMPT_LEN, "ms": pp_ms, "tok_s": PROMPT_LEN / (pp_ms * 1e-3)},
+        "gpu_launches": 2 * GEN_LEN * args.steps,
+        "note": "reference kernels compiled from the checkout for sm_100a with NUM_BLOCKS=148 (megakernel/setup.py flags)",
+    })
 
 
 _RESULT_FD = None
@@ -210,19 +333,33 @@ def emit(obj):
     os.write(_RESULT_FD if _RESULT_FD is not None else 1, line)
 
 
+def cpu_state_dict(weights):
+    """Rebuilds a transformers-style state dict (CPU tensors) from the packed device weights."""
+    from luce_megakernel_b200.model import _DN_KEYS, _FA_KEYS
+    sd = {"model.embed_tokens.weight": weights["embed_weight"].cpu(), "model.norm.weight": weights["final_norm_weight"].cpu()}
+    for i, ld in enumerate(weights["layer_data"]):
+        keys = _FA_KEYS if ld["type"] == 1 else _DN_KEYS
+        for k, t in zip(keys, ld["ptrs"]):
+            sd[f"model.layers.{i}.{k}"] = t.cpu()
+    return sd
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference_gpu"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-long-prefill", action="store_true")
     ap.add_argument("--no-batch", action="store_true", help="skip the batch 8 / batch 16 decode figures")
+    ap.add_argument("--no-nvfp4", action="store_true", help="skip the NVFP4 decode figure")
     args = ap.parse_args()
     protect_stdout()
     if args.impl == "reference":
         return run_reference(args)
+    if args.impl == "reference_gpu":
+        return run_reference_gpu(args)
 
     rank, local, world = dist_env()
     if not torch.cuda.is_available():
@@ -234,7 +371,7 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
 
-    from luce_megakernel_b200 import lib, model as M
+    from luce_megakernel_b200 import lib, model as M, replicas as R
     weights, _ = M.load_weights(seed=rank, device_init=True)
     dec = M.Decoder(weights=weights, max_seq_len=MAX_SEQ, api="cabi")
     g = torch.Generator().manual_seed(rank)
@@ -245,9 +382,9 @@ def main():
     prompt_dev = torch.tensor(prompt, dtype=torch.int32, device="cuda")
     first = dec.prefill(prompt_dev)
 
-    def tg128_device():
-        dec._position = PROMPT_LEN
-        return dec.step_many(first, GEN_LEN)
+    def tg128_device(d=dec):
+        d._position = PROMPT_LEN
+        return d.step_many(first, GEN_LEN)          # ONE persistent launch: 128 steps, token fed back on the device
 
     def tg128_e2e():
         # reference-style public API: one call per token, token id from the host, result read back
@@ -259,10 +396,17 @@ def main():
         return t
 
     def barrier():
-        torch.cuda.synchronize()
-        if use_dist:
-            dist.barrier()
-        torch.cuda.synchronize()
+        R.timing_barrier(torch.cuda.synchronize)
+
+    def timed(fn, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        barrier()
+        return e0.elapsed_time(e1)
 
     # the sampler starts with the warm-up (the same workload as the timed region) so that short runs, and runs where
     # eight ranks start nvidia-smi at once, still collect samples under load
@@ -270,15 +414,8 @@ def main():
     sampler.start()
     for _ in range(max(args.warmup, 3)):
         tg128_device()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        tg128_device()
-    e1.record()
-    barrier()
+    ms = timed(tg128_device, args.steps)
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
     status = lib().mk_device_status()
     if status != 0:
         raise SystemExit(f"device-side wait timed out (status {status})")
@@ -293,6 +430,21 @@ def main():
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
 
+    # NVFP4 decode: every linear layer and the LM head as e2m1 in 16-element blocks with E4M3
+    # block scales and an fp32 tensor scale, bf16 KV cache; same prompt state (bf16 prefill), then tg128
+    nv_ms = 0.0
+    if not args.no_nvfp4:
+        from luce_megakernel_b200 import model_nvfp4 as MQ
+        q = MQ.DecoderTS(weights, max_seq_len=MAX_SEQ)
+        q.adopt_state(dec)
+        for _ in range(3):
+            tg128_device(q)
+        nv_ms = timed(lambda: tg128_device(q), args.steps)
+        if lib().mk_device_status() != 0:
+            raise SystemExit("device-side wait timed out during the NVFP4 decode")
+        del q
+        weights.pop("nvfp4_ts", None)
+
     # prefill pp520 (secondary figure): 3 warm-ups, then 10 timed calls of the prefill op
     def pp():
         dec._position = 0
@@ -300,19 +452,13 @@ def main():
         return dec.prefill(prompt_dev)
     for _ in range(3):
         pp()
-    barrier()
-    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p0.record()
-    for _ in range(10):
-        pp()
-    p1.record()
-    barrier()
-    pp_ms = p0.elapsed_time(p1) / 10
+    pp_ms = timed(pp, 10) / 10
 
     # dense prefill at 8192 and 32768 tokens, single GPU only: 1 warm-up + 2 timed calls
     long_pp = []
     if world == 1 and not args.no_long_prefill:
         import ctypes
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         for S_, sparse in ((8192, False), (32768, False), (65536, True)):
             d2 = M.Decoder(weights=weights, max_seq_len=S_ + 8, api="cabi")
             ids = torch.randint(0, M.VOCAB_SIZE, (S_,), generator=g).to(torch.int32).cuda()
@@ -345,39 +491,44 @@ def main():
             for r in range(3):
                 bd.reset()
                 bd.prefill(prompts)
-                barrier()
-                p0.record()
-                bd.step_many(GEN_LEN)
-                p1.record()
-                barrier()
-                runs.append(p0.elapsed_time(p1))
+                runs.append(timed(lambda: bd.step_many(GEN_LEN), 1))
             batch_ms.append(sum(runs[1:]) / 2 / GEN_LEN)
             del bd
         if lib().mk_prefill_status() != 0:
             raise SystemExit("device-side wait timed out during the batched decode")
 
-    t_all = torch.tensor([ms, e2e_s, pp_ms] + (batch_ms or [0.0, 0.0]), dtype=torch.float64, device="cuda")
+    # every rank's device time for the timed tg128 region (the whole-job figure uses the slowest), plus the other timings
+    tokens = GEN_LEN * args.steps
+    per_rank = R.gather_results(R.ReplicaResult(tokens=tokens, seconds=ms * 1e-3))
+    agg = R.aggregate(per_rank)
+    t_all = torch.tensor([e2e_s, pp_ms, nv_ms] + (batch_ms or [0.0, 0.0]), dtype=torch.float64, device="cuda")
     if use_dist:
         dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
-    ms_max, e2e_max, pp_max = float(t_all[0]), float(t_all[1]), float(t_all[2])
+    e2e_max, pp_max, nv_max = float(t_all[0]), float(t_all[1]), float(t_all[2])
     batch_max = [float(t_all[3]), float(t_all[4])]
 
     if rank == 0:
-        tokens = GEN_LEN * args.steps
-        value = world * tokens / (ms_max * 1e-3)
-        us_per_launch = ms_max * 1e3 / tokens
+        ms_max = agg["seconds"] * 1e3
+        value = agg["tokens_per_s"]
+        us_per_launch_step = ms_max * 1e3 / tokens
         avg_ctx = PROMPT_LEN + 1 + (GEN_LEN - 1) / 2.0
         peak, peak_kind = measured_hbm_peak()
-        achieved = algorithmic_bytes_per_token(avg_ctx) / (us_per_launch * 1e-6) / 1e9
+        # one launch of the persistent kernel runs GEN_LEN steps: bytes and duration per launch are per 128 tokens
+        bytes_per_launch = GEN_LEN * algorithmic_bytes_per_token(avg_ctx)
+        achieved = bytes_per_launch / (GEN_LEN * us_per_launch_step * 1e-6) / 1e9
         out = {
             "metric": "decode_tokens_per_s_tg128", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": workload_config(world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": f"of {peak_kind}", "traffic": TRAFFIC_BYTES_PER_LAUNCH,
-                         "algorithmic_bytes_per_launch": algorithmic_bytes_per_token(avg_ctx),
-                         "us_per_launch": us_per_launch, "kernel": "decode_megakernel_bf16"},
+                         "peak_kind": f"of {peak_kind}", "traffic": GEN_LEN * TRAFFIC_BYTES_PER_LAUNCH,
+                         "algorithmic_bytes_per_launch": bytes_per_launch,
+                         "algorithmic_bytes_per_token": algorithmic_bytes_per_token(avg_ctx),
+                         "us_per_launch": GEN_LEN * us_per_launch_step, "us_per_token": us_per_launch_step,
+                         "tokens_per_launch": GEN_LEN, "kernel": "decode_megakernel_bf16",
+                         "traffic_note": "ncu capture of a one-token launch at context 520, times the 128 tokens of a launch"},
+            "per_rank_us_per_token": [r.seconds * 1e6 / r.tokens for r in per_rank],
             "e2e": {"value": world * GEN_LEN * e2e_steps / e2e_max, "unit": "tok/s",
                     "h2d_bytes_per_step": 4 * GEN_LEN, "d2h_bytes_per_step": 4 * GEN_LEN,
                     "api": "Decoder.step(): one launch_decode call per token, host token in, host token out"},
@@ -386,9 +537,19 @@ def main():
                         "frac_of_bf16_peak": PREFILL_TFLOP_PP520 / (pp_max * 1e-3) / measured_bf16_peak(),
                         "note": "prefill_bf16 op: persistent tcgen05/TMEM GEMMs fed by TMA, chunk-64 DeltaNet scan on "
                                 "mma.sync, causal GQA flash attention on tcgen05/TMEM"},
-            "gpu_launches": world * tokens,
+            "gpu_launches": world * args.steps,
             "clocks": clocks,
         }
+        if nv_max > 0:
+            nv_us = nv_max * 1e3 / tokens
+            nv_bytes = algorithmic_bytes_per_token(avg_ctx, nvfp4=True)
+            out["nvfp4_decode"] = {
+                "format": "e2m1 in 16-element blocks, E4M3 block scales, fp32 scale per matrix; all linear layers and the LM head; bf16 KV cache",
+                "tok_s": world * 1e6 / nv_us, "us_per_token": nv_us, "vs_bf16": us_per_launch_step / nv_us,
+                "roofline": {"bound": "hbm", "achieved": nv_bytes / (nv_us * 1e-6) / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": nv_bytes / (nv_us * 1e-6) / 1e9 / peak, "algorithmic_bytes_per_token": nv_bytes},
+                "note": "mk_decode_nvfp4_ts: 128 steps per launch; one dependent phase is one ring chunk per CTA, so the "
+                        "step is bound by the 120 activation exchanges, not by bytes"}
         if batch_ms:
             hbm, _ = measured_hbm_peak()
             out["decode_batch"] = [
@@ -406,30 +567,14 @@ def main():
                  "tflops_dense_equivalent": prefill_tflop(S_) / (ms_ * 1e-3)} for S_, ms_, sp_ in long_pp]
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            sd = {k: v for k, v in cpu_state_dict(weights).items()}
-            n_tok = 6
-            v = CpuDecodeBaseline(sd, 64, threads).tokens_per_s(n_tok)
-            out["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
-                                   "sample": f"{n_tok} greedy decode tokens after a 64-token prompt, fp32 oracle port"}
+            n_tok = 8
+            base = make_cpu_baseline(cpu_state_dict(weights), PROMPT_LEN, threads)
+            v = base.tokens_per_s(n_tok)
+            out["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads, "kind": base.kind,
+                                   "sample": cpu_sample_text(base, n_tok, PROMPT_LEN)}
         emit(out)
     if use_dist:
         dist.destroy_process_group()
-
-
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch, from the ncu capture
-# summarised under profiles/ (None until a capture exists).
-TRAFFIC_BYTES_PER_LAUNCH = 1_537_192_800   # profiles/decode_megakernel_bf16_ctx520.md
-
-
-def cpu_state_dict(weights):
-    """Rebuilds a transformers-style state dict (CPU tensors) from the packed device weights."""
-    from luce_megakernel_b200.model import _DN_KEYS, _FA_KEYS
-    sd = {"model.embed_tokens.weight": weights["embed_weight"].cpu(), "model.norm.weight": weights["final_norm_weight"].cpu()}
-    for i, ld in enumerate(weights["layer_data"]):
-        keys = _FA_KEYS if ld["type"] == 1 else _DN_KEYS
-        for k, t in zip(keys, ld["ptrs"]):
-            sd[f"model.layers.{i}.{k}"] = t.cpu()
-    return sd
 
 
 if __name__ == "__main__":

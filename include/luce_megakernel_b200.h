@@ -130,6 +130,12 @@ int launch_quantize_nvfp4_out(const void *weight, int rows, int cols, int group_
 int launch_quantize_nvfp4_lm_out(const void *weight, int rows, int cols,
                                  void *packed_out, void *scales_out, cudaStream_t stream);
 const char *mk_quantize_error(void);
+/* Arithmetic of the two quantisers above.  1 (default): that of the reference's binary -- its extension is built
+ * with --use_fast_math (megakernel/setup.py:49-59), so amax / 6 and 1 / scale are an approximate divide and an
+ * approximate reciprocal; packed codes and scales then equal what the reference extension writes.  0: every divide and
+ * multiply correctly rounded (the arithmetic of a plain-C restatement); about one packed byte in 1700 differs from
+ * mode 1 on N(0, 0.02) weights, always by one code step at a threshold. */
+void mk_set_quantize_arithmetic(int reference_binary);
 
 /* NVFP4 weights dequantised in registers.  format 0 = layer-weight format (fp16 scales per 32),
  * format 1 = LM-head format (E4M3 scales per 16, tiled); value = e2m1(code) * scale
@@ -154,6 +160,28 @@ int mk_quantize_nvfp4_tensor_scale(const void *weight, int rows, int cols, void 
                                    float *tensor_scale_out, cudaStream_t stream);
 int mk_dequantize_nvfp4_tensor_scale(const void *packed, const void *scales, const float *tensor_scale, void *out,
                                      int out_is_bf16, int rows, int cols, cudaStream_t stream);
+
+/* Decode on the NVFP4 format with a per-tensor scale (e2m1 values in 16-element blocks, E4M3 block scales, one fp32
+ * scale per matrix; every linear layer and the LM head, produced by mk_quantize_nvfp4_tensor_scale): `steps` greedy
+ * steps in one launch, the running token read from and written back to token_buffer[0] (device), step s's token to
+ * output_tokens[s].  No counterpart in the reference, whose NVFP4 decode (megakernel/kernel_gb10_nvfp4.cu:2006-2257)
+ * reads 32-element groups with fp16 scales and no tensor scale; same kernel schedule as launch_decode_nvfp4.
+ * layer_weights: num_layers entries of 224 bytes {int type; int pad[3]; void *ptrs[26]}; a quantised matrix takes
+ * three slots (packed codes [rows][K/2]; block scales as plain rows [rows][K/16], see mk_nvfp4_scales_to_rows; device
+ * pointer to its fp32 tensor scale), everything else one bf16 slot:
+ *   DeltaNet : in_norm, qkv(3), z(3), w_beta, w_alpha, conv_w, A_log, dt_bias, norm_w, out(3), post_norm, gate(3),
+ *              up(3), down(3)
+ *   attention: in_norm, q(3), k(3), v(3), q_norm, k_norm, o(3), post_norm, gate(3), up(3), down(3)
+ * The kernel multiplies exact f16 products code x block scale on the tensor cores, accumulates in f32 and applies the
+ * tensor scale to each finished row product.
+ * mk_nvfp4_scales_to_rows converts block scales from the 128 x 4 tiles the quantisers write to plain rows. */
+int mk_decode_nvfp4_ts(
+    int *token_buffer, int *output_tokens, int steps,
+    const void *embed_weight, const void *layer_weights, const void *final_norm_weight,
+    const void *lm_head_packed, const void *lm_head_scales_rows, const float *lm_head_tensor_scale,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *hidden_buffer, void *g_normalized, int position, int max_seq_len, cudaStream_t stream);
+int mk_nvfp4_scales_to_rows(const void *tiled_scales, int rows, int cols, void *rows_out, cudaStream_t stream);
 
 /* Prefill of a prompt of seq_len tokens from position 0: fills the KV caches for positions
  * 0..seq_len-1, advances the DeltaNet and conv state from their current content (callers zero
@@ -188,6 +216,17 @@ int mk_prefill_bf16(
     void *final_normed, void *hidden_bf16_out,
     int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
 const char *mk_prefill_error(void);
+/* The prefill entry points and the batched decode step share one library workspace per device (about 45 KB per
+ * prompt token).  It only ever grows: a call that needs more tokens than it holds synchronises the device, frees
+ * every buffer and allocates larger ones.  Consequences for callers:
+ *   - growing is refused (MK_ERR_CUDA) while `stream` is being captured into a CUDA graph: call
+ *     mk_prefill_reserve(max_tokens) once, before capturing, with the longest prompt the graphs will see;
+ *   - a graph captured before a growth holds device pointers into the freed buffers and must be captured again:
+ *     mk_prefill_workspace_generation() changes whenever the workspace was reallocated;
+ *   - a prefill and a batched step on one device use the same buffers: keep them on one stream or serialise them. */
+int mk_prefill_reserve(int max_tokens);
+int mk_prefill_workspace_tokens(void);              /* prompt tokens the workspace holds at present */
+unsigned int mk_prefill_workspace_generation(void);
 
 /* Batched decode: `batch` (1..16) independent sequences advance by one token each and share every weight pass.
  * The reference has no batched op (all of megakernel/torch_bindings.cpp:569-675 are batch 1); these calls keep the
@@ -321,8 +360,34 @@ void mk_get_model_dims(int *num_layers, int *vocab);
 /* Status of the last device-side failure on the current device (0 = none) and a text for the
  * last error returned on this thread.  mk_clear_error() re-arms the library after a timeout. */
 int mk_device_status(void);
+/* The whole status word: bits 0-7 the code mk_device_status() returns, 8-11 the phase of the kernel's schedule in
+ * which the first wait gave up (0 DeltaNet in-proj, 1 recurrence, 2 out-proj, 3 attention qkv-proj, 4 attention, 5 o-proj,
+ * 6 gate/up, 7 down, 8 LM head), 12-22 the layer, 23 set when it was the weight-streaming warp, 24-31 the step of the launch. */
+unsigned int mk_device_status_detail(void);
 const char *mk_last_error_string(void);
 void mk_clear_error(void);
+
+/* mk_decode_many_bf16 / launch_decode_many_nvfp4 run all their steps in ONE persistent launch
+ *   (the argmax of a step reaches the next step's embedding gather through the library workspace); a positive
+ *   value cuts a call into launches of at most that many steps (1 = one launch per token, as the reference's
+ *   launch_decode_many_nvfp4 does, megakernel/kernel_gb10_nvfp4.cu:2192-2257).  For measurements; default 0. */
+void mk_set_decode_steps_per_launch(int steps);
+/* How a thread of the decode kernel waits for an activation another CTA has not published yet: 1 (default) keeps
+ * three loads of the word in flight, a third of an L2 round trip apart, so that the value is seen at most ~0.2 us after
+ * it lands; 0 issues one load at a time (seen up to a whole round trip late).  For measurements. */
+void mk_set_decode_poll_pipelining(int enable);
+
+/* Limits of the decode kernel's device-side waits.  The reference's grid barrier spins without a limit
+ * (megakernel/kernel.cu:128-137); here every wait is bounded and a launch that gives up drains, writes -1 as its
+ * token and leaves a status (ST codes: 1 = a poll of an exchanged activation ran out, 2 = a ring barrier, 3 =
+ * misaligned source) that the next call reports as MK_ERR_DEVICE_TIMEOUT until mk_clear_error().
+ * poll_cycles: SM clocks a poll may take; mbar_tries: attempts on a ring barrier; 0 restores the default
+ * (about 2 s each).
+ * mk_selftest_bounded_wait launches two small CTAs that run the kernel's poll on a word nobody writes, so that
+ * the wait runs out after the configured limit and the whole failure path (status word, error return, re-arm)
+ * can be exercised without a launch that hangs: set a short limit first (1e6 cycles is about 0.5 ms). */
+void mk_set_wait_limits(unsigned long long poll_cycles, unsigned int mbar_tries);
+int mk_selftest_bounded_wait(cudaStream_t stream);
 
 /* Optional per-phase timeline: `buf` is a device buffer of
  * query_max_safe_decode_blocks() * slots_per_cta uint64; thread 0 of every CTA appends the global
@@ -350,8 +415,11 @@ void mk_set_trace_buffer(unsigned long long *buf, int slots_per_cta);
  * Sharing: every call on a device uses the same array and finds the previous call's contents
  * there; the entry point clears the control words it needs at zero on `stream` before the
  * launch.  Two calls that overlap on the GPU (different streams) race on the array: serialise
- * them.  A device-side wait that runs out is not reported by this entry point (the status word
- * of launch_decode() is itself an allocation); the next call re-arms the array. */
+ * them.  Pointer alignment: 16 bytes for weights, caches, states and the vector scratch, as for launch_decode().
+ * Failure: if a bounded device-side wait runs out, the launch drains and writes -1 to *output_token_id; the
+ * cause stays in the array until the next call clears it and can be fetched, again without an allocation, with
+ * mk_decode_bf16_static_scratch_status(): it queues a 4-byte copy of that word (0 = normal completion) to
+ * status_out (device or pinned host memory) on `stream`. */
 #define MK_STATIC_SCRATCH_MAX_CTAS 256
 int mk_decode_bf16_static_scratch(
     int input_token_id, int *output_token_id,
@@ -365,6 +433,7 @@ int mk_decode_bf16_static_scratch(
     void *g_alpha_scratch, void *g_normalized,
     float *seen_token_mask, float repetition_penalty,
     int position, int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
+int mk_decode_bf16_static_scratch_status(unsigned int *status_out, cudaStream_t stream);
 const char *mk_decode_bf16_static_scratch_error(void);
 
 #ifdef __cplusplus

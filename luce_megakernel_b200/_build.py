@@ -46,7 +46,9 @@ def build_core(force=False, verbose=False):
     for cu in cus:
         obj = os.path.join(CSRC, os.path.basename(cu)[:-3] + ".o")
         if force or _newer(obj, deps):
-            out = _run([nvcc] + NVCC_FLAGS + (["-Xptxas", "-v"] if verbose else []) + ["-c", cu, "-o", obj])
+            # *_fastmath.cu restate reference code that the reference compiles with --use_fast_math
+            extra = ["--use_fast_math"] if cu.endswith("_fastmath.cu") else []
+            out = _run([nvcc] + NVCC_FLAGS + extra + (["-Xptxas", "-v"] if verbose else []) + ["-c", cu, "-o", obj])
             if verbose:
                 print(out)
         objs.append(obj)

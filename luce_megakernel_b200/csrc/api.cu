@@ -24,6 +24,10 @@ int g_num_layers = mk::MAX_LAYERS;
 int g_vocab = mk::DEFAULT_VOCAB;
 unsigned long long* g_trace = nullptr;
 int g_trace_slots = 0;
+unsigned long long g_poll_limit = mk::DEFAULT_POLL_LIMIT_CYCLES;
+uint32_t g_mbar_tries = mk::DEFAULT_MBAR_LIMIT_TRIES;
+int g_steps_per_launch = 0;     // 0 = a multi-step call is one launch
+int g_poll_pipelined = 1;
 thread_local char g_err[256] = "";
 
 int set_err(int code, const char* what, cudaError_t e = cudaSuccess) {
@@ -69,7 +73,9 @@ int check_device_status(DeviceState& d, cudaStream_t stream) {
     const uint32_t st = *reinterpret_cast<volatile uint32_t*>(d.host_status);
     if (st == 0) return MK_OK;
     snprintf(g_err, sizeof(g_err),
-             "a previous launch gave up on a bounded device-side wait (status %u); call mk_clear_error()", st);
+             "a previous launch gave up on a bounded device-side wait (status %u, %s warp, layer %u, phase %u, step %u); "
+             "call mk_clear_error()", st & 0xffu, (st & 0x800000u) ? "weight-streaming" : "consumer", (st >> 12) & 0x7ffu,
+             (st >> 8) & 0xfu, st >> 24);
     (void)stream;
     return MK_ERR_DEVICE_TIMEOUT;
 }
@@ -113,6 +119,8 @@ mk::DecodeParams make_params(const DecodeCall& a, DeviceState& d) {
     p.position = a.position; p.max_seq_len = a.max_seq_len;
     p.num_layers = g_num_layers; p.vocab = g_vocab;
     p.ws = d.ws; p.host_status = d.host_status_dev; p.trace = g_trace; p.trace_slots = g_trace_slots;
+    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries; p.poll_pipelined = g_poll_pipelined;
+    p.steps = 1;
     return p;
 }
 
@@ -180,11 +188,15 @@ int mk_decode_many_bf16(
     if ((rc = check_device_status(*d, stream))) return rc;
     mk::DecodeParams p = make_params(a, *d);
     const int grid = decode_grid(*d);
-    for (int s = 0; s < steps; ++s) {
+    mk::fill_rope(p);
+    // one launch runs all the steps (the token travels from the argmax of one step to the embedding of the next
+    // through the workspace); mk_set_decode_steps_per_launch() can cut it into shorter launches
+    const int per = (g_steps_per_launch > 0) ? g_steps_per_launch : steps;
+    for (int s = 0; s < steps; s += per) {
         p.token_ptr = token_buffer; p.token_val = 0;
-        p.out_token = output_tokens + s; p.token_feedback = token_buffer; p.out_tokens_slot = nullptr;
+        p.out_token = output_tokens + s; p.token_feedback = token_buffer;
         p.position = position + s;
-        mk::fill_rope(p);
+        p.steps = (steps - s < per) ? steps - s : per;
         cudaError_t e = mk::launch_decode_kernel(p, grid, stream);
         if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
     }
@@ -197,13 +209,14 @@ static int decode_nvfp4_common(const int* token_in, int* token_out, int* token_f
                                const void* layer_weights, const void* final_norm_weight, const void* lm_packed,
                                const void* lm_scales, void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
                                void* hidden_buffer, void* g_normalized, int position, int max_seq_len, int group_size,
-                               cudaStream_t stream) {
+                               int steps, cudaStream_t stream) {
     if (!token_in || !token_out || !embed_weight || !layer_weights || !final_norm_weight || !lm_packed || !lm_scales ||
         !fa_k_cache || !fa_v_cache || !dn_states || !conv_bufs || !hidden_buffer || !g_normalized)
         return set_err(MK_ERR_BAD_ARG, "null pointer argument");
     if (group_size != 32) return set_err(MK_ERR_BAD_ARG, "the NVFP4 decode kernel is built for group_size 32");
     if (g_vocab % 128) return set_err(MK_ERR_BAD_ARG, "the NVFP4 LM-head format needs a vocabulary divisible by 128");
     if (max_seq_len <= 0 || position < 0 || position >= max_seq_len) return set_err(MK_ERR_BAD_ARG, "position out of range");
+    if (steps < 1 || position + steps > max_seq_len) return set_err(MK_ERR_BAD_ARG, "position + steps exceeds max_seq_len");
     const void* al[] = {embed_weight, layer_weights, final_norm_weight, lm_packed, fa_k_cache, fa_v_cache, dn_states,
                         conv_bufs, hidden_buffer, g_normalized};
     for (const void* q : al)
@@ -222,6 +235,8 @@ static int decode_nvfp4_common(const int* token_in, int* token_out, int* token_f
     p.token_ptr = token_in; p.token_val = 0; p.out_token = token_out; p.token_feedback = token_feedback;
     p.position = position; p.max_seq_len = max_seq_len; p.num_layers = g_num_layers; p.vocab = g_vocab;
     p.ws = d->ws; p.host_status = d->host_status_dev; p.trace = nullptr; p.trace_slots = 0;
+    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries; p.poll_pipelined = g_poll_pipelined;
+    p.steps = steps;
     mk::fill_rope(p);
     cudaError_t e = mk::launch_decode_kernel(p, decode_grid(*d), stream);
     if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
@@ -247,7 +262,7 @@ int launch_decode_nvfp4(
     (void)block_max_idxs; (void)lm_sync_counter;
     return decode_nvfp4_common(input_token_ptr, output_token_id, nullptr, embed_weight, layer_weights, final_norm_weight,
                                lm_head_weight_packed, lm_head_scales, fa_k_cache, fa_v_cache, dn_states, conv_bufs,
-                               hidden_buffer, g_normalized, position, max_seq_len, group_size, stream);
+                               hidden_buffer, g_normalized, position, max_seq_len, group_size, 1, stream);
 }
 
 int launch_decode_many_nvfp4(
@@ -270,14 +285,53 @@ int launch_decode_many_nvfp4(
     if (!output_tokens) return set_err(MK_ERR_BAD_ARG, "null output_tokens");
     if (steps < 0) return set_err(MK_ERR_BAD_ARG, "steps must be non-negative");
     if (position + steps > max_seq_len) return set_err(MK_ERR_BAD_ARG, "position + steps exceeds max_seq_len");
-    for (int s = 0; s < steps; ++s) {
-        // the kernel writes the new token to output_tokens[s] and back into token_buffer
-        const int rc = decode_nvfp4_common(token_buffer, output_tokens + s, token_buffer, embed_weight, layer_weights,
-                                           final_norm_weight, lm_head_weight_packed, lm_head_scales, fa_k_cache, fa_v_cache,
-                                           dn_states, conv_bufs, hidden_buffer, g_normalized, position + s, max_seq_len,
-                                           group_size, stream);
-        if (rc) return rc;
-    }
+    if (steps == 0) return MK_OK;
+    // one launch: step s writes output_tokens[s] and the running token back into token_buffer
+    return decode_nvfp4_common(token_buffer, output_tokens, token_buffer, embed_weight, layer_weights,
+                               final_norm_weight, lm_head_weight_packed, lm_head_scales, fa_k_cache, fa_v_cache,
+                               dn_states, conv_bufs, hidden_buffer, g_normalized, position, max_seq_len,
+                               group_size, steps, stream);
+}
+
+// Decode on the NVFP4 format with a per-tensor scale (16-element blocks, E4M3 block scales in plain rows, fp32 scale
+// per matrix): `steps` greedy steps in one launch, token in / out through device memory.
+int mk_decode_nvfp4_ts(
+    int* token_buffer, int* output_tokens, int steps,
+    const void* embed_weight, const void* layer_weights, const void* final_norm_weight,
+    const void* lm_head_packed, const void* lm_head_scales_rows, const float* lm_head_tensor_scale,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden_buffer, void* g_normalized, int position, int max_seq_len, cudaStream_t stream) {
+    if (!token_buffer || !output_tokens || !embed_weight || !layer_weights || !final_norm_weight || !lm_head_packed ||
+        !lm_head_scales_rows || !lm_head_tensor_scale || !fa_k_cache || !fa_v_cache || !dn_states || !conv_bufs ||
+        !hidden_buffer || !g_normalized)
+        return set_err(MK_ERR_BAD_ARG, "null pointer argument");
+    if (steps < 0) return set_err(MK_ERR_BAD_ARG, "steps must be non-negative");
+    if (steps == 0) return MK_OK;
+    if (max_seq_len <= 0 || position < 0 || position + steps > max_seq_len)
+        return set_err(MK_ERR_BAD_ARG, "position + steps exceeds max_seq_len");
+    const void* al[] = {embed_weight, layer_weights, final_norm_weight, lm_head_packed, lm_head_scales_rows, fa_k_cache,
+                        fa_v_cache, dn_states, conv_bufs, hidden_buffer, g_normalized};
+    for (const void* q : al)
+        if (misaligned16(q)) return set_err(MK_ERR_BAD_ARG, "pointer argument is not 16-byte aligned");
+    DeviceState* d = nullptr;
+    int rc = device_state(&d);
+    if (rc) return rc;
+    if ((rc = check_device_status(*d, stream))) return rc;
+    mk::DecodeParams p;
+    memset(&p, 0, sizeof(p));
+    p.embed = embed_weight; p.layers = layer_weights; p.final_norm = final_norm_weight;
+    p.lm_head = lm_head_packed; p.lm_scales = lm_head_scales_rows; p.lm_tensor_scale = lm_head_tensor_scale; p.wfmt = 2;
+    p.k_cache = fa_k_cache; p.v_cache = fa_v_cache; p.dn_states = (float*)dn_states; p.conv_bufs = (float*)conv_bufs;
+    p.hidden = hidden_buffer; p.normalized = (float*)g_normalized;
+    p.seen_mask = nullptr; p.rep_penalty = 1.0f;
+    p.token_ptr = token_buffer; p.token_val = 0; p.out_token = output_tokens; p.token_feedback = token_buffer;
+    p.position = position; p.max_seq_len = max_seq_len; p.num_layers = g_num_layers; p.vocab = g_vocab;
+    p.ws = d->ws; p.host_status = d->host_status_dev; p.trace = nullptr; p.trace_slots = 0;
+    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries; p.poll_pipelined = g_poll_pipelined;
+    p.steps = steps;
+    mk::fill_rope(p);
+    cudaError_t e = mk::launch_decode_kernel(p, decode_grid(*d), stream);
+    if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
     return MK_OK;
 }
 
@@ -305,7 +359,13 @@ void mk_get_model_dims(int* num_layers, int* vocab) {
 int mk_device_status(void) {
     DeviceState* d = nullptr;
     if (device_state(&d)) return -1;
-    return (int)*reinterpret_cast<volatile uint32_t*>(d->host_status);
+    return (int)(*reinterpret_cast<volatile uint32_t*>(d->host_status) & 0xffu);
+}
+
+unsigned int mk_device_status_detail(void) {
+    DeviceState* d = nullptr;
+    if (device_state(&d)) return 0xffffffffu;
+    return *reinterpret_cast<volatile uint32_t*>(d->host_status);
 }
 
 const char* mk_last_error_string(void) { return g_err; }
@@ -328,9 +388,30 @@ int mk_gemm_bf16_tn(const void* A, const void* W, void* C, const void* residual,
         if (e0 != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaMalloc(gemm status)", e0);
         cudaMemset(err_flag, 0, sizeof(int));
     }
-    cudaError_t e = mk::gemm_bf16_tn(A, W, C, residual, M, N, K, K, N, err_flag, stream);
+    cudaError_t e = mk::gemm_bf16_tn(A, W, C, residual, M, N, K, K, N, err_flag, nullptr, 0, stream);
     if (e == cudaErrorInvalidValue) return set_err(MK_ERR_BAD_ARG, "gemm shape or alignment not supported (N % 128, K % 64, 16-byte pointers)");
     if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "gemm launch", e);
+    return MK_OK;
+}
+
+void mk_set_decode_steps_per_launch(int steps) { g_steps_per_launch = steps > 0 ? steps : 0; }
+void mk_set_decode_poll_pipelining(int enable) { g_poll_pipelined = enable ? 1 : 0; }
+
+void mk_set_wait_limits(unsigned long long poll_cycles, unsigned int mbar_tries) {
+    g_poll_limit = poll_cycles ? poll_cycles : mk::DEFAULT_POLL_LIMIT_CYCLES;
+    g_mbar_tries = mbar_tries ? mbar_tries : mk::DEFAULT_MBAR_LIMIT_TRIES;
+}
+
+int mk_selftest_bounded_wait(cudaStream_t stream) {
+    DeviceState* d = nullptr;
+    int rc = device_state(&d);
+    if (rc) return rc;
+    mk::DecodeParams p;
+    memset(&p, 0, sizeof(p));
+    p.ws = d->ws; p.host_status = d->host_status_dev;
+    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries; p.poll_pipelined = g_poll_pipelined;
+    cudaError_t e = mk::launch_wait_selftest(p, stream);
+    if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "wait self-test launch", e);
     return MK_OK;
 }
 

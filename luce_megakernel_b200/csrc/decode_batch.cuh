@@ -836,7 +836,7 @@ int decode_batch_core(const int* tokens, const int* positions, int* output_token
                       void* hidden_bf16_out, int max_seq_len, int vocab, int dev, cudaStream_t stream) {
     PrefillWs& w = g_pws[dev];
     BatchWs& bw = g_bws[dev];
-    PF_CHECK(ensure_ws(w, B < 64 ? 64 : B), "step workspace");
+    PF_CHECK(ensure_ws(w, B < 64 ? 64 : B, stream, true), "step workspace (grow it with mk_prefill_reserve() before capturing a graph)");
     PF_CHECK(ensure_batch_ws(bw), "batch workspace");
     static bool attr[64] = {false};
     if (!attr[dev]) {

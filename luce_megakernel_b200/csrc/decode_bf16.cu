@@ -39,25 +39,26 @@ namespace {
 constexpr int NCW = 16;                    // consumer warps
 constexpr int NCT = NCW * 32;              // consumer threads
 constexpr int NTHREADS = NCT + 32;         // + producer warp
-constexpr int NSTAGE = 6;
-constexpr int STAGE_BYTES = 32768;
+constexpr int MAX_STAGES = 6;               // ring stages: 6 x 32 KB (bf16, NVFP4 layer format) or 5 x 36 KB (tensor-scale NVFP4)
+constexpr int RING_BYTES = 196608;
 constexpr int XK = 224;                    // largest K-slice of a warp (elements)
 constexpr int XSW = 3 * XK / 2;            // 32-bit words of staging per warp: three bf16 planes of XK elements
 
 constexpr int OFF_RING = 0;
-constexpr int OFF_SCRATCH = NSTAGE * STAGE_BYTES;          // activation staging (16 x 224 floats) / attention merge
+constexpr int OFF_SCRATCH = RING_BYTES;          // activation staging (16 x 224 floats) / attention merge
 constexpr int SCRATCH_BYTES = 21504;           // 16 x 1344 B of staging; attention uses 16640 B of merge slots + 4096 B of q
 constexpr int OFF_PART = OFF_SCRATCH + SCRATCH_BYTES;      // 2 x (4 chunks x 16 warps x 16 rows) partial sums
 constexpr int PART_HALF = 4 * NCW * 16;                    // floats; phases alternate between the halves
 constexpr int PART_BYTES = 2 * PART_HALF * 4;
 constexpr int OFF_RED = OFF_PART + PART_BYTES;             // 32 floats
 constexpr int OFF_MISC = OFF_RED + 128;                    // 8 ints
-constexpr int OFF_BAR = OFF_MISC + 32;                     // full[NSTAGE], empty[NSTAGE]
-constexpr int OFF_LAYERS = OFF_BAR + 2 * NSTAGE * 8;       // copy of the layer pointer table
-constexpr int SMEM_BYTES = OFF_LAYERS + MAX_LAYERS * (int)sizeof(LayerWeightsNVFP4);
+constexpr int OFF_BAR = OFF_MISC + 32;                     // full[stages], empty[stages]
+constexpr int OFF_ROPE = OFF_BAR + 2 * MAX_STAGES * 8;         // cos[32] | sin[32] of the step's position
+constexpr int OFF_LAYERS = OFF_ROPE + 256;                 // copy of the layer pointer table
+constexpr int SMEM_BYTES = OFF_LAYERS + MAX_LAYERS * (int)sizeof(LayerWeightsNVFP4TS);
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
-enum { MISC_ABORT = 0, MISC_LAST = 1 };
+enum { MISC_ABORT = 0, MISC_LAST = 1, MISC_TOKEN = 2, MISC_DETAIL = 3 };
 
 // pause between failed polls of a flagged word: keeps the waiting threads of 148 CTAs from
 // saturating the L2 slices that hold the words (and from delaying the stores they wait for)
@@ -90,6 +91,16 @@ namespace {
 }  // namespace
 }  // namespace nvfp4
 
+namespace nvfp4ts {
+namespace {
+#define MK_TRACE 0
+#define MK_WFMT 2
+#include "decode_body.cuh"
+#undef MK_WFMT
+#undef MK_TRACE
+}  // namespace
+}  // namespace nvfp4ts
+
 namespace traced {
 namespace {
 #define MK_TRACE 1
@@ -113,15 +124,10 @@ int decode_max_grid() {
     return g > MAX_GRID ? MAX_GRID : g;
 }
 
-// RoPE angles of one position: inv_freq_i = theta^(-2i/64) in double, angle in f32 like the
-// reference (megakernel/kernel.cu:468-470), sine and cosine evaluated in double.
+// RoPE frequencies: inv_freq_i = theta^(-2i/64) evaluated in double; the kernel forms angle = position * inv_freq
+// in f32 like the reference (megakernel/kernel.cu:468-470) and takes an accurate f32 sine and cosine of it.
 void fill_rope(DecodeParams& p) {
-    for (int i = 0; i < FA_ROT / 2; ++i) {
-        const float inv_freq = (float)(1.0 / pow(ROPE_THETA, (2.0 * i) / FA_ROT));
-        const float ang = (float)p.position * inv_freq;
-        p.rope_cos[i] = (float)cos((double)ang);
-        p.rope_sin[i] = (float)sin((double)ang);
-    }
+    for (int i = 0; i < FA_ROT / 2; ++i) p.rope_inv_freq[i] = (float)(1.0 / pow(ROPE_THETA, (2.0 * i) / FA_ROT));
 }
 
 cudaError_t launch_decode_kernel(const DecodeParams& p, int grid, cudaStream_t stream) {
@@ -136,14 +142,22 @@ cudaError_t launch_decode_kernel(const DecodeParams& p, int grid, cudaStream_t s
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(nvfp4::decode_megakernel_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(nvfp4ts::decode_megakernel_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
         attr_done[dev] = true;
     }
     if (grid < MIN_GRID || grid > MAX_GRID) return cudaErrorInvalidConfiguration;
     void* args[] = {(void*)&p};
-    const void* fn = p.wfmt == 1 ? (const void*)nvfp4::decode_megakernel_bf16
+    const void* fn = p.wfmt == 2 ? (const void*)nvfp4ts::decode_megakernel_bf16
+                   : p.wfmt == 1 ? (const void*)nvfp4::decode_megakernel_bf16
                    : p.trace   ? (const void*)traced::decode_megakernel_bf16
                                : (const void*)plain::decode_megakernel_bf16;
     return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(NTHREADS), args, SMEM_BYTES, stream);
+}
+
+cudaError_t launch_wait_selftest(const DecodeParams& p, cudaStream_t stream) {
+    plain::wait_selftest_kernel<<<2, 32, 0, stream>>>(p);
+    return cudaGetLastError();
 }
 
 }  // namespace mk

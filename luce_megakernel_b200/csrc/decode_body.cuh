@@ -10,12 +10,16 @@
 //            computed outside the ring; the LM head uses the 16-block E4M3 format.
 #if MK_WFMT == 0
 typedef LayerWeights LW;
+constexpr int NSTAGE = 6;                               // ring stages
+constexpr int STAGE_BYTES = 32768;
 constexpr int IN_ROWS_DN = DN_IN_ROWS;                  // qkv | z | beta | alpha
 constexpr int LM_RPC = 16;                              // LM-head rows per ring chunk
 __device__ __forceinline__ constexpr int row_bytes(int K) { return K * 2; }
 __device__ __forceinline__ constexpr int row_stride(int K) { return K * 2; }
-#else
+#elif MK_WFMT == 1
 typedef LayerWeightsNVFP4 LW;
+constexpr int NSTAGE = 6;
+constexpr int STAGE_BYTES = 32768;
 // slots of the NVFP4 table: a quantised matrix takes (data, scales) (reference: megakernel/model_nvfp4.py:274-311)
 enum { DN_IN_NORM = 0, DN_W_QKV = 1, DN_W_Z = 3, DN_W_B = 5, DN_W_A = 6, DN_CONV_W = 7, DN_A_LOG = 8, DN_DT_BIAS = 9,
        DN_NORM_W = 10, DN_W_OUT = 11, DN_POST_NORM = 13, DN_W_GATE = 14, DN_W_UP = 16, DN_W_DOWN = 18 };
@@ -26,7 +30,27 @@ constexpr int LM_RPC = 64;
 __device__ __forceinline__ constexpr int row_bytes(int K) { return K / 2; }
 __device__ __forceinline__ constexpr int row_stride(int K) { return K / 2 + 16; }
 __device__ __forceinline__ constexpr int scale_bytes(int K) { return K / 16; }
+#else
+// MK_WFMT 2: e2m1 values in 16-element blocks, E4M3 block scales stored row-major ([rows][K/16] bytes), an fp32 scale
+// per matrix.  A ring chunk is R consecutive packed rows (R * K/2 bytes, no padding) followed by the R rows of
+// block scales (R * K/16 bytes): two bulk copies per matrix the chunk touches.  R = 64 for K = 1024, 32 for
+// K = 2048, 16 for K = 3584, so every phase of a layer is ONE chunk per CTA.  The table entry has three slots per
+// quantised matrix: packed data, row-major scales, pointer to the tensor scale.  (The rows sit in the stage in eight
+// groups, 16 bytes apart more than their size: see chunk_slot_src.)
+typedef LayerWeightsNVFP4TS LW;
+constexpr int NSTAGE = 5;
+constexpr int STAGE_BYTES = 37120;                      // 64 rows of K = 1024: 8 x (4 KB + 16) of codes + 4 KB of scales
+enum { DN_IN_NORM = 0, DN_W_QKV = 1, DN_W_Z = 4, DN_W_B = 7, DN_W_A = 8, DN_CONV_W = 9, DN_A_LOG = 10, DN_DT_BIAS = 11,
+       DN_NORM_W = 12, DN_W_OUT = 13, DN_POST_NORM = 16, DN_W_GATE = 17, DN_W_UP = 20, DN_W_DOWN = 23 };
+enum { FA_IN_NORM = 0, FA_W_Q = 1, FA_W_K = 4, FA_W_V = 7, FA_Q_NORM = 10, FA_K_NORM = 11, FA_W_O = 12, FA_POST_NORM = 15,
+       FA_W_GATE = 16, FA_W_UP = 19, FA_W_DOWN = 22 };
+constexpr int IN_ROWS_DN = DN_CONV_CH + DN_V;           // qkv | z (beta / alpha stay bf16, outside the ring)
+constexpr int LM_RPC = 64;
+__device__ __forceinline__ constexpr int row_bytes(int K) { return K / 2; }
+__device__ __forceinline__ constexpr int scale_bytes(int K) { return K / 16; }
+__device__ __forceinline__ constexpr int rows_per_chunk(int K) { return K == 1024 ? 64 : (K == 2048 ? 32 : 16); }
 #endif
+static_assert(NSTAGE * STAGE_BYTES <= RING_BYTES && NSTAGE <= MAX_STAGES, "ring does not fit its region");
 
 struct Geo {
     int r0, r1;       // rows (or outputs for gate/up, first unit for the recurrence)
@@ -58,12 +82,21 @@ __device__ __forceinline__ Geo phase_geo(int type, int cta, int G, int vocab, in
     g.r0 = g.r1 = 0;
     g.nchunks = 0;
     switch (type) {
+#if MK_WFMT == 2
+        case T_DN_IN:  split_rows(IN_ROWS_DN, G, cta, g.r0, g.r1);  g.nchunks = (g.r1 - g.r0 + 63) >> 6; break;
+        case T_FA_IN:  split_rows(FA_QKV_ROWS, G, cta, g.r0, g.r1); g.nchunks = (g.r1 - g.r0 + 63) >> 6; break;
+        case T_DN_OUT:
+        case T_FA_OUT: split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = (g.r1 - g.r0 + 31) >> 5; break;
+        case T_GATEUP: split_rows(INTER, G, cta, g.r0, g.r1);       g.nchunks = (g.r1 - g.r0 + 31) >> 5; break;
+        case T_DOWN:   split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = (g.r1 - g.r0 + 15) >> 4; break;
+#else
         case T_DN_IN:  split_rows(IN_ROWS_DN, G, cta, g.r0, g.r1);  g.nchunks = (g.r1 - g.r0 + 15) >> 4; break;
         case T_FA_IN:  split_rows(FA_QKV_ROWS, G, cta, g.r0, g.r1); g.nchunks = (g.r1 - g.r0 + 15) >> 4; break;
         case T_DN_OUT:
         case T_FA_OUT: split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = (g.r1 - g.r0 + 7) >> 3; break;
         case T_GATEUP: split_rows(INTER, G, cta, g.r0, g.r1);       g.nchunks = (g.r1 - g.r0 + 7) >> 3; break;
         case T_DOWN:   split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = (g.r1 - g.r0 + 3) >> 2; break;
+#endif
         case T_LM:     split_rows(vocab, G, cta, g.r0, g.r1);       g.nchunks = (g.r1 - g.r0 + LM_RPC - 1) / LM_RPC; break;
         case T_DN_REC: g.r0 = cta; g.nchunks = (cta < 128) ? (128 - cta + G - 1) / G : 0; break;
         case T_FA_ATT: {
@@ -85,11 +118,11 @@ __device__ __forceinline__ Geo phase_geo(int type, int cta, int G, int vocab, in
 // ring offset.  bf16: lane = row slot.  NVFP4: lanes 0-15 = packed rows, lanes 16-31 = their scales.
 __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const DecodeParams& P,
                                                    const Geo& g, int q, int lane, int G, int dn_idx,
-                                                   const char*& src, uint32_t& dst_off, int cta_of_geo) {
+                                                   const char*& src, uint32_t& dst_off, int cta_of_geo, int pos) {
     if (type == T_FA_ATT) {
         // dn_idx carries the attention layer index here; chunk q = tile * 4 + {K lo, K hi, V lo, V hi}
         const int u = cta_of_geo;
-        const int NC = att_num_chunks(P.position + 1);
+        const int NC = att_num_chunks(pos + 1);
         const int kvh = u / NC, part = q & 3;
         const int p = g.r0 + (q >> 2) * 64 + (part & 1) * 32 + lane;
         if (p >= g.r1) return 0;
@@ -98,6 +131,87 @@ __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const
         dst_off = lane * ATT_ROW_STRIDE;
         return FA_HEAD_DIM * 2;
     }
+#if MK_WFMT == 2
+    if (type == T_DN_REC) {
+        if (lane != 0) return 0;
+        const int u = g.r0 + q * G;
+        const int h = u >> 3, sl = u & 7;
+        src = (const char*)(P.dn_states + ((size_t)(dn_idx * DN_HEADS + h) * DN_VAL + sl * 16) * DN_KEY);
+        dst_off = 0;
+        return 16 * DN_KEY * 4;
+    }
+    {
+        // Stage layout: the chunk's R rows in 8 groups of GR = R/8 consecutive rows, group k at offset
+        // k * (GR * K/2 + 16) -- the 16-byte step puts the 8 rows a quarter-warp reads together (one per group) on
+        // different banks -- then the R rows of block scales, unpadded.
+        // lanes 0-15: packed rows of group k = lane/2; part lane&1 = the rows of the group that lie in the first /
+        // second matrix the group touches (a group straddles at most one matrix boundary).
+        // lanes 16-18: block scales of the chunk's rows in matrix segment lane-16.
+        // matrix segments of the phase's concatenated row space: [0, h0) [h0, h1) [h1, h2), table slots i0 i1 i2
+        int K = HIDDEN, nseg = 1, h0 = 0, h1 = 0, h2 = 0, i0 = -1, i1 = -1, i2 = -1;
+        const bool dn = (lw.layer_type == 0);
+        bool gateup = false;
+        switch (type) {
+            case T_DN_IN: nseg = 2; i0 = DN_W_QKV; h0 = DN_CONV_CH; i1 = DN_W_Z; h1 = DN_CONV_CH + DN_V; break;
+            case T_FA_IN: nseg = 3; i0 = FA_W_Q; h0 = FA_QPROJ; i1 = FA_W_K; h1 = FA_QPROJ + FA_KV_SIZE; i2 = FA_W_V; h2 = FA_QKV_ROWS; break;
+            case T_DN_OUT: i0 = DN_W_OUT; K = 2048; h0 = HIDDEN; break;
+            case T_FA_OUT: i0 = FA_W_O; K = 2048; h0 = HIDDEN; break;
+            case T_GATEUP: gateup = true; i0 = dn ? (int)DN_W_GATE : (int)FA_W_GATE; i1 = dn ? (int)DN_W_UP : (int)FA_W_UP; break;
+            case T_DOWN: i0 = dn ? (int)DN_W_DOWN : (int)FA_W_DOWN; K = INTER; h0 = HIDDEN; break;
+            case T_LM: h0 = P.vocab; break;
+            default: return 0;
+        }
+        const int R = rows_per_chunk(K), GR = R / 8;
+        const uint32_t gstride = (uint32_t)GR * row_bytes(K) + 16u, sc_off = 8u * gstride;
+        auto seg_lo = [&](int sgi) { return sgi == 0 ? 0 : (sgi == 1 ? h0 : h1); };
+        auto seg_hi = [&](int sgi) { return sgi == 0 ? h0 : (sgi == 1 ? h1 : h2); };
+        auto mat = [&](int sgi, int kind) -> const char* {
+            if (type == T_LM) return (const char*)(kind ? P.lm_scales : P.lm_head);
+            const int ix = sgi == 0 ? i0 : (sgi == 1 ? i1 : i2);
+            return (const char*)lw.ptrs[ix + kind];
+        };
+        if (gateup) {
+            // outputs [oa, ob) of this chunk: gate rows at stage rows 0.., up rows at stage rows 32..
+            const int oa = g.r0 + q * 32, ob = min(g.r1, oa + 32);
+            if (lane < 16) {
+                if (lane & 1) return 0;
+                const int k = lane >> 1, m = k >> 2;                 // groups 0-3: gate, 4-7: up
+                const int lo = oa + (k & 3) * 8, hi = min(ob, lo + 8);
+                if (hi <= lo) return 0;
+                src = mat(m, 0) + (size_t)lo * row_bytes(K);
+                dst_off = (uint32_t)k * gstride;
+                return (uint32_t)(hi - lo) * row_bytes(K);
+            }
+            const int m = lane - 16;
+            if (m >= 2 || ob <= oa) return 0;
+            src = mat(m, 1) + (size_t)oa * scale_bytes(K);
+            dst_off = sc_off + (uint32_t)(m * 32) * scale_bytes(K);
+            return (uint32_t)(ob - oa) * scale_bytes(K);
+        }
+        const int ra = g.r0 + q * R, rb = min(g.r1, ra + R);
+        if (lane < 16) {
+            const int k = lane >> 1, part = lane & 1;
+            const int lo = ra + k * GR, hi = min(rb, lo + GR);
+            if (hi <= lo) return 0;
+            int s0 = 0;                                               // segment of the group's first row
+            while (s0 + 1 < nseg && lo >= seg_hi(s0)) ++s0;
+            const int sg = s0 + part;
+            if (sg >= nseg) return 0;
+            const int a = max(lo, seg_lo(sg)), b = min(hi, seg_hi(sg));
+            if (b <= a) return 0;
+            src = mat(sg, 0) + (size_t)(a - seg_lo(sg)) * row_bytes(K);
+            dst_off = (uint32_t)k * gstride + (uint32_t)(a - lo) * row_bytes(K);
+            return (uint32_t)(b - a) * row_bytes(K);
+        }
+        const int sg = lane - 16;
+        if (sg >= nseg) return 0;
+        const int a = max(ra, seg_lo(sg)), b = min(rb, seg_hi(sg));
+        if (b <= a) return 0;
+        src = mat(sg, 1) + (size_t)(a - seg_lo(sg)) * scale_bytes(K);
+        dst_off = sc_off + (uint32_t)(a - ra) * scale_bytes(K);
+        return (uint32_t)(b - a) * scale_bytes(K);
+    }
+#else
 #if MK_WFMT == 0
     const int slot = lane, kind = 0;
 #else
@@ -149,7 +263,7 @@ __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const
             src = (const char*)P.lm_head + (size_t)r * (HIDDEN * 2); dst_off = slot * (HIDDEN * 2);
             return HIDDEN * 2;
 #else
-            // packed LM-head rows are read one row per warp step: no padding, one copy per chunk
+            // (MK_WFMT 1) packed LM-head rows are read one row per warp step: no padding, one copy per chunk
             if (lane != 0) return 0;
             const int r = g.r0 + q * LM_RPC;
             const int n = min(LM_RPC, g.r1 - r);
@@ -182,6 +296,7 @@ __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const
     dst_off = rpc * row_stride(K) + slot * scale_bytes(K);
     return scale_bytes(K);
 #endif
+#endif   // MK_WFMT == 2
 }
 
 struct Ctx {
@@ -195,14 +310,19 @@ struct Ctx {
     uint32_t full0, empty0, ring0;
     int tid, warp, lane, cta, G;
     uint32_t it;          // ring chunk counter (producer and consumers advance it identically)
-    uint32_t seq;         // launches completed before this one
+    uint32_t seq;         // decode steps completed on this workspace before the current one
     uint32_t trace_slot;
+    uint32_t where;       // (layer << 4) | phase of the schedule this thread is in; bit 15: producer warp (diagnostics)
+    int pos;              // position of the token being decoded in this step
+    int step;             // index of the step inside this launch
+    const float* rope;    // shared memory: cos[32] | sin[32] of pos * inv_freq_i, recomputed every step
 };
 
 // A bounded wait ran out (or another CTA reported one): from here on every wait of this CTA
 // returns at once and the launch drains; the status reaches the host when the kernel ends.
 // Kept tiny and inline: a call here would cost a register save/restore at every wait site.
 __device__ __forceinline__ void fail(const DecodeParams& P, Ctx& c, uint32_t code) {
+    if (c.misc[MISC_ABORT] == 0) c.misc[MISC_DETAIL] = (int)(c.where | ((uint32_t)c.step << 16));
     c.misc[MISC_ABORT] = (int)code;
     P.ws->abort_flag = 1u;
 }
@@ -219,7 +339,7 @@ __device__ __forceinline__ void trace_point(const DecodeParams& P, Ctx& c) {
 __device__ __forceinline__ void wait_full(const DecodeParams& P, Ctx& c, uint32_t stage, uint32_t parity) {
     if (mbar_try_wait(c.full0 + stage * 8, parity)) return;
     if (c.misc[MISC_ABORT]) return;
-    if (!mbar_wait(c.full0 + stage * 8, parity)) fail(P, c, ST_MBAR_TIMEOUT);
+    if (!mbar_wait(c.full0 + stage * 8, parity, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
 }
 
 __device__ __forceinline__ void release_stage(Ctx& c, uint32_t stage) {
@@ -244,30 +364,101 @@ __device__ __forceinline__ void ld_word2(const unsigned long long* p, unsigned l
     asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-// Slow path of a poll (every 1024 failed tries): bounded to about 2 s of SM clock, gives up at
-// once if another CTA gave up.
+// Slow path of a poll: bounded by P.poll_limit_cycles (about 2 s of SM clock by default), gives up at once if
+// another CTA gave up.
 __device__ __forceinline__ bool poll_give_up(const DecodeParams& P, Ctx& c, uint64_t& t0) {
     if (c.misc[MISC_ABORT]) return true;
     const uint64_t now = (uint64_t)clock64();
     if (t0 == 0) t0 = now;
-    if (now - t0 > 4000000000ull || *((volatile uint32_t*)&P.ws->abort_flag) != 0u) {
+    if (now - t0 > P.poll_limit_cycles || *((volatile uint32_t*)&P.ws->abort_flag) != 0u) {
         fail(P, c, ST_GRID_TIMEOUT);
         return true;
     }
     return false;
 }
 
+// A poll that failed once costs a full L2 round trip (~0.7 us) before the next look at the word; with the loads issued
+// one after the other a value that lands just after a look is seen a whole round trip late.  The waits below keep
+// several loads in flight, issued a fraction of a round trip apart, and re-issue each one as it returns: the word is
+// sampled every ~0.2 us at two or three times the (small) polling traffic.  Out of line: the waits are inlined in
+// dozens of places and this part runs only while the thread has nothing else to do.  P.poll_pipelined = 0 selects
+// the plain loop (one load at a time).  The stagger is a spin on the SM clock: __nanosleep() overshoots by a
+// multiple of what is asked for at this scale.
+constexpr unsigned POLL_STAGGER_CLK = 400;
+__device__ __forceinline__ void spin_clocks(unsigned n) {
+    const unsigned t0 = (unsigned)clock();
+    while ((unsigned)clock() - t0 < n) {}
+}
+__device__ __forceinline__ bool wait_give_up(volatile int* misc, DecodeWorkspace* ws, unsigned long long limit, uint32_t where,
+                                             uint64_t& t0) {
+    if (misc[MISC_ABORT]) return true;
+    const uint64_t now = (uint64_t)clock64();
+    if (t0 == 0) t0 = now;
+    if (now - t0 > limit || *((volatile uint32_t*)&ws->abort_flag) != 0u) {
+        if (misc[MISC_ABORT] == 0) misc[MISC_DETAIL] = (int)where;
+        misc[MISC_ABORT] = (int)ST_GRID_TIMEOUT;
+        ws->abort_flag = 1u;
+        return true;
+    }
+    return false;
+}
+__device__ __noinline__ unsigned long long poll1_wait(const unsigned long long* p, uint32_t epoch, volatile int* misc,
+                                                      DecodeWorkspace* ws, unsigned long long limit, uint32_t where, int pipelined) {
+    uint64_t t0 = 0;
+    uint32_t n = 0;
+    if (!pipelined) {
+        while (true) {
+            const unsigned long long w = ld_word(p);
+            if ((uint32_t)(w >> 32) == epoch) return w;
+            if ((++n & 255u) == 0 && wait_give_up(misc, ws, limit, where, t0)) return w;
+        }
+    }
+    unsigned long long w0 = ld_word(p);
+    spin_clocks(POLL_STAGGER_CLK);
+    unsigned long long w1 = ld_word(p);
+    spin_clocks(POLL_STAGGER_CLK);
+    unsigned long long w2 = ld_word(p);
+    while (true) {
+        if ((uint32_t)(w0 >> 32) == epoch) return w0;
+        w0 = ld_word(p);
+        if ((uint32_t)(w1 >> 32) == epoch) return w1;
+        w1 = ld_word(p);
+        if ((uint32_t)(w2 >> 32) == epoch) return w2;
+        w2 = ld_word(p);
+        if ((++n & 127u) == 0 && wait_give_up(misc, ws, limit, where, t0)) return w0;
+    }
+}
+__device__ __noinline__ ulonglong2 poll2_wait(const unsigned long long* p, uint32_t epoch, volatile int* misc,
+                                              DecodeWorkspace* ws, unsigned long long limit, uint32_t where, int pipelined) {
+    uint64_t t0 = 0;
+    uint32_t n = 0;
+    unsigned long long a0, b0, a1, b1, a2, b2;
+    if (!pipelined) {
+        while (true) {
+            ld_word2(p, a0, b0);
+            if ((uint32_t)(a0 >> 32) == epoch && (uint32_t)(b0 >> 32) == epoch) return make_ulonglong2(a0, b0);
+            if ((++n & 255u) == 0 && wait_give_up(misc, ws, limit, where, t0)) return make_ulonglong2(a0, b0);
+        }
+    }
+    ld_word2(p, a0, b0);
+    spin_clocks(POLL_STAGGER_CLK);
+    ld_word2(p, a1, b1);
+    spin_clocks(POLL_STAGGER_CLK);
+    ld_word2(p, a2, b2);
+    while (true) {
+        if ((uint32_t)(a0 >> 32) == epoch && (uint32_t)(b0 >> 32) == epoch) return make_ulonglong2(a0, b0);
+        ld_word2(p, a0, b0);
+        if ((uint32_t)(a1 >> 32) == epoch && (uint32_t)(b1 >> 32) == epoch) return make_ulonglong2(a1, b1);
+        ld_word2(p, a1, b1);
+        if ((uint32_t)(a2 >> 32) == epoch && (uint32_t)(b2 >> 32) == epoch) return make_ulonglong2(a2, b2);
+        ld_word2(p, a2, b2);
+        if ((++n & 127u) == 0 && wait_give_up(misc, ws, limit, where, t0)) return make_ulonglong2(a0, b0);
+    }
+}
+
 __device__ __forceinline__ float poll1(const DecodeParams& P, Ctx& c, const unsigned long long* p, uint32_t epoch) {
     unsigned long long w = ld_word(p);
-    if ((uint32_t)(w >> 32) != epoch) {
-        uint64_t t0 = 0;
-        uint32_t n = 0;
-        do {
-            if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
-            MK_POLL_BACKOFF();
-            w = ld_word(p);
-        } while ((uint32_t)(w >> 32) != epoch);
-    }
+    if ((uint32_t)(w >> 32) != epoch) w = poll1_wait(p, epoch, c.misc, P.ws, P.poll_limit_cycles, c.where | ((uint32_t)c.step << 16), P.poll_pipelined);
     return __uint_as_float((uint32_t)w);
 }
 
@@ -276,35 +467,52 @@ __device__ __forceinline__ float2 poll2(const DecodeParams& P, Ctx& c, const uns
     unsigned long long a, b;
     ld_word2(p, a, b);
     if ((uint32_t)(a >> 32) != epoch || (uint32_t)(b >> 32) != epoch) {
-        uint64_t t0 = 0;
-        uint32_t n = 0;
-        do {
-            if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
-            MK_POLL_BACKOFF();
-            ld_word2(p, a, b);
-        } while ((uint32_t)(a >> 32) != epoch || (uint32_t)(b >> 32) != epoch);
+        const ulonglong2 r = poll2_wait(p, epoch, c.misc, P.ws, P.poll_limit_cycles, c.where | ((uint32_t)c.step << 16), P.poll_pipelined);
+        a = r.x; b = r.y;
     }
     return make_float2(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b));
 }
 
-// Batched polls: all loads are issued before any epoch is checked, so the N words cost one
-// L2 round trip instead of N.  W = words per load (1 or 2); words of one load are consecutive.
+// Batched polls: all loads of a round are issued before any epoch is checked, so the N words cost one L2 round
+// trip instead of N; after a failed first round two rounds are kept in flight half a round trip apart.
 template <int N>
 __device__ __forceinline__ void poll1_batch(const DecodeParams& P, Ctx& c, const unsigned long long* const (&p)[N],
                                             uint32_t epoch, float (&out)[N]) {
     unsigned long long w[N];
-    uint64_t t0 = 0;
-    uint32_t n = 0;
-#pragma unroll 1
-    while (true) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) w[i] = ld_word(p[i]);
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(w[i] >> 32) == epoch);
+    if (!ok) {
+        unsigned long long v[N];
 #pragma unroll
         for (int i = 0; i < N; ++i) w[i] = ld_word(p[i]);
-        bool ok = true;
+        if (P.poll_pipelined) spin_clocks(POLL_STAGGER_CLK + POLL_STAGGER_CLK / 2);
 #pragma unroll
-        for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(w[i] >> 32) == epoch);
-        if (ok) break;
-        if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
-        MK_POLL_BACKOFF();
+        for (int i = 0; i < N; ++i) v[i] = ld_word(p[i]);
+        uint64_t t0 = 0;
+        uint32_t n = 0;
+#pragma unroll 1
+        while (true) {
+            ok = true;
+#pragma unroll
+            for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(w[i] >> 32) == epoch);
+            if (ok) break;
+#pragma unroll
+            for (int i = 0; i < N; ++i) w[i] = ld_word(p[i]);
+            ok = true;
+#pragma unroll
+            for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(v[i] >> 32) == epoch);
+            if (ok) {
+#pragma unroll
+                for (int i = 0; i < N; ++i) w[i] = v[i];
+                break;
+            }
+#pragma unroll
+            for (int i = 0; i < N; ++i) v[i] = ld_word(p[i]);
+            if ((++n & 255u) == 0 && poll_give_up(P, c, t0)) break;
+        }
     }
 #pragma unroll
     for (int i = 0; i < N; ++i) out[i] = __uint_as_float((uint32_t)w[i]);
@@ -314,18 +522,40 @@ template <int N>
 __device__ __forceinline__ void poll2_batch(const DecodeParams& P, Ctx& c, const unsigned long long* const (&p)[N],
                                             uint32_t epoch, float2 (&out)[N]) {
     unsigned long long a[N], b[N];
-    uint64_t t0 = 0;
-    uint32_t n = 0;
-#pragma unroll 1
-    while (true) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) ld_word2(p[i], a[i], b[i]);
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(a[i] >> 32) == epoch) && ((uint32_t)(b[i] >> 32) == epoch);
+    if (!ok) {
+        unsigned long long x[N], y[N];
 #pragma unroll
         for (int i = 0; i < N; ++i) ld_word2(p[i], a[i], b[i]);
-        bool ok = true;
+        if (P.poll_pipelined) spin_clocks(POLL_STAGGER_CLK + POLL_STAGGER_CLK / 2);
 #pragma unroll
-        for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(a[i] >> 32) == epoch) && ((uint32_t)(b[i] >> 32) == epoch);
-        if (ok) break;
-        if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
-        MK_POLL_BACKOFF();
+        for (int i = 0; i < N; ++i) ld_word2(p[i], x[i], y[i]);
+        uint64_t t0 = 0;
+        uint32_t n = 0;
+#pragma unroll 1
+        while (true) {
+            ok = true;
+#pragma unroll
+            for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(a[i] >> 32) == epoch) && ((uint32_t)(b[i] >> 32) == epoch);
+            if (ok) break;
+#pragma unroll
+            for (int i = 0; i < N; ++i) ld_word2(p[i], a[i], b[i]);
+            ok = true;
+#pragma unroll
+            for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(x[i] >> 32) == epoch) && ((uint32_t)(y[i] >> 32) == epoch);
+            if (ok) {
+#pragma unroll
+                for (int i = 0; i < N; ++i) { a[i] = x[i]; b[i] = y[i]; }
+                break;
+            }
+#pragma unroll
+            for (int i = 0; i < N; ++i) ld_word2(p[i], x[i], y[i]);
+            if ((++n & 255u) == 0 && poll_give_up(P, c, t0)) break;
+        }
     }
 #pragma unroll
     for (int i = 0; i < N; ++i) out[i] = make_float2(__uint_as_float((uint32_t)a[i]), __uint_as_float((uint32_t)b[i]));
@@ -333,38 +563,54 @@ __device__ __forceinline__ void poll2_batch(const DecodeParams& P, Ctx& c, const
 
 // ---- producer ---------------------------------------------------------------------------
 
+// What producer lane `lane` moves for chunk q, with runs of consecutive slots whose sources and ring
+// destinations are contiguous (consecutive rows of one matrix) merged into ONE transfer issued by the run's
+// first lane: the issue rate, not the size, limits a CTA.  Returns this lane's bytes; `head` says whether the
+// lane issues, `run_bytes` how much.
+__device__ __forceinline__ uint32_t chunk_runs(const DecodeParams& P, Ctx& c, int type, const LW& lw, const Geo& g, int q,
+                                               int idx, int pos, const char*& src, uint32_t& dst_off, bool& head,
+                                               uint32_t& run_bytes) {
+    uint32_t bytes = chunk_slot_src(type, lw, P, g, q, c.lane, c.G, idx, src, dst_off, c.cta, pos);
+    if (bytes && (((uintptr_t)src) & 15u)) { fail(P, c, ST_MISALIGNED); bytes = 0; }
+    const unsigned long long prev_src = __shfl_up_sync(0xffffffffu, (unsigned long long)(uintptr_t)src, 1);
+    const uint32_t prev_bytes = __shfl_up_sync(0xffffffffu, bytes, 1);
+    const uint32_t prev_dst = __shfl_up_sync(0xffffffffu, dst_off, 1);
+    head = bytes && (c.lane == 0 || prev_bytes == 0 ||
+                     prev_src + prev_bytes != (unsigned long long)(uintptr_t)src ||
+                     prev_dst + prev_bytes != dst_off);
+    const uint32_t heads = __ballot_sync(0xffffffffu, head);
+    const uint32_t valid = __ballot_sync(0xffffffffu, bytes != 0);
+    const uint32_t above = (c.lane == 31) ? 0u : ~((2u << c.lane) - 1u);
+    const uint32_t stop = (heads | ~valid) & above;
+    const int end = stop ? (__ffs(stop) - 1) : 32;
+    run_bytes = bytes * (uint32_t)(end - c.lane);
+    return bytes;
+}
+
 __device__ __forceinline__ void producer_phase(const DecodeParams& P, Ctx& c, int type, const LW& lw, int dn_idx,
                                uint64_t pol_stream, uint64_t pol_keep) {
-    const Geo g = phase_geo(type, c.cta, c.G, P.vocab, P.position);
+    const Geo g = phase_geo(type, c.cta, c.G, P.vocab, c.pos);
+    // State rows and cache rows were written with ordinary stores, possibly by an earlier step of this launch.  The
+    // writers released (ring barrier / ready word) long before this warp acquired the stage it is about to fill; the
+    // proxy fence orders those writes before the bulk copies below, which read through the async proxy.  (A fence
+    // on the writers' side would sit on the critical path: it waits for their stores to complete.)
+    if (type == T_DN_REC || type == T_FA_ATT) fence_proxy_async();
 #pragma unroll 1
     for (int q = 0; q < g.nchunks; ++q, ++c.it) {
         if (c.misc[MISC_ABORT]) continue;
         const uint32_t stage = c.it % NSTAGE, parity = (c.it / NSTAGE) & 1u;
-        if (c.lane == 0 && !mbar_wait(c.empty0 + stage * 8, parity ^ 1u)) fail(P, c, ST_MBAR_TIMEOUT);
+        if (c.lane == 0 && !mbar_wait(c.empty0 + stage * 8, parity ^ 1u, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
         __syncwarp();
         const char* src = nullptr;
-        uint32_t dst_off = 0;
-        uint32_t bytes = chunk_slot_src(type, lw, P, g, q, c.lane, c.G, dn_idx, src, dst_off, c.cta);
-        if (bytes && (((uintptr_t)src) & 15u)) { fail(P, c, ST_MISALIGNED); bytes = 0; }
+        uint32_t dst_off = 0, run_bytes = 0;
+        bool head = false;
+        const uint32_t bytes = chunk_runs(P, c, type, lw, g, q, dn_idx, c.pos, src, dst_off, head, run_bytes);
         const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
         if (c.misc[MISC_ABORT]) continue;
-        // Consecutive slots whose sources and destinations are contiguous (consecutive rows of one
-        // matrix) travel as ONE bulk copy: the copy issue rate, not its size, limits a CTA.
-        const unsigned long long prev_src = __shfl_up_sync(0xffffffffu, (unsigned long long)(uintptr_t)src, 1);
-        const uint32_t prev_bytes = __shfl_up_sync(0xffffffffu, bytes, 1);
-        const uint32_t prev_dst = __shfl_up_sync(0xffffffffu, dst_off, 1);
-        const bool head = bytes && (c.lane == 0 || prev_bytes == 0 ||
-                                    prev_src + prev_bytes != (unsigned long long)(uintptr_t)src ||
-                                    prev_dst + prev_bytes != dst_off);
-        const uint32_t heads = __ballot_sync(0xffffffffu, head);
-        const uint32_t valid = __ballot_sync(0xffffffffu, bytes != 0);
-        const uint32_t above = (c.lane == 31) ? 0u : ~((2u << c.lane) - 1u);
-        const uint32_t stop = (heads | ~valid) & above;
-        const int end = stop ? (__ffs(stop) - 1) : 32;
         if (c.lane == 0) mbar_expect_tx(c.full0 + stage * 8, total);
         __syncwarp();
         if (head)
-            bulk_g2s(c.ring0 + stage * STAGE_BYTES + dst_off, src, bytes * (uint32_t)(end - c.lane), c.full0 + stage * 8,
+            bulk_g2s(c.ring0 + stage * STAGE_BYTES + dst_off, src, run_bytes, c.full0 + stage * 8,
                      (type == T_DN_REC || type == T_FA_ATT) ? pol_keep : pol_stream);
     }
 }
@@ -461,10 +707,12 @@ __device__ __forceinline__ void load_bfrags(const uint32_t* xw, int lane, uint32
 // `kofs` bytes into each row.  ROWS = 16: tile rows g and g+8; ROWS = 8: row g; ROWS = 4: rows g < 4.
 // Odd g read their chunks rotated by one so that the two rows of a quarter-warp hit different
 // banks (all rows alias: the row stride is a multiple of 128 bytes).  Writes the warp's partial
-// sums of tile rows into `out[0..15]`.
+// sums of tile rows into `out[0..15]`.  Not inlined (one copy per shape instead of one per phase: the
+// instruction cache is a scarce resource of this kernel); it loads the warp's activation fragments itself.
 template <int NLOAD, int ROWS>
-__device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, int lane,
-                                          const uint32_t (&b)[2 * NLOAD][2], float* out) {
+__device__ __noinline__ void mma_chunk(const char* stage, const uint32_t* xw, int K, int warp, int lane, float* out) {
+    uint32_t b[2 * NLOAD][2];
+    load_bfrags<NLOAD>(xw, lane, b);
     const int g = lane >> 2, t = lane & 3, odd = g & 1;
     const int rowbytes = row_stride(K), kofs = warp * NLOAD * 64;      // 32*NLOAD elements of 2 bytes per warp
     const bool live = (ROWS >= 8) || (g < 4);
@@ -509,7 +757,7 @@ __device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, in
     }
 }
 
-#else
+#elif MK_WFMT == 1
 // NVFP4 version of the chunk product.  Stage: packed rows at a stride of K/2+16 bytes, then the
 // fp16 scales of the chunk's rows.  The 16-byte weight chunk i of the bf16 layout (8 elements) is
 // one 32-bit word of nibbles here; the 32 elements the four lanes of a row cover in chunk i are
@@ -517,8 +765,9 @@ __device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, in
 // that is then scaled by the group's scale of each row: the dequantised value never has to be
 // rounded.  The row stride keeps the 8 rows of a quarter-warp on different banks.
 template <int NLOAD, int ROWS>
-__device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, int lane,
-                                          const uint32_t (&b)[2 * NLOAD][2], float* out) {
+__device__ __noinline__ void mma_chunk(const char* stage, const uint32_t* xw, int K, int warp, int lane, float* out) {
+    uint32_t b[2 * NLOAD][2];
+    load_bfrags<NLOAD>(xw, lane, b);
     const int g = lane >> 2, t = lane & 3;
     const bool live = (ROWS >= 8) || (g < 4);
     const int stride = row_stride(K);
@@ -562,20 +811,157 @@ __device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, in
 }
 #endif
 
+#if MK_WFMT == 2
+// ---- tensor-scale NVFP4: one chunk per phase, warps split it into row tiles x K parts ------------------------
+// A chunk of R = 8 GR rows is RT = GR / 2 row tiles of 16 rows; the 16 warps are RT row tiles x KS = 16 / RT K parts
+// of PK = NSEG * 32 elements.  MMA tile T takes, as its row g (g + 8 for the second half h), chunk row
+// GR g + 2 T + h: the eight rows a quarter-warp reads at once lie in the eight different row groups of the stage.
+// Activations: part p of the K dimension is staged as three f16 planes of PK elements (hi / mid / lo terms) at
+// xs + p * 3 PK / 2 words, written by whichever warps own those elements and read by the RT warps of that part.
+template <int PK>
+__device__ __forceinline__ void stage_pair_ts(uint32_t* xs_words, int e, float x0, float x1) {
+    uint32_t* xw = xs_words + (e / PK) * (3 * PK / 2);
+    const int l = e % PK;
+    uint32_t h0, m0, l0, h1, m1, l1;
+    split3(x0, h0, m0, l0);
+    split3(x1, h1, m1, l1);
+    xw[l >> 1] = __byte_perm(h0, h1, 0x7632);
+    xw[(PK >> 1) + (l >> 1)] = __byte_perm(m0, m1, 0x7632);
+    xw[PK + (l >> 1)] = __byte_perm(l0, l1, 0x7632);
+}
+template <int PK>
+__device__ __forceinline__ void stage_one_ts(uint32_t* xs_words, int e, float x) {
+    unsigned short* p = reinterpret_cast<unsigned short*>(xs_words + (e / PK) * (3 * PK / 2));
+    const int l = e % PK;
+    uint32_t h, m, lo;
+    split3(x, h, m, lo);
+    p[l] = (unsigned short)(h >> 16);
+    p[PK + l] = (unsigned short)(m >> 16);
+    p[2 * PK + l] = (unsigned short)(lo >> 16);
+}
+template <int NSEG>
+__device__ __forceinline__ void load_bfrags_ts(const uint32_t* xw, int lane, uint32_t (&b)[2 * NSEG][2]) {
+    constexpr int PK = NSEG * 32;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t* plane = xw + (g < 3 ? g : 0) * (PK >> 1);
+#pragma unroll
+    for (int i = 0; i < NSEG; ++i) {
+        uint4 v = *reinterpret_cast<const uint4*>(plane + 4 * (t + 4 * i));
+        if (g >= 3) v = make_uint4(0, 0, 0, 0);
+        b[2 * i][0] = v.x; b[2 * i][1] = v.y;
+        b[2 * i + 1][0] = v.z; b[2 * i + 1][1] = v.w;
+    }
+}
+// e2m1 pair (one byte) times an E4M3 block scale, both exact in f16: the product has at most 6 significant bits and
+// lies in [2^-10, 2688], so it is exact as well
+__device__ __forceinline__ uint32_t deq2(uint32_t byte, __half2 sc) {
+    const uint32_t w = e2m1x2_to_f16x2(byte);
+    const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&w), sc);
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ __half2 e4m3_to_h2(uint32_t byte) {
+    const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)(byte & 0xffu), __NV_E4M3);
+    return __half2half2(*reinterpret_cast<const __half*>(&h));
+}
+
+// The chunk in `stage` times the staged activation; this warp's partial sums of its tile's 16 rows go to
+// part[warp * 16 + 0..15] (warp = kq * RT + T).  K = KS * NSEG * 32.
+// Not inlined: the body is large, every phase would carry its own copy, and the instruction cache is a scarce
+// resource of this kernel; the arguments are scalars, so the call costs a few cycles per chunk.
+template <int NSEG, int RT>
+__device__ __noinline__ void mma_chunk_ts(const char* stage, const uint32_t* xw, int K, int warp, int lane, float* out) {
+    constexpr int GR = 2 * RT;
+    uint32_t b[2 * NSEG][2];
+    load_bfrags_ts<NSEG>(xw, lane, b);
+    const int g = lane >> 2, t = lane & 3, T = warp % RT, kq = warp / RT;
+    const int rb = K / 2, sb = K / 16;
+    const char* r0 = stage + g * (GR * rb + 16) + (2 * T) * rb + kq * (NSEG * 16) + 4 * t;
+    const char* r1 = r0 + rb;
+    const unsigned char* sc0 = reinterpret_cast<const unsigned char*>(stage) + 8 * (GR * rb + 16) + (GR * g + 2 * T) * sb + kq * (NSEG * 2);
+    const unsigned char* sc1 = sc0 + sb;
+    uint32_t w0[NSEG], w1[NSEG];
+    unsigned short s0[NSEG], s1[NSEG];
+#pragma unroll
+    for (int i = 0; i < NSEG; ++i) {
+        w0[i] = *reinterpret_cast<const uint32_t*>(r0 + 16 * i);
+        w1[i] = *reinterpret_cast<const uint32_t*>(r1 + 16 * i);
+    }
+    if (NSEG == 8) {       // the slice's 16 scale bytes of each row in one load
+        const uint4 a = *reinterpret_cast<const uint4*>(sc0), d = *reinterpret_cast<const uint4*>(sc1);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, dw[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+        for (int i = 0; i < NSEG; ++i) {
+            s0[i] = (unsigned short)(aw[i >> 1] >> (16 * (i & 1)));
+            s1[i] = (unsigned short)(dw[i >> 1] >> (16 * (i & 1)));
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < NSEG; ++i) {
+            s0[i] = *reinterpret_cast<const unsigned short*>(sc0 + 2 * i);
+            s1[i] = *reinterpret_cast<const unsigned short*>(sc1 + 2 * i);
+        }
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+    const int sh = (t >> 1) * 8;          // lanes t = 0,1 hold elements of the segment's first block, t = 2,3 of its second
+#pragma unroll
+    for (int i = 0; i < NSEG; ++i) {
+        const __half2 h0 = e4m3_to_h2((uint32_t)s0[i] >> sh), h1 = e4m3_to_h2((uint32_t)s1[i] >> sh);
+        mma_16816(acc, deq2(w0[i], h0), deq2(w1[i], h1), deq2(w0[i] >> 8, h0), deq2(w1[i] >> 8, h1), b[2 * i][0], b[2 * i][1]);
+        mma_16816(acc2, deq2(w0[i] >> 16, h0), deq2(w1[i] >> 16, h1), deq2(w0[i] >> 24, h0), deq2(w1[i] >> 24, h1),
+                  b[2 * i + 1][0], b[2 * i + 1][1]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] += acc2[k];
+    float q0 = acc[0] + (t == 0 ? acc[1] : 0.f);
+    float q1 = acc[2] + (t == 0 ? acc[3] : 0.f);
+    q0 += __shfl_down_sync(0xffffffffu, q0, 1);
+    q1 += __shfl_down_sync(0xffffffffu, q1, 1);
+    if (t == 0) { out[g] = q0; out[g + 8] = q1; }
+}
+
+// One-chunk phase.  `sync_parts`: the staged activation was written by other warps than the ones that read it.
+template <int NSEG, int RT>
+__device__ __forceinline__ void mma_phase_ts(const DecodeParams& P, Ctx& c, int nchunks, int K, bool sync_parts) {
+    constexpr int PK = NSEG * 32;
+    c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
+    if (sync_parts) named_bar_sync(1, NCT);
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(c.xs) + (c.warp / RT) * (3 * PK / 2);
+    if (nchunks > 1) { fail(P, c, ST_MISALIGNED); nchunks = 1; }   // never reached for grids >= MIN_GRID
+    if (nchunks > 0) {
+        const uint32_t stage = c.it % NSTAGE;
+        wait_full(P, c, stage, (c.it / NSTAGE) & 1u);
+        mma_chunk_ts<NSEG, RT>(c.smem + OFF_RING + stage * STAGE_BYTES, xw, K, c.warp, c.lane, c.part + c.warp * 16);
+        release_stage(c, stage);
+        ++c.it;
+    }
+}
+// sum over the K parts of stage row r of the chunk (RT row tiles, KS = 16 / RT parts)
+template <int RT>
+__device__ __forceinline__ float part_sum_ts(const Ctx& c, int r) {
+    constexpr int GR = 2 * RT, KS = NCW / RT;
+    const int g = r / GR, j = r % GR, T = j >> 1, h = j & 1;
+    float s = 0.f;
+#pragma unroll
+    for (int kq = 0; kq < KS; ++kq) s += c.part[(kq * RT + T) * 16 + g + 8 * h];
+    return s;
+}
+__device__ __forceinline__ float tensor_scale_of(const LW& lw, int slot) { return __ldg(reinterpret_cast<const float*>(lw.ptrs[slot + 2])); }
+#endif
+
+#if MK_WFMT != 2
 // Runs all chunks of a phase; partial sums land in part[(q * 16 + warp) * 16 + tile_row].
 template <int NLOAD, int ROWS>
 __device__ __forceinline__ void mma_phase(const DecodeParams& P, Ctx& c, int nchunks_in, int K) {
     int nchunks = nchunks_in;
     // alternate halves: a slow warp may still be reading the previous phase's sums in its epilogue
     c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
-    uint32_t b[2 * NLOAD][2];
-    load_bfrags<NLOAD>(reinterpret_cast<const uint32_t*>(c.xs) + c.warp * XSW, c.lane, b);
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(c.xs) + c.warp * XSW;
     if (nchunks > 4) { fail(P, c, ST_MISALIGNED); nchunks = 4; }   // never reached for grids >= MIN_GRID
     if (nchunks > 0) wait_full(P, c, c.it % NSTAGE, (c.it / NSTAGE) & 1u);
 #pragma unroll 1
     for (int q = 0; q < nchunks; ++q, ++c.it) {
         const uint32_t stage = c.it % NSTAGE;
-        mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + stage * STAGE_BYTES, K, c.warp, c.lane, b,
+        mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + stage * STAGE_BYTES, xw, K, c.warp, c.lane,
                                c.part + (q * NCW + c.warp) * 16);
         release_stage(c, stage);
         // the mbarrier test of the next chunk overlaps the tail of this chunk's MMAs
@@ -589,6 +975,7 @@ __device__ __forceinline__ float part_sum(const Ctx& c, int q, int row) {
     for (int w = 0; w < NCW; ++w) s += c.part[(q * NCW + w) * 16 + row];
     return s;
 }
+#endif
 
 // ---- activation staging -----------------------------------------------------------------
 
@@ -622,8 +1009,12 @@ __device__ __forceinline__ float2 rmsnorm_to_slice(Ctx& c, float2 v, float w0, f
     const float rstd = rsqrtf(tot * (1.0f / HIDDEN) + RMS_EPS);
     float x0 = v.x * rstd * w0, x1 = v.y * rstd * w1;
     if (round_to_bf16) { x0 = round_bf16(x0); x1 = round_bf16(x1); }
+#if MK_WFMT == 2
+    stage_pair_ts<256>(reinterpret_cast<uint32_t*>(c.xs), 2 * c.tid, x0, x1);    // read by other warps: mma_phase_ts syncs
+#else
     stage_pair(reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW, 2 * c.lane, x0, x1);
     __syncwarp();
+#endif
     return make_float2(x0, x1);
 }
 
@@ -654,7 +1045,10 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
             dt_b = bf2f(reinterpret_cast<const __nv_bfloat16*>(lw.ptrs[DN_DT_BIAS])[h]);
         }
     }
-#if MK_WFMT == 1
+#if MK_WFMT == 2
+    const float ts_in = (c.tid < nloc) ? tensor_scale_of(lw, r < DN_CONV_CH ? (int)DN_W_QKV : (int)DN_W_Z) : 0.f;
+#endif
+#if MK_WFMT >= 1
     // beta / alpha projections are bf16 rows outside the ring: CTA c < 32 owns row c of [Wb; Wa];
     // every thread multiplies its two activations with its two weights (fetched before the wait)
     uint32_t ba_w = 0u;
@@ -668,7 +1062,7 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
 #endif
     const float2 v = fetch_hidden2(P, c, embed_row, P.ws->x_hidden[1], epoch_of(c, layer - 1));
     const float2 xn = rmsnorm_to_slice(c, v, w0, w1, true);
-#if MK_WFMT == 1
+#if MK_WFMT >= 1
     if (c.cta < 2 * DN_HEADS) {
         const float pd = warp_sum(bf_lo(ba_w) * xn.x + bf_hi(ba_w) * xn.y);
         if (c.lane == 0) c.red[16 + c.warp] = pd;
@@ -677,10 +1071,14 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
     (void)xn;
 #endif
     trace_point(P, c);
+#if MK_WFMT == 2
+    mma_phase_ts<8, 4>(P, c, g.nchunks, HIDDEN, true);
+#else
     mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
+#endif
     trace_point(P, c);
     named_bar_sync(1, NCT);
-#if MK_WFMT == 1
+#if MK_WFMT >= 1
     if (c.tid == NCT - 1 && c.cta < 2 * DN_HEADS) {
         float val = 0.f;
 #pragma unroll
@@ -695,7 +1093,11 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
     }
 #endif
     if (c.tid < nloc) {
+#if MK_WFMT == 2
+        const float val = part_sum_ts<4>(c, c.tid) * ts_in;
+#else
         const float val = part_sum(c, c.tid >> 4, c.tid & 15);
+#endif
         if (r < DN_CONV_CH) {
             // shift the 4-tap window, append, dot with the taps, SiLU (reference: megakernel/kernel.cu:640-646)
             const float4 ns = make_float4(cs.y, cs.z, cs.w, val);
@@ -783,14 +1185,23 @@ __device__ __forceinline__ void phase_dn_rec(const DecodeParams& P, Ctx& c, int 
 }
 
 // out-projection (K = 2048, 8 rows per chunk) + residual -> bf16-rounded hidden words
-__device__ __forceinline__ void outproj_rows(const DecodeParams& P, Ctx& c, const Geo& g, int type, float resid, uint32_t ep) {
-    (void)type;
+__device__ __forceinline__ void outproj_rows(const DecodeParams& P, Ctx& c, const Geo& g, int type, float resid, uint32_t ep,
+                                             float tscale) {
+    (void)type; (void)tscale;
     const int nloc = g.r1 - g.r0;
+#if MK_WFMT == 2
+    mma_phase_ts<8, 2>(P, c, g.nchunks, 2048, true);
+#else
     mma_phase<4, 8>(P, c, g.nchunks, 2048);
+#endif
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nloc) {
+#if MK_WFMT == 2
+        const float y = part_sum_ts<2>(c, c.tid) * tscale + resid;
+#else
         const float y = part_sum(c, c.tid >> 3, c.tid & 7) + resid;
+#endif
         st_flagged(P.ws->x_hidden[0] + g.r0 + c.tid, round_bf16(y), ep);
     }
     trace_point(P, c);
@@ -827,13 +1238,23 @@ __device__ __forceinline__ void phase_dn_out(const DecodeParams& P, Ctx& c, cons
         x.y = oa.y * rstd * bf_hi(nwr.x) * silu_f(za.y);
         x.z = ob.x * rstd * bf_lo(nwr.y) * silu_f(zb.x);
         x.w = ob.y * rstd * bf_hi(nwr.y) * silu_f(zb.y);
+#if MK_WFMT == 2
+        uint32_t* xs_words = reinterpret_cast<uint32_t*>(c.xs);
+        stage_pair_ts<256>(xs_words, 128 * c.warp + 4 * c.lane, x.x, x.y);
+        stage_pair_ts<256>(xs_words, 128 * c.warp + 4 * c.lane + 2, x.z, x.w);
+#else
         uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
         stage_pair(xw, 4 * c.lane, x.x, x.y);
         stage_pair(xw, 4 * c.lane + 2, x.z, x.w);
         __syncwarp();
+#endif
     }
     trace_point(P, c);
-    outproj_rows(P, c, g, T_DN_OUT, resid, ep);
+#if MK_WFMT == 2
+    outproj_rows(P, c, g, T_DN_OUT, resid, ep, tensor_scale_of(lw, DN_W_OUT));
+#else
+    outproj_rows(P, c, g, T_DN_OUT, resid, ep, 1.0f);
+#endif
 }
 
 __device__ __forceinline__ void phase_fa_in(const DecodeParams& P, Ctx& c, const LW& lw, int layer,
@@ -847,11 +1268,23 @@ __device__ __forceinline__ void phase_fa_in(const DecodeParams& P, Ctx& c, const
     const float2 v = fetch_hidden2(P, c, embed_row, P.ws->x_hidden[1], epoch_of(c, layer - 1));
     rmsnorm_to_slice(c, v, w0, w1, true);
     trace_point(P, c);
+#if MK_WFMT == 2
+    float ts_in = 0.f;
+    if (c.tid < nloc) {
+        const int r = g.r0 + c.tid;
+        ts_in = tensor_scale_of(lw, r < FA_QPROJ ? (int)FA_W_Q : (r < FA_QPROJ + FA_KV_SIZE ? (int)FA_W_K : (int)FA_W_V));
+    }
+    mma_phase_ts<8, 4>(P, c, g.nchunks, HIDDEN, true);
+    trace_point(P, c);
+    named_bar_sync(1, NCT);
+    if (c.tid < nloc) st_flagged(P.ws->x_fain + g.r0 + c.tid, part_sum_ts<4>(c, c.tid) * ts_in, ep);
+#else
     mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nloc)      // rows 0..4095: per head [q(256) | gate(256)]; then k[512], v[512]
         st_flagged(P.ws->x_fain + g.r0 + c.tid, part_sum(c, c.tid >> 4, c.tid & 15), ep);
+#endif
     trace_point(P, c);
 }
 
@@ -879,7 +1312,7 @@ __device__ __forceinline__ void head_norm_rope(const DecodeParams& P, Ctx& c, co
     for (int e = 0; e < 8; ++e)
         n[e] = n[e] * rstd * (1.0f + bf2f(reinterpret_cast<const __nv_bfloat16*>(wn)[c.lane + 32 * e]));
     (void)pos;
-    const float sn = P.rope_sin[c.lane], cs = P.rope_cos[c.lane];   // host-computed for this position
+    const float cs = c.rope[c.lane], sn = c.rope[32 + c.lane];      // this step's position, computed at step start
     const float a = n[0], b = n[1];
     n[0] = a * cs - b * sn;
     n[1] = b * cs + a * sn;
@@ -916,7 +1349,7 @@ __device__ __forceinline__ uint32_t att_pack(float x, float y, bool lo_part) {
 }
 
 __device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, const LW& lw, int layer, int fa_idx) {
-    const int pos = P.position, L = pos + 1;
+    const int pos = c.pos, L = pos + 1;
     const uint32_t ep = epoch_of(c, layer);
     const Geo geo = phase_geo(T_FA_ATT, c.cta, c.G, P.vocab, pos);
     // scratch: query tile [8 rows][264] bf16 (rows 0-3 heads, 4-7 remainders), probability tile [8][72] bf16,
@@ -1098,9 +1531,8 @@ __device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, cons
 // (reference: megakernel/kernel.cu:542-570)
 __device__ __forceinline__ void phase_fa_out(const DecodeParams& P, Ctx& c, const LW& lw, int layer,
                              const __nv_bfloat16* embed_row) {
-    (void)lw;
     const Geo g = phase_geo(T_FA_OUT, c.cta, c.G, P.vocab);
-    const int NC = att_num_chunks(P.position + 1);
+    const int NC = att_num_chunks(c.pos + 1);
     const uint32_t ep = epoch_of(c, layer);
     trace_point(P, c);
     float resid = 0.f;
@@ -1139,13 +1571,23 @@ __device__ __forceinline__ void phase_fa_out(const DecodeParams& P, Ctx& c, cons
         float4 x;
         x.x = o.x * inv * sigmoid_f(ga.x); x.y = o.y * inv * sigmoid_f(ga.y);
         x.z = o.z * inv * sigmoid_f(gb.x); x.w = o.w * inv * sigmoid_f(gb.y);
+#if MK_WFMT == 2
+        uint32_t* xs_words = reinterpret_cast<uint32_t*>(c.xs);
+        stage_pair_ts<256>(xs_words, 128 * c.warp + 4 * c.lane, x.x, x.y);
+        stage_pair_ts<256>(xs_words, 128 * c.warp + 4 * c.lane + 2, x.z, x.w);
+#else
         uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
         stage_pair(xw, 4 * c.lane, x.x, x.y);
         stage_pair(xw, 4 * c.lane + 2, x.z, x.w);
         __syncwarp();
+#endif
     }
     trace_point(P, c);
-    outproj_rows(P, c, g, T_FA_OUT, resid, ep);
+#if MK_WFMT == 2
+    outproj_rows(P, c, g, T_FA_OUT, resid, ep, tensor_scale_of(lw, FA_W_O));
+#else
+    outproj_rows(P, c, g, T_FA_OUT, resid, ep, 1.0f);
+#endif
 }
 
 // post norm + SiLU(Wg x) * (Wu x): tile rows 0-7 are gate rows, 8-15 the matching up rows
@@ -1160,19 +1602,32 @@ __device__ __forceinline__ void phase_gateup(const DecodeParams& P, Ctx& c, cons
     const float2 v = poll2(P, c, P.ws->x_hidden[0] + 2 * c.tid, ep);
     rmsnorm_to_slice(c, v, w0, w1, true);
     trace_point(P, c);
+#if MK_WFMT == 2
+    const bool dnl = (lw.layer_type == 0);
+    const float ts_g = tensor_scale_of(lw, dnl ? (int)DN_W_GATE : (int)FA_W_GATE);
+    const float ts_u = tensor_scale_of(lw, dnl ? (int)DN_W_UP : (int)FA_W_UP);
+    mma_phase_ts<8, 4>(P, c, g.nchunks, HIDDEN, true);
+#else
     mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
+#endif
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nout) {
+#if MK_WFMT == 2
+        const float gv = part_sum_ts<4>(c, c.tid) * ts_g;
+        const float uv = part_sum_ts<4>(c, 32 + c.tid) * ts_u;
+#else
         const float gv = part_sum(c, c.tid >> 3, c.tid & 7);
         const float uv = part_sum(c, c.tid >> 3, 8 + (c.tid & 7));
+#endif
         st_flagged(P.ws->x_mlp + g.r0 + c.tid, silu_f(gv) * uv, ep);
     }
     trace_point(P, c);
 }
 
 // down projection (K = 3584, 4 rows per chunk) + residual (reference: megakernel/kernel.cu:350-384)
-__device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, int layer) {
+__device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, const LW& lw, int layer) {
+    (void)lw;
     const Geo g = phase_geo(T_DOWN, c.cta, c.G, P.vocab);
     const int nloc = g.r1 - g.r0;
     const uint32_t ep = epoch_of(c, layer);
@@ -1184,17 +1639,32 @@ __device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, int la
         const unsigned long long* base = P.ws->x_mlp + c.warp * XK + c.lane;
         const unsigned long long* const p1[7] = {base, base + 32, base + 64, base + 96, base + 128, base + 160, base + 192};
         poll1_batch<7>(P, c, p1, ep, xv);
+#if MK_WFMT == 2
+        uint32_t* xs_words = reinterpret_cast<uint32_t*>(c.xs);
+#pragma unroll
+        for (int k = 0; k < 7; ++k) stage_one_ts<224>(xs_words, 224 * c.warp + c.lane + 32 * k, xv[k]);
+#else
         uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
 #pragma unroll
         for (int k = 0; k < 7; ++k) stage_one(xw, c.lane + 32 * k, xv[k]);
+#endif
         __syncwarp();
     }
     trace_point(P, c);
+#if MK_WFMT == 2
+    const float ts_d = tensor_scale_of(lw, lw.layer_type == 0 ? (int)DN_W_DOWN : (int)FA_W_DOWN);
+    mma_phase_ts<7, 1>(P, c, g.nchunks, INTER, false);
+#else
     mma_phase<7, 4>(P, c, g.nchunks, INTER);
+#endif
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nloc) {
+#if MK_WFMT == 2
+        const float y = part_sum_ts<1>(c, c.tid) * ts_d + resid;
+#else
         const float y = part_sum(c, c.tid >> 2, c.tid & 3) + resid;
+#endif
         st_flagged(P.ws->x_hidden[1] + g.r0 + c.tid, round_bf16(y), ep);
     }
     trace_point(P, c);
@@ -1264,6 +1734,40 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
             if (acc > bestv) { bestv = acc; besti = row; }
         }
         release_stage(c, stage);
+    }
+#elif MK_WFMT == 2
+    // LM head in the tensor-scale format on the tensor cores: a chunk is 64 packed rows with their block scales,
+    // processed like a K = 1024 layer chunk (4 row tiles x 4 K parts); the final-normed vector (f32) is staged once
+    // as three f16 terms.  Partial sums alternate between the two halves of `part` from chunk to chunk, so one
+    // CTA barrier per chunk is enough: rows are finished by threads 0-63 while the warps start the next chunk.
+    {
+        const float2 xv = reinterpret_cast<const float2*>(c.xs)[c.tid];
+        named_bar_sync(1, NCT);                                   // everyone has read the f32 vector: reuse the scratch
+        stage_pair_ts<256>(reinterpret_cast<uint32_t*>(c.xs), 2 * c.tid, xv.x, xv.y);
+        named_bar_sync(1, NCT);
+    }
+    const uint32_t* xw_lm = reinterpret_cast<const uint32_t*>(c.xs) + (c.warp / 4) * (3 * 256 / 2);
+    const float ts_lm = __ldg(P.lm_tensor_scale);
+#pragma unroll 1
+    for (int q = 0; q < g.nchunks; ++q, ++c.it) {
+        const uint32_t stage = c.it % NSTAGE, parity = (c.it / NSTAGE) & 1u;
+        c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
+        wait_full(P, c, stage, parity);
+        mma_chunk_ts<8, 4>(c.smem + OFF_RING + stage * STAGE_BYTES, xw_lm, HIDDEN, c.warp, c.lane, c.part + c.warp * 16);
+        release_stage(c, stage);
+        named_bar_sync(1, NCT);
+        const int lr = q * LM_RPC + c.tid;
+        if (c.tid < LM_RPC && lr < nloc) {
+            const float acc = part_sum_ts<4>(c, c.tid) * ts_lm;
+            if (acc > bestv) { bestv = acc; besti = g.r0 + lr; }
+        }
+    }
+    // every thread holds the best of its own rows: make it warp-uniform, like the other variants leave it
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bestv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+        if (ov > bestv || (ov == bestv && oi < besti)) { bestv = ov; besti = oi; }
     }
 #else
     // LM head in the 16-block E4M3 format: a chunk is 64 packed rows (512 bytes each); a warp takes
@@ -1363,16 +1867,41 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
         if (c.lane == 0) {
-            *P.out_token = bi;
+            // a wait ran out somewhere in this launch: the argmax was taken over garbage, report -1 instead
+            if (*((volatile uint32_t*)&P.ws->abort_flag) != 0u) bi = -1;
+            P.out_token[c.step] = bi;
             if (P.token_feedback) *P.token_feedback = bi;
-            if (P.out_tokens_slot) *P.out_tokens_slot = bi;
-            // every CTA has finished: re-arm the workspace for the next launch
+            // every CTA has finished this step: re-arm the workspace, then hand the token to the next step of this
+            // launch (every CTA waits for this word before it touches the workspace again)
             P.ws->lm_count = 0u;
             P.ws->seq = c.seq + 1u;
+            __threadfence();
+            st_flagged(&P.ws->next_token, __int_as_float(bi), ((c.seq + 2u) << 5));
         }
     }
     trace_point(P, c);
 }
+
+#if MK_WFMT == 0 && MK_TRACE == 0
+// The kernel's poll of a flagged word, on a word whose epoch never comes: see launch_wait_selftest().
+__global__ void wait_selftest_kernel(const __grid_constant__ DecodeParams P) {
+    __shared__ int misc[8];
+    Ctx c;
+    c.misc = misc;
+    c.tid = threadIdx.x; c.warp = 0; c.lane = threadIdx.x; c.cta = blockIdx.x; c.G = gridDim.x;
+    c.seq = __ldcg(&P.ws->seq);
+    c.where = 0; c.step = 0;
+    if (threadIdx.x == 0) { misc[MISC_ABORT] = 0; misc[MISC_DETAIL] = 0; }
+    __syncthreads();
+    // epoch of a layer index no phase ever publishes: the word keeps whatever epoch it had
+    (void)poll1(P, c, P.ws->x_mlp + blockIdx.x, epoch_of(c, 30));
+    __syncthreads();
+    if (threadIdx.x == 0 && misc[MISC_ABORT] && P.host_status) {
+        *((volatile uint32_t*)P.host_status) = (uint32_t)misc[MISC_ABORT];
+        __threadfence_system();
+    }
+}
+#endif
 
 __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(1024) char smem[];
@@ -1391,6 +1920,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
     c.cta = blockIdx.x; c.G = gridDim.x;
     c.it = 0; c.trace_slot = 0;
     c.seq = __ldcg(&P.ws->seq);
+    c.pos = P.position; c.step = 0; c.where = 0;
+    float* s_rope = reinterpret_cast<float*>(smem + OFF_ROPE);
+    c.rope = s_rope;
 
     // The pointer table is read on every chunk; keep it in shared memory.
     LW* s_layers = reinterpret_cast<LW*>(smem + OFF_LAYERS);
@@ -1403,62 +1935,95 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
         }
         c.misc[MISC_ABORT] = 0;
         c.misc[MISC_LAST] = 0;
+        c.misc[MISC_DETAIL] = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
-    int token = P.token_ptr ? __ldcg(P.token_ptr) : P.token_val;
-    token = token < 0 ? 0 : (token >= P.vocab ? P.vocab - 1 : token);
-    const __nv_bfloat16* embed_row = reinterpret_cast<const __nv_bfloat16*>(P.embed) + (size_t)token * HIDDEN;
-
     if (c.warp == NCW) {
         // ===== producer warp =====
+        // Walks the weight schedule of every step of the launch; it never needs the token, so it runs ahead of the
+        // consumers across step boundaries (the next step's first layer streams in while the argmax finishes).
         const uint64_t pol_stream = l2_policy_evict_first();
         const uint64_t pol_keep = l2_policy_evict_last();
-        // one copy of the issue code: the phase type is a run-time value here
-        int dn_idx = 0, fa_idx = 0;
-        for (int layer = 0; layer <= P.num_layers; ++layer) {
-            const bool lm = (layer == P.num_layers);
-            const LW& lw = s_layers[lm ? 0 : layer];
-            const bool dn = (lw.layer_type == 0);
-            const int nph = 5 - (lm ? 4 : 0);
 #pragma unroll 1
-            for (int ph = 0; ph < nph; ++ph) {
-                int type;
-                if (lm) type = T_LM;
-                else if (dn) type = (ph == 0) ? T_DN_IN : (ph == 1) ? T_DN_REC : (ph == 2) ? T_DN_OUT : (ph == 3) ? T_GATEUP : T_DOWN;
-                else type = (ph == 0) ? T_FA_IN : (ph == 1) ? T_FA_ATT : (ph == 2) ? T_FA_OUT : (ph == 3) ? T_GATEUP : T_DOWN;
-                producer_phase(P, c, type, lw, dn ? dn_idx : fa_idx, pol_stream, pol_keep);
+        for (int step = 0; step < P.steps; ++step) {
+            c.pos = P.position + step;
+            c.step = step;
+            int dn_idx = 0, fa_idx = 0;
+            for (int layer = 0; layer <= P.num_layers; ++layer) {
+                const bool lm = (layer == P.num_layers);
+                const LW& lw = s_layers[lm ? 0 : layer];
+                const bool dn = (lw.layer_type == 0);
+                const int nph = 5 - (lm ? 4 : 0);
+#pragma unroll 1
+                for (int ph = 0; ph < nph; ++ph) {
+                    int type;
+                    if (lm) type = T_LM;
+                    else if (dn) type = (ph == 0) ? T_DN_IN : (ph == 1) ? T_DN_REC : (ph == 2) ? T_DN_OUT : (ph == 3) ? T_GATEUP : T_DOWN;
+                    else type = (ph == 0) ? T_FA_IN : (ph == 1) ? T_FA_ATT : (ph == 2) ? T_FA_OUT : (ph == 3) ? T_GATEUP : T_DOWN;
+                    c.where = 0x8000u | ((uint32_t)layer << 4) | (uint32_t)type;
+                    producer_phase(P, c, type, lw, dn ? dn_idx : fa_idx, pol_stream, pol_keep);
+                }
+                if (!lm) { if (dn) ++dn_idx; else ++fa_idx; }
             }
-            if (!lm) { if (dn) ++dn_idx; else ++fa_idx; }
         }
     } else {
         // ===== consumer warps =====
-        if (c.cta == 0 && c.tid == 0 && P.seen_mask && P.rep_penalty > 1.0f) P.seen_mask[token] = 1.0f;
-        int dn_idx = 0, fa_idx = 0;
-        for (int layer = 0; layer < P.num_layers; ++layer) {
-            const LW& lw = s_layers[layer];
-            const __nv_bfloat16* erow = (layer == 0) ? embed_row : nullptr;
-            if (lw.layer_type == 0) {
-                phase_dn_in(P, c, lw, layer, dn_idx, erow);
-                phase_dn_rec(P, c, layer, dn_idx);
-                phase_dn_out(P, c, lw, layer, erow);
-                ++dn_idx;
-            } else {
-                phase_fa_in(P, c, lw, layer, erow);
-                phase_fa_att(P, c, lw, layer, fa_idx);
-                phase_fa_out(P, c, lw, layer, erow);
-                ++fa_idx;
+#pragma unroll 1
+        for (int step = 0; step < P.steps; ++step) {
+            c.step = step;
+            c.pos = P.position + step;
+            // this step's token: the launch argument, or the previous step's argmax handed over through the workspace
+            if (c.tid == 0) {
+                int t;
+                if (step == 0) t = P.token_ptr ? __ldcg(P.token_ptr) : P.token_val;
+                else t = __float_as_int(poll1(P, c, &P.ws->next_token, (c.seq + 1u) << 5));
+                c.misc[MISC_TOKEN] = t < 0 ? 0 : (t >= P.vocab ? P.vocab - 1 : t);
             }
-            phase_gateup(P, c, lw, layer);
-            phase_down(P, c, layer);
+            // rotary angles of this position (reference: megakernel/kernel.cu:468-470): angle in f32, accurate sincosf
+            if (c.warp == NCW - 1) {
+                float sn, cs;
+                sincosf((float)c.pos * P.rope_inv_freq[c.lane], &sn, &cs);
+                s_rope[c.lane] = cs;
+                s_rope[32 + c.lane] = sn;
+            }
+            named_bar_sync(1, NCT);
+            const int token = c.misc[MISC_TOKEN];
+            const __nv_bfloat16* embed_row = reinterpret_cast<const __nv_bfloat16*>(P.embed) + (size_t)token * HIDDEN;
+            if (c.cta == 0 && c.tid == 0 && P.seen_mask && P.rep_penalty > 1.0f) P.seen_mask[token] = 1.0f;
+            int dn_idx = 0, fa_idx = 0;
+#pragma unroll 1
+            for (int layer = 0; layer < P.num_layers; ++layer) {
+                const LW& lw = s_layers[layer];
+                const __nv_bfloat16* erow = (layer == 0) ? embed_row : nullptr;
+                const uint32_t wl = (uint32_t)layer << 4;
+                if (lw.layer_type == 0) {
+                    c.where = wl | T_DN_IN;  phase_dn_in(P, c, lw, layer, dn_idx, erow);
+                    c.where = wl | T_DN_REC; phase_dn_rec(P, c, layer, dn_idx);
+                    c.where = wl | T_DN_OUT; phase_dn_out(P, c, lw, layer, erow);
+                    ++dn_idx;
+                } else {
+                    c.where = wl | T_FA_IN;  phase_fa_in(P, c, lw, layer, erow);
+                    c.where = wl | T_FA_ATT; phase_fa_att(P, c, lw, layer, fa_idx);
+                    c.where = wl | T_FA_OUT; phase_fa_out(P, c, lw, layer, erow);
+                    ++fa_idx;
+                }
+                c.where = wl | T_GATEUP; phase_gateup(P, c, lw, layer);
+                c.where = wl | T_DOWN;   phase_down(P, c, lw, layer);
+            }
+            c.where = ((uint32_t)P.num_layers << 4) | T_LM;
+            phase_lm(P, c);
+            ++c.seq;
         }
-        phase_lm(P, c);
     }
     __syncthreads();
     if (c.misc[MISC_ABORT]) {
         if (threadIdx.x == 0 && P.host_status) {
-            *((volatile uint32_t*)P.host_status) = (uint32_t)c.misc[MISC_ABORT];
+            // low byte: ST code; bits 8-11 phase, 12-18 layer, 23 producer warp, 24-31 step (where the first wait gave up)
+            const uint32_t d = (uint32_t)c.misc[MISC_DETAIL];
+            *((volatile uint32_t*)P.host_status) = ((uint32_t)c.misc[MISC_ABORT] & 0xffu) | ((d & 0x7fffu) << 8) |
+                                                   ((d & 0x8000u) << 8) | ((d >> 16) << 24);
             __threadfence_system();
         }
         // a wait ran out: give bulk copies that are still in flight time to land before the CTA exits

@@ -59,10 +59,17 @@ extern "C" int mk_decode_bf16_static_scratch(
     const void* req[] = {output_token_id, embed_weight, layer_weights, final_norm_weight, lm_head_weight,
                          fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden_buffer, g_qkv_scratch, g_kv_scratch,
                          g_attn_out, g_mlp_inter, g_z_scratch, g_beta_scratch, g_alpha_scratch, g_normalized};
-    for (const void* p : req) {
+    for (const void* p : req)
         if (!p) return fail_with(MK_ERR_BAD_ARG, "null pointer argument");
-        if (reinterpret_cast<uintptr_t>(p) & 3u) return fail_with(MK_ERR_BAD_ARG, "misaligned pointer argument");
-    }
+    // the kernel streams weight and cache rows with 16-byte bulk copies and vector loads: same rule as launch_decode()
+    const void* al16[] = {embed_weight, layer_weights, final_norm_weight, lm_head_weight, fa_k_cache, fa_v_cache,
+                          dn_states, conv_bufs, hidden_buffer, g_qkv_scratch, g_kv_scratch, g_attn_out, g_mlp_inter,
+                          g_z_scratch, g_normalized};
+    for (const void* p : al16)
+        if (reinterpret_cast<uintptr_t>(p) & 15u) return fail_with(MK_ERR_BAD_ARG, "pointer argument is not 16-byte aligned");
+    const void* al4[] = {output_token_id, g_beta_scratch, g_alpha_scratch, seen_token_mask};
+    for (const void* p : al4)
+        if (reinterpret_cast<uintptr_t>(p) & 3u) return fail_with(MK_ERR_BAD_ARG, "pointer argument is not 4-byte aligned");
     if (num_layers < 1 || num_layers > mk::MAX_LAYERS)
         return fail_with(MK_ERR_BAD_ARG, "num_layers beyond the maximum of 24 the static scratch variant is built for");
     if (vocab < 1) return fail_with(MK_ERR_BAD_ARG, "vocab must be positive");
@@ -121,8 +128,25 @@ extern "C" int mk_decode_bf16_static_scratch(
     p.ws = s.scratch;
     p.host_status = nullptr;   // the mapped status word of launch_decode would be an allocation
     p.trace = nullptr; p.trace_slots = 0;
+    p.poll_limit_cycles = mk::DEFAULT_POLL_LIMIT_CYCLES; p.mbar_limit_tries = mk::DEFAULT_MBAR_LIMIT_TRIES;
+    p.steps = 1; p.poll_pipelined = 1;
     mk::fill_rope(p);
     e = mk::launch_decode_kernel(p, s.grid, stream);
     if (e != cudaSuccess) return fail_with(MK_ERR_CUDA, "decode launch", e);
+    return MK_OK;
+}
+
+// Status of the last call on the current device, without an allocation: copies the array's "a wait ran out"
+// word (0 = the launch completed normally) to `status_out` on `stream`.  Queue it after the decode call and
+// before the next one, which clears the word.
+extern "C" int mk_decode_bf16_static_scratch_status(unsigned int* status_out, cudaStream_t stream) {
+    if (!status_out) return fail_with(MK_ERR_BAD_ARG, "null status_out");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail_with(MK_ERR_CUDA, "cudaGetDevice", e);
+    if (dev < 0 || dev >= MAX_DEVICES || !g_static[dev].done)
+        return fail_with(MK_ERR_BAD_ARG, "no static-scratch decode call has run on this device yet");
+    e = cudaMemcpyAsync(status_out, &g_static[dev].scratch->abort_flag, sizeof(unsigned int), cudaMemcpyDefault, stream);
+    if (e != cudaSuccess) return fail_with(MK_ERR_CUDA, "cudaMemcpyAsync(static scratch status)", e);
     return MK_OK;
 }

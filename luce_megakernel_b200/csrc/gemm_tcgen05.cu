@@ -292,7 +292,7 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int k, int ld, int b
 
 template <int BN>
 cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc, int* err_flag,
-                        int sms, cudaStream_t stream) {
+                        int sms, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream) {
     static bool attr_done = false;
     if (!attr_done) {
         cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
@@ -308,17 +308,11 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
     int ks = sms / ntiles;
     if (ks > 4) ks = 4;
     while (ks > 1 && (K / BK) / ks < 4) --ks;
+    // the f32 partials live in the caller's workspace (nothing is allocated here: the call must stay capturable into
+    // a CUDA graph); without room for them the product is not split
+    while (ks > 1 && (size_t)ks * M * N * sizeof(float) > splitk_bytes) --ks;
     if (BN == 128 && ks >= 2 && K >= 2048) {      // only the long-K projections: K = 1024 products keep one summation order
-        static float* ws = nullptr;
-        static size_t ws_bytes = 0;
-        const size_t need = (size_t)ks * M * N * sizeof(float);
-        if (need > ws_bytes) {
-            if (ws) cudaFree(ws);
-            ws = nullptr; ws_bytes = 0;
-            cudaError_t e = cudaMalloc((void**)&ws, need);
-            if (e != cudaSuccess) return e;
-            ws_bytes = need;
-        }
+        float* ws = splitk_ws;
         const int items = ntiles * ks;
         launch_pdl(gemm_bf16_tn_kernel<BN, true>, items < sms ? items : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, nullptr, nullptr, M, N, K, ldc, err_flag, ws, ks);
         const size_t n = (size_t)M * (N / 8);
@@ -332,7 +326,7 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
 }  // namespace
 
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
-                         int* err_flag, cudaStream_t stream) {
+                         int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream) {
     if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % BK) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(C)) & 15u)
         return cudaErrorInvalidValue;
@@ -346,8 +340,8 @@ cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, i
     }
     // 256-wide tiles once they fill the machine; 128-wide tiles keep more SMs busy on small problems
     const int mt = (M + BM - 1) / BM;
-    if (N % 256 == 0 && mt * (N / 256) >= sms) return launch_gemm<256>(A, W, C, R, M, N, K, lda, ldc, err_flag, sms, stream);
-    return launch_gemm<128>(A, W, C, R, M, N, K, lda, ldc, err_flag, sms, stream);
+    if (N % 256 == 0 && mt * (N / 256) >= sms) return launch_gemm<256>(A, W, C, R, M, N, K, lda, ldc, err_flag, sms, splitk_ws, splitk_bytes, stream);
+    return launch_gemm<128>(A, W, C, R, M, N, K, lda, ldc, err_flag, sms, splitk_ws, splitk_bytes, stream);
 }
 
 }  // namespace mk

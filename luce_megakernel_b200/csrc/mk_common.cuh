@@ -55,6 +55,17 @@ struct LayerWeightsNVFP4 {
 };
 static_assert(sizeof(LayerWeightsNVFP4) == 208, "NVFP4 pointer table entry must be 208 bytes");
 
+// Pointer table entry of the NVFP4 format with a per-tensor scale, 224 bytes: a quantised matrix takes three slots
+// (packed e2m1 codes [rows][K/2], E4M3 block scales row-major [rows][K/16], device pointer to the fp32 tensor scale);
+// norms, conv, beta / alpha projections, A_log, dt_bias stay bf16 (one slot each).  DeltaNet layers use 26 slots,
+// attention layers 25.  No counterpart in the reference (its NVFP4 table has no tensor scale).
+struct LayerWeightsNVFP4TS {
+    int layer_type;
+    int pad[3];
+    const void* ptrs[26];
+};
+static_assert(sizeof(LayerWeightsNVFP4TS) == 224, "tensor-scale NVFP4 pointer table entry must be 224 bytes");
+
 // pointer slots, DeltaNet layer (reference: megakernel/model.py:117-132)
 enum { DN_IN_NORM = 0, DN_W_QKV, DN_W_Z, DN_W_B, DN_W_A, DN_CONV_W, DN_A_LOG, DN_DT_BIAS,
        DN_NORM_W, DN_W_OUT, DN_POST_NORM, DN_W_GATE, DN_W_UP, DN_W_DOWN };
@@ -95,8 +106,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait: returns false when the limit ran out (the caller records the status).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t n = 0; n < (1u << 22); ++n)
+constexpr uint32_t MBAR_WAIT_TRIES = 1u << 22;
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t tries = MBAR_WAIT_TRIES) {
+    for (uint32_t n = 0; n < tries; ++n)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }

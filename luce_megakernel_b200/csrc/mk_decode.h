@@ -25,8 +25,10 @@ struct DecodeWorkspace {
     uint32_t lm_count;    // CTAs that have published their argmax partial
     uint32_t abort_flag;  // set by the first CTA whose bounded wait ran out
     uint32_t pad0[14];
-    uint32_t seq;         // launches completed on this workspace
-    uint32_t pad1[15];
+    uint32_t seq;         // decode steps completed on this workspace
+    uint32_t pad1a;
+    unsigned long long next_token;   // {token, epoch}: a step's argmax, handed to the next step of the same launch
+    uint32_t pad1[12];
     float argmax_val[MAX_GRID];
     int argmax_idx[MAX_GRID];
     uint32_t att_ready[32];                 // per attention unit: epoch once its partials are written
@@ -43,8 +45,10 @@ struct DecodeParams {
     const void* layers;           // device pointer table: LayerWeights[] (bf16) or LayerWeightsNVFP4[] (wfmt 1)
     const void* final_norm;       // bf16 [1024]
     const void* lm_head;          // bf16 [vocab, 1024], or packed e2m1 [vocab, 512] when wfmt is 1
-    const void* lm_scales;        // wfmt 1: E4M3 block scales of the LM head (128 x 4 tiles)
-    int wfmt;                     // 0 = bf16 weights, 1 = NVFP4 (layer format A, LM head format B)
+    const void* lm_scales;        // wfmt 1: E4M3 block scales of the LM head (128 x 4 tiles); wfmt 2: row-major [vocab][64]
+    const float* lm_tensor_scale; // wfmt 2: fp32 scale of the LM-head matrix
+    int wfmt;                     // 0 = bf16 weights, 1 = NVFP4 (layer format A, LM head format B), 2 = NVFP4 with
+                                  // 16-element blocks, E4M3 block scales (row-major) and an fp32 scale per matrix
     void* k_cache;                // bf16 [n_fa, 2, max_seq, 256]
     void* v_cache;
     float* dn_states;             // f32 [n_dn, 16, 128(value), 128(key)]
@@ -62,12 +66,11 @@ struct DecodeParams {
     float rep_penalty;
     const int* token_ptr;         // device token (feedback mode) or null
     int token_val;                // host token when token_ptr is null
-    int* out_token;               // int32 [1]
-    int* token_feedback;          // optional: also receives the new token
-    int* out_tokens_slot;         // optional: also receives the new token
-    int position;
-    float rope_cos[32];           // cos / sin of position * inv_freq_i, filled by fill_rope()
-    float rope_sin[32];
+    int* out_token;               // int32 [steps]: out_token[s] receives the token chosen by step s
+    int* token_feedback;          // optional: also receives every new token (the last one remains)
+    int position;                 // position of the first step's token; step s decodes at position + s
+    int steps;                    // greedy steps in this launch (>= 1), the argmax fed back on the device
+    float rope_inv_freq[32];      // theta^(-2i/64), filled by fill_rope(); the angles are formed on the device
     int max_seq_len;
     int num_layers;
     int vocab;
@@ -75,14 +78,25 @@ struct DecodeParams {
     uint32_t* host_status;        // mapped pinned word, written only on failure
     unsigned long long* trace;    // optional [grid][trace_slots] globaltimer stamps
     int trace_slots;              // entries per CTA in `trace`
+    unsigned long long poll_limit_cycles;   // SM clocks a poll of a flagged word may take before the CTA gives up
+    uint32_t mbar_limit_tries;              // try_wait attempts on a ring barrier before the CTA gives up
+    int poll_pipelined;                     // 1: a failed poll keeps several loads in flight (see decode_body.cuh)
 };
 
-// Fills rope_cos / rope_sin for p.position (call after setting the position).
+// Defaults of the two wait limits: about 2 s of SM clock each.
+constexpr unsigned long long DEFAULT_POLL_LIMIT_CYCLES = 4000000000ull;
+constexpr uint32_t DEFAULT_MBAR_LIMIT_TRIES = 1u << 22;
+
+// Fills rope_inv_freq (position-independent).
 void fill_rope(DecodeParams& p);
 // Launches the persistent decode kernel (cooperative launch, `grid` CTAs of 544 threads).
 cudaError_t launch_decode_kernel(const DecodeParams& p, int grid, cudaStream_t stream);
 // Largest grid that is guaranteed co-resident on the current device.
 int decode_max_grid();
 size_t decode_smem_bytes();
+// Two CTAs run the kernel's own poll of a flagged word on a word nobody writes, with p.poll_limit_cycles as the
+// limit: the wait runs out, the CTAs record ST_GRID_TIMEOUT through the kernel's failure path and return.  Exists
+// so that the failure path can be exercised without a hung launch; p needs ws, host_status and the limit only.
+cudaError_t launch_wait_selftest(const DecodeParams& p, cudaStream_t stream);
 
 }  // namespace mk

@@ -23,8 +23,10 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 // C[M,N] = A[M,K] . W[N,K]^T (+ R[M,N]); bf16 row-major, f32 accumulate; tcgen05 / TMEM / TMA.
 // N % 128 == 0, K % 64 == 0, lda and ldc multiples of 8 elements, pointers 16-byte aligned.
 // err_flag: device int, set to 1 if a bounded wait ran out inside the kernel.
+// splitk_ws / splitk_bytes: caller-owned f32 scratch for the partial products of a K-split (small M, K >= 2048);
+// the split uses as many parts as fit (none when null).  The call allocates nothing.
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
-                         int* err_flag, cudaStream_t stream);
+                         int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream);
 
 // Gated delta rule over a prompt in chunks of 64 tokens (all 16 heads of one layer).
 // qkv: bf16 [S][6144] projection outputs q | k | v (the causal conv1d + SiLU and the L2 norms are applied inside);

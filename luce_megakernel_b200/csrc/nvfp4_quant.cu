@@ -1,4 +1,6 @@
-// NVFP4 weight quantisers for sm_100a, bit-exact to the reference's two formats.
+// NVFP4 weight quantisers for sm_100a, bit-exact to the reference's two formats.  Two arithmetics: the
+// reference binary's (its extension is built with --use_fast_math; kernels in nvfp4_quant_fastmath.cu, the
+// default) and IEEE (what the plain-C restatement computes); mk_set_quantize_arithmetic() selects.
 //
 //  format A (layer weights; reference: megakernel/kernel_gb10_nvfp4.cu:1764-1817)
 //    groups of `group_size` along K, scale = amax/6 as fp16 (1 for an all-zero group), code by the
@@ -20,91 +22,10 @@
 
 namespace {
 
-__device__ __forceinline__ float bf_at(const uint4& v, int i) {
-    const uint32_t w = (i < 2) ? v.x : (i < 4) ? v.y : (i < 6) ? v.z : v.w;
-    return __uint_as_float((i & 1) ? (w & 0xffff0000u) : (w << 16));
-}
-
-__device__ __forceinline__ unsigned code_thresholds(float x) {
-    const float ax = fabsf(x);
-    const unsigned mag = ax < 0.25f ? 0u : ax < 0.75f ? 1u : ax < 1.25f ? 2u : ax < 1.75f ? 3u
-                       : ax < 2.5f ? 4u : ax < 3.5f ? 5u : ax < 5.0f ? 6u : 7u;
-    return (x < 0.0f) ? (mag | 8u) : mag;
-}
-
-__global__ void quantize_a_kernel(const __nv_bfloat16* __restrict__ w, uint8_t* __restrict__ packed,
-                                  __half* __restrict__ scales, long long total_groups, int groups_per_row, int group) {
-    const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= total_groups) return;
-    const long long row = gid / groups_per_row;
-    const int g = (int)(gid - row * groups_per_row);
-    const size_t cols = (size_t)groups_per_row * group;
-    const __nv_bfloat16* src = w + row * cols + (size_t)g * group;
-    uint8_t* dst = packed + row * (cols / 2) + (size_t)g * (group / 2);
-    float amax = 0.0f;
-    const bool vec = (group % 8 == 0) && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0);
-    if (vec) {
-        for (int i = 0; i < group; i += 8) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + i));
-#pragma unroll
-            for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(bf_at(v, e)));
-        }
-    } else {
-        for (int i = 0; i < group; ++i) amax = fmaxf(amax, fabsf(__bfloat162float(src[i])));
-    }
-    const float scale = (amax > 0.0f) ? __fdiv_rn(amax, 6.0f) : 1.0f;
-    scales[gid] = __float2half_rn(scale);
-    if (amax == 0.0f) {
-        for (int i = 0; i < group / 2; ++i) dst[i] = 0;
-        return;
-    }
-    const float inv = __fdiv_rn(1.0f, scale);
-    if (vec) {
-        for (int i = 0; i < group; i += 8) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + i));
-            uint32_t out = 0;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) out |= code_thresholds(__fmul_rn(bf_at(v, e), inv)) << (4 * e);
-            if ((reinterpret_cast<uintptr_t>(dst + i / 2) & 3u) == 0) *reinterpret_cast<uint32_t*>(dst + i / 2) = out;
-            else for (int b = 0; b < 4; ++b) dst[i / 2 + b] = (uint8_t)(out >> (8 * b));
-        }
-    } else {
-        for (int i = 0; i < group; i += 2) {
-            const unsigned lo = code_thresholds(__fmul_rn(__bfloat162float(src[i]), inv));
-            const unsigned hi = code_thresholds(__fmul_rn(__bfloat162float(src[i + 1]), inv));
-            dst[i / 2] = (uint8_t)(lo | (hi << 4));
-        }
-    }
-}
-
-__global__ void quantize_b_kernel(const __nv_bfloat16* __restrict__ w, uint8_t* __restrict__ packed,
-                                  uint8_t* __restrict__ scales, int rows, int cols) {
-    const int blocks_per_row = cols / 16;
-    const long long bid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (bid >= (long long)rows * blocks_per_row) return;
-    const int row = (int)(bid / blocks_per_row), sc = (int)(bid % blocks_per_row);
-    const uint4* src = reinterpret_cast<const uint4*>(w + (size_t)row * cols + (size_t)sc * 16);
-    const uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
-    float amax = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fmaxf(fabsf(bf_at(v0, e)), fabsf(bf_at(v1, e))));
-    const float scale_f = fmaxf(__fmul_rn(amax, 1.0f / 6.0f), 1.0f / (float)(1 << 28));
-    const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale_f, __NV_SATFINITE, __NV_E4M3);
-    const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
-    const float dec = __half2float(*reinterpret_cast<const __half*>(&hr));
-    const float inv = (dec > 0.0f) ? __fdiv_rn(1.0f, dec) : 0.0f;
-    unsigned long long out = 0;
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-        const uint4& v = (p < 4) ? v0 : v1;
-        const float2 f = make_float2(__fmul_rn(bf_at(v, (2 * p) & 7), inv), __fmul_rn(bf_at(v, (2 * p + 1) & 7), inv));
-        const __nv_fp4x2_storage_t q = __nv_cvt_float2_to_fp4x2(f, __NV_E2M1, cudaRoundNearest);
-        out |= (unsigned long long)(uint8_t)q << (8 * p);
-    }
-    *reinterpret_cast<unsigned long long*>(packed + (size_t)row * (cols / 2) + (size_t)sc * 8) = out;
-    const size_t tile = (size_t)(row >> 7) * (cols / 64) + (sc >> 2);
-    scales[tile * 512 + (size_t)(row & 31) * 16 + (size_t)((row & 127) >> 5) * 4 + (sc & 3)] = (uint8_t)s8;
-}
+#define MK_QK(name) name
+#define MK_Q_DIV(a, b) __fdiv_rn((a), (b))
+#define MK_Q_MUL(a, b) __fmul_rn((a), (b))
+#include "nvfp4_quant_kernels.cuh"
 
 // ---- format B with a per-tensor scale ------------------------------------------------------------------------
 // s_t = amax(tensor) / (6 * 448) (1 for an all-zero tensor); block scale = E4M3(max((amax(block) / 6) / s_t, 2^-28));
@@ -158,12 +79,32 @@ __global__ void quantize_ts_kernel(const __nv_bfloat16* __restrict__ w, uint8_t*
     scales[tile * 512 + (size_t)(row & 31) * 16 + (size_t)((row & 127) >> 5) * 4 + (sc & 3)] = (uint8_t)s8;
 }
 
+// E4M3 block scales from the 128-row x 4-column tiles of the tensor-core layout to plain rows [rows][cols / 16]
+__global__ void scales_to_rows_kernel(const uint8_t* __restrict__ tiled, uint8_t* __restrict__ rows_out, int rows, int cols) {
+    const int spr = cols / 16;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * spr) return;
+    const int row = (int)(i / spr), sc = (int)(i % spr);
+    const size_t tile = (size_t)(row >> 7) * (cols / 64) + (sc >> 2);
+    rows_out[i] = tiled[tile * 512 + (size_t)(row & 31) * 16 + (size_t)((row & 127) >> 5) * 4 + (sc & 3)];
+}
+
 thread_local char g_qerr[160] = "";
+int g_quant_arith = 1;      // 1 = the reference binary's arithmetic (fast-math divide / reciprocal), 0 = IEEE
 int qfail(const char* m) { snprintf(g_qerr, sizeof(g_qerr), "%s", m); return MK_ERR_BAD_ARG; }
 
 }  // namespace
 
+namespace mk {
+// nvfp4_quant_fastmath.cu: the same two kernels compiled with --use_fast_math
+void launch_quantize_a_fastmath(const __nv_bfloat16* w, uint8_t* packed, __half* scales, long long total, int gpr, int group,
+                                unsigned blocks, int threads, cudaStream_t stream);
+void launch_quantize_b_fastmath(const __nv_bfloat16* w, uint8_t* packed, uint8_t* scales, int rows, int cols, unsigned blocks,
+                                int threads, cudaStream_t stream);
+}  // namespace mk
+
 extern "C" const char* mk_quantize_error(void) { return g_qerr; }
+extern "C" void mk_set_quantize_arithmetic(int reference_binary) { g_quant_arith = reference_binary ? 1 : 0; }
 
 extern "C" int launch_quantize_nvfp4_out(const void* weight, int rows, int cols, int group_size, void* packed_out,
                                          void* scales_out, cudaStream_t stream) {
@@ -174,8 +115,12 @@ extern "C" int launch_quantize_nvfp4_out(const void* weight, int rows, int cols,
     const long long total = (long long)rows * gpr;
     const int threads = 256;
     const unsigned blocks = (unsigned)((total + threads - 1) / threads);
-    quantize_a_kernel<<<blocks, threads, 0, stream>>>((const __nv_bfloat16*)weight, (uint8_t*)packed_out,
-                                                      (__half*)scales_out, total, gpr, group_size);
+    if (g_quant_arith)
+        mk::launch_quantize_a_fastmath((const __nv_bfloat16*)weight, (uint8_t*)packed_out, (__half*)scales_out, total, gpr,
+                                       group_size, blocks, threads, stream);
+    else
+        quantize_a_kernel<<<blocks, threads, 0, stream>>>((const __nv_bfloat16*)weight, (uint8_t*)packed_out,
+                                                          (__half*)scales_out, total, gpr, group_size);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_qerr, sizeof(g_qerr), "quantize launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
     return MK_OK;
@@ -191,8 +136,12 @@ extern "C" int launch_quantize_nvfp4_lm_out(const void* weight, int rows, int co
     const long long total = (long long)rows * (cols / 16);
     const int threads = 256;
     const unsigned blocks = (unsigned)((total + threads - 1) / threads);
-    quantize_b_kernel<<<blocks, threads, 0, stream>>>((const __nv_bfloat16*)weight, (uint8_t*)packed_out,
-                                                      (uint8_t*)scales_out, rows, cols);
+    if (g_quant_arith)
+        mk::launch_quantize_b_fastmath((const __nv_bfloat16*)weight, (uint8_t*)packed_out, (uint8_t*)scales_out, rows, cols,
+                                       blocks, threads, stream);
+    else
+        quantize_b_kernel<<<blocks, threads, 0, stream>>>((const __nv_bfloat16*)weight, (uint8_t*)packed_out,
+                                                          (uint8_t*)scales_out, rows, cols);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { snprintf(g_qerr, sizeof(g_qerr), "quantize launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
     return MK_OK;
@@ -217,5 +166,17 @@ extern "C" int mk_quantize_nvfp4_tensor_scale(const void* weight, int rows, int 
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) { snprintf(g_qerr, sizeof(g_qerr), "quantize launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
+    return MK_OK;
+}
+
+// Block scales of the tiled layout as plain rows: what the decode kernel streams (a row's scales contiguous).
+extern "C" int mk_nvfp4_scales_to_rows(const void* tiled_scales, int rows, int cols, void* rows_out, cudaStream_t stream) {
+    if (!tiled_scales || !rows_out) return qfail("null pointer argument");
+    if (rows <= 0 || rows % 128) return qfail("rows must be a positive multiple of 128");
+    if (cols <= 0 || cols % 64) return qfail("cols must be a positive multiple of 64");
+    const long long total = (long long)rows * (cols / 16);
+    scales_to_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>((const uint8_t*)tiled_scales, (uint8_t*)rows_out, rows, cols);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { snprintf(g_qerr, sizeof(g_qerr), "scale re-layout launch: %s", cudaGetErrorString(e)); return MK_ERR_CUDA; }
     return MK_OK;
 }

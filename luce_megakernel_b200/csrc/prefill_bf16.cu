@@ -444,19 +444,39 @@ struct PrefillWs {
     int *bidx = nullptr, *err = nullptr;
     void* chunk_scratch = nullptr;
     void* select_scratch = nullptr;
+    float* splitk = nullptr;        // f32 partial products of the K-split projections of short prompts
+    size_t splitk_bytes = 0;
 };
 PrefillWs g_pws[64];
+constexpr int SPLITK_MAX_TOKENS = 2048;     // longer prompts fill the SMs without a K-split
 constexpr int LM_BLOCKS = 1184;     // 8 resident blocks of 256 threads on each of 148 SMs
 
-cudaError_t ensure_ws(PrefillWs& w, int S) {
+// Grow-only.  Growing frees and reallocates every buffer, which (a) is illegal while `stream` is being captured
+// into a CUDA graph and (b) invalidates the device pointers baked into graphs captured earlier: the first is
+// refused here, the second is made visible through g_ws_generation (mk_prefill_workspace_generation()).
+// Callers that capture graphs size the workspace once with mk_prefill_reserve() and never grow it afterwards.
+unsigned g_ws_generation[64] = {0};
+cudaError_t ensure_ws(PrefillWs& w, int S, cudaStream_t stream = nullptr, bool check_capture = false) {
     if (S <= w.cap) return cudaSuccess;
+    if (check_capture) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+            return cudaErrorStreamCaptureUnsupported;
+    }
+    // work enqueued earlier (on any stream) may still use the buffers about to be freed
+    cudaError_t es = cudaDeviceSynchronize();
+    if (es != cudaSuccess) return es;
+    ++g_ws_generation[&w - g_pws];
     void** ptrs[] = {(void**)&w.hidden, (void**)&w.normed, (void**)&w.wide, (void**)&w.z, (void**)&w.act, (void**)&w.pre,
-                     (void**)&w.o, (void**)&w.beta, (void**)&w.decay, (void**)&w.kq, &w.chunk_scratch, &w.select_scratch};
+                     (void**)&w.o, (void**)&w.beta, (void**)&w.decay, (void**)&w.kq, &w.chunk_scratch, &w.select_scratch,
+                     (void**)&w.splitk};
+    w.splitk_bytes = 0;
     for (void** p : ptrs) { if (*p) cudaFree(*p); *p = nullptr; }
     const size_t s = (size_t)S;
     const size_t sizes[] = {s * HIDDEN * 2, s * HIDDEN * 2, s * 2 * INTER * 2, s * DN_V * 2, s * INTER * 2,
-                            s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 16, 16, 16, dn_chunked_scratch_bytes(S), block_select_scratch_bytes(S)};
-    for (int i = 0; i < 12; ++i) {
+                            s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 16, 16, 16, dn_chunked_scratch_bytes(S), block_select_scratch_bytes(S),
+                            (size_t)(S < SPLITK_MAX_TOKENS ? S : SPLITK_MAX_TOKENS) * 4 * HIDDEN * sizeof(float)};
+    for (int i = 0; i < 13; ++i) {
         cudaError_t e = cudaMalloc(ptrs[i], sizes[i]);
         if (e != cudaSuccess) { w.cap = 0; return e; }
     }
@@ -473,6 +493,7 @@ cudaError_t ensure_ws(PrefillWs& w, int S) {
         if (e != cudaSuccess) return e;
     }
     w.cap = S;
+    w.splitk_bytes = sizes[12];
     return cudaSuccess;
 }
 
@@ -499,6 +520,25 @@ int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
 }  // namespace mk
 
 extern "C" const char* mk_prefill_error(void) { return mk::g_perr; }
+extern "C" int mk_prefill_reserve(int max_tokens) {
+    using namespace mk;
+    if (max_tokens < 1) return pfail(MK_ERR_BAD_ARG, "max_tokens must be positive");
+    int dev = 0;
+    PF_CHECK(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return pfail(MK_ERR_BAD_ARG, "device index out of range");
+    PF_CHECK(ensure_ws(g_pws[dev], max_tokens < 64 ? 64 : max_tokens), "prefill workspace");
+    return MK_OK;
+}
+extern "C" int mk_prefill_workspace_tokens(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    return mk::g_pws[dev].cap;
+}
+extern "C" unsigned int mk_prefill_workspace_generation(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    return mk::g_ws_generation[dev];
+}
 extern "C" void mk_prefill_forget_tables(void) { for (auto& t : mk::g_tables) { t.src = nullptr; t.n = 0; } }
 extern "C" int mk_prefill_set_block_sparse(int enable, double top_frac, int window, int sink) {
     if (enable && (!(top_frac >= 0.0 && top_frac <= 1.0) || window < 1 || sink < 0)) return MK_ERR_BAD_ARG;
@@ -622,7 +662,7 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
                  void* conv_bufs, void* final_normed, void* hidden_bf16_out, int max_seq_len, int vocab, int dev,
                  cudaStream_t stream) {
     PrefillWs& w = g_pws[dev];
-    PF_CHECK(ensure_ws(w, seq_len), "prefill workspace");
+    PF_CHECK(ensure_ws(w, seq_len, stream, true), "prefill workspace (grow it with mk_prefill_reserve() before capturing a graph)");
     static bool scan_attr[64] = {false};
     if (!scan_attr[dev]) {
         PF_CHECK(cudaFuncSetAttribute(k_dn_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM), "scan smem");
@@ -631,7 +671,7 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
     const int S = seq_len;
     typedef __nv_bfloat16 bf;
     auto gemm = [&](const void* A, const void* W, void* C, const void* R, int N, int K, int ldc) {
-        return gemm_bf16_tn(A, W, C, R, S, N, K, K, ldc, w.err, stream);
+        return gemm_bf16_tn(A, W, C, R, S, N, K, K, ldc, w.err, w.splitk, w.splitk_bytes, stream);
     };
     const int wpb = 8;                                            // warps per 256-thread block
     auto blocks_for_warps = [&](long long nw) { return (unsigned)((nw + wpb - 1) / wpb); };

@@ -190,3 +190,132 @@ class Decoder:
         self._position = 0
         for t in (self._fa_k_cache, self._fa_v_cache, self._dn_states, self._conv_bufs):
             t.zero_()
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# NVFP4 with a per-tensor scale: e2m1 values in 16-element blocks, E4M3 block scales, one fp32 scale per matrix, for
+# every linear layer and the LM head.  The reference's NVFP4 decode has no such format (megakernel/model_nvfp4.py:
+# 249-337 packs 32-groups with fp16 scales for the layers); this is the additional format next to it.
+# ---------------------------------------------------------------------------------------------------------------
+
+def _quantize_matrix_nvfp4_ts(lib, w):
+    """bf16 [rows, cols] -> packed codes, block scales as plain rows [rows, cols/16], device float[1] tensor scale."""
+    rows, cols = w.shape
+    if rows % 128 or cols % 64:
+        raise ValueError("the tensor-scale NVFP4 format needs rows % 128 == 0 and cols % 64 == 0")
+    stream = ctypes.c_void_p(torch.cuda.current_stream(w.device).cuda_stream)
+    packed = torch.empty(rows, cols // 2, dtype=torch.uint8, device=w.device)
+    tiled = torch.zeros((rows // 128) * (cols // 64) * 512, dtype=torch.uint8, device=w.device)
+    ts = torch.zeros(4, dtype=torch.float32, device=w.device)        # 16 bytes: keeps later allocations aligned
+    if lib.mk_quantize_nvfp4_tensor_scale(_ptr(w), rows, cols, _ptr(packed), _ptr(tiled), _ptr(ts), stream) != 0:
+        raise RuntimeError("mk_quantize_nvfp4_tensor_scale failed")
+    srows = torch.empty(rows, cols // 16, dtype=torch.uint8, device=w.device)
+    if lib.mk_nvfp4_scales_to_rows(_ptr(tiled), rows, cols, _ptr(srows), stream) != 0:
+        raise RuntimeError("mk_nvfp4_scales_to_rows failed")
+    return {"packed": packed, "scales_tiled": tiled, "scales": srows, "tensor_scale": ts}
+
+
+def attach_nvfp4_ts_weights(weights):
+    """Adds weights["nvfp4_ts"]: per layer the slot list of the 224-byte table (a quantised matrix takes three
+    slots: packed, row-major block scales, tensor scale), plus the LM head's own packed copy."""
+    from . import lib as _lib
+    lib = _lib()
+    if "nvfp4_ts" in weights:
+        return weights
+    layers = []
+    for ld in weights["layer_data"]:
+        p = ld["ptrs"]
+
+        def q(i):
+            m = _quantize_matrix_nvfp4_ts(lib, p[i])
+            return [m["packed"], m["scales"], m["tensor_scale"]]
+        if ld["type"] == 1:
+            ptrs = [p[0]] + q(1) + q(2) + q(3) + [p[4], p[5]] + q(6) + [p[7]] + q(8) + q(9) + q(10)
+        else:
+            ptrs = [p[0]] + q(1) + q(2) + [p[3], p[4], p[5], p[6], p[7], p[8]] + q(9) + [p[10]] + q(11) + q(12) + q(13)
+        layers.append({"type": ld["type"], "ptrs": ptrs})
+    lm = _quantize_matrix_nvfp4_ts(lib, weights["lm_head_weight"])
+    weights["nvfp4_ts"] = {"layer_data": layers, "lm": lm}
+    return weights
+
+
+def _pack_layer_weights_nvfp4_ts(layer_data):
+    """Device blob of 224-byte entries {int type; int pad[3]; void* ptrs[26]}."""
+    entry = struct.Struct("<4i26Q")
+    assert entry.size == 224
+    blob = bytearray()
+    for ld in layer_data:
+        ptrs = [t.data_ptr() for t in ld["ptrs"]]
+        assert len(ptrs) == (25 if ld["type"] == 1 else 26)
+        blob += entry.pack(ld["type"], 0, 0, 0, *(ptrs + [0] * (26 - len(ptrs))))
+    return torch.frombuffer(blob, dtype=torch.uint8).cuda()
+
+
+class DecoderTS:
+    """Stateful greedy decoder over the tensor-scale NVFP4 weights (mk_decode_nvfp4_ts); same session interface as
+    Decoder above.  The prompt is fed token by token or prefilled in bf16 by a model.Decoder sharing the state."""
+
+    def __init__(self, weights, max_seq_len=2048):
+        from . import lib as _lib
+        self._lib = _lib()
+        self._weights = attach_nvfp4_ts_weights(weights)
+        nv = self._weights["nvfp4_ts"]
+        self.max_seq_len = int(max_seq_len)
+        self._embed_weight = weights["embed_weight"]
+        self._final_norm_weight = weights["final_norm_weight"]
+        self._lm = nv["lm"]
+        self.num_layers = len(nv["layer_data"])
+        self.vocab = int(self._embed_weight.shape[0])
+        self._layer_weights_packed = _pack_layer_weights_nvfp4_ts(nv["layer_data"])
+        dev = self._embed_weight.device
+        types = [ld["type"] for ld in nv["layer_data"]]
+        n_fa, n_dn = sum(types), len(types) - sum(types)
+        self._fa_k_cache = torch.zeros(max(n_fa, 1), FA_NUM_KV_HEADS, self.max_seq_len, FA_HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        self._fa_v_cache = torch.zeros_like(self._fa_k_cache)
+        self._dn_states = torch.zeros(max(n_dn, 1), DN_NUM_HEADS, DN_KEY_DIM, DN_VALUE_DIM, dtype=torch.float32, device=dev)
+        self._conv_bufs = torch.zeros(max(n_dn, 1), DN_CONV_CHANNELS, DN_CONV_KERNEL, dtype=torch.float32, device=dev)
+        self._hidden = torch.empty(HIDDEN_SIZE, dtype=torch.bfloat16, device=dev)
+        self._normalized = torch.empty(HIDDEN_SIZE, dtype=torch.float32, device=dev)
+        self._token_buffer = torch.empty(1, dtype=torch.int32, device=dev)
+        self._position = 0
+
+    def _check(self, rc):
+        if rc != 0:
+            raise RuntimeError(f"luce_megakernel_b200 error {rc}: {self._lib.mk_last_error_string().decode()}")
+
+    def step_many(self, token_id: int, steps: int) -> torch.Tensor:
+        """`steps` greedy steps in one launch; returns the int32 device tensor of tokens without synchronising."""
+        if steps < 1 or self._position + steps > self.max_seq_len:
+            raise ValueError("steps must be positive and position + steps within max_seq_len")
+        self._check(self._lib.mk_set_model_dims(self.num_layers, self.vocab))
+        out = torch.empty(steps, dtype=torch.int32, device=self._token_buffer.device)
+        self._token_buffer.fill_(int(token_id))
+        self._check(self._lib.mk_decode_nvfp4_ts(
+            _ptr(self._token_buffer), _ptr(out), ctypes.c_int(steps), _ptr(self._embed_weight),
+            _ptr(self._layer_weights_packed), _ptr(self._final_norm_weight), _ptr(self._lm["packed"]),
+            _ptr(self._lm["scales"]), _ptr(self._lm["tensor_scale"]), _ptr(self._fa_k_cache), _ptr(self._fa_v_cache),
+            _ptr(self._dn_states), _ptr(self._conv_bufs), _ptr(self._hidden), _ptr(self._normalized),
+            ctypes.c_int(self._position), ctypes.c_int(self.max_seq_len),
+            ctypes.c_void_p(torch.cuda.current_stream(self._embed_weight.device).cuda_stream)))
+        self._position += steps
+        return out
+
+    def step(self, token_id: int) -> int:
+        tok = int(self.step_many(token_id, 1).item())
+        if tok < 0:     # the launch gave up on a bounded wait and drained
+            self._lib.mk_device_status_detail.restype = ctypes.c_uint
+            raise RuntimeError("decode launch gave up on a device-side wait: status word 0x%08x"
+                               % self._lib.mk_device_status_detail())
+        return tok
+
+    def adopt_state(self, other):
+        """Take over the session state (caches, DeltaNet state, conv window, position) of another decoder over the
+        same model, e.g. a bf16 model.Decoder that has just prefilled the prompt."""
+        self._fa_k_cache, self._fa_v_cache = other._fa_k_cache, other._fa_v_cache
+        self._dn_states, self._conv_bufs = other._dn_states, other._conv_bufs
+        self.max_seq_len, self._position = other.max_seq_len, other._position
+
+    def reset(self):
+        self._position = 0
+        for t in (self._fa_k_cache, self._fa_v_cache, self._dn_states, self._conv_bufs):
+            t.zero_()

@@ -1,6 +1,12 @@
 """Builds the checker libraries under oracle/ (test infrastructure, never part of the product).
 
   oracle/libnvfp4_oracle.so        plain-C restatement of the reference's NVFP4 quantisers (gcc)
+  oracle/_ref/libref_nvfp4_quant.so the reference's two NVFP4 weight quantiser kernels with their launchers
+                                   (megakernel/kernel_gb10_nvfp4.cu: quantize_fp4_code, quantize_nvfp4_kernel,
+                                   quantize_nvfp4_lm_kernel, launch_quantize_nvfp4_out, launch_quantize_nvfp4_lm_out),
+                                   cut out of the checkout at build time into a generated translation unit under
+                                   oracle/_ref/ (the file as a whole refuses to compile below sm_120) and compiled
+                                   for sm_100a with the reference's own flags, --use_fast_math included.
   oracle/_ref/libref_megakernel.so the reference's own decode and prefill kernels (megakernel/kernel.cu,
                                    megakernel/prefill.cu), compiled for sm_100a from the sources where they lie
                                    in the reference checkout, with the flags of megakernel/setup.py and
@@ -8,7 +14,9 @@
                                    it as a second pin (token identity against the reference kernels) and skip
                                    when it is absent.  No reference source is copied.
 """
+import json
 import os
+import re
 import subprocess
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -28,8 +36,25 @@ def build_nvfp4(force=False):
     return NVFP4_LIB
 
 
-REF_DIR = os.environ.get("LUCE_REFERENCE_DIR", "/root/reference")
+def _reference_dir():
+    """The reference checkout: $LUCE_REFERENCE_DIR, else `reference_path` of the BASELINE.json next to this
+    package; None when neither names an existing directory (the prebuilt files are then used as they are)."""
+    cand = os.environ.get("LUCE_REFERENCE_DIR")
+    if not cand:
+        try:
+            cand = json.load(open(os.path.join(HERE, "..", "BASELINE.json"))).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    return cand if cand and os.path.isdir(cand) else None
+
+
+REF_DIR = _reference_dir() or ""
 REF_LIB = os.path.join(HERE, "_ref", "libref_megakernel.so")
+REF_QUANT_LIB = os.path.join(HERE, "_ref", "libref_nvfp4_quant.so")
+# flags of megakernel/setup.py:49-59 (the arch is this build's)
+REF_NVCC_FLAGS = ["-O3", "-gencode", "arch=compute_100a,code=sm_100a", "--use_fast_math", "-std=c++17",
+                  "-DNUM_BLOCKS=148", "-DBLOCK_SIZE=512", "-DLM_NUM_BLOCKS=512", "-DLM_BLOCK_SIZE=256",
+                  "-DMEGAKERNEL_DN_PHASE2_WMMA=0", "-DTARGET_SM=100"]
 
 
 def build_ref(force=False):
@@ -42,17 +67,58 @@ def build_ref(force=False):
         return REF_LIB
     os.makedirs(os.path.dirname(REF_LIB), exist_ok=True)
     nvcc = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-    cmd = [nvcc, "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "--use_fast_math", "-std=c++17",
-           "-DNUM_BLOCKS=148", "-DBLOCK_SIZE=512", "-DLM_NUM_BLOCKS=512", "-DLM_BLOCK_SIZE=256",
-           "-DMEGAKERNEL_DN_PHASE2_WMMA=0", "-DTARGET_SM=100", "-shared", "-Xcompiler", "-fPIC",
-           *srcs, "-lcublas", "-o", REF_LIB]
+    cmd = [nvcc, *REF_NVCC_FLAGS, "-shared", "-Xcompiler", "-fPIC", *srcs, "-lcublas", "-o", REF_LIB]
     subprocess.check_call(cmd)
     return REF_LIB
+
+
+def _cut_definition(text, start_pattern):
+    """The definition that starts at the first match of start_pattern, up to its closing brace."""
+    m = re.search(start_pattern, text, re.M)
+    if not m:
+        raise RuntimeError("not found in the reference source: " + start_pattern)
+    i = text.index("{", m.end())
+    depth, j = 0, i
+    while True:
+        depth += {"{": 1, "}": -1}.get(text[j], 0)
+        j += 1
+        if depth == 0:
+            return text[m.start():j]
+
+
+def build_ref_quant(force=False):
+    """The reference's NVFP4 quantisers as the reference builds them.  Returns the library path, or None when
+    neither the checkout nor a prebuilt library is there."""
+    src = os.path.join(REF_DIR, "megakernel", "kernel_gb10_nvfp4.cu")
+    if not os.path.exists(src):
+        return REF_QUANT_LIB if os.path.exists(REF_QUANT_LIB) else None
+    if not force and os.path.exists(REF_QUANT_LIB) and os.path.getmtime(src) <= os.path.getmtime(REF_QUANT_LIB) \
+            and os.path.getmtime(__file__) <= os.path.getmtime(REF_QUANT_LIB):
+        return REF_QUANT_LIB
+    os.makedirs(os.path.dirname(REF_QUANT_LIB), exist_ok=True)
+    text = open(src).read()
+    parts = ["// GENERATED at build time from the reference checkout (never committed): the two NVFP4 weight\n"
+             "// quantisers of megakernel/kernel_gb10_nvfp4.cu with their launchers, nothing else of that file.\n"
+             "#include <cuda_bf16.h>\n#include <cuda_fp8.h>\n#include <cuda_fp4.h>\n#include <cuda_fp16.h>\n"
+             "#include <cuda_runtime.h>\n#include <stdint.h>\n"]
+    parts += re.findall(r"^constexpr int LM_SCALE_(?:ROWS_PER_TILE|COLS_PER_TILE|BLOCK_K|K_PER_TILE|THREADS) = [^;]*;", text, re.M)
+    parts.append(_cut_definition(text, r"^__device__ __forceinline__ unsigned int quantize_fp4_code\("))
+    parts.append(_cut_definition(text, r"^__global__ void quantize_nvfp4_kernel\("))
+    parts.append(_cut_definition(text, r"^__global__ void __launch_bounds__\(LM_SCALE_THREADS\)\s*quantize_nvfp4_lm_kernel\("))
+    parts.append(_cut_definition(text, r'^extern "C" void launch_quantize_nvfp4_out\('))
+    parts.append(_cut_definition(text, r'^extern "C" void launch_quantize_nvfp4_lm_out\('))
+    gen = os.path.join(HERE, "_ref", "ref_nvfp4_quant_gen.cu")
+    with open(gen, "w") as f:
+        f.write("\n\n".join(parts) + "\n")
+    nvcc = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+    subprocess.check_call([nvcc, *REF_NVCC_FLAGS, "-shared", "-Xcompiler", "-fPIC", gen, "-o", REF_QUANT_LIB])
+    return REF_QUANT_LIB
 
 
 def build_all(force=False):
     build_nvfp4(force)
     build_ref(force)
+    build_ref_quant(force)
 
 
 if __name__ == "__main__":

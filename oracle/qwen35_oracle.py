@@ -306,15 +306,26 @@ class Oracle:
         L = pos0 + T
         K = st.k_cache[idx, :, :L].repeat_interleave(FA_Q_HEADS // FA_KV_HEADS, dim=0)   # [8, L, 256]
         V = st.v_cache[idx, :, :L].repeat_interleave(FA_Q_HEADS // FA_KV_HEADS, dim=0)
-        s = torch.einsum("thd,hld->htl", q, K) / math.sqrt(FA_HEAD_DIM)                  # kernel.cu:509,528-529
-        causal = torch.arange(L)[None, :] <= (pos0 + torch.arange(T))[:, None]
-        s = s.masked_fill(~causal[None], float("-inf"))
+        keep = None
         if self.block_sparse is not None and pos0 == 0 and T > 1:
             from . import block_sparse as BS
             keep = BS.select_for_heads(_bf(q).permute(1, 0, 2).numpy(), st.k_cache[idx, :, :L].numpy(), **self.block_sparse)
-            for hh in range(FA_Q_HEADS):
-                s[hh] = s[hh].masked_fill(~torch.from_numpy(BS.token_mask(keep[hh], L)), float("-inf"))
-        o = torch.einsum("htl,hld->thd", torch.softmax(s, dim=-1), V)
+        # query rows in slabs of 1024 (every row's softmax is independent; the slabs only bound the size of the
+        # score matrix for prompts of many thousand tokens)
+        o = torch.empty(T, FA_Q_HEADS, FA_HEAD_DIM)
+        for r0 in range(0, T, 1024):
+            r1 = min(T, r0 + 1024)
+            Lr = pos0 + r1                                                               # keys a row of this slab can see
+            s = torch.einsum("thd,hld->htl", q[r0:r1], K[:, :Lr]) / math.sqrt(FA_HEAD_DIM)   # kernel.cu:509,528-529
+            causal = torch.arange(Lr)[None, :] <= (pos0 + torch.arange(r0, r1))[:, None]
+            s = s.masked_fill(~causal[None], float("-inf"))
+            if keep is not None:
+                blk_q = torch.arange(r0, r1) // BS.BLOCK
+                blk_k = torch.arange(Lr) // BS.BLOCK
+                for hh in range(FA_Q_HEADS):
+                    kept = torch.from_numpy(keep[hh])[blk_q][:, blk_k]                   # [rows, Lr] bool
+                    s[hh] = s[hh].masked_fill(~kept, float("-inf"))
+            o[r0:r1] = torch.einsum("htl,hld->thd", torch.softmax(s, dim=-1), V[:, :Lr])
         o = o * torch.sigmoid(gate)                                                      # kernel.cu:551-556
         return o.reshape(T, FA_Q_SIZE)
 

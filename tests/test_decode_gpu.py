@@ -290,3 +290,34 @@ def test_full_size_model_prompt32_greedy16(norm_init):
             f"step {i}: token {tok} vs {tr.token} (margin {margin})"
         t = tr.token     # teacher forcing
     print(f"{norm_init}: worst logit error {worst:.4g}")
+
+
+def test_bounded_wait_runs_out_and_is_reported(dec_small, small_model):
+    """Failure detection without a hung launch: two small CTAs run the decode kernel's own poll on a word that
+    nobody writes, with the limit set to about a millisecond.  The wait runs out, the kernel returns, the status
+    word reads 1 (a poll of an exchanged activation gave up), the next decode call is refused with
+    MK_ERR_DEVICE_TIMEOUT, and after mk_clear_error() a step matches the oracle again."""
+    import luce_megakernel_b200 as L
+    lib = L.lib()
+    lib.mk_set_wait_limits.argtypes = [ctypes.c_ulonglong, ctypes.c_uint]
+    sd, orc = small_model("unit", "decode")
+    dec_small.reset()
+    tok = seeded_prompt(1, seed=12)[0]
+    assert lib.mk_device_status() == 0
+    lib.mk_set_wait_limits(2_000_000, 0)
+    try:
+        assert lib.mk_selftest_bounded_wait(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+        torch.cuda.synchronize()                       # the launch returns: nothing spins forever
+        assert lib.mk_device_status() == 1             # ST_GRID_TIMEOUT
+        with pytest.raises(RuntimeError, match="bounded device-side wait"):
+            dec_small.step(tok)
+        assert dec_small._position == 0                # the refused call did not advance the session
+    finally:
+        lib.mk_set_wait_limits(0, 0)
+        lib.mk_clear_error()
+    assert lib.mk_device_status() == 0
+    dec_small.reset()
+    got = dec_small.step(tok)
+    tr = orc.forward([tok], O.State.new(NL, MAXSEQ, V))
+    assert accept_token(got, tr.logits)
+    assert float((dec_small._hidden.float().cpu() - tr.hidden[-1][0]).abs().max()) <= 2e-2

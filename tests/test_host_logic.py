@@ -78,6 +78,28 @@ def test_bad_arguments_are_rejected_without_a_gpu():
     assert rc == 1
 
 
+def test_static_scratch_entry_rejects_misaligned_pointers_without_a_gpu():
+    """A pointer that is 4-byte but not 16-byte aligned (a sliced cache or embedding tensor) would make the kernel's
+    bulk copies and vector loads fault on the device: it must be refused on the host, before any CUDA call."""
+    lib = ctypes.CDLL(CORE_LIB_PATH)
+    lib.mk_decode_bf16_static_scratch_error.restype = ctypes.c_char_p
+    base = 0x7f0000000000                      # never dereferenced: validation fails first
+
+    def call(bad_index):
+        ptrs = [ctypes.c_void_p(base + 4096 * i + (4 if i == bad_index else 0)) for i in range(19)]
+        return lib.mk_decode_bf16_static_scratch(
+            ctypes.c_int(1), *ptrs, ctypes.c_float(1.0), ctypes.c_int(0), ctypes.c_int(16), ctypes.c_int(4),
+            ctypes.c_int(1024), ctypes.c_void_p(0))
+
+    # 1 embed, 2 layer table, 3 final norm, 4 lm head, 5/6 caches, 7 states, 8 conv, 9 hidden, 10-14 vector scratch, 17 normalized
+    for i in (1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 17):
+        assert call(i) == 1, f"argument {i} misaligned by 4 bytes was accepted"
+        assert b"16-byte" in lib.mk_decode_bf16_static_scratch_error()
+    ptrs = [ctypes.c_void_p(base + 4096 * i + (2 if i == 0 else 0)) for i in range(19)]
+    assert lib.mk_decode_bf16_static_scratch(ctypes.c_int(1), *ptrs, ctypes.c_float(1.0), ctypes.c_int(0), ctypes.c_int(16),
+                                             ctypes.c_int(4), ctypes.c_int(1024), ctypes.c_void_p(0)) == 1
+
+
 def test_missing_library_fails_loudly(monkeypatch):
     import luce_megakernel_b200 as L
     monkeypatch.setattr(L, "_lib", None)

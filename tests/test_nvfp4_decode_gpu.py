@@ -34,7 +34,13 @@ def bf16_ulp(x):
 def setup(small_model):
     from luce_megakernel_b200 import model as M, model_nvfp4 as MQ
     sd, _ = small_model("unit", "decode")
-    dec = MQ.Decoder(M.weights_from_state_dict(sd), max_seq_len=MAXSEQ)
+    import luce_megakernel_b200 as L
+    L.lib().mk_set_quantize_arithmetic(0)      # the oracle's weights come from the C restatement (IEEE divides)
+    try:
+        dec = MQ.Decoder(M.weights_from_state_dict(sd), max_seq_len=MAXSEQ)
+        torch.cuda.synchronize()
+    finally:
+        L.lib().mk_set_quantize_arithmetic(1)
     orc = O.Oracle(dequantised_state_dict(sd), rounding="decode")
     return dec, orc
 

@@ -19,7 +19,7 @@ What the runs show, and what is asserted:
   recurrence, conv, gates, attention, MLP, norms, LM head argmax) to the reference kernels.
 * This library, the oracle without the flag and the reference kernels agree at position 0.
 
-Reference throughput on this GPU is printed next to this library's (pytest -s).
+The reference kernels' throughput on the same GPU is measured by `bench.py --impl reference_gpu`.
 """
 import ctypes
 import math
@@ -30,94 +30,13 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-REF_LIB = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref", "libref_megakernel.so")
+from oracle.ref_kernels import REF_LIB, RefDecoder  # noqa: E402
+
 MAXSEQ = 1024
-
-
-def _p(t):
-    return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
 
 
 def bf16_ulp(x):
     return 2.0 ** (math.floor(math.log2(max(x, 1e-30))) - 7)
-
-
-class RefDecoder:
-    """The reference kernels behind their C entry points, with buffers sized as megakernel/model.py:208-240."""
-
-    def __init__(self, lib, mine):
-        self.lib, self.m = lib, mine
-        dev = "cuda"
-        bf, f32, i32 = torch.bfloat16, torch.float32, torch.int32
-        self.k = torch.zeros_like(mine._fa_k_cache)
-        self.v = torch.zeros_like(mine._fa_v_cache)
-        self.dn = torch.zeros_like(mine._dn_states)
-        self.conv = torch.zeros_like(mine._conv_bufs)
-        self.hidden = torch.zeros(1024, dtype=bf, device=dev)
-        self.act = torch.empty(1024 * 8 + 3584, dtype=f32, device=dev)
-        self.residual = torch.empty(1024, dtype=bf, device=dev)
-        self.qkv = torch.empty(6144, dtype=f32, device=dev)
-        self.kv = torch.empty(1024, dtype=f32, device=dev)
-        self.attn = torch.empty(2048, dtype=f32, device=dev)
-        self.mlp = torch.empty(3584, dtype=f32, device=dev)
-        self.z = torch.empty(2048, dtype=f32, device=dev)
-        self.beta = torch.empty(16, dtype=f32, device=dev)
-        self.alpha = torch.empty(16, dtype=f32, device=dev)
-        self.normalized = torch.empty(1024, dtype=f32, device=dev)
-        self.bar_c = torch.zeros(1, dtype=i32, device=dev)
-        self.bar_g = torch.zeros(1, dtype=i32, device=dev)
-        self.bmv = torch.empty(1024, dtype=f32, device=dev)
-        self.bmi = torch.empty(1024, dtype=i32, device=dev)
-        self.lm_sync = torch.zeros(1, dtype=i32, device=dev)
-        self.seen = torch.zeros(mine.vocab, dtype=f32, device=dev)
-        self.out = torch.zeros(1, dtype=i32, device=dev)
-        self.pos = 0
-
-    def reset(self):
-        for t in (self.k, self.v, self.dn, self.conv):
-            t.zero_()
-        self.pos = 0
-
-    def step_async(self, tok):
-        m = self.m
-        self.lib.launch_decode(
-            ctypes.c_int(int(tok)), _p(self.out), _p(m._embed_weight), _p(m._layer_weights_packed), _p(m._final_norm_weight),
-            _p(m._lm_head_weight), _p(self.k), _p(self.v), _p(self.dn), _p(self.conv), _p(self.hidden), _p(self.act),
-            _p(self.residual), _p(self.qkv), _p(self.kv), _p(self.attn), _p(self.mlp), _p(self.z), _p(self.beta),
-            _p(self.alpha), _p(self.normalized), _p(self.bar_c), _p(self.bar_g), _p(self.bmv), _p(self.bmi),
-            _p(self.lm_sync), _p(self.seen), ctypes.c_float(1.0), ctypes.c_int(self.pos), ctypes.c_int(MAXSEQ),
-            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-        self.pos += 1
-
-    def step(self, tok):
-        self.step_async(tok)
-        return int(self.out.item())
-
-    def prefill(self, ids):
-        """Scratch sizes: megakernel/final_bench.py:52-63 and megakernel/model.py:262-272, except the two
-        projection buffers: the reference writes the fused gate/up output ([S, 7168], prefill.cu:1269) into a
-        buffer its callers size for 6144 columns, so they are made 7168 wide here."""
-        m, S = self.m, int(ids.numel())
-        bf, f32, i32, dev = torch.bfloat16, torch.float32, torch.int32, "cuda"
-        mx, spad = 7168, ((S + 31) // 32) * 32
-        b = dict(hidden=torch.empty(S * 1024, dtype=bf, device=dev), residual=torch.empty(S * 1024, dtype=bf, device=dev),
-                 normalized=torch.empty(S * 1024, dtype=bf, device=dev), proj=torch.empty(S * mx, dtype=bf, device=dev),
-                 proj2=torch.empty(S * mx, dtype=bf, device=dev), attn=torch.empty(S * 2048, dtype=bf, device=dev),
-                 mlp=torch.empty(S * 3584, dtype=bf, device=dev), dn_out=torch.empty(S * 2048, dtype=bf, device=dev),
-                 beta=torch.empty(S * 16, dtype=f32, device=dev), alpha=torch.empty(S * 16, dtype=f32, device=dev),
-                 pre=torch.empty(S * 6144, dtype=f32, device=dev), u=torch.empty(spad * 16 * 128, dtype=f32, device=dev),
-                 w=torch.empty(spad * 16 * 128, dtype=f32, device=dev), cs=torch.empty(spad * 16, dtype=f32, device=dev),
-                 fn=torch.empty(1024, dtype=bf, device=dev), hout=torch.empty(1024, dtype=bf, device=dev))
-        self._pf = b
-        self.lib.launch_prefill_bf16(
-            _p(ids), ctypes.c_int(S), _p(self.out), _p(m._embed_weight), _p(m._layer_weights_packed), _p(m._final_norm_weight),
-            _p(m._lm_head_weight), _p(self.k), _p(self.v), _p(self.dn), _p(self.conv), _p(b["hidden"]), _p(b["residual"]),
-            _p(b["normalized"]), _p(b["proj"]), _p(b["proj2"]), _p(b["attn"]), _p(b["mlp"]), _p(b["dn_out"]), _p(b["beta"]),
-            _p(b["alpha"]), _p(b["pre"]), _p(b["u"]), _p(b["w"]), _p(b["cs"]), _p(m._fused_fa_qkv), _p(m._fused_gate_up),
-            _p(b["fn"]), _p(b["hout"]), _p(self.bmv), _p(self.bmi), ctypes.c_int(MAXSEQ),
-            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-        self.pos = S
-        return int(self.out.item())
 
 
 @pytest.fixture(scope="module")
@@ -130,7 +49,7 @@ def pair():
     sd = O.init_weights(0, 24, O.VOCAB, norm_init="unit")
     mine = M.Decoder(weights=M.weights_from_state_dict(sd), max_seq_len=MAXSEQ, api="cabi")
     mine._sd = sd
-    return mine, RefDecoder(lib, mine)
+    return mine, RefDecoder(lib, mine, MAXSEQ)
 
 
 def seeded(n, seed, vocab):
@@ -230,30 +149,3 @@ def test_reference_prefill_layers_before_first_attention(pair):
         print(f"\nprefill S={S}, DeltaNet layer {l}: state diff {es:.6f} (rms {rms:.5f}), conv diff {ec:.5f}")
         assert (es <= 5e-5 and ec <= 1e-5) if l == 0 else (es <= 2e-3 and ec <= 0.1)
     assert float((mine._fa_v_cache[0].float()[:, :S] - ref.v[0].float()[:, :S]).abs().max()) <= 0.07
-
-
-def test_reference_throughput_beside_ours(pair):
-    """Not a parity check: prints the reference kernels' speed on this GPU next to this library's."""
-    mine, ref = pair
-    S = 520
-    ids = torch.tensor(seeded(S, 3, mine.vocab), dtype=torch.int32, device="cuda")
-    res = {}
-    for name, d in (("reference", ref), ("this library", mine)):
-        d.reset(); d.prefill(ids)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(3):
-            if d is mine:
-                d._position = 0
-            d.prefill(ids)
-        e1.record(); torch.cuda.synchronize()
-        pp = S / (e0.elapsed_time(e1) / 3e3)
-        t = 11
-        e0.record()
-        for _ in range(128):
-            t = d.step(t)
-        e1.record(); torch.cuda.synchronize()
-        tg = 128 / (e0.elapsed_time(e1) / 1e3)
-        res[name] = (pp, tg)
-        print(f"\n{name}: pp520 {pp:.0f} tok/s, tg128 (host token loop) {tg:.0f} tok/s")
-    assert res["this library"][1] > 0

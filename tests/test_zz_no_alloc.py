@@ -78,3 +78,24 @@ def test_static_scratch_entry_rejects_sizes_beyond_its_maximum():
     assert b"maximum" in lib.mk_decode_bf16_static_scratch_error()
     assert call(NL, MAXSEQ) == 1
     torch.cuda.synchronize()
+
+
+def test_static_scratch_entry_allocates_nothing_and_reports_its_status():
+    """The property the entry point exists for: free device memory is the same before and after further calls
+    (the first call only resolves the array's address; nothing here calls launch_decode on this decoder), and the
+    status word of a normal launch reads 0 through the allocation-free status query."""
+    dec = _decoder()
+    status = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+    _static_step(dec, 5)                                      # first call: one-time set-up for this device
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    toks = []
+    for t in (9, 33, 2):
+        toks.append(_static_step(dec, t))
+        rc = dec._lib.mk_decode_bf16_static_scratch_status(ctypes.c_void_p(status.data_ptr()), dec._stream())
+        assert rc == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, f"free device memory changed by {free0 - free1} bytes across static-scratch calls"
+    assert int(status.item()) == 0
+    assert all(0 <= t < V for t in toks)
