@@ -372,10 +372,6 @@ void mk_clear_error(void);
  *   value cuts a call into launches of at most that many steps (1 = one launch per token, as the reference's
  *   launch_decode_many_nvfp4 does, megakernel/kernel_gb10_nvfp4.cu:2192-2257).  For measurements; default 0. */
 void mk_set_decode_steps_per_launch(int steps);
-/* How a thread of the decode kernel waits for an activation another CTA has not published yet: 1 (default) keeps
- * three loads of the word in flight, a third of an L2 round trip apart, so that the value is seen at most ~0.2 us after
- * it lands; 0 issues one load at a time (seen up to a whole round trip late).  For measurements. */
-void mk_set_decode_poll_pipelining(int enable);
 
 /* Limits of the decode kernel's device-side waits.  The reference's grid barrier spins without a limit
  * (megakernel/kernel.cu:128-137); here every wait is bounded and a launch that gives up drains, writes -1 as its
@@ -388,6 +384,20 @@ void mk_set_decode_poll_pipelining(int enable);
  * can be exercised without a launch that hangs: set a short limit first (1e6 cycles is about 0.5 ms). */
 void mk_set_wait_limits(unsigned long long poll_cycles, unsigned int mbar_tries);
 int mk_selftest_bounded_wait(cudaStream_t stream);
+
+/* Sampling at the LM-head boundary.  The reference decodes greedily; its hook here is the repetition penalty on the
+ * logits before the argmax (megakernel/kernel.cu:793-795).
+ * mk_set_logits_buffer: every decode entry point of this library also stores the step's logits (f32 [vocab], after the
+ *   penalty; the last step's for a multi-step call) into `logits` while it takes the argmax; NULL switches it off.
+ * mk_sample_top_k: draws a token from softmax(logits / temperature) restricted to the top_k largest logits (ties to
+ *   the lower index; top_k <= 0 keeps everything; temperature <= 0 or top_k == 1 is the argmax) as
+ *   argmax_i( logit_i / temperature - log(-log(u_i)) ) with u_i a hash of (seed, counter, i): exact categorical
+ *   sampling, reproducible from (seed, counter).  token_out: device int32[1], e.g. the token buffer the next
+ *   launch_decode_nvfp4 / mk_decode_many_bf16 call reads its input from. */
+void mk_set_logits_buffer(float *logits);
+int mk_sample_top_k(const float *logits, int n, float temperature, int top_k, unsigned long long seed,
+                    unsigned long long counter, int *token_out, cudaStream_t stream);
+const char *mk_sample_error(void);
 
 /* Optional per-phase timeline: `buf` is a device buffer of
  * query_max_safe_decode_blocks() * slots_per_cta uint64; thread 0 of every CTA appends the global

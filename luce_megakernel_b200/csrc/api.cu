@@ -22,12 +22,12 @@ DeviceState g_dev[MAX_DEVICES];
 int g_blocks_override = 0;
 int g_num_layers = mk::MAX_LAYERS;
 int g_vocab = mk::DEFAULT_VOCAB;
+float* g_logits = nullptr;
 unsigned long long* g_trace = nullptr;
 int g_trace_slots = 0;
 unsigned long long g_poll_limit = mk::DEFAULT_POLL_LIMIT_CYCLES;
 uint32_t g_mbar_tries = mk::DEFAULT_MBAR_LIMIT_TRIES;
 int g_steps_per_launch = 0;     // 0 = a multi-step call is one launch
-int g_poll_pipelined = 1;
 thread_local char g_err[256] = "";
 
 int set_err(int code, const char* what, cudaError_t e = cudaSuccess) {
@@ -119,8 +119,8 @@ mk::DecodeParams make_params(const DecodeCall& a, DeviceState& d) {
     p.position = a.position; p.max_seq_len = a.max_seq_len;
     p.num_layers = g_num_layers; p.vocab = g_vocab;
     p.ws = d.ws; p.host_status = d.host_status_dev; p.trace = g_trace; p.trace_slots = g_trace_slots;
-    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries; p.poll_pipelined = g_poll_pipelined;
-    p.steps = 1;
+    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries;
+    p.steps = 1; p.logits_out = g_logits;
     return p;
 }
 
@@ -235,8 +235,8 @@ static int decode_nvfp4_common(const int* token_in, int* token_out, int* token_f
     p.token_ptr = token_in; p.token_val = 0; p.out_token = token_out; p.token_feedback = token_feedback;
     p.position = position; p.max_seq_len = max_seq_len; p.num_layers = g_num_layers; p.vocab = g_vocab;
     p.ws = d->ws; p.host_status = d->host_status_dev; p.trace = nullptr; p.trace_slots = 0;
-    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries; p.poll_pipelined = g_poll_pipelined;
-    p.steps = steps;
+    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries;
+    p.steps = steps; p.logits_out = g_logits;
     mk::fill_rope(p);
     cudaError_t e = mk::launch_decode_kernel(p, decode_grid(*d), stream);
     if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
@@ -326,9 +326,9 @@ int mk_decode_nvfp4_ts(
     p.seen_mask = nullptr; p.rep_penalty = 1.0f;
     p.token_ptr = token_buffer; p.token_val = 0; p.out_token = output_tokens; p.token_feedback = token_buffer;
     p.position = position; p.max_seq_len = max_seq_len; p.num_layers = g_num_layers; p.vocab = g_vocab;
-    p.ws = d->ws; p.host_status = d->host_status_dev; p.trace = nullptr; p.trace_slots = 0;
-    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries; p.poll_pipelined = g_poll_pipelined;
-    p.steps = steps;
+    p.ws = d->ws; p.host_status = d->host_status_dev; p.trace = g_trace; p.trace_slots = g_trace_slots;
+    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries;
+    p.steps = steps; p.logits_out = g_logits;
     mk::fill_rope(p);
     cudaError_t e = mk::launch_decode_kernel(p, decode_grid(*d), stream);
     if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
@@ -395,7 +395,6 @@ int mk_gemm_bf16_tn(const void* A, const void* W, void* C, const void* residual,
 }
 
 void mk_set_decode_steps_per_launch(int steps) { g_steps_per_launch = steps > 0 ? steps : 0; }
-void mk_set_decode_poll_pipelining(int enable) { g_poll_pipelined = enable ? 1 : 0; }
 
 void mk_set_wait_limits(unsigned long long poll_cycles, unsigned int mbar_tries) {
     g_poll_limit = poll_cycles ? poll_cycles : mk::DEFAULT_POLL_LIMIT_CYCLES;
@@ -409,11 +408,13 @@ int mk_selftest_bounded_wait(cudaStream_t stream) {
     mk::DecodeParams p;
     memset(&p, 0, sizeof(p));
     p.ws = d->ws; p.host_status = d->host_status_dev;
-    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries; p.poll_pipelined = g_poll_pipelined;
+    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries;
     cudaError_t e = mk::launch_wait_selftest(p, stream);
     if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "wait self-test launch", e);
     return MK_OK;
 }
+
+void mk_set_logits_buffer(float* logits) { g_logits = logits; }
 
 void mk_set_trace_buffer(unsigned long long* buf, int slots_per_cta) {
     g_trace = (buf && slots_per_cta > 0) ? buf : nullptr;

@@ -111,6 +111,16 @@ namespace {
 }  // namespace
 }  // namespace traced
 
+namespace traced_ts {
+namespace {
+#define MK_TRACE 1
+#define MK_WFMT 2
+#include "decode_body.cuh"
+#undef MK_WFMT
+#undef MK_TRACE
+}  // namespace
+}  // namespace traced_ts
+
 size_t decode_smem_bytes() { return SMEM_BYTES; }
 
 int decode_max_grid() {
@@ -144,11 +154,14 @@ cudaError_t launch_decode_kernel(const DecodeParams& p, int grid, cudaStream_t s
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(nvfp4ts::decode_megakernel_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(traced_ts::decode_megakernel_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
         attr_done[dev] = true;
     }
     if (grid < MIN_GRID || grid > MAX_GRID) return cudaErrorInvalidConfiguration;
     void* args[] = {(void*)&p};
-    const void* fn = p.wfmt == 2 ? (const void*)nvfp4ts::decode_megakernel_bf16
+    const void* fn = (p.wfmt == 2 && p.trace) ? (const void*)traced_ts::decode_megakernel_bf16
+                   : p.wfmt == 2 ? (const void*)nvfp4ts::decode_megakernel_bf16
                    : p.wfmt == 1 ? (const void*)nvfp4::decode_megakernel_bf16
                    : p.trace   ? (const void*)traced::decode_megakernel_bf16
                                : (const void*)plain::decode_megakernel_bf16;

@@ -364,8 +364,11 @@ __device__ __forceinline__ void ld_word2(const unsigned long long* p, unsigned l
     asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-// Slow path of a poll: bounded by P.poll_limit_cycles (about 2 s of SM clock by default), gives up at once if
-// another CTA gave up.
+// (Tried and dropped, both slower on B200: keeping two or three loads of a polled word in flight, staggered by a
+// fraction of an L2 round trip, and moving the retry loops out of line -- a call from this 96-register kernel
+// sends the caller's live registers through local memory, and the retry loop is the common case, not the rare one.)
+// Slow path of a poll (every 1024 failed tries): bounded by P.poll_limit_cycles (about 2 s of SM clock by
+// default), gives up at once if another CTA gave up.
 __device__ __forceinline__ bool poll_give_up(const DecodeParams& P, Ctx& c, uint64_t& t0) {
     if (c.misc[MISC_ABORT]) return true;
     const uint64_t now = (uint64_t)clock64();
@@ -377,88 +380,17 @@ __device__ __forceinline__ bool poll_give_up(const DecodeParams& P, Ctx& c, uint
     return false;
 }
 
-// A poll that failed once costs a full L2 round trip (~0.7 us) before the next look at the word; with the loads issued
-// one after the other a value that lands just after a look is seen a whole round trip late.  The waits below keep
-// several loads in flight, issued a fraction of a round trip apart, and re-issue each one as it returns: the word is
-// sampled every ~0.2 us at two or three times the (small) polling traffic.  Out of line: the waits are inlined in
-// dozens of places and this part runs only while the thread has nothing else to do.  P.poll_pipelined = 0 selects
-// the plain loop (one load at a time).  The stagger is a spin on the SM clock: __nanosleep() overshoots by a
-// multiple of what is asked for at this scale.
-constexpr unsigned POLL_STAGGER_CLK = 400;
-__device__ __forceinline__ void spin_clocks(unsigned n) {
-    const unsigned t0 = (unsigned)clock();
-    while ((unsigned)clock() - t0 < n) {}
-}
-__device__ __forceinline__ bool wait_give_up(volatile int* misc, DecodeWorkspace* ws, unsigned long long limit, uint32_t where,
-                                             uint64_t& t0) {
-    if (misc[MISC_ABORT]) return true;
-    const uint64_t now = (uint64_t)clock64();
-    if (t0 == 0) t0 = now;
-    if (now - t0 > limit || *((volatile uint32_t*)&ws->abort_flag) != 0u) {
-        if (misc[MISC_ABORT] == 0) misc[MISC_DETAIL] = (int)where;
-        misc[MISC_ABORT] = (int)ST_GRID_TIMEOUT;
-        ws->abort_flag = 1u;
-        return true;
-    }
-    return false;
-}
-__device__ __noinline__ unsigned long long poll1_wait(const unsigned long long* p, uint32_t epoch, volatile int* misc,
-                                                      DecodeWorkspace* ws, unsigned long long limit, uint32_t where, int pipelined) {
-    uint64_t t0 = 0;
-    uint32_t n = 0;
-    if (!pipelined) {
-        while (true) {
-            const unsigned long long w = ld_word(p);
-            if ((uint32_t)(w >> 32) == epoch) return w;
-            if ((++n & 255u) == 0 && wait_give_up(misc, ws, limit, where, t0)) return w;
-        }
-    }
-    unsigned long long w0 = ld_word(p);
-    spin_clocks(POLL_STAGGER_CLK);
-    unsigned long long w1 = ld_word(p);
-    spin_clocks(POLL_STAGGER_CLK);
-    unsigned long long w2 = ld_word(p);
-    while (true) {
-        if ((uint32_t)(w0 >> 32) == epoch) return w0;
-        w0 = ld_word(p);
-        if ((uint32_t)(w1 >> 32) == epoch) return w1;
-        w1 = ld_word(p);
-        if ((uint32_t)(w2 >> 32) == epoch) return w2;
-        w2 = ld_word(p);
-        if ((++n & 127u) == 0 && wait_give_up(misc, ws, limit, where, t0)) return w0;
-    }
-}
-__device__ __noinline__ ulonglong2 poll2_wait(const unsigned long long* p, uint32_t epoch, volatile int* misc,
-                                              DecodeWorkspace* ws, unsigned long long limit, uint32_t where, int pipelined) {
-    uint64_t t0 = 0;
-    uint32_t n = 0;
-    unsigned long long a0, b0, a1, b1, a2, b2;
-    if (!pipelined) {
-        while (true) {
-            ld_word2(p, a0, b0);
-            if ((uint32_t)(a0 >> 32) == epoch && (uint32_t)(b0 >> 32) == epoch) return make_ulonglong2(a0, b0);
-            if ((++n & 255u) == 0 && wait_give_up(misc, ws, limit, where, t0)) return make_ulonglong2(a0, b0);
-        }
-    }
-    ld_word2(p, a0, b0);
-    spin_clocks(POLL_STAGGER_CLK);
-    ld_word2(p, a1, b1);
-    spin_clocks(POLL_STAGGER_CLK);
-    ld_word2(p, a2, b2);
-    while (true) {
-        if ((uint32_t)(a0 >> 32) == epoch && (uint32_t)(b0 >> 32) == epoch) return make_ulonglong2(a0, b0);
-        ld_word2(p, a0, b0);
-        if ((uint32_t)(a1 >> 32) == epoch && (uint32_t)(b1 >> 32) == epoch) return make_ulonglong2(a1, b1);
-        ld_word2(p, a1, b1);
-        if ((uint32_t)(a2 >> 32) == epoch && (uint32_t)(b2 >> 32) == epoch) return make_ulonglong2(a2, b2);
-        ld_word2(p, a2, b2);
-        if ((++n & 127u) == 0 && wait_give_up(misc, ws, limit, where, t0)) return make_ulonglong2(a0, b0);
-    }
-}
-
 __device__ __forceinline__ float poll1(const DecodeParams& P, Ctx& c, const unsigned long long* p, uint32_t epoch) {
     unsigned long long w = ld_word(p);
-    if ((uint32_t)(w >> 32) != epoch) w = poll1_wait(p, epoch, c.misc, P.ws, P.poll_limit_cycles, c.where | ((uint32_t)c.step << 16), P.poll_pipelined);
+    if ((uint32_t)(w >> 32) != epoch) {
+        uint64_t t0 = 0;
+        uint32_t n = 0;
+        do {
+            if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
+            MK_POLL_BACKOFF();
+            w = ld_word(p);
+        } while ((uint32_t)(w >> 32) != epoch);
+    }
     return __uint_as_float((uint32_t)w);
 }
 
@@ -467,52 +399,35 @@ __device__ __forceinline__ float2 poll2(const DecodeParams& P, Ctx& c, const uns
     unsigned long long a, b;
     ld_word2(p, a, b);
     if ((uint32_t)(a >> 32) != epoch || (uint32_t)(b >> 32) != epoch) {
-        const ulonglong2 r = poll2_wait(p, epoch, c.misc, P.ws, P.poll_limit_cycles, c.where | ((uint32_t)c.step << 16), P.poll_pipelined);
-        a = r.x; b = r.y;
+        uint64_t t0 = 0;
+        uint32_t n = 0;
+        do {
+            if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
+            MK_POLL_BACKOFF();
+            ld_word2(p, a, b);
+        } while ((uint32_t)(a >> 32) != epoch || (uint32_t)(b >> 32) != epoch);
     }
     return make_float2(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b));
 }
 
-// Batched polls: all loads of a round are issued before any epoch is checked, so the N words cost one L2 round
-// trip instead of N; after a failed first round two rounds are kept in flight half a round trip apart.
+// Batched polls: all loads are issued before any epoch is checked, so the N words cost one
+// L2 round trip instead of N.  W = words per load (1 or 2); words of one load are consecutive.
 template <int N>
 __device__ __forceinline__ void poll1_batch(const DecodeParams& P, Ctx& c, const unsigned long long* const (&p)[N],
                                             uint32_t epoch, float (&out)[N]) {
     unsigned long long w[N];
-#pragma unroll
-    for (int i = 0; i < N; ++i) w[i] = ld_word(p[i]);
-    bool ok = true;
-#pragma unroll
-    for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(w[i] >> 32) == epoch);
-    if (!ok) {
-        unsigned long long v[N];
+    uint64_t t0 = 0;
+    uint32_t n = 0;
+#pragma unroll 1
+    while (true) {
 #pragma unroll
         for (int i = 0; i < N; ++i) w[i] = ld_word(p[i]);
-        if (P.poll_pipelined) spin_clocks(POLL_STAGGER_CLK + POLL_STAGGER_CLK / 2);
+        bool ok = true;
 #pragma unroll
-        for (int i = 0; i < N; ++i) v[i] = ld_word(p[i]);
-        uint64_t t0 = 0;
-        uint32_t n = 0;
-#pragma unroll 1
-        while (true) {
-            ok = true;
-#pragma unroll
-            for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(w[i] >> 32) == epoch);
-            if (ok) break;
-#pragma unroll
-            for (int i = 0; i < N; ++i) w[i] = ld_word(p[i]);
-            ok = true;
-#pragma unroll
-            for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(v[i] >> 32) == epoch);
-            if (ok) {
-#pragma unroll
-                for (int i = 0; i < N; ++i) w[i] = v[i];
-                break;
-            }
-#pragma unroll
-            for (int i = 0; i < N; ++i) v[i] = ld_word(p[i]);
-            if ((++n & 255u) == 0 && poll_give_up(P, c, t0)) break;
-        }
+        for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(w[i] >> 32) == epoch);
+        if (ok) break;
+        if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
+        MK_POLL_BACKOFF();
     }
 #pragma unroll
     for (int i = 0; i < N; ++i) out[i] = __uint_as_float((uint32_t)w[i]);
@@ -522,40 +437,18 @@ template <int N>
 __device__ __forceinline__ void poll2_batch(const DecodeParams& P, Ctx& c, const unsigned long long* const (&p)[N],
                                             uint32_t epoch, float2 (&out)[N]) {
     unsigned long long a[N], b[N];
-#pragma unroll
-    for (int i = 0; i < N; ++i) ld_word2(p[i], a[i], b[i]);
-    bool ok = true;
-#pragma unroll
-    for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(a[i] >> 32) == epoch) && ((uint32_t)(b[i] >> 32) == epoch);
-    if (!ok) {
-        unsigned long long x[N], y[N];
+    uint64_t t0 = 0;
+    uint32_t n = 0;
+#pragma unroll 1
+    while (true) {
 #pragma unroll
         for (int i = 0; i < N; ++i) ld_word2(p[i], a[i], b[i]);
-        if (P.poll_pipelined) spin_clocks(POLL_STAGGER_CLK + POLL_STAGGER_CLK / 2);
+        bool ok = true;
 #pragma unroll
-        for (int i = 0; i < N; ++i) ld_word2(p[i], x[i], y[i]);
-        uint64_t t0 = 0;
-        uint32_t n = 0;
-#pragma unroll 1
-        while (true) {
-            ok = true;
-#pragma unroll
-            for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(a[i] >> 32) == epoch) && ((uint32_t)(b[i] >> 32) == epoch);
-            if (ok) break;
-#pragma unroll
-            for (int i = 0; i < N; ++i) ld_word2(p[i], a[i], b[i]);
-            ok = true;
-#pragma unroll
-            for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(x[i] >> 32) == epoch) && ((uint32_t)(y[i] >> 32) == epoch);
-            if (ok) {
-#pragma unroll
-                for (int i = 0; i < N; ++i) { a[i] = x[i]; b[i] = y[i]; }
-                break;
-            }
-#pragma unroll
-            for (int i = 0; i < N; ++i) ld_word2(p[i], x[i], y[i]);
-            if ((++n & 255u) == 0 && poll_give_up(P, c, t0)) break;
-        }
+        for (int i = 0; i < N; ++i) ok = ok && ((uint32_t)(a[i] >> 32) == epoch) && ((uint32_t)(b[i] >> 32) == epoch);
+        if (ok) break;
+        if ((++n & 1023u) == 0 && poll_give_up(P, c, t0)) break;
+        MK_POLL_BACKOFF();
     }
 #pragma unroll
     for (int i = 0; i < N; ++i) out[i] = make_float2(__uint_as_float((uint32_t)a[i]), __uint_as_float((uint32_t)b[i]));
@@ -572,6 +465,15 @@ __device__ __forceinline__ uint32_t chunk_runs(const DecodeParams& P, Ctx& c, in
                                                uint32_t& run_bytes) {
     uint32_t bytes = chunk_slot_src(type, lw, P, g, q, c.lane, c.G, idx, src, dst_off, c.cta, pos);
     if (bytes && (((uintptr_t)src) & 15u)) { fail(P, c, ST_MISALIGNED); bytes = 0; }
+#if MK_WFMT == 2
+    // every lane already describes a whole run (a row group, or a matrix's scale rows) of its own size: no merging
+    // (two matrices that happen to lie back to back in memory must not be taken for one run of equal pieces)
+    if (type != T_FA_ATT) {
+        head = bytes != 0;
+        run_bytes = bytes;
+        return bytes;
+    }
+#endif
     const unsigned long long prev_src = __shfl_up_sync(0xffffffffu, (unsigned long long)(uintptr_t)src, 1);
     const uint32_t prev_bytes = __shfl_up_sync(0xffffffffu, bytes, 1);
     const uint32_t prev_dst = __shfl_up_sync(0xffffffffu, dst_off, 1);
@@ -707,12 +609,11 @@ __device__ __forceinline__ void load_bfrags(const uint32_t* xw, int lane, uint32
 // `kofs` bytes into each row.  ROWS = 16: tile rows g and g+8; ROWS = 8: row g; ROWS = 4: rows g < 4.
 // Odd g read their chunks rotated by one so that the two rows of a quarter-warp hit different
 // banks (all rows alias: the row stride is a multiple of 128 bytes).  Writes the warp's partial
-// sums of tile rows into `out[0..15]`.  Not inlined (one copy per shape instead of one per phase: the
-// instruction cache is a scarce resource of this kernel); it loads the warp's activation fragments itself.
+// sums of tile rows into `out[0..15]`.  (Inlined: as a called function it cost ~0.18 us per chunk, the caller's
+// live registers going through local memory around every call.)
 template <int NLOAD, int ROWS>
-__device__ __noinline__ void mma_chunk(const char* stage, const uint32_t* xw, int K, int warp, int lane, float* out) {
-    uint32_t b[2 * NLOAD][2];
-    load_bfrags<NLOAD>(xw, lane, b);
+__device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, int lane,
+                                          const uint32_t (&b)[2 * NLOAD][2], float* out) {
     const int g = lane >> 2, t = lane & 3, odd = g & 1;
     const int rowbytes = row_stride(K), kofs = warp * NLOAD * 64;      // 32*NLOAD elements of 2 bytes per warp
     const bool live = (ROWS >= 8) || (g < 4);
@@ -765,9 +666,8 @@ __device__ __noinline__ void mma_chunk(const char* stage, const uint32_t* xw, in
 // that is then scaled by the group's scale of each row: the dequantised value never has to be
 // rounded.  The row stride keeps the 8 rows of a quarter-warp on different banks.
 template <int NLOAD, int ROWS>
-__device__ __noinline__ void mma_chunk(const char* stage, const uint32_t* xw, int K, int warp, int lane, float* out) {
-    uint32_t b[2 * NLOAD][2];
-    load_bfrags<NLOAD>(xw, lane, b);
+__device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, int lane,
+                                          const uint32_t (&b)[2 * NLOAD][2], float* out) {
     const int g = lane >> 2, t = lane & 3;
     const bool live = (ROWS >= 8) || (g < 4);
     const int stride = row_stride(K);
@@ -866,10 +766,8 @@ __device__ __forceinline__ __half2 e4m3_to_h2(uint32_t byte) {
 
 // The chunk in `stage` times the staged activation; this warp's partial sums of its tile's 16 rows go to
 // part[warp * 16 + 0..15] (warp = kq * RT + T).  K = KS * NSEG * 32.
-// Not inlined: the body is large, every phase would carry its own copy, and the instruction cache is a scarce
-// resource of this kernel; the arguments are scalars, so the call costs a few cycles per chunk.
 template <int NSEG, int RT>
-__device__ __noinline__ void mma_chunk_ts(const char* stage, const uint32_t* xw, int K, int warp, int lane, float* out) {
+__device__ __forceinline__ void mma_chunk_ts(const char* stage, const uint32_t* xw, int K, int warp, int lane, float* out) {
     constexpr int GR = 2 * RT;
     uint32_t b[2 * NSEG][2];
     load_bfrags_ts<NSEG>(xw, lane, b);
@@ -955,13 +853,14 @@ __device__ __forceinline__ void mma_phase(const DecodeParams& P, Ctx& c, int nch
     int nchunks = nchunks_in;
     // alternate halves: a slow warp may still be reading the previous phase's sums in its epilogue
     c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
-    const uint32_t* xw = reinterpret_cast<const uint32_t*>(c.xs) + c.warp * XSW;
+    uint32_t b[2 * NLOAD][2];
+    load_bfrags<NLOAD>(reinterpret_cast<const uint32_t*>(c.xs) + c.warp * XSW, c.lane, b);
     if (nchunks > 4) { fail(P, c, ST_MISALIGNED); nchunks = 4; }   // never reached for grids >= MIN_GRID
     if (nchunks > 0) wait_full(P, c, c.it % NSTAGE, (c.it / NSTAGE) & 1u);
 #pragma unroll 1
     for (int q = 0; q < nchunks; ++q, ++c.it) {
         const uint32_t stage = c.it % NSTAGE;
-        mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + stage * STAGE_BYTES, xw, K, c.warp, c.lane,
+        mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + stage * STAGE_BYTES, K, c.warp, c.lane, b,
                                c.part + (q * NCW + c.warp) * 16);
         release_stage(c, stage);
         // the mbarrier test of the next chunk overlaps the tail of this chunk's MMAs
@@ -1731,6 +1630,7 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
         acc = warp_sum(acc);
         if (valid) {
             if (seen > 0.f) acc = (acc > 0.f) ? acc / P.rep_penalty : acc * P.rep_penalty;
+            if (P.logits_out && c.lane == 0) P.logits_out[row] = acc;
             if (acc > bestv) { bestv = acc; besti = row; }
         }
         release_stage(c, stage);
@@ -1759,6 +1659,7 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
         const int lr = q * LM_RPC + c.tid;
         if (c.tid < LM_RPC && lr < nloc) {
             const float acc = part_sum_ts<4>(c, c.tid) * ts_lm;
+            if (P.logits_out) P.logits_out[g.r0 + lr] = acc;
             if (acc > bestv) { bestv = acc; besti = g.r0 + lr; }
         }
     }
@@ -1823,6 +1724,7 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
                 acc = a0 * s0 + a1 * s1;
             }
             acc = warp_sum(acc);
+            if (P.logits_out && valid && c.lane == 0) P.logits_out[g.r0 + lr] = acc;
             if (valid && acc > bestv) { bestv = acc; besti = g.r0 + lr; }
         }
         release_stage(c, stage);

@@ -129,7 +129,7 @@ extern "C" int mk_decode_bf16_static_scratch(
     p.host_status = nullptr;   // the mapped status word of launch_decode would be an allocation
     p.trace = nullptr; p.trace_slots = 0;
     p.poll_limit_cycles = mk::DEFAULT_POLL_LIMIT_CYCLES; p.mbar_limit_tries = mk::DEFAULT_MBAR_LIMIT_TRIES;
-    p.steps = 1; p.poll_pipelined = 1;
+    p.steps = 1;
     mk::fill_rope(p);
     e = mk::launch_decode_kernel(p, s.grid, stream);
     if (e != cudaSuccess) return fail_with(MK_ERR_CUDA, "decode launch", e);

@@ -63,6 +63,7 @@ struct DecodeParams {
     float* alpha;
     float* normalized;            // f32 [1024] final-normed hidden (output)
     float* seen_mask;             // f32 [vocab] or null
+    float* logits_out;            // optional f32 [vocab]: receives every logit of the (last) step, after the penalty
     float rep_penalty;
     const int* token_ptr;         // device token (feedback mode) or null
     int token_val;                // host token when token_ptr is null
@@ -80,7 +81,6 @@ struct DecodeParams {
     int trace_slots;              // entries per CTA in `trace`
     unsigned long long poll_limit_cycles;   // SM clocks a poll of a flagged word may take before the CTA gives up
     uint32_t mbar_limit_tries;              // try_wait attempts on a ring barrier before the CTA gives up
-    int poll_pipelined;                     // 1: a failed poll keeps several loads in flight (see decode_body.cuh)
 };
 
 // Defaults of the two wait limits: about 2 s of SM clock each.
