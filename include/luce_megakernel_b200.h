@@ -259,6 +259,19 @@ int mk_decode_batch_many(
     const void *fused_fa_qkv_base, const void *fused_gate_up_base,
     int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
 
+/* The batched step on the NVFP4 format with a per-tensor scale (see mk_decode_nvfp4_ts for the format and the 224-byte
+ * table): `steps` steps for `batch` sequences.  steps == 1 with output_tokens set: one step, tokens / positions
+ * untouched (mk_decode_batch's behaviour); otherwise the chosen tokens are fed back on the device, tokens / positions
+ * are updated in place and tokens_log [steps][batch] receives every step's tokens (mk_decode_batch_many's).  State
+ * tensors as for mk_decode_batch.  Same kernel sequence as the bf16 step; the projections and the LM head read 4-bit
+ * weights (0.5625 bytes per weight).  No counterpart in the reference. */
+int mk_decode_batch_nvfp4_ts(
+    int steps, int *tokens, int *positions, int *output_tokens, int *tokens_log, int batch,
+    const void *embed_weight, const void *layers, const void *final_norm_w,
+    const void *lm_head_packed, const void *lm_head_scales_rows, const float *lm_head_tensor_scale,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs, void *final_normed, void *hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
+
 /* The reference's other prefill entry points, with their argument lists: launch_prefill_bf16_mega (bf16, per-matrix
  * weights from the 128-byte table only; reference: megakernel/prefill_megakernel.cu:1031-1045),
  * launch_prefill_bf16_nvfp4_lm (bf16 layers, NVFP4 LM head; megakernel/prefill_bw.cu:1486-1503) and

@@ -35,11 +35,10 @@ __device__ __forceinline__ constexpr int scale_bytes(int K) { return K / 16; }
 // per matrix.  A ring chunk is R consecutive packed rows (R * K/2 bytes, no padding) followed by the R rows of
 // block scales (R * K/16 bytes): two bulk copies per matrix the chunk touches.  R = 64 for K = 1024, 32 for
 // K = 2048, 16 for K = 3584, so every phase of a layer is ONE chunk per CTA.  The table entry has three slots per
-// quantised matrix: packed data, row-major scales, pointer to the tensor scale.  (The rows sit in the stage in eight
-// groups, 16 bytes apart more than their size: see chunk_slot_src.)
+// quantised matrix: packed data, row-major scales, pointer to the tensor scale.
 typedef LayerWeightsNVFP4TS LW;
 constexpr int NSTAGE = 5;
-constexpr int STAGE_BYTES = 37120;                      // 64 rows of K = 1024: 8 x (4 KB + 16) of codes + 4 KB of scales
+constexpr int STAGE_BYTES = 36864;                      // 64 rows of K = 1024: 32 KB of codes + 4 KB of scales
 enum { DN_IN_NORM = 0, DN_W_QKV = 1, DN_W_Z = 4, DN_W_B = 7, DN_W_A = 8, DN_CONV_W = 9, DN_A_LOG = 10, DN_DT_BIAS = 11,
        DN_NORM_W = 12, DN_W_OUT = 13, DN_POST_NORM = 16, DN_W_GATE = 17, DN_W_UP = 20, DN_W_DOWN = 23 };
 enum { FA_IN_NORM = 0, FA_W_Q = 1, FA_W_K = 4, FA_W_V = 7, FA_Q_NORM = 10, FA_K_NORM = 11, FA_W_O = 12, FA_POST_NORM = 15,
@@ -141,12 +140,13 @@ __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const
         return 16 * DN_KEY * 4;
     }
     {
-        // Stage layout: the chunk's R rows in 8 groups of GR = R/8 consecutive rows, group k at offset
-        // k * (GR * K/2 + 16) -- the 16-byte step puts the 8 rows a quarter-warp reads together (one per group) on
-        // different banks -- then the R rows of block scales, unpadded.
-        // lanes 0-15: packed rows of group k = lane/2; part lane&1 = the rows of the group that lie in the first /
-        // second matrix the group touches (a group straddles at most one matrix boundary).
-        // lanes 16-18: block scales of the chunk's rows in matrix segment lane-16.
+        // Stage layout: the chunk's R rows of packed codes, contiguous (R * K/2 bytes), then their R rows of block scales.
+        // lane = 2 * segment + kind: segment = a matrix the chunk's rows fall into (at most 3; gate / up for the SwiGLU
+        // phase), kind 0 = packed rows, 1 = scales.  Few copies per chunk on purpose: a CTA can issue a bulk copy only
+        // every ~0.1 us, and an earlier layout with eight padded row groups (17-19 copies per chunk) spent over 2 us
+        // per chunk just issuing them; the bank conflicts of the unpadded rows are avoided on the reading side instead.
+        const int seg = lane >> 1, kind = lane & 1;
+        if (seg >= 3) return 0;
         // matrix segments of the phase's concatenated row space: [0, h0) [h0, h1) [h1, h2), table slots i0 i1 i2
         int K = HIDDEN, nseg = 1, h0 = 0, h1 = 0, h2 = 0, i0 = -1, i1 = -1, i2 = -1;
         const bool dn = (lw.layer_type == 0);
@@ -156,60 +156,34 @@ __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const
             case T_FA_IN: nseg = 3; i0 = FA_W_Q; h0 = FA_QPROJ; i1 = FA_W_K; h1 = FA_QPROJ + FA_KV_SIZE; i2 = FA_W_V; h2 = FA_QKV_ROWS; break;
             case T_DN_OUT: i0 = DN_W_OUT; K = 2048; h0 = HIDDEN; break;
             case T_FA_OUT: i0 = FA_W_O; K = 2048; h0 = HIDDEN; break;
-            case T_GATEUP: gateup = true; i0 = dn ? (int)DN_W_GATE : (int)FA_W_GATE; i1 = dn ? (int)DN_W_UP : (int)FA_W_UP; break;
+            case T_GATEUP: gateup = true; nseg = 2; i0 = dn ? (int)DN_W_GATE : (int)FA_W_GATE; i1 = dn ? (int)DN_W_UP : (int)FA_W_UP; break;
             case T_DOWN: i0 = dn ? (int)DN_W_DOWN : (int)FA_W_DOWN; K = INTER; h0 = HIDDEN; break;
             case T_LM: h0 = P.vocab; break;
             default: return 0;
         }
-        const int R = rows_per_chunk(K), GR = R / 8;
-        const uint32_t gstride = (uint32_t)GR * row_bytes(K) + 16u, sc_off = 8u * gstride;
-        auto seg_lo = [&](int sgi) { return sgi == 0 ? 0 : (sgi == 1 ? h0 : h1); };
-        auto seg_hi = [&](int sgi) { return sgi == 0 ? h0 : (sgi == 1 ? h1 : h2); };
-        auto mat = [&](int sgi, int kind) -> const char* {
-            if (type == T_LM) return (const char*)(kind ? P.lm_scales : P.lm_head);
-            const int ix = sgi == 0 ? i0 : (sgi == 1 ? i1 : i2);
-            return (const char*)lw.ptrs[ix + kind];
-        };
+        if (seg >= nseg) return 0;
+        const int R = rows_per_chunk(K);
+        const uint32_t sc_off = (uint32_t)R * row_bytes(K);
+        const char* base;
+        if (type == T_LM) base = (const char*)(kind ? P.lm_scales : P.lm_head);
+        else base = (const char*)lw.ptrs[(seg == 0 ? i0 : (seg == 1 ? i1 : i2)) + kind];
+        const uint32_t unit = kind ? scale_bytes(K) : row_bytes(K);
+        const uint32_t region = kind ? sc_off : 0u;
         if (gateup) {
-            // outputs [oa, ob) of this chunk: gate rows at stage rows 0.., up rows at stage rows 32..
+            // outputs [oa, ob) of this chunk: gate rows at stage rows 0.., the matching up rows at stage rows 32..
             const int oa = g.r0 + q * 32, ob = min(g.r1, oa + 32);
-            if (lane < 16) {
-                if (lane & 1) return 0;
-                const int k = lane >> 1, m = k >> 2;                 // groups 0-3: gate, 4-7: up
-                const int lo = oa + (k & 3) * 8, hi = min(ob, lo + 8);
-                if (hi <= lo) return 0;
-                src = mat(m, 0) + (size_t)lo * row_bytes(K);
-                dst_off = (uint32_t)k * gstride;
-                return (uint32_t)(hi - lo) * row_bytes(K);
-            }
-            const int m = lane - 16;
-            if (m >= 2 || ob <= oa) return 0;
-            src = mat(m, 1) + (size_t)oa * scale_bytes(K);
-            dst_off = sc_off + (uint32_t)(m * 32) * scale_bytes(K);
-            return (uint32_t)(ob - oa) * scale_bytes(K);
+            if (ob <= oa) return 0;
+            src = base + (size_t)oa * unit;
+            dst_off = region + (uint32_t)(seg * 32) * unit;
+            return (uint32_t)(ob - oa) * unit;
         }
         const int ra = g.r0 + q * R, rb = min(g.r1, ra + R);
-        if (lane < 16) {
-            const int k = lane >> 1, part = lane & 1;
-            const int lo = ra + k * GR, hi = min(rb, lo + GR);
-            if (hi <= lo) return 0;
-            int s0 = 0;                                               // segment of the group's first row
-            while (s0 + 1 < nseg && lo >= seg_hi(s0)) ++s0;
-            const int sg = s0 + part;
-            if (sg >= nseg) return 0;
-            const int a = max(lo, seg_lo(sg)), b = min(hi, seg_hi(sg));
-            if (b <= a) return 0;
-            src = mat(sg, 0) + (size_t)(a - seg_lo(sg)) * row_bytes(K);
-            dst_off = (uint32_t)k * gstride + (uint32_t)(a - lo) * row_bytes(K);
-            return (uint32_t)(b - a) * row_bytes(K);
-        }
-        const int sg = lane - 16;
-        if (sg >= nseg) return 0;
-        const int a = max(ra, seg_lo(sg)), b = min(rb, seg_hi(sg));
+        const int lo_s = seg == 0 ? 0 : (seg == 1 ? h0 : h1), hi_s = seg == 0 ? h0 : (seg == 1 ? h1 : h2);
+        const int a = max(ra, lo_s), b = min(rb, hi_s);
         if (b <= a) return 0;
-        src = mat(sg, 1) + (size_t)(a - seg_lo(sg)) * scale_bytes(K);
-        dst_off = sc_off + (uint32_t)(a - ra) * scale_bytes(K);
-        return (uint32_t)(b - a) * scale_bytes(K);
+        src = base + (size_t)(a - lo_s) * unit;
+        dst_off = region + (uint32_t)(a - ra) * unit;
+        return (uint32_t)(b - a) * unit;
     }
 #else
 #if MK_WFMT == 0
@@ -567,6 +541,7 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
     const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)(byte & 0xffu), __NV_E2M1);
     return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
+
 #endif
 
 // Staging of a warp's K-slice: three planes of XK bf16.  Elements e, e+1 (e even) as one word.
@@ -688,15 +663,11 @@ __device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, in
 #pragma unroll
     for (int i = 0; i < NLOAD; ++i) {
         float tmp[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t a0 = e2m1x2_to_f16x2(w0[i]), a2 = e2m1x2_to_f16x2(w0[i] >> 8);
-        const uint32_t c0 = e2m1x2_to_f16x2(w0[i] >> 16), c2 = e2m1x2_to_f16x2(w0[i] >> 24);
-        uint32_t a1 = 0u, a3 = 0u, c1 = 0u, c3 = 0u;
-        if (ROWS == 16) {
-            a1 = e2m1x2_to_f16x2(w1[i]); a3 = e2m1x2_to_f16x2(w1[i] >> 8);
-            c1 = e2m1x2_to_f16x2(w1[i] >> 16); c3 = e2m1x2_to_f16x2(w1[i] >> 24);
-        }
-        mma_16816(tmp, a0, a1, a2, a3, b[2 * i][0], b[2 * i][1]);
-        mma_16816(tmp, c0, c1, c2, c3, b[2 * i + 1][0], b[2 * i + 1][1]);
+        uint32_t ra[4], rb[4] = {0u, 0u, 0u, 0u};
+        e2m1x8_to_f16x2x4(w0[i], ra);
+        if (ROWS == 16) e2m1x8_to_f16x2x4(w1[i], rb);
+        mma_16816(tmp, ra[0], rb[0], ra[1], rb[1], b[2 * i][0], b[2 * i][1]);
+        mma_16816(tmp, ra[2], rb[2], ra[3], rb[3], b[2 * i + 1][0], b[2 * i + 1][1]);
         acc[0] = fmaf(s0[i], tmp[0], acc[0]); acc[1] = fmaf(s0[i], tmp[1], acc[1]);
         acc[2] = fmaf(s1[i], tmp[2], acc[2]); acc[3] = fmaf(s1[i], tmp[3], acc[3]);
     }
@@ -713,11 +684,13 @@ __device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, in
 
 #if MK_WFMT == 2
 // ---- tensor-scale NVFP4: one chunk per phase, warps split it into row tiles x K parts ------------------------
-// A chunk of R = 8 GR rows is RT = GR / 2 row tiles of 16 rows; the 16 warps are RT row tiles x KS = 16 / RT K parts
-// of PK = NSEG * 32 elements.  MMA tile T takes, as its row g (g + 8 for the second half h), chunk row
-// GR g + 2 T + h: the eight rows a quarter-warp reads at once lie in the eight different row groups of the stage.
-// Activations: part p of the K dimension is staged as three f16 planes of PK elements (hi / mid / lo terms) at
-// xs + p * 3 PK / 2 words, written by whichever warps own those elements and read by the RT warps of that part.
+// A chunk holds R consecutive rows (64 / 32 / 16 for K = 1024 / 2048 / 3584), unpadded.  RT row tiles of 16 rows x KS
+// parts of the K dimension of 256 elements (8 segments of 32) make RT * KS working warps (16, 8 or 14 of the 16).
+// Rows are a multiple of 128 bytes apart, so the eight rows a quarter-warp reads at once would collide on the same
+// banks; instead lane group g reads segment i ^ g in step i (eight different 16-byte columns: no conflict) and a
+// three-stage network of selects puts the words back in segment order.
+// Activations: part p of the K dimension is staged as three f16 planes of 256 elements (hi / mid / lo terms) at
+// xs + p * 384 words, written by whichever warps own those elements and read by the RT warps of that part.
 template <int PK>
 __device__ __forceinline__ void stage_pair_ts(uint32_t* xs_words, int e, float x0, float x1) {
     uint32_t* xw = xs_words + (e / PK) * (3 * PK / 2);
@@ -739,73 +712,66 @@ __device__ __forceinline__ void stage_one_ts(uint32_t* xs_words, int e, float x)
     p[PK + l] = (unsigned short)(m >> 16);
     p[2 * PK + l] = (unsigned short)(lo >> 16);
 }
-template <int NSEG>
-__device__ __forceinline__ void load_bfrags_ts(const uint32_t* xw, int lane, uint32_t (&b)[2 * NSEG][2]) {
-    constexpr int PK = NSEG * 32;
+__device__ __forceinline__ void load_bfrags_ts(const uint32_t* xw, int lane, uint32_t (&b)[16][2]) {
     const int g = lane >> 2, t = lane & 3;
-    const uint32_t* plane = xw + (g < 3 ? g : 0) * (PK >> 1);
+    const uint32_t* plane = xw + (g < 3 ? g : 0) * 128;
 #pragma unroll
-    for (int i = 0; i < NSEG; ++i) {
+    for (int i = 0; i < 8; ++i) {
         uint4 v = *reinterpret_cast<const uint4*>(plane + 4 * (t + 4 * i));
         if (g >= 3) v = make_uint4(0, 0, 0, 0);
         b[2 * i][0] = v.x; b[2 * i][1] = v.y;
         b[2 * i + 1][0] = v.z; b[2 * i + 1][1] = v.w;
     }
 }
-// e2m1 pair (one byte) times an E4M3 block scale, both exact in f16: the product has at most 6 significant bits and
-// lies in [2^-10, 2688], so it is exact as well
-__device__ __forceinline__ uint32_t deq2(uint32_t byte, __half2 sc) {
-    const uint32_t w = e2m1x2_to_f16x2(byte);
-    const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&w), sc);
-    return *reinterpret_cast<const uint32_t*>(&r);
-}
-__device__ __forceinline__ __half2 e4m3_to_h2(uint32_t byte) {
-    const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)(byte & 0xffu), __NV_E4M3);
-    return __half2half2(*reinterpret_cast<const __half*>(&h));
+// w[i] holds segment i ^ g on entry and segment i on return
+__device__ __forceinline__ void unxor8(uint32_t (&w)[8], int g) {
+#pragma unroll
+    for (int bit = 1; bit < 8; bit <<= 1) {
+        const bool sw = (g & bit) != 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if ((i & bit) == 0) {
+                const uint32_t a = w[i], d = w[i | bit];
+                w[i] = sw ? d : a;
+                w[i | bit] = sw ? a : d;
+            }
+        }
+    }
 }
 
-// The chunk in `stage` times the staged activation; this warp's partial sums of its tile's 16 rows go to
-// part[warp * 16 + 0..15] (warp = kq * RT + T).  K = KS * NSEG * 32.
-template <int NSEG, int RT>
+// The chunk in `stage` times the staged activation; warp (kq, T) = warp / RT, warp % RT leaves its partial sums of
+// tile T's 16 rows (8 when !TWO: the phase has at most 8 rows) in out[0..15].
+template <int RT, bool TWO>
 __device__ __forceinline__ void mma_chunk_ts(const char* stage, const uint32_t* xw, int K, int warp, int lane, float* out) {
-    constexpr int GR = 2 * RT;
-    uint32_t b[2 * NSEG][2];
-    load_bfrags_ts<NSEG>(xw, lane, b);
     const int g = lane >> 2, t = lane & 3, T = warp % RT, kq = warp / RT;
     const int rb = K / 2, sb = K / 16;
-    const char* r0 = stage + g * (GR * rb + 16) + (2 * T) * rb + kq * (NSEG * 16) + 4 * t;
-    const char* r1 = r0 + rb;
-    const unsigned char* sc0 = reinterpret_cast<const unsigned char*>(stage) + 8 * (GR * rb + 16) + (GR * g + 2 * T) * sb + kq * (NSEG * 2);
-    const unsigned char* sc1 = sc0 + sb;
-    uint32_t w0[NSEG], w1[NSEG];
-    unsigned short s0[NSEG], s1[NSEG];
+    uint32_t b[16][2];
+    load_bfrags_ts(xw, lane, b);
+    const char* r0 = stage + (16 * T + g) * rb + kq * 128 + 4 * t;
+    const unsigned char* sc0 = reinterpret_cast<const unsigned char*>(stage) + rows_per_chunk(K) * rb + (16 * T + g) * sb + kq * 16;
+    uint32_t w0[8], w1[8];
 #pragma unroll
-    for (int i = 0; i < NSEG; ++i) {
-        w0[i] = *reinterpret_cast<const uint32_t*>(r0 + 16 * i);
-        w1[i] = *reinterpret_cast<const uint32_t*>(r1 + 16 * i);
+    for (int i = 0; i < 8; ++i) {
+        w0[i] = *reinterpret_cast<const uint32_t*>(r0 + 16 * (i ^ g));
+        w1[i] = TWO ? *reinterpret_cast<const uint32_t*>(r0 + 8 * rb + 16 * (i ^ g)) : 0u;
     }
-    if (NSEG == 8) {       // the slice's 16 scale bytes of each row in one load
-        const uint4 a = *reinterpret_cast<const uint4*>(sc0), d = *reinterpret_cast<const uint4*>(sc1);
-        const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, dw[4] = {d.x, d.y, d.z, d.w};
-#pragma unroll
-        for (int i = 0; i < NSEG; ++i) {
-            s0[i] = (unsigned short)(aw[i >> 1] >> (16 * (i & 1)));
-            s1[i] = (unsigned short)(dw[i >> 1] >> (16 * (i & 1)));
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < NSEG; ++i) {
-            s0[i] = *reinterpret_cast<const unsigned short*>(sc0 + 2 * i);
-            s1[i] = *reinterpret_cast<const unsigned short*>(sc1 + 2 * i);
-        }
-    }
+    const uint4 sa = *reinterpret_cast<const uint4*>(sc0);
+    const uint4 sd = TWO ? *reinterpret_cast<const uint4*>(sc0 + 8 * sb) : make_uint4(0, 0, 0, 0);
+    unxor8(w0, g);
+    if (TWO) unxor8(w1, g);
+    const uint32_t aw[4] = {sa.x, sa.y, sa.z, sa.w}, dw[4] = {sd.x, sd.y, sd.z, sd.w};
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
     const int sh = (t >> 1) * 8;          // lanes t = 0,1 hold elements of the segment's first block, t = 2,3 of its second
 #pragma unroll
-    for (int i = 0; i < NSEG; ++i) {
-        const __half2 h0 = e4m3_to_h2((uint32_t)s0[i] >> sh), h1 = e4m3_to_h2((uint32_t)s1[i] >> sh);
-        mma_16816(acc, deq2(w0[i], h0), deq2(w1[i], h1), deq2(w0[i] >> 8, h0), deq2(w1[i] >> 8, h1), b[2 * i][0], b[2 * i][1]);
-        mma_16816(acc2, deq2(w0[i] >> 16, h0), deq2(w1[i] >> 16, h1), deq2(w0[i] >> 24, h0), deq2(w1[i] >> 24, h1),
+    for (int i = 0; i < 8; ++i) {
+        const __half2 h0 = e4m3_to_h2_div256((aw[i >> 1] >> (16 * (i & 1))) >> sh);
+        const __half2 h1 = e4m3_to_h2_div256((dw[i >> 1] >> (16 * (i & 1))) >> sh);
+        uint32_t ra[4], rbv[4] = {0u, 0u, 0u, 0u};
+        e2m1x8_to_f16x2x4(w0[i], ra);
+        if (TWO) e2m1x8_to_f16x2x4(w1[i], rbv);
+        mma_16816(acc, hmul2_bits(ra[0], h0), TWO ? hmul2_bits(rbv[0], h1) : 0u, hmul2_bits(ra[1], h0), TWO ? hmul2_bits(rbv[1], h1) : 0u,
+                  b[2 * i][0], b[2 * i][1]);
+        mma_16816(acc2, hmul2_bits(ra[2], h0), TWO ? hmul2_bits(rbv[2], h1) : 0u, hmul2_bits(ra[3], h0), TWO ? hmul2_bits(rbv[3], h1) : 0u,
                   b[2 * i + 1][0], b[2 * i + 1][1]);
     }
 #pragma unroll
@@ -814,36 +780,38 @@ __device__ __forceinline__ void mma_chunk_ts(const char* stage, const uint32_t* 
     float q1 = acc[2] + (t == 0 ? acc[3] : 0.f);
     q0 += __shfl_down_sync(0xffffffffu, q0, 1);
     q1 += __shfl_down_sync(0xffffffffu, q1, 1);
-    if (t == 0) { out[g] = q0; out[g + 8] = q1; }
+    if (t == 0) { out[g] = q0; if (TWO) out[g + 8] = q1; }
 }
 
 // One-chunk phase.  `sync_parts`: the staged activation was written by other warps than the ones that read it.
-template <int NSEG, int RT>
+template <int RT, int KS, bool TWO>
 __device__ __forceinline__ void mma_phase_ts(const DecodeParams& P, Ctx& c, int nchunks, int K, bool sync_parts) {
-    constexpr int PK = NSEG * 32;
     c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
     if (sync_parts) named_bar_sync(1, NCT);
-    const uint32_t* xw = reinterpret_cast<const uint32_t*>(c.xs) + (c.warp / RT) * (3 * PK / 2);
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(c.xs) + (c.warp / RT) * 384;
     if (nchunks > 1) { fail(P, c, ST_MISALIGNED); nchunks = 1; }   // never reached for grids >= MIN_GRID
     if (nchunks > 0) {
         const uint32_t stage = c.it % NSTAGE;
         wait_full(P, c, stage, (c.it / NSTAGE) & 1u);
-        mma_chunk_ts<NSEG, RT>(c.smem + OFF_RING + stage * STAGE_BYTES, xw, K, c.warp, c.lane, c.part + c.warp * 16);
+        if (c.warp < RT * KS)
+            mma_chunk_ts<RT, TWO>(c.smem + OFF_RING + stage * STAGE_BYTES, xw, K, c.warp, c.lane, c.part + c.warp * 16);
         release_stage(c, stage);
         ++c.it;
     }
 }
-// sum over the K parts of stage row r of the chunk (RT row tiles, KS = 16 / RT parts)
-template <int RT>
+// sum over the K parts of stage row r of the chunk
+template <int RT, int KS>
 __device__ __forceinline__ float part_sum_ts(const Ctx& c, int r) {
-    constexpr int GR = 2 * RT, KS = NCW / RT;
-    const int g = r / GR, j = r % GR, T = j >> 1, h = j & 1;
+    const int T = r >> 4, idx = r & 15;
     float s = 0.f;
 #pragma unroll
-    for (int kq = 0; kq < KS; ++kq) s += c.part[(kq * RT + T) * 16 + g + 8 * h];
+    for (int kq = 0; kq < KS; ++kq) s += c.part[(kq * RT + T) * 16 + idx];
     return s;
 }
-__device__ __forceinline__ float tensor_scale_of(const LW& lw, int slot) { return __ldg(reinterpret_cast<const float*>(lw.ptrs[slot + 2])); }
+// the matrix's fp32 scale times the 2^8 the block scales were divided by
+__device__ __forceinline__ float tensor_scale_of(const LW& lw, int slot) {
+    return __ldg(reinterpret_cast<const float*>(lw.ptrs[slot + 2])) * TS_SCALE_FOLD;
+}
 #endif
 
 #if MK_WFMT != 2
@@ -971,7 +939,7 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
 #endif
     trace_point(P, c);
 #if MK_WFMT == 2
-    mma_phase_ts<8, 4>(P, c, g.nchunks, HIDDEN, true);
+    mma_phase_ts<4, 4, true>(P, c, g.nchunks, HIDDEN, true);
 #else
     mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
 #endif
@@ -993,7 +961,7 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
 #endif
     if (c.tid < nloc) {
 #if MK_WFMT == 2
-        const float val = part_sum_ts<4>(c, c.tid) * ts_in;
+        const float val = part_sum_ts<4, 4>(c, c.tid) * ts_in;
 #else
         const float val = part_sum(c, c.tid >> 4, c.tid & 15);
 #endif
@@ -1089,7 +1057,7 @@ __device__ __forceinline__ void outproj_rows(const DecodeParams& P, Ctx& c, cons
     (void)type; (void)tscale;
     const int nloc = g.r1 - g.r0;
 #if MK_WFMT == 2
-    mma_phase_ts<8, 2>(P, c, g.nchunks, 2048, true);
+    mma_phase_ts<1, 8, false>(P, c, g.nchunks, 2048, true);
 #else
     mma_phase<4, 8>(P, c, g.nchunks, 2048);
 #endif
@@ -1097,7 +1065,7 @@ __device__ __forceinline__ void outproj_rows(const DecodeParams& P, Ctx& c, cons
     named_bar_sync(1, NCT);
     if (c.tid < nloc) {
 #if MK_WFMT == 2
-        const float y = part_sum_ts<2>(c, c.tid) * tscale + resid;
+        const float y = part_sum_ts<1, 8>(c, c.tid) * tscale + resid;
 #else
         const float y = part_sum(c, c.tid >> 3, c.tid & 7) + resid;
 #endif
@@ -1173,10 +1141,10 @@ __device__ __forceinline__ void phase_fa_in(const DecodeParams& P, Ctx& c, const
         const int r = g.r0 + c.tid;
         ts_in = tensor_scale_of(lw, r < FA_QPROJ ? (int)FA_W_Q : (r < FA_QPROJ + FA_KV_SIZE ? (int)FA_W_K : (int)FA_W_V));
     }
-    mma_phase_ts<8, 4>(P, c, g.nchunks, HIDDEN, true);
+    mma_phase_ts<4, 4, true>(P, c, g.nchunks, HIDDEN, true);
     trace_point(P, c);
     named_bar_sync(1, NCT);
-    if (c.tid < nloc) st_flagged(P.ws->x_fain + g.r0 + c.tid, part_sum_ts<4>(c, c.tid) * ts_in, ep);
+    if (c.tid < nloc) st_flagged(P.ws->x_fain + g.r0 + c.tid, part_sum_ts<4, 4>(c, c.tid) * ts_in, ep);
 #else
     mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
     trace_point(P, c);
@@ -1505,7 +1473,7 @@ __device__ __forceinline__ void phase_gateup(const DecodeParams& P, Ctx& c, cons
     const bool dnl = (lw.layer_type == 0);
     const float ts_g = tensor_scale_of(lw, dnl ? (int)DN_W_GATE : (int)FA_W_GATE);
     const float ts_u = tensor_scale_of(lw, dnl ? (int)DN_W_UP : (int)FA_W_UP);
-    mma_phase_ts<8, 4>(P, c, g.nchunks, HIDDEN, true);
+    mma_phase_ts<4, 4, true>(P, c, g.nchunks, HIDDEN, true);
 #else
     mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
 #endif
@@ -1513,8 +1481,8 @@ __device__ __forceinline__ void phase_gateup(const DecodeParams& P, Ctx& c, cons
     named_bar_sync(1, NCT);
     if (c.tid < nout) {
 #if MK_WFMT == 2
-        const float gv = part_sum_ts<4>(c, c.tid) * ts_g;
-        const float uv = part_sum_ts<4>(c, 32 + c.tid) * ts_u;
+        const float gv = part_sum_ts<4, 4>(c, c.tid) * ts_g;
+        const float uv = part_sum_ts<4, 4>(c, 32 + c.tid) * ts_u;
 #else
         const float gv = part_sum(c, c.tid >> 3, c.tid & 7);
         const float uv = part_sum(c, c.tid >> 3, 8 + (c.tid & 7));
@@ -1541,7 +1509,7 @@ __device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, const 
 #if MK_WFMT == 2
         uint32_t* xs_words = reinterpret_cast<uint32_t*>(c.xs);
 #pragma unroll
-        for (int k = 0; k < 7; ++k) stage_one_ts<224>(xs_words, 224 * c.warp + c.lane + 32 * k, xv[k]);
+        for (int k = 0; k < 7; ++k) stage_one_ts<256>(xs_words, 224 * c.warp + c.lane + 32 * k, xv[k]);
 #else
         uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
 #pragma unroll
@@ -1552,7 +1520,7 @@ __device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, const 
     trace_point(P, c);
 #if MK_WFMT == 2
     const float ts_d = tensor_scale_of(lw, lw.layer_type == 0 ? (int)DN_W_DOWN : (int)FA_W_DOWN);
-    mma_phase_ts<7, 1>(P, c, g.nchunks, INTER, false);
+    mma_phase_ts<1, 14, false>(P, c, g.nchunks, INTER, true);
 #else
     mma_phase<7, 4>(P, c, g.nchunks, INTER);
 #endif
@@ -1560,7 +1528,7 @@ __device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, const 
     named_bar_sync(1, NCT);
     if (c.tid < nloc) {
 #if MK_WFMT == 2
-        const float y = part_sum_ts<1>(c, c.tid) * ts_d + resid;
+        const float y = part_sum_ts<1, 14>(c, c.tid) * ts_d + resid;
 #else
         const float y = part_sum(c, c.tid >> 2, c.tid & 3) + resid;
 #endif
@@ -1647,18 +1615,18 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
         named_bar_sync(1, NCT);
     }
     const uint32_t* xw_lm = reinterpret_cast<const uint32_t*>(c.xs) + (c.warp / 4) * (3 * 256 / 2);
-    const float ts_lm = __ldg(P.lm_tensor_scale);
+    const float ts_lm = __ldg(P.lm_tensor_scale) * TS_SCALE_FOLD;
 #pragma unroll 1
     for (int q = 0; q < g.nchunks; ++q, ++c.it) {
         const uint32_t stage = c.it % NSTAGE, parity = (c.it / NSTAGE) & 1u;
         c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
         wait_full(P, c, stage, parity);
-        mma_chunk_ts<8, 4>(c.smem + OFF_RING + stage * STAGE_BYTES, xw_lm, HIDDEN, c.warp, c.lane, c.part + c.warp * 16);
+        mma_chunk_ts<4, true>(c.smem + OFF_RING + stage * STAGE_BYTES, xw_lm, HIDDEN, c.warp, c.lane, c.part + c.warp * 16);
         release_stage(c, stage);
         named_bar_sync(1, NCT);
         const int lr = q * LM_RPC + c.tid;
         if (c.tid < LM_RPC && lr < nloc) {
-            const float acc = part_sum_ts<4>(c, c.tid) * ts_lm;
+            const float acc = part_sum_ts<4, 4>(c, c.tid) * ts_lm;
             if (P.logits_out) P.logits_out[g.r0 + lr] = acc;
             if (acc > bestv) { bestv = acc; besti = g.r0 + lr; }
         }

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -189,6 +190,39 @@ __device__ __forceinline__ float dot4(const uint2& w, const float* x, float acc)
     acc = fmaf(bf_lo(w.x), x[0], acc); acc = fmaf(bf_hi(w.x), x[1], acc);
     acc = fmaf(bf_lo(w.y), x[2], acc); acc = fmaf(bf_hi(w.y), x[3], acc);
     return acc;
+}
+
+// ---- NVFP4 decoding without conversion instructions -------------------------------------------------------
+
+// Eight e2m1 codes (one 32-bit word, lowest nibble first) -> four f16x2 registers (codes 0|1, 2|3, 4|5, 6|7) with
+// byte permutes instead of conversion instructions: the cvt from e2m1 issues at a small fraction of the integer
+// rate on this GPU (a 64-row chunk spent ~2.3 us in conversions), and a row product converts every weight once.
+// An e2m1 magnitude is one of 8 values whose f16 encodings differ in the high byte only (00 38 3C 3E 40 42 44 46):
+// prmt looks four of them up at once, the packed nibbles being the selector; a second prmt spreads the bytes into
+// f16 positions; the sign comes from prmt's sign-replicate mode (the msb of byte j of w is the sign of code 2j+1,
+// that of w << 4 the sign of code 2j).
+__device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t w, uint32_t (&r)[4]) {
+    const uint32_t mag = w & 0x77777777u;
+    const uint32_t h_lo = __byte_perm(0x3E3C3800u, 0x46444240u, mag);          // f16 high bytes of codes 0..3
+    const uint32_t h_hi = __byte_perm(0x3E3C3800u, 0x46444240u, mag >> 16);    // codes 4..7
+    const uint32_t we = w << 4;
+    r[0] = __byte_perm(h_lo, 0u, 0x1404u) | (__byte_perm(we, w, 0xC080u) & 0x80008000u);
+    r[1] = __byte_perm(h_lo, 0u, 0x3424u) | (__byte_perm(we, w, 0xD090u) & 0x80008000u);
+    r[2] = __byte_perm(h_hi, 0u, 0x1404u) | (__byte_perm(we, w, 0xE0A0u) & 0x80008000u);
+    r[3] = __byte_perm(h_hi, 0u, 0x3424u) | (__byte_perm(we, w, 0xF0B0u) & 0x80008000u);
+}
+// E4M3 block scale (non-negative) as f16x2, without a conversion instruction: the f16 with bit pattern byte << 7
+// is exactly scale * 2^-8, for normal and subnormal E4M3 alike (same exponent / mantissa split, exponent bias 15
+// instead of 7; E4M3 subnormals land on f16 subnormals).  The factor 2^8 is applied with the tensor scale.
+// A code times such a scale has at most 6 significant bits and lies in [2^-18, 10.5]: exact in f16.
+constexpr float TS_SCALE_FOLD = 256.0f;
+__device__ __forceinline__ __half2 e4m3_to_h2_div256(uint32_t byte) {
+    const uint32_t v = (byte & 0xffu) * 0x00800080u;
+    return *reinterpret_cast<const __half2*>(&v);
+}
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, __half2 s) {
+    const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), s);
+    return *reinterpret_cast<const uint32_t*>(&r);
 }
 
 }  // namespace mk

@@ -499,6 +499,9 @@ cudaError_t ensure_ws(PrefillWs& w, int S, cudaStream_t stream = nullptr, bool c
 
 struct HostTable { const void* src = nullptr; int n = 0; size_t entry = 0; unsigned char rows[MAX_LAYERS * sizeof(LayerWeightsNVFP4)]; };
 HostTable g_tables[64];
+// host copy of a 224-byte-per-entry table (tensor-scale NVFP4), cached like the others
+struct HostTableTS { const void* src = nullptr; int n = 0; LayerWeightsNVFP4TS rows[MAX_LAYERS]; };
+HostTableTS g_tables_ts[64];
 thread_local char g_perr[200] = "";
 struct SparseCfg { bool enabled = false; double top_frac = 0.10; int window = 4, sink = 1; };
 SparseCfg g_sparse;
@@ -539,7 +542,10 @@ extern "C" unsigned int mk_prefill_workspace_generation(void) {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     return mk::g_ws_generation[dev];
 }
-extern "C" void mk_prefill_forget_tables(void) { for (auto& t : mk::g_tables) { t.src = nullptr; t.n = 0; } }
+extern "C" void mk_prefill_forget_tables(void) {
+    for (auto& t : mk::g_tables) { t.src = nullptr; t.n = 0; }
+    for (auto& t : mk::g_tables_ts) { t.src = nullptr; t.n = 0; }
+}
 extern "C" int mk_prefill_set_block_sparse(int enable, double top_frac, int window, int sink) {
     if (enable && (!(top_frac >= 0.0 && top_frac <= 1.0) || window < 1 || sink < 0)) return MK_ERR_BAD_ARG;
     mk::g_sparse.enabled = enable != 0;
@@ -774,6 +780,7 @@ int host_table(int dev, const void* layers, int num_layers, size_t entry, cudaSt
 }
 
 #include "decode_batch.cuh"
+#include "decode_batch_fp4.cuh"
 
 }  // namespace
 }  // namespace mk
@@ -1081,6 +1088,49 @@ int decode_batch_entry(int steps, int* tokens, int* positions, int* output_token
 }
 }  // namespace
 }  // namespace mk
+
+// Batched step(s) on the tensor-scale NVFP4 weights: the arguments of mk_decode_batch / mk_decode_batch_many with the
+// 224-byte table and the LM head's three tensors in place of the bf16 ones.
+extern "C" int mk_decode_batch_nvfp4_ts(
+    int steps, int* tokens, int* positions, int* output_tokens, int* tokens_log, int batch,
+    const void* embed_weight, const void* layers, const void* final_norm_w,
+    const void* lm_head_packed, const void* lm_head_scales_rows, const float* lm_head_tensor_scale,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs, void* final_normed, void* hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream) {
+    using namespace mk;
+    const void* req[] = {tokens, positions, embed_weight, layers, final_norm_w, lm_head_packed, lm_head_scales_rows,
+                         lm_head_tensor_scale, fa_k_cache, fa_v_cache, dn_states, conv_bufs};
+    int dev = 0;
+    int rc = check_common(req, 12, 1, max_seq_len, num_layers, vocab, dev);
+    if (rc != MK_OK) return rc;
+    if (batch < 1 || batch > BATCH_MAX) return pfail(MK_ERR_BAD_ARG, "batch must be in [1, 16]");
+    if (steps < 1 || (steps > 1 && !tokens_log) || (steps == 1 && !output_tokens && !tokens_log))
+        return pfail(MK_ERR_BAD_ARG, "bad step count or missing output");
+    HostTableTS& ht = g_tables_ts[dev];
+    if (ht.src != layers || ht.n != num_layers) {
+        PF_CHECK(cudaMemcpyAsync(ht.rows, layers, (size_t)num_layers * sizeof(LayerWeightsNVFP4TS), cudaMemcpyDeviceToHost, stream), "table copy");
+        PF_CHECK(cudaStreamSynchronize(stream), "table copy sync");
+        ht.src = layers; ht.n = num_layers;
+    }
+    int n_fa = 0;
+    for (int li = 0; li < num_layers; ++li) n_fa += ht.rows[li].layer_type != 0;
+    const int n_dn = num_layers - n_fa;
+    const Fp4Mat lm{(const uint8_t*)lm_head_packed, (const uint8_t*)lm_head_scales_rows, lm_head_tensor_scale};
+    if (steps == 1 && output_tokens)
+        return decode_batch_core_fp4(tokens, positions, output_tokens, batch, embed_weight, ht.rows, num_layers, n_fa, n_dn, final_norm_w,
+                                     lm, fa_k_cache, fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out, max_seq_len,
+                                     vocab, dev, stream);
+    PF_CHECK(ensure_batch_ws(g_bws[dev]), "batch workspace");
+    for (int s = 0; s < steps; ++s) {
+        rc = decode_batch_core_fp4(tokens, positions, g_bws[dev].chosen, batch, embed_weight, ht.rows, num_layers, n_fa, n_dn,
+                                   final_norm_w, lm, fa_k_cache, fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out,
+                                   max_seq_len, vocab, dev, stream);
+        if (rc != MK_OK) return rc;
+        launch_pdl(k_batch_advance, 1, 32, 0, stream, tokens, (const int*)g_bws[dev].chosen, positions, tokens_log + (size_t)s * batch, batch);
+    }
+    PF_CHECK(cudaGetLastError(), "batched steps launch");
+    return MK_OK;
+}
 
 extern "C" void mk_decode_batch_set_residual_kernel(int mode) { mk::g_batch_res_kernel = (mode >= 0 && mode <= 2) ? mode : 1; }
 extern "C" void mk_decode_batch_set_lm_head(int tensor_cores) { mk::g_batch_lm_mma = tensor_cores ? 1 : 0; }

@@ -75,14 +75,27 @@ def load_weights(model_name="Qwen/Qwen3.5-0.8B", verbose=True, seed=None, num_la
                  vocab=VOCAB_SIZE, norm_init="literal", device_init=False):
     """Returns (weights, tokenizer).  With `seed` set, seeded random-init weights of the
     architecture are produced (tokenizer None; drawn on the CPU unless device_init, see
-    weights.random_state_dict); otherwise the checkpoint `model_name` is
-    loaded through transformers, like the reference does (megakernel/model.py:66-157)."""
+    weights.random_state_dict); otherwise `model_name` is a local checkpoint directory (its safetensors
+    shards are read directly, see checkpoint.py) or a hub name loaded through transformers, like the
+    reference does (megakernel/model.py:66-157)."""
     if seed is not None:
         from .weights import random_state_dict
         dev = torch.device("cuda", torch.cuda.current_device()) if device_init else "cpu"
         sd = random_state_dict(seed, num_layers, vocab, norm_init, device=dev)
         return weights_from_state_dict(sd, device=torch.device("cuda", torch.cuda.current_device()),
                                        num_layers=num_layers), None
+    import os
+    if os.path.isdir(model_name):
+        # a local checkpoint directory: read the safetensors shards directly (no model object, no network)
+        from .checkpoint import weights_from_checkpoint
+        if verbose:
+            print(f"Reading checkpoint {model_name} (bf16)...")
+        weights = weights_from_checkpoint(model_name, device=torch.device("cuda", torch.cuda.current_device()))
+        tokenizer = None
+        if os.path.exists(os.path.join(model_name, "tokenizer_config.json")):
+            from transformers import AutoTokenizer
+            tokenizer = AutoTokenizer.from_pretrained(model_name)
+        return weights, tokenizer
     from transformers import AutoModelForCausalLM, AutoTokenizer
     if verbose:
         print(f"Loading {model_name} (bf16)...")
@@ -237,6 +250,26 @@ class Decoder:
         self.step_async(token_id)
         return int(self._out_token.item())
 
+    def step_sampled(self, token_id: int, temperature: float, top_k: int = 0, seed: int = 0) -> int:
+        """One decode step whose next token is drawn from softmax(logits / temperature) over the top_k largest
+        logits instead of the argmax (the repetition penalty, if any, is applied to the logits first, as in the greedy
+        path; reference hook: megakernel/kernel.cu:793-795).  Reproducible: the draw depends on (seed, position) only.
+        The step's logits stay in self._logits (f32 [vocab])."""
+        if not hasattr(self, "_logits"):
+            self._logits = torch.empty(self.vocab, dtype=torch.float32, device=self._embed_weight.device)
+        self._lib.mk_set_logits_buffer(_ptr(self._logits))
+        try:
+            self.step_async(token_id)
+        finally:
+            self._lib.mk_set_logits_buffer(ctypes.c_void_p(0))
+        rc = self._lib.mk_sample_top_k(_ptr(self._logits), ctypes.c_int(self.vocab), ctypes.c_float(float(temperature)),
+                                       ctypes.c_int(int(top_k)), ctypes.c_ulonglong(int(seed)),
+                                       ctypes.c_ulonglong(self._position), _ptr(self._out_token), self._stream())
+        if rc != 0:
+            self._lib.mk_sample_error.restype = ctypes.c_char_p
+            raise RuntimeError(f"sampling failed ({rc}): {self._lib.mk_sample_error().decode()}")
+        return int(self._out_token.item())
+
     def step_many(self, token_id: int, steps: int) -> torch.Tensor:
         """`steps` greedy steps with the token fed back on the device; returns the int32 device
         tensor of generated tokens without synchronising (bf16 counterpart of the reference's
@@ -331,14 +364,14 @@ class Decoder:
         self._conv_bufs.copy_(sd["conv_bufs"])
         self._seen_token_mask.copy_(sd["seen_token_mask"])
 
-    def generate_ids(self, prompt_ids, max_tokens=100, eos=None):
-        """Token-level generate: feeds the prompt token by token, then decodes greedily."""
+    def generate_ids(self, prompt_ids, max_tokens=100, eos=None, temperature=0.0, top_k=0, seed=0):
+        """Token-level generate: feeds the prompt token by token, then decodes greedily (temperature 0) or samples."""
         self.reset()
         for tid in prompt_ids[:-1]:
             self.step_async(int(tid))
         out, nxt = [], int(prompt_ids[-1])
         for _ in range(max_tokens):
-            nxt = self.step(nxt)
+            nxt = self.step(nxt) if not temperature > 0 else self.step_sampled(nxt, temperature, top_k, seed)
             if eos is not None and nxt == eos:
                 break
             out.append(nxt)
@@ -361,10 +394,17 @@ class BatchDecoder:
 
     MAX_BATCH = 16
 
-    def __init__(self, decoder: Decoder, batch: int):
+    def __init__(self, decoder: Decoder, batch: int, nvfp4_ts: bool = False):
+        """nvfp4_ts: the steps read the NVFP4 packing with a per-tensor scale (model_nvfp4.attach_nvfp4_ts_weights) instead
+        of the bf16 weights; prompts are still prefilled in bf16."""
         if not 1 <= batch <= self.MAX_BATCH:
             raise ValueError(f"batch must be in [1, {self.MAX_BATCH}]")
         self._d = decoder
+        self._ts = None
+        if nvfp4_ts:
+            from . import model_nvfp4 as MQ
+            nv = MQ.attach_nvfp4_ts_weights(decoder._weights)["nvfp4_ts"]
+            self._ts = {"table": MQ._pack_layer_weights_nvfp4_ts(nv["layer_data"]), "lm": nv["lm"]}
         self._lib = decoder._lib
         self.batch = int(batch)
         self.max_seq_len = decoder.max_seq_len
@@ -432,6 +472,12 @@ class BatchDecoder:
                 _ptr(self._fa_k_cache), _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs),
                 _ptr(d._fused_fa_qkv), _ptr(d._fused_gate_up))
 
+    def _args_ts(self):
+        d, t = self._d, self._ts
+        return (_ptr(d._embed_weight), _ptr(t["table"]), _ptr(d._final_norm_weight), _ptr(t["lm"]["packed"]),
+                _ptr(t["lm"]["scales"]), _ptr(t["lm"]["tensor_scale"]), _ptr(self._fa_k_cache), _ptr(self._fa_v_cache),
+                _ptr(self._dn_states), _ptr(self._conv_bufs))
+
     def step_async(self, tokens=None):
         """Enqueue one step for all sequences (inputs: `tokens`, or the tokens of the previous step / prefill).
         Returns the device int32[batch] tensor that will hold the chosen tokens.  Capturable into a CUDA graph
@@ -441,10 +487,16 @@ class BatchDecoder:
             raise ValueError("a sequence has reached max_seq_len")
         if tokens is not None:
             self._tokens.copy_(torch.as_tensor(tokens, dtype=torch.int32), non_blocking=True)
-        rc = self._lib.mk_decode_batch(
-            _ptr(self._tokens), _ptr(self._positions), _ptr(self._out_tokens), ctypes.c_int(self.batch), *self._args(),
-            _ptr(self._final_normed), _ptr(self._hidden_bf16_out), ctypes.c_int(self.max_seq_len),
-            ctypes.c_int(d.num_layers), ctypes.c_int(d.vocab), d._stream())
+        if self._ts is not None:
+            rc = self._lib.mk_decode_batch_nvfp4_ts(
+                ctypes.c_int(1), _ptr(self._tokens), _ptr(self._positions), _ptr(self._out_tokens), ctypes.c_void_p(0),
+                ctypes.c_int(self.batch), *self._args_ts(), _ptr(self._final_normed), _ptr(self._hidden_bf16_out),
+                ctypes.c_int(self.max_seq_len), ctypes.c_int(d.num_layers), ctypes.c_int(d.vocab), d._stream())
+        else:
+            rc = self._lib.mk_decode_batch(
+                _ptr(self._tokens), _ptr(self._positions), _ptr(self._out_tokens), ctypes.c_int(self.batch), *self._args(),
+                _ptr(self._final_normed), _ptr(self._hidden_bf16_out), ctypes.c_int(self.max_seq_len),
+                ctypes.c_int(d.num_layers), ctypes.c_int(d.vocab), d._stream())
         if rc != 0:
             self._fail(rc, "batched step")
         self._positions += 1
@@ -463,9 +515,15 @@ class BatchDecoder:
         if steps < 1 or max(self._host_positions) + steps > self.max_seq_len:
             raise ValueError("steps must be positive and stay within max_seq_len")
         log = torch.empty(steps, self.batch, dtype=torch.int32, device=self._tokens.device)
-        rc = self._lib.mk_decode_batch_many(
-            ctypes.c_int(steps), _ptr(self._tokens), _ptr(self._positions), _ptr(log), ctypes.c_int(self.batch), *self._args(),
-            ctypes.c_int(self.max_seq_len), ctypes.c_int(d.num_layers), ctypes.c_int(d.vocab), d._stream())
+        if self._ts is not None:
+            rc = self._lib.mk_decode_batch_nvfp4_ts(
+                ctypes.c_int(steps), _ptr(self._tokens), _ptr(self._positions), ctypes.c_void_p(0), _ptr(log),
+                ctypes.c_int(self.batch), *self._args_ts(), ctypes.c_void_p(0), ctypes.c_void_p(0),
+                ctypes.c_int(self.max_seq_len), ctypes.c_int(d.num_layers), ctypes.c_int(d.vocab), d._stream())
+        else:
+            rc = self._lib.mk_decode_batch_many(
+                ctypes.c_int(steps), _ptr(self._tokens), _ptr(self._positions), _ptr(log), ctypes.c_int(self.batch), *self._args(),
+                ctypes.c_int(self.max_seq_len), ctypes.c_int(d.num_layers), ctypes.c_int(d.vocab), d._stream())
         if rc != 0:
             self._fail(rc, "batched steps")
         self._host_positions = [p + steps for p in self._host_positions]
