@@ -183,6 +183,32 @@ int mk_decode_nvfp4_ts(
     void *hidden_buffer, void *g_normalized, int position, int max_seq_len, cudaStream_t stream);
 int mk_nvfp4_scales_to_rows(const void *tiled_scales, int rows, int cols, void *rows_out, cudaStream_t stream);
 
+/* The decode of mk_decode_nvfp4_ts on the block-scaled 5th-generation tensor cores: tcgen05.mma kind::mxf4nvf4 reads
+ * the e2m1 codes from shared memory and the E4M3 block scales from tensor memory, accumulators live in tensor memory.
+ * Same quantised values and tensor scales as mk_decode_nvfp4_ts, same 224-byte table, except that the FIRST slot of
+ * each phase's matrix group (DeltaNet: qkv, out, gate, down; attention: q, o, gate, down) points at an array of 148
+ * chunk images, one per CTA of the decode grid, holding that CTA's rows of the phase (qkv|z, q|k|v, out, gate|up,
+ * down) in the operand layout of the MMA, and lm_head_images at 148 x lm_image_chunks images of 56 LM-head rows
+ * (the down projection has two images per CTA, one per half of K):
+ *   codes : K/256 tiles of RP x 128 bytes (RP = 56, 40, 8, 56, 8; 56 for the LM head); tile t, local row i = codes
+ *           k = 256 t .. 256 t + 255 of that row, its eight 16-byte pieces stored at piece j ^ (i % 8);
+ *   scales: one unit of 32 lanes x 16 bytes (one tcgen05.cp) per MMA step of 64 k: unit ks, lane l, byte 4 g + b =
+ *           the scale of block b of row l + 32 g in that step; bytes of absent rows are zero;
+ *   CTA c owns rows [n c / 148, n (c + 1) / 148) of the phase's n rows; gate row o and up row o of an output sit at
+ *   local rows o - first and 28 + o - first; image sizes 36864, 28672, 24576, 36864, 2 x 21504 and 36864 bytes.
+ * (luce_megakernel_b200/nvfp4_images.py builds them from the quantiser's output.)  The activation vector of every
+ * projection is the other operand: it is scaled to a fixed range and expanded on the fly into act_terms (1..8) NVFP4
+ * residual terms, term n + 1 encoding six times what term n left over, one MMA column per term; 8 terms reproduce
+ * the f32 vector to about 1e-6 of each block's largest value, 4 terms to better than bf16.  Needs a device that
+ * co-schedules 148 CTAs.  No counterpart in the reference (its NVFP4 decode dequantises through a LUT and multiplies
+ * on mma.sync, megakernel/kernel_gb10_nvfp4.cu:528-552). */
+int mk_decode_nvfp4_mma(
+    int *token_buffer, int *output_tokens, int steps,
+    const void *embed_weight, const void *layer_weights, const void *final_norm_weight,
+    const void *lm_head_images, int lm_image_chunks, const float *lm_head_tensor_scale,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *hidden_buffer, void *g_normalized, int position, int max_seq_len, int act_terms, cudaStream_t stream);
+
 /* Prefill of a prompt of seq_len tokens from position 0: fills the KV caches for positions
  * 0..seq_len-1, advances the DeltaNet and conv state from their current content (callers zero
  * them first), writes the first generated token to output_token, the last row's final-normed
@@ -362,6 +388,19 @@ int mk_attention_prefill(const void *qkv, const void *k_cache, const void *v_cac
  * (reference: megakernel/prefill.cu:1526-1534).  N % 128 == 0, K % 64 == 0, 16-byte aligned pointers. */
 int mk_gemm_bf16_tn(const void *A, const void *W, void *C, const void *residual, int M, int N, int K,
                     cudaStream_t stream);
+
+/* NVFP4 x NVFP4 product on the block-scaled tensor-core path (tcgen05.mma kind::mxf4nvf4, E4M3 scales per 16 values
+ * read from tensor memory): C[M,N] = a_tensor_scale[0] * w_tensor_scale[0] * (A[M,K] . W[N,K]^T) (+ residual), C and
+ * residual bf16 row-major.  Both operands in the format mk_quantize_nvfp4_tensor_scale writes (packed e2m1 rows, 128 x 4
+ * scale tiles, device fp32 tensor scale); an operand with M % 128 != 0 is quantised from a zero-padded copy, so that
+ * its scale array covers whole 128-row blocks.  No counterpart in the reference, which dequantises NVFP4 weights to
+ * bf16 for cuBLAS in prefill (megakernel/kernel_gb10_nvfp4.cu:2127-2145) and multiplies them on mma.sync in decode
+ * (megakernel/kernel_gb10_nvfp4.cu:528-552).  N % 128 == 0, K % 256 == 0, 16-byte aligned pointers.
+ * mk_gemm_nvfp4_status: 0, or 1 after a bounded wait inside the kernel ran out (synchronises the device). */
+int mk_gemm_nvfp4_tn(const void *a_packed, const void *a_scales, const float *a_tensor_scale, const void *w_packed,
+                     const void *w_scales, const float *w_tensor_scale, void *C, const void *residual, int M, int N, int K,
+                     cudaStream_t stream);
+int mk_gemm_nvfp4_status(void);
 
 /* Model depth and vocabulary the entry points assume (defaults 24 and 248320, the
  * compile-time constants of the reference: megakernel/kernel.cu:20,22).  Reduced values let

@@ -335,6 +335,54 @@ int mk_decode_nvfp4_ts(
     return MK_OK;
 }
 
+// The same decode on the block-scaled tensor cores (tcgen05.mma kind::mxf4nvf4): the table's matrix slots and
+// lm_head_images point at per-CTA chunk images (see the header), the activation is expanded into act_terms NVFP4
+// residual terms.
+int mk_decode_nvfp4_mma(
+    int* token_buffer, int* output_tokens, int steps,
+    const void* embed_weight, const void* layer_weights, const void* final_norm_weight,
+    const void* lm_head_images, int lm_image_chunks, const float* lm_head_tensor_scale,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden_buffer, void* g_normalized, int position, int max_seq_len, int act_terms, cudaStream_t stream) {
+    if (!token_buffer || !output_tokens || !embed_weight || !layer_weights || !final_norm_weight || !lm_head_images ||
+        !lm_head_tensor_scale || !fa_k_cache || !fa_v_cache || !dn_states || !conv_bufs || !hidden_buffer || !g_normalized)
+        return set_err(MK_ERR_BAD_ARG, "null pointer argument");
+    if (steps < 0) return set_err(MK_ERR_BAD_ARG, "steps must be non-negative");
+    if (steps == 0) return MK_OK;
+    if (max_seq_len <= 0 || position < 0 || position + steps > max_seq_len)
+        return set_err(MK_ERR_BAD_ARG, "position + steps exceeds max_seq_len");
+    if (act_terms < 1 || act_terms > 8) return set_err(MK_ERR_BAD_ARG, "act_terms must be in [1, 8]");
+    const int ctas = mk::decode_image_ctas();
+    if (lm_image_chunks < 1 || (long long)lm_image_chunks * 56 * ctas < (long long)g_vocab)
+        return set_err(MK_ERR_BAD_ARG, "lm_image_chunks does not cover the vocabulary");
+    const void* al[] = {embed_weight, layer_weights, final_norm_weight, lm_head_images, fa_k_cache,
+                        fa_v_cache, dn_states, conv_bufs, hidden_buffer, g_normalized};
+    for (const void* q : al)
+        if (misaligned16(q)) return set_err(MK_ERR_BAD_ARG, "pointer argument is not 16-byte aligned");
+    DeviceState* d = nullptr;
+    int rc = device_state(&d);
+    if (rc) return rc;
+    if ((rc = check_device_status(*d, stream))) return rc;
+    if (d->max_grid < ctas) return set_err(MK_ERR_BAD_ARG, "the device cannot co-schedule the 148 CTAs the chunk images are cut for");
+    mk::DecodeParams p;
+    memset(&p, 0, sizeof(p));
+    p.embed = embed_weight; p.layers = layer_weights; p.final_norm = final_norm_weight;
+    p.lm_head = lm_head_images; p.lm_image_chunks = lm_image_chunks; p.lm_tensor_scale = lm_head_tensor_scale; p.wfmt = 3;
+    p.act_terms = act_terms;
+    p.k_cache = fa_k_cache; p.v_cache = fa_v_cache; p.dn_states = (float*)dn_states; p.conv_bufs = (float*)conv_bufs;
+    p.hidden = hidden_buffer; p.normalized = (float*)g_normalized;
+    p.seen_mask = nullptr; p.rep_penalty = 1.0f;
+    p.token_ptr = token_buffer; p.token_val = 0; p.out_token = output_tokens; p.token_feedback = token_buffer;
+    p.position = position; p.max_seq_len = max_seq_len; p.num_layers = g_num_layers; p.vocab = g_vocab;
+    p.ws = d->ws; p.host_status = d->host_status_dev; p.trace = g_trace; p.trace_slots = g_trace_slots;
+    p.poll_limit_cycles = g_poll_limit; p.mbar_limit_tries = g_mbar_tries;
+    p.steps = steps; p.logits_out = g_logits;
+    mk::fill_rope(p);
+    cudaError_t e = mk::launch_decode_kernel(p, ctas, stream);
+    if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
+    return MK_OK;
+}
+
 void set_decode_blocks_override(int blocks) { g_blocks_override = blocks < 0 ? 0 : blocks; }
 
 int query_max_safe_decode_blocks(void) {
@@ -379,6 +427,8 @@ void mk_clear_error(void) {
     g_err[0] = 0;
 }
 
+static int* g_nvfp4_gemm_err = nullptr;
+
 int mk_gemm_bf16_tn(const void* A, const void* W, void* C, const void* residual, int M, int N, int K,
                     cudaStream_t stream) {
     if (!A || !W || !C) return set_err(MK_ERR_BAD_ARG, "null pointer argument");
@@ -392,6 +442,33 @@ int mk_gemm_bf16_tn(const void* A, const void* W, void* C, const void* residual,
     if (e == cudaErrorInvalidValue) return set_err(MK_ERR_BAD_ARG, "gemm shape or alignment not supported (N % 128, K % 64, 16-byte pointers)");
     if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "gemm launch", e);
     return MK_OK;
+}
+
+int mk_gemm_nvfp4_tn(const void* a_packed, const void* a_scales, const float* a_tensor_scale, const void* w_packed,
+                     const void* w_scales, const float* w_tensor_scale, void* C, const void* residual, int M, int N, int K,
+                     cudaStream_t stream) {
+    if (!a_packed || !a_scales || !a_tensor_scale || !w_packed || !w_scales || !w_tensor_scale || !C)
+        return set_err(MK_ERR_BAD_ARG, "null pointer argument");
+    static int* err_flag = nullptr;
+    if (!err_flag) {
+        cudaError_t e0 = cudaMalloc(&err_flag, sizeof(int));
+        if (e0 != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaMalloc(gemm status)", e0);
+        cudaMemset(err_flag, 0, sizeof(int));
+    }
+    cudaError_t e = mk::gemm_nvfp4_tn(a_packed, a_scales, a_tensor_scale, w_packed, w_scales, w_tensor_scale, C, residual, M, N, K,
+                                      N, err_flag, stream);
+    if (e == cudaErrorInvalidValue)
+        return set_err(MK_ERR_BAD_ARG, "nvfp4 gemm shape or alignment not supported (N % 128, K % 256, 16-byte pointers)");
+    if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "nvfp4 gemm launch", e);
+    g_nvfp4_gemm_err = err_flag;
+    return MK_OK;
+}
+
+int mk_gemm_nvfp4_status(void) {
+    if (!g_nvfp4_gemm_err) return 0;
+    int v = 0;
+    if (cudaMemcpy(&v, g_nvfp4_gemm_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    return v;
 }
 
 void mk_set_decode_steps_per_launch(int steps) { g_steps_per_launch = steps > 0 ? steps : 0; }

@@ -39,7 +39,8 @@ namespace {
 constexpr int NCW = 16;                    // consumer warps
 constexpr int NCT = NCW * 32;              // consumer threads
 constexpr int NTHREADS = NCT + 32;         // + producer warp
-constexpr int MAX_STAGES = 6;               // ring stages: 6 x 32 KB (bf16, NVFP4 layer format) or 5 x 36 KB (tensor-scale NVFP4)
+constexpr int MAX_STAGES = 6;               // ring stages: 6 x 32 KB (bf16, NVFP4 layer format), 5 x 36 KB (tensor-scale NVFP4) or
+                                            // 4 x 36 KB plus the tensor-core activation operand (tensor-scale NVFP4 on tcgen05)
 constexpr int RING_BYTES = 196608;
 constexpr int XK = 224;                    // largest K-slice of a warp (elements)
 constexpr int XSW = 3 * XK / 2;            // 32-bit words of staging per warp: three bf16 planes of XK elements
@@ -121,7 +122,28 @@ namespace {
 }  // namespace
 }  // namespace traced_ts
 
+namespace nvfp4mma {
+namespace {
+#define MK_TRACE 0
+#define MK_WFMT 3
+#include "decode_body.cuh"
+#undef MK_WFMT
+#undef MK_TRACE
+}  // namespace
+}  // namespace nvfp4mma
+
+namespace traced_mma {
+namespace {
+#define MK_TRACE 1
+#define MK_WFMT 3
+#include "decode_body.cuh"
+#undef MK_WFMT
+#undef MK_TRACE
+}  // namespace
+}  // namespace traced_mma
+
 size_t decode_smem_bytes() { return SMEM_BYTES; }
+int decode_image_ctas() { return nvfp4mma::U_CTAS; }
 
 int decode_max_grid() {
     int dev = 0, sms = 0, per_sm = 0;
@@ -156,11 +178,19 @@ cudaError_t launch_decode_kernel(const DecodeParams& p, int grid, cudaStream_t s
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(traced_ts::decode_megakernel_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(nvfp4mma::decode_megakernel_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(traced_mma::decode_megakernel_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
         attr_done[dev] = true;
     }
     if (grid < MIN_GRID || grid > MAX_GRID) return cudaErrorInvalidConfiguration;
     void* args[] = {(void*)&p};
-    const void* fn = (p.wfmt == 2 && p.trace) ? (const void*)traced_ts::decode_megakernel_bf16
+    if (p.wfmt == 3 && (grid != nvfp4mma::U_CTAS || p.act_terms < 1 || p.act_terms > 8 || p.lm_image_chunks < 1))
+        return cudaErrorInvalidConfiguration;
+    const void* fn = (p.wfmt == 3 && p.trace) ? (const void*)traced_mma::decode_megakernel_bf16
+                   : p.wfmt == 3 ? (const void*)nvfp4mma::decode_megakernel_bf16
+                   : (p.wfmt == 2 && p.trace) ? (const void*)traced_ts::decode_megakernel_bf16
                    : p.wfmt == 2 ? (const void*)nvfp4ts::decode_megakernel_bf16
                    : p.wfmt == 1 ? (const void*)nvfp4::decode_megakernel_bf16
                    : p.trace   ? (const void*)traced::decode_megakernel_bf16

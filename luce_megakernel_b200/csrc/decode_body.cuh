@@ -36,18 +36,68 @@ __device__ __forceinline__ constexpr int scale_bytes(int K) { return K / 16; }
 // block scales (R * K/16 bytes): two bulk copies per matrix the chunk touches.  R = 64 for K = 1024, 32 for
 // K = 2048, 16 for K = 3584, so every phase of a layer is ONE chunk per CTA.  The table entry has three slots per
 // quantised matrix: packed data, row-major scales, pointer to the tensor scale.
+// MK_WFMT 3: the same quantised values, multiplied on the block-scaled 5th-generation tensor cores (tcgen05.mma
+// kind::mxf4nvf4, accumulators and block scales in tensor memory).  The table's first slot of every phase's matrix
+// group points at an array of per-CTA chunk IMAGES instead of plain rows: image c holds the rows CTA c owns in that
+// phase, already in the shared-memory layout the MMA reads (K-major, 128-byte swizzle, 256 values per 128-byte row
+// segment, k-tile after k-tile), followed by the rows' block scales in the order tcgen05.cp lays them into tensor
+// memory, so that a phase is ONE bulk copy per CTA.  Images are built for a grid of exactly U_CTAS CTAs.  The
+// activation vector is the B operand: quantised on the fly into up to eight NVFP4 residual terms (term n+1 encodes
+// six times what term n left over), one MMA column each, recombined after the product.
 typedef LayerWeightsNVFP4TS LW;
+#if MK_WFMT == 3
+constexpr int NSTAGE = 4;                               // the attention phase needs four chunks resident at once
+constexpr int STAGE_BYTES = 36864;                      // 56 rows of K = 1024: 28 KB of codes + 16 scale units of 512 B
+#else
 constexpr int NSTAGE = 5;
 constexpr int STAGE_BYTES = 36864;                      // 64 rows of K = 1024: 32 KB of codes + 4 KB of scales
+#endif
 enum { DN_IN_NORM = 0, DN_W_QKV = 1, DN_W_Z = 4, DN_W_B = 7, DN_W_A = 8, DN_CONV_W = 9, DN_A_LOG = 10, DN_DT_BIAS = 11,
        DN_NORM_W = 12, DN_W_OUT = 13, DN_POST_NORM = 16, DN_W_GATE = 17, DN_W_UP = 20, DN_W_DOWN = 23 };
 enum { FA_IN_NORM = 0, FA_W_Q = 1, FA_W_K = 4, FA_W_V = 7, FA_Q_NORM = 10, FA_K_NORM = 11, FA_W_O = 12, FA_POST_NORM = 15,
        FA_W_GATE = 16, FA_W_UP = 19, FA_W_DOWN = 22 };
 constexpr int IN_ROWS_DN = DN_CONV_CH + DN_V;           // qkv | z (beta / alpha stay bf16, outside the ring)
+#if MK_WFMT == 3
+constexpr int LM_RPC = 56;                              // LM-head rows per chunk image
+constexpr int UP_ROW0 = 28;                             // local row of the first up-projection row in a gate|up chunk
+#else
 constexpr int LM_RPC = 64;
+constexpr int UP_ROW0 = 32;
+#endif
 __device__ __forceinline__ constexpr int row_bytes(int K) { return K / 2; }
 __device__ __forceinline__ constexpr int scale_bytes(int K) { return K / 16; }
 __device__ __forceinline__ constexpr int rows_per_chunk(int K) { return K == 1024 ? 64 : (K == 2048 ? 32 : 16); }
+#if MK_WFMT == 3
+constexpr int U_CTAS = 148;                             // the grid the chunk images are cut for
+constexpr int U_OFF_B = NSTAGE * STAGE_BYTES;           // activation terms: 8 rows x K/2 bytes, swizzled like the weights
+constexpr int U_B_BYTES = 8 * (INTER / 2);
+constexpr int U_OFF_SFB = U_OFF_B + U_B_BYTES;          // their block scales: one 512-byte copy unit per MMA step (64 k)
+constexpr int U_SFB_BYTES = (INTER / 64) * 512;
+constexpr int U_OFF_BARS = U_OFF_SFB + U_SFB_BYTES;     // MMA-done barriers [2], accumulator-free barriers [2]
+constexpr int U_OFF_TMEM = U_OFF_BARS + 32;             // tensor-memory base address
+constexpr int U_OFF_AMAX = U_OFF_BARS + 64;             // per-warp maxima of the staged activation [16]
+static_assert(U_OFF_AMAX + 64 <= RING_BYTES, "tensor-core operands do not fit behind the ring");
+// tensor-memory columns: accumulator buffers at 0 and 32 (8 columns each); block scales take four columns per MMA
+// step and operand (the unit one tcgen05.cp writes, which is also the alignment the MMA is given): weights from
+// column 64, activation from column 288, 56 steps each at most
+constexpr uint32_t U_TM_COLS = 512;
+constexpr uint32_t U_TM_SFA = 64, U_TM_SFB = 288;
+// padded row count of a CTA's chunk per phase, and the image size (codes + scales)
+__device__ __forceinline__ constexpr int u_rp(int type) {
+    return (type == T_DN_IN || type == T_GATEUP || type == T_LM) ? 56 : type == T_FA_IN ? 40 : 8;
+}
+__device__ __forceinline__ constexpr int u_k(int type) {           // K of the whole product
+    return (type == T_DN_OUT || type == T_FA_OUT) ? 2048 : type == T_DOWN ? INTER : HIDDEN;
+}
+__device__ __forceinline__ constexpr int u_kc(int type) {          // K of one chunk image: the down projection takes two
+    return type == T_DOWN ? INTER / 2 : u_k(type);
+}
+__device__ __forceinline__ constexpr int u_img_bytes(int type) {
+    return u_rp(type) * (u_kc(type) / 2) + (u_kc(type) / 64) * 512;
+}
+static_assert(u_img_bytes(T_GATEUP) <= STAGE_BYTES && u_img_bytes(T_DOWN) <= STAGE_BYTES && u_img_bytes(T_DN_OUT) <= STAGE_BYTES,
+              "image exceeds a ring stage");
+#endif
 #endif
 static_assert(NSTAGE * STAGE_BYTES <= RING_BYTES && NSTAGE <= MAX_STAGES, "ring does not fit its region");
 
@@ -81,13 +131,17 @@ __device__ __forceinline__ Geo phase_geo(int type, int cta, int G, int vocab, in
     g.r0 = g.r1 = 0;
     g.nchunks = 0;
     switch (type) {
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
         case T_DN_IN:  split_rows(IN_ROWS_DN, G, cta, g.r0, g.r1);  g.nchunks = (g.r1 - g.r0 + 63) >> 6; break;
         case T_FA_IN:  split_rows(FA_QKV_ROWS, G, cta, g.r0, g.r1); g.nchunks = (g.r1 - g.r0 + 63) >> 6; break;
         case T_DN_OUT:
         case T_FA_OUT: split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = (g.r1 - g.r0 + 31) >> 5; break;
         case T_GATEUP: split_rows(INTER, G, cta, g.r0, g.r1);       g.nchunks = (g.r1 - g.r0 + 31) >> 5; break;
+#if MK_WFMT == 3
+        case T_DOWN:   split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = 2; break;      // two K halves
+#else
         case T_DOWN:   split_rows(HIDDEN, G, cta, g.r0, g.r1);      g.nchunks = (g.r1 - g.r0 + 15) >> 4; break;
+#endif
 #else
         case T_DN_IN:  split_rows(IN_ROWS_DN, G, cta, g.r0, g.r1);  g.nchunks = (g.r1 - g.r0 + 15) >> 4; break;
         case T_FA_IN:  split_rows(FA_QKV_ROWS, G, cta, g.r0, g.r1); g.nchunks = (g.r1 - g.r0 + 15) >> 4; break;
@@ -130,7 +184,7 @@ __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const
         dst_off = lane * ATT_ROW_STRIDE;
         return FA_HEAD_DIM * 2;
     }
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     if (type == T_DN_REC) {
         if (lane != 0) return 0;
         const int u = g.r0 + q * G;
@@ -139,6 +193,31 @@ __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const
         dst_off = 0;
         return 16 * DN_KEY * 4;
     }
+#if MK_WFMT == 3
+    {
+        // one image per CTA and phase (per chunk for the LM head), copied as it lies
+        if (lane != 0 || q >= g.nchunks) return 0;
+        const bool dn = (lw.layer_type == 0);
+        const uint32_t img = (uint32_t)u_img_bytes(type);
+        if (type == T_LM) {
+            src = (const char*)P.lm_head + ((size_t)cta_of_geo * P.lm_image_chunks + q) * img;
+        } else {
+            int slot;
+            switch (type) {
+                case T_DN_IN: slot = DN_W_QKV; break;
+                case T_FA_IN: slot = FA_W_Q; break;
+                case T_DN_OUT: slot = DN_W_OUT; break;
+                case T_FA_OUT: slot = FA_W_O; break;
+                case T_GATEUP: slot = dn ? (int)DN_W_GATE : (int)FA_W_GATE; break;
+                case T_DOWN: slot = dn ? (int)DN_W_DOWN : (int)FA_W_DOWN; break;
+                default: return 0;
+            }
+            src = (const char*)lw.ptrs[slot] + ((size_t)cta_of_geo * g.nchunks + q) * img;
+        }
+        dst_off = 0;
+        return img;
+    }
+#else
     {
         // Stage layout: the chunk's R rows of packed codes, contiguous (R * K/2 bytes), then their R rows of block scales.
         // lane = 2 * segment + kind: segment = a matrix the chunk's rows fall into (at most 3; gate / up for the SwiGLU
@@ -185,6 +264,7 @@ __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const
         dst_off = region + (uint32_t)(a - ra) * unit;
         return (uint32_t)(b - a) * unit;
     }
+#endif   // MK_WFMT == 3
 #else
 #if MK_WFMT == 0
     const int slot = lane, kind = 0;
@@ -270,7 +350,7 @@ __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const
     dst_off = rpc * row_stride(K) + slot * scale_bytes(K);
     return scale_bytes(K);
 #endif
-#endif   // MK_WFMT == 2
+#endif   // MK_WFMT >= 2
 }
 
 struct Ctx {
@@ -290,6 +370,11 @@ struct Ctx {
     int pos;              // position of the token being decoded in this step
     int step;             // index of the step inside this launch
     const float* rope;    // shared memory: cos[32] | sin[32] of pos * inv_freq_i, recomputed every step
+    // tcgen05 variant only
+    float amax;           // largest |value| this thread staged for the coming row product
+    uint32_t mma_n;       // row products issued so far: selects the accumulator buffer and the barrier phases
+    uint32_t tmem;        // base address of the CTA's tensor-memory allocation
+    float inv_g;          // 1 / normalisation factor of the staged activation
 };
 
 // A bounded wait ran out (or another CTA reported one): from here on every wait of this CTA
@@ -439,7 +524,7 @@ __device__ __forceinline__ uint32_t chunk_runs(const DecodeParams& P, Ctx& c, in
                                                uint32_t& run_bytes) {
     uint32_t bytes = chunk_slot_src(type, lw, P, g, q, c.lane, c.G, idx, src, dst_off, c.cta, pos);
     if (bytes && (((uintptr_t)src) & 15u)) { fail(P, c, ST_MISALIGNED); bytes = 0; }
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     // every lane already describes a whole run (a row group, or a matrix's scale rows) of its own size: no merging
     // (two matrices that happen to lie back to back in memory must not be taken for one run of equal pieces)
     if (type != T_FA_ATT) {
@@ -692,8 +777,8 @@ __device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, in
 // Activations: part p of the K dimension is staged as three f16 planes of 256 elements (hi / mid / lo terms) at
 // xs + p * 384 words, written by whichever warps own those elements and read by the RT warps of that part.
 template <int PK>
-__device__ __forceinline__ void stage_pair_ts(uint32_t* xs_words, int e, float x0, float x1) {
-    uint32_t* xw = xs_words + (e / PK) * (3 * PK / 2);
+__device__ __forceinline__ void stage_pair_ts(Ctx& c, int e, float x0, float x1) {
+    uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + (e / PK) * (3 * PK / 2);
     const int l = e % PK;
     uint32_t h0, m0, l0, h1, m1, l1;
     split3(x0, h0, m0, l0);
@@ -703,8 +788,8 @@ __device__ __forceinline__ void stage_pair_ts(uint32_t* xs_words, int e, float x
     xw[PK + (l >> 1)] = __byte_perm(l0, l1, 0x7632);
 }
 template <int PK>
-__device__ __forceinline__ void stage_one_ts(uint32_t* xs_words, int e, float x) {
-    unsigned short* p = reinterpret_cast<unsigned short*>(xs_words + (e / PK) * (3 * PK / 2));
+__device__ __forceinline__ void stage_one_ts(Ctx& c, int e, float x) {
+    unsigned short* p = reinterpret_cast<unsigned short*>(reinterpret_cast<uint32_t*>(c.xs) + (e / PK) * (3 * PK / 2));
     const int l = e % PK;
     uint32_t h, m, lo;
     split3(x, h, m, lo);
@@ -814,7 +899,210 @@ __device__ __forceinline__ float tensor_scale_of(const LW& lw, int slot) {
 }
 #endif
 
-#if MK_WFMT != 2
+#if MK_WFMT == 3
+// ---- tensor-scale NVFP4 on tcgen05: the CTA's rows of a phase x the activation as NVFP4 residual terms ---------
+// A (weights): the chunk image in the ring stage, M = 128 rows of which the first u_rp(type) are real (what lies
+// behind them in shared memory feeds accumulator rows nobody reads).  B (activation): up to 8 rows, one per residual
+// term, quantised by the consumer warps into U_OFF_B / U_OFF_SFB.  D: 128 lanes x 8 columns of tensor memory, one of
+// two buffers.  Block scales: one tcgen05.cp (32 lanes x 16 bytes, replicated to the four lane quadrants) per MMA step
+// and operand fills four columns: row r of the operand reads lane r % 32, column r / 32, one byte per 16-value block.
+template <int PK>
+__device__ __forceinline__ void stage_pair_ts(Ctx& c, int e, float x0, float x1) {
+    reinterpret_cast<float2*>(c.xs)[e >> 1] = make_float2(x0, x1);
+    c.amax = fmaxf(c.amax, fmaxf(fabsf(x0), fabsf(x1)));
+}
+template <int PK>
+__device__ __forceinline__ void stage_one_ts(Ctx& c, int e, float x) {
+    c.xs[e] = x;
+    c.amax = fmaxf(c.amax, fabsf(x));
+}
+
+__device__ __forceinline__ uint64_t u_desc_sw128(uint32_t saddr) {   // K-major, 128-byte swizzle, 8-row groups 1024 B apart
+    return (uint64_t)((saddr & 0x3ffffu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
+           ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ uint64_t u_desc_sf(uint32_t saddr) {      // 32 rows of 16 bytes, no swizzle, 8-row groups 128 B apart
+    return (uint64_t)((saddr & 0x3ffffu) >> 4) | ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
+}
+// kind::mxf4nvf4, e2m1 x e2m1, E4M3 block scales, K-major operands, M = 128, N = 8
+constexpr uint32_t U_IDESC = (1u << 7) | (1u << 10) | ((8u >> 3) << 17) | ((128u >> 4) << 24);
+__device__ __forceinline__ void u_mma(uint32_t d, uint64_t ad, uint64_t bd, uint32_t sfa, uint32_t sfb, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        ::"r"(d), "l"(ad), "l"(bd), "r"(U_IDESC), "r"(acc), "r"(sfa), "r"(sfb) : "memory");
+}
+__device__ __forceinline__ void u_cp_sf(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+__device__ __forceinline__ void u_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void u_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void u_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float e4m3_value(uint32_t code) {       // code << 7 read as f16 is the value / 256
+    return __half2float(__ushort_as_half((unsigned short)(code << 7))) * 256.0f;
+}
+// eight floats -> eight e2m1 codes, element 0 in the low nibble (round to nearest even, saturating at 6)
+__device__ __forceinline__ uint32_t f32x8_to_e2m1x8(const float (&v)[8]) {
+    uint32_t w;
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+        "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+        : "=r"(w)
+        : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+    return w;
+}
+
+// The staged f32 vector (c.xs[0..K)) -> P.act_terms NVFP4 residual terms in the B operand layout.  Two threads per
+// 16-element block.  x is first scaled by g = 192 / max|x| so that block scales start at or below 32 whatever the
+// vector's magnitude; term n holds round(r_n / s_n) with s_n = E4M3 rounded UP from max|r_n| / 6 (no clipping), and
+// r_{n+1} = 6 (r_n - s_n code_n): a term leaves at most s_n <= max|r_n| / 6 (1 + 1/8) behind, so block scales never
+// grow by more than 9/8 per term and stay far inside E4M3.  x = (1/g) sum_n 6^-n s_n code_n up to the last residual.
+// Ends with the barrier that makes the operand visible to the issuing thread; returns nothing, sets c.inv_g.
+__device__ __forceinline__ void u_prepare_acts(const DecodeParams& P, Ctx& c, int K) {
+    float* wmax = reinterpret_cast<float*>(c.smem + U_OFF_AMAX);
+    const float m = warp_max(c.amax);
+    c.amax = 0.f;
+    if (c.lane == 0) wmax[c.warp] = m;
+    named_bar_sync(1, NCT);                       // the vector is staged, the warp maxima are written
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) am = fmaxf(am, wmax[i]);
+    const float g = (am > 0.f && am < 3.0e38f) ? 192.0f / am : 1.0f;
+    c.inv_g = 1.0f / g;
+    const int b = c.tid >> 1, h = c.tid & 1;
+    if (b < K / 16) {
+        float r[8];
+        {
+            const float4 a = *reinterpret_cast<const float4*>(c.xs + 16 * b + 8 * h);
+            const float4 d = *reinterpret_cast<const float4*>(c.xs + 16 * b + 8 * h + 4);
+            r[0] = a.x * g; r[1] = a.y * g; r[2] = a.z * g; r[3] = a.w * g;
+            r[4] = d.x * g; r[5] = d.y * g; r[6] = d.z * g; r[7] = d.w * g;
+        }
+        const int bb = b & 15;
+        char* brow = c.smem + U_OFF_B + (b >> 4) * 1024 + (bb & 1) * 8 + h * 4;
+        unsigned char* sfb = reinterpret_cast<unsigned char*>(c.smem) + U_OFF_SFB + (b >> 2) * 512 + (b & 3);
+        const int terms = P.act_terms;
+#pragma unroll 1
+        for (int n = 0; n < terms; ++n) {
+            float a = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(r[i]));
+            a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+            const float t = a * (1.0f / 6.0f);
+            uint32_t code = (uint32_t)__nv_cvt_float_to_fp8(t, __NV_SATFINITE, __NV_E4M3);
+            float sv = e4m3_value(code);
+            if (sv < t && code < 0x7eu) { ++code; sv = e4m3_value(code); }
+            if (code == 0u) { code = 1u; sv = 0.001953125f; }
+            const float inv = __fdividef(1.0f, sv);
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = r[i] * inv;
+            const uint32_t w = f32x8_to_e2m1x8(v);
+            uint32_t hh[4];
+            e2m1x8_to_f16x2x4(w, hh);
+            const float s6 = -6.0f * sv;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hh[i]));
+                r[2 * i] = fmaf(f.x, s6, 6.0f * r[2 * i]);
+                r[2 * i + 1] = fmaf(f.y, s6, 6.0f * r[2 * i + 1]);
+            }
+            *reinterpret_cast<uint32_t*>(brow + n * 128 + (((bb >> 1) ^ n) << 4)) = w;
+            if (h == 0) sfb[n * 16] = (unsigned char)code;
+        }
+    }
+    fence_proxy_async();                          // the tensor core reads shared memory through the async proxy
+    named_bar_sync(1, NCT);
+}
+
+// Thread 0: scale copies and the K / 64 MMAs of one chunk in `stage`, product number m; arrives on the product's
+// barrier when the tensor core is done with it.
+__device__ __forceinline__ void u_issue(const DecodeParams& P, Ctx& c, int type, uint32_t stage, uint32_t it, uint32_t m,
+                                        bool copy_sfb, int q = 0, bool last = true) {
+    const int K = u_k(type), KC = u_kc(type), RP = u_rp(type);
+    const uint32_t ubar = smem_u32(c.smem + U_OFF_BARS);
+    if (q == 0 && m >= 2u && !c.misc[MISC_ABORT] &&
+        !mbar_wait(ubar + 16 + 8 * (m & 1u), ((m >> 1) - 1u) & 1u, P.mbar_limit_tries))
+        fail(P, c, ST_MBAR_TIMEOUT);              // the readers of product m - 2 have drained this accumulator buffer
+    wait_full(P, c, stage, (it / NSTAGE) & 1u);
+    u_fence_after();
+    const uint32_t a_s = c.ring0 + stage * STAGE_BYTES, sfa_s = a_s + RP * (KC / 2);
+    const uint32_t b_s = smem_u32(c.smem + U_OFF_B), sfb_s = smem_u32(c.smem + U_OFF_SFB);
+    const uint32_t d_t = c.tmem + 32u * (m & 1u);
+    const uint32_t sfa_t = c.tmem + U_TM_SFA + ((K == HIDDEN) ? 64u * (m & 1u) : 0u), sfb_t = c.tmem + U_TM_SFB;
+    const int ks0 = q * (KC / 64);                // first MMA step of this chunk within the product
+    for (int i = 0; i < KC / 64; ++i) u_cp_sf(sfa_t + 4 * (ks0 + i), u_desc_sf(sfa_s + 512 * i));
+    if (copy_sfb && q == 0)
+        for (int i = 0; i < K / 64; ++i) u_cp_sf(sfb_t + 4 * i, u_desc_sf(sfb_s + 512 * i));
+    for (int kl = 0; kl < KC / 64; ++kl) {
+        const int ks = ks0 + kl;
+        u_mma(d_t, u_desc_sw128(a_s + (kl >> 2) * (RP * 128) + (kl & 3) * 32), u_desc_sw128(b_s + (ks >> 2) * 1024 + (ks & 3) * 32),
+              sfa_t + 4 * ks, sfb_t + 4 * ks, ks ? 1u : 0u);
+    }
+    if (last) u_commit(ubar + 8 * (m & 1u));
+}
+
+// Everyone: wait for product m.  Returns false after an abort.
+__device__ __forceinline__ void u_wait_product(const DecodeParams& P, Ctx& c, uint32_t m) {
+    const uint32_t ubar = smem_u32(c.smem + U_OFF_BARS);
+    if (!c.misc[MISC_ABORT] && !mbar_wait(ubar + 8 * (m & 1u), (m >> 1) & 1u, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
+    u_fence_after();
+}
+
+// Warps 0 and 1: row 32 warp + lane of product m, the residual terms recombined; then the buffer is handed back.
+__device__ __forceinline__ float u_read_row(Ctx& c, uint32_t m) {
+    uint32_t v[8];
+    __syncwarp();
+    const uint32_t taddr = c.tmem + ((uint32_t)(32 * c.warp) << 16) + 32u * (m & 1u);
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    u_fence_before();
+    __syncwarp();
+    if (c.lane == 0) mbar_arrive(smem_u32(c.smem + U_OFF_BARS) + 16 + 8 * (m & 1u));
+    float y = 0.f, f = 1.0f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) { y = fmaf(__uint_as_float(v[n]), f, y); f *= (1.0f / 6.0f); }
+    return y * c.inv_g;
+}
+
+// One-chunk phase: same call as the mma.sync variant (the template arguments describe that variant's warp split).
+template <int RT, int KS, bool TWO>
+__device__ __forceinline__ void mma_phase_ts(const DecodeParams& P, Ctx& c, int nchunks, int K, bool sync_parts) {
+    (void)sync_parts;
+    const int type = (int)(c.where & 15u);
+    c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
+    u_prepare_acts(P, c, K);
+    if (nchunks > 2) { fail(P, c, ST_MISALIGNED); nchunks = 2; }
+    if (nchunks > 0) {
+        const uint32_t m = c.mma_n++;
+        if (c.tid == 0)
+            for (int q = 0; q < nchunks; ++q) u_issue(P, c, type, (c.it + q) % NSTAGE, c.it + q, m, true, q, q == nchunks - 1);
+        u_wait_product(P, c, m);
+        if (c.warp < 2) c.part[32 * c.warp + c.lane] = u_read_row(c, m);
+        for (int q = 0; q < nchunks; ++q, ++c.it) release_stage(c, c.it % NSTAGE);
+    }
+}
+template <int RT, int KS>
+__device__ __forceinline__ float part_sum_ts(const Ctx& c, int r) { return c.part[r]; }
+__device__ __forceinline__ float tensor_scale_of(const LW& lw, int slot) {
+    return __ldg(reinterpret_cast<const float*>(lw.ptrs[slot + 2]));
+}
+#endif
+
+#if MK_WFMT < 2
 // Runs all chunks of a phase; partial sums land in part[(q * 16 + warp) * 16 + tile_row].
 template <int NLOAD, int ROWS>
 __device__ __forceinline__ void mma_phase(const DecodeParams& P, Ctx& c, int nchunks_in, int K) {
@@ -876,8 +1164,8 @@ __device__ __forceinline__ float2 rmsnorm_to_slice(Ctx& c, float2 v, float w0, f
     const float rstd = rsqrtf(tot * (1.0f / HIDDEN) + RMS_EPS);
     float x0 = v.x * rstd * w0, x1 = v.y * rstd * w1;
     if (round_to_bf16) { x0 = round_bf16(x0); x1 = round_bf16(x1); }
-#if MK_WFMT == 2
-    stage_pair_ts<256>(reinterpret_cast<uint32_t*>(c.xs), 2 * c.tid, x0, x1);    // read by other warps: mma_phase_ts syncs
+#if MK_WFMT >= 2
+    stage_pair_ts<256>(c, 2 * c.tid, x0, x1);    // read by other warps: mma_phase_ts syncs
 #else
     stage_pair(reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW, 2 * c.lane, x0, x1);
     __syncwarp();
@@ -912,7 +1200,7 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
             dt_b = bf2f(reinterpret_cast<const __nv_bfloat16*>(lw.ptrs[DN_DT_BIAS])[h]);
         }
     }
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     const float ts_in = (c.tid < nloc) ? tensor_scale_of(lw, r < DN_CONV_CH ? (int)DN_W_QKV : (int)DN_W_Z) : 0.f;
 #endif
 #if MK_WFMT >= 1
@@ -938,7 +1226,7 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
     (void)xn;
 #endif
     trace_point(P, c);
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     mma_phase_ts<4, 4, true>(P, c, g.nchunks, HIDDEN, true);
 #else
     mma_phase<2, 16>(P, c, g.nchunks, HIDDEN);
@@ -960,7 +1248,7 @@ __device__ __forceinline__ void phase_dn_in(const DecodeParams& P, Ctx& c, const
     }
 #endif
     if (c.tid < nloc) {
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
         const float val = part_sum_ts<4, 4>(c, c.tid) * ts_in;
 #else
         const float val = part_sum(c, c.tid >> 4, c.tid & 15);
@@ -1056,7 +1344,7 @@ __device__ __forceinline__ void outproj_rows(const DecodeParams& P, Ctx& c, cons
                                              float tscale) {
     (void)type; (void)tscale;
     const int nloc = g.r1 - g.r0;
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     mma_phase_ts<1, 8, false>(P, c, g.nchunks, 2048, true);
 #else
     mma_phase<4, 8>(P, c, g.nchunks, 2048);
@@ -1064,7 +1352,7 @@ __device__ __forceinline__ void outproj_rows(const DecodeParams& P, Ctx& c, cons
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nloc) {
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
         const float y = part_sum_ts<1, 8>(c, c.tid) * tscale + resid;
 #else
         const float y = part_sum(c, c.tid >> 3, c.tid & 7) + resid;
@@ -1105,10 +1393,9 @@ __device__ __forceinline__ void phase_dn_out(const DecodeParams& P, Ctx& c, cons
         x.y = oa.y * rstd * bf_hi(nwr.x) * silu_f(za.y);
         x.z = ob.x * rstd * bf_lo(nwr.y) * silu_f(zb.x);
         x.w = ob.y * rstd * bf_hi(nwr.y) * silu_f(zb.y);
-#if MK_WFMT == 2
-        uint32_t* xs_words = reinterpret_cast<uint32_t*>(c.xs);
-        stage_pair_ts<256>(xs_words, 128 * c.warp + 4 * c.lane, x.x, x.y);
-        stage_pair_ts<256>(xs_words, 128 * c.warp + 4 * c.lane + 2, x.z, x.w);
+#if MK_WFMT >= 2
+        stage_pair_ts<256>(c, 128 * c.warp + 4 * c.lane, x.x, x.y);
+        stage_pair_ts<256>(c, 128 * c.warp + 4 * c.lane + 2, x.z, x.w);
 #else
         uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
         stage_pair(xw, 4 * c.lane, x.x, x.y);
@@ -1117,7 +1404,7 @@ __device__ __forceinline__ void phase_dn_out(const DecodeParams& P, Ctx& c, cons
 #endif
     }
     trace_point(P, c);
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     outproj_rows(P, c, g, T_DN_OUT, resid, ep, tensor_scale_of(lw, DN_W_OUT));
 #else
     outproj_rows(P, c, g, T_DN_OUT, resid, ep, 1.0f);
@@ -1135,7 +1422,7 @@ __device__ __forceinline__ void phase_fa_in(const DecodeParams& P, Ctx& c, const
     const float2 v = fetch_hidden2(P, c, embed_row, P.ws->x_hidden[1], epoch_of(c, layer - 1));
     rmsnorm_to_slice(c, v, w0, w1, true);
     trace_point(P, c);
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     float ts_in = 0.f;
     if (c.tid < nloc) {
         const int r = g.r0 + c.tid;
@@ -1438,10 +1725,9 @@ __device__ __forceinline__ void phase_fa_out(const DecodeParams& P, Ctx& c, cons
         float4 x;
         x.x = o.x * inv * sigmoid_f(ga.x); x.y = o.y * inv * sigmoid_f(ga.y);
         x.z = o.z * inv * sigmoid_f(gb.x); x.w = o.w * inv * sigmoid_f(gb.y);
-#if MK_WFMT == 2
-        uint32_t* xs_words = reinterpret_cast<uint32_t*>(c.xs);
-        stage_pair_ts<256>(xs_words, 128 * c.warp + 4 * c.lane, x.x, x.y);
-        stage_pair_ts<256>(xs_words, 128 * c.warp + 4 * c.lane + 2, x.z, x.w);
+#if MK_WFMT >= 2
+        stage_pair_ts<256>(c, 128 * c.warp + 4 * c.lane, x.x, x.y);
+        stage_pair_ts<256>(c, 128 * c.warp + 4 * c.lane + 2, x.z, x.w);
 #else
         uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
         stage_pair(xw, 4 * c.lane, x.x, x.y);
@@ -1450,7 +1736,7 @@ __device__ __forceinline__ void phase_fa_out(const DecodeParams& P, Ctx& c, cons
 #endif
     }
     trace_point(P, c);
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     outproj_rows(P, c, g, T_FA_OUT, resid, ep, tensor_scale_of(lw, FA_W_O));
 #else
     outproj_rows(P, c, g, T_FA_OUT, resid, ep, 1.0f);
@@ -1469,7 +1755,7 @@ __device__ __forceinline__ void phase_gateup(const DecodeParams& P, Ctx& c, cons
     const float2 v = poll2(P, c, P.ws->x_hidden[0] + 2 * c.tid, ep);
     rmsnorm_to_slice(c, v, w0, w1, true);
     trace_point(P, c);
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     const bool dnl = (lw.layer_type == 0);
     const float ts_g = tensor_scale_of(lw, dnl ? (int)DN_W_GATE : (int)FA_W_GATE);
     const float ts_u = tensor_scale_of(lw, dnl ? (int)DN_W_UP : (int)FA_W_UP);
@@ -1480,9 +1766,9 @@ __device__ __forceinline__ void phase_gateup(const DecodeParams& P, Ctx& c, cons
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nout) {
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
         const float gv = part_sum_ts<4, 4>(c, c.tid) * ts_g;
-        const float uv = part_sum_ts<4, 4>(c, 32 + c.tid) * ts_u;
+        const float uv = part_sum_ts<4, 4>(c, UP_ROW0 + c.tid) * ts_u;
 #else
         const float gv = part_sum(c, c.tid >> 3, c.tid & 7);
         const float uv = part_sum(c, c.tid >> 3, 8 + (c.tid & 7));
@@ -1506,10 +1792,9 @@ __device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, const 
         const unsigned long long* base = P.ws->x_mlp + c.warp * XK + c.lane;
         const unsigned long long* const p1[7] = {base, base + 32, base + 64, base + 96, base + 128, base + 160, base + 192};
         poll1_batch<7>(P, c, p1, ep, xv);
-#if MK_WFMT == 2
-        uint32_t* xs_words = reinterpret_cast<uint32_t*>(c.xs);
+#if MK_WFMT >= 2
 #pragma unroll
-        for (int k = 0; k < 7; ++k) stage_one_ts<256>(xs_words, 224 * c.warp + c.lane + 32 * k, xv[k]);
+        for (int k = 0; k < 7; ++k) stage_one_ts<256>(c, 224 * c.warp + c.lane + 32 * k, xv[k]);
 #else
         uint32_t* xw = reinterpret_cast<uint32_t*>(c.xs) + c.warp * XSW;
 #pragma unroll
@@ -1518,7 +1803,7 @@ __device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, const 
         __syncwarp();
     }
     trace_point(P, c);
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
     const float ts_d = tensor_scale_of(lw, lw.layer_type == 0 ? (int)DN_W_DOWN : (int)FA_W_DOWN);
     mma_phase_ts<1, 14, false>(P, c, g.nchunks, INTER, true);
 #else
@@ -1527,7 +1812,7 @@ __device__ __forceinline__ void phase_down(const DecodeParams& P, Ctx& c, const 
     trace_point(P, c);
     named_bar_sync(1, NCT);
     if (c.tid < nloc) {
-#if MK_WFMT == 2
+#if MK_WFMT >= 2
         const float y = part_sum_ts<1, 14>(c, c.tid) * ts_d + resid;
 #else
         const float y = part_sum(c, c.tid >> 2, c.tid & 3) + resid;
@@ -1603,6 +1888,39 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
         }
         release_stage(c, stage);
     }
+#elif MK_WFMT == 3
+    // LM head on tcgen05: the final-normed vector is quantised once; chunk q + 1 (64 rows, its own image) is issued
+    // into the other accumulator buffer as soon as chunk q's product is done, while warps 0 and 1 read q back.
+    {
+        const float2 xv = reinterpret_cast<const float2*>(c.xs)[c.tid];
+        c.amax = fmaxf(fabsf(xv.x), fabsf(xv.y));
+        u_prepare_acts(P, c, HIDDEN);
+    }
+    const float ts_lm = __ldg(P.lm_tensor_scale);
+    const uint32_t m0 = c.mma_n;
+    if (c.tid == 0 && g.nchunks > 0) u_issue(P, c, T_LM, c.it % NSTAGE, c.it, m0, true);
+#pragma unroll 1
+    for (int q = 0; q < g.nchunks; ++q, ++c.it) {
+        const uint32_t stage = c.it % NSTAGE, m = m0 + (uint32_t)q;
+        u_wait_product(P, c, m);
+        if (c.tid == 0 && q + 1 < g.nchunks) u_issue(P, c, T_LM, (c.it + 1) % NSTAGE, c.it + 1, m + 1, false);
+        if (c.warp < 2) {
+            const float acc = u_read_row(c, m) * ts_lm;
+            const int lr = q * LM_RPC + c.tid;
+            if (c.tid < LM_RPC && lr < nloc) {
+                if (P.logits_out) P.logits_out[g.r0 + lr] = acc;
+                if (acc > bestv) { bestv = acc; besti = g.r0 + lr; }
+            }
+        }
+        release_stage(c, stage);
+    }
+    c.mma_n = m0 + (uint32_t)g.nchunks;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bestv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+        if (ov > bestv || (ov == bestv && oi < besti)) { bestv = ov; besti = oi; }
+    }
 #elif MK_WFMT == 2
     // LM head in the tensor-scale format on the tensor cores: a chunk is 64 packed rows with their block scales,
     // processed like a K = 1024 layer chunk (4 row tiles x 4 K parts); the final-normed vector (f32) is staged once
@@ -1611,7 +1929,7 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
     {
         const float2 xv = reinterpret_cast<const float2*>(c.xs)[c.tid];
         named_bar_sync(1, NCT);                                   // everyone has read the f32 vector: reuse the scratch
-        stage_pair_ts<256>(reinterpret_cast<uint32_t*>(c.xs), 2 * c.tid, xv.x, xv.y);
+        stage_pair_ts<256>(c, 2 * c.tid, xv.x, xv.y);
         named_bar_sync(1, NCT);
     }
     const uint32_t* xw_lm = reinterpret_cast<const uint32_t*>(c.xs) + (c.warp / 4) * (3 * 256 / 2);
@@ -1806,9 +2124,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
         c.misc[MISC_ABORT] = 0;
         c.misc[MISC_LAST] = 0;
         c.misc[MISC_DETAIL] = 0;
+#if MK_WFMT == 3
+        const uint32_t ubar = smem_u32(smem + U_OFF_BARS);
+        mbar_init(ubar, 1); mbar_init(ubar + 8, 1);             // product done (tcgen05.commit)
+        mbar_init(ubar + 16, 2); mbar_init(ubar + 24, 2);       // accumulator buffer read back by warps 0 and 1
+#endif
         fence_mbar_init();
     }
+#if MK_WFMT == 3
+    c.amax = 0.f; c.mma_n = 0; c.inv_g = 1.0f;
+    // activation operand and its scales start as zeros: rows of unused residual terms must stay zero
+    for (int i = threadIdx.x; i < (U_B_BYTES + U_SFB_BYTES) / 16; i += NTHREADS)
+        reinterpret_cast<uint4*>(smem + U_OFF_B)[i] = make_uint4(0, 0, 0, 0);
+    if (c.warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem + U_OFF_TMEM)), "r"(U_TM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_proxy_async();
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    c.tmem = *reinterpret_cast<volatile uint32_t*>(smem + U_OFF_TMEM);
+#else
+    __syncthreads();
+#endif
 
     if (c.warp == NCW) {
         // ===== producer warp =====
@@ -1887,7 +2226,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
             ++c.seq;
         }
     }
+#if MK_WFMT == 3
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+#endif
     __syncthreads();
+#if MK_WFMT == 3
+    if (c.warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(c.tmem), "r"(U_TM_COLS) : "memory");
+    }
+#endif
     if (c.misc[MISC_ABORT]) {
         if (threadIdx.x == 0 && P.host_status) {
             // low byte: ST code; bits 8-11 phase, 12-18 layer, 23 producer warp, 24-31 step (where the first wait gave up)

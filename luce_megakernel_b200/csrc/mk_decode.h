@@ -48,7 +48,8 @@ struct DecodeParams {
     const void* lm_scales;        // wfmt 1: E4M3 block scales of the LM head (128 x 4 tiles); wfmt 2: row-major [vocab][64]
     const float* lm_tensor_scale; // wfmt 2: fp32 scale of the LM-head matrix
     int wfmt;                     // 0 = bf16 weights, 1 = NVFP4 (layer format A, LM head format B), 2 = NVFP4 with
-                                  // 16-element blocks, E4M3 block scales (row-major) and an fp32 scale per matrix
+                                  // 16-element blocks, E4M3 block scales (row-major) and an fp32 scale per matrix,
+                                  // 3 = the values of 2 as per-CTA chunk images for the block-scaled tcgen05 path
     void* k_cache;                // bf16 [n_fa, 2, max_seq, 256]
     void* v_cache;
     float* dn_states;             // f32 [n_dn, 16, 128(value), 128(key)]
@@ -81,6 +82,8 @@ struct DecodeParams {
     int trace_slots;              // entries per CTA in `trace`
     unsigned long long poll_limit_cycles;   // SM clocks a poll of a flagged word may take before the CTA gives up
     uint32_t mbar_limit_tries;              // try_wait attempts on a ring barrier before the CTA gives up
+    int lm_image_chunks;          // wfmt 3: 64-row chunk images per CTA in the LM-head image array
+    int act_terms;                // wfmt 3: NVFP4 residual terms the activation vector is expanded into (1..8)
 };
 
 // Defaults of the two wait limits: about 2 s of SM clock each.
@@ -94,6 +97,8 @@ cudaError_t launch_decode_kernel(const DecodeParams& p, int grid, cudaStream_t s
 // Largest grid that is guaranteed co-resident on the current device.
 int decode_max_grid();
 size_t decode_smem_bytes();
+// Grid size the chunk images of the tcgen05 NVFP4 variant (wfmt 3) are cut for.
+int decode_image_ctas();
 // Two CTAs run the kernel's own poll of a flagged word on a word nobody writes, with p.poll_limit_cycles as the
 // limit: the wait runs out, the CTAs record ST_GRID_TIMEOUT through the kernel's failure path and return.  Exists
 // so that the failure path can be exercised without a hung launch; p needs ws, host_status and the limit only.

@@ -28,6 +28,14 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
                          int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream);
 
+// C[M,N] = (ta[0] * tw[0]) * (A[M,K] . W[N,K]^T) (+ R[M,N]); A and W NVFP4 (packed e2m1 rows of K/2 bytes, E4M3 block
+// scales in 128-row x 4-block tiles of 512 bytes, one fp32 tensor scale each), C and R bf16 row-major; block-scaled
+// tcgen05 (kind::mxf4nvf4) with the scale tiles copied into tensor memory.  N % 128 == 0, K % 256 == 0, ldc % 8 == 0,
+// pointers 16-byte aligned; the scale arrays cover whole 128-row blocks (rows rounded up).  Allocates nothing.
+cudaError_t gemm_nvfp4_tn(const void* a_packed, const void* a_scales, const float* a_tensor_scale, const void* w_packed,
+                          const void* w_scales, const float* w_tensor_scale, void* C, const void* R, int M, int N, int K, int ldc,
+                          int* err_flag, cudaStream_t stream);
+
 // Gated delta rule over a prompt in chunks of 64 tokens (all 16 heads of one layer).
 // qkv: bf16 [S][6144] projection outputs q | k | v (the causal conv1d + SiLU and the L2 norms are applied inside);
 // conv_w: bf16 [6144][4]; conv_state: f32 [6144][4], the four inputs before the prompt (read only);

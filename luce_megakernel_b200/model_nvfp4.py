@@ -319,3 +319,66 @@ class DecoderTS:
         self._position = 0
         for t in (self._fa_k_cache, self._fa_v_cache, self._dn_states, self._conv_bufs):
             t.zero_()
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# The same tensor-scale NVFP4 values as per-CTA chunk images for the tcgen05 decode kernel (mk_decode_nvfp4_mma).
+# ---------------------------------------------------------------------------------------------------------------
+
+def attach_nvfp4_mma_weights(weights):
+    """Adds weights["nvfp4_mma"]: the slot lists of weights["nvfp4_ts"] with the first slot of every phase's matrix
+    group replaced by that phase's chunk images, and the LM-head images."""
+    from . import nvfp4_images as I
+    if "nvfp4_mma" in weights:
+        return weights
+    attach_nvfp4_ts_weights(weights)
+    ts = weights["nvfp4_ts"]
+    layers = []
+    for ld in ts["layer_data"]:
+        p = list(ld["ptrs"])
+        if ld["type"] == 1:       # attention: q(1) k(4) v(7) o(12) gate(16) up(19) down(22)
+            groups, o, g, u, d = (1, 4, 7), 12, 16, 19, 22
+            in_phase = "fa_in"
+        else:                     # DeltaNet: qkv(1) z(4) out(13) gate(17) up(20) down(23)
+            groups, o, g, u, d = (1, 4), 13, 17, 20, 23
+            in_phase = "dn_in"
+        img_in = I.build_phase_images(in_phase, torch.cat([p[i] for i in groups]), torch.cat([p[i + 1] for i in groups]))
+        img_o = I.build_phase_images("out", p[o], p[o + 1])
+        img_g = I.build_gateup_images(p[g], p[g + 1], p[u], p[u + 1])
+        img_d = I.build_phase_images("down", p[d], p[d + 1])
+        q = list(p)
+        q[groups[0]], q[o], q[g], q[d] = img_in, img_o, img_g, img_d
+        layers.append({"type": ld["type"], "ptrs": q})
+    lm_img, chunks = I.build_lm_images(ts["lm"]["packed"], ts["lm"]["scales"])
+    weights["nvfp4_mma"] = {"layer_data": layers, "lm_images": lm_img, "lm_chunks": chunks,
+                            "lm_tensor_scale": ts["lm"]["tensor_scale"]}
+    return weights
+
+
+class DecoderMMA(DecoderTS):
+    """DecoderTS on the block-scaled tensor-core kernel (mk_decode_nvfp4_mma).  act_terms: NVFP4 residual terms the
+    activation vector of every projection is expanded into (1..8)."""
+
+    def __init__(self, weights, max_seq_len=2048, act_terms=4):
+        super().__init__(weights, max_seq_len)
+        attach_nvfp4_mma_weights(self._weights)
+        mm = self._weights["nvfp4_mma"]
+        self._mma = mm
+        self._layer_weights_packed = _pack_layer_weights_nvfp4_ts(mm["layer_data"])
+        self.act_terms = int(act_terms)
+
+    def step_many(self, token_id: int, steps: int) -> torch.Tensor:
+        if steps < 1 or self._position + steps > self.max_seq_len:
+            raise ValueError("steps must be positive and position + steps within max_seq_len")
+        self._check(self._lib.mk_set_model_dims(self.num_layers, self.vocab))
+        out = torch.empty(steps, dtype=torch.int32, device=self._token_buffer.device)
+        self._token_buffer.fill_(int(token_id))
+        self._check(self._lib.mk_decode_nvfp4_mma(
+            _ptr(self._token_buffer), _ptr(out), ctypes.c_int(steps), _ptr(self._embed_weight),
+            _ptr(self._layer_weights_packed), _ptr(self._final_norm_weight), _ptr(self._mma["lm_images"]),
+            ctypes.c_int(self._mma["lm_chunks"]), _ptr(self._mma["lm_tensor_scale"]), _ptr(self._fa_k_cache),
+            _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs), _ptr(self._hidden), _ptr(self._normalized),
+            ctypes.c_int(self._position), ctypes.c_int(self.max_seq_len), ctypes.c_int(self.act_terms),
+            ctypes.c_void_p(torch.cuda.current_stream(self._embed_weight.device).cuda_stream)))
+        self._position += steps
+        return out

@@ -31,11 +31,20 @@ def bf16_ulp(x):
     return 2.0 ** (math.floor(math.log2(max(x, 1e-30))) - 7)
 
 
-@pytest.fixture(scope="module")
-def setup(small_model):
-    from luce_megakernel_b200 import model as M, model_nvfp4 as MQ
+def _make_decoder(kind, weights, max_seq_len):
+    """kind: "ts" = mma.sync kernel (mk_decode_nvfp4_ts); "mma8" / "mma4" = block-scaled tcgen05 kernel
+    (mk_decode_nvfp4_mma) with the activation expanded into 8 / 4 NVFP4 residual terms."""
+    from luce_megakernel_b200 import model_nvfp4 as MQ
+    if kind == "ts":
+        return MQ.DecoderTS(weights, max_seq_len=max_seq_len)
+    return MQ.DecoderMMA(weights, max_seq_len=max_seq_len, act_terms=int(kind[3:]))
+
+
+@pytest.fixture(scope="module", params=["ts", "mma8", "mma4"])
+def setup(request, small_model):
+    from luce_megakernel_b200 import model as M
     sd, _ = small_model("unit", "decode")
-    dec = MQ.DecoderTS(M.weights_from_state_dict(sd), max_seq_len=MAXSEQ)
+    dec = _make_decoder(request.param, M.weights_from_state_dict(sd), MAXSEQ)
     orc = O.Oracle(dequantised_state_dict(sd), rounding="decode")
     return dec, orc
 
@@ -102,11 +111,12 @@ def test_ts_one_launch_equals_single_steps(setup):
     assert torch.equal(runs[0][2], runs[1][2])
 
 
-def test_ts_full_size_model_short_run():
+@pytest.mark.parametrize("kind", ["ts", "mma8", "mma4"])
+def test_ts_full_size_model_short_run(kind):
     """24 layers, vocabulary 248320: 8 prompt tokens and 8 teacher-forced steps against the oracle on dequantised weights."""
-    from luce_megakernel_b200 import model as M, model_nvfp4 as MQ
+    from luce_megakernel_b200 import model as M
     sd = O.init_weights(0, 24, O.VOCAB, norm_init="unit")
-    dec = MQ.DecoderTS(M.weights_from_state_dict(sd), max_seq_len=64)
+    dec = _make_decoder(kind, M.weights_from_state_dict(sd), 64)
     dq = dequantised_state_dict(sd)
     orc, o32 = O.Oracle(dq, rounding="decode"), O.Oracle(dq, rounding="none")
     g = torch.Generator().manual_seed(33)
