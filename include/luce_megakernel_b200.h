@@ -389,6 +389,22 @@ int mk_attention_prefill(const void *qkv, const void *k_cache, const void *v_cac
 int mk_gemm_bf16_tn(const void *A, const void *W, void *C, const void *residual, int M, int N, int K,
                     cudaStream_t stream);
 
+/* Prefill with NVFP4 weights and NVFP4 activations: the input of every projection (normed hidden state, DeltaNet /
+ * attention output, SwiGLU output) is quantised per 16 values along K with E4M3 block scales (the arithmetic of
+ * launch_quantize_nvfp4_lm_out, no tensor scale) and multiplied with the tensor-scale NVFP4 weights by
+ * mk_gemm_nvfp4_tn's kernel; no bf16 copy of a weight matrix is made.  The reference's NVFP4 prefill dequantises
+ * every matrix to bf16 scratch and calls cuBLAS (megakernel/kernel_gb10_nvfp4.cu:2127-2145); its Blackwell prefill
+ * keeps bf16 weights (megakernel/prefill_bw.cu:1036-1171).  layer_weights: the 224-byte entries of mk_decode_nvfp4_ts
+ * with each matrix's scale slot pointing at the quantiser's 128 x 4 scale tiles instead of plain rows; beta / alpha
+ * projections, norms and the convolution stay bf16.  Outputs and state as mk_prefill_bf16.  vocab % 128 == 0. */
+int mk_prefill_nvfp4_mma(
+    const int *token_ids, int seq_len, int *output_token,
+    const void *embed_weight, const void *layer_weights, const void *final_norm_weight,
+    const void *lm_head_packed, const void *lm_head_scales_tiled,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *final_normed, void *hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
+
 /* NVFP4 x NVFP4 product on the block-scaled tensor-core path (tcgen05.mma kind::mxf4nvf4, E4M3 scales per 16 values
  * read from tensor memory): C[M,N] = a_tensor_scale[0] * w_tensor_scale[0] * (A[M,K] . W[N,K]^T) (+ residual), C and
  * residual bf16 row-major.  Both operands in the format mk_quantize_nvfp4_tensor_scale writes (packed e2m1 rows, 128 x 4

@@ -195,7 +195,7 @@ cudaError_t launch_decode_kernel(const DecodeParams& p, int grid, cudaStream_t s
                    : p.wfmt == 1 ? (const void*)nvfp4::decode_megakernel_bf16
                    : p.trace   ? (const void*)traced::decode_megakernel_bf16
                                : (const void*)plain::decode_megakernel_bf16;
-    return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(NTHREADS), args, SMEM_BYTES, stream);
+    return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(p.wfmt == 3 ? nvfp4mma::NTHR : NTHREADS), args, SMEM_BYTES, stream);
 }
 
 cudaError_t launch_wait_selftest(const DecodeParams& p, cudaStream_t stream) {

@@ -73,8 +73,8 @@ constexpr int U_OFF_B = NSTAGE * STAGE_BYTES;           // activation terms: 8 r
 constexpr int U_B_BYTES = 8 * (INTER / 2);
 constexpr int U_OFF_SFB = U_OFF_B + U_B_BYTES;          // their block scales: one 512-byte copy unit per MMA step (64 k)
 constexpr int U_SFB_BYTES = (INTER / 64) * 512;
-constexpr int U_OFF_BARS = U_OFF_SFB + U_SFB_BYTES;     // MMA-done barriers [2], accumulator-free barriers [2]
-constexpr int U_OFF_TMEM = U_OFF_BARS + 32;             // tensor-memory base address
+constexpr int U_OFF_BARS = U_OFF_SFB + U_SFB_BYTES;     // barriers: product done [2], accumulator drained [2], activation ready
+constexpr int U_OFF_TMEM = U_OFF_BARS + 40;             // tensor-memory base address
 constexpr int U_OFF_AMAX = U_OFF_BARS + 64;             // per-warp maxima of the staged activation [16]
 static_assert(U_OFF_AMAX + 64 <= RING_BYTES, "tensor-core operands do not fit behind the ring");
 // tensor-memory columns: accumulator buffers at 0 and 32 (8 columns each); block scales take four columns per MMA
@@ -963,12 +963,14 @@ __device__ __forceinline__ uint32_t f32x8_to_e2m1x8(const float (&v)[8]) {
     return w;
 }
 
-// The staged f32 vector (c.xs[0..K)) -> P.act_terms NVFP4 residual terms in the B operand layout.  Two threads per
-// 16-element block.  x is first scaled by g = 192 / max|x| so that block scales start at or below 32 whatever the
-// vector's magnitude; term n holds round(r_n / s_n) with s_n = E4M3 rounded UP from max|r_n| / 6 (no clipping), and
-// r_{n+1} = 6 (r_n - s_n code_n): a term leaves at most s_n <= max|r_n| / 6 (1 + 1/8) behind, so block scales never
-// grow by more than 9/8 per term and stay far inside E4M3.  x = (1/g) sum_n 6^-n s_n code_n up to the last residual.
-// Ends with the barrier that makes the operand visible to the issuing thread; returns nothing, sets c.inv_g.
+// The staged f32 vector (c.xs[0..K)) -> P.act_terms NVFP4 terms in the B operand layout.  Two threads per 16-element
+// block.  x is first scaled by g = 192 / max|x|, so that block scales start at or below 32 whatever the vector's
+// magnitude.  All terms of a block share ONE scale s = E4M3 rounded UP from max|g x| / 6; with u_0 = g x / s (|u_0| <= 6)
+//   code_n = e2m1_rne(u_n),   u_1 = 4 (u_0 - code_0),   u_{n+1} = 8 (u_n - code_n)  for n >= 1:
+// the first residual is at most 1 (half the widest e2m1 gap), so |u_1| <= 4, and from there on residuals are at most
+// 1/2, so every |u_n| <= 4: nothing ever saturates and every step is exact in f32.  Hence
+//   x = (s / g) (code_0 + code_1 / 4 + code_2 / 32 + code_3 / 256 + ...)   up to the last residual, <= s / (g 4 8^(T-1)).
+// Ends by arriving on the "activation ready" barrier the MMA warp waits on; sets c.inv_g.
 __device__ __forceinline__ void u_prepare_acts(const DecodeParams& P, Ctx& c, int K) {
     float* wmax = reinterpret_cast<float*>(c.smem + U_OFF_AMAX);
     const float m = warp_max(c.amax);
@@ -982,85 +984,147 @@ __device__ __forceinline__ void u_prepare_acts(const DecodeParams& P, Ctx& c, in
     c.inv_g = 1.0f / g;
     const int b = c.tid >> 1, h = c.tid & 1;
     if (b < K / 16) {
-        float r[8];
+        float u[8];
         {
             const float4 a = *reinterpret_cast<const float4*>(c.xs + 16 * b + 8 * h);
             const float4 d = *reinterpret_cast<const float4*>(c.xs + 16 * b + 8 * h + 4);
-            r[0] = a.x * g; r[1] = a.y * g; r[2] = a.z * g; r[3] = a.w * g;
-            r[4] = d.x * g; r[5] = d.y * g; r[6] = d.z * g; r[7] = d.w * g;
+            u[0] = a.x * g; u[1] = a.y * g; u[2] = a.z * g; u[3] = a.w * g;
+            u[4] = d.x * g; u[5] = d.y * g; u[6] = d.z * g; u[7] = d.w * g;
         }
+        float a = fmaxf(fmaxf(fmaxf(fabsf(u[0]), fabsf(u[1])), fmaxf(fabsf(u[2]), fabsf(u[3]))),
+                        fmaxf(fmaxf(fabsf(u[4]), fabsf(u[5])), fmaxf(fabsf(u[6]), fabsf(u[7]))));
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+        const float t = a * (1.0f / 6.0f);
+        uint32_t code = (uint32_t)__nv_cvt_float_to_fp8(t, __NV_SATFINITE, __NV_E4M3);
+        float sv = e4m3_value(code);
+        if (sv < t && code < 0x7eu) { ++code; sv = e4m3_value(code); }
+        if (code == 0u) { code = 1u; sv = 0.001953125f; }
+        const float inv = 1.0f / sv;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u[i] *= inv;
         const int bb = b & 15;
         char* brow = c.smem + U_OFF_B + (b >> 4) * 1024 + (bb & 1) * 8 + h * 4;
         unsigned char* sfb = reinterpret_cast<unsigned char*>(c.smem) + U_OFF_SFB + (b >> 2) * 512 + (b & 3);
         const int terms = P.act_terms;
 #pragma unroll 1
         for (int n = 0; n < terms; ++n) {
-            float a = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(r[i]));
-            a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-            const float t = a * (1.0f / 6.0f);
-            uint32_t code = (uint32_t)__nv_cvt_float_to_fp8(t, __NV_SATFINITE, __NV_E4M3);
-            float sv = e4m3_value(code);
-            if (sv < t && code < 0x7eu) { ++code; sv = e4m3_value(code); }
-            if (code == 0u) { code = 1u; sv = 0.001953125f; }
-            const float inv = __fdividef(1.0f, sv);
-            float v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = r[i] * inv;
-            const uint32_t w = f32x8_to_e2m1x8(v);
+            const uint32_t w = f32x8_to_e2m1x8(u);
             uint32_t hh[4];
             e2m1x8_to_f16x2x4(w, hh);
-            const float s6 = -6.0f * sv;
+            const float up = n ? 8.0f : 4.0f;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hh[i]));
-                r[2 * i] = fmaf(f.x, s6, 6.0f * r[2 * i]);
-                r[2 * i + 1] = fmaf(f.y, s6, 6.0f * r[2 * i + 1]);
+                u[2 * i] = (u[2 * i] - f.x) * up;
+                u[2 * i + 1] = (u[2 * i + 1] - f.y) * up;
             }
             *reinterpret_cast<uint32_t*>(brow + n * 128 + (((bb >> 1) ^ n) << 4)) = w;
             if (h == 0) sfb[n * 16] = (unsigned char)code;
         }
     }
     fence_proxy_async();                          // the tensor core reads shared memory through the async proxy
-    named_bar_sync(1, NCT);
+    __syncwarp();
+    if (c.lane == 0) mbar_arrive(smem_u32(c.smem + U_OFF_BARS) + 32);
 }
 
-// Thread 0: scale copies and the K / 64 MMAs of one chunk in `stage`, product number m; arrives on the product's
-// barrier when the tensor core is done with it.
-__device__ __forceinline__ void u_issue(const DecodeParams& P, Ctx& c, int type, uint32_t stage, uint32_t it, uint32_t m,
-                                        bool copy_sfb, int q = 0, bool last = true) {
-    const int K = u_k(type), KC = u_kc(type), RP = u_rp(type);
+// ---- the MMA warp's side ---------------------------------------------------------------------------------------
+// Descriptors advance by plain additions on their low words: a K-major 128-byte-swizzled operand moves 32 bytes (2
+// units of 16) per MMA step inside a k-tile; a scale unit is 512 bytes (32 units).
+__device__ __forceinline__ uint64_t u_desc(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
+constexpr uint32_t U_HI_SW128 = (1024u >> 4) | (1u << 14) | (2u << 29);
+constexpr uint32_t U_HI_SF = (128u >> 4) | (1u << 14);
+
+template <int N>
+__device__ __forceinline__ void u_copy_units(uint32_t taddr, uint32_t saddr) {
+    const uint32_t lo = (saddr & 0x3ffffu) >> 4;
+#pragma unroll
+    for (int i = 0; i < N; ++i) u_cp_sf(taddr + 4 * i, u_desc(lo + 32 * i, U_HI_SF));
+}
+// NS MMA steps of one chunk image of RP rows at a_s; ks0 = first step's index within the product
+template <int NS, int RP>
+__device__ __forceinline__ void u_mma_steps(uint32_t d_t, uint32_t a_s, uint32_t b_s, uint32_t sfa_t, uint32_t sfb_t, int ks0) {
+    const uint32_t a_lo = ((a_s & 0x3ffffu) >> 4) | (1u << 16);
+    const uint32_t b_lo = (((b_s + (ks0 >> 2) * 1024) & 0x3ffffu) >> 4) | (1u << 16);
+    static_assert(NS % 4 == 0, "whole k-tiles");
+#pragma unroll
+    for (int kl = 0; kl < NS; ++kl)
+        // (spreading the steps over several accumulator column groups changes nothing: a step costs about 42 ns
+        // whether or not it depends on the one before)
+        u_mma(d_t, u_desc(a_lo + (kl >> 2) * (RP * 128 / 16) + (kl & 3) * 2, U_HI_SW128),
+              u_desc(b_lo + (kl >> 2) * (1024 / 16) + (kl & 3) * 2, U_HI_SW128), sfa_t + 4 * (ks0 + kl), sfb_t + 4 * (ks0 + kl),
+              (ks0 + kl) ? 1u : 0u);
+}
+
+__device__ __forceinline__ void u_wait(const DecodeParams& P, Ctx& c, uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return;
+    if (c.misc[MISC_ABORT]) return;
+    if (!mbar_wait(bar, parity, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
+}
+
+// One projection phase (or one LM-head chunk when `lm`): weight scales go to tensor memory as soon as the chunk has
+// landed and the previous product no longer reads that region; the MMAs follow the activation.
+//   barriers at U_OFF_BARS: +0,+8 product m done (by parity of m); +16,+24 accumulator buffer drained; +32 activation ready
+__device__ __forceinline__ void u_mma_phase(const DecodeParams& P, Ctx& c, int type, int nchunks, uint32_t& m, uint32_t& an,
+                                            bool lm_chunk, bool lm_first) {
     const uint32_t ubar = smem_u32(c.smem + U_OFF_BARS);
-    if (q == 0 && m >= 2u && !c.misc[MISC_ABORT] &&
-        !mbar_wait(ubar + 16 + 8 * (m & 1u), ((m >> 1) - 1u) & 1u, P.mbar_limit_tries))
-        fail(P, c, ST_MBAR_TIMEOUT);              // the readers of product m - 2 have drained this accumulator buffer
-    wait_full(P, c, stage, (it / NSTAGE) & 1u);
-    u_fence_after();
-    const uint32_t a_s = c.ring0 + stage * STAGE_BYTES, sfa_s = a_s + RP * (KC / 2);
-    const uint32_t b_s = smem_u32(c.smem + U_OFF_B), sfb_s = smem_u32(c.smem + U_OFF_SFB);
+    const int K = u_k(type);
     const uint32_t d_t = c.tmem + 32u * (m & 1u);
     const uint32_t sfa_t = c.tmem + U_TM_SFA + ((K == HIDDEN) ? 64u * (m & 1u) : 0u), sfb_t = c.tmem + U_TM_SFB;
-    const int ks0 = q * (KC / 64);                // first MMA step of this chunk within the product
-    for (int i = 0; i < KC / 64; ++i) u_cp_sf(sfa_t + 4 * (ks0 + i), u_desc_sf(sfa_s + 512 * i));
-    if (copy_sfb && q == 0)
-        for (int i = 0; i < K / 64; ++i) u_cp_sf(sfb_t + 4 * i, u_desc_sf(sfb_s + 512 * i));
-    for (int kl = 0; kl < KC / 64; ++kl) {
-        const int ks = ks0 + kl;
-        u_mma(d_t, u_desc_sw128(a_s + (kl >> 2) * (RP * 128) + (kl & 3) * 32), u_desc_sw128(b_s + (ks >> 2) * 1024 + (ks & 3) * 32),
-              sfa_t + 4 * ks, sfb_t + 4 * ks, ks ? 1u : 0u);
+    const uint32_t b_s = smem_u32(c.smem + U_OFF_B), sfb_s = smem_u32(c.smem + U_OFF_SFB);
+    // region of the weight scales is free: inside the LM head regions alternate and product m - 2 has been read back
+    // (waited for below); everywhere else the previous product must have finished
+    if (lm_chunk && !lm_first) {
+        if (m >= 2u) u_wait(P, c, ubar + 16 + 8 * (m & 1u), ((m >> 1) - 1u) & 1u);
+    } else if (m >= 1u) {
+        u_wait(P, c, ubar + 8 * ((m - 1u) & 1u), ((m - 1u) >> 1) & 1u);
     }
-    if (last) u_commit(ubar + 8 * (m & 1u));
+    for (int q = 0; q < nchunks; ++q) {
+        const uint32_t itq = c.it + q, stage = itq % NSTAGE;
+        wait_full(P, c, stage, (itq / NSTAGE) & 1u);
+        const uint32_t a_s = c.ring0 + stage * STAGE_BYTES;
+        u_fence_after();
+        switch (type) {
+            case T_FA_IN:  u_copy_units<16>(sfa_t, a_s + 40 * 512); break;
+            case T_DN_OUT:
+            case T_FA_OUT: u_copy_units<32>(sfa_t, a_s + 8 * 1024); break;
+            case T_DOWN:   u_copy_units<28>(sfa_t + 4 * 28 * q, a_s + 8 * 896); break;
+            default:       u_copy_units<16>(sfa_t, a_s + 56 * 512); break;       // qkv|z, gate|up, LM head
+        }
+    }
+    if (!lm_chunk || lm_first) {
+        u_wait(P, c, ubar + 32, an & 1u);          // the activation operand is in shared memory
+        ++an;
+        u_fence_after();
+        switch (K) {
+            case HIDDEN: u_copy_units<16>(sfb_t, sfb_s); break;
+            case 2048:   u_copy_units<32>(sfb_t, sfb_s); break;
+            default:     u_copy_units<56>(sfb_t, sfb_s); break;
+        }
+    }
+    if (m >= 2u) u_wait(P, c, ubar + 16 + 8 * (m & 1u), ((m >> 1) - 1u) & 1u);   // accumulator buffer drained
+    u_fence_after();
+    for (int q = 0; q < nchunks; ++q) {
+        const uint32_t a_s = c.ring0 + ((c.it + q) % NSTAGE) * STAGE_BYTES;
+        switch (type) {
+            case T_FA_IN:  u_mma_steps<16, 40>(d_t, a_s, b_s, sfa_t, sfb_t, 0); break;
+            case T_DN_OUT:
+            case T_FA_OUT: u_mma_steps<32, 8>(d_t, a_s, b_s, sfa_t, sfb_t, 0); break;
+            case T_DOWN:   u_mma_steps<28, 8>(d_t, a_s, b_s, sfa_t, sfb_t, 28 * q); break;
+            default:       u_mma_steps<16, 56>(d_t, a_s, b_s, sfa_t, sfb_t, 0); break;
+        }
+    }
+    u_commit(ubar + 8 * (m & 1u));
+    c.it += nchunks;
+    ++m;
 }
 
-// Everyone: wait for product m.  Returns false after an abort.
+// Everyone: wait for product m.
 __device__ __forceinline__ void u_wait_product(const DecodeParams& P, Ctx& c, uint32_t m) {
-    const uint32_t ubar = smem_u32(c.smem + U_OFF_BARS);
-    if (!c.misc[MISC_ABORT] && !mbar_wait(ubar + 8 * (m & 1u), (m >> 1) & 1u, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
+    u_wait(P, c, smem_u32(c.smem + U_OFF_BARS) + 8 * (m & 1u), (m >> 1) & 1u);
     u_fence_after();
 }
 
-// Warps 0 and 1: row 32 warp + lane of product m, the residual terms recombined; then the buffer is handed back.
+// Warps 0 and 1: row 32 warp + lane of product m, the terms recombined; then the buffer is handed back.
 __device__ __forceinline__ float u_read_row(Ctx& c, uint32_t m) {
     uint32_t v[8];
     __syncwarp();
@@ -1072,25 +1136,25 @@ __device__ __forceinline__ float u_read_row(Ctx& c, uint32_t m) {
     u_fence_before();
     __syncwarp();
     if (c.lane == 0) mbar_arrive(smem_u32(c.smem + U_OFF_BARS) + 16 + 8 * (m & 1u));
-    float y = 0.f, f = 1.0f;
+    float y = __uint_as_float(v[0]), f = 0.25f;
 #pragma unroll
-    for (int n = 0; n < 8; ++n) { y = fmaf(__uint_as_float(v[n]), f, y); f *= (1.0f / 6.0f); }
+    for (int n = 1; n < 8; ++n) { y = fmaf(__uint_as_float(v[n]), f, y); f *= 0.125f; }
     return y * c.inv_g;
 }
 
-// One-chunk phase: same call as the mma.sync variant (the template arguments describe that variant's warp split).
+// One projection phase, consumer side: same call as the mma.sync variant (whose warp split the template arguments
+// describe).
 template <int RT, int KS, bool TWO>
 __device__ __forceinline__ void mma_phase_ts(const DecodeParams& P, Ctx& c, int nchunks, int K, bool sync_parts) {
     (void)sync_parts;
-    const int type = (int)(c.where & 15u);
     c.part = c.part_base + ((c.part_flip++ & 1u) ? PART_HALF : 0);
     u_prepare_acts(P, c, K);
+    trace_point(P, c);
     if (nchunks > 2) { fail(P, c, ST_MISALIGNED); nchunks = 2; }
     if (nchunks > 0) {
         const uint32_t m = c.mma_n++;
-        if (c.tid == 0)
-            for (int q = 0; q < nchunks; ++q) u_issue(P, c, type, (c.it + q) % NSTAGE, c.it + q, m, true, q, q == nchunks - 1);
         u_wait_product(P, c, m);
+        trace_point(P, c);
         if (c.warp < 2) c.part[32 * c.warp + c.lane] = u_read_row(c, m);
         for (int q = 0; q < nchunks; ++q, ++c.it) release_stage(c, c.it % NSTAGE);
     }
@@ -1889,21 +1953,18 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
         release_stage(c, stage);
     }
 #elif MK_WFMT == 3
-    // LM head on tcgen05: the final-normed vector is quantised once; chunk q + 1 (64 rows, its own image) is issued
-    // into the other accumulator buffer as soon as chunk q's product is done, while warps 0 and 1 read q back.
+    // LM head on tcgen05: the final-normed vector is quantised once; the MMA warp works through the CTA's chunk images
+    // (56 rows each) on its own, two accumulator buffers ahead at most, while warps 0 and 1 read the products back.
     {
         const float2 xv = reinterpret_cast<const float2*>(c.xs)[c.tid];
         c.amax = fmaxf(fabsf(xv.x), fabsf(xv.y));
         u_prepare_acts(P, c, HIDDEN);
     }
     const float ts_lm = __ldg(P.lm_tensor_scale);
-    const uint32_t m0 = c.mma_n;
-    if (c.tid == 0 && g.nchunks > 0) u_issue(P, c, T_LM, c.it % NSTAGE, c.it, m0, true);
 #pragma unroll 1
     for (int q = 0; q < g.nchunks; ++q, ++c.it) {
-        const uint32_t stage = c.it % NSTAGE, m = m0 + (uint32_t)q;
+        const uint32_t m = c.mma_n++;
         u_wait_product(P, c, m);
-        if (c.tid == 0 && q + 1 < g.nchunks) u_issue(P, c, T_LM, (c.it + 1) % NSTAGE, c.it + 1, m + 1, false);
         if (c.warp < 2) {
             const float acc = u_read_row(c, m) * ts_lm;
             const int lr = q * LM_RPC + c.tid;
@@ -1912,9 +1973,8 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
                 if (acc > bestv) { bestv = acc; besti = g.r0 + lr; }
             }
         }
-        release_stage(c, stage);
+        release_stage(c, c.it % NSTAGE);
     }
-    c.mma_n = m0 + (uint32_t)g.nchunks;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bestv, o);
@@ -2091,7 +2151,12 @@ __global__ void wait_selftest_kernel(const __grid_constant__ DecodeParams P) {
 }
 #endif
 
-__global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __grid_constant__ DecodeParams P) {
+#if MK_WFMT == 3
+constexpr int NTHR = NTHREADS + 32;        // + the warp that issues the tensor-core work
+#else
+constexpr int NTHR = NTHREADS;
+#endif
+__global__ void __launch_bounds__(NTHR, 1) decode_megakernel_bf16(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(1024) char smem[];
     Ctx c;
     c.smem = smem;
@@ -2114,7 +2179,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
 
     // The pointer table is read on every chunk; keep it in shared memory.
     LW* s_layers = reinterpret_cast<LW*>(smem + OFF_LAYERS);
-    for (int i = threadIdx.x; i < P.num_layers * (int)(sizeof(LW) / 16); i += NTHREADS)
+    for (int i = threadIdx.x; i < P.num_layers * (int)(sizeof(LW) / 16); i += NTHR)
         reinterpret_cast<uint4*>(s_layers)[i] = __ldg(reinterpret_cast<const uint4*>(P.layers) + i);
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSTAGE; ++s) {
@@ -2128,13 +2193,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
         const uint32_t ubar = smem_u32(smem + U_OFF_BARS);
         mbar_init(ubar, 1); mbar_init(ubar + 8, 1);             // product done (tcgen05.commit)
         mbar_init(ubar + 16, 2); mbar_init(ubar + 24, 2);       // accumulator buffer read back by warps 0 and 1
+        mbar_init(ubar + 32, NCW);                              // activation operand written by the consumer warps
 #endif
         fence_mbar_init();
     }
 #if MK_WFMT == 3
     c.amax = 0.f; c.mma_n = 0; c.inv_g = 1.0f;
     // activation operand and its scales start as zeros: rows of unused residual terms must stay zero
-    for (int i = threadIdx.x; i < (U_B_BYTES + U_SFB_BYTES) / 16; i += NTHREADS)
+    for (int i = threadIdx.x; i < (U_B_BYTES + U_SFB_BYTES) / 16; i += NTHR)
         reinterpret_cast<uint4*>(smem + U_OFF_B)[i] = make_uint4(0, 0, 0, 0);
     if (c.warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem + U_OFF_TMEM)), "r"(U_TM_COLS) : "memory");
@@ -2177,6 +2243,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_megakernel_bf16(const __gr
                 if (!lm) { if (dn) ++dn_idx; else ++fa_idx; }
             }
         }
+#if MK_WFMT == 3
+    } else if (c.warp == NCW + 1) {
+        // ===== MMA warp: one thread walks the same schedule and issues the tensor-core work of every projection =====
+        if (c.lane == 0) {
+            uint32_t m = 0, an = 0;
+#pragma unroll 1
+            for (int step = 0; step < P.steps; ++step) {
+                c.pos = P.position + step;
+                c.step = step;
+                for (int layer = 0; layer < P.num_layers; ++layer) {
+                    const bool dn = (s_layers[layer].layer_type == 0);
+#pragma unroll 1
+                    for (int ph = 0; ph < 5; ++ph) {
+                        int type;
+                        if (dn) type = (ph == 0) ? T_DN_IN : (ph == 1) ? T_DN_REC : (ph == 2) ? T_DN_OUT : (ph == 3) ? T_GATEUP : T_DOWN;
+                        else type = (ph == 0) ? T_FA_IN : (ph == 1) ? T_FA_ATT : (ph == 2) ? T_FA_OUT : (ph == 3) ? T_GATEUP : T_DOWN;
+                        c.where = 0x4000u | ((uint32_t)layer << 4) | (uint32_t)type;
+                        const Geo g = phase_geo(type, c.cta, c.G, P.vocab, c.pos);
+                        if (ph == 1) c.it += g.nchunks;               // recurrence / attention chunks: not this warp's
+                        else if (g.nchunks > 0) u_mma_phase(P, c, type, g.nchunks, m, an, false, false);
+                    }
+                }
+                c.where = 0x4000u | ((uint32_t)P.num_layers << 4) | T_LM;
+                const Geo g = phase_geo(T_LM, c.cta, c.G, P.vocab, c.pos);
+                for (int q = 0; q < g.nchunks; ++q) u_mma_phase(P, c, T_LM, 1, m, an, true, q == 0);
+            }
+        }
+#endif
     } else {
         // ===== consumer warps =====
 #pragma unroll 1

@@ -446,6 +446,10 @@ struct PrefillWs {
     void* select_scratch = nullptr;
     float* splitk = nullptr;        // f32 partial products of the K-split projections of short prompts
     size_t splitk_bytes = 0;
+    // NVFP4 x NVFP4 prefill: the current GEMM input quantised to NVFP4 (codes, 128 x 4 scale tiles) and the constant 1
+    // that stands in for an activation tensor scale
+    uint8_t *q_packed = nullptr, *q_scales = nullptr;
+    float* one = nullptr;
 };
 PrefillWs g_pws[64];
 constexpr int SPLITK_MAX_TOKENS = 2048;     // longer prompts fill the SMs without a K-split
@@ -457,6 +461,7 @@ constexpr int LM_BLOCKS = 1184;     // 8 resident blocks of 256 threads on each 
 // Callers that capture graphs size the workspace once with mk_prefill_reserve() and never grow it afterwards.
 unsigned g_ws_generation[64] = {0};
 cudaError_t ensure_ws(PrefillWs& w, int S, cudaStream_t stream = nullptr, bool check_capture = false) {
+    S = (S + 127) & ~127;           // whole 128-row blocks: the NVFP4 activation quantiser and its scale tiles work on those
     if (S <= w.cap) return cudaSuccess;
     if (check_capture) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -469,14 +474,15 @@ cudaError_t ensure_ws(PrefillWs& w, int S, cudaStream_t stream = nullptr, bool c
     ++g_ws_generation[&w - g_pws];
     void** ptrs[] = {(void**)&w.hidden, (void**)&w.normed, (void**)&w.wide, (void**)&w.z, (void**)&w.act, (void**)&w.pre,
                      (void**)&w.o, (void**)&w.beta, (void**)&w.decay, (void**)&w.kq, &w.chunk_scratch, &w.select_scratch,
-                     (void**)&w.splitk};
+                     (void**)&w.splitk, (void**)&w.q_packed, (void**)&w.q_scales};
     w.splitk_bytes = 0;
     for (void** p : ptrs) { if (*p) cudaFree(*p); *p = nullptr; }
     const size_t s = (size_t)S;
     const size_t sizes[] = {s * HIDDEN * 2, s * HIDDEN * 2, s * 2 * INTER * 2, s * DN_V * 2, s * INTER * 2,
                             s * DN_CONV_CH * 4, s * DN_V * 4, s * 16 * 16, 16, 16, dn_chunked_scratch_bytes(S), block_select_scratch_bytes(S),
-                            (size_t)(S < SPLITK_MAX_TOKENS ? S : SPLITK_MAX_TOKENS) * 4 * HIDDEN * sizeof(float)};
-    for (int i = 0; i < 13; ++i) {
+                            (size_t)(S < SPLITK_MAX_TOKENS ? S : SPLITK_MAX_TOKENS) * 4 * HIDDEN * sizeof(float),
+                            s * (INTER / 2), (s / 128) * (INTER / 64) * 512};
+    for (int i = 0; i < 15; ++i) {
         cudaError_t e = cudaMalloc(ptrs[i], sizes[i]);
         if (e != cudaSuccess) { w.cap = 0; return e; }
     }
@@ -486,6 +492,9 @@ cudaError_t ensure_ws(PrefillWs& w, int S, cudaStream_t stream = nullptr, bool c
         if (e == cudaSuccess) e = cudaMalloc((void**)&w.bidx, LM_BLOCKS * 4);
         if (e == cudaSuccess) e = cudaMalloc((void**)&w.err, 4);
         if (e == cudaSuccess) e = cudaMemset(w.err, 0, 4);
+        if (e == cudaSuccess) e = cudaMalloc((void**)&w.one, 16);
+        const float one = 1.0f;
+        if (e == cudaSuccess) e = cudaMemcpy(w.one, &one, 4, cudaMemcpyHostToDevice);
         if (e != cudaSuccess) return e;
         float tab[FA_ROT / 2];
         for (int i = 0; i < FA_ROT / 2; ++i) tab[i] = (float)(1.0 / pow(ROPE_THETA, (2.0 * i) / FA_ROT));
@@ -580,6 +589,11 @@ struct LayerView {
     const void *w_faqkv = nullptr, *w_q = nullptr, *w_k = nullptr, *w_v = nullptr, *q_norm = nullptr, *k_norm = nullptr,
                *w_o = nullptr;                                                                  // attention
     const void *w_gateup = nullptr, *w_gate = nullptr, *w_up = nullptr, *w_down = nullptr;      // MLP
+    // NVFP4 x NVFP4 prefill: when fp4 is set, the projections above are these quantised matrices instead
+    // (packed e2m1, E4M3 block scales in 128 x 4 tiles, device fp32 tensor scale); beta / alpha stay bf16
+    struct W4 { const void* packed = nullptr; const void* scales = nullptr; const float* ts = nullptr; };
+    bool fp4 = false;
+    W4 x_qkv, x_z, x_out, x_q, x_k, x_v, x_o, x_gate, x_up, x_down;
 };
 struct LmView { const void* bf16 = nullptr; const void* packed = nullptr; const void* scales = nullptr; };
 
@@ -679,6 +693,17 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
     auto gemm = [&](const void* A, const void* W, void* C, const void* R, int N, int K, int ldc) {
         return gemm_bf16_tn(A, W, C, R, S, N, K, K, ldc, w.err, w.splitk, w.splitk_bytes, stream);
     };
+    // NVFP4 x NVFP4: quantise the [S, K] input of the coming projections once (16-element blocks along K, E4M3 block
+    // scales, no tensor scale: the quantiser of the reference's LM-head format), then multiply on the block-scaled
+    // tensor cores.  Rows S .. (S rounded up to 128) of the input are whatever the buffer holds: they are quantised
+    // with the rest and never stored.
+    const int S_pad = (S + 127) & ~127;
+    auto quant = [&](const void* X, int K) {
+        return launch_quantize_nvfp4_lm_out(X, S_pad, K, w.q_packed, w.q_scales, stream) == MK_OK ? cudaSuccess : cudaErrorInvalidValue;
+    };
+    auto gemm4 = [&](const LayerView::W4& W, void* C, const void* R, int N, int K, int ldc) {
+        return gemm_nvfp4_tn(w.q_packed, w.q_scales, w.one, W.packed, W.scales, W.ts, C, R, S, N, K, ldc, w.err, stream);
+    };
     const int wpb = 8;                                            // warps per 256-thread block
     auto blocks_for_warps = [&](long long nw) { return (unsigned)((nw + wpb - 1) / wpb); };
 
@@ -693,8 +718,14 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
         if (dn) {
             float* state = (float*)dn_states + (size_t)dn_idx * DN_HEADS * DN_VAL * DN_KEY;
             float* cstate = (float*)conv_bufs + (size_t)dn_idx * DN_CONV_CH * DN_CONV_K;
-            PF_CHECK(gemm(w.normed, lv.w_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
-            PF_CHECK(gemm(w.normed, lv.w_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
+            if (lv.fp4) {
+                PF_CHECK(quant(w.normed, HIDDEN), "quantise activations");
+                PF_CHECK(gemm4(lv.x_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
+                PF_CHECK(gemm4(lv.x_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
+            } else {
+                PF_CHECK(gemm(w.normed, lv.w_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
+                PF_CHECK(gemm(w.normed, lv.w_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
+            }
             launch_pdl(k_dn_gates_mma, (unsigned)((S + 15) / 16), 128, 0, stream, w.normed, (const bf*)lv.w_b, (const bf*)lv.w_a,
                        (const bf*)lv.a_log, (const bf*)lv.dt_bias, w.beta, S);
             if (g_scan_mode == 0) {
@@ -705,12 +736,22 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
             }
             launch_pdl(k_dn_conv_state, (DN_CONV_CH + 255) / 256, 256, 0, stream, w.wide, cstate, S);
             launch_pdl(k_dn_gated_norm, blocks_for_warps((long long)S * DN_HEADS), 256, 0, stream, w.o, w.z, (const bf*)lv.dn_norm, w.act, S);
-            PF_CHECK(gemm(w.act, lv.w_out, w.hidden, w.hidden, HIDDEN, DN_V, HIDDEN), "gemm out");
+            if (lv.fp4) {
+                PF_CHECK(quant(w.act, DN_V), "quantise activations");
+                PF_CHECK(gemm4(lv.x_out, w.hidden, w.hidden, HIDDEN, DN_V, HIDDEN), "gemm out");
+            } else {
+                PF_CHECK(gemm(w.act, lv.w_out, w.hidden, w.hidden, HIDDEN, DN_V, HIDDEN), "gemm out");
+            }
             ++dn_idx;
         } else {
             bf* kc = (bf*)fa_k_cache + (size_t)fa_idx * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;
             bf* vc = (bf*)fa_v_cache + (size_t)fa_idx * FA_KV_HEADS * max_seq_len * FA_HEAD_DIM;
-            if (lv.w_faqkv) {
+            if (lv.fp4) {
+                PF_CHECK(quant(w.normed, HIDDEN), "quantise activations");
+                PF_CHECK(gemm4(lv.x_q, w.wide, nullptr, FA_QPROJ, HIDDEN, FA_QKV_ROWS), "gemm q");
+                PF_CHECK(gemm4(lv.x_k, w.wide + FA_QPROJ, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm k");
+                PF_CHECK(gemm4(lv.x_v, w.wide + FA_QPROJ + FA_KV_SIZE, nullptr, FA_KV_SIZE, HIDDEN, FA_QKV_ROWS), "gemm v");
+            } else if (lv.w_faqkv) {
                 PF_CHECK(gemm(w.normed, lv.w_faqkv, w.wide, nullptr, FA_QKV_ROWS, HIDDEN, FA_QKV_ROWS), "gemm fa qkv");
             } else {
                 PF_CHECK(gemm(w.normed, lv.w_q, w.wide, nullptr, FA_QPROJ, HIDDEN, FA_QKV_ROWS), "gemm q");
@@ -728,18 +769,32 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
             }
             if (g_attn_impl == 1) PF_CHECK(fa_prefill_tcgen05(w.wide, kc, vc, w.act, S, max_seq_len, w.err, bmask, stream), "attention");
             else PF_CHECK(fa_prefill(w.wide, kc, vc, w.act, S, max_seq_len, bmask, stream), "attention");
-            PF_CHECK(gemm(w.act, lv.w_o, w.hidden, w.hidden, HIDDEN, FA_Q_SIZE, HIDDEN), "gemm o");
+            if (lv.fp4) {
+                PF_CHECK(quant(w.act, FA_Q_SIZE), "quantise activations");
+                PF_CHECK(gemm4(lv.x_o, w.hidden, w.hidden, HIDDEN, FA_Q_SIZE, HIDDEN), "gemm o");
+            } else {
+                PF_CHECK(gemm(w.act, lv.w_o, w.hidden, w.hidden, HIDDEN, FA_Q_SIZE, HIDDEN), "gemm o");
+            }
             ++fa_idx;
         }
         launch_pdl(k_rmsnorm, blocks_for_warps(S), 256, 0, stream, w.hidden, (const bf*)lv.post_norm, w.normed, S);
-        if (lv.w_gateup) {
+        if (lv.fp4) {
+            PF_CHECK(quant(w.normed, HIDDEN), "quantise activations");
+            PF_CHECK(gemm4(lv.x_gate, w.wide, nullptr, INTER, HIDDEN, 2 * INTER), "gemm gate");
+            PF_CHECK(gemm4(lv.x_up, w.wide + INTER, nullptr, INTER, HIDDEN, 2 * INTER), "gemm up");
+        } else if (lv.w_gateup) {
             PF_CHECK(gemm(w.normed, lv.w_gateup, w.wide, nullptr, 2 * INTER, HIDDEN, 2 * INTER), "gemm gate_up");
         } else {
             PF_CHECK(gemm(w.normed, lv.w_gate, w.wide, nullptr, INTER, HIDDEN, 2 * INTER), "gemm gate");
             PF_CHECK(gemm(w.normed, lv.w_up, w.wide + INTER, nullptr, INTER, HIDDEN, 2 * INTER), "gemm up");
         }
         launch_pdl(k_silu_mul, (unsigned)(((size_t)S * (INTER / 8) + 255) / 256), 256, 0, stream, w.wide, w.act, S);
-        PF_CHECK(gemm(w.act, lv.w_down, w.hidden, w.hidden, HIDDEN, INTER, HIDDEN), "gemm down");
+        if (lv.fp4) {
+            PF_CHECK(quant(w.act, INTER), "quantise activations");
+            PF_CHECK(gemm4(lv.x_down, w.hidden, w.hidden, HIDDEN, INTER, HIDDEN), "gemm down");
+        } else {
+            PF_CHECK(gemm(w.act, lv.w_down, w.hidden, w.hidden, HIDDEN, INTER, HIDDEN), "gemm down");
+        }
     }
     launch_pdl(k_final_norm, 1, 512, 0, stream, w.hidden + (size_t)(S - 1) * HIDDEN, (const bf*)final_norm_w, w.normed_f32,
                                         (bf*)final_normed, (bf*)hidden_bf16_out);
@@ -1008,6 +1063,53 @@ extern "C" int launch_prefill_megakernel_nvfp4(
     return mk_prefill_nvfp4(token_ids, seq_len, output_token_id, embed_weight, layer_weights, final_norm_weight,
                             lm_head_weight_packed, lm_head_scales, fa_k_cache, fa_v_cache, dn_states, conv_bufs, nullptr,
                             hidden_buffer, max_seq_len, group_size, nl, vocab, stream);
+}
+
+// Prefill with NVFP4 weights AND NVFP4 activations on the block-scaled tensor cores: every projection input is
+// quantised per 16 values along K (E4M3 block scales) and multiplied with the quantised weights by
+// tcgen05.mma kind::mxf4nvf4; nothing is dequantised to bf16.  layers: 224-byte entries as for mk_decode_nvfp4_ts, but
+// the scale slot of each matrix points at the 128 x 4 scale TILES the quantiser writes (not at plain rows).
+extern "C" int mk_prefill_nvfp4_mma(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const void* layers, const void* final_norm_w,
+    const void* lm_head_packed, const void* lm_head_scales_tiled,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* final_normed, void* hidden_bf16_out,
+    int max_seq_len, int num_layers, int vocab, cudaStream_t stream) {
+    using namespace mk;
+    const void* req[] = {token_ids, output_token, embed_weight, layers, final_norm_w, lm_head_packed, lm_head_scales_tiled,
+                         fa_k_cache, fa_v_cache, dn_states, conv_bufs};
+    int dev = 0;
+    int rc = check_common(req, 11, seq_len, max_seq_len, num_layers, vocab, dev);
+    if (rc != MK_OK) return rc;
+    if (vocab % 128) return pfail(MK_ERR_BAD_ARG, "the NVFP4 LM head needs a vocabulary that is a multiple of 128");
+    HostTableTS& ht = g_tables_ts[dev];
+    if (ht.src != layers || ht.n != num_layers) {
+        PF_CHECK(cudaMemcpyAsync(ht.rows, layers, (size_t)num_layers * sizeof(LayerWeightsNVFP4TS), cudaMemcpyDeviceToHost, stream), "table copy");
+        PF_CHECK(cudaStreamSynchronize(stream), "table copy sync");
+        ht.src = layers; ht.n = num_layers;
+    }
+    const LayerWeightsNVFP4TS* hl = ht.rows;
+    auto source = [&](int li, LayerView& lv) -> int {
+        const LayerWeightsNVFP4TS& e = hl[li];
+        auto m = [&](int slot) { return LayerView::W4{e.ptrs[slot], e.ptrs[slot + 1], (const float*)e.ptrs[slot + 2]}; };
+        lv.type = e.layer_type;
+        lv.fp4 = true;
+        lv.in_norm = e.ptrs[0];
+        if (e.layer_type == 0) {   // in_norm, qkv(3), z(3), w_beta, w_alpha, conv_w, A_log, dt_bias, norm_w, out(3), post_norm, gate(3), up(3), down(3)
+            lv.x_qkv = m(1); lv.x_z = m(4); lv.w_b = e.ptrs[7]; lv.w_a = e.ptrs[8]; lv.conv_w = e.ptrs[9]; lv.a_log = e.ptrs[10];
+            lv.dt_bias = e.ptrs[11]; lv.dn_norm = e.ptrs[12]; lv.x_out = m(13); lv.post_norm = e.ptrs[16];
+            lv.x_gate = m(17); lv.x_up = m(20); lv.x_down = m(23);
+        } else {                   // in_norm, q(3), k(3), v(3), q_norm, k_norm, o(3), post_norm, gate(3), up(3), down(3)
+            lv.x_q = m(1); lv.x_k = m(4); lv.x_v = m(7); lv.q_norm = e.ptrs[10]; lv.k_norm = e.ptrs[11]; lv.x_o = m(12);
+            lv.post_norm = e.ptrs[15]; lv.x_gate = m(16); lv.x_up = m(19); lv.x_down = m(22);
+        }
+        return MK_OK;
+    };
+    LmView lm;
+    lm.packed = lm_head_packed; lm.scales = lm_head_scales_tiled;     // the LM head's tensor scale is positive: the argmax does not need it
+    return prefill_core(token_ids, seq_len, output_token, embed_weight, source, num_layers, final_norm_w, lm, fa_k_cache, fa_v_cache,
+                        dn_states, conv_bufs, final_normed, hidden_bf16_out, max_seq_len, vocab, dev, stream);
 }
 
 // The attention building blocks on their own (tests call these through the C ABI).

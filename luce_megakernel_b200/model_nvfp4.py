@@ -226,14 +226,19 @@ def attach_nvfp4_ts_weights(weights):
     for ld in weights["layer_data"]:
         p = ld["ptrs"]
 
+        tiled = {}
+
         def q(i):
             m = _quantize_matrix_nvfp4_ts(lib, p[i])
+            tiled[id(m["scales"])] = m["scales_tiled"]
             return [m["packed"], m["scales"], m["tensor_scale"]]
         if ld["type"] == 1:
             ptrs = [p[0]] + q(1) + q(2) + q(3) + [p[4], p[5]] + q(6) + [p[7]] + q(8) + q(9) + q(10)
         else:
             ptrs = [p[0]] + q(1) + q(2) + [p[3], p[4], p[5], p[6], p[7], p[8]] + q(9) + [p[10]] + q(11) + q(12) + q(13)
-        layers.append({"type": ld["type"], "ptrs": ptrs})
+        # the same slot list with every scale slot pointing at the quantiser's 128 x 4 tiles (block-scaled GEMM operand)
+        ptrs_tiled = [tiled.get(id(t), t) for t in ptrs]
+        layers.append({"type": ld["type"], "ptrs": ptrs, "ptrs_tiled": ptrs_tiled})
     lm = _quantize_matrix_nvfp4_ts(lib, weights["lm_head_weight"])
     weights["nvfp4_ts"] = {"layer_data": layers, "lm": lm}
     return weights
@@ -307,6 +312,28 @@ class DecoderTS:
             raise RuntimeError("decode launch gave up on a device-side wait: status word 0x%08x"
                                % self._lib.mk_device_status_detail())
         return tok
+
+    def prefill(self, token_ids) -> int:
+        """Prompt from position 0 with NVFP4 weights and NVFP4 activations on the block-scaled tensor cores
+        (mk_prefill_nvfp4_mma); returns the first generated token."""
+        ids = torch.as_tensor(token_ids, dtype=torch.int32).to(self._embed_weight.device).contiguous()
+        S = int(ids.numel())
+        if S < 1 or S > self.max_seq_len:
+            raise ValueError("prompt length must be in [1, max_seq_len]")
+        if not hasattr(self, "_table_tiled"):
+            nv = self._weights["nvfp4_ts"]
+            self._table_tiled = _pack_layer_weights_nvfp4_ts([{"type": ld["type"], "ptrs": ld["ptrs_tiled"]} for ld in nv["layer_data"]])
+            self._final_normed_bf16 = torch.empty(HIDDEN_SIZE, dtype=torch.bfloat16, device=self._embed_weight.device)
+        self._check(self._lib.mk_set_model_dims(self.num_layers, self.vocab))
+        out = torch.empty(1, dtype=torch.int32, device=self._embed_weight.device)
+        self._check(self._lib.mk_prefill_nvfp4_mma(
+            _ptr(ids), ctypes.c_int(S), _ptr(out), _ptr(self._embed_weight), _ptr(self._table_tiled),
+            _ptr(self._final_norm_weight), _ptr(self._lm["packed"]), _ptr(self._lm["scales_tiled"]), _ptr(self._fa_k_cache),
+            _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs), _ptr(self._final_normed_bf16), _ptr(self._hidden),
+            ctypes.c_int(self.max_seq_len), ctypes.c_int(self.num_layers), ctypes.c_int(self.vocab),
+            ctypes.c_void_p(torch.cuda.current_stream(self._embed_weight.device).cuda_stream)))
+        self._position = S
+        return int(out.item())
 
     def adopt_state(self, other):
         """Take over the session state (caches, DeltaNet state, conv window, position) of another decoder over the

@@ -212,7 +212,7 @@ class Oracle:
     """fp32 restatement of the reference decode arithmetic, usable for T>=1 consecutive tokens."""
 
     def __init__(self, weights: Dict[str, torch.Tensor], rounding: str = "decode", ref_q_rope_in_place: bool = False,
-                 block_sparse: Optional[dict] = None):
+                 block_sparse: Optional[dict] = None, act_quant=None):
         """ref_q_rope_in_place reproduces what the reference decode kernel actually computes for the
         query's rotary dims 32..63: it rotates q in place (kernel.cu:487-497), so by the time a lane
         reaches dim i+32 its partner dim i already holds the rotated value, which is then normalised
@@ -222,6 +222,10 @@ class Oracle:
         restatement against the reference kernels themselves, run on a GPU."""
         assert rounding in ("decode", "none")
         self.rounding = rounding
+        # act_quant: optional callable [T, K] f32 -> [T, K] f32 applied to the input of every quantised projection
+        # (qkv / z / out, q / k / v / o, gate / up / down; not beta / alpha, not the LM head): models a path that
+        # multiplies quantised activations, e.g. NVFP4 x NVFP4 on the block-scaled tensor cores
+        self.act_quant = act_quant
         self.ref_q_rope_in_place = ref_q_rope_in_place
         # block_sparse = {"top_frac": .., "window": .., "sink": ..}: prompts processed from position 0 attend
         # only to the key blocks oracle/block_sparse.py selects (bf16-rounded q and k feed the selection)
@@ -237,13 +241,17 @@ class Oracle:
     def _r(self, x):
         return _bf(x) if self.rounding == "decode" else x
 
+    def _q(self, x):
+        return self.act_quant(x) if self.act_quant is not None else x
+
     # -- token mixers ----------------------------------------------------------------
 
     def _deltanet(self, p: str, x: torch.Tensor, st: State, idx: int) -> torch.Tensor:
         w = self.w
         T = x.shape[0]
-        c = x @ w[p + "in_proj_qkv.weight"].T                    # [T, 6144]  kernel.cu:621
-        z = x @ w[p + "in_proj_z.weight"].T                      # [T, 2048]
+        xq = self._q(x)
+        c = xq @ w[p + "in_proj_qkv.weight"].T                   # [T, 6144]  kernel.cu:621
+        z = xq @ w[p + "in_proj_z.weight"].T                     # [T, 2048]
         b = x @ w[p + "in_proj_b.weight"].T                      # [T, 16]
         a = x @ w[p + "in_proj_a.weight"].T                      # [T, 16]
         # causal depthwise conv over [state(4) | new(T)], SiLU        kernel.cu:633-648
@@ -277,6 +285,7 @@ class Oracle:
     def _attention(self, p: str, x: torch.Tensor, st: State, idx: int, pos0: int) -> torch.Tensor:
         w = self.w
         T = x.shape[0]
+        x = self._q(x)
         qg = (x @ w[p + "q_proj.weight"].T).reshape(T, FA_Q_HEADS, 2 * FA_HEAD_DIM)     # kernel.cu:450
         q, gate = qg[..., :FA_HEAD_DIM], qg[..., FA_HEAD_DIM:]
         k = (x @ w[p + "k_proj.weight"].T).reshape(T, FA_KV_HEADS, FA_HEAD_DIM)
@@ -351,15 +360,16 @@ class Oracle:
             x = self._r(_rms(h, 1.0 + w[p + "input_layernorm.weight"]))                  # kernel.cu:228
             if lt == 0:
                 a = self._deltanet(p + "linear_attn.", x, st, dn_i)
-                h = self._r(a @ w[p + "linear_attn.out_proj.weight"].T + h)              # kernel.cu:739
+                h = self._r(self._q(a) @ w[p + "linear_attn.out_proj.weight"].T + h)     # kernel.cu:739
                 dn_i += 1
             else:
                 a = self._attention(p + "self_attn.", x, st, fa_i, pos0)
-                h = self._r(a @ w[p + "self_attn.o_proj.weight"].T + h)                  # kernel.cu:568
+                h = self._r(self._q(a) @ w[p + "self_attn.o_proj.weight"].T + h)         # kernel.cu:568
                 fa_i += 1
             x = self._r(_rms(h, 1.0 + w[p + "post_attention_layernorm.weight"]))         # kernel.cu:574
-            m = F.silu(x @ w[p + "mlp.gate_proj.weight"].T) * (x @ w[p + "mlp.up_proj.weight"].T)
-            h = self._r(m @ w[p + "mlp.down_proj.weight"].T + h)                         # kernel.cu:585
+            xq = self._q(x)
+            m = F.silu(xq @ w[p + "mlp.gate_proj.weight"].T) * (xq @ w[p + "mlp.up_proj.weight"].T)
+            h = self._r(self._q(m) @ w[p + "mlp.down_proj.weight"].T + h)                # kernel.cu:585
             tr.hidden.append(h.clone())
         st.position = pos0 + T
         n = _rms(h[-1], 1.0 + w["model.norm.weight"])                                    # kernel.cu:916-919 (f32)
