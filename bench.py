@@ -317,6 +317,101 @@ def run_reference_gpu(args):
 _RESULT_FD = None
 
 
+NVFP4_NOMINAL_TFLOPS = 9000.0      # dense fp4 tensor peak of a B200 (nominal: the measured-peaks file has bf16 only)
+
+
+def nvfp4_extras(MQ, M, weights, dec, q, prompt_dev, tg128_device, timed, g, args):
+    """Single-GPU figures of the block-scaled tensor-core path (tcgen05.mma kind::mxf4nvf4): the GEMM on its own,
+    the prefill with NVFP4 weights and activations, the decode variant that multiplies chunk images, and the batched
+    step on NVFP4 weights.  `q` is the DecoderTS sharing dec's session state."""
+    import ctypes
+    from luce_megakernel_b200 import lib
+    L = lib()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    stream = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out = {}
+
+    def quant(x):
+        rows, cols = x.shape
+        pk = torch.zeros(rows, cols // 2, dtype=torch.uint8, device="cuda")
+        sc = torch.zeros((rows // 128) * (cols // 64) * 512, dtype=torch.uint8, device="cuda")
+        ts = torch.zeros(4, dtype=torch.float32, device="cuda")
+        if L.mk_quantize_nvfp4_tensor_scale(P(x), rows, cols, P(pk), P(sc), P(ts), stream()) != 0:
+            raise SystemExit("quantiser failed")
+        return pk, sc, ts
+
+    gemms = []
+    for (m, n, k) in ((8192, 7168, 1024), (8192, 1024, 3584), (8192, 8192, 8192)):
+        a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(n, k, device="cuda") * 0.05).to(torch.bfloat16)
+        (apk, asc, ats), (wpk, wsc, wts) = quant(a), quant(w)
+        c = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        f4 = lambda: L.mk_gemm_nvfp4_tn(P(apk), P(asc), P(ats), P(wpk), P(wsc), P(wts), P(c), None, m, n, k, stream())
+        f16 = lambda: L.mk_gemm_bf16_tn(P(a), P(w), P(c), None, m, n, k, stream())
+        for f in (f4, f16):
+            for _ in range(3):
+                f()
+        us4 = timed(lambda: [f4() for _ in range(10)], 1) * 100.0
+        us16 = timed(lambda: [f16() for _ in range(10)], 1) * 100.0
+        tf4 = 2.0 * m * n * k / us4 / 1e6
+        gemms.append({"m": m, "n": n, "k": k, "us": us4, "tflops": tf4, "frac_of_nominal_fp4_peak": tf4 / NVFP4_NOMINAL_TFLOPS,
+                      "vs_measured_bf16_peak": tf4 / measured_bf16_peak(), "bf16_kernel_us": us16, "speedup_vs_bf16_kernel": us16 / us4})
+        del a, w, apk, asc, wpk, wsc, c
+    if L.mk_gemm_nvfp4_status() != 0:
+        raise SystemExit("a bounded wait ran out in the NVFP4 GEMM")
+    out["gemm"] = {"kernel": "gemm_nvfp4_tn_kernel: NVFP4 x NVFP4 -> bf16, 128 x 128 tiles, block scales in tensor memory",
+                   "peak_note": f"fraction of the NOMINAL dense fp4 peak ({NVFP4_NOMINAL_TFLOPS:.0f} TFLOP/s); no fp4 peak was measured on this pool",
+                   "shapes": gemms}
+
+    # prefill with NVFP4 weights and NVFP4 activations, pp520 (into the shared session state) and 8192 tokens
+    pf = []
+    for S_ in (PROMPT_LEN, 8192):
+        d4 = q if S_ == PROMPT_LEN else MQ.DecoderTS(weights, max_seq_len=S_ + 8)
+        ids = prompt_dev if S_ == PROMPT_LEN else torch.randint(0, M.VOCAB_SIZE, (S_,), generator=g).to(torch.int32).cuda()
+
+        def run(d=d4, x=ids):
+            d._dn_states.zero_(); d._conv_bufs.zero_()
+            return d.prefill(x)
+        run(); run()
+        ms_ = timed(lambda: [run() for _ in range(3)], 1) / 3
+        pf.append({"prompt_len": S_, "ms": ms_, "tok_s": S_ / (ms_ * 1e-3)})
+    if L.mk_prefill_status() != 0 or L.mk_gemm_nvfp4_status() != 0:
+        raise SystemExit("a bounded wait ran out in the NVFP4 prefill")
+    out["prefill"] = {"op": "mk_prefill_nvfp4_mma: every projection input quantised to NVFP4, block-scaled GEMMs; "
+                            "attention, DeltaNet scan and norms as in the bf16 prefill", "runs": pf}
+
+    # restore the bf16 prompt state, then the decode variant on the block-scaled tensor cores
+    dec._position = 0
+    dec._dn_states.zero_(); dec._conv_bufs.zero_()
+    dec.prefill(prompt_dev)
+    qm = MQ.DecoderMMA(weights, max_seq_len=MAX_SEQ, act_terms=4)
+    qm.adopt_state(dec)
+    for _ in range(3):
+        tg128_device(qm)
+    mm_ms = timed(lambda: tg128_device(qm), args.steps)
+    if L.mk_device_status() != 0:
+        raise SystemExit("device-side wait timed out during the tcgen05 NVFP4 decode")
+    out["decode"] = {"op": "mk_decode_nvfp4_mma, activation expanded into 4 NVFP4 terms", "us_per_token": mm_ms * 1e3 / (GEN_LEN * args.steps),
+                     "tok_s": GEN_LEN * args.steps / (mm_ms * 1e-3),
+                     "note": "issue-bound: one tcgen05.cp / tcgen05.mma costs about 42 ns and a projection of K inputs needs K/32 of "
+                             "them after the activation is known; the mma.sync variant (nvfp4_decode) is the faster NVFP4 decode"}
+    del qm
+
+    # batched step on NVFP4 weights (BASELINE.json configs[3]: batch 8)
+    bd = M.BatchDecoder(dec, 8, nvfp4_ts=True)
+    prompts = [torch.randint(0, M.VOCAB_SIZE, (PROMPT_LEN,), generator=g).tolist() for _ in range(8)]
+    runs = []
+    for r in range(3):
+        bd.reset()
+        bd.prefill(prompts)
+        runs.append(timed(lambda: bd.step_many(GEN_LEN), 1))
+    t_ = sum(runs[1:]) / 2 / GEN_LEN
+    out["decode_batch"] = {"batch_per_gpu": 8, "ms_per_step": t_, "tok_s": 8 / (t_ * 1e-3),
+                           "note": "mk_decode_batch_nvfp4_ts: NVFP4 weights dequantised in registers for mma.sync; launch-bound like the bf16 step"}
+    del bd
+    return out
+
+
 def protect_stdout():
     """Libraries print to stdout from native code (NCCL's version banner): keep fd 1 for the one JSON line and send
     everything else to stderr."""
@@ -433,6 +528,7 @@ def main():
     # NVFP4 decode: every linear layer and the LM head as e2m1 in 16-element blocks with E4M3
     # block scales and an fp32 tensor scale, bf16 KV cache; same prompt state (bf16 prefill), then tg128
     nv_ms = 0.0
+    nv_extra = None
     if not args.no_nvfp4:
         from luce_megakernel_b200 import model_nvfp4 as MQ
         q = MQ.DecoderTS(weights, max_seq_len=MAX_SEQ)
@@ -442,7 +538,10 @@ def main():
         nv_ms = timed(lambda: tg128_device(q), args.steps)
         if lib().mk_device_status() != 0:
             raise SystemExit("device-side wait timed out during the NVFP4 decode")
+        if world == 1:
+            nv_extra = nvfp4_extras(MQ, M, weights, dec, q, prompt_dev, tg128_device, timed, g, args)
         del q
+        weights.pop("nvfp4_mma", None)
         weights.pop("nvfp4_ts", None)
 
     # prefill pp520 (secondary figure): 3 warm-ups, then 10 timed calls of the prefill op
@@ -550,6 +649,8 @@ def main():
                              "frac": nv_bytes / (nv_us * 1e-6) / 1e9 / peak, "algorithmic_bytes_per_token": nv_bytes},
                 "note": "mk_decode_nvfp4_ts: 128 steps per launch; one dependent phase is one ring chunk per CTA, so the "
                         "step is bound by the 120 activation exchanges, not by bytes"}
+            if nv_extra:
+                out["nvfp4_tensor_core"] = nv_extra
         if batch_ms:
             hbm, _ = measured_hbm_peak()
             out["decode_batch"] = [
