@@ -481,6 +481,12 @@ def main():
     ap.add_argument("--no-long-prefill", action="store_true")
     ap.add_argument("--no-batch", action="store_true", help="skip the batch 8 / batch 16 decode figures")
     ap.add_argument("--no-nvfp4", action="store_true", help="skip the NVFP4 decode figure")
+    ap.add_argument("--barrier", default="gloo", choices=["nccl", "gloo"],
+                    help="process group for the timing barriers and the final reduction (N > 1); the data path has no "
+                         "collective.  gloo by default: with an NCCL communicator alive in the process the persistent "
+                         "decode kernel ran 0.7 % (rank 0) and 5.7 % (rank 1) slower on 2 GPUs, with gloo every rank runs "
+                         "at its single-GPU speed")
+    ap.add_argument("--no-sampler", action="store_true", help="do not run the nvidia-smi clock sampler beside the timed region")
     args = ap.parse_args()
     protect_stdout()
     if args.impl == "reference":
@@ -496,7 +502,10 @@ def main():
     if use_dist:
         import torch.distributed as dist
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        if args.barrier == "gloo":
+            dist.init_process_group("gloo")
+        else:
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
 
     from luce_megakernel_b200 import lib, model as M, replicas as R
     weights, _ = M.load_weights(seed=rank, device_init=True)
@@ -538,11 +547,12 @@ def main():
     # the sampler starts with the warm-up (the same workload as the timed region) so that short runs, and runs where
     # eight ranks start nvidia-smi at once, still collect samples under load
     sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ else 0)
-    sampler.start()
+    if not args.no_sampler:
+        sampler.start()
     for _ in range(max(args.warmup, 3)):
         tg128_device()
     ms = timed(tg128_device, args.steps)
-    clocks = sampler.stop()
+    clocks = sampler.stop() if not args.no_sampler else {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["not sampled"]}
     status = lib().mk_device_status()
     if status != 0:
         raise SystemExit(f"device-side wait timed out (status {status})")
@@ -634,6 +644,8 @@ def main():
     agg = R.aggregate(per_rank)
     t_all = torch.tensor([e2e_s, pp_ms, nv_ms] + (batch_ms or [0.0, 0.0]), dtype=torch.float64, device="cuda")
     if use_dist:
+        if args.barrier == "gloo":
+            t_all = t_all.cpu()
         dist.all_reduce(t_all, op=dist.ReduceOp.MAX)
     e2e_max, pp_max, nv_max = float(t_all[0]), float(t_all[1]), float(t_all[2])
     batch_max = [float(t_all[3]), float(t_all[4])]
