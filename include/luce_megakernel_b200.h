@@ -405,6 +405,20 @@ int mk_prefill_nvfp4_mma(
     void *final_normed, void *hidden_bf16_out,
     int max_seq_len, int num_layers, int vocab, cudaStream_t stream);
 
+/* Prompt compression for speculative prefill, with this model as its own drafter (the reference's pflash drafter scores
+ * a long prompt with a small model and keeps the chunks the last tokens attend to: dflash/src/qwen3_drafter.cpp:86-183,
+ * tail attention in dflash/src/qwen3_0p6b_graph.cpp:430-496).
+ * mk_prefill_set_tail_scoring(n, buf): later prefill calls of more than n tokens also fill buf [n][seq_len] (device
+ *   f32) with running_max[t][j] = max over attention layers and query heads of softmax_j(q_t . k_j / 16), t = the last n
+ *   prompt positions, keys j <= position of t (0 beyond); n = 0 or buf = NULL switches it off.  Works with the dense
+ *   and the block-sparse prefill (mk_prefill_set_block_sparse), which is how a long prompt is scored cheaply.
+ * mk_drafter_select (host arrays): mean over the n rows, average-pool smoothing over pool_kernel positions, mean per
+ *   chunk of chunk_size positions, the max(1, int(n_chunks * keep_ratio)) best chunks (equal means: lower chunk first);
+ *   writes the kept token positions in ascending order, returns their count (-1: bad argument). */
+void mk_prefill_set_tail_scoring(int n_lookahead, float *running_max);
+int mk_drafter_select(const float *running_max, int n_lookahead, int seq_len, float keep_ratio, int chunk_size,
+                      int pool_kernel, int *kept_positions_out);
+
 /* NVFP4 x NVFP4 product on the block-scaled tensor-core path (tcgen05.mma kind::mxf4nvf4, E4M3 scales per 16 values
  * read from tensor memory): C[M,N] = a_tensor_scale[0] * w_tensor_scale[0] * (A[M,K] . W[N,K]^T) (+ residual), C and
  * residual bf16 row-major.  Both operands in the format mk_quantize_nvfp4_tensor_scale writes (packed e2m1 rows, 128 x 4

@@ -36,6 +36,12 @@ cudaError_t gemm_nvfp4_tn(const void* a_packed, const void* a_scales, const floa
                           const void* w_scales, const float* w_tensor_scale, void* C, const void* R, int M, int N, int K, int ldc,
                           int* err_flag, cudaStream_t stream);
 
+// Tail attention of one attention layer for the prompt compressor: for each of the last n_look prompt positions and each
+// query head, the causal softmax over all keys, folded into running_max [n_look][S] (f32, >= 0) with a maximum.
+// qkv: [S][5120] bf16 with q normalised and rotated in place; kc: that layer's K cache [2][max_seq][256].
+cudaError_t tail_attention_scores(const void* qkv, const void* kc, int S, int max_seq, int n_look, float* running_max,
+                                  cudaStream_t stream);
+
 // Gated delta rule over a prompt in chunks of 64 tokens (all 16 heads of one layer).
 // qkv: bf16 [S][6144] projection outputs q | k | v (the causal conv1d + SiLU and the L2 norms are applied inside);
 // conv_w: bf16 [6144][4]; conv_state: f32 [6144][4], the four inputs before the prompt (read only);

@@ -514,6 +514,8 @@ HostTableTS g_tables_ts[64];
 thread_local char g_perr[200] = "";
 struct SparseCfg { bool enabled = false; double top_frac = 0.10; int window = 4, sink = 1; };
 SparseCfg g_sparse;
+struct TailCfg { int n = 0; float* running_max = nullptr; };   // tail-attention scoring for the prompt compressor (drafter.cu)
+TailCfg g_tail;
 int g_attn_impl = 1;              // attention kernel: 1 = tcgen05 / TMEM (default), 0 = mma.sync
 int g_scan_mode = 1;              // 1 = chunks of 64 on the tensor cores, 0 = token-serial recurrence
 int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
@@ -573,6 +575,10 @@ extern "C" int mk_prefill_status(void) {
     return v;
 }
 extern "C" void mk_prefill_set_attention_impl(int tcgen05) { mk::g_attn_impl = tcgen05 ? 1 : 0; }
+extern "C" void mk_prefill_set_tail_scoring(int n_lookahead, float* running_max) {
+    mk::g_tail.n = (n_lookahead > 0 && running_max) ? n_lookahead : 0;
+    mk::g_tail.running_max = mk::g_tail.n ? running_max : nullptr;
+}
 extern "C" void mk_prefill_set_scan_mode(int chunked) { mk::g_scan_mode = chunked ? 1 : 0; }
 
 namespace mk {
@@ -707,6 +713,8 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
     const int wpb = 8;                                            // warps per 256-thread block
     auto blocks_for_warps = [&](long long nw) { return (unsigned)((nw + wpb - 1) / wpb); };
 
+    const bool tail = g_tail.n > 0 && g_tail.running_max && S > g_tail.n;
+    if (tail) PF_CHECK(cudaMemsetAsync(g_tail.running_max, 0, (size_t)g_tail.n * S * sizeof(float), stream), "tail score reset");
     launch_pdl(k_embed, S, 128, 0, stream, token_ids, (const bf*)embed_weight, w.hidden, S, vocab);
     int dn_idx = 0, fa_idx = 0;
     for (int li = 0; li < num_layers; ++li) {
@@ -760,6 +768,7 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
             }
             launch_pdl(k_fa_norm_rope, blocks_for_warps((long long)S * 12), 256, 0, stream, w.wide, (const bf*)lv.q_norm, (const bf*)lv.k_norm, kc, vc, S, max_seq_len,
                        (const int*)nullptr, (size_t)0);
+            if (tail) PF_CHECK(tail_attention_scores(w.wide, kc, S, max_seq_len, g_tail.n, g_tail.running_max, stream), "tail scores");
             const uint32_t* bmask = nullptr;
             if (g_sparse.enabled) {
                 uint32_t* m = nullptr;

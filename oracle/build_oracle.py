@@ -7,6 +7,8 @@
                                    cut out of the checkout at build time into a generated translation unit under
                                    oracle/_ref/ (the file as a whole refuses to compile below sm_120) and compiled
                                    for sm_100a with the reference's own flags, --use_fast_math included.
+  oracle/_ref/libref_drafter_select.so steps 2-4 of the reference's prompt compressor (dflash/src/qwen3_drafter.cpp),
+                                   cut out at build time and wrapped in one C function (g++, host only).
   oracle/_ref/libref_megakernel.so the reference's own decode and prefill kernels (megakernel/kernel.cu,
                                    megakernel/prefill.cu), compiled for sm_100a from the sources where they lie
                                    in the reference checkout, with the flags of megakernel/setup.py and
@@ -115,10 +117,47 @@ def build_ref_quant(force=False):
     return REF_QUANT_LIB
 
 
+REF_DRAFTER_LIB = os.path.join(HERE, "_ref", "libref_drafter_select.so")
+
+
+def build_ref_drafter(force=False):
+    """Steps 2-4 of the reference's drafter_score_and_compress (dflash/src/qwen3_drafter.cpp: mean over the lookahead,
+    average-pool smoothing, chunk top-K, span merge) -- plain C++ on std::vector, cut out of the checkout at build time
+    between its own section comments into a generated translation unit under oracle/_ref/ and wrapped in one C
+    function.  (Step 1, the forward pass, needs ggml and another model.)  Returns the library path or None."""
+    src = os.path.join(REF_DIR, "dflash", "src", "qwen3_drafter.cpp")
+    if not os.path.exists(src):
+        return REF_DRAFTER_LIB if os.path.exists(REF_DRAFTER_LIB) else None
+    if not force and os.path.exists(REF_DRAFTER_LIB) and os.path.getmtime(src) <= os.path.getmtime(REF_DRAFTER_LIB) \
+            and os.path.getmtime(__file__) <= os.path.getmtime(REF_DRAFTER_LIB):
+        return REF_DRAFTER_LIB
+    os.makedirs(os.path.dirname(REF_DRAFTER_LIB), exist_ok=True)
+    text = open(src).read()
+    a = text.index("2. Mean over lookahead")
+    a = text.rindex("\n", 0, a) + 1
+    b = text.index("auto t2 = std::chrono", a)
+    body = text[a:b]
+    gen = os.path.join(HERE, "_ref", "ref_drafter_select_gen.cpp")
+    with open(gen, "w") as f:
+        f.write("// GENERATED at build time from the reference checkout (never committed): steps 2-4 of\n"
+                "// drafter_score_and_compress in dflash/src/qwen3_drafter.cpp, wrapped in one C function.\n"
+                "#include <algorithm>\n#include <cstdint>\n#include <utility>\n#include <vector>\n"
+                'extern "C" int ref_drafter_select(const float* rm, int n_lookahead, int S, float keep_ratio, int chunk_size,\n'
+                "                                  int pool_kernel, const int32_t* ids_in, int32_t* out_ids) {\n"
+                "    std::vector<float> running_max(rm, rm + (size_t)n_lookahead * S);\n"
+                "    std::vector<int32_t> ids(ids_in, ids_in + S);\n"
+                + body +
+                "    for (size_t i = 0; i < out.size(); ++i) out_ids[i] = out[i];\n"
+                "    return (int)out.size();\n}\n")
+    subprocess.check_call(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", gen, "-o", REF_DRAFTER_LIB])
+    return REF_DRAFTER_LIB
+
+
 def build_all(force=False):
     build_nvfp4(force)
     build_ref(force)
     build_ref_quant(force)
+    build_ref_drafter(force)
 
 
 if __name__ == "__main__":

@@ -226,6 +226,11 @@ class Oracle:
         # (qkv / z / out, q / k / v / o, gate / up / down; not beta / alpha, not the LM head): models a path that
         # multiplies quantised activations, e.g. NVFP4 x NVFP4 on the block-scaled tensor cores
         self.act_quant = act_quant
+        # tail_lookahead = n > 0: a prompt processed from position 0 also leaves tail_running_max [n, T], the maximum
+        # over attention layers and query heads of the causal softmax of the last n queries over every key
+        # (what the reference's prompt compressor scores with, dflash/src/qwen3_0p6b_graph.cpp:430-496)
+        self.tail_lookahead = 0
+        self.tail_running_max = None
         self.ref_q_rope_in_place = ref_q_rope_in_place
         # block_sparse = {"top_frac": .., "window": .., "sink": ..}: prompts processed from position 0 attend
         # only to the key blocks oracle/block_sparse.py selects (bf16-rounded q and k feed the selection)
@@ -315,6 +320,12 @@ class Oracle:
         L = pos0 + T
         K = st.k_cache[idx, :, :L].repeat_interleave(FA_Q_HEADS // FA_KV_HEADS, dim=0)   # [8, L, 256]
         V = st.v_cache[idx, :, :L].repeat_interleave(FA_Q_HEADS // FA_KV_HEADS, dim=0)
+        if self.tail_lookahead and pos0 == 0 and T > self.tail_lookahead:
+            n = self.tail_lookahead
+            s = torch.einsum("thd,hld->htl", _bf(q[T - n:]), K[:, :T]) / math.sqrt(FA_HEAD_DIM)       # [8, n, T]
+            causal = torch.arange(T)[None, :] <= torch.arange(T - n, T)[:, None]
+            pm = torch.softmax(s.masked_fill(~causal[None], float("-inf")), dim=-1).amax(dim=0)     # [n, T]
+            self.tail_running_max = pm if self.tail_running_max is None else torch.maximum(self.tail_running_max, pm)
         keep = None
         if self.block_sparse is not None and pos0 == 0 and T > 1:
             from . import block_sparse as BS
