@@ -674,7 +674,7 @@ def main():
             "per_rank_us_per_token": [r.seconds * 1e6 / r.tokens for r in per_rank],
             "e2e": {"value": world * GEN_LEN * e2e_steps / e2e_max, "unit": "tok/s",
                     "h2d_bytes_per_step": 4 * GEN_LEN, "d2h_bytes_per_step": 4 * GEN_LEN,
-                    "api": "Decoder.step(): one launch_decode call per token, host token in, host token out"},
+                    "api": "Decoder.step(): one mk_decode_step_host call per token (launch_decode + the token returned through mapped pinned memory), host token in, host token out"},
             "prefill": {"prompt_len": PROMPT_LEN, "ms": pp_max, "tok_s": world * PROMPT_LEN / (pp_max * 1e-3),
                         "tflops_algorithmic": PREFILL_TFLOP_PP520 / (pp_max * 1e-3),
                         "frac_of_bf16_peak": PREFILL_TFLOP_PP520 / (pp_max * 1e-3) / measured_bf16_peak(),

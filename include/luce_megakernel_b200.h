@@ -432,6 +432,23 @@ int mk_gemm_nvfp4_tn(const void *a_packed, const void *a_scales, const float *a_
                      cudaStream_t stream);
 int mk_gemm_nvfp4_status(void);
 
+/* launch_decode for a host loop that needs every token at once (the reference's Decoder.step(),
+ * megakernel/model.py:278-293, reads the token back with .item() after each launch): the kernel also writes the token
+ * and a ticket into mapped pinned memory and this call returns when the ticket has arrived, without a device-to-host
+ * copy or a stream synchronisation.  Arguments as launch_decode (minus the scratch the kernel never used);
+ * *next_token_out is host memory; output_token_id (device) is written as well. */
+int mk_decode_step_host(
+    int input_token_id, int *output_token_id, int *next_token_out,
+    const void *embed_weight, const MkLayerWeights *layer_weights,
+    const void *final_norm_weight, const void *lm_head_weight,
+    void *fa_k_cache, void *fa_v_cache, void *dn_states, void *conv_bufs,
+    void *hidden_buffer,
+    void *g_qkv_scratch, void *g_kv_scratch, void *g_attn_out,
+    void *g_mlp_inter, void *g_z_scratch, void *g_beta_scratch,
+    void *g_alpha_scratch, void *g_normalized,
+    float *seen_token_mask, float repetition_penalty,
+    int position, int max_seq_len, cudaStream_t stream);
+
 /* Model depth and vocabulary the entry points assume (defaults 24 and 248320, the
  * compile-time constants of the reference: megakernel/kernel.cu:20,22).  Reduced values let
  * the parity tests run the same kernels on a small model.  num_layers in [1,24]; the layer

@@ -13,8 +13,10 @@ constexpr int MAX_DEVICES = 64;
 
 struct DeviceState {
     mk::DecodeWorkspace* ws = nullptr;
-    uint32_t* host_status = nullptr;      // mapped pinned word the kernels write on failure
+    uint32_t* host_status = nullptr;      // mapped pinned block: word 0 = status the kernels write on failure,
+                                          // words 4, 5 = {token, ticket} of mk_decode_step_host
     uint32_t* host_status_dev = nullptr;  // its device alias
+    uint32_t ticket = 0;                  // last ticket handed to a launch
     int max_grid = 0;
 };
 
@@ -48,9 +50,9 @@ int device_state(DeviceState** out) {
         if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaMalloc(workspace)", e);
         e = cudaMemset(d.ws, 0, sizeof(mk::DecodeWorkspace));
         if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaMemset(workspace)", e);
-        e = cudaHostAlloc(&d.host_status, sizeof(uint32_t), cudaHostAllocMapped);
+        e = cudaHostAlloc(&d.host_status, 16 * sizeof(uint32_t), cudaHostAllocMapped);
         if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaHostAlloc(status)", e);
-        *d.host_status = 0;
+        memset(d.host_status, 0, 16 * sizeof(uint32_t));
         e = cudaHostGetDevicePointer(&d.host_status_dev, d.host_status, 0);
         if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "cudaHostGetDevicePointer", e);
         d.max_grid = mk::decode_max_grid();
@@ -159,6 +161,53 @@ int launch_decode(
     mk::fill_rope(p);
     cudaError_t e = mk::launch_decode_kernel(p, decode_grid(*d), stream);
     if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
+    return MK_OK;
+}
+
+// launch_decode for a host loop that needs the token at once: the kernel also writes the token and a ticket into
+// mapped pinned memory, and this call spins on the ticket instead of paying a device-to-host copy and a stream
+// synchronisation.  Same arguments as launch_decode; *next_token_out receives the token (host memory).
+int mk_decode_step_host(
+    int input_token_id, int* output_token_id, int* next_token_out,
+    const void* embed_weight, const MkLayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden_buffer,
+    void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch,
+    void* g_alpha_scratch, void* g_normalized,
+    float* seen_token_mask, float repetition_penalty,
+    int position, int max_seq_len, cudaStream_t stream) {
+    DecodeCall a{embed_weight, final_norm_weight, lm_head_weight, layer_weights,
+                 fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden_buffer,
+                 g_qkv_scratch, g_kv_scratch, g_attn_out, g_mlp_inter, g_z_scratch, g_beta_scratch, g_alpha_scratch,
+                 g_normalized, seen_token_mask, repetition_penalty, position, max_seq_len};
+    if (!output_token_id || !next_token_out) return set_err(MK_ERR_BAD_ARG, "null output pointer");
+    if (input_token_id < 0 || input_token_id >= g_vocab) return set_err(MK_ERR_BAD_ARG, "input_token_id out of range");
+    int rc = validate(a);
+    if (rc) return rc;
+    DeviceState* d = nullptr;
+    if ((rc = device_state(&d))) return rc;
+    if ((rc = check_device_status(*d, stream))) return rc;
+    mk::DecodeParams p = make_params(a, *d);
+    p.token_ptr = nullptr; p.token_val = input_token_id; p.out_token = output_token_id;
+    const uint32_t ticket = ++d->ticket ? d->ticket : ++d->ticket;      // never 0
+    p.host_token = reinterpret_cast<int*>(d->host_status_dev + 4);
+    p.host_ticket = ticket;
+    mk::fill_rope(p);
+    cudaError_t e = mk::launch_decode_kernel(p, decode_grid(*d), stream);
+    if (e != cudaSuccess) return set_err(MK_ERR_CUDA, "decode launch", e);
+    volatile uint32_t* hv = d->host_status;
+    unsigned n = 0;
+    while (hv[5] != ticket) {
+        if ((++n & 0xfffu) == 0) {          // every few thousand looks: has the stream finished or failed without a ticket?
+            e = cudaStreamQuery(stream);
+            if (e == cudaSuccess) { if (hv[5] == ticket) break; return set_err(MK_ERR_CUDA, "decode finished without publishing its token"); }
+            if (e != cudaErrorNotReady) return set_err(MK_ERR_CUDA, "decode step", e);
+        }
+    }
+    *next_token_out = (int)hv[4];
+    if (hv[0] != 0) return check_device_status(*d, stream);
     return MK_OK;
 }
 

@@ -2121,6 +2121,11 @@ __device__ __forceinline__ void phase_lm(const DecodeParams& P, Ctx& c) {
             if (*((volatile uint32_t*)&P.ws->abort_flag) != 0u) bi = -1;
             P.out_token[c.step] = bi;
             if (P.token_feedback) *P.token_feedback = bi;
+            if (P.host_token && c.step == P.steps - 1) {        // a host thread spins on the ticket (mk_decode_step_host)
+                *((volatile int*)P.host_token) = bi;
+                __threadfence_system();
+                *((volatile uint32_t*)P.host_token + 1) = P.host_ticket;
+            }
             // every CTA has finished this step: re-arm the workspace, then hand the token to the next step of this
             // launch (every CTA waits for this word before it touches the workspace again)
             P.ws->lm_count = 0u;

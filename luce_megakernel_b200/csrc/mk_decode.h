@@ -82,6 +82,8 @@ struct DecodeParams {
     int trace_slots;              // entries per CTA in `trace`
     unsigned long long poll_limit_cycles;   // SM clocks a poll of a flagged word may take before the CTA gives up
     uint32_t mbar_limit_tries;              // try_wait attempts on a ring barrier before the CTA gives up
+    int* host_token;              // optional mapped pinned {token, ticket}: the last step's token for a host that spins
+    uint32_t host_ticket;         // value written to host_token[1] after the token (system-scope fence in between)
     int lm_image_chunks;          // wfmt 3: 64-row chunk images per CTA in the LM-head image array
     int act_terms;                // wfmt 3: NVFP4 residual terms the activation vector is expanded into (1..8)
 };

@@ -145,6 +145,7 @@ class Decoder:
         self._lib = lib()
         self._ops = load_ops() if api == "ops" else None
         self.api = api
+        self._step_args = None          # ctypes argument tuple of step(), built on first use
         if weights is None:
             weights, tokenizer = load_weights(model_name, verbose=verbose)
         self.tokenizer = tokenizer
@@ -247,8 +248,28 @@ class Decoder:
 
     def step(self, token_id: int) -> int:
         """Decode one token.  Returns the next token id (synchronises with the device)."""
-        self.step_async(token_id)
-        return int(self._out_token.item())
+        if self.api != "cabi":
+            self.step_async(token_id)
+            return int(self._out_token.item())
+        # C ABI: mk_decode_step_host returns the token through mapped pinned memory (no device-to-host copy, no stream
+        # synchronisation); the pointer arguments of a session never change, so they are converted once
+        if self._position >= self.max_seq_len:
+            raise ValueError(f"position {self._position} exceeds max_seq_len={self.max_seq_len}")
+        if self._step_args is None:
+            self._step_host_tok = ctypes.c_int(0)
+            self._step_args = (
+                _ptr(self._out_token), ctypes.byref(self._step_host_tok), _ptr(self._embed_weight),
+                _ptr(self._layer_weights_packed), _ptr(self._final_norm_weight), _ptr(self._lm_head_weight),
+                _ptr(self._fa_k_cache), _ptr(self._fa_v_cache), _ptr(self._dn_states), _ptr(self._conv_bufs),
+                _ptr(self._hidden), _ptr(self._qkv_scratch), _ptr(self._kv_scratch), _ptr(self._attn_out),
+                _ptr(self._mlp_inter), _ptr(self._z_scratch), _ptr(self._beta_scratch), _ptr(self._alpha_scratch),
+                _ptr(self._normalized), _ptr(self._seen_token_mask))
+        self._bind_dims()
+        self._check(self._lib.mk_decode_step_host(
+            ctypes.c_int(int(token_id)), *self._step_args, ctypes.c_float(self.repetition_penalty),
+            ctypes.c_int(self._position), ctypes.c_int(self.max_seq_len), self._stream()))
+        self._position += 1
+        return int(self._step_host_tok.value)
 
     def step_sampled(self, token_id: int, temperature: float, top_k: int = 0, seed: int = 0) -> int:
         """One decode step whose next token is drawn from softmax(logits / temperature) over the top_k largest
