@@ -375,6 +375,8 @@ struct Ctx {
     uint32_t mma_n;       // row products issued so far: selects the accumulator buffer and the barrier phases
     uint32_t tmem;        // base address of the CTA's tensor-memory allocation
     float inv_g;          // 1 / normalisation factor of the staged activation
+    unsigned long long wf_cycles;   // traced variants: SM clocks this thread spent waiting for ring chunks to land
+    uint32_t wf_count;              // ... and how many waits did not find their chunk already there
 };
 
 // A bounded wait ran out (or another CTA reported one): from here on every wait of this CTA
@@ -398,7 +400,14 @@ __device__ __forceinline__ void trace_point(const DecodeParams& P, Ctx& c) {
 __device__ __forceinline__ void wait_full(const DecodeParams& P, Ctx& c, uint32_t stage, uint32_t parity) {
     if (mbar_try_wait(c.full0 + stage * 8, parity)) return;
     if (c.misc[MISC_ABORT]) return;
+#if MK_TRACE
+    const long long t0 = clock64();
+#endif
     if (!mbar_wait(c.full0 + stage * 8, parity, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
+#if MK_TRACE
+    c.wf_cycles += (unsigned long long)(clock64() - t0);
+    c.wf_count++;
+#endif
 }
 
 __device__ __forceinline__ void release_stage(Ctx& c, uint32_t stage) {
@@ -715,6 +724,40 @@ __device__ __forceinline__ void mma_chunk(const char* stage, int K, int warp, in
     if (t == 0) {
         out[g] = s0;
         if (ROWS == 16) out[g + 8] = s1;
+    }
+}
+
+// Two 4-row chunks (the down projection) as ONE 8-row tile: lane groups 0-3 read the rows of the first chunk, 4-7 the
+// rows of the second, so the pair costs the MMAs of one chunk instead of two half-empty tiles one after the other.
+template <int NLOAD>
+__device__ __forceinline__ void mma_chunk_pair4(const char* stage0, const char* stage1, int K, int warp, int lane,
+                                                const uint32_t (&b)[2 * NLOAD][2], float* out0, float* out1) {
+    const int g = lane >> 2, t = lane & 3, odd = g & 1;
+    const int rowbytes = row_stride(K), kofs = warp * NLOAD * 64;
+    const char* r0 = (g < 4 ? stage0 + g * rowbytes : stage1 + (g - 4) * rowbytes) + kofs + 16 * t;
+    uint4 A0[NLOAD];
+#pragma unroll
+    for (int s = 0; s < NLOAD; ++s) {
+        int i = s + odd;
+        if (i >= NLOAD) i -= NLOAD;
+        A0[s] = *reinterpret_cast<const uint4*>(r0 + 64 * i);
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < NLOAD; ++i) {
+        constexpr int N = NLOAD;
+        const int so = (i + N - 1) % N;
+        uint4 a;
+        a.x = odd ? A0[so].x : A0[i].x; a.y = odd ? A0[so].y : A0[i].y;
+        a.z = odd ? A0[so].z : A0[i].z; a.w = odd ? A0[so].w : A0[i].w;
+        mma_16816(acc, a.x, 0u, a.y, 0u, b[2 * i][0], b[2 * i][1]);
+        mma_16816(acc2, a.z, 0u, a.w, 0u, b[2 * i + 1][0], b[2 * i + 1][1]);
+    }
+    float s0 = (acc[0] + acc2[0]) + (t == 0 ? acc[1] + acc2[1] : 0.f);
+    s0 += __shfl_down_sync(0xffffffffu, s0, 1);
+    if (t == 0) {
+        if (g < 4) out0[g] = s0;
+        else out1[g - 4] = s0;
     }
 }
 
@@ -1178,15 +1221,35 @@ __device__ __forceinline__ void mma_phase(const DecodeParams& P, Ctx& c, int nch
     uint32_t b[2 * NLOAD][2];
     load_bfrags<NLOAD>(reinterpret_cast<const uint32_t*>(c.xs) + c.warp * XSW, c.lane, b);
     if (nchunks > 4) { fail(P, c, ST_MISALIGNED); nchunks = 4; }   // never reached for grids >= MIN_GRID
-    if (nchunks > 0) wait_full(P, c, c.it % NSTAGE, (c.it / NSTAGE) & 1u);
+    // Chunks two at a time: the weights are in the ring long before the activation is (the waits below practically
+    // never block), so what a chunk costs is its own dependent chain load -> MMA -> shuffle -> store; two independent
+    // chains in flight per warp hide most of one of them.
+    int q = 0;
+    // (all four chunks of an input projection in one go measured no better than two pairs)
 #pragma unroll 1
-    for (int q = 0; q < nchunks; ++q, ++c.it) {
+    for (; q + 2 <= nchunks; q += 2, c.it += 2) {
+        const uint32_t s0 = c.it % NSTAGE, s1 = (c.it + 1) % NSTAGE;
+        wait_full(P, c, s0, (c.it / NSTAGE) & 1u);
+        wait_full(P, c, s1, ((c.it + 1) / NSTAGE) & 1u);
+#if MK_WFMT == 0
+        if (ROWS == 4) {
+            mma_chunk_pair4<NLOAD>(c.smem + OFF_RING + s0 * STAGE_BYTES, c.smem + OFF_RING + s1 * STAGE_BYTES, K, c.warp, c.lane, b,
+                                   c.part + (q * NCW + c.warp) * 16, c.part + ((q + 1) * NCW + c.warp) * 16);
+        } else
+#endif
+        {
+            mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + s0 * STAGE_BYTES, K, c.warp, c.lane, b, c.part + (q * NCW + c.warp) * 16);
+            mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + s1 * STAGE_BYTES, K, c.warp, c.lane, b, c.part + ((q + 1) * NCW + c.warp) * 16);
+        }
+        release_stage(c, s0);
+        release_stage(c, s1);
+    }
+    if (q < nchunks) {
         const uint32_t stage = c.it % NSTAGE;
-        mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + stage * STAGE_BYTES, K, c.warp, c.lane, b,
-                               c.part + (q * NCW + c.warp) * 16);
+        wait_full(P, c, stage, (c.it / NSTAGE) & 1u);
+        mma_chunk<NLOAD, ROWS>(c.smem + OFF_RING + stage * STAGE_BYTES, K, c.warp, c.lane, b, c.part + (q * NCW + c.warp) * 16);
         release_stage(c, stage);
-        // the mbarrier test of the next chunk overlaps the tail of this chunk's MMAs
-        if (q + 1 < nchunks) wait_full(P, c, (c.it + 1) % NSTAGE, ((c.it + 1) / NSTAGE) & 1u);
+        ++c.it;
     }
 }
 
@@ -2181,6 +2244,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_megakernel_bf16(const __grid_c
     c.it = 0; c.trace_slot = 0;
     c.seq = __ldcg(&P.ws->seq);
     c.pos = P.position; c.step = 0; c.where = 0;
+    c.wf_cycles = 0; c.wf_count = 0;
     float* s_rope = reinterpret_cast<float*>(smem + OFF_ROPE);
     c.rope = s_rope;
 
@@ -2335,6 +2399,13 @@ __global__ void __launch_bounds__(NTHR, 1) decode_megakernel_bf16(const __grid_c
     if (c.warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(c.tmem), "r"(U_TM_COLS) : "memory");
+    }
+#endif
+#if MK_TRACE
+    // last two trace slots of the CTA: thread 0's wait for ring chunks (SM clocks, number of waits that had to wait)
+    if (P.trace && threadIdx.x == 0 && P.trace_slots >= 2) {
+        P.trace[(size_t)c.cta * P.trace_slots + P.trace_slots - 2] = c.wf_cycles;
+        P.trace[(size_t)c.cta * P.trace_slots + P.trace_slots - 1] = c.wf_count;
     }
 #endif
     if (c.misc[MISC_ABORT]) {
