@@ -162,7 +162,47 @@ void fill_rope(DecodeParams& p) {
     for (int i = 0; i < FA_ROT / 2; ++i) p.rope_inv_freq[i] = (float)(1.0 / pow(ROPE_THETA, (2.0 * i) / FA_ROT));
 }
 
-cudaError_t launch_decode_kernel(const DecodeParams& p, int grid, cudaStream_t stream) {
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                  const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// [rows][256] bf16 cache, boxes of 64 elements x 32 rows, 128-byte swizzle; rows past the end read as zeros
+bool make_kv_map(CUtensorMap* map, const void* base, unsigned long long rows) {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* q = nullptr;
+        cudaDriverEntryPointQueryResult r;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) != cudaSuccess || !q) return false;
+        fn = (EncodeTiledFn)q;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)FA_HEAD_DIM, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)FA_HEAD_DIM * 2};
+    cuuint32_t box[2] = {64, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct KvMapCache { const void* k = nullptr; const void* v = nullptr; unsigned long long rows = 0; CUtensorMap mk, mv; };
+thread_local KvMapCache g_kvmaps;
+
+}  // namespace
+
+cudaError_t launch_decode_kernel(const DecodeParams& p_in, int grid, cudaStream_t stream) {
+    DecodeParams p = p_in;
+    // every attention layer owns 2 * max_seq rows of each cache; n_fa_layers == 0 means the reference model's pattern
+    // (every fourth layer)
+    const int n_fa = p.n_fa_layers > 0 ? p.n_fa_layers : (p.num_layers / 4 > 0 ? p.num_layers / 4 : 1);
+    const unsigned long long rows = (unsigned long long)n_fa * FA_KV_HEADS * (unsigned long long)p.max_seq_len;
+    KvMapCache& kc = g_kvmaps;
+    if (kc.k != p.k_cache || kc.v != p.v_cache || kc.rows != rows) {
+        if (!make_kv_map(&kc.mk, p.k_cache, rows) || !make_kv_map(&kc.mv, p.v_cache, rows)) return cudaErrorInvalidValue;
+        kc.k = p.k_cache; kc.v = p.v_cache; kc.rows = rows;
+    }
+    p.map_k = kc.mk; p.map_v = kc.mv;
     static bool attr_done[64] = {false};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

@@ -113,9 +113,15 @@ __device__ __forceinline__ void split_rows(int n, int G, int c, int& a, int& b) 
 }
 
 // attention units: (KV head, chunk of positions); a unit's K and V rows travel through the ring in tiles of
-// 64 positions, four ring chunks per tile: K rows 0-31, K rows 32-63, V rows 0-31, V rows 32-63, each row
-// at a stride of ATT_ROW_STRIDE bytes so that the 8 rows an ldmatrix reads fall in different banks
-constexpr int ATT_ROW_STRIDE = FA_HEAD_DIM * 2 + 16;
+// 64 positions, four ring chunks per tile: K rows 0-31, K rows 32-63, V rows 0-31, V rows 32-63
+constexpr int ATT_ROW_STRIDE = FA_HEAD_DIM * 2 + 16;      // (row stride of the query / probability scratch tiles)
+// A K or V chunk in a ring stage: 32 positions x 256 dims as four boxes of 64 dims (32 rows x 128 bytes = 4 KB each,
+// 128-byte swizzle), the layout cp.async.bulk.tensor writes: 16-byte piece c of row r of a box sits at piece c ^ (r & 7).
+// Four tensor copies per chunk instead of one bulk copy per row: a CTA issues a copy only every ~0.1 us, and 128 row
+// copies per tile made the tile arrive ~3 us after the attention phase had started.
+__device__ __forceinline__ uint32_t att_tile_off(int rr, int bytecol) {
+    return (uint32_t)(((bytecol >> 7) << 12) + rr * 128 + ((((bytecol >> 4) & 7) ^ (rr & 7)) << 4));
+}
 __device__ __forceinline__ int att_num_chunks(int L) {
     int nc = (L + ATT_CHUNK_POS - 1) / ATT_CHUNK_POS;
     return nc < 1 ? 1 : (nc > ATT_MAX_CHUNKS ? ATT_MAX_CHUNKS : nc);
@@ -172,18 +178,7 @@ __device__ __forceinline__ Geo phase_geo(int type, int cta, int G, int vocab, in
 __device__ __forceinline__ uint32_t chunk_slot_src(int type, const LW& lw, const DecodeParams& P,
                                                    const Geo& g, int q, int lane, int G, int dn_idx,
                                                    const char*& src, uint32_t& dst_off, int cta_of_geo, int pos) {
-    if (type == T_FA_ATT) {
-        // dn_idx carries the attention layer index here; chunk q = tile * 4 + {K lo, K hi, V lo, V hi}
-        const int u = cta_of_geo;
-        const int NC = att_num_chunks(pos + 1);
-        const int kvh = u / NC, part = q & 3;
-        const int p = g.r0 + (q >> 2) * 64 + (part & 1) * 32 + lane;
-        if (p >= g.r1) return 0;
-        const char* base = (const char*)((part & 2) ? P.v_cache : P.k_cache);
-        src = base + ((size_t)(dn_idx * FA_KV_HEADS + kvh) * P.max_seq_len + p) * (FA_HEAD_DIM * 2);
-        dst_off = lane * ATT_ROW_STRIDE;
-        return FA_HEAD_DIM * 2;
-    }
+    if (type == T_FA_ATT) return 0;      // attention tiles travel as tensor copies (producer_phase)
 #if MK_WFMT >= 2
     if (type == T_DN_REC) {
         if (lane != 0) return 0;
@@ -377,6 +372,8 @@ struct Ctx {
     float inv_g;          // 1 / normalisation factor of the staged activation
     unsigned long long wf_cycles;   // traced variants: SM clocks this thread spent waiting for ring chunks to land
     uint32_t wf_count;              // ... and how many waits did not find their chunk already there
+    uint32_t wf_calls;              // ... out of how many
+    uint32_t dirty_stages;          // producer warp: ring stages whose last occupant the consumers wrote into
 };
 
 // A bounded wait ran out (or another CTA reported one): from here on every wait of this CTA
@@ -398,15 +395,18 @@ __device__ __forceinline__ void trace_point(const DecodeParams& P, Ctx& c) {
 }
 
 __device__ __forceinline__ void wait_full(const DecodeParams& P, Ctx& c, uint32_t stage, uint32_t parity) {
+#if MK_TRACE
+    // mbarrier.try_wait may itself suspend the thread for a while before it answers: time the whole call
+    const long long t0 = clock64();
+    c.wf_calls++;
+    bool done = mbar_try_wait(c.full0 + stage * 8, parity);
+    if (!done && !c.misc[MISC_ABORT] && !mbar_wait(c.full0 + stage * 8, parity, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
+    const unsigned long long dt = (unsigned long long)(clock64() - t0);
+    if (dt > 400ull) { c.wf_cycles += dt; c.wf_count++; }      // more than ~0.2 us: the chunk was not there yet
+#else
     if (mbar_try_wait(c.full0 + stage * 8, parity)) return;
     if (c.misc[MISC_ABORT]) return;
-#if MK_TRACE
-    const long long t0 = clock64();
-#endif
     if (!mbar_wait(c.full0 + stage * 8, parity, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
-#if MK_TRACE
-    c.wf_cycles += (unsigned long long)(clock64() - t0);
-    c.wf_count++;
 #endif
 }
 
@@ -571,6 +571,32 @@ __device__ __forceinline__ void producer_phase(const DecodeParams& P, Ctx& c, in
         const uint32_t stage = c.it % NSTAGE, parity = (c.it / NSTAGE) & 1u;
         if (c.lane == 0 && !mbar_wait(c.empty0 + stage * 8, parity ^ 1u, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
         __syncwarp();
+        // The attention phase patches and pads its K/V tile in place, with ordinary stores into the ring stage.  Those
+        // stores were released through the stage's "empty" barrier, acquired just above; the proxy fence orders them
+        // before the bulk copies that now overwrite the stage (async proxy).  It sits here, in the warp that runs
+        // ahead, because on the consumers' side it cost 1.8 us per attention layer on the critical path.
+        if (c.dirty_stages & (1u << stage)) { fence_proxy_async(); c.dirty_stages &= ~(1u << stage); }
+        if (type == T_FA_ATT) {
+            // chunk q = tile * 4 + {K lo, K hi, V lo, V hi} of this CTA's unit (dn_idx carries the attention layer index):
+            // 32 positions from p0 as four 64-dim boxes, lanes 0-3; rows past the unit's last position come along and are
+            // masked by the consumers; a chunk that starts past it completes with nothing
+            c.dirty_stages |= 1u << stage;
+            if (c.misc[MISC_ABORT]) continue;
+            const int kvh = c.cta / att_num_chunks(c.pos + 1), part = q & 3;
+            const int p0 = g.r0 + (q >> 2) * 64 + (part & 1) * 32;
+            const bool any = p0 < g.r1;
+            if (c.lane == 0) mbar_expect_tx(c.full0 + stage * 8, any ? 32u * FA_HEAD_DIM * 2u : 0u);
+            __syncwarp();
+            if (any && c.lane < 4) {
+                const CUtensorMap* map = (part & 2) ? &P.map_v : &P.map_k;
+                const int row = (dn_idx * FA_KV_HEADS + kvh) * P.max_seq_len + p0;
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+                    ::"r"(c.ring0 + stage * STAGE_BYTES + c.lane * 4096), "l"(map), "r"(64 * c.lane), "r"(row), "r"(c.full0 + stage * 8)
+                    : "memory");
+            }
+            continue;
+        }
         const char* src = nullptr;
         uint32_t dst_off = 0, run_bytes = 0;
         bool head = false;
@@ -1651,6 +1677,21 @@ __device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, cons
         int g, ch, p_lo, p_hi;
         att_unit_range(L, u, g, ch, p_lo, p_hi);
         const bool owner = (pos >= p_lo && pos < p_hi);
+        // The first K/V tile does not depend on this step's projections (the producer fetched it from the caches long
+        // ago): take it over and pad it while the query is still on its way.
+        {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) wait_full(P, c, (c.it + k) % NSTAGE, ((c.it + k) / NSTAGE) & 1u);
+            const int nvalid0 = min(64, p_hi - p_lo);
+            if (nvalid0 < 64 && c.warp >= 6) {
+                for (int r = nvalid0 + (c.warp - 6); r < 64; r += NCW - 6) {
+                    char* dst = c.smem + OFF_RING + ((c.it + 2 + (r >> 5)) % NSTAGE) * STAGE_BYTES + att_tile_off(r & 31, 16 * c.lane);
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+                }
+            }
+        }
+        const int r_own = pos - p_lo;                 // row of the current position, if it lies in the first tile
+        const bool patch0 = owner && r_own < 64;
         if (c.warp < 4) {
             float n[8];
             head_norm_rope(P, c, P.ws->x_fain + (g * FA_GQA + c.warp) * 2 * FA_HEAD_DIM, ep, lw.ptrs[FA_Q_NORM], pos, n);
@@ -1666,10 +1707,15 @@ __device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, cons
             head_norm_rope(P, c, P.ws->x_fain + FA_QPROJ + g * FA_HEAD_DIM, ep, lw.ptrs[FA_K_NORM], pos, n);
             __nv_bfloat16* Kb = reinterpret_cast<__nv_bfloat16*>(P.k_cache) + ((size_t)(fa_idx * FA_KV_HEADS + g) * P.max_seq_len + pos) * FA_HEAD_DIM;
 #pragma unroll
+            char* tile = c.smem + OFF_RING + ((c.it + (r_own >> 5)) % NSTAGE) * STAGE_BYTES;
+#pragma unroll
             for (int e = 0; e < 8; ++e) {
                 const __nv_bfloat16 v = __float2bfloat16_rn(n[e]);
-                Kb[c.lane + 32 * e] = v;
-                krow[c.lane + 32 * e] = v;
+                const int d = c.lane + 32 * e;
+                Kb[d] = v;
+                krow[d] = v;
+                // straight into the tile (the producer fences before it refills the stage)
+                if (patch0) *reinterpret_cast<__nv_bfloat16*>(tile + att_tile_off(r_own & 31, 2 * d) + ((2 * d) & 15)) = v;
             }
         } else if (c.warp == 5 && owner) {
             const unsigned long long* b0 = P.ws->x_fain + FA_QPROJ + FA_KV_SIZE + g * FA_HEAD_DIM + c.lane;
@@ -1678,10 +1724,14 @@ __device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, cons
             poll1_batch<8>(P, c, p1, ep, v);
             __nv_bfloat16* Vb = reinterpret_cast<__nv_bfloat16*>(P.v_cache) + ((size_t)(fa_idx * FA_KV_HEADS + g) * P.max_seq_len + pos) * FA_HEAD_DIM;
 #pragma unroll
+            char* tile = c.smem + OFF_RING + ((c.it + 2 + (r_own >> 5)) % NSTAGE) * STAGE_BYTES;
+#pragma unroll
             for (int e = 0; e < 8; ++e) {
                 const __nv_bfloat16 b = __float2bfloat16_rn(v[e]);
-                Vb[c.lane + 32 * e] = b;
-                vrow[c.lane + 32 * e] = b;
+                const int d = c.lane + 32 * e;
+                Vb[d] = b;
+                vrow[d] = b;
+                if (patch0) *reinterpret_cast<__nv_bfloat16*>(tile + att_tile_off(r_own & 31, 2 * d) + ((2 * d) & 15)) = b;
             }
         }
         named_bar_sync(1, NCT);
@@ -1704,34 +1754,33 @@ __device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, cons
                 stg[k] = smem_u32(c.smem + OFF_RING + (itk % NSTAGE) * STAGE_BYTES);
             }
             const int tbase = p_lo + tile * 64, nvalid = min(64, p_hi - tbase);
-            // patch the row of the current position, zero the value rows past the end of the chunk
-            if (owner && pos >= tbase && pos < tbase + 64 && c.warp >= 4 && c.warp < 6) {
+            // patch the row of the current position, zero the value rows past the end of the chunk (first tile: done above)
+            if (tile > 0 && owner && pos >= tbase && pos < tbase + 64 && c.warp >= 4 && c.warp < 6) {
                 const int r = pos - tbase;
-                char* dst = c.smem + OFF_RING + ((c.it + (c.warp == 4 ? 0 : 2) + (r >> 5)) % NSTAGE) * STAGE_BYTES + (r & 31) * ATT_ROW_STRIDE;
+                char* dst = c.smem + OFF_RING + ((c.it + (c.warp == 4 ? 0 : 2) + (r >> 5)) % NSTAGE) * STAGE_BYTES + att_tile_off(r & 31, 16 * c.lane);
                 const uint4* srcv = reinterpret_cast<const uint4*>(c.warp == 4 ? krow : vrow);
-                reinterpret_cast<uint4*>(dst)[c.lane] = srcv[c.lane];
-                fence_proxy_async();      // the stage is refilled by bulk copies later
+                *reinterpret_cast<uint4*>(dst) = srcv[c.lane];      // (the producer fences before it refills this stage)
             }
-            if (nvalid < 64 && c.warp >= 6) {
+            if (tile > 0 && nvalid < 64 && c.warp >= 6) {
                 for (int r = nvalid + (c.warp - 6); r < 64; r += NCW - 6) {
-                    char* dst = c.smem + OFF_RING + ((c.it + 2 + (r >> 5)) % NSTAGE) * STAGE_BYTES + (r & 31) * ATT_ROW_STRIDE;
-                    reinterpret_cast<uint4*>(dst)[c.lane] = make_uint4(0, 0, 0, 0);
+                    char* dst = c.smem + OFF_RING + ((c.it + 2 + (r >> 5)) % NSTAGE) * STAGE_BYTES + att_tile_off(r & 31, 16 * c.lane);
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
                 }
-                fence_proxy_async();
             }
-            named_bar_sync(1, NCT);
+            if (tile > 0) named_bar_sync(1, NCT);
             if (tile == 0) trace_point(P, c);      // first K/V tile landed and patched
             float sc[2][2];
             if (c.warp < 4) {
                 // scores of keys [16 warp, 16 warp + 16): rows = (head, part)
                 float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
                 const int brow = (c.lane & 7) + (c.lane >> 4) * 8, bcol = ((c.lane >> 3) & 1) * 16;
-                const uint32_t kb = stg[c.warp >> 1] + ((c.warp & 1) * 16 + brow) * ATT_ROW_STRIDE + bcol;
+                const uint32_t kb = stg[c.warp >> 1];
+                const int krow_i = (c.warp & 1) * 16 + brow;
                 const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qt + g8 * QROW) + t4;
 #pragma unroll
                 for (int ks = 0; ks < 16; ++ks) {
                     uint32_t b0, b1, b2, b3;
-                    att_ldsm4(kb + ks * 32, b0, b1, b2, b3);
+                    att_ldsm4(kb + att_tile_off(krow_i, bcol + ks * 32), b0, b1, b2, b3);
                     const uint32_t a0 = qrow[ks * 8], a2 = qrow[ks * 8 + 4];
                     att_mma(acc[0], a0, a2, b0, b1);
                     att_mma(acc[1], a0, a2, b2, b3);
@@ -1781,7 +1830,7 @@ __device__ __forceinline__ void phase_fa_att(const DecodeParams& P, Ctx& c, cons
 #pragma unroll
                     for (int np = 0; np < 2; ++np) {
                         uint32_t b0, b1, b2, b3;
-                        att_ldsm4t(stg[2 + (ks >> 1)] + ((ks & 1) * 16 + trow) * ATT_ROW_STRIDE + (c.warp * 32 + np * 16) * 2 + tcol, b0, b1, b2, b3);
+                        att_ldsm4t(stg[2 + (ks >> 1)] + att_tile_off((ks & 1) * 16 + trow, (c.warp * 32 + np * 16) * 2 + tcol), b0, b1, b2, b3);
                         att_mma(oacc[2 * np], a0, a2, b0, b1);
                         att_mma(oacc[2 * np + 1], a0, a2, b2, b3);
                     }
@@ -2244,7 +2293,7 @@ __global__ void __launch_bounds__(NTHR, 1) decode_megakernel_bf16(const __grid_c
     c.it = 0; c.trace_slot = 0;
     c.seq = __ldcg(&P.ws->seq);
     c.pos = P.position; c.step = 0; c.where = 0;
-    c.wf_cycles = 0; c.wf_count = 0;
+    c.wf_cycles = 0; c.wf_count = 0; c.wf_calls = 0; c.dirty_stages = 0;
     float* s_rope = reinterpret_cast<float*>(smem + OFF_ROPE);
     c.rope = s_rope;
 
@@ -2402,8 +2451,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_megakernel_bf16(const __grid_c
     }
 #endif
 #if MK_TRACE
-    // last two trace slots of the CTA: thread 0's wait for ring chunks (SM clocks, number of waits that had to wait)
-    if (P.trace && threadIdx.x == 0 && P.trace_slots >= 2) {
+    // last three trace slots of the CTA: thread 0's waits for ring chunks (calls, SM clocks blocked, calls that blocked)
+    if (P.trace && threadIdx.x == 0 && P.trace_slots >= 3) {
+        P.trace[(size_t)c.cta * P.trace_slots + P.trace_slots - 3] = c.wf_calls;
         P.trace[(size_t)c.cta * P.trace_slots + P.trace_slots - 2] = c.wf_cycles;
         P.trace[(size_t)c.cta * P.trace_slots + P.trace_slots - 1] = c.wf_count;
     }

@@ -1,6 +1,7 @@
 // Host-visible parameter block and launcher declarations for the bf16 decode megakernel.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -41,6 +42,11 @@ struct DecodeWorkspace {
 };
 
 struct DecodeParams {
+    // Tensor maps over the K and the V cache, seen as [n_fa * 2 * max_seq rows][256] bf16: a K/V tile of the attention
+    // phase travels as 64-element x 32-row boxes with the 128-byte swizzle (four per ring chunk) instead of one bulk
+    // copy per row.  Filled by launch_decode_kernel.
+    alignas(64) CUtensorMap map_k;
+    alignas(64) CUtensorMap map_v;
     const void* embed;            // bf16 [vocab, 1024]
     const void* layers;           // device pointer table: LayerWeights[] (bf16) or LayerWeightsNVFP4[] (wfmt 1)
     const void* final_norm;       // bf16 [1024]
@@ -75,6 +81,7 @@ struct DecodeParams {
     float rope_inv_freq[32];      // theta^(-2i/64), filled by fill_rope(); the angles are formed on the device
     int max_seq_len;
     int num_layers;
+    int n_fa_layers;              // attention layers the caches hold (0 = num_layers / 4, the reference model's pattern)
     int vocab;
     DecodeWorkspace* ws;
     uint32_t* host_status;        // mapped pinned word, written only on failure
