@@ -56,7 +56,8 @@ constexpr int OFF_MISC = OFF_RED + 128;                    // 8 ints
 constexpr int OFF_BAR = OFF_MISC + 32;                     // full[stages], empty[stages]
 constexpr int OFF_ROPE = OFF_BAR + 2 * MAX_STAGES * 8;         // cos[32] | sin[32] of the step's position
 constexpr int OFF_LAYERS = OFF_ROPE + 256;                 // copy of the layer pointer table
-constexpr int SMEM_BYTES = OFF_LAYERS + MAX_LAYERS * (int)sizeof(LayerWeightsNVFP4TS);
+constexpr int OFF_DBG = OFF_LAYERS + MAX_LAYERS * (int)sizeof(LayerWeightsNVFP4TS);   // traced variants: 16 counters
+constexpr int SMEM_BYTES = OFF_DBG + 64;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 enum { MISC_ABORT = 0, MISC_LAST = 1, MISC_TOKEN = 2, MISC_DETAIL = 3 };

@@ -402,7 +402,10 @@ __device__ __forceinline__ void wait_full(const DecodeParams& P, Ctx& c, uint32_
     bool done = mbar_try_wait(c.full0 + stage * 8, parity);
     if (!done && !c.misc[MISC_ABORT] && !mbar_wait(c.full0 + stage * 8, parity, P.mbar_limit_tries)) fail(P, c, ST_MBAR_TIMEOUT);
     const unsigned long long dt = (unsigned long long)(clock64() - t0);
-    if (dt > 400ull) { c.wf_cycles += dt; c.wf_count++; }      // more than ~0.2 us: the chunk was not there yet
+    if (dt > 400ull) {                                         // more than ~0.2 us: the chunk was not there yet
+        c.wf_cycles += dt; c.wf_count++;
+        if (c.tid == 0) reinterpret_cast<volatile int*>(c.smem + OFF_DBG)[c.where & 15u] += (int)dt;    // ... by phase type (thread 0 only)
+    }
 #else
     if (mbar_try_wait(c.full0 + stage * 8, parity)) return;
     if (c.misc[MISC_ABORT]) return;
@@ -2309,6 +2312,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_megakernel_bf16(const __grid_c
         c.misc[MISC_ABORT] = 0;
         c.misc[MISC_LAST] = 0;
         c.misc[MISC_DETAIL] = 0;
+#if MK_TRACE
+        for (int k = 0; k < 16; ++k) reinterpret_cast<volatile int*>(smem + OFF_DBG)[k] = 0;
+#endif
 #if MK_WFMT == 3
         const uint32_t ubar = smem_u32(smem + U_OFF_BARS);
         mbar_init(ubar, 1); mbar_init(ubar + 8, 1);             // product done (tcgen05.commit)
@@ -2454,6 +2460,9 @@ __global__ void __launch_bounds__(NTHR, 1) decode_megakernel_bf16(const __grid_c
     // last three trace slots of the CTA: thread 0's waits for ring chunks (calls, SM clocks blocked, calls that blocked)
     if (P.trace && threadIdx.x == 0 && P.trace_slots >= 3) {
         P.trace[(size_t)c.cta * P.trace_slots + P.trace_slots - 3] = c.wf_calls;
+        if (P.trace_slots >= 32)
+            for (int k = 0; k < 16; ++k)
+                P.trace[(size_t)c.cta * P.trace_slots + P.trace_slots - 32 + k] = (unsigned long long)reinterpret_cast<volatile int*>(c.smem + OFF_DBG)[k];
         P.trace[(size_t)c.cta * P.trace_slots + P.trace_slots - 2] = c.wf_cycles;
         P.trace[(size_t)c.cta * P.trace_slots + P.trace_slots - 1] = c.wf_count;
     }
