@@ -32,8 +32,8 @@ NVFP4_BYTES_PER_TOKEN = 466_073_216         # the same with every linear layer a
 KV_BYTES_PER_POS = 12_288                   # K and V rows read per cached position, 6 layers
 STATE_BYTES_PER_SEQ = 41_287_680            # DeltaNet state and conv window, read + written once per token
 # dram__bytes_read.sum + dram__bytes_write.sum of one bf16 decode step: ncu capture of a 4-step launch at context 520
-# (6.0440 GB read + 11.9 MB written), divided by 4
-TRAFFIC_BYTES_PER_LAUNCH = 1_513_976_000
+# (6.0436 GB read + 7.2 MB written), divided by 4
+TRAFFIC_BYTES_PER_LAUNCH = 1_512_704_000
 
 
 def algorithmic_bytes_per_token(context_len: float, nvfp4: bool = False) -> float:
