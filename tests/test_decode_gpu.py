@@ -196,6 +196,33 @@ def test_long_context_attention_chunks(dec_small, small_model):
             assert accept_token(int(dec_small._out_token.item()), trs.logits)
 
 
+def test_context_beyond_1024_units_of_two_tiles(small_model):
+    """Past 1024 positions an attention unit (KV head, 1/16 of the context) covers more than one 64-position K/V tile:
+    positions 1100-1107 give units of 69-70 positions, i.e. a full tile plus a tail of 5-6 rows, with the current
+    position's row patched into the SECOND tile of the last unit.  The prompt goes through the decode kernel itself in
+    one multi-step launch (its outputs are ignored: teacher forcing comes from the prompt), so the caches it reads at
+    the checked positions are the ones it wrote; the oracle runs the prompt in one pass."""
+    from luce_megakernel_b200 import model as M
+    sd, orc = small_model("unit", "decode")
+    dec = M.Decoder(weights=M.weights_from_state_dict(sd), max_seq_len=2048, api="cabi")
+    toks = seeded_prompt(1108, seed=12)
+    dec.reset()
+    for t in toks[:1100]:
+        dec.step_async(t)
+    st = O.State.new(NL, 2048, V)
+    orc.forward(toks[:1100], st, want_logits=False)
+    for i in range(1100, 1108):
+        dec.step_async(toks[i])
+        trs = orc.forward([toks[i]], st)
+        ref_h = trs.hidden[-1][0]
+        eh = float((dec._hidden.float().cpu() - ref_h).abs().max())
+        assert eh <= 2 * hidden_tol(ref_h), f"pos {i}: hidden error {eh}"
+        assert accept_token(int(dec._out_token.item()), trs.logits)
+    L = 1108
+    kerr = float((dec._fa_k_cache.float().cpu()[:, :, :L] - st.k_cache[:, :, :L]).abs().max())
+    assert kerr <= 0.26, kerr
+
+
 def test_ops_surface_matches_cabi(dec_small, small_model):
     from luce_megakernel_b200 import model as M
     sd, _ = small_model("unit", "decode")
