@@ -380,6 +380,16 @@ int mk_prefill_set_block_sparse(int enable, double top_frac, int window, int sin
 int mk_block_select(const void *qkv, const void *k_cache, int seq_len, int max_seq_len, double top_frac, int window,
                     int sink, unsigned int *mask_out, void *scratch, cudaStream_t stream);
 size_t mk_block_select_scratch_bytes(int seq_len);
+/* The same scores under the reference's own keep rule (dflash/src/flashprefill_select.cpp:27-84, block_select_host):
+ * per query head and query block m the kept causal key blocks n <= m are n < sink, m - n < window, every block when
+ * m >= blocks - last_n_full, and score(m, n) >= alpha * max over n <= m of score(m, n) (one f32 multiply, compared
+ * with >=).  scores_out (optional, device): f32 [8][blocks][blocks], entries n <= m written -- the scores the rule
+ * saw, so that a caller can replay the decision.  mk_prefill_set_block_sparse_threshold selects this rule for
+ * the prefill ops (mk_prefill_set_block_sparse switches back to the ranking rule). */
+int mk_block_select_threshold(const void *qkv, const void *k_cache, int seq_len, int max_seq_len, float alpha,
+                              int window, int sink, int last_n_full, unsigned int *mask_out, float *scores_out,
+                              void *scratch, cudaStream_t stream);
+int mk_prefill_set_block_sparse_threshold(int enable, float alpha, int window, int sink, int last_n_full);
 int mk_attention_prefill(const void *qkv, const void *k_cache, const void *v_cache, void *out, int seq_len,
                          int max_seq_len, const unsigned int *mask, cudaStream_t stream);
 

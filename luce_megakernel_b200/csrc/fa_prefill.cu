@@ -252,8 +252,12 @@ __global__ void __launch_bounds__(256) k_bs_pool(const __nv_bfloat16* __restrict
 // One CTA per (query block i, head): scores against all causal key blocks, then keep the sink blocks, the
 // local window and the `topk` best by score (ties to the lower index).  Every add and multiply is rounded
 // on its own and in a fixed order, so the scores can be reproduced bit for bit on a CPU.
+// rule 1 is the reference's own keep rule (dflash/src/flashprefill_select.cpp:27-84) on the same scores: sink blocks,
+// the local window, every causal block for the last `last_full` query blocks, and the blocks whose score reaches
+// alpha times the row maximum (one f32 multiply, `>=`).  scores_out (optional): f32 [8][nblk][nblk], entries j <= i.
 __global__ void __launch_bounds__(256) k_bs_select(const float* __restrict__ means, uint32_t* __restrict__ mask, int nblk, int nwords,
-                                                   double top_frac, int window, int sink) {
+                                                   double top_frac, int window, int sink, int rule, float alpha, int last_full,
+                                                   float* __restrict__ scores_out) {
     pdl_enter();
     extern __shared__ float sc[];                           // nblk scores, then nwords mask words
     uint32_t* words = reinterpret_cast<uint32_t*>(sc + nblk);
@@ -274,8 +278,18 @@ __global__ void __launch_bounds__(256) k_bs_select(const float* __restrict__ mea
     }
     for (int w = threadIdx.x; w < nwords; w += 256) words[w] = 0u;
     __syncthreads();
+    if (scores_out)
+        for (int j = threadIdx.x; j < n; j += 256) scores_out[((size_t)h * nblk + i) * nblk + j] = sc[j];
+    if (rule == 1) {
+        float mx = -INFINITY;                               // every thread scans the row: max is order-independent
+        for (int o = 0; o < n; ++o) mx = fmaxf(mx, sc[o]);
+        const float thresh = __fmul_rn(mx, alpha);
+        const bool all = i >= nblk - last_full;
+        for (int j = threadIdx.x; j < n; j += 256)
+            if (j < sink || i - j < window || all || sc[j] >= thresh) atomicOr(&words[j >> 5], 1u << (j & 31));
+    }
     const int topk = (int)ceil(top_frac * (double)n);
-    for (int j = threadIdx.x; j < n; j += 256) {
+    for (int j = threadIdx.x; rule == 0 && j < n; j += 256) {
         bool keep = j < sink || j > i - window;
         if (!keep) {
             const float s = sc[j];
@@ -297,13 +311,15 @@ size_t block_select_scratch_bytes(int S) {
 }
 
 cudaError_t block_select(const void* qkv, const void* kc, int S, int max_seq, double top_frac, int window, int sink,
-                         void* scratch, uint32_t** mask_out, cudaStream_t stream) {
+                         void* scratch, uint32_t** mask_out, cudaStream_t stream, int rule, float alpha, int last_full,
+                         float* scores_out) {
     const int nblk = (S + 127) / 128, nwords = (nblk + 31) / 32;
     if (nblk > MAX_KEY_BLOCKS) return cudaErrorInvalidValue;
     float* means = (float*)scratch;
     uint32_t* mask = (uint32_t*)((char*)scratch + (size_t)10 * nblk * FA_HEAD_DIM * 4);
     launch_pdl(k_bs_pool, dim3(nblk, 10), 256, 0, stream, (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)kc, means, S, max_seq, nblk);
-    launch_pdl(k_bs_select, dim3(nblk, 8), 256, (nblk + nwords) * 4, stream, means, mask, nblk, nwords, top_frac, window, sink);
+    launch_pdl(k_bs_select, dim3(nblk, 8), 256, (nblk + nwords) * 4, stream, means, mask, nblk, nwords, top_frac, window, sink, rule, alpha,
+               last_full, scores_out);
     *mask_out = mask;
     return cudaGetLastError();
 }

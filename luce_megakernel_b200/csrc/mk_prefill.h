@@ -68,7 +68,10 @@ cudaError_t fa_prefill_tcgen05(const void* qkv, const void* kc, const void* vc, 
 // most recent ones and the ceil(top_frac * causal blocks) best by mean-pooled q . mean-pooled k, per query head.
 // scratch: block_select_scratch_bytes(S); *mask_out points into it: uint32 [8][blocks][ceil(blocks / 32)].
 size_t block_select_scratch_bytes(int S);
+// rule 1 replaces the ranking by the reference's threshold rule (score >= alpha * row maximum, and every causal block
+// for the last `last_full` query blocks); scores_out (optional) receives the f32 scores [8][blocks][blocks], j <= i.
 cudaError_t block_select(const void* qkv, const void* kc, int S, int max_seq, double top_frac, int window, int sink,
-                         void* scratch, uint32_t** mask_out, cudaStream_t stream);
+                         void* scratch, uint32_t** mask_out, cudaStream_t stream, int rule = 0, float alpha = 0.f,
+                         int last_full = 0, float* scores_out = nullptr);
 
 }  // namespace mk

@@ -512,7 +512,7 @@ HostTable g_tables[64];
 struct HostTableTS { const void* src = nullptr; int n = 0; LayerWeightsNVFP4TS rows[MAX_LAYERS]; };
 HostTableTS g_tables_ts[64];
 thread_local char g_perr[200] = "";
-struct SparseCfg { bool enabled = false; double top_frac = 0.10; int window = 4, sink = 1; };
+struct SparseCfg { bool enabled = false; double top_frac = 0.10; int window = 4, sink = 1; int rule = 0; float alpha = 0.f; int last_full = 0; };
 SparseCfg g_sparse;
 struct TailCfg { int n = 0; float* running_max = nullptr; };   // tail-attention scoring for the prompt compressor (drafter.cu)
 TailCfg g_tail;
@@ -560,7 +560,17 @@ extern "C" void mk_prefill_forget_tables(void) {
 extern "C" int mk_prefill_set_block_sparse(int enable, double top_frac, int window, int sink) {
     if (enable && (!(top_frac >= 0.0 && top_frac <= 1.0) || window < 1 || sink < 0)) return MK_ERR_BAD_ARG;
     mk::g_sparse.enabled = enable != 0;
-    if (enable) { mk::g_sparse.top_frac = top_frac; mk::g_sparse.window = window; mk::g_sparse.sink = sink; }
+    if (enable) { mk::g_sparse.top_frac = top_frac; mk::g_sparse.window = window; mk::g_sparse.sink = sink; mk::g_sparse.rule = 0; }
+    return MK_OK;
+}
+// The reference's keep rule instead of the ranking (dflash/src/flashprefill_select.cpp:27-84).
+extern "C" int mk_prefill_set_block_sparse_threshold(int enable, float alpha, int window, int sink, int last_n_full) {
+    if (enable && (!(alpha == alpha) || window < 1 || sink < 0 || last_n_full < 0)) return MK_ERR_BAD_ARG;
+    mk::g_sparse.enabled = enable != 0;
+    if (enable) {
+        mk::g_sparse.rule = 1; mk::g_sparse.alpha = alpha; mk::g_sparse.window = window; mk::g_sparse.sink = sink;
+        mk::g_sparse.last_full = last_n_full;
+    }
     return MK_OK;
 }
 // Status word of the prefill kernels on the current device: 0 = no bounded wait has run out; 1 = a GEMM wait,
@@ -773,7 +783,8 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
             if (g_sparse.enabled) {
                 uint32_t* m = nullptr;
                 PF_CHECK(block_select(w.wide, kc, S, max_seq_len, g_sparse.top_frac, g_sparse.window, g_sparse.sink,
-                                      w.select_scratch, &m, stream), "block selection");
+                                      w.select_scratch, &m, stream, g_sparse.rule, g_sparse.alpha, g_sparse.last_full, nullptr),
+                         "block selection");
                 bmask = m;
             }
             if (g_attn_impl == 1) PF_CHECK(fa_prefill_tcgen05(w.wide, kc, vc, w.act, S, max_seq_len, w.err, bmask, stream), "attention");
@@ -1129,6 +1140,20 @@ extern "C" int mk_block_select(const void* qkv, const void* k_cache, int seq_len
         return pfail(MK_ERR_BAD_ARG, "bad argument");
     uint32_t* m = nullptr;
     PF_CHECK(block_select(qkv, k_cache, seq_len, max_seq_len, top_frac, window, sink, scratch, &m, stream), "block selection");
+    const int nblk = (seq_len + 127) / 128, nwords = (nblk + 31) / 32;
+    PF_CHECK(cudaMemcpyAsync(mask_out, m, (size_t)8 * nblk * nwords * 4, cudaMemcpyDeviceToDevice, stream), "mask copy");
+    return MK_OK;
+}
+extern "C" int mk_block_select_threshold(const void* qkv, const void* k_cache, int seq_len, int max_seq_len, float alpha, int window,
+                                         int sink, int last_n_full, unsigned int* mask_out, float* scores_out, void* scratch,
+                                         cudaStream_t stream) {
+    using namespace mk;
+    if (!qkv || !k_cache || !mask_out || !scratch || seq_len < 1 || seq_len > max_seq_len || window < 1 || sink < 0 ||
+        last_n_full < 0 || !(alpha == alpha))
+        return pfail(MK_ERR_BAD_ARG, "bad argument");
+    uint32_t* m = nullptr;
+    PF_CHECK(block_select(qkv, k_cache, seq_len, max_seq_len, 0.0, window, sink, scratch, &m, stream, 1, alpha, last_n_full, scores_out),
+             "block selection");
     const int nblk = (seq_len + 127) / 128, nwords = (nblk + 31) / 32;
     PF_CHECK(cudaMemcpyAsync(mask_out, m, (size_t)8 * nblk * nwords * 4, cudaMemcpyDeviceToDevice, stream), "mask copy");
     return MK_OK;

@@ -13,9 +13,10 @@ query / key vectors, and ties broken towards the lower block index.  Structure a
 host-side selection (dflash/src/flashprefill_select.cpp:27-84: sink + window + score threshold against
 the row maximum); the ranking rule and the 10 % budget are the benchmark's.
 
-parity unpinned: the reference holds no vectors for this rule (its own selection rule differs and
+parity unpinned for the ranking rule: the reference holds no vectors for it (its own selection rule differs and
 belongs to another model); the CUDA kernels are held to this restatement bit for bit, which is why
-every floating-point step below fixes its summation order:
+every floating-point step below fixes its summation order.  The reference's own keep rule (select_threshold below)
+IS pinned: against the reference function compiled from its source file, and through a committed fixture made by it.
 
   * block sums run sequentially over positions 0..127 in f32, then one multiply by 1/count;
   * a score is a 256-term dot product taken as 32 lane partials (lane l sums dims 8l..8l+7 in order,
@@ -76,10 +77,63 @@ def select_blocks(scores, top_frac=0.10, window=4, sink=1):
     return keep
 
 
+def select_threshold(scores, sink=2, window=4, last_n_full=2, alpha=0.12):
+    """The reference's own keep rule on a score grid (dflash/src/flashprefill_select.cpp:27-84, block_select_host):
+    scores [M, N] f32 -> bool [M, N].  Per query block m, over the causal key blocks n <= m: n < sink, m - n < window,
+    every block when m >= M - last_n_full, and score >= max_score * alpha with the product taken in f32.
+    Pinned against the compiled reference function (tests/test_block_select_threshold.py)."""
+    M, N = scores.shape
+    keep = np.zeros((M, N), dtype=bool)
+    a = np.float32(alpha)
+    for m in range(M):
+        row = scores[m, :m + 1].astype(np.float32)
+        mx = np.float32(-np.inf)
+        for v in row:
+            if v > mx:
+                mx = v
+        with np.errstate(invalid="ignore"):
+            thresh = np.float32(mx * a)
+        full = m >= M - last_n_full
+        for n in range(m + 1):
+            keep[m, n] = (n < sink) or (m - n < window) or full or bool(row[n] >= thresh)
+    return keep
+
+
+def reference_block_select(scores_hmn, sink, window, last_n_full, alpha):
+    """Runs the compiled reference function (oracle/_ref/libref_block_select.so) on scores [H, M, N] f32 and
+    returns bool [H, M, N], or None when the library is not there."""
+    import ctypes
+    import os
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ref", "libref_block_select.so")
+    if not os.path.exists(path):
+        return None
+    lib = ctypes.CDLL(path)
+    H, M, N = scores_hmn.shape
+    sc = np.ascontiguousarray(np.transpose(scores_hmn.astype(np.float32), (1, 2, 0)))[None]      # [1, M, N, H]
+    idx = np.full((1, M, N, H), -7, dtype=np.int32)
+    cnt = np.zeros((1, M, H), dtype=np.int32)
+    lib.ref_block_select_host(sc.ctypes.data_as(ctypes.c_void_p), 1, M, N, H, int(sink), int(window), int(last_n_full),
+                              ctypes.c_float(alpha), idx.ctypes.data_as(ctypes.c_void_p), cnt.ctypes.data_as(ctypes.c_void_p))
+    keep = np.zeros((H, M, N), dtype=bool)
+    for h in range(H):
+        for m in range(M):
+            c = int(cnt[0, m, h])
+            ks = idx[0, m, :c, h]
+            assert np.all(ks[1:] > ks[:-1]) and np.all(idx[0, m, c:, h] == -1)
+            keep[h, m, ks] = True
+    return keep
+
+
 def select_for_heads(q, k, gqa=4, **kw):
     """q [Hq, S, D], k [Hk, S, D] float32 -> bool [Hq, M, N]."""
     kmeans = [pool_means(k[g]) for g in range(k.shape[0])]
     return np.stack([select_blocks(block_scores(pool_means(q[h]), kmeans[h // gqa]), **kw) for h in range(q.shape[0])])
+
+
+def select_threshold_for_heads(q, k, gqa=4, **kw):
+    """The reference's keep rule on the mean-pooled scores: q [Hq, S, D], k [Hk, S, D] float32 -> bool [Hq, M, N]."""
+    kmeans = [pool_means(k[g]) for g in range(k.shape[0])]
+    return np.stack([select_threshold(block_scores(pool_means(q[h]), kmeans[h // gqa]), **kw) for h in range(q.shape[0])])
 
 
 def token_mask(keep, S):

@@ -9,6 +9,8 @@
                                    for sm_100a with the reference's own flags, --use_fast_math included.
   oracle/_ref/libref_drafter_select.so steps 2-4 of the reference's prompt compressor (dflash/src/qwen3_drafter.cpp),
                                    cut out at build time and wrapped in one C function (g++, host only).
+  oracle/_ref/libref_block_select.so the reference's host-side block selection (dflash/src/flashprefill_select.cpp),
+                                   compiled where it lies together with oracle/ref_block_select_wrap.cpp (g++).
   oracle/_ref/libref_megakernel.so the reference's own decode and prefill kernels (megakernel/kernel.cu,
                                    megakernel/prefill.cu), compiled for sm_100a from the sources where they lie
                                    in the reference checkout, with the flags of megakernel/setup.py and
@@ -153,11 +155,30 @@ def build_ref_drafter(force=False):
     return REF_DRAFTER_LIB
 
 
+REF_BLOCK_SELECT_LIB = os.path.join(HERE, "_ref", "libref_block_select.so")
+
+
+def build_ref_block_select(force=False):
+    """The reference's block_select_host (dflash/src/flashprefill_select.cpp:27-84): plain C++ with no dependency,
+    compiled from the checkout together with the C wrapper of this folder.  Returns the library path or None."""
+    src = os.path.join(REF_DIR, "dflash", "src", "flashprefill_select.cpp")
+    wrap = os.path.join(HERE, "ref_block_select_wrap.cpp")
+    if not os.path.exists(src):
+        return REF_BLOCK_SELECT_LIB if os.path.exists(REF_BLOCK_SELECT_LIB) else None
+    if not force and os.path.exists(REF_BLOCK_SELECT_LIB) and not _newer(REF_BLOCK_SELECT_LIB, src) \
+            and not _newer(REF_BLOCK_SELECT_LIB, wrap):
+        return REF_BLOCK_SELECT_LIB
+    os.makedirs(os.path.dirname(REF_BLOCK_SELECT_LIB), exist_ok=True)
+    subprocess.check_call(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", wrap, src, "-o", REF_BLOCK_SELECT_LIB])
+    return REF_BLOCK_SELECT_LIB
+
+
 def build_all(force=False):
     build_nvfp4(force)
     build_ref(force)
     build_ref_quant(force)
     build_ref_drafter(force)
+    build_ref_block_select(force)
 
 
 if __name__ == "__main__":

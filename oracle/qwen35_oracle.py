@@ -232,8 +232,9 @@ class Oracle:
         self.tail_lookahead = 0
         self.tail_running_max = None
         self.ref_q_rope_in_place = ref_q_rope_in_place
-        # block_sparse = {"top_frac": .., "window": .., "sink": ..}: prompts processed from position 0 attend
-        # only to the key blocks oracle/block_sparse.py selects (bf16-rounded q and k feed the selection)
+        # block_sparse = {"top_frac": .., "window": .., "sink": ..} (ranking rule) or {"alpha": .., "window": .., "sink": ..,
+        # "last_n_full": ..} (the reference's threshold rule): prompts processed from position 0 attend only to the
+        # key blocks oracle/block_sparse.py selects (bf16-rounded q and k feed the selection)
         self.block_sparse = block_sparse
         self.w = {k: v.to(torch.float32) for k, v in weights.items()}
         self.num_layers = 1 + max(int(k.split(".")[2]) for k in weights if k.startswith("model.layers."))
@@ -329,7 +330,8 @@ class Oracle:
         keep = None
         if self.block_sparse is not None and pos0 == 0 and T > 1:
             from . import block_sparse as BS
-            keep = BS.select_for_heads(_bf(q).permute(1, 0, 2).numpy(), st.k_cache[idx, :, :L].numpy(), **self.block_sparse)
+            pick = BS.select_threshold_for_heads if "alpha" in self.block_sparse else BS.select_for_heads
+            keep = pick(_bf(q).permute(1, 0, 2).numpy(), st.k_cache[idx, :, :L].numpy(), **self.block_sparse)
         # query rows in slabs of 1024 (every row's softmax is independent; the slabs only bound the size of the
         # score matrix for prompts of many thousand tokens)
         o = torch.empty(T, FA_Q_HEADS, FA_HEAD_DIM)

@@ -176,7 +176,9 @@ def test_keeping_every_block_equals_dense():
 
 
 @pytest.mark.gpu
-def test_sparse_prefill_follows_oracle(small_model):
+@pytest.mark.parametrize("rule", [dict(top_frac=0.10, window=2, sink=1), dict(alpha=0.6, window=2, sink=1, last_n_full=0)],
+                         ids=["ranking", "threshold"])
+def test_sparse_prefill_follows_oracle(small_model, rule):
     """Whole prefill of the 8-layer model in sparse mode against the oracle with the same rule.  The rule
     ranks blocks by scores computed from each side's own bf16 queries and keys, so a near-tie at the
     10 % boundary may resolve differently: the bound is the dense prefill's, and the dense oracle must be
@@ -186,14 +188,17 @@ def test_sparse_prefill_follows_oracle(small_model):
     from test_prefill_gpu import bf16_ulp
     sd, dense = small_model("unit", "decode")
     S, NL, V = 1500, 8, 2048
-    rule = dict(top_frac=0.10, window=2, sink=1)
     sparse = O.Oracle(sd, rounding="decode", block_sparse=rule)
     g = torch.Generator().manual_seed(77)
     toks = torch.randint(0, V, (S,), generator=g).tolist()
     hs = sparse.forward(toks, O.State.new(NL, S + 8, V)).hidden[-1][-1]
     hd = dense.forward(toks, O.State.new(NL, S + 8, V), want_logits=False).hidden[-1][-1]
     dec = M.Decoder(weights=M.weights_from_state_dict(sd), max_seq_len=S + 8, api="cabi")
-    assert lib().mk_prefill_set_block_sparse(1, ctypes.c_double(rule["top_frac"]), rule["window"], rule["sink"]) == 0
+    if "alpha" in rule:
+        assert lib().mk_prefill_set_block_sparse_threshold(1, ctypes.c_float(rule["alpha"]), rule["window"], rule["sink"],
+                                                           rule["last_n_full"]) == 0
+    else:
+        assert lib().mk_prefill_set_block_sparse(1, ctypes.c_double(rule["top_frac"]), rule["window"], rule["sink"]) == 0
     try:
         dec.prefill(toks)
     finally:
