@@ -506,6 +506,14 @@ int mk_selftest_bounded_wait(cudaStream_t stream);
 void mk_set_logits_buffer(float *logits);
 int mk_sample_top_k(const float *logits, int n, float temperature, int top_k, unsigned long long seed,
                     unsigned long long counter, int *token_out, cudaStream_t stream);
+/* The same with a nucleus cut after top_k, in the order of the sampler chain of the reference's speculative-decoding
+ * driver (top_k -> softmax(logit / temperature) -> top_p -> draw; dflash/test/test_dflash.cpp:127-188): of the set
+ * top_k keeps, in descending logit order, the shortest prefix whose probability mass reaches top_p stays (the
+ * element that crosses it included; logits equal to it all stay); top_p <= 0 or >= 1 cuts nothing.  The draw is
+ * the Gumbel-max rule above over what is left (the reference draws by inverse CDF from a Mersenne twister: the
+ * two agree in distribution, not draw for draw). */
+int mk_sample_top_k_top_p(const float *logits, int n, float temperature, int top_k, float top_p,
+                          unsigned long long seed, unsigned long long counter, int *token_out, cudaStream_t stream);
 const char *mk_sample_error(void);
 
 /* Optional per-phase timeline: `buf` is a device buffer of

@@ -271,11 +271,12 @@ class Decoder:
         self._position += 1
         return int(self._step_host_tok.value)
 
-    def step_sampled(self, token_id: int, temperature: float, top_k: int = 0, seed: int = 0) -> int:
+    def step_sampled(self, token_id: int, temperature: float, top_k: int = 0, seed: int = 0, top_p: float = 1.0) -> int:
         """One decode step whose next token is drawn from softmax(logits / temperature) over the top_k largest
-        logits instead of the argmax (the repetition penalty, if any, is applied to the logits first, as in the greedy
-        path; reference hook: megakernel/kernel.cu:793-795).  Reproducible: the draw depends on (seed, position) only.
-        The step's logits stay in self._logits (f32 [vocab])."""
+        logits, cut to the nucleus of mass top_p, instead of the argmax (the repetition penalty, if any, is applied to
+        the logits first, as in the greedy path; reference hook: megakernel/kernel.cu:793-795; order of the stages as
+        in the sampler chain of dflash/test/test_dflash.cpp:127-188).  Reproducible: the draw depends on
+        (seed, position) only.  The step's logits stay in self._logits (f32 [vocab])."""
         if not hasattr(self, "_logits"):
             self._logits = torch.empty(self.vocab, dtype=torch.float32, device=self._embed_weight.device)
         self._lib.mk_set_logits_buffer(_ptr(self._logits))
@@ -283,9 +284,9 @@ class Decoder:
             self.step_async(token_id)
         finally:
             self._lib.mk_set_logits_buffer(ctypes.c_void_p(0))
-        rc = self._lib.mk_sample_top_k(_ptr(self._logits), ctypes.c_int(self.vocab), ctypes.c_float(float(temperature)),
-                                       ctypes.c_int(int(top_k)), ctypes.c_ulonglong(int(seed)),
-                                       ctypes.c_ulonglong(self._position), _ptr(self._out_token), self._stream())
+        rc = self._lib.mk_sample_top_k_top_p(_ptr(self._logits), ctypes.c_int(self.vocab), ctypes.c_float(float(temperature)),
+                                             ctypes.c_int(int(top_k)), ctypes.c_float(float(top_p)), ctypes.c_ulonglong(int(seed)),
+                                             ctypes.c_ulonglong(self._position), _ptr(self._out_token), self._stream())
         if rc != 0:
             self._lib.mk_sample_error.restype = ctypes.c_char_p
             raise RuntimeError(f"sampling failed ({rc}): {self._lib.mk_sample_error().decode()}")

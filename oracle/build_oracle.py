@@ -9,6 +9,9 @@
                                    for sm_100a with the reference's own flags, --use_fast_math included.
   oracle/_ref/libref_drafter_select.so steps 2-4 of the reference's prompt compressor (dflash/src/qwen3_drafter.cpp),
                                    cut out at build time and wrapped in one C function (g++, host only).
+  oracle/_ref/libref_sampler.so    the CPU sampler chain of the reference's speculative-decoding driver (SamplerCfg and
+                                   sample_logits, dflash/test/test_dflash.cpp), cut out at build time and wrapped
+                                   in one C function (g++, host only).
   oracle/_ref/libref_block_select.so the reference's host-side block selection (dflash/src/flashprefill_select.cpp),
                                    compiled where it lies together with oracle/ref_block_select_wrap.cpp (g++).
   oracle/_ref/libref_megakernel.so the reference's own decode and prefill kernels (megakernel/kernel.cu,
@@ -155,6 +158,43 @@ def build_ref_drafter(force=False):
     return REF_DRAFTER_LIB
 
 
+REF_SAMPLER_LIB = os.path.join(HERE, "_ref", "libref_sampler.so")
+
+
+def build_ref_sampler(force=False):
+    """SamplerCfg + sample_logits of the reference's driver (dflash/test/test_dflash.cpp: plain C++ on std containers
+    inside a 3 700-line program that needs ggml): the two definitions are cut out of the checkout at build time into a
+    generated translation unit under oracle/_ref/ and wrapped in one C function that seeds a std::mt19937_64 and
+    draws n times.  Returns the library path or None."""
+    src = os.path.join(REF_DIR, "dflash", "test", "test_dflash.cpp")
+    if not os.path.exists(src):
+        return REF_SAMPLER_LIB if os.path.exists(REF_SAMPLER_LIB) else None
+    if not force and os.path.exists(REF_SAMPLER_LIB) and not _newer(REF_SAMPLER_LIB, src) and not _newer(REF_SAMPLER_LIB, __file__):
+        return REF_SAMPLER_LIB
+    os.makedirs(os.path.dirname(REF_SAMPLER_LIB), exist_ok=True)
+    text = open(src).read()
+    a = text.index("struct SamplerCfg {")
+    b = text.index("static bool parse_sampler_token", a)
+    body = text[a:b]
+    gen = os.path.join(HERE, "_ref", "ref_sampler_gen.cpp")
+    with open(gen, "w") as f:
+        f.write("// GENERATED at build time from the reference checkout (never committed): SamplerCfg and sample_logits of\n"
+                "// dflash/test/test_dflash.cpp, wrapped in one C function.\n"
+                "#include <algorithm>\n#include <cmath>\n#include <cstdint>\n#include <random>\n#include <unordered_set>\n"
+                "#include <utility>\n#include <vector>\n"
+                + body +
+                'extern "C" int ref_sample_logits(const float* logits, int vocab, float temp, float top_p, int top_k, float rep_pen,\n'
+                "                                 const int32_t* history, int n_history, unsigned long long seed, int n_draws,\n"
+                "                                 int32_t* out) {\n"
+                "    SamplerCfg cfg; cfg.temp = temp; cfg.top_p = top_p; cfg.top_k = top_k; cfg.rep_pen = rep_pen; cfg.seed = seed;\n"
+                "    std::vector<int32_t> hist(history, history + n_history);\n"
+                "    std::mt19937_64 rng; rng.seed(seed);\n"
+                "    for (int i = 0; i < n_draws; ++i) out[i] = sample_logits(logits, vocab, cfg, hist, rng);\n"
+                "    return n_draws;\n}\n")
+    subprocess.check_call(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", gen, "-o", REF_SAMPLER_LIB])
+    return REF_SAMPLER_LIB
+
+
 REF_BLOCK_SELECT_LIB = os.path.join(HERE, "_ref", "libref_block_select.so")
 
 
@@ -179,6 +219,7 @@ def build_all(force=False):
     build_ref_quant(force)
     build_ref_drafter(force)
     build_ref_block_select(force)
+    build_ref_sampler(force)
 
 
 if __name__ == "__main__":
