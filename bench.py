@@ -594,6 +594,13 @@ def main():
     for _ in range(3):
         pp()
     pp_ms = timed(pp, 10) / 10
+    # the same prompt replayed from the CUDA graph Decoder.prefill_graphed keeps per prompt length (reset included)
+    dec._position = 0
+    dec.prefill_graphed(prompt_dev)
+    pp_graph = dec._prefill_graphs[PROMPT_LEN]["graph"]
+    for _ in range(3):
+        pp_graph.replay()
+    pp_graph_ms = timed(pp_graph.replay, 10) / 10
 
     # dense prefill at 8192 and 32768 tokens, single GPU only: 1 warm-up + 2 timed calls
     long_pp = []
@@ -678,6 +685,7 @@ def main():
             "prefill": {"prompt_len": PROMPT_LEN, "ms": pp_max, "tok_s": world * PROMPT_LEN / (pp_max * 1e-3),
                         "tflops_algorithmic": PREFILL_TFLOP_PP520 / (pp_max * 1e-3),
                         "frac_of_bf16_peak": PREFILL_TFLOP_PP520 / (pp_max * 1e-3) / measured_bf16_peak(),
+                        "graph_replay_ms": pp_graph_ms,
                         "note": "prefill_bf16 op: persistent tcgen05/TMEM GEMMs fed by TMA, chunk-64 DeltaNet scan on "
                                 "mma.sync, causal GQA flash attention on tcgen05/TMEM"},
             "gpu_launches": world * args.steps,

@@ -364,6 +364,45 @@ class Decoder:
         self._position = S
         return self._out_token
 
+    def prefill_graphed(self, token_ids) -> int:
+        """reset() + prefill() replayed from a CUDA graph kept per prompt length, the ids going through a static device
+        buffer (the reference's NVFP4 driver does the same: megakernel/model_nvfp4.py:676-702, _build_prefill_graph /
+        _prefill_graph_state).  The graph bakes in the library workspace's addresses: the workspace is reserved for
+        the length before the capture, and a graph taken before a later growth is captured again."""
+        ids = torch.as_tensor(token_ids, dtype=torch.int32).to(self._embed_weight.device).contiguous()
+        S = int(ids.numel())
+        if S < 1 or S > self.max_seq_len:
+            raise ValueError("prompt length must be in [1, max_seq_len]")
+        lib = self._lib
+        lib.mk_prefill_workspace_generation.restype = ctypes.c_uint
+        cache = self.__dict__.setdefault("_prefill_graphs", {})
+        st = cache.get(S)
+        if st is None or st["generation"] != lib.mk_prefill_workspace_generation():
+            if lib.mk_prefill_reserve(ctypes.c_int(S)) != 0:
+                raise RuntimeError("mk_prefill_reserve failed")
+            static_ids = torch.zeros(S, dtype=torch.int32, device=ids.device)
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):            # eager once: host-side caches filled, nothing left to allocate
+                self.reset()
+                self.prefill_async(static_ids)
+            side.synchronize()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self.reset()
+                self.prefill_async(static_ids)
+            st = {"graph": graph, "ids": static_ids, "generation": lib.mk_prefill_workspace_generation()}
+            cache[S] = st
+        st["ids"].copy_(ids)
+        st["graph"].replay()
+        self._position = S
+        tok = int(self._out_token.item())
+        status = lib.mk_prefill_status()
+        if status != 0:
+            raise RuntimeError(f"a bounded wait ran out inside a prefill kernel (status {status})")
+        return tok
+
     def reset(self):
         self._position = 0
         self._fa_k_cache.zero_()

@@ -96,3 +96,28 @@ def test_growth_is_refused_during_capture_and_visible_afterwards(dec):
     big.prefill(long_ids)                            # outside a capture the workspace grows ...
     assert L.mk_prefill_workspace_generation() != gen        # ... and says so: earlier graphs must be captured again
     assert L.mk_prefill_workspace_tokens() >= cap + 64 and L.mk_prefill_status() == 0
+
+
+def test_prefill_graphed_keeps_one_graph_per_length_and_recaptures_after_growth(dec):
+    """Decoder.prefill_graphed (the reference's per-length prefill graph cache, megakernel/model_nvfp4.py:676-702)."""
+    from luce_megakernel_b200 import model as M, lib
+    L = lib()
+    a, b = _ids(33, 5), _ids(33, 6)
+    dec.reset(); want_a = dec.prefill(a); state_a = dec._dn_states.clone()
+    dec.reset(); want_b = dec.prefill(b)
+    assert dec.prefill_graphed(a) == want_a and torch.equal(dec._dn_states, state_a) and dec._position == 33
+    g33 = dec._prefill_graphs[33]["graph"]
+    assert dec.prefill_graphed(b) == want_b                   # same length: the cached graph, new ids, state reset inside
+    assert dec._prefill_graphs[33]["graph"] is g33
+    assert dec.step(int(want_b)) >= 0                          # decoding continues from the graph's state
+    c = _ids(57, 7)
+    dec.reset(); want_c = dec.prefill(c)
+    assert dec.prefill_graphed(c) == want_c and set(dec._prefill_graphs) >= {33, 57}
+    # a growth of the library workspace invalidates the baked-in addresses: the next call captures again
+    L.mk_prefill_workspace_generation.restype = ctypes.c_uint
+    cap = L.mk_prefill_workspace_tokens()
+    big = M.Decoder(weights=dec._weights, max_seq_len=cap + 80, api="cabi")
+    big.prefill(_ids(cap + 64, 8))
+    assert L.mk_prefill_workspace_generation() != dec._prefill_graphs[33]["generation"]
+    assert dec.prefill_graphed(a) == want_a and dec._prefill_graphs[33]["graph"] is not g33
+    assert L.mk_prefill_status() == 0
