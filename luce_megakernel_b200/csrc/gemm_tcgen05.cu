@@ -79,11 +79,17 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, int*
 // SPLIT: the K range is cut into `ks` parts, a work item is (tile, part) and leaves its f32 partial tile in
 // `partial` ([part][M][N]); gemm_splitk_reduce adds the parts (and the residual) and rounds to bf16.  Used when
 // a problem has far fewer tiles than the machine has SMs (the K = 2048 / 3584 projections of a short prompt).
-template <int BN, bool SPLIT>
+// GLU: the weight matrix holds two blocks of rows, gate rows [0, N) and up rows [glu_off, glu_off + N); a tile's B
+// operand is BN/2 gate rows stacked on the BN/2 up rows of the same outputs (two tensor copies per stage), so the
+// accumulator holds gate and up of BN/2 output columns side by side and the epilogue stores
+// silu(bf16(gate)) * bf16(up) -- bit for bit what the separate SwiGLU kernel makes of the two rounded products
+// (reference: megakernel/prefill.cu:1239-1247) -- without the [M, 2 N] intermediate ever reaching memory.
+template <int BN, bool SPLIT, bool GLU = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                     __nv_bfloat16* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc,
-                    int* err, float* __restrict__ partial, int ks) {
+                    int* err, float* __restrict__ partial, int ks, int glu_off) {
+    constexpr int BNO = GLU ? BN / 2 : BN;                // output columns per tile
     // the next kernel may be scheduled now; this one sets up barriers and tensor memory while its predecessor
     // drains and waits for it (griddepcontrol.wait below) before the first operand is read
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -98,12 +104,12 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * G::STAGE_BYTES + 16 * STAGES + 32);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk_all = K / BK;
-    const int mt = (M + BM - 1) / BM, ntiles = mt * (N / BN) * (SPLIT ? ks : 1);
+    const int mt = (M + BM - 1) / BM, ntiles = mt * (N / BNO) * (SPLIT ? ks : 1);
     // work item -> (tile, K part); part p covers k-steps [p nk / ks, (p + 1) nk / ks)
     auto item = [&](int it_, int& m0, int& n0, int& kb0, int& kb1, int& part) {
         const int tile = SPLIT ? it_ / ks : it_;
         part = SPLIT ? it_ - tile * ks : 0;
-        m0 = (tile % mt) * BM; n0 = (tile / mt) * BN;
+        m0 = (tile % mt) * BM; n0 = (tile / mt) * BNO;
         kb0 = SPLIT ? (part * nk_all) / ks : 0;
         kb1 = SPLIT ? ((part + 1) * nk_all) / ks : nk_all;
     };
@@ -137,6 +143,7 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
                     mbar_expect_tx(full0 + 8 * s, G::STAGE_BYTES);
                     tma_load_2d(a0 + s * TILE_A_BYTES, &map_a, kb * BK, m0, full0 + 8 * s);
                     tma_load_2d(b0 + s * G::TILE_B_BYTES, &map_w, kb * BK, n0, full0 + 8 * s);
+                    if (GLU) tma_load_2d(b0 + s * G::TILE_B_BYTES + BNO * BK * 2, &map_w, kb * BK, glu_off + n0, full0 + 8 * s);
                 }
             }
         }
@@ -179,9 +186,25 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int row = m0 + quad * 32 + lane;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c0 = 0; c0 < BNO; c0 += 32) {
                 uint32_t v[32];
                 const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * BN + (uint32_t)c0;
+                uint32_t u[32];
+                if (GLU) {
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]),
+                          "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+                          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]),
+                          "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15]),
+                          "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]),
+                          "=r"(u[20]), "=r"(u[21]), "=r"(u[22]), "=r"(u[23]),
+                          "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]),
+                          "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+                        : "r"(taddr + (uint32_t)BNO) : "memory");
+                }
                 asm volatile(
                     "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
                     "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -192,7 +215,26 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
                       "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
                     : "r"(taddr) : "memory");
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (SPLIT) {
+                if (GLU) {
+                    if (row < M) {
+                        __nv_bfloat16* dst = C + (size_t)row * ldc + n0 + c0;
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            uint32_t o[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                // both products rounded to bf16 first, as when they were stored and read back
+                                const __nv_bfloat162 gp = __floats2bfloat162_rn(__uint_as_float(v[j + 2 * e]), __uint_as_float(v[j + 2 * e + 1]));
+                                const __nv_bfloat162 up = __floats2bfloat162_rn(__uint_as_float(u[j + 2 * e]),
+                                                                                __uint_as_float(u[j + 2 * e + 1]));
+                                const uint32_t gw = *reinterpret_cast<const uint32_t*>(&gp), uw = *reinterpret_cast<const uint32_t*>(&up);
+                                const __nv_bfloat162 p = __floats2bfloat162_rn(silu_f(bf_lo(gw)) * bf_lo(uw), silu_f(bf_hi(gw)) * bf_hi(uw));
+                                o[e] = *reinterpret_cast<const uint32_t*>(&p);
+                            }
+                            *reinterpret_cast<uint4*>(dst + j) = make_uint4(o[0], o[1], o[2], o[3]);
+                        }
+                    }
+                } else if (SPLIT) {
                     if (row < M) {
                         float4* dst = reinterpret_cast<float4*>(partial + ((size_t)part * M + row) * N + n0 + c0);
 #pragma unroll
@@ -314,16 +356,50 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
     if (BN == 128 && ks >= 2 && K >= 2048) {      // only the long-K projections: K = 1024 products keep one summation order
         float* ws = splitk_ws;
         const int items = ntiles * ks;
-        launch_pdl(gemm_bf16_tn_kernel<BN, true>, items < sms ? items : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, nullptr, nullptr, M, N, K, ldc, err_flag, ws, ks);
+        launch_pdl(gemm_bf16_tn_kernel<BN, true>, items < sms ? items : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, nullptr, nullptr, M, N, K, ldc, err_flag, ws, ks, 0);
         const size_t n = (size_t)M * (N / 8);
         launch_pdl(gemm_splitk_reduce, (unsigned)((n + 255) / 256), 256, 0, stream, ws, ks, (const __nv_bfloat16*)R, (__nv_bfloat16*)C, M, N, ldc);
         return cudaGetLastError();
     }
-    launch_pdl(gemm_bf16_tn_kernel<BN, false>, ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K, ldc, err_flag, nullptr, 1);
+    launch_pdl(gemm_bf16_tn_kernel<BN, false>, ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K, ldc, err_flag, nullptr, 1, 0);
+    return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t launch_gemm_glu(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldc, int glu_off, int* err_flag,
+                            int sms, cudaStream_t stream) {
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+        if (e != cudaSuccess) return e;
+        attr_done = true;
+    }
+    CUtensorMap ma, mw;
+    if (!make_map(&ma, A, M, K, lda, BM) || !make_map(&mw, W, glu_off + N, K, K, BN / 2)) return cudaErrorInvalidValue;
+    const int ntiles = ((M + BM - 1) / BM) * (N / (BN / 2));
+    launch_pdl(gemm_bf16_tn_kernel<BN, false, true>, ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw,
+               (__nv_bfloat16*)C, (const __nv_bfloat16*)nullptr, M, N, K, ldc, err_flag, (float*)nullptr, 1, glu_off);
     return cudaGetLastError();
 }
 
 }  // namespace
+
+// C[M, N] = silu(A . Wg^T) * (A . Wu^T) with Wg = rows [0, N) and Wu = rows [glu_off, glu_off + N) of W, both
+// products rounded to bf16 before the activation.  N % 128 == 0.
+cudaError_t gemm_bf16_glu(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldc, int glu_off, int* err_flag,
+                          cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % BK || glu_off < N) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(C)) & 15u)
+        return cudaErrorInvalidValue;
+    if ((lda % 8) || (ldc % 8)) return cudaErrorInvalidValue;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    const int mt = (M + BM - 1) / BM;
+    if (mt * (N / 128) >= sms) return launch_gemm_glu<256>(A, W, C, M, N, K, lda, ldc, glu_off, err_flag, sms, stream);
+    return launch_gemm_glu<128>(A, W, C, M, N, K, lda, ldc, glu_off, err_flag, sms, stream);
+}
 
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
                          int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream) {

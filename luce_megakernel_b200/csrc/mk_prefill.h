@@ -27,6 +27,11 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 // the split uses as many parts as fit (none when null).  The call allocates nothing.
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
                          int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream);
+// C[M, N] = silu(A . Wg^T) * (A . Wu^T), Wg = rows [0, N) and Wu = rows [glu_off, glu_off + N) of W [*, K]: the SwiGLU
+// of the MLP inside the gate|up product's epilogue (both products rounded to bf16 first, as the separate kernel saw
+// them).  N % 128 == 0, K % 64 == 0.
+cudaError_t gemm_bf16_glu(const void* A, const void* W, void* C, int M, int N, int K, int lda, int ldc, int glu_off, int* err_flag,
+                          cudaStream_t stream);
 
 // C[M,N] = (ta[0] * tw[0]) * (A[M,K] . W[N,K]^T) (+ R[M,N]); A and W NVFP4 (packed e2m1 rows of K/2 bytes, E4M3 block
 // scales in 128-row x 4-block tiles of 512 bytes, one fp32 tensor scale each), C and R bf16 row-major; block-scaled

@@ -517,6 +517,7 @@ SparseCfg g_sparse;
 struct TailCfg { int n = 0; float* running_max = nullptr; };   // tail-attention scoring for the prompt compressor (drafter.cu)
 TailCfg g_tail;
 int g_attn_impl = 1;              // attention kernel: 1 = tcgen05 / TMEM (default), 0 = mma.sync
+int g_fuse_glu = 1;               // 1 = SwiGLU in the gate|up product's epilogue (default), 0 = separate kernel
 int g_scan_mode = 1;              // 1 = chunks of 64 on the tensor cores, 0 = token-serial recurrence
 int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
     if (e != cudaSuccess) snprintf(g_perr, sizeof(g_perr), "%s: %s", what, cudaGetErrorString(e));
@@ -585,6 +586,7 @@ extern "C" int mk_prefill_status(void) {
     return v;
 }
 extern "C" void mk_prefill_set_attention_impl(int tcgen05) { mk::g_attn_impl = tcgen05 ? 1 : 0; }
+extern "C" void mk_prefill_set_fused_swiglu(int on) { mk::g_fuse_glu = on ? 1 : 0; }
 extern "C" void mk_prefill_set_tail_scoring(int n_lookahead, float* running_max) {
     mk::g_tail.n = (n_lookahead > 0 && running_max) ? n_lookahead : 0;
     mk::g_tail.running_max = mk::g_tail.n ? running_max : nullptr;
@@ -802,13 +804,17 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
             PF_CHECK(quant(w.normed, HIDDEN), "quantise activations");
             PF_CHECK(gemm4(lv.x_gate, w.wide, nullptr, INTER, HIDDEN, 2 * INTER), "gemm gate");
             PF_CHECK(gemm4(lv.x_up, w.wide + INTER, nullptr, INTER, HIDDEN, 2 * INTER), "gemm up");
+        } else if (lv.w_gateup && g_fuse_glu) {
+            // gate | up product with the SwiGLU in its epilogue: straight to the down projection's input
+            PF_CHECK(gemm_bf16_glu(w.normed, lv.w_gateup, w.act, S, INTER, HIDDEN, HIDDEN, INTER, INTER, w.err, stream), "gemm gate_up + SwiGLU");
         } else if (lv.w_gateup) {
             PF_CHECK(gemm(w.normed, lv.w_gateup, w.wide, nullptr, 2 * INTER, HIDDEN, 2 * INTER), "gemm gate_up");
         } else {
             PF_CHECK(gemm(w.normed, lv.w_gate, w.wide, nullptr, INTER, HIDDEN, 2 * INTER), "gemm gate");
             PF_CHECK(gemm(w.normed, lv.w_up, w.wide + INTER, nullptr, INTER, HIDDEN, 2 * INTER), "gemm up");
         }
-        launch_pdl(k_silu_mul, (unsigned)(((size_t)S * (INTER / 8) + 255) / 256), 256, 0, stream, w.wide, w.act, S);
+        if (lv.fp4 || !lv.w_gateup || !g_fuse_glu)
+            launch_pdl(k_silu_mul, (unsigned)(((size_t)S * (INTER / 8) + 255) / 256), 256, 0, stream, w.wide, w.act, S);
         if (lv.fp4) {
             PF_CHECK(quant(w.act, INTER), "quantise activations");
             PF_CHECK(gemm4(lv.x_down, w.hidden, w.hidden, HIDDEN, INTER, HIDDEN), "gemm down");

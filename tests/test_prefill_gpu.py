@@ -156,3 +156,30 @@ def test_decode_after_long_prefill(small_model):
         top = torch.topk(tr.logits, 2)
         assert got == tr.token or (float(top.values[0] - top.values[1]) <= 0.1 and got in top.indices.tolist())
         feed = tr.token
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S", [77, 520, 1300])
+def test_swiglu_in_the_gemm_epilogue_gives_the_bits_of_the_separate_kernel(S):
+    """mk_prefill_set_fused_swiglu: the gate|up product with the activation in its epilogue (128- and 256-wide tiles)
+    against the product followed by the SwiGLU kernel -- same hidden row, same state, same token, bit for bit."""
+    from luce_megakernel_b200 import model as M, lib
+    from luce_megakernel_b200.weights import random_state_dict
+    L = lib()
+    sd = random_state_dict(31, 4, 1024, "unit")
+    dec = M.Decoder(weights=M.weights_from_state_dict(sd), max_seq_len=S + 8, api="cabi")
+    g = torch.Generator().manual_seed(S)
+    ids = torch.randint(0, 1024, (S,), generator=g).to(torch.int32).cuda()
+    outs = []
+    try:
+        for on in (0, 1):
+            L.mk_prefill_set_fused_swiglu(on)
+            dec.reset()
+            tok = dec.prefill(ids)
+            outs.append((tok, dec._hidden_bf16_out.clone(), dec._dn_states.clone(), dec._fa_k_cache.clone()))
+    finally:
+        L.mk_prefill_set_fused_swiglu(1)
+    assert outs[0][0] == outs[1][0]
+    for a, b in zip(outs[0][1:], outs[1][1:]):
+        assert torch.equal(a, b)
+    assert L.mk_prefill_status() == 0
