@@ -358,10 +358,13 @@ void mk_prefill_set_scan_mode(int chunked);
 /* Dense prefill attention kernel: 1 = tcgen05 / TMEM kernel, 0 = mma.sync kernel (the block-sparse mode always
  * uses the mma.sync kernel).  Both compute softmax(q k^T / 16) v * sigmoid(gate). */
 void mk_prefill_set_attention_impl(int tcgen05);
-/* SwiGLU of the MLP (reference: megakernel/prefill.cu:1239-1247): 1 (default) = inside the epilogue of the gate|up
- * product, the [S, 7168] intermediate never reaching memory; 0 = as a kernel of its own after the product.  Both
- * give the same bits (the epilogue rounds the two products to bf16 before the activation); bf16 weights with a
- * fused gate|up matrix only. */
+/* Elementwise steps folded into the projection kernels of the bf16 prefill: 1 = both (default), 0 = kernels of their
+ * own, 2 = SwiGLU only, 3 = RMSNorm only.
+ *   SwiGLU of the MLP (reference: megakernel/prefill.cu:1239-1247) inside the epilogue of the gate|up product, the
+ *   [S, 7168] intermediate never reaching memory (fused gate|up matrix only);
+ *   the RMSNorm after the out / o / down projections (megakernel/prefill.cu:72-88) inside the kernel that adds the
+ *   K parts of those products (prompts short enough for the products to be split along K).
+ * Both settings give the same bits: the folded forms round where the separate kernels read rounded values. */
 void mk_prefill_set_fused_swiglu(int on);
 /* Status word of the prefill kernels on the current device (synchronises the device): 0 = every bounded wait
  * inside the kernels completed; 1 / 2 / 3 = a wait ran out in a GEMM / the chunk scan / the attention kernel

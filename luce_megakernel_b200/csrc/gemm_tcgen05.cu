@@ -305,6 +305,64 @@ __global__ void gemm_splitk_reduce(const float* __restrict__ partial, int ks, co
     *reinterpret_cast<uint4*>(C + (size_t)row * ldc + col) = o;
 }
 
+// The same for N = 1024 with the RMSNorm of the finished row behind it (one block of four warps per row, warp i =
+// columns [256 i, 256 i + 256), 8 per lane): the row is rounded to bf16 and stored, and
+// out = bf16(x rsqrt(mean x^2 + eps) (1 + w)) is computed from the rounded values.  The sum of squares is taken in the
+// order of the prefill's RMSNorm kernel (lane l adds its 32 values chunk after chunk, then a butterfly over the lanes),
+// so the pair gives the bits of the two kernels it replaces (reference: megakernel/prefill.cu:72-88).
+__global__ void __launch_bounds__(128) gemm_splitk_reduce_norm(const float* __restrict__ partial, int ks, const __nv_bfloat16* __restrict__ R,
+                                                              __nv_bfloat16* __restrict__ C, int M, int ldc,
+                                                              const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ normed) {
+    pdl_enter();
+    constexpr int N = 1024;
+    __shared__ float sq[4][8][32];                        // [chunk][element][lane]
+    __shared__ float s_rstd;
+    const int row = blockIdx.x, i = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int col = (i * 32 + lane) * 8;
+    const uint4 wu = __ldg(reinterpret_cast<const uint4*>(w) + i * 32 + lane);
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int p = 0; p < ks; ++p) {
+        const float4* src = reinterpret_cast<const float4*>(partial + ((size_t)p * M + row) * N + col);
+        const float4 a = src[0], b = src[1];
+        f[0] += a.x; f[1] += a.y; f[2] += a.z; f[3] += a.w; f[4] += b.x; f[5] += b.y; f[6] += b.z; f[7] += b.w;
+    }
+    if (R) {
+        const uint4 r4 = *reinterpret_cast<const uint4*>(R + (size_t)row * ldc + col);
+        f[0] += bf_lo(r4.x); f[1] += bf_hi(r4.x); f[2] += bf_lo(r4.y); f[3] += bf_hi(r4.y);
+        f[4] += bf_lo(r4.z); f[5] += bf_hi(r4.z); f[6] += bf_lo(r4.w); f[7] += bf_hi(r4.w);
+    }
+    float v[8];
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 p2 = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+        o[e] = *reinterpret_cast<const uint32_t*>(&p2);
+        v[2 * e] = bf_lo(o[e]); v[2 * e + 1] = bf_hi(o[e]);
+    }
+    *reinterpret_cast<uint4*>(C + (size_t)row * ldc + col) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sq[i][e][lane] = v[e] * v[e];
+    __syncthreads();
+    if (i == 0) {
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss += sq[c][e][lane];
+        ss = warp_sum(ss);
+        if (lane == 0) s_rstd = rsqrtf(ss * (1.0f / N) + RMS_EPS);
+    }
+    __syncthreads();
+    const float rstd = s_rstd;
+    const uint32_t wq[4] = {wu.x, wu.y, wu.z, wu.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 p2 = __floats2bfloat162_rn(v[2 * e] * rstd * (1.0f + bf_lo(wq[e])), v[2 * e + 1] * rstd * (1.0f + bf_hi(wq[e])));
+        o[e] = *reinterpret_cast<const uint32_t*>(&p2);
+    }
+    reinterpret_cast<uint4*>(normed + (size_t)row * N)[i * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
                                   const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -334,7 +392,8 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int k, int ld, int b
 
 template <int BN>
 cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc, int* err_flag,
-                        int sms, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream) {
+                        int sms, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream, const void* norm_w = nullptr,
+                        void* norm_out = nullptr, bool* norm_done = nullptr) {
     static bool attr_done = false;
     if (!attr_done) {
         cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
@@ -357,6 +416,12 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
         float* ws = splitk_ws;
         const int items = ntiles * ks;
         launch_pdl(gemm_bf16_tn_kernel<BN, true>, items < sms ? items : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, nullptr, nullptr, M, N, K, ldc, err_flag, ws, ks, 0);
+        if (norm_w && norm_out && N == 1024) {
+            launch_pdl(gemm_splitk_reduce_norm, (unsigned)M, 128, 0, stream, (const float*)ws, ks, (const __nv_bfloat16*)R,
+                       (__nv_bfloat16*)C, M, ldc, (const __nv_bfloat16*)norm_w, (__nv_bfloat16*)norm_out);
+            if (norm_done) *norm_done = true;
+            return cudaGetLastError();
+        }
         const size_t n = (size_t)M * (N / 8);
         launch_pdl(gemm_splitk_reduce, (unsigned)((n + 255) / 256), 256, 0, stream, ws, ks, (const __nv_bfloat16*)R, (__nv_bfloat16*)C, M, N, ldc);
         return cudaGetLastError();
@@ -402,7 +467,9 @@ cudaError_t gemm_bf16_glu(const void* A, const void* W, void* C, int M, int N, i
 }
 
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
-                         int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream) {
+                         int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream, const void* norm_w,
+                         void* norm_out, bool* norm_done) {
+    if (norm_done) *norm_done = false;
     if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % BK) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(C)) & 15u)
         return cudaErrorInvalidValue;
@@ -417,7 +484,7 @@ cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, i
     // 256-wide tiles once they fill the machine; 128-wide tiles keep more SMs busy on small problems
     const int mt = (M + BM - 1) / BM;
     if (N % 256 == 0 && mt * (N / 256) >= sms) return launch_gemm<256>(A, W, C, R, M, N, K, lda, ldc, err_flag, sms, splitk_ws, splitk_bytes, stream);
-    return launch_gemm<128>(A, W, C, R, M, N, K, lda, ldc, err_flag, sms, splitk_ws, splitk_bytes, stream);
+    return launch_gemm<128>(A, W, C, R, M, N, K, lda, ldc, err_flag, sms, splitk_ws, splitk_bytes, stream, norm_w, norm_out, norm_done);
 }
 
 }  // namespace mk

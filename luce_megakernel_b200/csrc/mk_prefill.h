@@ -25,8 +25,12 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 // err_flag: device int, set to 1 if a bounded wait ran out inside the kernel.
 // splitk_ws / splitk_bytes: caller-owned f32 scratch for the partial products of a K-split (small M, K >= 2048);
 // the split uses as many parts as fit (none when null).  The call allocates nothing.
+// norm_w / norm_out (optional, N = 1024): when the product is split along K, the kernel that adds the parts also
+// writes norm_out = RMSNorm(C) * (1 + norm_w) (the bits of the separate RMSNorm kernel) and sets *norm_done;
+// otherwise *norm_done stays false and the caller normalises C itself.
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
-                         int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream);
+                         int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream,
+                         const void* norm_w = nullptr, void* norm_out = nullptr, bool* norm_done = nullptr);
 // C[M, N] = silu(A . Wg^T) * (A . Wu^T), Wg = rows [0, N) and Wu = rows [glu_off, glu_off + N) of W [*, K]: the SwiGLU
 // of the MLP inside the gate|up product's epilogue (both products rounded to bf16 first, as the separate kernel saw
 // them).  N % 128 == 0, K % 64 == 0.

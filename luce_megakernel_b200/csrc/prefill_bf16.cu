@@ -518,6 +518,7 @@ struct TailCfg { int n = 0; float* running_max = nullptr; };   // tail-attention
 TailCfg g_tail;
 int g_attn_impl = 1;              // attention kernel: 1 = tcgen05 / TMEM (default), 0 = mma.sync
 int g_fuse_glu = 1;               // 1 = SwiGLU in the gate|up product's epilogue (default), 0 = separate kernel
+int g_fuse_norm = 1;              // 1 = RMSNorm in the kernel that adds the K parts of a split product (default), 0 = separate kernel
 int g_scan_mode = 1;              // 1 = chunks of 64 on the tensor cores, 0 = token-serial recurrence
 int pfail(int code, const char* what, cudaError_t e = cudaSuccess) {
     if (e != cudaSuccess) snprintf(g_perr, sizeof(g_perr), "%s: %s", what, cudaGetErrorString(e));
@@ -586,7 +587,10 @@ extern "C" int mk_prefill_status(void) {
     return v;
 }
 extern "C" void mk_prefill_set_attention_impl(int tcgen05) { mk::g_attn_impl = tcgen05 ? 1 : 0; }
-extern "C" void mk_prefill_set_fused_swiglu(int on) { mk::g_fuse_glu = on ? 1 : 0; }
+extern "C" void mk_prefill_set_fused_swiglu(int on) {     // 0 none, 1 both (default), 2 SwiGLU only, 3 RMSNorm only
+    mk::g_fuse_glu = (on == 1 || on == 2) ? 1 : 0;
+    mk::g_fuse_norm = (on == 1 || on == 3) ? 1 : 0;
+}
 extern "C" void mk_prefill_set_tail_scoring(int n_lookahead, float* running_max) {
     mk::g_tail.n = (n_lookahead > 0 && running_max) ? n_lookahead : 0;
     mk::g_tail.running_max = mk::g_tail.n ? running_max : nullptr;
@@ -698,7 +702,10 @@ template <typename LayerSource>
 int prefill_core(const int* token_ids, int seq_len, int* output_token, const void* embed_weight, LayerSource source,
                  int num_layers, const void* final_norm_w, LmView lm, void* fa_k_cache, void* fa_v_cache, void* dn_states,
                  void* conv_bufs, void* final_normed, void* hidden_bf16_out, int max_seq_len, int vocab, int dev,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, bool source_ahead = false) {
+    // source(li, view) is called once per layer, in order.  source_ahead: it may be called for layer li + 1 before the
+    // last projection of layer li is enqueued (it only reads tables; a source that launches work of its own into
+    // scratch shared between layers must not be)
     PrefillWs& w = g_pws[dev];
     PF_CHECK(ensure_ws(w, seq_len, stream, true), "prefill workspace (grow it with mk_prefill_reserve() before capturing a graph)");
     static bool scan_attr[64] = {false};
@@ -710,6 +717,13 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
     typedef __nv_bfloat16 bf;
     auto gemm = [&](const void* A, const void* W, void* C, const void* R, int N, int K, int ldc) {
         return gemm_bf16_tn(A, W, C, R, S, N, K, K, ldc, w.err, w.splitk, w.splitk_bytes, stream);
+    };
+    // a projection into the residual stream followed by the RMSNorm of the result: for short prompts (K-split products)
+    // the norm rides in the kernel that adds the K parts; `normed` says whether w.normed already holds it
+    bool normed = false;
+    auto gemm_norm = [&](const void* A, const void* W, int K, const void* norm_w) {
+        return gemm_bf16_tn(A, W, w.hidden, w.hidden, S, HIDDEN, K, K, HIDDEN, w.err, w.splitk, w.splitk_bytes, stream,
+                            g_fuse_norm ? norm_w : nullptr, w.normed, &normed);
     };
     // NVFP4 x NVFP4: quantise the [S, K] input of the coming projections once (16-element blocks along K, E4M3 block
     // scales, no tensor scale: the quantiser of the reference's LM-head format), then multiply on the block-scaled
@@ -729,12 +743,20 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
     if (tail) PF_CHECK(cudaMemsetAsync(g_tail.running_max, 0, (size_t)g_tail.n * S * sizeof(float), stream), "tail score reset");
     launch_pdl(k_embed, S, 128, 0, stream, token_ids, (const bf*)embed_weight, w.hidden, S, vocab);
     int dn_idx = 0, fa_idx = 0;
+    LayerView ahead;
+    bool have_ahead = false;
     for (int li = 0; li < num_layers; ++li) {
         LayerView lv;
-        const int rc = source(li, lv);
-        if (rc != MK_OK) return rc;
+        if (have_ahead) {
+            lv = ahead;
+            have_ahead = false;
+        } else {
+            const int rc = source(li, lv);
+            if (rc != MK_OK) return rc;
+        }
         const bool dn = (lv.type == 0);
-        launch_pdl(k_rmsnorm, blocks_for_warps(S), 256, 0, stream, w.hidden, (const bf*)lv.in_norm, w.normed, S);
+        if (!normed) launch_pdl(k_rmsnorm, blocks_for_warps(S), 256, 0, stream, w.hidden, (const bf*)lv.in_norm, w.normed, S);
+        normed = false;
         if (dn) {
             float* state = (float*)dn_states + (size_t)dn_idx * DN_HEADS * DN_VAL * DN_KEY;
             float* cstate = (float*)conv_bufs + (size_t)dn_idx * DN_CONV_CH * DN_CONV_K;
@@ -760,7 +782,7 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
                 PF_CHECK(quant(w.act, DN_V), "quantise activations");
                 PF_CHECK(gemm4(lv.x_out, w.hidden, w.hidden, HIDDEN, DN_V, HIDDEN), "gemm out");
             } else {
-                PF_CHECK(gemm(w.act, lv.w_out, w.hidden, w.hidden, HIDDEN, DN_V, HIDDEN), "gemm out");
+                PF_CHECK(gemm_norm(w.act, lv.w_out, DN_V, lv.post_norm), "gemm out");
             }
             ++dn_idx;
         } else {
@@ -795,11 +817,12 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
                 PF_CHECK(quant(w.act, FA_Q_SIZE), "quantise activations");
                 PF_CHECK(gemm4(lv.x_o, w.hidden, w.hidden, HIDDEN, FA_Q_SIZE, HIDDEN), "gemm o");
             } else {
-                PF_CHECK(gemm(w.act, lv.w_o, w.hidden, w.hidden, HIDDEN, FA_Q_SIZE, HIDDEN), "gemm o");
+                PF_CHECK(gemm_norm(w.act, lv.w_o, FA_Q_SIZE, lv.post_norm), "gemm o");
             }
             ++fa_idx;
         }
-        launch_pdl(k_rmsnorm, blocks_for_warps(S), 256, 0, stream, w.hidden, (const bf*)lv.post_norm, w.normed, S);
+        if (!normed) launch_pdl(k_rmsnorm, blocks_for_warps(S), 256, 0, stream, w.hidden, (const bf*)lv.post_norm, w.normed, S);
+        normed = false;
         if (lv.fp4) {
             PF_CHECK(quant(w.normed, HIDDEN), "quantise activations");
             PF_CHECK(gemm4(lv.x_gate, w.wide, nullptr, INTER, HIDDEN, 2 * INTER), "gemm gate");
@@ -819,7 +842,16 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
             PF_CHECK(quant(w.act, INTER), "quantise activations");
             PF_CHECK(gemm4(lv.x_down, w.hidden, w.hidden, HIDDEN, INTER, HIDDEN), "gemm down");
         } else {
-            PF_CHECK(gemm(w.act, lv.w_down, w.hidden, w.hidden, HIDDEN, INTER, HIDDEN), "gemm down");
+            // the next layer's input norm, if there is a next layer
+            const void* next_norm = nullptr;
+            if (source_ahead && li + 1 < num_layers) {
+                ahead = LayerView();
+                const int rn = source(li + 1, ahead);
+                if (rn != MK_OK) return rn;
+                have_ahead = true;
+                next_norm = ahead.in_norm;
+            }
+            PF_CHECK(gemm_norm(w.act, lv.w_down, INTER, next_norm), "gemm down");
         }
     }
     launch_pdl(k_final_norm, 1, 512, 0, stream, w.hidden + (size_t)(S - 1) * HIDDEN, (const bf*)final_norm_w, w.normed_f32,
@@ -898,7 +930,7 @@ extern "C" int mk_prefill_bf16(
     LmView lm;
     lm.bf16 = lm_head_w;
     return prefill_core(token_ids, seq_len, output_token, embed_weight, source, num_layers, final_norm_w, lm, fa_k_cache,
-                        fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out, max_seq_len, vocab, dev, stream);
+                        fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out, max_seq_len, vocab, dev, stream, true);
 }
 
 // bf16 layers, NVFP4 LM head (16-block / E4M3 format) for the first generated token
@@ -925,7 +957,7 @@ extern "C" int mk_prefill_bf16_nvfp4_lm(
     LmView lm;
     lm.packed = lm_head_weight_packed; lm.scales = lm_head_scales;
     return prefill_core(token_ids, seq_len, output_token, embed_weight, source, num_layers, final_norm_w, lm, fa_k_cache,
-                        fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out, max_seq_len, vocab, dev, stream);
+                        fa_v_cache, dn_states, conv_bufs, final_normed, hidden_bf16_out, max_seq_len, vocab, dev, stream, true);
 }
 
 // Prefill on NVFP4 weights (208-byte table): every quantised matrix of a layer is dequantised into bf16 scratch
