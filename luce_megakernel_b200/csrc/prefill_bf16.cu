@@ -85,37 +85,43 @@ __global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bfloat
 // beta = sigmoid(Wb x), decay = exp(g), g = -exp(A_log) softplus(Wa x + dt_bias)  (reference: prefill.cu:91-99, 400-412)
 // gates: [t][head][4] = beta, decay, (q.k, written by the recurrent path's conv kernel), g.
 // One CTA per 16 tokens: [16 x 1024] x [1024 x 32] with mma.sync (columns 0-15 = beta rows of Wb, 16-31 = alpha
-// rows of Wa), the four warps split K, operands read straight from global memory (the 64 KB of gate weights
-// stay in L1), partial sums meet in shared memory.
-__global__ void __launch_bounds__(128) k_dn_gates_mma(const __nv_bfloat16* __restrict__ xn, const __nv_bfloat16* __restrict__ Wb,
+// rows of Wa), eight warps split K and each requests its whole eighth of both operands before the first product
+// (the kernel is one memory round trip long, not one per k-step); operands straight from global memory (the 64 KB
+// of gate weights stay in L1 / L2), partial sums meet in shared memory.
+__global__ void __launch_bounds__(256) k_dn_gates_mma(const __nv_bfloat16* __restrict__ xn, const __nv_bfloat16* __restrict__ Wb,
                                                       const __nv_bfloat16* __restrict__ Wa, const __nv_bfloat16* __restrict__ a_log,
                                                       const __nv_bfloat16* __restrict__ dt_bias, float* __restrict__ gates, int S) {
     pdl_enter();
-    __shared__ float part[4][16][33];
+    __shared__ float part[8][16][33];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g8 = lane >> 2, t4 = lane & 3;
     const int t0 = blockIdx.x * 16;
     const int r0 = min(t0 + g8, S - 1), r1 = min(t0 + g8 + 8, S - 1);        // rows past the prompt repeat the last one
-    const uint32_t* x0 = reinterpret_cast<const uint32_t*>(xn + (size_t)r0 * HIDDEN) + warp * 128 + t4;
-    const uint32_t* x1 = reinterpret_cast<const uint32_t*>(xn + (size_t)r1 * HIDDEN) + warp * 128 + t4;
+    const uint32_t* x0 = reinterpret_cast<const uint32_t*>(xn + (size_t)r0 * HIDDEN) + warp * 64 + t4;
+    const uint32_t* x1 = reinterpret_cast<const uint32_t*>(xn + (size_t)r1 * HIDDEN) + warp * 64 + t4;
     // B fragment of n-tile n: column g8 = output row 8 n + g8 of [Wb ; Wa]
     const uint32_t* wrow[4];
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
         const int o = n * 8 + g8;
-        wrow[n] = reinterpret_cast<const uint32_t*>((o < 16 ? Wb + (size_t)o * HIDDEN : Wa + (size_t)(o - 16) * HIDDEN)) + warp * 128 + t4;
+        wrow[n] = reinterpret_cast<const uint32_t*>((o < 16 ? Wb + (size_t)o * HIDDEN : Wa + (size_t)(o - 16) * HIDDEN)) + warp * 64 + t4;
     }
     float acc[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n) { acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f; }
-#pragma unroll 4
-    for (int ks = 0; ks < 16; ++ks) {                       // this warp's quarter of K: 256 elements
-        const uint32_t a0 = x0[ks * 8], a1 = x1[ks * 8], a2 = x0[ks * 8 + 4], a3 = x1[ks * 8 + 4];
+    uint32_t a[8][4], b[8][4][2];                           // this warp's eighth of K: 128 elements = 8 k-steps
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+        a[ks][0] = x0[ks * 8]; a[ks][1] = x1[ks * 8]; a[ks][2] = x0[ks * 8 + 4]; a[ks][3] = x1[ks * 8 + 4];
+#pragma unroll
+        for (int n = 0; n < 4; ++n) { b[ks][n][0] = __ldg(wrow[n] + ks * 8); b[ks][n][1] = __ldg(wrow[n] + ks * 8 + 4); }
+    }
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
-            const uint32_t b0 = __ldg(wrow[n] + ks * 8), b1 = __ldg(wrow[n] + ks * 8 + 4);
             asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                          : "+f"(acc[n][0]), "+f"(acc[n][1]), "+f"(acc[n][2]), "+f"(acc[n][3])
-                         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+                         : "r"(a[ks][0]), "r"(a[ks][1]), "r"(a[ks][2]), "r"(a[ks][3]), "r"(b[ks][n][0]), "r"(b[ks][n][1]));
         }
     }
 #pragma unroll
@@ -124,10 +130,11 @@ __global__ void __launch_bounds__(128) k_dn_gates_mma(const __nv_bfloat16* __res
         for (int e = 0; e < 4; ++e) part[warp][g8 + (e >> 1) * 8][n * 8 + 2 * t4 + (e & 1)] = acc[n][e];
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < 16 * 32; i += 128) {
+    for (int i = threadIdx.x; i < 16 * 32; i += 256) {
         const int tt = i >> 5, o = i & 31, t = t0 + tt;
         if (t >= S) continue;
-        const float v = (part[0][tt][o] + part[1][tt][o]) + (part[2][tt][o] + part[3][tt][o]);
+        const float v = ((part[0][tt][o] + part[1][tt][o]) + (part[2][tt][o] + part[3][tt][o])) +
+                        ((part[4][tt][o] + part[5][tt][o]) + (part[6][tt][o] + part[7][tt][o]));
         if (o < 16) gates[((size_t)t * 16 + o) * 4] = 1.0f / (1.0f + expf(-v));
         else {
             const int h = o - 16;
@@ -768,7 +775,7 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
                 PF_CHECK(gemm(w.normed, lv.w_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
                 PF_CHECK(gemm(w.normed, lv.w_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
             }
-            launch_pdl(k_dn_gates_mma, (unsigned)((S + 15) / 16), 128, 0, stream, w.normed, (const bf*)lv.w_b, (const bf*)lv.w_a,
+            launch_pdl(k_dn_gates_mma, (unsigned)((S + 15) / 16), 256, 0, stream, w.normed, (const bf*)lv.w_b, (const bf*)lv.w_a,
                        (const bf*)lv.a_log, (const bf*)lv.dt_bias, w.beta, S);
             if (g_scan_mode == 0) {
                 launch_pdl(k_dn_preproject, dim3(S, DN_HEADS), 128, 0, stream, w.wide, (const bf*)lv.conv_w, cstate, w.pre, w.beta, S);
