@@ -363,7 +363,9 @@ void mk_prefill_set_attention_impl(int tcgen05);
  *   SwiGLU of the MLP (reference: megakernel/prefill.cu:1239-1247) inside the epilogue of the gate|up product, the
  *   [S, 7168] intermediate never reaching memory (fused gate|up matrix only);
  *   the RMSNorm after the out / o / down projections (megakernel/prefill.cu:72-88) inside the kernel that adds the
- *   K parts of those products (prompts short enough for the products to be split along K).
+ *   K parts of those products (prompts short enough for the products to be split along K);
+ *   with the SwiGLU setting, the qkv and the z projection of a DeltaNet layer also run as one launch over both weight
+ *   matrices (the tiles of the two products, side by side).
  * Both settings give the same bits: the folded forms round where the separate kernels read rounded values. */
 void mk_prefill_set_fused_swiglu(int on);
 /* Status word of the prefill kernels on the current device (synchronises the device): 0 = every bounded wait

@@ -88,7 +88,10 @@ template <int BN, bool SPLIT, bool GLU = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                     __nv_bfloat16* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc,
-                    int* err, float* __restrict__ partial, int ks, int glu_off) {
+                    int* err, float* __restrict__ partial, int ks, int glu_off,
+                    const __grid_constant__ CUtensorMap map_w2, __nv_bfloat16* __restrict__ C2, int n_split, int ldc2) {
+    // n_split > 0: two products that share A in one launch -- output columns [0, n_split) come from map_w into C,
+    // columns [n_split, N) from map_w2 into C2 (row pitch ldc2); no residual, no K split
     constexpr int BNO = GLU ? BN / 2 : BN;                // output columns per tile
     // the next kernel may be scheduled now; this one sets up barriers and tensor memory while its predecessor
     // drains and waits for it (griddepcontrol.wait below) before the first operand is read
@@ -142,7 +145,10 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
                     if (!ok) break;
                     mbar_expect_tx(full0 + 8 * s, G::STAGE_BYTES);
                     tma_load_2d(a0 + s * TILE_A_BYTES, &map_a, kb * BK, m0, full0 + 8 * s);
-                    tma_load_2d(b0 + s * G::TILE_B_BYTES, &map_w, kb * BK, n0, full0 + 8 * s);
+                    if (!GLU && !SPLIT && n_split > 0 && n0 >= n_split)
+                        tma_load_2d(b0 + s * G::TILE_B_BYTES, &map_w2, kb * BK, n0 - n_split, full0 + 8 * s);
+                    else
+                        tma_load_2d(b0 + s * G::TILE_B_BYTES, &map_w, kb * BK, n0, full0 + 8 * s);
                     if (GLU) tma_load_2d(b0 + s * G::TILE_B_BYTES + BNO * BK * 2, &map_w, kb * BK, glu_off + n0, full0 + 8 * s);
                 }
             }
@@ -243,7 +249,8 @@ gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
                                                  __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
                     }
                 } else if (row < M) {
-                    __nv_bfloat16* dst = C + (size_t)row * ldc + n0 + c0;
+                    const bool second = n_split > 0 && n0 >= n_split;
+                    __nv_bfloat16* dst = second ? C2 + (size_t)row * ldc2 + (n0 - n_split) + c0 : C + (size_t)row * ldc + n0 + c0;
                     const __nv_bfloat16* res = R ? R + (size_t)row * ldc + n0 + c0 : nullptr;
 #pragma unroll
                     for (int j = 0; j < 32; j += 8) {
@@ -415,7 +422,7 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
     if (BN == 128 && ks >= 2 && K >= 2048) {      // only the long-K projections: K = 1024 products keep one summation order
         float* ws = splitk_ws;
         const int items = ntiles * ks;
-        launch_pdl(gemm_bf16_tn_kernel<BN, true>, items < sms ? items : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, nullptr, nullptr, M, N, K, ldc, err_flag, ws, ks, 0);
+        launch_pdl(gemm_bf16_tn_kernel<BN, true>, items < sms ? items : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, nullptr, nullptr, M, N, K, ldc, err_flag, ws, ks, 0, ma, nullptr, 0, 0);
         if (norm_w && norm_out && N == 1024) {
             launch_pdl(gemm_splitk_reduce_norm, (unsigned)M, 128, 0, stream, (const float*)ws, ks, (const __nv_bfloat16*)R,
                        (__nv_bfloat16*)C, M, ldc, (const __nv_bfloat16*)norm_w, (__nv_bfloat16*)norm_out);
@@ -426,7 +433,7 @@ cudaError_t launch_gemm(const void* A, const void* W, void* C, const void* R, in
         launch_pdl(gemm_splitk_reduce, (unsigned)((n + 255) / 256), 256, 0, stream, ws, ks, (const __nv_bfloat16*)R, (__nv_bfloat16*)C, M, N, ldc);
         return cudaGetLastError();
     }
-    launch_pdl(gemm_bf16_tn_kernel<BN, false>, ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K, ldc, err_flag, nullptr, 1, 0);
+    launch_pdl(gemm_bf16_tn_kernel<BN, false>, ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw, (__nv_bfloat16*)C, (const __nv_bfloat16*)R, M, N, K, ldc, err_flag, nullptr, 1, 0, ma, nullptr, 0, 0);
     return cudaGetLastError();
 }
 
@@ -443,11 +450,48 @@ cudaError_t launch_gemm_glu(const void* A, const void* W, void* C, int M, int N,
     if (!make_map(&ma, A, M, K, lda, BM) || !make_map(&mw, W, glu_off + N, K, K, BN / 2)) return cudaErrorInvalidValue;
     const int ntiles = ((M + BM - 1) / BM) * (N / (BN / 2));
     launch_pdl(gemm_bf16_tn_kernel<BN, false, true>, ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw,
-               (__nv_bfloat16*)C, (const __nv_bfloat16*)nullptr, M, N, K, ldc, err_flag, (float*)nullptr, 1, glu_off);
+               (__nv_bfloat16*)C, (const __nv_bfloat16*)nullptr, M, N, K, ldc, err_flag, (float*)nullptr, 1, glu_off, ma, (__nv_bfloat16*)nullptr, 0, 0);
     return cudaGetLastError();
 }
 
 }  // namespace
+
+template <int BN>
+cudaError_t launch_gemm_dual(const void* A, const void* W1, void* C1, int N1, int ldc1, const void* W2, void* C2, int N2, int ldc2,
+                             int M, int K, int lda, int* err_flag, int sms, cudaStream_t stream) {
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM);
+        if (e != cudaSuccess) return e;
+        attr_done = true;
+    }
+    CUtensorMap ma, mw1, mw2;
+    if (!make_map(&ma, A, M, K, lda, BM) || !make_map(&mw1, W1, N1, K, K, BN) || !make_map(&mw2, W2, N2, K, K, BN))
+        return cudaErrorInvalidValue;
+    const int ntiles = ((M + BM - 1) / BM) * ((N1 + N2) / BN);
+    launch_pdl(gemm_bf16_tn_kernel<BN, false>, ntiles < sms ? ntiles : sms, GEMM_THREADS, Cfg<BN>::SMEM, stream, ma, mw1, (__nv_bfloat16*)C1,
+               (const __nv_bfloat16*)nullptr, M, N1 + N2, K, ldc1, err_flag, (float*)nullptr, 1, 0, mw2, (__nv_bfloat16*)C2, N1, ldc2);
+    return cudaGetLastError();
+}
+
+// Two products that share their left operand in one launch: C1[M, N1] = A . W1^T and C2[M, N2] = A . W2^T (the qkv and
+// the z projection of a DeltaNet layer).  The tiles are the tiles of the two separate products, so are the bits.
+cudaError_t gemm_bf16_tn_dual(const void* A, const void* W1, void* C1, int N1, int ldc1, const void* W2, void* C2, int N2, int ldc2,
+                              int M, int K, int lda, int* err_flag, cudaStream_t stream) {
+    if (M <= 0 || N1 <= 0 || N2 <= 0 || K <= 0 || N1 % 256 || N2 % 256 || K % BK) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W1) | reinterpret_cast<uintptr_t>(W2) |
+         reinterpret_cast<uintptr_t>(C1) | reinterpret_cast<uintptr_t>(C2)) & 15u)
+        return cudaErrorInvalidValue;
+    if ((lda % 8) || (ldc1 % 8) || (ldc2 % 8)) return cudaErrorInvalidValue;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    const int mt = (M + BM - 1) / BM;
+    if (mt * ((N1 + N2) / 256) >= sms)
+        return launch_gemm_dual<256>(A, W1, C1, N1, ldc1, W2, C2, N2, ldc2, M, K, lda, err_flag, sms, stream);
+    return launch_gemm_dual<128>(A, W1, C1, N1, ldc1, W2, C2, N2, ldc2, M, K, lda, err_flag, sms, stream);
+}
 
 // C[M, N] = silu(A . Wg^T) * (A . Wu^T) with Wg = rows [0, N) and Wu = rows [glu_off, glu_off + N) of W, both
 // products rounded to bf16 before the activation.  N % 128 == 0.

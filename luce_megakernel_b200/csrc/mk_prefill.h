@@ -31,6 +31,9 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 cudaError_t gemm_bf16_tn(const void* A, const void* W, void* C, const void* R, int M, int N, int K, int lda, int ldc,
                          int* err_flag, float* splitk_ws, size_t splitk_bytes, cudaStream_t stream,
                          const void* norm_w = nullptr, void* norm_out = nullptr, bool* norm_done = nullptr);
+// C1[M, N1] = A . W1^T and C2[M, N2] = A . W2^T in one launch (same tiles, same bits as two calls).  N1, N2 % 256 == 0.
+cudaError_t gemm_bf16_tn_dual(const void* A, const void* W1, void* C1, int N1, int ldc1, const void* W2, void* C2, int N2, int ldc2,
+                              int M, int K, int lda, int* err_flag, cudaStream_t stream);
 // C[M, N] = silu(A . Wg^T) * (A . Wu^T), Wg = rows [0, N) and Wu = rows [glu_off, glu_off + N) of W [*, K]: the SwiGLU
 // of the MLP inside the gate|up product's epilogue (both products rounded to bf16 first, as the separate kernel saw
 // them).  N % 128 == 0, K % 64 == 0.

@@ -772,8 +772,13 @@ int prefill_core(const int* token_ids, int seq_len, int* output_token, const voi
                 PF_CHECK(gemm4(lv.x_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
                 PF_CHECK(gemm4(lv.x_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
             } else {
-                PF_CHECK(gemm(w.normed, lv.w_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
-                PF_CHECK(gemm(w.normed, lv.w_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
+                if (g_fuse_glu) {          // the qkv and the z projection as one launch over both weight matrices
+                    PF_CHECK(gemm_bf16_tn_dual(w.normed, lv.w_qkv, w.wide, DN_CONV_CH, DN_CONV_CH, lv.w_z, w.z, DN_V, DN_V, S, HIDDEN, HIDDEN,
+                                               w.err, stream), "gemm qkv + z");
+                } else {
+                    PF_CHECK(gemm(w.normed, lv.w_qkv, w.wide, nullptr, DN_CONV_CH, HIDDEN, DN_CONV_CH), "gemm qkv");
+                    PF_CHECK(gemm(w.normed, lv.w_z, w.z, nullptr, DN_V, HIDDEN, DN_V), "gemm z");
+                }
             }
             launch_pdl(k_dn_gates_mma, (unsigned)((S + 15) / 16), 256, 0, stream, w.normed, (const bf*)lv.w_b, (const bf*)lv.w_a,
                        (const bf*)lv.a_log, (const bf*)lv.dt_bias, w.beta, S);
