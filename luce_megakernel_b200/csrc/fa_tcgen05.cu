@@ -1,7 +1,8 @@
 // Causal GQA attention for prefill on the 5th-generation tensor cores (dense mode).
 //
 // One CTA = 32 consecutive query positions x the 4 query heads of one KV head = 128 rows, one row per TMEM lane.
-//   warp 0      TMA: the Q tile once, then K/V tiles of 64 keys into a two-stage ring (128-byte swizzle)
+//   warp 0      TMA: the Q tile once, then K tiles (lane 0) and V tiles (lane 1) of 64 keys into two-stage rings with
+//               barriers of their own (128-byte swizzle)
 //   warp 1      one thread issues tcgen05.mma: S = Q K^T (M128 N64, K = 256 in 16 steps) into one of two score
 //               buffers in tensor memory, and O += P V (M128 N256, K = 64 in 4 steps; V is read MN-major, i.e.
 //               as it lies in the cache: keys x dims)
@@ -63,6 +64,14 @@ __device__ __forceinline__ void mma5(uint32_t d, uint64_t a, uint64_t b, uint32_
     asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
                  ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc) : "memory");
 }
+// 2^x on the special-function unit alone (exp2f wraps the same instruction in a range fix-up for denormal results,
+// four more instructions per probability; results below 2^-126 are flushed to zero, which is what a probability that
+// small rounds to in bf16 anyway)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ void commit5(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -118,8 +127,11 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sb = smem_u32(smem);
     const uint32_t bars = sb + OFF_BARS;
-    const uint32_t q_full = bars, kv_full0 = bars + 8, kv_empty0 = bars + 24, s_full0 = bars + 40, s_empty0 = bars + 56,
-                   p_full = bars + 72, pv_done = bars + 80;
+    // K and V stages have barriers of their own: a K stage is free as soon as the score MMA that read it is done (one
+    // tile earlier than the V stage of the same tile), so the next K tile is requested that much sooner -- with one pair
+    // of barriers for both, every score MMA waited for a K tile that had been requested only when the previous P V ended.
+    const uint32_t q_full = bars, k_full0 = bars + 8, k_empty0 = bars + 24, s_full0 = bars + 40, s_empty0 = bars + 56,
+                   p_full = bars + 72, pv_done = bars + 80, v_full0 = bars + 120, v_empty0 = bars + 136;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BARS + 96);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qblk = gridDim.x - 1 - blockIdx.x, g = blockIdx.y;
@@ -155,7 +167,8 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int s = 0; s < 2; ++s) {
-            mbar_init(kv_full0 + 8 * s, 1); mbar_init(kv_empty0 + 8 * s, 1);
+            mbar_init(k_full0 + 8 * s, 1); mbar_init(k_empty0 + 8 * s, 1);
+            mbar_init(v_full0 + 8 * s, 1); mbar_init(v_empty0 + 8 * s, 1);
             mbar_init(s_full0 + 8 * s, 1); mbar_init(s_empty0 + 8 * s, 256);
         }
         mbar_init(p_full, 256); mbar_init(pv_done, 1);
@@ -180,17 +193,24 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
             for (int hh = 0; hh < 4; ++hh)
                 for (int b = 0; b < 4; ++b)
                     tma2d(sb + OFF_Q + b * (128 * 128) + hh * (32 * 128), &map_q, (g * 4 + hh) * 512 + b * 64, q0, q_full);
+            const CUtensorMap* mk_ = g ? &map_k1 : &map_k0;
             for (int j = 0; j < ntiles && ok; ++j) {
                 const int s = j & 1;
-                ok = waitb(kv_empty0 + 8 * s, ((j >> 1) & 1) ^ 1u, err);
+                ok = waitb(k_empty0 + 8 * s, ((j >> 1) & 1) ^ 1u, err);
                 if (!ok) break;
-                mbar_expect_tx(kv_full0 + 8 * s, 2 * KV_BYTES);
-                const CUtensorMap* mk_ = g ? &map_k1 : &map_k0;
-                const CUtensorMap* mv_ = g ? &map_v1 : &map_v0;
-                for (int b = 0; b < 4; ++b) {
-                    tma2d(sb + OFF_K + s * KV_BYTES + b * (TK * 128), mk_, b * 64, tile_of(j) * TK, kv_full0 + 8 * s);
-                    tma2d(sb + OFF_V + s * KV_BYTES + b * (TK * 128), mv_, b * 64, tile_of(j) * TK, kv_full0 + 8 * s);
-                }
+                mbar_expect_tx(k_full0 + 8 * s, KV_BYTES);
+                for (int b = 0; b < 4; ++b)
+                    tma2d(sb + OFF_K + s * KV_BYTES + b * (TK * 128), mk_, b * 64, tile_of(j) * TK, k_full0 + 8 * s);
+            }
+        } else if (lane == 1) {          // the V tiles go through a second thread: a wait for a V stage never delays a K request
+            const CUtensorMap* mv_ = g ? &map_v1 : &map_v0;
+            for (int j = 0; j < ntiles && ok; ++j) {
+                const int s = j & 1;
+                ok = waitb(v_empty0 + 8 * s, ((j >> 1) & 1) ^ 1u, err);
+                if (!ok) break;
+                mbar_expect_tx(v_full0 + 8 * s, KV_BYTES);
+                for (int b = 0; b < 4; ++b)
+                    tma2d(sb + OFF_V + s * KV_BYTES + b * (TK * 128), mv_, b * 64, tile_of(j) * TK, v_full0 + 8 * s);
             }
         }
     } else if (warp == 1) {
@@ -204,8 +224,9 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
                     mma5(tmem + TM_S0 + s * TK, desc_k(qb + (ks >> 2) * (128 * 128) + (ks & 3) * 32),
                          desc_k(kb + (ks >> 2) * (TK * 128) + (ks & 3) * 32), id_s, ks ? 1u : 0u);
                 commit5(s_full0 + 8 * s);
+                commit5(k_empty0 + 8 * s);
             };
-            ok = waitb(q_full, 0, err) && waitb(kv_full0, 0, err);
+            ok = waitb(q_full, 0, err) && waitb(k_full0, 0, err);
             if (ok) {
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 issue_s(0);
@@ -214,20 +235,20 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
                 const int s = j & 1;
                 if (j + 1 < ntiles) {
                     const int s1 = (j + 1) & 1;
-                    ok = waitb(kv_full0 + 8 * s1, ((j + 1) >> 1) & 1, err);
+                    ok = waitb(k_full0 + 8 * s1, ((j + 1) >> 1) & 1, err);
                     if (ok && j >= 1) ok = waitb(s_empty0 + 8 * s1, ((j - 1) >> 1) & 1, err);   // scores of tile j-1 were read
                     if (!ok) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     issue_s(j + 1);
                 }
-                ok = waitb(p_full, j & 1, err);
+                ok = waitb(v_full0 + 8 * s, (j >> 1) & 1, err) && waitb(p_full, j & 1, err);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t pb = sb + OFF_P, vb = sb + OFF_V + s * KV_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
                     mma5(tmem + TM_O, desc_k(pb + kk * 32), desc_mn(vb + kk * (16 * 128), TK * 128), id_o, (j | kk) ? 1u : 0u);
-                commit5(kv_empty0 + 8 * s);
+                commit5(v_empty0 + 8 * s);
                 commit5(pv_done);
             }
         }
@@ -301,8 +322,8 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float p0 = exp2f(__uint_as_float(v[c4 * 8 + 2 * e]) - m_ref);
-                    const float p1 = exp2f(__uint_as_float(v[c4 * 8 + 2 * e + 1]) - m_ref);
+                    const float p0 = ex2_approx(__uint_as_float(v[c4 * 8 + 2 * e]) - m_ref);
+                    const float p1 = ex2_approx(__uint_as_float(v[c4 * 8 + 2 * e + 1]) - m_ref);
                     const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
                     w[e] = *reinterpret_cast<const uint32_t*>(&pp);
                     lsum += bf_lo(w[e]) + bf_hi(w[e]);
