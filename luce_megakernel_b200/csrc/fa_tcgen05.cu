@@ -41,6 +41,7 @@ constexpr int OFF_LIST = OFF_BARS + 160 + 2048;            // after the barriers
 constexpr int FA5_SMEM = OFF_LIST + 4096 + 1024;           // + alignment slack
 constexpr uint32_t TM_COLS = 512;
 constexpr uint32_t TM_S0 = 0, TM_O = 128;                  // score buffers at columns 0 and 64, output at 128..383
+constexpr uint32_t TM_P = 384;                             // probabilities, bf16 pairs: two buffers of 32 columns (64 keys)
 
 __device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
@@ -72,6 +73,15 @@ __device__ __forceinline__ float ex2_approx(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+// the same with the A operand in tensor memory (row = lane, two bf16 of consecutive k per 32-bit column)
+__device__ __forceinline__ void mma5_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+                 ::"r"(d), "r"(a_tmem), "l"(b), "r"(id), "r"(acc) : "memory");
+}
+#define TM_ST16(taddr, v)                                                                                              \
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"                  \
+                 ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),           \
+                   "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]) : "memory")
 __device__ __forceinline__ void commit5(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -131,7 +141,8 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
     // tile earlier than the V stage of the same tile), so the next K tile is requested that much sooner -- with one pair
     // of barriers for both, every score MMA waited for a K tile that had been requested only when the previous P V ended.
     const uint32_t q_full = bars, k_full0 = bars + 8, k_empty0 = bars + 24, s_full0 = bars + 40, s_empty0 = bars + 56,
-                   p_full = bars + 72, pv_done = bars + 80, v_full0 = bars + 120, v_empty0 = bars + 136;
+                   p_full = bars + 72, pv_done0 = bars + 80, v_full0 = bars + 120, v_empty0 = bars + 136;
+    // pv_done0 + 8 (j & 1): the P V product of tile j is complete (one barrier per probability buffer)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BARS + 96);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qblk = gridDim.x - 1 - blockIdx.x, g = blockIdx.y;
@@ -171,7 +182,7 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
             mbar_init(v_full0 + 8 * s, 1); mbar_init(v_empty0 + 8 * s, 1);
             mbar_init(s_full0 + 8 * s, 1); mbar_init(s_empty0 + 8 * s, 256);
         }
-        mbar_init(p_full, 256); mbar_init(pv_done, 1);
+        mbar_init(p_full, 256); mbar_init(pv_done0, 1); mbar_init(pv_done0 + 8, 1);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -244,12 +255,12 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
                 ok = waitb(v_full0 + 8 * s, (j >> 1) & 1, err) && waitb(p_full, j & 1, err);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t pb = sb + OFF_P, vb = sb + OFF_V + s * KV_BYTES;
+                const uint32_t vb = sb + OFF_V + s * KV_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma5(tmem + TM_O, desc_k(pb + kk * 32), desc_mn(vb + kk * (16 * 128), TK * 128), id_o, (j | kk) ? 1u : 0u);
+                for (int kk = 0; kk < 4; ++kk)   // 16 keys = 8 columns of the probability buffer per step
+                    mma5_ta(tmem + TM_O, tmem + TM_P + (uint32_t)s * 32 + kk * 8, desc_mn(vb + kk * (16 * 128), TK * 128), id_o, (j | kk) ? 1u : 0u);
                 commit5(v_empty0 + 8 * s);
-                commit5(pv_done);
+                commit5(pv_done0 + 8 * s);
             }
         }
     } else {
@@ -290,9 +301,9 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
             xmax[half * 128 + r] = hmax;
             named_bar_sync(1, 256);
             const float tmax = fmaxf(hmax, xmax[(half ^ 1) * 128 + r]);
-            // the previous P V must be complete before P is overwritten or O rescaled
-            if (j >= 1) {
-                wait_all(pv_done, (j - 1) & 1);
+            // the probability buffer of this parity was last read by the P V of tile j - 2
+            if (j >= 2) {
+                wait_all(pv_done0 + 8 * s, ((j - 2) >> 1) & 1);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             }
             // tcgen05.ld / st are warp-wide: the decision to rescale is taken per warp, every lane takes part
@@ -300,6 +311,9 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
             const bool grow = tmax > m_ref + 8.0f;
             if (__any_sync(0xffffffffu, grow)) {
                 if (j >= 1) {
+                    // the output accumulator is rescaled in place: every P V issued so far must be complete
+                    wait_all(pv_done0 + 8 * (s ^ 1), ((j - 1) >> 1) & 1);
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const float f = grow ? exp2f(m_ref - tmax) : 1.0f;
                     lsum *= f;
 #pragma unroll 1
@@ -315,27 +329,23 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
                 }
                 if (grow) m_ref = tmax;
             }
-            // probabilities -> bf16 half row of the P tile (128-byte rows, 16-byte pieces xor (row & 7))
-            char* prow = smem + OFF_P + r * 128;
+            // probabilities -> bf16 pairs into this thread's 16 columns of the tensor-memory buffer (the A operand of P V)
+            uint32_t w[16];
 #pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float p0 = ex2_approx(__uint_as_float(v[c4 * 8 + 2 * e]) - m_ref);
-                    const float p1 = ex2_approx(__uint_as_float(v[c4 * 8 + 2 * e + 1]) - m_ref);
-                    const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                    w[e] = *reinterpret_cast<const uint32_t*>(&pp);
-                    lsum += bf_lo(w[e]) + bf_hi(w[e]);
-                }
-                *reinterpret_cast<uint4*>(prow + (((half * 4 + c4) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int e = 0; e < 16; ++e) {
+                const float p0 = ex2_approx(__uint_as_float(v[2 * e]) - m_ref);
+                const float p1 = ex2_approx(__uint_as_float(v[2 * e + 1]) - m_ref);
+                const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                w[e] = *reinterpret_cast<const uint32_t*>(&pp);
+                lsum += bf_lo(w[e]) + bf_hi(w[e]);
             }
-            fence_proxy_async();
+            TM_ST16(lane_addr + TM_P + (uint32_t)s * 32 + half * 16, w);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(p_full);
         }
         // epilogue: O / l * sigmoid(gate) -> bf16; the row sum is the two halves' sums
-        wait_all(pv_done, (ntiles - 1) & 1);
+        wait_all(pv_done0 + 8 * ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1);
         float* xsum = xbuf + (ntiles & 1) * 256;
         xsum[half * 128 + r] = lsum;
         named_bar_sync(1, 256);
