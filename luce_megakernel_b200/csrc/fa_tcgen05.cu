@@ -141,7 +141,11 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
     // tile earlier than the V stage of the same tile), so the next K tile is requested that much sooner -- with one pair
     // of barriers for both, every score MMA waited for a K tile that had been requested only when the previous P V ended.
     const uint32_t q_full = bars, k_full0 = bars + 8, k_empty0 = bars + 24, s_full0 = bars + 40, s_empty0 = bars + 56,
-                   p_full = bars + 72, pv_done0 = bars + 80, v_full0 = bars + 120, v_empty0 = bars + 136;
+                   pv_done0 = bars + 80, v_full0 = bars + 120, v_empty0 = bars + 136;
+    // p_full(b): the probabilities of a tile are in buffer b.  One barrier per buffer: with a single barrier, the softmax
+    // threads -- which may run a whole tile ahead of the P V product -- could complete the next phase before the MMA
+    // thread has looked at this one (it waits for the V tile first), and a parity wait cannot tell phase j from j + 2.
+    auto p_full = [&](int b) { return b ? bars + 152 : bars + 72; };
     // pv_done0 + 8 (j & 1): the P V product of tile j is complete (one barrier per probability buffer)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BARS + 96);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -182,7 +186,7 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
             mbar_init(v_full0 + 8 * s, 1); mbar_init(v_empty0 + 8 * s, 1);
             mbar_init(s_full0 + 8 * s, 1); mbar_init(s_empty0 + 8 * s, 256);
         }
-        mbar_init(p_full, 256); mbar_init(pv_done0, 1); mbar_init(pv_done0 + 8, 1);
+        mbar_init(p_full(0), 256); mbar_init(p_full(1), 256); mbar_init(pv_done0, 1); mbar_init(pv_done0 + 8, 1);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -252,7 +256,7 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     issue_s(j + 1);
                 }
-                ok = waitb(v_full0 + 8 * s, (j >> 1) & 1, err) && waitb(p_full, j & 1, err);
+                ok = waitb(v_full0 + 8 * s, (j >> 1) & 1, err) && waitb(p_full(s), (j >> 1) & 1, err);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t vb = sb + OFF_V + s * KV_BYTES;
@@ -342,7 +346,7 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
             TM_ST16(lane_addr + TM_P + (uint32_t)s * 32 + half * 16, w);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            mbar_arrive(p_full);
+            mbar_arrive(p_full(s));
         }
         // epilogue: O / l * sigmoid(gate) -> bf16; the row sum is the two halves' sums
         wait_all(pv_done0 + 8 * ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1);
