@@ -2,15 +2,18 @@
 //
 // One CTA = 32 consecutive query positions x the 4 query heads of one KV head = 128 rows, one row per TMEM lane.
 //   warp 0      TMA: the Q tile once, then K tiles (lane 0) and V tiles (lane 1) of 64 keys into two-stage rings with
-//               barriers of their own (128-byte swizzle)
-//   warp 1      one thread issues tcgen05.mma: S = Q K^T (M128 N64, K = 256 in 16 steps) into one of two score
-//               buffers in tensor memory, and O += P V (M128 N256, K = 64 in 4 steps; V is read MN-major, i.e.
-//               as it lies in the cache: keys x dims)
-//   warps 2-9   softmax, two threads per row (warps 2-5 take score columns 0-31, warps 6-9 columns 32-63 of the
-//               same TMEM lanes): tcgen05.ld the scores, running maximum (exchanged through shared memory) and
-//               sum, probabilities rounded to bf16 into shared memory (the A operand of P V), and the epilogue
-// The score MMA of tile j+1 is issued before the P V MMA of tile j, so the tensor pipe works while the softmax
-// threads process tile j.  The output accumulator is rescaled only when a row maximum grows by more than 2^8
+//               barriers of their own (128-byte swizzle); the two K stages are rows 0-63 / 64-127 of one operand
+//   warp 1      one thread issues tcgen05.mma: S = Q K^T for a PAIR of tiles at once (M128 N128, K = 256 in 16
+//               steps, over both K stages into the two adjacent score buffers in tensor memory; a lone last tile
+//               M128 N64), and O += P V per tile (M128 N256, K = 64 in 4 steps; P is read from tensor memory, V
+//               MN-major, i.e. as it lies in the cache: keys x dims)
+//   warps 2-9   softmax, two threads per row (warps 2-5 take score columns 0-31, warps 6-9 columns 32-63 of each
+//               tile, same TMEM lanes), two tiles per pass: tcgen05.ld the scores, running maximum (exchanged
+//               through shared memory) and sum, probabilities rounded to bf16 pairs into one of four buffers in
+//               tensor memory (the A operand of P V), and the epilogue
+// The score MMAs of the next pair are issued before the P V MMAs of this pair (their buffers are free as soon as the
+// softmax has loaded this pair's scores), so the tensor pipe works while the softmax threads process the pair.  The
+// output accumulator is rescaled only when a row maximum grows by more than 2^8
 // since the last rescale (probabilities then stay below 2^8, exact enough in bf16/f32): with a causal mask the
 // maximum settles after the first tiles, so the TMEM round trip of a rescale is rare.
 // Every wait is bounded; on expiry the kernel sets *err and leaves.
@@ -36,12 +39,13 @@ constexpr int OFF_K = OFF_Q + Q_BYTES;                     // 2 stages
 constexpr int OFF_V = OFF_K + 2 * KV_BYTES;                // 2 stages
 constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
 constexpr int OFF_BARS = OFF_P + P_BYTES;
-constexpr int OFF_LIST = OFF_BARS + 160 + 2048;            // after the barriers and the 2 x 2 x 128 floats of row-maximum exchange;
+constexpr int BAR_BYTES = 256;                             // barriers, tensor-memory slot, tile count
+constexpr int OFF_LIST = OFF_BARS + BAR_BYTES + 2048;            // after the barriers and the 2 x 2 x 128 floats of row-maximum exchange;
                                                            // block-sparse mode: up to 2048 tile ids (u16)
 constexpr int FA5_SMEM = OFF_LIST + 4096 + 1024;           // + alignment slack
 constexpr uint32_t TM_COLS = 512;
 constexpr uint32_t TM_S0 = 0, TM_O = 128;                  // score buffers at columns 0 and 64, output at 128..383
-constexpr uint32_t TM_P = 384;                             // probabilities, bf16 pairs: two buffers of 32 columns (64 keys)
+constexpr uint32_t TM_P = 384;                             // probabilities, bf16 pairs: four buffers of 32 columns (64 keys)
 
 __device__ __forceinline__ void tma2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
@@ -141,12 +145,12 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
     // tile earlier than the V stage of the same tile), so the next K tile is requested that much sooner -- with one pair
     // of barriers for both, every score MMA waited for a K tile that had been requested only when the previous P V ended.
     const uint32_t q_full = bars, k_full0 = bars + 8, k_empty0 = bars + 24, s_full0 = bars + 40, s_empty0 = bars + 56,
-                   pv_done0 = bars + 80, v_full0 = bars + 120, v_empty0 = bars + 136;
-    // p_full(b): the probabilities of a tile are in buffer b.  One barrier per buffer: with a single barrier, the softmax
-    // threads -- which may run a whole tile ahead of the P V product -- could complete the next phase before the MMA
-    // thread has looked at this one (it waits for the V tile first), and a parity wait cannot tell phase j from j + 2.
-    auto p_full = [&](int b) { return b ? bars + 152 : bars + 72; };
-    // pv_done0 + 8 (j & 1): the P V product of tile j is complete (one barrier per probability buffer)
+                   v_full0 = bars + 120, v_empty0 = bars + 136;
+    // Per probability buffer b = tile & 3: p_full(b) = the softmax has written the tile's probabilities, pv_done(b) =
+    // the P V product that read them is complete.  (One barrier per buffer: the softmax runs up to a pair of tiles
+    // ahead of the P V products, and a parity wait cannot tell a phase from the one two phases later.)
+    auto p_full = [&](int b) { return bars + 160 + 8 * (uint32_t)b; };
+    auto pv_done = [&](int b) { return bars + 192 + 8 * (uint32_t)b; };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BARS + 96);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qblk = gridDim.x - 1 - blockIdx.x, g = blockIdx.y;
@@ -186,7 +190,7 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
             mbar_init(v_full0 + 8 * s, 1); mbar_init(v_empty0 + 8 * s, 1);
             mbar_init(s_full0 + 8 * s, 1); mbar_init(s_empty0 + 8 * s, 256);
         }
-        mbar_init(p_full(0), 256); mbar_init(p_full(1), 256); mbar_init(pv_done0, 1); mbar_init(pv_done0 + 8, 1);
+        for (int b = 0; b < 4; ++b) { mbar_init(p_full(b), 256); mbar_init(pv_done(b), 1); }
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -214,8 +218,8 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
                 ok = waitb(k_empty0 + 8 * s, ((j >> 1) & 1) ^ 1u, err);
                 if (!ok) break;
                 mbar_expect_tx(k_full0 + 8 * s, KV_BYTES);
-                for (int b = 0; b < 4; ++b)
-                    tma2d(sb + OFF_K + s * KV_BYTES + b * (TK * 128), mk_, b * 64, tile_of(j) * TK, k_full0 + 8 * s);
+                for (int b = 0; b < 4; ++b)      // dim-block b: 128 rows of 128 bytes, stage s = rows 64 s .. 64 s + 63
+                    tma2d(sb + OFF_K + b * (2 * TK * 128) + s * (TK * 128), mk_, b * 64, tile_of(j) * TK, k_full0 + 8 * s);
             }
         } else if (lane == 1) {          // the V tiles go through a second thread: a wait for a V stage never delays a K request
             const CUtensorMap* mv_ = g ? &map_v1 : &map_v0;
@@ -231,40 +235,60 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t id_s = idesc(128, TK, false), id_o = idesc(128, 256, true);
-            auto issue_s = [&](int j) {
+            // The two K stages are rows 0-63 and 64-127 of ONE K-major operand per dim-block, and the two score buffers are
+            // adjacent columns: the scores of a pair of tiles are one sequence of 16 instructions 128 keys wide instead of
+            // two sequences 64 wide (an instruction costs about the same either way).
+            const uint32_t id_s2 = idesc(128, 2 * TK, false);
+            auto issue_s = [&](int j) {          // one tile (the last of an odd count): stage and score buffer j & 1
                 const int s = j & 1;
-                const uint32_t qb = sb + OFF_Q, kb = sb + OFF_K + s * KV_BYTES;
+                const uint32_t qb = sb + OFF_Q, kb = sb + OFF_K + s * (TK * 128);
 #pragma unroll
                 for (int ks = 0; ks < 16; ++ks)
                     mma5(tmem + TM_S0 + s * TK, desc_k(qb + (ks >> 2) * (128 * 128) + (ks & 3) * 32),
-                         desc_k(kb + (ks >> 2) * (TK * 128) + (ks & 3) * 32), id_s, ks ? 1u : 0u);
+                         desc_k(kb + (ks >> 2) * (2 * TK * 128) + (ks & 3) * 32), id_s, ks ? 1u : 0u);
                 commit5(s_full0 + 8 * s);
                 commit5(k_empty0 + 8 * s);
             };
+            auto issue_s_pair = [&]() {          // tiles (even, odd): both stages, both score buffers
+                const uint32_t qb = sb + OFF_Q, kb = sb + OFF_K;
+#pragma unroll
+                for (int ks = 0; ks < 16; ++ks)
+                    mma5(tmem + TM_S0, desc_k(qb + (ks >> 2) * (128 * 128) + (ks & 3) * 32),
+                         desc_k(kb + (ks >> 2) * (2 * TK * 128) + (ks & 3) * 32), id_s2, ks ? 1u : 0u);
+                commit5(s_full0); commit5(s_full0 + 8);
+                commit5(k_empty0); commit5(k_empty0 + 8);
+            };
             ok = waitb(q_full, 0, err) && waitb(k_full0, 0, err);
+            if (ok && ntiles > 1) ok = waitb(k_full0 + 8, 0, err);
             if (ok) {
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                issue_s(0);
+                if (ntiles > 1) issue_s_pair(); else issue_s(0);
             }
-            for (int j = 0; j < ntiles && ok; ++j) {
-                const int s = j & 1;
-                if (j + 1 < ntiles) {
-                    const int s1 = (j + 1) & 1;
-                    ok = waitb(k_full0 + 8 * s1, ((j + 1) >> 1) & 1, err);
-                    if (ok && j >= 1) ok = waitb(s_empty0 + 8 * s1, ((j - 1) >> 1) & 1, err);   // scores of tile j-1 were read
+            // The softmax threads take the tiles two at a time (one pass of barrier hops and tensor-memory round trips
+            // per 128 keys): per pair, first the score products of the NEXT pair -- their buffers are free as soon as the
+            // softmax has loaded this pair's scores -- then the two P V products of this pair.
+            for (int jp = 0; jp < ntiles && ok; jp += 2) {
+                if (jp + 2 < ntiles) {
+                    const bool pair = jp + 3 < ntiles;
+                    const uint32_t ph = ((jp + 2) >> 1) & 1, ph_read = (jp >> 1) & 1;
+                    ok = waitb(k_full0, ph, err) && waitb(s_empty0, ph_read, err);
+                    if (ok && pair) ok = waitb(k_full0 + 8, ph, err) && waitb(s_empty0 + 8, ph_read, err);
                     if (!ok) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    issue_s(j + 1);
+                    if (pair) issue_s_pair(); else issue_s(jp + 2);
                 }
-                ok = waitb(v_full0 + 8 * s, (j >> 1) & 1, err) && waitb(p_full(s), (j >> 1) & 1, err);
-                if (!ok) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t vb = sb + OFF_V + s * KV_BYTES;
+                for (int t = jp; t < min(jp + 2, ntiles) && ok; ++t) {
+                    const int s = t & 1, pb = t & 3;
+                    ok = waitb(v_full0 + 8 * s, (t >> 1) & 1, err) && waitb(p_full(pb), (t >> 2) & 1, err);
+                    if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t vb = sb + OFF_V + s * KV_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)   // 16 keys = 8 columns of the probability buffer per step
-                    mma5_ta(tmem + TM_O, tmem + TM_P + (uint32_t)s * 32 + kk * 8, desc_mn(vb + kk * (16 * 128), TK * 128), id_o, (j | kk) ? 1u : 0u);
-                commit5(v_empty0 + 8 * s);
-                commit5(pv_done0 + 8 * s);
+                    for (int kk = 0; kk < 4; ++kk)   // 16 keys = 8 columns of the probability buffer per step
+                        mma5_ta(tmem + TM_O, tmem + TM_P + (uint32_t)pb * 32 + kk * 8, desc_mn(vb + kk * (16 * 128), TK * 128), id_o, (t | kk) ? 1u : 0u);
+                    commit5(v_empty0 + 8 * s);
+                    commit5(pv_done(pb));
+                }
             }
         }
     } else {
@@ -273,7 +297,7 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
         const int hh = r >> 5, qi = r & 31, qpos = q0 + qi;
         const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const float sc = 0.0625f * 1.4426950408889634f;       // 1/sqrt(256) * log2(e)
-        float* xbuf = reinterpret_cast<float*>(smem + OFF_BARS + 160);      // [tile parity][2 halves][128 rows]
+        float* xbuf = reinterpret_cast<float*>(smem + OFF_BARS + BAR_BYTES);      // [pass parity][2 halves][128 rows]
         float m_ref = -1e30f, lsum = 0.f;
         // A wait that ran out must not make one warp leave the loop while the others sit in the named barrier
         // below: from then on this warp skips every wait (its results are garbage, *err is set) but keeps step.
@@ -281,42 +305,59 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
         auto wait_all = [&](uint32_t bar, uint32_t parity) {
             if (!dead && !__all_sync(0xffffffffu, waitb(bar, parity, err))) dead = true;
         };
-        for (int j = 0; j < ntiles; ++j) {
-            const int s = j & 1;
-            float* xmax = xbuf + (j & 1) * 256;
-            wait_all(s_full0 + 8 * s, (j >> 1) & 1);
+        for (int jp = 0; jp < ntiles; jp += 2) {
+            const bool two = jp + 1 < ntiles;                  // tiles jp (score buffer 0) and jp + 1 (score buffer 1)
+            float* xmax = xbuf + ((jp >> 1) & 1) * 256;
+            wait_all(s_full0, (jp >> 1) & 1);
+            if (two) wait_all(s_full0 + 8, (jp >> 1) & 1);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            uint32_t v[32];
-            TM_LD32(lane_addr + TM_S0 + s * TK + half * 32, v);
+            uint32_t va[32], vb[32];
+            TM_LD32(lane_addr + TM_S0 + half * 32, va);
+            if (two) TM_LD32(lane_addr + TM_S0 + TK + half * 32, vb);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            mbar_arrive(s_empty0 + 8 * s);
-            const int tj = tile_of(j), key0 = tj * TK + half * 32;
-            const bool dropped = mask && !((m0[hh * hstride + (tj >> 6)] >> ((tj >> 1) & 31)) & 1u);   // this head dropped the block
+            mbar_arrive(s_empty0);
+            if (two) mbar_arrive(s_empty0 + 8);
             float hmax = -1e30f;
+            {
+                const int tj = tile_of(jp), key0 = tj * TK + half * 32;
+                const bool dropped = mask && !((m0[hh * hstride + (tj >> 6)] >> ((tj >> 1) & 31)) & 1u);   // this head dropped the block
 #pragma unroll
-            for (int k = 0; k < 32; ++k) {
-                float x = __uint_as_float(v[k]) * sc;
-                if (key0 + k > qpos || dropped) x = -1e30f;
-                v[k] = __float_as_uint(x);
-                hmax = fmaxf(hmax, x);
+                for (int k = 0; k < 32; ++k) {
+                    float x = __uint_as_float(va[k]) * sc;
+                    if (key0 + k > qpos || dropped) x = -1e30f;
+                    va[k] = __float_as_uint(x);
+                    hmax = fmaxf(hmax, x);
+                }
             }
-            // row maximum over both halves
+            if (two) {
+                const int tj = tile_of(jp + 1), key0 = tj * TK + half * 32;
+                const bool dropped = mask && !((m0[hh * hstride + (tj >> 6)] >> ((tj >> 1) & 31)) & 1u);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    float x = __uint_as_float(vb[k]) * sc;
+                    if (key0 + k > qpos || dropped) x = -1e30f;
+                    vb[k] = __float_as_uint(x);
+                    hmax = fmaxf(hmax, x);
+                }
+            }
+            // row maximum over both halves (and both tiles)
             xmax[half * 128 + r] = hmax;
             named_bar_sync(1, 256);
             const float tmax = fmaxf(hmax, xmax[(half ^ 1) * 128 + r]);
-            // the probability buffer of this parity was last read by the P V of tile j - 2
-            if (j >= 2) {
-                wait_all(pv_done0 + 8 * s, ((j - 2) >> 1) & 1);
+            // the probability buffers of these two tiles were last read by the P V products of tiles jp - 4 and jp - 3
+            if (jp >= 4) {
+                wait_all(pv_done(jp & 3), ((jp - 4) >> 2) & 1);
+                if (two) wait_all(pv_done((jp + 1) & 3), ((jp - 3) >> 2) & 1);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             }
             // tcgen05.ld / st are warp-wide: the decision to rescale is taken per warp, every lane takes part
             // with its own factor (1 for a row whose maximum did not move); each half rescales 128 output columns
             const bool grow = tmax > m_ref + 8.0f;
             if (__any_sync(0xffffffffu, grow)) {
-                if (j >= 1) {
+                if (jp >= 1) {
                     // the output accumulator is rescaled in place: every P V issued so far must be complete
-                    wait_all(pv_done0 + 8 * (s ^ 1), ((j - 1) >> 1) & 1);
+                    wait_all(pv_done((jp - 1) & 3), ((jp - 1) >> 2) & 1);
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const float f = grow ? exp2f(m_ref - tmax) : 1.0f;
                     lsum *= f;
@@ -333,24 +374,39 @@ k_fa_tcgen05(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
                 }
                 if (grow) m_ref = tmax;
             }
-            // probabilities -> bf16 pairs into this thread's 16 columns of the tensor-memory buffer (the A operand of P V)
-            uint32_t w[16];
+            // probabilities -> bf16 pairs into this thread's 16 columns of the tiles' tensor-memory buffers (the A operand of P V)
+            {
+                uint32_t w[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const float p0 = ex2_approx(__uint_as_float(v[2 * e]) - m_ref);
-                const float p1 = ex2_approx(__uint_as_float(v[2 * e + 1]) - m_ref);
-                const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                w[e] = *reinterpret_cast<const uint32_t*>(&pp);
-                lsum += bf_lo(w[e]) + bf_hi(w[e]);
+                for (int e = 0; e < 16; ++e) {
+                    const float p0 = ex2_approx(__uint_as_float(va[2 * e]) - m_ref);
+                    const float p1 = ex2_approx(__uint_as_float(va[2 * e + 1]) - m_ref);
+                    const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                    w[e] = *reinterpret_cast<const uint32_t*>(&pp);
+                    lsum += bf_lo(w[e]) + bf_hi(w[e]);
+                }
+                TM_ST16(lane_addr + TM_P + (uint32_t)(jp & 3) * 32 + half * 16, w);
             }
-            TM_ST16(lane_addr + TM_P + (uint32_t)s * 32 + half * 16, w);
+            if (two) {
+                uint32_t w[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float p0 = ex2_approx(__uint_as_float(vb[2 * e]) - m_ref);
+                    const float p1 = ex2_approx(__uint_as_float(vb[2 * e + 1]) - m_ref);
+                    const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                    w[e] = *reinterpret_cast<const uint32_t*>(&pp);
+                    lsum += bf_lo(w[e]) + bf_hi(w[e]);
+                }
+                TM_ST16(lane_addr + TM_P + (uint32_t)((jp + 1) & 3) * 32 + half * 16, w);
+            }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            mbar_arrive(p_full(s));
+            mbar_arrive(p_full(jp & 3));
+            if (two) mbar_arrive(p_full((jp + 1) & 3));
         }
         // epilogue: O / l * sigmoid(gate) -> bf16; the row sum is the two halves' sums
-        wait_all(pv_done0 + 8 * ((ntiles - 1) & 1), ((ntiles - 1) >> 1) & 1);
-        float* xsum = xbuf + (ntiles & 1) * 256;
+        wait_all(pv_done((ntiles - 1) & 3), ((ntiles - 1) >> 2) & 1);
+        float* xsum = xbuf + ((((ntiles - 1) >> 1) + 1) & 1) * 256;       // the exchange buffer the last pass did not use
         xsum[half * 128 + r] = lsum;
         named_bar_sync(1, 256);
         if (!dead) {
