@@ -10,6 +10,10 @@
 // thread is already working on the next tile.  With BN = 256 an MMA reads 12 KB of shared memory per
 // 128 tensor-core cycles, which stays under the shared-memory bandwidth; 128-wide tiles sit at it.
 // M is the token dimension: rows beyond M are zero-filled by TMA and not stored.
+// Variants of the same kernel: a K split for products with far fewer tiles than SMs (f32 partial tiles, added up by
+// gemm_splitk_reduce, or by gemm_splitk_reduce_norm which also writes the RMSNorm of the finished row); GLU (gate and up
+// rows of the same outputs stacked in one B tile, silu(gate) * up in the epilogue); two products sharing A in one
+// launch (the tiles of both, two weight maps, two outputs).
 // Every wait is bounded; on expiry the kernel sets *err and leaves.
 #include <cuda.h>
 #include <cuda_bf16.h>
